@@ -1,0 +1,380 @@
+// Causal EMA scan: one-pass chunked scan chained by decoupled look-back.
+//
+// Replaces the reference's three-launch blocked scan (_fwd_local -> _fwd_carry
+// -> _fwd_apply, kernels/causal_ema_scan.py:73-155, launched from
+// _CausalEMAFn.forward :265-313), which writes y twice and serialises the
+// carry over time blocks in one program per channel block.
+//
+// Recurrence: y[t] = a*x[t] + d*y[t-1], d = 1 - a, y[-1] = 0, fp32 state.
+//
+// Decomposition. A "series" is one (batch row, block of C = 32*VEC channels);
+// each lane owns VEC adjacent channels and moves them with one 16-byte access
+// per token. A tile is one chunk of CH = WARPS*TS consecutive tokens of one
+// series; warp w of the CTA scans tokens [w*TS, (w+1)*TS) of the tile.
+// Persistent CTAs (cooperative launch, so all are co-resident) take tiles
+// round-robin in chunk-major order, and for each tile:
+//   1. stage the tile's x in shared memory (cp.async; the next tile is staged
+//      while the current one is finished),
+//   2. scan each warp's TS tokens from a zero state -> warp end states,
+//   3. warp 0 combines them into the tile aggregate, publishes it, walks back
+//      over up to 8 predecessor tiles of the same series (7 aggregates + 1
+//      inclusive prefix) to get the carry-in, and publishes the inclusive
+//      prefix,
+//   4. each warp rescans its tokens from its true carry-in and writes y once.
+//
+// Publication without fences: every published channel value travels in one
+// 64-bit word {value bits, tag}, written and read as a single-copy-atomic
+// 8-byte access, where tag identifies this launch. A reader spins until the
+// tag matches, so no __threadfence/flag pair is needed. The launch tag is kept
+// in the workspace header: each launch uses tag = header.epoch + 1 and the last
+// CTA to exit advances header.epoch, so consecutive launches never see each
+// other's records and the workspace needs zero-filling only once, before its
+// first use.
+//
+// Waits are bounded (kSpinLimit); a timed-out wait records
+// DWARF_DEVICE_TIMEOUT and continues with a zero carry instead of hanging.
+// Summation order in the look-back is fixed, so results are bitwise
+// reproducible run to run.
+#include "common.cuh"
+
+#include <algorithm>
+
+namespace dwarf {
+namespace {
+
+constexpr int kLookback = 8;
+
+struct EmaWorkspace {
+  uint32_t* header;  // [0] epoch, [32] exit counter (separate 128-B lines)
+  uint2* agg;        // [ntiles][C] {value bits, tag}
+  uint2* incl;       // [ntiles][C]
+};
+
+inline int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
+constexpr int64_t kHeaderBytes = 256;
+
+__device__ __forceinline__ void st_rec(uint2* p, float v, uint32_t tag) {
+  asm volatile("st.relaxed.gpu.global.v2.u32 [%0], {%1, %2};" ::"l"(p), "r"(__float_as_uint(v)), "r"(tag)
+               : "memory");
+}
+__device__ __forceinline__ uint2 ld_rec(const uint2* p) {
+  uint2 r;
+  asm volatile("ld.relaxed.gpu.global.v2.u32 {%0, %1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p) : "memory");
+  return r;
+}
+
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
+
+template <typename T, int VEC>
+__device__ __forceinline__ void stage_row(T* smem, const T* gmem, bool valid) {
+  if constexpr (VEC * sizeof(T) == 16) {
+    const uint32_t saddr = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+    const int src_bytes = valid ? 16 : 0;  // 0 => zero-fill
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(saddr), "l"(gmem), "r"(src_bytes)
+                 : "memory");
+  } else {
+#pragma unroll
+    for (int v = 0; v < VEC; ++v) smem[v] = valid ? gmem[v] : T(0.0f);
+  }
+}
+
+template <typename T, int VEC, int TS, int WARPS>
+__global__ void __launch_bounds__(WARPS * 32, 1)
+ema_scan_lookback_kernel(const T* __restrict__ x, T* __restrict__ y, int64_t seq_len, int64_t width,
+                         int64_t sxb, int64_t sxn, int64_t sxd, int64_t syb, int64_t syn, int64_t syd,
+                         const float* __restrict__ alpha, int alpha_per_channel, int clamp, float lo,
+                         float hi, EmaWorkspace ws, int64_t nseries, int64_t ncb, int64_t ntiles,
+                         int32_t* device_status) {
+  constexpr int C = 32 * VEC;  // channels per series
+  constexpr int CH = WARPS * TS;
+  constexpr bool kAsync = VEC * sizeof(T) == 16;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  T* bufs = reinterpret_cast<T*>(smem_raw);  // [2][WARPS][TS][C]
+  __shared__ float s_end[WARPS][C];
+  __shared__ float s_carry[C];
+
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(ws.header);
+  const uint32_t tag = epoch + 1u;  // never 0 (0 = never written)
+  bool timed_out = false;
+
+  auto stage = [&](int64_t tile, int slot) {
+    const int64_t chunk = tile / nseries;
+    const int64_t series = tile % nseries;
+    const int64_t b = series / ncb;
+    const int64_t c0 = (series % ncb) * C + (int64_t)lane * VEC;
+    const int64_t t0 = chunk * CH + (int64_t)warp * TS;
+    const bool active = c0 < width;
+    T* my_x = bufs + ((size_t)slot * WARPS * TS + (size_t)warp * TS) * C + lane * VEC;
+    const T* xrow = x + b * sxb + t0 * sxn + c0 * sxd;
+#pragma unroll
+    for (int i = 0; i < TS; ++i) stage_row<T, VEC>(my_x + i * C, xrow + i * sxn, active && t0 + i < seq_len);
+  };
+
+  int64_t cur = blockIdx.x;
+  if (cur < ntiles) stage(cur, 0);
+  if constexpr (kAsync) cp_async_commit();
+  int64_t nxt = cur + gridDim.x;
+  if (nxt < ntiles) stage(nxt, 1);
+  if constexpr (kAsync) cp_async_commit();
+
+  for (int it = 0; cur < ntiles; ++it) {
+    const int slot = it & 1;
+    const int64_t tile = cur;
+    const int64_t chunk = tile / nseries;
+    const int64_t series = tile % nseries;
+    const int64_t b = series / ncb;
+    const int64_t c0 = (series % ncb) * C + (int64_t)lane * VEC;
+    const bool lane_active = c0 < width;  // width % VEC == 0 for VEC > 1
+    const int64_t t0 = chunk * CH + (int64_t)warp * TS;
+    const int64_t rem = seq_len - t0;
+    const int nvalid = rem <= 0 ? 0 : (rem >= TS ? TS : (int)rem);
+    const T* my_x = bufs + ((size_t)slot * WARPS * TS + (size_t)warp * TS) * C + lane * VEC;
+
+    float a[VEC], d[VEC], dts[VEC];
+#pragma unroll
+    for (int v = 0; v < VEC; ++v) {
+      float av = alpha[alpha_per_channel ? (lane_active ? c0 + v : 0) : 0];
+      if (clamp) av = fminf(fmaxf(av, lo), hi);
+      a[v] = av;
+      d[v] = 1.0f - av;
+      float p = 1.0f;  // d^TS by repeated multiplication
+#pragma unroll
+      for (int i = 0; i < TS; ++i) p *= d[v];
+      dts[v] = p;
+    }
+    if constexpr (kAsync) cp_async_wait<1>();
+
+    // 2. Zero-state scan of the warp's TS tokens -> warp end state.
+    {
+      float s[VEC];
+#pragma unroll
+      for (int v = 0; v < VEC; ++v) s[v] = 0.0f;
+#pragma unroll
+      for (int i = 0; i < TS; ++i) {
+        float xv[VEC];
+        VecIO<T, VEC>::load(my_x + i * C, xv);
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) s[v] = a[v] * xv[v] + d[v] * s[v];
+      }
+#pragma unroll
+      for (int v = 0; v < VEC; ++v) s_end[warp][lane * VEC + v] = s[v];
+    }
+    __syncthreads();
+
+    // 3. Look-back (warp 0).
+    if (warp == 0) {
+      float agg[VEC], dch[VEC], carry[VEC];
+#pragma unroll
+      for (int v = 0; v < VEC; ++v) { agg[v] = 0.0f; dch[v] = 1.0f; carry[v] = 0.0f; }
+      for (int k = 0; k < WARPS; ++k) {
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) {
+          agg[v] = agg[v] * dts[v] + s_end[k][lane * VEC + v];
+          dch[v] *= dts[v];
+        }
+      }
+      const int64_t rec = tile * C + lane * VEC;
+#pragma unroll
+      for (int v = 0; v < VEC; ++v) st_rec(ws.agg + rec + v, agg[v], tag);
+      if (chunk == 0) {
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) st_rec(ws.incl + rec + v, agg[v], tag);
+      } else {
+        // Window: aggregates of chunk-1 .. chunk-7 and, in the farthest slot,
+        // the inclusive prefix of chunk-8 (the aggregate of chunk 0 is its
+        // inclusive prefix, so a window that reaches chunk 0 uses it).
+        const int window = chunk < kLookback ? (int)chunk : kLookback;
+        float val[kLookback][VEC];
+#pragma unroll
+        for (int k = 0; k < kLookback; ++k) {
+#pragma unroll
+          for (int v = 0; v < VEC; ++v) val[k][v] = 0.0f;
+        }
+        uint32_t spins = 0;
+        for (;;) {
+          bool ready = true;
+#pragma unroll
+          for (int k = 0; k < kLookback; ++k) {
+            if (k < window) {
+              const int64_t pc = chunk - 1 - k;
+              const bool use_incl = (k == kLookback - 1) && pc > 0;
+              const uint2* src = (use_incl ? ws.incl : ws.agg) + (pc * nseries + series) * C + lane * VEC;
+#pragma unroll
+              for (int v = 0; v < VEC; ++v) {
+                const uint2 r = ld_rec(src + v);
+                if (r.y == tag) val[k][v] = __uint_as_float(r.x);
+                else ready = false;
+              }
+            }
+          }
+          if (__all_sync(0xffffffffu, ready)) break;
+          if (++spins > kSpinLimit) { timed_out = true; break; }
+          __nanosleep(20);
+        }
+        float f[VEC];
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) f[v] = 1.0f;
+#pragma unroll
+        for (int k = 0; k < kLookback; ++k) {
+#pragma unroll
+          for (int v = 0; v < VEC; ++v) {
+            carry[v] += f[v] * val[k][v];
+            f[v] *= dch[v];
+          }
+        }
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) st_rec(ws.incl + rec + v, agg[v] + dch[v] * carry[v], tag);
+      }
+#pragma unroll
+      for (int v = 0; v < VEC; ++v) s_carry[lane * VEC + v] = carry[v];
+    }
+    __syncthreads();
+
+    // 4. Carry into this warp = tile carry-in pushed through the warps before
+    //    it; rescan from it and write y once.
+    float s[VEC];
+#pragma unroll
+    for (int v = 0; v < VEC; ++v) s[v] = s_carry[lane * VEC + v];
+    for (int k = 0; k < warp; ++k) {
+#pragma unroll
+      for (int v = 0; v < VEC; ++v) s[v] = s[v] * dts[v] + s_end[k][lane * VEC + v];
+    }
+    if (lane_active) {
+      T* yrow = y + b * syb + t0 * syn + c0 * syd;
+#pragma unroll
+      for (int i = 0; i < TS; ++i) {
+        float xv[VEC];
+        VecIO<T, VEC>::load(my_x + i * C, xv);
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) s[v] = a[v] * xv[v] + d[v] * s[v];
+        if (i < nvalid) VecIO<T, VEC>::store(yrow + i * syn, s);
+      }
+    }
+
+    cur = nxt;
+    nxt += gridDim.x;
+    __syncthreads();  // every reader of this slot and of s_end/s_carry is done
+    if (nxt < ntiles) stage(nxt, slot);
+    if constexpr (kAsync) cp_async_commit();
+  }
+
+  if (timed_out && device_status != nullptr) atomicExch(device_status, DWARF_DEVICE_TIMEOUT);
+  // The last CTA to exit advances the launch epoch for the next call.
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const uint32_t done = atomicAdd(ws.header + 32, 1u);
+    if (done == gridDim.x - 1) {
+      ws.header[32] = 0u;
+      ws.header[0] = (tag == 0xffffffffu) ? 0u : tag;
+      __threadfence();
+    }
+  }
+}
+
+struct EmaPlan {
+  int vec, ts, warps;
+  int64_t ncb, nseries, nchunks, ntiles;
+};
+
+EmaPlan plan_for(int64_t batch, int64_t seq_len, int64_t width, int dtype, bool vector_ok) {
+  EmaPlan p{};
+  p.vec = dtype == DWARF_F32 ? (vector_ok ? 4 : 1) : (vector_ok ? 8 : 1);
+  p.ts = 16;
+  p.warps = 4;
+  const int64_t C = 32 * p.vec;
+  p.ncb = (width + C - 1) / C;
+  p.nseries = batch * p.ncb;
+  const int64_t CH = (int64_t)p.ts * p.warps;
+  p.nchunks = (seq_len + CH - 1) / CH;
+  p.ntiles = p.nseries * p.nchunks;
+  return p;
+}
+
+int64_t workspace_bytes_for(const EmaPlan& p) {
+  const int64_t C = 32 * p.vec;
+  return kHeaderBytes + 2 * round_up(p.ntiles * C * 8, 256);
+}
+
+// Worst case over the two layouts the host may choose for these sizes.
+int64_t workspace_bytes_any(int64_t batch, int64_t seq_len, int64_t width, int dtype) {
+  int64_t a = workspace_bytes_for(plan_for(batch, seq_len, width, dtype, true));
+  int64_t b = workspace_bytes_for(plan_for(batch, seq_len, width, dtype, false));
+  return a > b ? a : b;
+}
+
+template <typename T, int VEC, int TS, int WARPS>
+int launch_ema(const dwarf_ema_scan_args* a, const EmaPlan& p, cudaStream_t stream) {
+  char* base = static_cast<char*>(a->workspace);
+  EmaWorkspace ws;
+  const int64_t C = 32 * VEC;
+  ws.header = reinterpret_cast<uint32_t*>(base);
+  ws.agg = reinterpret_cast<uint2*>(base + kHeaderBytes);
+  ws.incl = reinterpret_cast<uint2*>(base + kHeaderBytes + round_up(p.ntiles * C * 8, 256));
+  const size_t smem = 2 * (size_t)WARPS * TS * C * sizeof(T);
+  auto kernel = ema_scan_lookback_kernel<T, VEC, TS, WARPS>;
+  if (smem > 48 * 1024 &&
+      cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    return DWARF_ERR_LAUNCH;
+  int device = 0, sms = kNumSMs, per_sm = 1;
+  cudaGetDevice(&device);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, WARPS * 32, smem) != cudaSuccess ||
+      per_sm < 1)
+    per_sm = 1;
+  const int64_t grid = std::min<int64_t>(p.ntiles, (int64_t)sms * per_sm);
+  const T* x = static_cast<const T*>(a->x);
+  T* y = static_cast<T*>(a->y);
+  int64_t seq_len = a->seq_len, width = a->width;
+  int64_t sxb = a->sxb, sxn = a->sxn, sxd = a->sxd, syb = a->syb, syn = a->syn, syd = a->syd;
+  const float* alpha = a->alpha;
+  int per_channel = a->alpha_per_channel, clamp = a->clamp;
+  float lo = a->floor_, hi = a->ceiling;
+  int64_t nseries = p.nseries, ncb = p.ncb, ntiles = p.ntiles;
+  int32_t* status = a->device_status;
+  void* params[] = {&x, &y, &seq_len, &width, &sxb, &sxn, &sxd, &syb, &syn, &syd, &alpha,
+                    &per_channel, &clamp, &lo, &hi, &ws, &nseries, &ncb, &ntiles, &status};
+  if (cudaLaunchCooperativeKernel((const void*)kernel, dim3((unsigned)grid), dim3(WARPS * 32), params, smem,
+                                  stream) != cudaSuccess)
+    return DWARF_ERR_LAUNCH;
+  return launch_status();
+}
+
+}  // namespace
+}  // namespace dwarf
+
+using namespace dwarf;
+
+extern "C" int64_t dwarf_ema_scan_workspace_bytes(int64_t batch, int64_t seq_len, int64_t width,
+                                                  int32_t dtype) {
+  if (batch < 0 || seq_len < 0 || width < 0) return -1;
+  if (dtype != DWARF_F32 && dtype != DWARF_BF16) return -1;
+  return workspace_bytes_any(batch, seq_len, width, dtype);
+}
+
+extern "C" int dwarf_ema_scan(const dwarf_ema_scan_args* a, void* stream_) {
+  DWARF_CHECK_VERSION(a);
+  if (a->dtype != DWARF_F32 && a->dtype != DWARF_BF16) return DWARF_ERR_DTYPE;
+  if (a->batch < 0 || a->seq_len < 0 || a->width < 0) return DWARF_ERR_SHAPE;
+  if (a->batch == 0 || a->seq_len == 0 || a->width == 0) return DWARF_OK;
+  if (!a->x || !a->y || !a->alpha) return DWARF_ERR_NULL;
+  if (a->clamp && !(a->floor_ <= a->ceiling)) return DWARF_ERR_VALUE;
+  if (a->workspace == nullptr) return DWARF_ERR_WORKSPACE;
+  if (!aligned16(a->workspace)) return DWARF_ERR_ALIGN;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  const int vec = a->dtype == DWARF_F32 ? 4 : 8;
+  const bool vector_ok = a->sxd == 1 && a->syd == 1 && a->width % vec == 0 && a->sxb % vec == 0 &&
+                         a->sxn % vec == 0 && a->syb % vec == 0 && a->syn % vec == 0 &&
+                         aligned16(a->x) && aligned16(a->y);
+  EmaPlan p = plan_for(a->batch, a->seq_len, a->width, a->dtype, vector_ok);
+  if (a->workspace_bytes < workspace_bytes_for(p)) return DWARF_ERR_WORKSPACE;
+  if (a->dtype == DWARF_F32) {
+    return vector_ok ? launch_ema<float, 4, 16, 4>(a, p, stream) : launch_ema<float, 1, 16, 4>(a, p, stream);
+  }
+  return vector_ok ? launch_ema<__nv_bfloat16, 8, 16, 4>(a, p, stream)
+                   : launch_ema<__nv_bfloat16, 1, 16, 4>(a, p, stream);
+}
