@@ -140,8 +140,73 @@ class EmaScanArgs(ctypes.Structure):
     ]
 
 
+def _fields(spec: str):
+    """Build a ctypes field list from 'name:type, ...' (i32 i64 f32 ptr)."""
+    kinds = {"i32": c_i32, "i64": c_i64, "f32": c_f32, "ptr": c_ptr}
+    out = []
+    for item in spec.replace("\n", " ").split(","):
+        item = item.strip()
+        if item:
+            name, kind = item.split(":")
+            out.append((name.strip(), kinds[kind.strip()]))
+    return out
+
+
+class Q6PackArgs(ctypes.Structure):
+    _fields_ = _fields("""version:i32, dtype:i32, x:ptr, B:i64, H:i64, T:i64, sxb:i64, sxh:i64, sxt:i64,
+        codes:ptr, scb:i64, sch:i64, sct:i64, scales:ptr, ssb:i64, ssh:i64, sst:i64""")
+
+
+class Q6UnpackArgs(ctypes.Structure):
+    _fields_ = _fields("""version:i32, out_dtype:i32, codes:ptr, B:i64, H:i64, T:i64, scb:i64, sch:i64, sct:i64,
+        scales:ptr, ssb:i64, ssh:i64, sst:i64, x:ptr, sxb:i64, sxh:i64, sxt:i64""")
+
+
+class DsqgFwdArgs(ctypes.Structure):
+    _fields_ = _fields("""version:i32, kv_format:i32, B:i64, H:i64, H_kv:i64, N:i64, head_dim:i32,
+        J:i32, j_small:i32, j_large:i32, plane_shift:i32, query_start:i32,
+        q:ptr, sqb:i64, sqh:i64, sqn:i64, k:ptr, skb:i64, skh:i64, skn:i64, v:ptr, svb:i64, svh:i64, svn:i64,
+        k_codes:ptr, k_scales:ptr, v_codes:ptr, v_scales:ptr, ccb:i64, cch:i64, cct:i64, csb:i64, csh:i64, cst:i64,
+        offsets:ptr, pos_bias:ptr, spj:i64, sph:i64, scale_embed:ptr, sej:i64, sed:i64,
+        phase_base:ptr, sbj:i64, sbh:i64, phase_gain:ptr, sgj:i64, sgh:i64,
+        y_pre:ptr, syb:i64, syh:i64, syn:i64, z_pre:ptr, szb:i64, szh:i64, szn:i64,
+        out:ptr, sob:i64, soh:i64, son:i64, lse:ptr, slb:i64, slh:i64, sln:i64,
+        head_gain:ptr, head_gain_dtype:i32, gate:ptr, sgb_:i64, sgn_:i64""")
+
+
+class DsqgPrepArgs(ctypes.Structure):
+    _fields_ = _fields("""version:i32, pack_q6:i32, B:i64, H:i64, H_kv:i64, N:i64,
+        q:ptr, sqb:i64, sqh:i64, sqn:i64, k:ptr, skb:i64, skh:i64, skn:i64, v:ptr, svb:i64, svh:i64, svn:i64,
+        q_probe:ptr, k_probe:ptr, y_pre:ptr, z_pre:ptr, k_codes:ptr, k_scales:ptr, v_codes:ptr, v_scales:ptr""")
+
+
+class NpciArgs(ctypes.Structure):
+    _fields_ = _fields("""version:i32, dtype:i32, B:i64, H:i64, N:i64, x:ptr, sxb:i64, sxh:i64, sxn:i64,
+        addend:ptr, sab:i64, sah:i64, san:i64, delta:ptr, sdb:i64, sdh:i64, sdn:i64, theta:ptr, tau:f32,
+        out:ptr, sob:i64, soh:i64, son:i64""")
+
+
+_ENTRY_POINTS = {
+    "dwarf_npci_rotate": NpciArgs,
+    "dwarf_ema_scan": EmaScanArgs,
+    "dwarf_q6_pack": Q6PackArgs,
+    "dwarf_q6_unpack": Q6UnpackArgs,
+    "dwarf_dsqg_fwd": DsqgFwdArgs,
+    "dwarf_dsqg_prep": DsqgPrepArgs,
+}
+
+
+def call(name: str, args: ctypes.Structure, device: torch.device) -> None:
+    """Invoke a C entry point on the current stream of `device`; raise on error."""
+    lib = load()
+    status = getattr(lib, name)(ctypes.byref(args), stream_handle(device))
+    check(status, name)
+
+
 def _declare(lib: ctypes.CDLL) -> None:
+    for name, struct in _ENTRY_POINTS.items():
+        fn = getattr(lib, name)
+        fn.restype = c_i32
+        fn.argtypes = [ctypes.POINTER(struct), c_ptr]
     lib.dwarf_ema_scan_workspace_bytes.restype = c_i64
     lib.dwarf_ema_scan_workspace_bytes.argtypes = [c_i64, c_i64, c_i64, c_i32]
-    lib.dwarf_ema_scan.restype = c_i32
-    lib.dwarf_ema_scan.argtypes = [ctypes.POINTER(EmaScanArgs), c_ptr]

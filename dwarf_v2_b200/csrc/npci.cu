@@ -1,0 +1,101 @@
+// NPCI magnitude-aware rotation, one 64-value head row per 16 threads.
+//
+// Replaces npci_rotate (kernels/dsqg_attention_v22.py:223-254) and the
+// identical _magnitude_aware_rotate (kernels/hierarchical_sparse_attn_v18_hisa.py:99-125),
+// which run as ~15 separate elementwise/reduction passes in the reference.
+// Two 16-lane reduction rounds: (|x|^2, d.x, nothing else) then |p|^2 of the
+// explicit perpendicular p = d - (d.u) u, as the reference computes it.
+#include "common.cuh"
+
+namespace dwarf {
+namespace {
+
+struct NpciParams {
+  int64_t B, H, N;
+  const void* x; int64_t sxb, sxh, sxn;
+  const void* add; int64_t sab, sah, san;
+  const void* d; int64_t sdb, sdh, sdn;
+  const float* theta;
+  float tau;
+  void* out; int64_t sob, soh, son;
+};
+
+__device__ __forceinline__ float sum16(float v) {
+#pragma unroll
+  for (int o = 8; o >= 1; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o, 16);
+  return v;
+}
+
+template <typename T>
+__device__ __forceinline__ void load4(const void* base, int64_t off, float (&v)[4]) {
+  const T* p = static_cast<const T*>(base) + off;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) v[i] = static_cast<float>(p[i]);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) npci_kernel(const NpciParams p) {
+  const int64_t rows = p.B * p.H * p.N;
+  const int64_t row = (int64_t)blockIdx.x * 16 + threadIdx.x / 16;
+  const int g = threadIdx.x & 15;
+  const int64_t r = row < rows ? row : rows - 1;
+  const int64_t n = r % p.N, h = (r / p.N) % p.H, b = r / (p.N * p.H);
+  float x[4], d[4];
+  load4<T>(p.x, b * p.sxb + h * p.sxh + n * p.sxn + g * 4, x);
+  if (p.add != nullptr) {
+    float a[4];
+    load4<T>(p.add, b * p.sab + h * p.sah + n * p.san + g * 4, a);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) x[i] = static_cast<float>(static_cast<T>(x[i] + a[i]));
+  }
+  load4<T>(p.d, b * p.sdb + h * p.sdh + n * p.sdn + g * 4, d);
+  float xx = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) xx += x[i] * x[i];
+  const float norm = fmaxf(sqrtf(sum16(xx)), 1e-12f);
+  float u[4], du = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) { u[i] = x[i] / norm; du += d[i] * u[i]; }
+  du = sum16(du);
+  float perp[4], pp = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) { perp[i] = d[i] - du * u[i]; pp += perp[i] * perp[i]; }
+  const float pn = sqrtf(sum16(pp));
+  const bool active = pn > norm * 1e-7f;
+  const float angle = p.theta[h] * tanhf(pn / (p.tau * norm + 1e-12f));
+  float sn, cs;
+  sincosf(angle, &sn, &cs);
+  const float inv_pn = 1.0f / fmaxf(pn, 1e-20f);
+  if (row >= rows) return;
+  T* o = static_cast<T*>(p.out) + b * p.sob + h * p.soh + n * p.son + g * 4;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float dir = active ? perp[i] * inv_pn : 0.0f;
+    const float rot = cs * x[i] + sn * norm * dir;
+    o[i] = static_cast<T>(active ? rot : x[i]);
+  }
+}
+
+}  // namespace
+}  // namespace dwarf
+
+using namespace dwarf;
+
+extern "C" int dwarf_npci_rotate(const dwarf_npci_rotate_args* a, void* stream) {
+  DWARF_CHECK_VERSION(a);
+  if (a->dtype != DWARF_BF16 && a->dtype != DWARF_F32) return DWARF_ERR_DTYPE;
+  if (a->B < 0 || a->H <= 0 || a->N < 0) return DWARF_ERR_SHAPE;
+  const int64_t rows = a->B * a->H * a->N;
+  if (rows == 0) return DWARF_OK;
+  if (!a->x || !a->delta || !a->theta || !a->out) return DWARF_ERR_NULL;
+  if (!(a->tau > 0.0f)) return DWARF_ERR_VALUE;
+  NpciParams p{a->B, a->H, a->N, a->x, a->sxb, a->sxh, a->sxn, a->addend, a->sab, a->sah, a->san,
+               a->delta, a->sdb, a->sdh, a->sdn, a->theta, a->tau, a->out, a->sob, a->soh, a->son};
+  const int64_t blocks = (rows + 15) / 16;
+  if (blocks > 0x7fffffffLL) return DWARF_ERR_SHAPE;
+  if (a->dtype == DWARF_BF16)
+    npci_kernel<__nv_bfloat16><<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(p);
+  else
+    npci_kernel<float><<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(p);
+  return launch_status();
+}

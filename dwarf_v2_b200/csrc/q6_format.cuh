@@ -1,0 +1,44 @@
+// q6 format primitives shared by the codec, the QKV prep kernel and the
+// DSQG kernel (the format is specified in include/dwarf_b200.h).
+#pragma once
+
+#include "common.cuh"
+
+namespace dwarf {
+
+// fp16 scale of a row from its absolute maximum.
+__device__ __forceinline__ __half q6_scale_from_amax(float amax) {
+  return __float2half_rn(fminf(amax, 65504.0f));
+}
+
+// Code of one value: clamp(rint((x*31)/s), -31, 31); s == 0 -> 0.
+__device__ __forceinline__ int q6_quantize(float x, float s) {
+  if (!(s > 0.0f)) return 0;
+  float q = rintf(__fdiv_rn(__fmul_rn(x, 31.0f), s));
+  q = fminf(fmaxf(q, -31.0f), 31.0f);
+  return (int)q;
+}
+
+// Dequantisation step float(s) / 31 (IEEE division).
+__device__ __forceinline__ float q6_step(__half s) { return __fdiv_rn(__half2float(s), 31.0f); }
+
+// Signed 6-bit code starting at bit `bit` (< 27) of w.
+__device__ __forceinline__ int q6_code(uint32_t w, int bit) {
+  return (int)(w << (26 - bit)) >> 26;
+}
+
+// Signed 6-bit code i (0..15) of a 96-bit little-endian stream w[0..2].
+template <int I>
+__device__ __forceinline__ int q6_code96(const uint32_t (&w)[3]) {
+  constexpr int bit = 6 * I;
+  constexpr int word = bit >> 5;
+  constexpr int off = bit & 31;
+  if constexpr (off <= 26) {
+    return (int)(w[word] << (26 - off)) >> 26;
+  } else {
+    const uint32_t u = __funnelshift_r(w[word], w[word + 1], off);
+    return (int)(u << 26) >> 26;
+  }
+}
+
+}  // namespace dwarf

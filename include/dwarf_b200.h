@@ -94,6 +94,176 @@ int64_t dwarf_ema_scan_workspace_bytes(int64_t batch, int64_t seq_len, int64_t w
                                        int32_t dtype);
 int dwarf_ema_scan(const dwarf_ema_scan_args* args, void* stream);
 
+
+/* ------------------------------------------------------------------------
+ * q6 KV codec (no reference counterpart: the reference declares a packed-KV
+ * mode unimplemented, kernels/dsqg_attention_v22.py:467,473-476).
+ *
+ * One row = one (b, h, t) head vector of 64 values.
+ *   amax  = max_d |x_d|                         (fp32)
+ *   s     = fp16(min(amax, 65504))              (round to nearest even)
+ *   c_d   = clamp(rint((x_d * 31) / float(s)), -31, 31)   (RNE; s == 0 -> 0)
+ *   bytes = 16 groups of 4 codes, each group 3 bytes little-endian:
+ *           w = u0 | u1 << 6 | u2 << 12 | u3 << 18, u = c & 63 (6-bit two's
+ *           complement); row = 48 bytes.
+ *   dequant x^_d = float(c_d) * (float(s) / 31)
+ * Codes [rows][48] u8, scales [rows] fp16, rows addressed (b, h, t) by strides.
+ * ---------------------------------------------------------------------- */
+typedef struct {
+  int32_t version;
+  int32_t dtype;              /* dtype of x: DWARF_BF16 or DWARF_F32        */
+  const void* x;              /* [B, H, T, 64]                              */
+  int64_t B, H, T;
+  int64_t sxb, sxh, sxt;      /* element strides of x; dim stride must be 1 */
+  uint8_t* codes;             /* [B, H, T, 48]                              */
+  int64_t scb, sch, sct;      /* byte strides of codes rows (multiple of 16)*/
+  uint16_t* scales;           /* fp16 bits [B, H, T]                        */
+  int64_t ssb, ssh, sst;      /* element strides of scales                  */
+} dwarf_q6_pack_args;
+
+typedef struct {
+  int32_t version;
+  int32_t out_dtype;          /* DWARF_F32 or DWARF_BF16                    */
+  const uint8_t* codes;
+  int64_t B, H, T;
+  int64_t scb, sch, sct;
+  const uint16_t* scales;
+  int64_t ssb, ssh, sst;
+  void* x;                    /* [B, H, T, 64] output                       */
+  int64_t sxb, sxh, sxt;
+} dwarf_q6_unpack_args;
+
+int dwarf_q6_pack(const dwarf_q6_pack_args* args, void* stream);
+int dwarf_q6_unpack(const dwarf_q6_unpack_args* args, void* stream);
+
+/* ------------------------------------------------------------------------
+ * DSQG lattice attention forward.
+ *
+ * Replaces dsqg_attention_v18_grouped -> _DSQGV18GroupedFn.forward ->
+ * _fwd_v22_online (kernels/dsqg_attention_v22.py:2691-2777, 2197-2352,
+ * 698-860) for grouped_mode "baseline". For every query n and offset j
+ * (canonical order: small offsets then large), src = n - off[j]:
+ *   score = (q_n . (k_src + bf16(E_j))) / sqrt(64) + pos_bias[j, h]
+ * online softmax over valid (src >= 0) offsets, accumulating v_src, where for
+ * j >= j_small the four MOVT planes (a_r = 16 r + plane_shift, a_r + 1) of
+ * v_src are rotated by theta = phase_base[j',h,r] + phase_gain[j',h,r] *
+ * y_pre[n,r] * z_pre[src,r], j' = j - j_small. Rows with no valid offset
+ * produce exact zeros and LSE = -inf.
+ *
+ * K/V come either as bf16 tensors (kv_format 0, the reference's layout,
+ * any strides) or as a q6 cache (kv_format 1, dwarf_q6_pack layout).
+ * head_dim must be 64; GQA (H % H_kv == 0) is supported.
+ *
+ * Optional fused epilogue (the module's `out * if_gain` and
+ * `* sigmoid(content_gate)`, dsqg_attention_v22.py:3285-3289), with the
+ * module's bf16 rounding points: o = bf16(acc/l); if head_gain:
+ * o = bf16(o * head_gain[h]); if gate: o = bf16(o * bf16(sigmoid(gate))).
+ * ---------------------------------------------------------------------- */
+typedef struct {
+  int32_t version;
+  int32_t kv_format;              /* 0 = bf16 K/V, 1 = q6 cache           */
+  int64_t B, H, H_kv, N;
+  int32_t head_dim;               /* must be 64                           */
+  int32_t J, j_small, j_large;
+  int32_t plane_shift;
+  int32_t query_start;            /* rows < query_start are written as 0  */
+  const void* q;                  /* bf16 [B, H, N, 64]                   */
+  int64_t sqb, sqh, sqn;          /* element strides; dim stride 1        */
+  const void* k;                  /* bf16 [B, H_kv, N, 64] (kv_format 0)  */
+  int64_t skb, skh, skn;
+  const void* v;
+  int64_t svb, svh, svn;
+  const uint8_t* k_codes;         /* q6 (kv_format 1)                     */
+  const uint16_t* k_scales;
+  const uint8_t* v_codes;
+  const uint16_t* v_scales;
+  int64_t ccb, cch, cct;          /* byte strides of code rows (K and V)  */
+  int64_t csb, csh, cst;          /* element strides of scales (K and V)  */
+  const int32_t* offsets;         /* [J], device                          */
+  const float* pos_bias;          /* [J, H]                               */
+  int64_t spj, sph;
+  const float* scale_embed;       /* [J, 64]                              */
+  int64_t sej, sed;
+  const float* phase_base;        /* [j_large, H, 4] (last dim stride 1)  */
+  int64_t sbj, sbh;
+  const float* phase_gain;        /* [j_large, H, 4]                      */
+  int64_t sgj, sgh;
+  const float* y_pre;             /* [B, H, N, 4] (last dim stride 1)     */
+  int64_t syb, syh, syn;
+  const float* z_pre;             /* [B, H_kv, N, 4]                      */
+  int64_t szb, szh, szn;
+  void* out;                      /* bf16 [B, H, N, 64] by strides        */
+  int64_t sob, soh, son;
+  float* lse;                     /* optional fp32 [B, H, N]              */
+  int64_t slb, slh, sln;
+  const void* head_gain;          /* optional [H], dtype head_gain_dtype  */
+  int32_t head_gain_dtype;        /* DWARF_F32 or DWARF_BF16              */
+  const void* gate;               /* optional bf16 [B, N, H*64] view      */
+  int64_t sgb_, sgn_;             /* element strides (b, n); h*64+d is +1 */
+} dwarf_dsqg_fwd_args;
+
+int dwarf_dsqg_fwd(const dwarf_dsqg_fwd_args* args, void* stream);
+
+/* ------------------------------------------------------------------------
+ * DSQG QKV prep: the per-row work between the qkvg projection and the DSQG
+ * kernel, fused into one pass over the projection output.
+ *
+ * Replaces the probe projections of DSQGAttentionV19.forward
+ * (kernels/dsqg_attention_v22.py:3231-3254):
+ *   y_pre[b,h,n,r] = (q . qp_r) / sqrt(|q|^2 + 1e-6*64)
+ *   z_pre[b,h,n,r] = (k . kp_r) / sqrt(|k|^2 + 1e-6*64)
+ * with qp/kp the L2-normalised probes [4][64] (fp32), and optionally packs K
+ * and V rows into the q6 cache (dwarf_q6_pack format) in the same pass.
+ * ---------------------------------------------------------------------- */
+typedef struct {
+  int32_t version;
+  int32_t pack_q6;                /* 1: also write K/V q6 codes + scales  */
+  int64_t B, H, H_kv, N;
+  const void* q;                  /* bf16 [B, H, N, 64]                   */
+  int64_t sqb, sqh, sqn;
+  const void* k;                  /* bf16 [B, H_kv, N, 64]                */
+  int64_t skb, skh, skn;
+  const void* v;                  /* bf16 [B, H_kv, N, 64] (pack_q6 only) */
+  int64_t svb, svh, svn;
+  const float* q_probe;           /* [4][64]                              */
+  const float* k_probe;           /* [4][64]                              */
+  float* y_pre;                   /* [B, H, N, 4] contiguous              */
+  float* z_pre;                   /* [B, H_kv, N, 4] contiguous           */
+  uint8_t* k_codes;               /* [B, H_kv, N, 48] contiguous          */
+  uint16_t* k_scales;             /* [B, H_kv, N] contiguous              */
+  uint8_t* v_codes;
+  uint16_t* v_scales;
+} dwarf_dsqg_prep_args;
+
+int dwarf_dsqg_prep(const dwarf_dsqg_prep_args* args, void* stream);
+
+/* ------------------------------------------------------------------------
+ * NPCI magnitude-aware rotation of head vectors (64 values per row).
+ *
+ * Replaces npci_rotate (kernels/dsqg_attention_v22.py:223-254) and
+ * _magnitude_aware_rotate (kernels/hierarchical_sparse_attn_v18_hisa.py:99-125):
+ *   x' = x (+ addend, rounded to the I/O dtype, when addend != NULL)
+ *   u = x'/max(|x'|,1e-12); p = d - (d.u) u; active = |p| > |x'| 1e-7
+ *   angle = theta[h] * tanh(|p| / (tau |x'| + 1e-12))
+ *   out = active ? cos(angle) x' + sin(angle) |x'| p/max(|p|,1e-20) : x'
+ * Math in fp32; x, addend, delta and out share one dtype (bf16 or fp32).
+ * The optional addend fuses the HISA low-rank global K/V adapter add
+ * (hierarchical_sparse_attn_v18_hisa.py:2579-2591).
+ * ---------------------------------------------------------------------- */
+typedef struct {
+  int32_t version;
+  int32_t dtype;                  /* DWARF_BF16 or DWARF_F32              */
+  int64_t B, H, N;
+  const void* x;   int64_t sxb, sxh, sxn;
+  const void* addend; int64_t sab, sah, san;   /* optional            */
+  const void* delta; int64_t sdb, sdh, sdn;
+  const float* theta;             /* [H] fp32                             */
+  float tau;
+  void* out;       int64_t sob, soh, son;
+} dwarf_npci_rotate_args;
+
+int dwarf_npci_rotate(const dwarf_npci_rotate_args* args, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

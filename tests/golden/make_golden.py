@@ -86,9 +86,131 @@ def make_ema() -> None:
     save("ema_per_channel_f32", x=x, decay=decay, y=y)
 
 
+def _dsqg_case(module, q, k, v):
+    """Reference tables + probe projections exactly as DSQGAttentionV19.forward builds them."""
+    import torch.nn.functional as F
+
+    gate = torch.sigmoid(module.phase_gate)[:, None, None]
+    qp = F.normalize(module.query_probes.float(), dim=-1)
+    kp = F.normalize(module.key_probes.float(), dim=-1)
+    eps = 1e-6 * q.shape[-1]
+    qf, kf = q.float(), k.float()
+    y = torch.einsum("bhnd,rd->bhnr", qf, qp) * torch.rsqrt(qf.square().sum(-1, keepdim=True) + eps)
+    z = torch.einsum("bhnd,rd->bhnr", kf, kp) * torch.rsqrt(kf.square().sum(-1, keepdim=True) + eps)
+    return dict(
+        pos_bias=module.pos_bias.detach().float(),
+        scale_embed=module.centered_scale_embed.detach().float(),
+        phase_base=(module.phase_base * gate).detach().float(),
+        phase_gain=(module.phase_gain * gate).detach().float(),
+        y_pre=y.detach(), z_pre=z.detach(),
+        offsets=module.offsets_dev.clone(),
+    )
+
+
+def _randomize_dsqg(module, seed):
+    g = torch.Generator().manual_seed(seed)
+    with torch.no_grad():
+        module.pos_bias_residual.copy_(torch.randn(module.pos_bias_residual.shape, generator=g) * 0.3)
+        module.scale_embed.copy_(torch.randn(module.scale_embed.shape, generator=g) * 0.3)
+        module.phase_base.copy_(torch.randn(module.phase_base.shape, generator=g) * 0.7)
+        module.phase_gain.copy_(torch.randn(module.phase_gain.shape, generator=g) * 3.0)
+        module.phase_gate.copy_(torch.randn(module.phase_gate.shape, generator=g))
+
+
+def _triton_interpret_dsqg(case: dict, q, k, v, j_small, j_large, plane_shift, query_start):
+    """Run the reference Triton kernel _fwd_v22_online on CPU under TRITON_INTERPRET=1."""
+    import subprocess
+    import tempfile
+
+    with tempfile.TemporaryDirectory() as tmp:
+        torch.save(dict(case=case, q=q, k=k, v=v, j_small=j_small, j_large=j_large,
+                        plane_shift=plane_shift, query_start=query_start), f"{tmp}/in.pt")
+        code = f"""
+import sys, torch
+sys.path.insert(0, {str(REFERENCE / 'kernels')!r})
+import dsqg_attention_v22 as ref
+d = torch.load({tmp!r} + '/in.pt')
+c = d['case']; q, k, v = d['q'], d['k'], d['v']
+B, H, N, HD = q.shape
+out = torch.zeros_like(q); lse = torch.full((B, H, N), float('-inf'))
+pb, se = c['pos_bias'].contiguous(), c['scale_embed'].contiguous()
+ph, pg = c['phase_base'].contiguous(), c['phase_gain'].contiguous()
+y, z = c['y_pre'].contiguous(), c['z_pre'].contiguous()
+qs = d['query_start']
+grid = (B * H, ref.triton.cdiv(max(0, N - qs), 64))
+ref._fwd_v22_online[grid](q, k, v, pb, se, ph, pg, y, z, out, lse, c['offsets'],
+    *q.stride(), *k.stride(), *v.stride(), *out.stride(), *lse.stride(), *pb.stride(), *se.stride(),
+    *ph.stride()[:2], *pg.stride()[:2], *y.stride()[:3], *z.stride()[:3],
+    H=H, N=N, HD=HD, BLOCK_N=64, BLOCK_HD=64, J_VAL=d['j_small'] + d['j_large'], J_SMALL_VAL=d['j_small'],
+    J_LARGE_VAL=d['j_large'], R_PLANES_VAL=4, PLANE_SHIFT=d['plane_shift'], K_GROUP_SIZE=3,
+    KV_HEAD_GROUP_SIZE=H // k.shape[1], QUERY_START=qs)
+torch.save(dict(out=out, lse=lse), {tmp!r} + '/out.pt')
+"""
+        env = dict(os.environ, TRITON_INTERPRET="1")
+        subprocess.run([sys.executable, "-c", code], check=True, env=env)
+        return torch.load(f"{tmp}/out.pt")
+
+
+def make_dsqg(with_triton: bool = True) -> None:
+    _import_reference()
+    import dsqg_attention_v22 as ref
+
+    # BASELINE config 1: B=1, H=8, hd=64, T=256, canonical 96-offset lattice.
+    torch.manual_seed(1)
+    module = ref.DSQGAttentionV19(512, 8, ref.ALL_OFFSETS, 17, 79, seq_len=2048, grouped_mode="baseline")
+    _randomize_dsqg(module, 101)
+    torch.manual_seed(0)
+    q = torch.randn(1, 8, 256, 64).to(torch.bfloat16)
+    k = torch.randn(1, 8, 256, 64).to(torch.bfloat16)
+    v = torch.randn(1, 8, 256, 64).to(torch.bfloat16)
+    case = _dsqg_case(module, q, k, v)
+    eager = ref._eager_dsqg_attention(q.float(), k.float(), v.float(), case["pos_bias"], case["scale_embed"],
+                                      case["phase_base"], case["phase_gain"], case["y_pre"], case["z_pre"],
+                                      case["offsets"], 17, plane_shift=0)
+    extra = {}
+    if with_triton:
+        tri = _triton_interpret_dsqg(case, q, k, v, 17, 79, 0, 1)
+        extra = dict(triton_out=tri["out"], triton_lse=tri["lse"])
+    save("dsqg_config1", q=q, k=k, v=v, eager_out=eager, j_small=17, j_large=79, plane_shift=0,
+         query_start=1, **case, **extra)
+
+    # GQA (H=4, H_kv=2), plane shift 10, ragged N, query_start past the minimum offset.
+    torch.manual_seed(2)
+    offsets = [1, 3, 7, 12, 28, 48, 50, 77, 130, 200]
+    module = ref.DSQGAttentionV19(256, 4, offsets, 5, 5, seq_len=256, plane_shift=10)
+    _randomize_dsqg(module, 202)
+    q = torch.randn(2, 4, 157, 64).to(torch.bfloat16)
+    k = torch.randn(2, 2, 157, 64).to(torch.bfloat16)
+    v = torch.randn(2, 2, 157, 64).to(torch.bfloat16)
+    case = _dsqg_case(module, q, k, v)
+    case["z_pre"] = case["z_pre"]  # computed from the 2 KV heads
+    eager = ref._eager_dsqg_attention(q.float(), k.float(), v.float(), case["pos_bias"], case["scale_embed"],
+                                      case["phase_base"], case["phase_gain"], case["y_pre"], case["z_pre"],
+                                      case["offsets"], 5, plane_shift=10)
+    extra = {}
+    if with_triton:
+        tri = _triton_interpret_dsqg(case, q, k, v, 5, 5, 10, 1)
+        extra = dict(triton_out=tri["out"], triton_lse=tri["lse"])
+    save("dsqg_gqa_ragged", q=q, k=k, v=v, eager_out=eager, j_small=5, j_large=5, plane_shift=10,
+         query_start=1, **case, **extra)
+
+    # Whole module (eval, fp32 reference on bf16-valued inputs), head_dim 64.
+    torch.manual_seed(3)
+    module = ref.DSQGAttentionV19(128, 2, [1, 2, 3, 5, 8, 13, 21, 48, 64, 100], 7, 3, seq_len=160,
+                                  dropout=0.0, plane_shift=6).eval()
+    _randomize_dsqg(module, 303)
+    with torch.no_grad():
+        module.if_gain.copy_(torch.tensor([0.7, 1.3]))
+    x = torch.randn(2, 150, 128).to(torch.bfloat16).float()
+    with torch.no_grad():
+        y = module(x)
+    state = {f"state.{k}": val for k, val in module.state_dict().items()}
+    save("dsqg_module_eval", x=x, y=y, **state)
+
+
 def main(argv: list[str]) -> None:
     which = argv[1] if len(argv) > 1 else "all"
-    makers = {"ema": make_ema}
+    makers = {"ema": make_ema, "dsqg": make_dsqg}
     for name, maker in makers.items():
         if which in ("all", name):
             maker()

@@ -1,0 +1,260 @@
+"""DSQG lattice attention and the q6 KV codec.
+
+CPU: the numpy oracle is pinned to the reference's own outputs (the eager
+oracle ``_eager_dsqg_attention`` and the Triton kernel ``_fwd_v22_online``
+run under TRITON_INTERPRET=1, both captured in tests/golden/). GPU: the CUDA
+kernels (dwarf_dsqg_fwd, dwarf_dsqg_prep, dwarf_q6_pack/unpack, through the
+C ABI) against the oracle and the golden outputs.
+
+Tolerances: attention outputs are bf16, compared at 2e-2 max-abs and 1e-2
+mean-relative (the north-star bf16 tolerance); LSE at 1e-3; q6 bytes and
+scales bit-exact.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import dsqg as odsqg
+from oracle import q6 as oq6
+from tests._golden import load
+
+CASES = ["dsqg_config1", "dsqg_gqa_ragged"]
+
+
+def _np(t):
+    return t.double().numpy() if isinstance(t, torch.Tensor) else np.asarray(t)
+
+
+def _oracle(g, round_se=True, k=None, v=None):
+    return odsqg.dsqg_forward(
+        _np(g["q"]), _np(g["k"] if k is None else k), _np(g["v"] if v is None else v), _np(g["pos_bias"]),
+        _np(g["scale_embed"]), _np(g["phase_base"]), _np(g["phase_gain"]), _np(g["y_pre"]), _np(g["z_pre"]),
+        g["offsets"].tolist(), int(g["j_small"]), int(g["plane_shift"]), int(g["query_start"]),
+        round_scale_embed=round_se)
+
+
+def _assert_close(out, ref, tol=2e-2, mean_rel=1e-2):
+    out, ref = np.asarray(out, np.float64), np.asarray(ref, np.float64)
+    err = np.abs(out - ref)
+    assert err.max() <= tol, err.max()
+    assert err.mean() / max(np.abs(ref).mean(), 1e-12) <= mean_rel
+
+
+# ------------------------------------------------------------------ CPU: oracle pinning
+
+@pytest.mark.parametrize("name", CASES)
+def test_oracle_matches_reference_eager(name):
+    g = load(name)
+    out, _ = _oracle(g, round_se=False)
+    assert np.abs(out - _np(g["eager_out"])).max() < 1e-4
+
+
+@pytest.mark.parametrize("name", CASES)
+def test_oracle_matches_reference_triton_interpret(name):
+    g = load(name)
+    out, lse = _oracle(g, round_se=True)
+    ref = _np(g["triton_out"])
+    # The reference's own Triton kernel and eager oracle differ by up to ~one
+    # bf16 step at |x| in [2, 4) (0.0156); the spec tolerance covers both.
+    _assert_close(out, ref)
+    ref_lse = _np(g["triton_lse"])
+    finite = np.isfinite(ref_lse)
+    assert np.array_equal(finite, np.isfinite(lse))
+    # the interpreted kernel carries ~bf16-level score noise (see above)
+    assert np.abs(lse[finite] - ref_lse[finite]).max() < 5e-3
+
+
+def test_oracle_zero_rows_and_causality():
+    g = load("dsqg_config1")
+    out, _ = _oracle(g)
+    assert np.all(out[:, :, 0] == 0.0)  # row 0 has no source (reference :3312)
+    k = _np(g["k"]).copy()
+    v = _np(g["v"]).copy()
+    k[:, :, 100:] += 5.0
+    v[:, :, 100:] -= 3.0
+    out2, _ = _oracle(g, k=k, v=v)
+    assert np.array_equal(out[:, :, :101], out2[:, :, :101])  # row n reads sources < n only
+
+
+def test_q6_oracle_known_answers():
+    x = np.zeros((6, 64), np.float32)
+    x[1, 0] = 31.0                      # amax 31 -> s = 31, code 31
+    x[1, 1] = -15.5                     # -15.5 -> tie -> -16 (RNE)
+    x[1, 2] = 0.5                       # 0.5 -> tie -> 0 (RNE)
+    x[1, 3] = 1.5                       # 1.5 -> 2
+    x[2, :] = np.linspace(-1, 1, 64)
+    x[3, 5] = 1e6                       # scale saturates at fp16 max
+    x[4, 7] = -2.0 ** -20               # tiny scale (fp16 subnormal)
+    x[5, :] = 3.0                       # constant row
+    codes, scales = oq6.pack(x)
+    c = oq6.codes(codes)
+    assert np.all(c[0] == 0) and scales[0] == 0
+    assert scales[1] == np.float16(31.0) and c[1, :4].tolist() == [31, -16, 0, 2]
+    assert c[2, 0] == -31 and c[2, -1] == 31
+    assert scales[3] == np.float16(65504.0) and c[3, 5] == 31
+    assert c[4, 7] == -31
+    assert np.all(c[5] == 31)
+    # byte layout: group 0 of row 1 = u0 | u1<<6 | u2<<12 | u3<<18, little endian
+    u = [31 & 63, -16 & 63, 0, 2]
+    w = u[0] | u[1] << 6 | u[2] << 12 | u[3] << 18
+    assert codes[1, :3].tolist() == [w & 255, (w >> 8) & 255, (w >> 16) & 255]
+    x_hat = oq6.unpack(codes, scales)
+    assert np.all(np.abs(x_hat[2] - x[2]) <= (np.float32(scales[2]) / 31) / 2 + 1e-7)
+
+
+def test_q6_oracle_roundtrip_bound():
+    rng = np.random.default_rng(0)
+    x = rng.standard_normal((200, 64)).astype(np.float32)
+    codes, scales = oq6.pack(x)
+    err = np.abs(oq6.unpack(codes, scales) - x)
+    bound = scales.astype(np.float32)[:, None] / 31 * 0.5 + np.abs(x) * 2e-3  # fp16 scale rounding
+    assert np.all(err <= bound)
+
+
+# ------------------------------------------------------------------ GPU parity
+
+def _gpu_case(g):
+    dev = torch.device("cuda")
+    return {key: (val.to(dev) if isinstance(val, torch.Tensor) else val) for key, val in g.items()}
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", CASES)
+def test_kernel_bf16_kv_matches_reference(name):
+    from dwarf_v2_b200.dsqg_attention_v22 import dsqg_attention_v18_grouped
+
+    g = load(name)
+    c = _gpu_case(g)
+    js, jl = int(g["j_small"]), int(g["j_large"])
+    empty = torch.empty(0, dtype=torch.int32, device="cuda")
+    out = dsqg_attention_v18_grouped(c["q"], c["k"], c["v"], c["pos_bias"], c["scale_embed"], c["phase_base"],
+                                     c["phase_gain"], c["y_pre"], c["z_pre"], js + jl, js, jl, c["offsets"],
+                                     empty, empty, empty, empty, empty, 3, 0, False, 0,
+                                     int(g["plane_shift"]), int(g["query_start"]))
+    torch.cuda.synchronize()
+    out = out.float().cpu().numpy()
+    _assert_close(out, _np(g["triton_out"]))
+    _assert_close(out, _oracle(g)[0])
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", CASES)
+def test_kernel_q6_kv_matches_oracle_on_dequantised_cache(name):
+    from dwarf_v2_b200.dsqg_attention_v22 import dsqg_attention_q6
+    from dwarf_v2_b200.q6 import q6_pack
+
+    g = load(name)
+    c = _gpu_case(g)
+    kc, ks = q6_pack(c["k"])
+    vc, vs = q6_pack(c["v"])
+    out, lse = dsqg_attention_q6(c["q"], kc, ks, vc, vs, c["pos_bias"], c["scale_embed"], c["phase_base"],
+                                 c["phase_gain"], c["y_pre"], c["z_pre"], c["offsets"], int(g["j_small"]),
+                                 int(g["j_large"]), int(g["plane_shift"]), int(g["query_start"]), return_lse=True)
+    torch.cuda.synchronize()
+    k_hat = oq6.unpack(kc.cpu().numpy(), ks.cpu().numpy())
+    v_hat = oq6.unpack(vc.cpu().numpy(), vs.cpu().numpy())
+    ref, ref_lse = _oracle(g, k=k_hat, v=v_hat)
+    _assert_close(out.float().cpu().numpy(), ref)
+    lse = lse.cpu().numpy()
+    fin = np.isfinite(ref_lse)
+    assert np.array_equal(fin, np.isfinite(lse))
+    assert np.abs(lse[fin] - ref_lse[fin]).max() < 1e-3
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("shape,dtype", [((2, 3, 37, 64), torch.bfloat16), ((1, 8, 2048, 64), torch.bfloat16),
+                                         ((3, 2, 11, 64), torch.float32)])
+def test_q6_pack_unpack_bit_exact(shape, dtype):
+    from dwarf_v2_b200.q6 import q6_pack, q6_unpack
+
+    gen = torch.Generator().manual_seed(7)
+    x = (torch.randn(shape, generator=gen) * torch.rand(shape[:-1] + (1,), generator=gen) * 4).to(dtype)
+    x[0, 0, 0] = 0.0                       # zero row
+    x[0, 0, 1, 3] = 1e6 if dtype == torch.float32 else 3e5  # saturated scale
+    codes, scales = q6_pack(x.cuda())
+    ref_codes, ref_scales = oq6.pack(x.float().numpy())
+    assert np.array_equal(codes.cpu().numpy(), ref_codes)
+    assert np.array_equal(scales.cpu().numpy().view(np.uint16), ref_scales.view(np.uint16))
+    x_hat = q6_unpack(codes, scales).cpu().numpy()
+    assert np.array_equal(x_hat.view(np.uint32), oq6.unpack(ref_codes, ref_scales).view(np.uint32))
+    # strided input (a head view of a projection output) packs identically
+    wide = torch.zeros(shape[0], shape[2], shape[1], 2, 64, dtype=dtype)
+    wide[:, :, :, 1] = x.permute(0, 2, 1, 3)
+    view = wide.cuda()[:, :, :, 1].permute(0, 2, 1, 3)
+    c2, s2 = q6_pack(view)
+    assert torch.equal(c2, codes) and torch.equal(s2, scales)
+
+
+@pytest.mark.gpu
+def test_prep_kernel_matches_oracle_probes_and_q6():
+    from dwarf_v2_b200.dsqg_attention_v22 import _orthogonal_phase_probes, dsqg_prep
+
+    gen = torch.Generator().manual_seed(9)
+    qkvg = torch.randn(2, 77, 4 * 192, generator=gen).to(torch.bfloat16)
+    split = qkvg.cuda().view(2, 77, 4, 3, 64)
+    q, k, v = (split[:, :, i].permute(0, 2, 1, 3) for i in range(3))
+    qp, kp = _orthogonal_phase_probes(4, 64, 6)
+    qp = qp + 0.1 * torch.randn(4, 64, generator=gen)
+    y, z, cache = dsqg_prep(q, k, v, torch.nn.functional.normalize(qp, dim=-1).cuda(),
+                            torch.nn.functional.normalize(kp, dim=-1).cuda(), pack_q6=True)
+    torch.cuda.synchronize()
+    y_ref = odsqg.probe_projection(q.float().cpu().numpy(), qp.numpy())
+    z_ref = odsqg.probe_projection(k.float().cpu().numpy(), kp.numpy())
+    assert np.abs(y.cpu().numpy() - y_ref).max() < 1e-5
+    assert np.abs(z.cpu().numpy() - z_ref).max() < 1e-5
+    kc, ks, vc, vs = cache
+    rc, rs = oq6.pack(k.float().cpu().numpy())
+    assert np.array_equal(kc.cpu().numpy(), rc) and np.array_equal(ks.cpu().numpy().view(np.uint16), rs.view(np.uint16))
+    rc, rs = oq6.pack(v.float().cpu().numpy())
+    assert np.array_equal(vc.cpu().numpy(), rc)
+
+
+@pytest.mark.gpu
+def test_module_matches_reference_module():
+    from dwarf_v2_b200.dsqg_attention_v22 import DSQGAttentionV19
+
+    g = load("dsqg_module_eval")
+    module = DSQGAttentionV19(128, 2, [1, 2, 3, 5, 8, 13, 21, 48, 64, 100], 7, 3, seq_len=160, dropout=0.0,
+                              plane_shift=6).eval()
+    state = {k[len("state."):]: v for k, v in g.items() if k.startswith("state.")}
+    module.load_state_dict(state)
+    module = module.cuda()
+    with torch.no_grad():
+        y = module(g["x"].to(torch.bfloat16).cuda()).float().cpu().numpy()
+    _assert_close(y, _np(g["y"]), tol=2e-2, mean_rel=2e-2)
+
+
+@pytest.mark.gpu
+def test_kernel_config3_full_size_properties():
+    """BASELINE config 3 shapes (B=32, H=8, T=2048, J=96, q6 K/V): oracle on sampled heads."""
+    from dwarf_v2_b200.dsqg_attention_v22 import ALL_OFFSETS, dsqg_attention_q6
+    from dwarf_v2_b200.q6 import q6_pack
+
+    gen = torch.Generator().manual_seed(0)
+    B, H, N = 32, 8, 2048
+    q = torch.randn(B, H, N, 64, generator=gen).to(torch.bfloat16).cuda()
+    k = torch.randn(B, H, N, 64, generator=gen).to(torch.bfloat16).cuda()
+    v = torch.randn(B, H, N, 64, generator=gen).to(torch.bfloat16).cuda()
+    J, js = 96, 17
+    pb = (torch.randn(J, H, generator=gen) * 0.3 - torch.log1p(torch.tensor(ALL_OFFSETS, dtype=torch.float32))[:, None]).cuda()
+    se = (torch.randn(J, 64, generator=gen) * 0.05).cuda()
+    pbase = (torch.randn(J - js, H, 4, generator=gen) * 0.5).cuda()
+    pgain = (torch.randn(J - js, H, 4, generator=gen) * 2.0).cuda()
+    y = torch.randn(B, H, N, 4, generator=gen).cuda() * 0.2
+    z = torch.randn(B, H, N, 4, generator=gen).cuda() * 0.2
+    offs = torch.tensor(ALL_OFFSETS, dtype=torch.int32).cuda()
+    kc, ks = q6_pack(k)
+    vc, vs = q6_pack(v)
+    out = dsqg_attention_q6(q, kc, ks, vc, vs, pb, se, pbase, pgain, y, z, offs, js, J - js, 0, 1)
+    out2 = dsqg_attention_q6(q, kc, ks, vc, vs, pb, se, pbase, pgain, y, z, offs, js, J - js, 0, 1)
+    assert torch.equal(out, out2)  # deterministic
+    assert torch.all(out[:, :, 0] == 0)
+    for b, h in [(0, 0), (17, 5), (31, 7)]:
+        k_hat = oq6.unpack(kc[b:b + 1, h:h + 1].cpu().numpy(), ks[b:b + 1, h:h + 1].cpu().numpy())
+        v_hat = oq6.unpack(vc[b:b + 1, h:h + 1].cpu().numpy(), vs[b:b + 1, h:h + 1].cpu().numpy())
+        ref, _ = odsqg.dsqg_forward(q[b:b + 1, h:h + 1].double().cpu().numpy(), k_hat, v_hat,
+                                    pb[:, h:h + 1].cpu().numpy(), se.cpu().numpy(), pbase[:, h:h + 1].cpu().numpy(),
+                                    pgain[:, h:h + 1].cpu().numpy(), y[b:b + 1, h:h + 1].cpu().numpy(),
+                                    z[b:b + 1, h:h + 1].cpu().numpy(), ALL_OFFSETS, js, 0, 1)
+        _assert_close(out[b:b + 1, h:h + 1].float().cpu().numpy(), ref)
