@@ -186,7 +186,59 @@ class NpciArgs(ctypes.Structure):
         out:ptr, sob:i64, soh:i64, son:i64""")
 
 
+class HisaRepsArgs(ctypes.Structure):
+    _fields_ = _fields("""version:i32, head_dim:i32, chunk_size:i32, B:i64, H:i64, T:i64, key:ptr,
+        skb:i64, skh:i64, skn:i64, lengths:ptr, blend_alpha:f32, reps:ptr""")
+
+
+class HisaSelectArgs(ctypes.Structure):
+    _fields_ = _fields("""version:i32, head_dim:i32, chunk_size:i32, selector_tile:i32, top_k:i32,
+        B:i64, H:i64, T:i64, query:ptr, sqb:i64, sqh:i64, sqn:i64, reps:ptr, lengths:ptr, temperature:f32,
+        top_chunk_idx:ptr, logits:ptr""")
+
+
+class HisaAttnArgs(ctypes.Structure):
+    _fields_ = _fields("""version:i32, head_dim:i32, chunk_size:i32, selector_tile:i32, local_window:i32,
+        k_slots:i32, B:i64, H:i64, T:i64,
+        query:ptr, sqb:i64, sqh:i64, sqn:i64, local_key:ptr, slkb:i64, slkh:i64, slkn:i64,
+        local_value:ptr, slvb:i64, slvh:i64, slvn:i64, global_key:ptr, sgkb:i64, sgkh:i64, sgkn:i64,
+        global_value:ptr, sgvb:i64, sgvh:i64, sgvn:i64, reps:ptr, top_chunk_idx:ptr, route_scale:ptr,
+        lengths:ptr, out:ptr, sob:i64, soh:i64, son:i64, route_out:ptr""")
+
+
+class AddRmsNormArgs(ctypes.Structure):
+    _fields_ = _fields("""version:i32, w_dtype:i32, rows:i64, width:i64, x:ptr, sx:i64, a:ptr, sa:i64,
+        g:ptr, sg:i64, x_out:ptr, sxo:i64, w:ptr, eps:f32, n_out:ptr, sno:i64""")
+
+
+class EmbedRmsNormArgs(ctypes.Structure):
+    _fields_ = _fields("""version:i32, w_dtype:i32, rows:i64, width:i64, vocab:i64, ids:ptr, embedding:ptr,
+        w:ptr, eps:f32, x_out:ptr, n_out:ptr""")
+
+
+class SwigluArgs(ctypes.Structure):
+    _fields_ = _fields("version:i32, rows:i64, hidden:i64, in_:ptr, sin:i64, out:ptr, sout:i64")
+
+
+class GateMulArgs(ctypes.Structure):
+    _fields_ = _fields("version:i32, rows:i64, width:i64, a:ptr, sa:i64, g:ptr, sg:i64, out:ptr, so:i64")
+
+
+class PacketArgs(ctypes.Structure):
+    _fields_ = [("version", c_i32), ("n_scans", c_i32), ("rows", c_i64), ("width", c_i64),
+                ("scans", c_ptr * 3), ("sscan", c_i64), ("mix", c_f32 * 3), ("gate_pre", c_ptr),
+                ("sgp", c_i64), ("out", c_ptr), ("so", c_i64)]
+
+
 _ENTRY_POINTS = {
+    "dwarf_hisa_reps": HisaRepsArgs,
+    "dwarf_hisa_select": HisaSelectArgs,
+    "dwarf_hisa_attn": HisaAttnArgs,
+    "dwarf_add_rmsnorm": AddRmsNormArgs,
+    "dwarf_embed_rmsnorm": EmbedRmsNormArgs,
+    "dwarf_swiglu": SwigluArgs,
+    "dwarf_gate_mul": GateMulArgs,
+    "dwarf_packet": PacketArgs,
     "dwarf_npci_rotate": NpciArgs,
     "dwarf_ema_scan": EmaScanArgs,
     "dwarf_q6_pack": Q6PackArgs,

@@ -48,7 +48,11 @@ __global__ void __launch_bounds__(256) npci_kernel(const NpciParams p) {
 #pragma unroll
     for (int i = 0; i < 4; ++i) x[i] = static_cast<float>(static_cast<T>(x[i] + a[i]));
   }
-  load4<T>(p.d, b * p.sdb + h * p.sdh + n * p.sdn + g * 4, d);
+  if (p.d != nullptr) {
+    load4<T>(p.d, b * p.sdb + h * p.sdh + n * p.sdn + g * 4, d);
+  } else {
+    d[0] = d[1] = d[2] = d[3] = 0.0f;  // no packet: plain (adapter) add
+  }
   float xx = 0.f;
 #pragma unroll
   for (int i = 0; i < 4; ++i) xx += x[i] * x[i];
@@ -87,7 +91,7 @@ extern "C" int dwarf_npci_rotate(const dwarf_npci_rotate_args* a, void* stream) 
   if (a->B < 0 || a->H <= 0 || a->N < 0) return DWARF_ERR_SHAPE;
   const int64_t rows = a->B * a->H * a->N;
   if (rows == 0) return DWARF_OK;
-  if (!a->x || !a->delta || !a->theta || !a->out) return DWARF_ERR_NULL;
+  if (!a->x || !a->out || (a->delta && !a->theta)) return DWARF_ERR_NULL;
   if (!(a->tau > 0.0f)) return DWARF_ERR_VALUE;
   NpciParams p{a->B, a->H, a->N, a->x, a->sxb, a->sxh, a->sxn, a->addend, a->sab, a->sah, a->san,
                a->delta, a->sdb, a->sdh, a->sdn, a->theta, a->tau, a->out, a->sob, a->soh, a->son};

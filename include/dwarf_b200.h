@@ -248,7 +248,8 @@ int dwarf_dsqg_prep(const dwarf_dsqg_prep_args* args, void* stream);
  *   out = active ? cos(angle) x' + sin(angle) |x'| p/max(|p|,1e-20) : x'
  * Math in fp32; x, addend, delta and out share one dtype (bf16 or fp32).
  * The optional addend fuses the HISA low-rank global K/V adapter add
- * (hierarchical_sparse_attn_v18_hisa.py:2579-2591).
+ * (hierarchical_sparse_attn_v18_hisa.py:2579-2591). delta == NULL means no
+ * rotation (out = x + addend).
  * ---------------------------------------------------------------------- */
 typedef struct {
   int32_t version;
@@ -263,6 +264,152 @@ typedef struct {
 } dwarf_npci_rotate_args;
 
 int dwarf_npci_rotate(const dwarf_npci_rotate_args* args, void* stream);
+
+/* ------------------------------------------------------------------------
+ * HISA L3 mixer (production configuration: head_dim 64, chunk 64, selector
+ * tile 16, local window 64, top-k <= 4, enumerate_all token selection).
+ * ---------------------------------------------------------------------- */
+
+/* Chunk representatives: per 64-token chunk of the global keys,
+ * L2-normalise((1-a)*masked mean + a*row of max |k|^2 (first max)), zero for
+ * chunks past the valid length, bf16. Replaces
+ * _completed_chunk_representatives (hierarchical_sparse_attn_v18_hisa.py:171-219)
+ * for representative_mode mean_max_blend (a = blend_alpha; mean: a = 0;
+ * max_l2: a = 1). */
+typedef struct {
+  int32_t version;
+  int32_t head_dim, chunk_size;   /* must be 64, 64                       */
+  int64_t B, H, T;
+  const void* key;                /* bf16 [B, H, T, 64]                   */
+  int64_t skb, skh, skn;
+  const int32_t* lengths;         /* [B] valid lengths                    */
+  float blend_alpha;
+  void* reps;                     /* bf16 [B, H, ceil(T/64), 64] contiguous */
+} dwarf_hisa_reps_args;
+
+/* Strict-causal top-k tile router: anchor q^ = bf16(normalize(q[16 t])),
+ * logits[c] = (q^ . rep_c) / temperature over chunks completed before the
+ * tile starts (and inside the valid length); top-k by value, ties to the
+ * lower chunk index, -1 where no eligible chunk is left. Replaces forward
+ * :2614-2624, _eligibility :222-237 and _build_causal_tile_metadata
+ * :290-397 (hierarchical_sparse_attn_v18_hisa.py). ceil(T/64) <= 128. */
+typedef struct {
+  int32_t version;
+  int32_t head_dim, chunk_size, selector_tile;   /* 64, 64, 16            */
+  int32_t top_k;
+  int64_t B, H, T;
+  const void* query;              /* bf16 [B, H, T, 64]                   */
+  int64_t sqb, sqh, sqn;
+  const void* reps;               /* bf16 [B, H, C, 64]                   */
+  const int32_t* lengths;
+  float temperature;
+  int32_t* top_chunk_idx;         /* [B, H, ceil(T/16), min(top_k, C)]    */
+  float* logits;                  /* optional [B, H, tiles, C] (masked)   */
+} dwarf_hisa_select_args;
+
+/* Fused tile attention: for each query n of tile t, one softmax over
+ *   local keys  [n-64, n-1] of (local_key, local_value), score q.k/8, and
+ *   routed keys of the selected chunks with id < n-64 of (global_key,
+ *   global_value), score q.k/8 + route[n, slot],
+ * where route[n, slot] = bf16((q^_n . rep_c - mean over valid slots) *
+ * route_scale[h]) is computed in-kernel (_selected_route_scores :418-468).
+ * Equals the reference's local lane + global lane + exact LSE merge
+ * (:2424-2461, 1002-1100, 808-835). Output bf16, zero past the valid length. */
+typedef struct {
+  int32_t version;
+  int32_t head_dim, chunk_size, selector_tile, local_window;  /* 64,64,16,64 */
+  int32_t k_slots;                /* last dim of top_chunk_idx (<= 4)     */
+  int64_t B, H, T;
+  const void* query;        int64_t sqb, sqh, sqn;
+  const void* local_key;    int64_t slkb, slkh, slkn;
+  const void* local_value;  int64_t slvb, slvh, slvn;
+  const void* global_key;   int64_t sgkb, sgkh, sgkn;
+  const void* global_value; int64_t sgvb, sgvh, sgvn;
+  const void* reps;               /* bf16 [B, H, C, 64]                   */
+  const int32_t* top_chunk_idx;   /* [B, H, tiles, k_slots]               */
+  const float* route_scale;       /* [H] = softplus(route_prior_raw)      */
+  const int32_t* lengths;
+  void* out;                int64_t sob, soh, son;   /* bf16              */
+  void* route_out;                /* optional bf16 [B, H, T, 4]           */
+} dwarf_hisa_attn_args;
+
+int dwarf_hisa_reps(const dwarf_hisa_reps_args* args, void* stream);
+int dwarf_hisa_select(const dwarf_hisa_select_args* args, void* stream);
+int dwarf_hisa_attn(const dwarf_hisa_attn_args* args, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Row-wise block glue (one warp per row of `width` values, width % 256 == 0
+ * and <= 1024), with the reference's bf16 rounding points
+ * (train/train_dwarf.py:218-240, 260-284, 320-322, 356-364, 439-459).
+ * All activations are bf16, rows addressed by an element stride.
+ * ---------------------------------------------------------------------- */
+
+/* x_out = bf16(x + bf16(a * bf16(sigmoid(g))))  (gate optional: bf16(x + a);
+ * a optional: x_out = x), then n_out = bf16(x_out * rsqrt(mean(x_out^2) +
+ * eps) * w). x_out may alias x; x_out NULL skips the write. */
+typedef struct {
+  int32_t version;
+  int32_t w_dtype;                /* DWARF_F32 or DWARF_BF16              */
+  int64_t rows, width;
+  const void* x;     int64_t sx;
+  const void* a;     int64_t sa;  /* optional addend                      */
+  const void* g;     int64_t sg;  /* optional gate logits for a           */
+  void* x_out;       int64_t sxo; /* optional                             */
+  const void* w;                  /* [width] RMSNorm weight               */
+  float eps;
+  void* n_out;       int64_t sno;
+} dwarf_add_rmsnorm_args;
+
+/* x_out = embedding[ids] (bf16), n_out = RMSNorm(x_out) * w. */
+typedef struct {
+  int32_t version;
+  int32_t w_dtype;
+  int64_t rows, width, vocab;
+  const int64_t* ids;
+  const void* embedding;          /* bf16 [vocab, width] contiguous       */
+  const void* w;
+  float eps;
+  void* x_out;                    /* bf16 [rows, width] contiguous        */
+  void* n_out;                    /* bf16 [rows, width] contiguous        */
+} dwarf_embed_rmsnorm_args;
+
+/* out[r, f] = bf16(bf16(silu(in[r, F + f])) * in[r, f]) -- SwiGLU with the
+ * (up | gate) chunk order of SwiGLUFFN (train/train_dwarf.py:230-240). */
+typedef struct {
+  int32_t version;
+  int64_t rows, hidden;           /* hidden = F                            */
+  const void* in;    int64_t sin; /* bf16 [rows, 2F]                       */
+  void* out;         int64_t sout;/* bf16 [rows, F]                        */
+} dwarf_swiglu_args;
+
+/* out = bf16(a * bf16(sigmoid(g))) elementwise over rows. */
+typedef struct {
+  int32_t version;
+  int64_t rows, width;
+  const void* a;     int64_t sa;
+  const void* g;     int64_t sg;
+  void* out;         int64_t so;
+} dwarf_gate_mul_args;
+
+/* InterferencePacket epilogue (train/train_dwarf.py:264-276):
+ * pooled = bf16 sum_i bf16(mix_i * scan_i) (left to right, bf16 rounding),
+ * packet = bf16(dir * tanh(rms / 0.25) * sigmoid(gate_pre)), dir = pooled *
+ * rsqrt(mean(pooled^2) + 1e-6), rms = sqrt(mean(pooled^2)). */
+typedef struct {
+  int32_t version;
+  int32_t n_scans;                /* 1..3                                  */
+  int64_t rows, width;
+  const void* scans[3];  int64_t sscan;   /* bf16 [rows, width] each       */
+  float mix[3];                   /* softmax(mix_logits) already in bf16   */
+  const void* gate_pre;  int64_t sgp;     /* bf16 gate_proj output          */
+  void* out;             int64_t so;
+} dwarf_packet_args;
+
+int dwarf_add_rmsnorm(const dwarf_add_rmsnorm_args* args, void* stream);
+int dwarf_embed_rmsnorm(const dwarf_embed_rmsnorm_args* args, void* stream);
+int dwarf_swiglu(const dwarf_swiglu_args* args, void* stream);
+int dwarf_gate_mul(const dwarf_gate_mul_args* args, void* stream);
+int dwarf_packet(const dwarf_packet_args* args, void* stream);
 
 #ifdef __cplusplus
 }

@@ -208,9 +208,81 @@ def make_dsqg(with_triton: bool = True) -> None:
     save("dsqg_module_eval", x=x, y=y, **state)
 
 
+def make_hisa() -> None:
+    _import_reference()
+    import torch.nn.functional as F
+
+    import hierarchical_sparse_attn_v18_hisa as ref
+
+    def router(q, gk, lengths, scale):
+        T = q.shape[2]
+        reps = ref._completed_chunk_representatives(gk, chunk_size=64, valid_lengths=lengths,
+                                                    representative_mode="mean_max_blend", blend_alpha=0.5)
+        qn = F.normalize(q.float(), dim=-1, eps=1e-6).to(q.dtype)
+        starts = torch.arange(-(-T // 16)) * 16
+        anchor = qn[:, :, starts.clamp_max(T - 1)]
+        logits = torch.matmul(anchor.float(), reps.float().transpose(-2, -1))
+        meta = ref._build_causal_tile_metadata(anchor, gk, logits, chunk_size=64, top_k_chunks=4,
+                                               top_m_tokens=64, selector_tile_size=16, valid_lengths=lengths,
+                                               canonical_token_order=False, exploration_probability=0.0)
+        route = ref._selected_route_scores(qn, reps, meta, scale)
+        return reps, logits, meta, route
+
+    # Router + lanes on raw Q/K/V: ragged length (5 chunks, last one partial),
+    # per-row valid lengths, distinct local/global K/V.
+    g = torch.Generator().manual_seed(21)
+    B, H, T, D = 2, 2, 300, 64
+    q = (torch.randn(B, H, T, D, generator=g) * 0.5).to(torch.bfloat16)
+    lk = (torch.randn(B, H, T, D, generator=g) * 0.5).to(torch.bfloat16)
+    lv = torch.randn(B, H, T, D, generator=g).to(torch.bfloat16)
+    gk = (lk.float() + 0.3 * torch.randn(B, H, T, D, generator=g)).to(torch.bfloat16)
+    gv = (lv.float() + 0.3 * torch.randn(B, H, T, D, generator=g)).to(torch.bfloat16)
+    lengths = torch.tensor([300, 250], dtype=torch.int32)
+    scale = torch.tensor([0.1, 0.35])
+    reps, logits, meta, route = router(q, gk, lengths, scale)
+    f32 = lambda t: t.float()
+    lo, llse = ref._eager_local_lane(f32(q), f32(lk), f32(lv), lengths, local_window=64, selector_tile_size=16)
+    go, glse = ref._eager_global_lane(f32(q), f32(gk), f32(gv), route.float(), meta, local_window=64)
+    merged, mlse = ref._merge_attention_lanes(lo, llse, go, glse)
+    save("hisa_router_lanes", q=q, local_key=lk, local_value=lv, global_key=gk, global_value=gv,
+         valid_lengths=lengths, route_scale=scale, reps=reps, logits=logits, top_chunk_idx=meta.top_chunk_idx,
+         route=route, merged=merged, merged_lse=mlse)
+
+    # Router only, long enough that top-4 picks among up to 31 completed chunks.
+    g = torch.Generator().manual_seed(22)
+    B, H, T = 1, 4, 2048
+    q = (torch.randn(B, H, T, D, generator=g) * 0.125).to(torch.bfloat16)
+    gk = (torch.randn(B, H, T, D, generator=g) * 0.125).to(torch.bfloat16)
+    lengths = torch.tensor([2048], dtype=torch.int32)
+    reps, logits, meta, route = router(q, gk, lengths, torch.full((H,), 0.1))
+    save("hisa_router_long", q=q, global_key=gk, valid_lengths=lengths, reps=reps, logits=logits,
+         top_chunk_idx=meta.top_chunk_idx, route=route)
+
+    # Whole module (eval, fp32, with an EMA/NPCI kv_inject packet), head_dim 64.
+    torch.manual_seed(4)
+    module = ref.HierarchicalSparseAttentionV16HISACausal(
+        D=128, H=2, hd=64, chunk_size=64, top_k_chunks=4, hisa_top_m_tokens=64, local_window=64,
+        selector_tile_size=16, representative_mode="mean_max_blend", representative_blend_alpha=0.5,
+        route_prior_scale=0.1, global_adapter_rank=16, npci_theta_max=0.25, local_backend="flex").eval()
+    gen = torch.Generator().manual_seed(44)
+    with torch.no_grad():
+        for p in (module.global_k_up.weight, module.global_v_up.weight):
+            p.copy_(torch.randn(p.shape, generator=gen) * 0.05)
+        module.route_prior_raw.copy_(torch.tensor([-1.0, 0.5]))
+        module.npci_theta_k.copy_(torch.tensor([1.5, -0.7]))
+        module.npci_theta_v.copy_(torch.tensor([0.4, 2.0]))
+    x = torch.randn(2, 200, 128, generator=gen).to(torch.bfloat16).float()
+    kd = torch.randn(2, 2, 200, 64, generator=gen) * 0.5
+    vd = torch.randn(2, 2, 200, 64, generator=gen) * 0.5
+    with torch.no_grad():
+        y = module(x, kv_inject=(kd, vd))
+    state = {f"state.{k}": val for k, val in module.state_dict().items()}
+    save("hisa_module_eval", x=x, key_delta=kd, value_delta=vd, y=y, **state)
+
+
 def main(argv: list[str]) -> None:
     which = argv[1] if len(argv) > 1 else "all"
-    makers = {"ema": make_ema, "dsqg": make_dsqg}
+    makers = {"ema": make_ema, "dsqg": make_dsqg, "hisa": make_hisa}
     for name, maker in makers.items():
         if which in ("all", name):
             maker()
