@@ -1,0 +1,433 @@
+"""HISA L3 mixer on B200: drop-in for the reference ``kernels/hierarchical_sparse_attn_v18_hisa.py``.
+
+Public surface kept from the reference (same names, arguments, validation and
+state_dict layout): ``HierarchicalSparseAttentionV16HISACausal`` (aliases V17,
+V18) with ``forward(x, kv_inject=None, *, valid_lengths=None,
+return_metadata=False, return_auxiliary=False)`` and ``prepare_runtime``;
+``HISAMetadata``; ``HISASelectionCapture``.
+
+Device pipeline of one forward (eval mode):
+qkvg GEMM and the rank-16 adapter GEMMs (cuBLAS) -> ``dwarf_npci_rotate``
+(adapter add + EMA/NPCI rotation of global K and V, one pass each) ->
+``dwarf_hisa_reps`` (chunk representatives) -> ``dwarf_hisa_select`` (tile
+anchor logits, strict-causal top-k) -> ``dwarf_hisa_attn`` (route prior, local
+window and routed chunks in one tensor-core softmax) -> W_o GEMM ->
+``dwarf_gate_mul``.
+
+Supported configuration: head_dim 64, chunk 64, selector tile 16, local
+window 64, top_k <= 4, hisa_top_m_tokens >= chunk (the reference's
+``enumerate_all`` path), representative modes mean_max_blend / mean / max_l2.
+Metadata requested with ``return_metadata=True`` carries the routed chunk
+indices with ``enumerate_all=True`` (every token of a routed chunk is used,
+the same token set the reference's canonical listing names). Training mode
+(exploration slot, router auxiliary loss) raises: this is a forward engine.
+"""
+
+from __future__ import annotations
+
+import math
+import os
+from dataclasses import dataclass
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from . import _lib
+from .glue import gate_mul
+from .npci import npci_rotate_cuda
+
+_HD = 64
+_CHUNK = 64
+_TILE = 16
+_WINDOW = 64
+_MAX_TOP_K = 4
+
+
+def _next_pow2(value: int) -> int:
+    return 1 if value <= 1 else 1 << (int(value) - 1).bit_length()
+
+
+def _is_power_of_two(value: int) -> bool:
+    return value > 0 and value & (value - 1) == 0
+
+
+def _inverse_softplus(value: float) -> float:
+    value = float(value)
+    if not math.isfinite(value) or value <= 0:
+        raise ValueError("softplus target must be finite and positive")
+    return math.log(math.expm1(value))
+
+
+@dataclass(frozen=True)
+class HISAMetadata:
+    top_chunk_idx: torch.Tensor          # int32 [B,H,T,K]
+    token_idx: torch.Tensor              # empty or int32 [B,H,T,K,M]
+    token_scores: torch.Tensor           # empty or fp32 [B,H,T,K,M]
+    tile_starts: torch.Tensor            # int32 [T]
+    valid_lengths: torch.Tensor          # int32 [B]
+    chunk_size: int
+    selector_tile_size: int
+    enumerate_all: bool
+
+
+@dataclass(frozen=True)
+class HISASelectionCapture:
+    anchor_logits: torch.Tensor
+    metadata: HISAMetadata
+    auxiliary_loss: torch.Tensor
+
+
+def _as_valid_lengths(lengths, *, batch_size: int, seq_len: int, device) -> torch.Tensor:
+    """int32 [B] valid lengths (reference :82-96), range-checked on the host."""
+    if lengths is None:
+        return torch.full((batch_size,), seq_len, dtype=torch.int32, device=device)
+    result = lengths.to(device=device, dtype=torch.int32).reshape(-1)
+    if result.numel() != batch_size:
+        raise ValueError(f"valid_lengths must contain {batch_size} entries")
+    if not bool(((result >= 0) & (result <= seq_len)).all()):
+        raise ValueError(f"valid_lengths must be in [0,{seq_len}]")
+    return result.contiguous()
+
+
+def _strides3(t):
+    return t.stride(0), t.stride(1), t.stride(2)
+
+
+def chunk_representatives(global_key: torch.Tensor, lengths: torch.Tensor, *, blend_alpha: float) -> torch.Tensor:
+    """``dwarf_hisa_reps``: bf16 [B,H,ceil(T/64),64] normalised chunk representatives."""
+    B, H, T, D = global_key.shape
+    C = max(1, -(-T // _CHUNK))
+    reps = torch.empty(B, H, C, D, dtype=torch.bfloat16, device=global_key.device)
+    args = _lib.HisaRepsArgs(version=_lib.ABI_VERSION, head_dim=D, chunk_size=_CHUNK, B=B, H=H, T=T,
+                             key=global_key.data_ptr(), lengths=lengths.data_ptr(), blend_alpha=float(blend_alpha),
+                             reps=reps.data_ptr())
+    args.skb, args.skh, args.skn = _strides3(global_key)
+    _lib.call("dwarf_hisa_reps", args, global_key.device)
+    return reps
+
+
+def select_chunks(query: torch.Tensor, reps: torch.Tensor, lengths: torch.Tensor, *, top_k: int,
+                  temperature: float, want_logits: bool = False):
+    """``dwarf_hisa_select``: (top_chunk_idx int32 [B,H,tiles,K], optional masked logits)."""
+    B, H, T, D = query.shape
+    C = reps.shape[2]
+    tiles = -(-T // _TILE)
+    k_slots = min(int(top_k), C)
+    top = torch.empty(B, H, tiles, k_slots, dtype=torch.int32, device=query.device)
+    logits = torch.empty(B, H, tiles, C, dtype=torch.float32, device=query.device) if want_logits else None
+    args = _lib.HisaSelectArgs(version=_lib.ABI_VERSION, head_dim=D, chunk_size=_CHUNK, selector_tile=_TILE,
+                               top_k=int(top_k), B=B, H=H, T=T, query=query.data_ptr(), reps=reps.data_ptr(),
+                               lengths=lengths.data_ptr(), temperature=float(temperature),
+                               top_chunk_idx=top.data_ptr(), logits=None if logits is None else logits.data_ptr())
+    args.sqb, args.sqh, args.sqn = _strides3(query)
+    _lib.call("dwarf_hisa_select", args, query.device)
+    return top, logits
+
+
+def tile_attention(query, local_key, local_value, global_key, global_value, reps, top, route_scale, lengths, *,
+                   out: torch.Tensor | None = None, want_route: bool = False):
+    """``dwarf_hisa_attn``: fused route prior + local window + routed chunks."""
+    B, H, T, D = query.shape
+    if out is None:
+        out = torch.empty(B, H, T, D, dtype=torch.bfloat16, device=query.device)
+    route = torch.empty(B, H, T, _MAX_TOP_K, dtype=torch.bfloat16, device=query.device) if want_route else None
+    args = _lib.HisaAttnArgs(version=_lib.ABI_VERSION, head_dim=D, chunk_size=_CHUNK, selector_tile=_TILE,
+                             local_window=_WINDOW, k_slots=top.shape[-1], B=B, H=H, T=T,
+                             query=query.data_ptr(), local_key=local_key.data_ptr(),
+                             local_value=local_value.data_ptr(), global_key=global_key.data_ptr(),
+                             global_value=global_value.data_ptr(), reps=reps.data_ptr(),
+                             top_chunk_idx=top.data_ptr(), route_scale=route_scale.data_ptr(),
+                             lengths=lengths.data_ptr(), out=out.data_ptr(),
+                             route_out=None if route is None else route.data_ptr())
+    args.sqb, args.sqh, args.sqn = _strides3(query)
+    args.slkb, args.slkh, args.slkn = _strides3(local_key)
+    args.slvb, args.slvh, args.slvn = _strides3(local_value)
+    args.sgkb, args.sgkh, args.sgkn = _strides3(global_key)
+    args.sgvb, args.sgvh, args.sgvn = _strides3(global_value)
+    args.sob, args.soh, args.son = _strides3(out)
+    _lib.call("dwarf_hisa_attn", args, query.device)
+    return out, route
+
+
+def hisa_attention(query, local_key, local_value, global_key, global_value, route_scale, valid_lengths=None, *,
+                   top_k: int = 4, temperature: float = 1.0, blend_alpha: float = 0.5, want_route: bool = False):
+    """Router + fused attention on head tensors [B,H,T,64] (bf16).
+
+    Returns (output bf16 [B,H,T,64], top_chunk_idx, route bf16 [B,H,T,4] or None).
+    """
+    _lib.require_cuda(query, local_key, local_value, global_key, global_value)
+    if torch.is_grad_enabled() and query.requires_grad:
+        raise NotImplementedError("dwarf_v2_b200 is a forward (inference) engine; run under torch.no_grad()")
+    B, H, T, D = query.shape
+    if D != _HD:
+        raise ValueError(f"the B200 HISA kernels support head_dim 64, got {D}")
+    if -(-T // _CHUNK) > 128:
+        raise ValueError("the B200 HISA router supports up to 128 chunks (T <= 8192)")
+    lengths = _as_valid_lengths(valid_lengths, batch_size=B, seq_len=T, device=query.device)
+    scale = route_scale.detach().reshape(-1).to(device=query.device, dtype=torch.float32).contiguous()
+    reps = chunk_representatives(global_key, lengths, blend_alpha=blend_alpha)
+    top, _ = select_chunks(query, reps, lengths, top_k=top_k, temperature=temperature)
+    out, route = tile_attention(query, local_key, local_value, global_key, global_value, reps, top, scale, lengths,
+                                want_route=want_route)
+    return out, top, route
+
+
+def _magnitude_aware_rotate(x, delta, theta_h, *, strength_tau: float = 0.25):
+    """Norm-preserving tangent rotation (reference :99-125), one CUDA kernel."""
+    return npci_rotate_cuda(x, delta, theta_h, strength_tau=strength_tau)
+
+
+def _to_heads(t: torch.Tensor, batch: int, seq_len: int, heads: int, head_dim: int) -> torch.Tensor:
+    return t.reshape(batch, seq_len, heads, head_dim).permute(0, 2, 1, 3)
+
+
+class HierarchicalSparseAttentionV16HISACausal(nn.Module):
+    """HISA V18 strict-causal L3 mixer with the reference's parameters (reference :2183-2787)."""
+
+    def __init__(self, D: int, H: int, hd: int, num_chunks: int = 32, top_k_chunks: int = 4,
+                 hisa_top_m_tokens: int = 64, *, chunk_size: int | None = None, local_window: int | None = None,
+                 selector_tile_size: int | None = None, temperature: float = 1.0, route_prior_scale: float = 0.1,
+                 backend: str | None = None, token_selection_mode: str | None = None,
+                 representative_mode: str = "mean_max_blend", representative_blend_alpha: float = 0.5,
+                 exploration_probability: float = 0.05, route_aux_weight: float = 0.01,
+                 route_aux_samples: int = 4, route_aux_temperature: float = 1.0, global_adapter_rank: int = 16,
+                 npci_theta_max: float = 0.25, max_seq_len: int | None = None, local_backend: str = "flex",
+                 collect_routing_diagnostics: bool | None = None, diagnostic_max_queries: int | None = None) -> None:
+        super().__init__()
+        D, H, hd = int(D), int(H), int(hd)
+        if D != H * hd:
+            raise ValueError(f"D={D} must equal H*hd={H * hd}")
+        if not _is_power_of_two(hd):
+            raise ValueError("HISA head dimension must be a power of two")
+        if top_k_chunks < 1 or hisa_top_m_tokens < 1:
+            raise ValueError("top_k_chunks and hisa_top_m_tokens must be positive")
+        if not math.isfinite(temperature) or temperature <= 0:
+            raise ValueError("temperature must be finite and positive")
+        if not math.isfinite(route_prior_scale) or route_prior_scale <= 0:
+            raise ValueError("route_prior_scale must be finite and positive")
+        if not 0.0 <= exploration_probability <= 1.0:
+            raise ValueError("exploration_probability must be in [0,1]")
+        if route_aux_weight < 0 or route_aux_samples < 0:
+            raise ValueError("route auxiliary weight/samples must be non-negative")
+        if not math.isfinite(route_aux_temperature) or route_aux_temperature <= 0:
+            raise ValueError("route_aux_temperature must be finite and positive")
+        if representative_mode not in {"max_l2", "mean", "mean_max_blend", "top2_blend"}:
+            raise ValueError("unsupported representative_mode")
+        if not 0.0 <= representative_blend_alpha <= 1.0:
+            raise ValueError("representative_blend_alpha must be in [0,1]")
+        if global_adapter_rank < 0:
+            raise ValueError("global_adapter_rank must be non-negative")
+        if not math.isfinite(npci_theta_max) or npci_theta_max <= 0:
+            raise ValueError("npci_theta_max must be finite and positive")
+        local_backend = str(local_backend).lower()
+        if local_backend not in {"flex", "combined"}:
+            raise ValueError("local_backend must be flex or combined")
+        if max_seq_len is not None and int(max_seq_len) < 1:
+            raise ValueError("max_seq_len must be positive when supplied")
+        self.D, self.H, self.num_heads, self.hd = D, H, H, hd
+        self.legacy_num_chunks = int(num_chunks)
+        self.chunk_size = int(chunk_size if chunk_size is not None else os.getenv("DWARF_HISA_CHUNK_SIZE", "64"))
+        self.local_window = int(local_window if local_window is not None
+                                else os.getenv("DWARF_HISA_V16_LOCAL_WINDOW", "64"))
+        self.selector_tile_size = int(selector_tile_size if selector_tile_size is not None
+                                      else os.getenv("DWARF_HISA_V16_SELECTOR_TILE", "16"))
+        if self.chunk_size < 1 or self.local_window < 1 or self.selector_tile_size < 1:
+            raise ValueError("chunk_size, local_window, and selector_tile_size must be positive")
+        self.top_k_chunks = int(top_k_chunks)
+        self.hisa_top_m_tokens = int(hisa_top_m_tokens)
+        self.temperature = float(temperature)
+        self.backend = (backend or os.getenv("DWARF_HISA_V16_BACKEND", "auto")).lower()
+        if self.backend not in {"auto", "eager", "triton"}:
+            raise ValueError("backend must be auto, eager, or triton")
+        self.token_selection_mode = (token_selection_mode
+                                     or os.getenv("DWARF_HISA_V16_TOKEN_SELECTION", "auto")).lower()
+        if self.token_selection_mode not in {"auto", "canonical"}:
+            raise ValueError("token_selection_mode must be auto or canonical")
+        self.representative_mode = representative_mode
+        self.representative_blend_alpha = float(representative_blend_alpha)
+        self.exploration_probability = float(exploration_probability)
+        self.route_aux_weight = float(route_aux_weight)
+        self.route_aux_samples = int(route_aux_samples)
+        self.route_aux_temperature = float(route_aux_temperature)
+        self.global_adapter_rank = int(global_adapter_rank)
+        self.npci_theta_max = float(npci_theta_max)
+        self.max_seq_len = None if max_seq_len is None else int(max_seq_len)
+        self.local_backend = local_backend
+        self.triton_block_q = int(os.getenv("DWARF_HISA_V16_BLOCK_Q", "16"))
+        self.backward_impl = os.getenv("DWARF_HISA_V16_BWD", "atomic_masked").lower()
+        if self.backward_impl not in {"atomic", "atomic_masked"}:
+            raise ValueError("DWARF_HISA_V16_BWD must be atomic or atomic_masked")
+        if collect_routing_diagnostics is None:
+            collect_routing_diagnostics = os.getenv("DWARF_HISA_V16_ROUTING_DIAGNOSTICS", "0") == "1"
+        self.collect_routing_diagnostics = bool(collect_routing_diagnostics)
+        self.diagnostic_max_queries = int(diagnostic_max_queries or 8)
+        if self.diagnostic_max_queries < 1:
+            raise ValueError("diagnostic_max_queries must be positive")
+
+        self.qkvg_proj = nn.Linear(D, 4 * D, bias=True)
+        self.W_o = nn.Linear(D, D, bias=False)
+        with torch.no_grad():
+            self.qkvg_proj.bias.zero_()
+        if self.global_adapter_rank:
+            rank = self.global_adapter_rank
+            self.global_k_down = nn.Linear(D, rank, bias=False)
+            self.global_k_up = nn.Linear(rank, D, bias=False)
+            self.global_v_down = nn.Linear(D, rank, bias=False)
+            self.global_v_up = nn.Linear(rank, D, bias=False)
+            nn.init.zeros_(self.global_k_up.weight)
+            nn.init.zeros_(self.global_v_up.weight)
+        else:
+            self.global_k_down = self.global_k_up = self.global_v_down = self.global_v_up = None
+        self.route_prior_raw = nn.Parameter(torch.full((H,), _inverse_softplus(route_prior_scale)))
+        raw_theta = math.atanh(min(0.01 / max(self.npci_theta_max, 1e-6), 0.99))
+        self.npci_theta_k = nn.Parameter(torch.full((H,), raw_theta))
+        self.npci_theta_v = nn.Parameter(torch.full((H,), raw_theta))
+        self._routing_entropy: torch.Tensor | float = float("nan")
+        self._routing_diagnostics: dict[str, torch.Tensor] = {}
+        self.hisa_evidence_capture: HISASelectionCapture | None = None
+        self._routing_auxiliary_loss: torch.Tensor | None = None
+        self._last_token_selection_path = ""
+
+    @property
+    def route_prior_scale(self) -> torch.Tensor:
+        return F.softplus(self.route_prior_raw)
+
+    def routing_auxiliary_loss(self, *, clear: bool = False) -> torch.Tensor | None:
+        value = self._routing_auxiliary_loss
+        if clear:
+            self._routing_auxiliary_loss = None
+        return value
+
+    def semantic_config(self) -> dict[str, object]:
+        return {
+            "implementation": "hisa-v18-split-lse",
+            "chunk_size": self.chunk_size,
+            "top_k_chunks": self.top_k_chunks,
+            "top_m_tokens": self.hisa_top_m_tokens,
+            "local_window": self.local_window,
+            "selector_tile_size": self.selector_tile_size,
+            "temperature": self.temperature,
+            "representative_mode": self.representative_mode,
+            "representative_blend_alpha": self.representative_blend_alpha,
+            "exploration_probability": self.exploration_probability,
+            "route_aux_weight": self.route_aux_weight,
+            "route_aux_samples": self.route_aux_samples,
+            "route_aux_temperature": self.route_aux_temperature,
+            "global_adapter_rank": self.global_adapter_rank,
+            "npci_theta_max": self.npci_theta_max,
+            "token_selection_mode": self.token_selection_mode,
+            "selected_route_scoring": "tile_gather",
+            "lane_merge": "exact_lse",
+        }
+
+    def execution_config(self) -> dict[str, object]:
+        return {
+            "backend": self.backend,
+            "local_backend": "dwarf_hisa_attn",
+            "triton_block_q": self.triton_block_q,
+            "backward_impl": self.backward_impl,
+            "collect_routing_diagnostics": self.collect_routing_diagnostics,
+            "flex_attention_available": False,
+            "flex_lse_api": "none",
+        }
+
+    def prepare_runtime(self, device, seq_len: int | None = None) -> None:
+        """Nothing to prebuild: the fused kernel needs no block mask."""
+        return None
+
+    def reset_global_adapters_(self) -> None:
+        if self.global_adapter_rank:
+            nn.init.zeros_(self.global_k_up.weight)
+            nn.init.zeros_(self.global_v_up.weight)
+
+    def _check_supported(self) -> None:
+        if (self.hd, self.chunk_size, self.selector_tile_size, self.local_window) != (_HD, _CHUNK, _TILE, _WINDOW):
+            raise NotImplementedError(
+                "the B200 HISA kernels implement head_dim 64, chunk 64, selector tile 16, local window 64")
+        if self.top_k_chunks > _MAX_TOP_K:
+            raise NotImplementedError("the B200 HISA kernels route to at most 4 chunks per tile")
+        if self.hisa_top_m_tokens < self.chunk_size:
+            raise NotImplementedError("the B200 HISA kernels implement top_m_tokens >= chunk_size (enumerate_all)")
+        if self.representative_mode == "top2_blend":
+            raise NotImplementedError("representative_mode='top2_blend' is not implemented on B200")
+        if self.backend == "eager":
+            raise NotImplementedError("the B200 engine has no eager backend")
+        if self.training:
+            raise NotImplementedError("the B200 engine is a forward engine; call .eval() (no exploration/aux loss)")
+
+    @property
+    def _blend_alpha(self) -> float:
+        return {"mean": 0.0, "max_l2": 1.0}.get(self.representative_mode, self.representative_blend_alpha)
+
+    def global_kv(self, x, local_key, local_value, kv_inject):
+        """Global K/V = local + low-rank adapter, NPCI-rotated toward the packet deltas when given."""
+        B, T, _ = x.shape
+        act = torch.bfloat16
+        addend_k = addend_v = None
+        if self.global_adapter_rank:
+            r = self.global_adapter_rank
+            down = F.linear(x, torch.cat((self.global_k_down.weight, self.global_v_down.weight)).to(act))
+            addend_k = _to_heads(F.linear(down[..., :r], self.global_k_up.weight.to(act)), B, T, self.H, self.hd)
+            addend_v = _to_heads(F.linear(down[..., r:], self.global_v_up.weight.to(act)), B, T, self.H, self.hd)
+        kd = vd = None
+        if kv_inject is not None:
+            kd, vd = kv_inject
+            if kd.shape != local_key.shape or vd.shape != local_value.shape:
+                raise ValueError("kv_inject must contain [B,H,N,HD] tensors")
+        if addend_k is None and kd is None:
+            return local_key, local_value
+        theta_k = self.npci_theta_max * torch.tanh(self.npci_theta_k.detach().float())
+        theta_v = self.npci_theta_max * torch.tanh(self.npci_theta_v.detach().float())
+        gk = npci_rotate_cuda(local_key, kd, theta_k, addend=addend_k)
+        gv = npci_rotate_cuda(local_value, vd, theta_v, addend=addend_v)
+        return gk, gv
+
+    def forward(self, x: torch.Tensor, kv_inject=None, *, valid_lengths=None, return_metadata: bool = False,
+                return_auxiliary: bool = False):
+        self._check_supported()
+        _lib.require_cuda(x)
+        if torch.is_grad_enabled() and (x.requires_grad or any(p.requires_grad for p in self.parameters())):
+            raise NotImplementedError("dwarf_v2_b200 is a forward (inference) engine; run under torch.no_grad()")
+        self.hisa_evidence_capture = None
+        self._routing_auxiliary_loss = None
+        B, T, _ = x.shape
+        if -(-T // self.chunk_size) > 128:
+            raise ValueError("the B200 HISA router supports up to 128 chunks (T <= 8192)")
+        act = torch.bfloat16
+        xb = x if x.dtype == act else x.to(act)
+        lengths = _as_valid_lengths(
+            valid_lengths if valid_lengths is not None else getattr(self, "_causal_control_valid_lengths", None),
+            batch_size=B, seq_len=T, device=x.device)
+        qkvg = F.linear(xb, self.qkvg_proj.weight.to(act), self.qkvg_proj.bias.to(act))
+        q, k, v, gate = qkvg.split(self.D, dim=-1)
+        query = _to_heads(q, B, T, self.H, self.hd)
+        local_key = _to_heads(k, B, T, self.H, self.hd)
+        local_value = _to_heads(v, B, T, self.H, self.hd)
+        global_key, global_value = self.global_kv(xb, local_key, local_value, kv_inject)
+        attended = torch.empty(B, T, self.D, dtype=act, device=x.device)
+        reps = chunk_representatives(global_key, lengths, blend_alpha=self._blend_alpha)
+        top, _ = select_chunks(query, reps, lengths, top_k=self.top_k_chunks, temperature=self.temperature)
+        scale = self.route_prior_scale.detach().float().contiguous()
+        tile_attention(query, local_key, local_value, global_key, global_value, reps, top, scale, lengths,
+                       out=_to_heads(attended, B, T, self.H, self.hd))
+        self._last_token_selection_path = "enumerate_all"
+        output = gate_mul(F.linear(attended, self.W_o.weight.to(act)), gate)
+        if x.dtype != act:
+            output = output.to(x.dtype)
+        auxiliary = output.new_zeros(())
+        if return_metadata:
+            tiles = top.shape[2]
+            metadata = HISAMetadata(
+                top_chunk_idx=top,
+                token_idx=torch.empty(0, dtype=torch.int32, device=x.device),
+                token_scores=torch.empty(0, dtype=torch.float32, device=x.device),
+                tile_starts=torch.arange(tiles, device=x.device, dtype=torch.int32) * self.selector_tile_size,
+                valid_lengths=lengths, chunk_size=self.chunk_size, selector_tile_size=self.selector_tile_size,
+                enumerate_all=True)
+            return (output, metadata, auxiliary) if return_auxiliary else (output, metadata)
+        return (output, auxiliary) if return_auxiliary else output
+
+
+HierarchicalSparseAttentionV17HISACausal = HierarchicalSparseAttentionV16HISACausal
+HierarchicalSparseAttentionV18HISACausal = HierarchicalSparseAttentionV16HISACausal

@@ -15,7 +15,7 @@ import torch
 from . import _lib
 
 
-def npci_rotate_cuda(x: torch.Tensor, x_delta: torch.Tensor, theta_h: torch.Tensor, *,
+def npci_rotate_cuda(x: torch.Tensor, x_delta: torch.Tensor | None, theta_h: torch.Tensor, *,
                      strength_tau: float = 0.25, addend: torch.Tensor | None = None,
                      out: torch.Tensor | None = None) -> torch.Tensor:
     tau = float(strength_tau)
@@ -23,13 +23,13 @@ def npci_rotate_cuda(x: torch.Tensor, x_delta: torch.Tensor, theta_h: torch.Tens
         raise ValueError("strength_tau must be finite and positive")
     if x.ndim != 4 or x.shape[-1] != 64:
         raise ValueError(f"npci rotation expects [B,H,N,64] rows, got {tuple(x.shape)}")
-    if x_delta.shape != x.shape or (addend is not None and addend.shape != x.shape):
+    if (x_delta is not None and x_delta.shape != x.shape) or (addend is not None and addend.shape != x.shape):
         raise ValueError("x, delta (and addend) must share one shape")
     _lib.require_cuda(x, x_delta, theta_h, addend)
     dtype = x.dtype
     if dtype not in (torch.bfloat16, torch.float32):
         raise TypeError(f"npci rotation supports bfloat16/float32, got {dtype}")
-    delta = x_delta if x_delta.dtype == dtype else x_delta.to(dtype)
+    delta = x if x_delta is None else (x_delta if x_delta.dtype == dtype else x_delta.to(dtype))
     if addend is not None and addend.dtype != dtype:
         addend = addend.to(dtype)
     theta = theta_h.detach().reshape(-1).to(device=x.device, dtype=torch.float32).contiguous()
@@ -45,6 +45,8 @@ def npci_rotate_cuda(x: torch.Tensor, x_delta: torch.Tensor, theta_h: torch.Tens
                          out=out.data_ptr(), sob=out.stride(0), soh=out.stride(1), son=out.stride(2))
     if addend is not None:
         args.addend, args.sab, args.sah, args.san = addend.data_ptr(), addend.stride(0), addend.stride(1), addend.stride(2)
+    if x_delta is None:  # no packet: out = x (+ addend), no rotation
+        args.delta = None
     for t in (x, delta, addend, out):
         if t is not None and t.stride(-1) != 1:
             raise ValueError("npci rotation needs a unit stride on the head dimension")

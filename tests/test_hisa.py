@@ -1,0 +1,155 @@
+"""HISA L3 mixer: router (representatives, top-k, route prior) and fused tile attention.
+
+CPU: the numpy oracle is pinned to the reference's own eager functions
+(golden fixtures from tests/golden/make_golden.py). GPU: the CUDA kernels
+(dwarf_hisa_reps / dwarf_hisa_select / dwarf_hisa_attn / dwarf_npci_rotate,
+through the C ABI) against the oracle and the fixtures.
+
+Tolerances: chunk indices bit-exact (ties to the lower index);
+representatives and route priors bit-exact against the oracle (which uses the
+kernels' summation order) and within one bf16 step of the reference;
+attention outputs (bf16) 2e-2 max-abs / 1e-2 mean-relative.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import hisa as oh
+from tests._golden import load
+
+
+def f(t):
+    return t.float().numpy()
+
+
+def _close(out, ref, tol=2e-2, mean_rel=1e-2):
+    err = np.abs(np.asarray(out, np.float64) - np.asarray(ref, np.float64))
+    assert err.max() <= tol, err.max()
+    assert err.mean() / max(np.abs(ref).mean(), 1e-12) <= mean_rel
+
+
+def _one_bf16_step(a, b):
+    a, b = np.asarray(a, np.float64), np.asarray(b, np.float64)
+    return np.all(np.abs(a - b) <= np.maximum(np.abs(b), 1e-30) * 2.0 ** -7 + 1e-12)
+
+
+# ------------------------------------------------------------------ CPU: oracle pinning
+
+@pytest.mark.parametrize("name", ["hisa_router_lanes", "hisa_router_long"])
+def test_oracle_router_matches_reference(name):
+    g = load(name)
+    lengths = g["valid_lengths"].numpy()
+    reps = oh.chunk_representatives(f(g["global_key"]), lengths)
+    assert np.array_equal(reps, f(g["reps"]))
+    top, masked = oh.select_chunks(f(g["q"]), f(g["reps"]), lengths)
+    assert np.array_equal(top, g["top_chunk_idx"].numpy())
+    fin = np.isfinite(masked)
+    assert np.array_equal(fin, np.isfinite(f(g["logits"])) & fin)
+    scale = g["route_scale"].numpy() if "route_scale" in g else np.full(top.shape[1], 0.1, np.float32)
+    route = oh.route_scores(f(g["q"]), f(g["reps"]), g["top_chunk_idx"].numpy(), scale)
+    assert _one_bf16_step(route, f(g["route"]))
+
+
+def test_oracle_attention_matches_reference_lanes():
+    g = load("hisa_router_lanes")
+    att = oh.attention(f(g["q"]), f(g["local_key"]), f(g["local_value"]), f(g["global_key"]),
+                       f(g["global_value"]), f(g["route"]), g["top_chunk_idx"].numpy(), g["valid_lengths"].numpy())
+    assert np.abs(att - f(g["merged"])).max() < 1e-5
+
+
+def test_oracle_topk_ties_go_to_lower_index():
+    reps = np.zeros((1, 1, 8, 64), np.float32)
+    reps[0, 0, :, 0] = 0.5          # all chunks tie
+    q = np.zeros((1, 1, 512, 64), np.float32)
+    q[..., 0] = 1.0
+    top, _ = oh.select_chunks(q, reps, np.array([512]))
+    assert top[0, 0, -1].tolist() == [0, 1, 2, 3]
+    assert top[0, 0, 0].tolist() == [-1, -1, -1, -1]      # tile 0: nothing completed
+    assert top[0, 0, 4].tolist() == [0, -1, -1, -1]       # tile 4 starts at 64: chunk 0 only
+
+
+# ------------------------------------------------------------------ GPU parity
+
+def _cuda(g, *keys):
+    return [g[k].cuda() for k in keys]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", ["hisa_router_lanes", "hisa_router_long"])
+def test_router_kernels_match_reference(name):
+    from dwarf_v2_b200.hierarchical_sparse_attn_v18_hisa import chunk_representatives, select_chunks
+
+    g = load(name)
+    q, gk, lengths = _cuda(g, "q", "global_key", "valid_lengths")
+    reps = chunk_representatives(gk, lengths.int(), blend_alpha=0.5)
+    top, logits = select_chunks(q, reps, lengths.int(), top_k=4, temperature=1.0, want_logits=True)
+    torch.cuda.synchronize()
+    assert np.array_equal(reps.view(torch.int16).cpu().numpy(), g["reps"].view(torch.int16).numpy())
+    assert np.array_equal(top.cpu().numpy(), g["top_chunk_idx"].numpy())
+    ref_top, ref_masked = oh.select_chunks(f(g["q"]), f(g["reps"]), g["valid_lengths"].numpy())
+    assert np.array_equal(logits.cpu().numpy(), ref_masked)
+
+
+@pytest.mark.gpu
+def test_tile_attention_matches_reference_lanes():
+    from dwarf_v2_b200.hierarchical_sparse_attn_v18_hisa import tile_attention
+
+    g = load("hisa_router_lanes")
+    q, lk, lv, gk, gv, reps, top, lengths, scale = _cuda(
+        g, "q", "local_key", "local_value", "global_key", "global_value", "reps", "top_chunk_idx",
+        "valid_lengths", "route_scale")
+    out, route = tile_attention(q, lk, lv, gk, gv, reps, top.int().contiguous(), scale.float(), lengths.int(),
+                                want_route=True)
+    torch.cuda.synchronize()
+    ref_route = oh.route_scores(f(g["q"]), f(g["reps"]), g["top_chunk_idx"].numpy(), g["route_scale"].numpy())
+    assert np.array_equal(route.float().cpu().numpy(), ref_route)
+    assert _one_bf16_step(route.float().cpu().numpy(), f(g["route"]))
+    _close(out.float().cpu().numpy(), f(g["merged"]))
+    # rows past each batch row's valid length are exactly zero
+    assert torch.all(out[1, :, 250:] == 0)
+
+
+@pytest.mark.gpu
+def test_config4_full_size():
+    """B=32, H=8, T=2048, Q/K/V ~ N(0, 0.125^2) bf16, local = global K/V."""
+    from dwarf_v2_b200.hierarchical_sparse_attn_v18_hisa import hisa_attention
+
+    gen = torch.Generator().manual_seed(0)
+    B, H, T = 32, 8, 2048
+    q = (torch.randn(B, H, T, 64, generator=gen) * 0.125).to(torch.bfloat16).cuda()
+    k = (torch.randn(B, H, T, 64, generator=gen) * 0.125).to(torch.bfloat16).cuda()
+    v = (torch.randn(B, H, T, 64, generator=gen) * 0.125).to(torch.bfloat16).cuda()
+    scale = torch.full((H,), 0.1)
+    out, top, route = hisa_attention(q, k, v, k, v, scale, want_route=True)
+    out2, top2, _ = hisa_attention(q, k, v, k, v, scale)
+    torch.cuda.synchronize()
+    assert torch.equal(out, out2) and torch.equal(top, top2)
+    assert torch.all(out[:, :, 0] == 0)
+    pairs = [(0, 0), (13, 3), (31, 7)]
+    for b, h in pairs:
+        qs, ks, vs = (t[b:b + 1, h:h + 1].float().cpu().numpy() for t in (q, k, v))
+        reps = oh.chunk_representatives(ks, np.array([T]))
+        rtop, _ = oh.select_chunks(qs, reps, np.array([T]))
+        assert np.array_equal(top[b:b + 1, h:h + 1].cpu().numpy(), rtop)
+        rroute = oh.route_scores(qs, reps, rtop, np.array([0.1], np.float32))
+        assert np.array_equal(route[b:b + 1, h:h + 1].float().cpu().numpy(), rroute)
+        ref = oh.attention(qs, ks, vs, ks, vs, rroute, rtop, np.array([T]))
+        _close(out[b:b + 1, h:h + 1].float().cpu().numpy(), ref)
+
+
+@pytest.mark.gpu
+def test_module_matches_reference_module():
+    from dwarf_v2_b200.hierarchical_sparse_attn_v18_hisa import HierarchicalSparseAttentionV16HISACausal
+
+    g = load("hisa_module_eval")
+    module = HierarchicalSparseAttentionV16HISACausal(
+        D=128, H=2, hd=64, chunk_size=64, top_k_chunks=4, hisa_top_m_tokens=64, local_window=64,
+        selector_tile_size=16, route_prior_scale=0.1, global_adapter_rank=16).eval()
+    state = {k[len("state."):]: val for k, val in g.items() if k.startswith("state.")}
+    module.load_state_dict(state)
+    module = module.cuda()
+    with torch.no_grad():
+        y = module(g["x"].to(torch.bfloat16).cuda(),
+                   kv_inject=(g["key_delta"].to(torch.bfloat16).cuda(), g["value_delta"].to(torch.bfloat16).cuda()))
+    _close(y.float().cpu().numpy(), f(g["y"]), tol=2e-2, mean_rel=3e-2)
