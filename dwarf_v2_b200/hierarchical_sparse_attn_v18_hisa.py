@@ -383,22 +383,14 @@ class HierarchicalSparseAttentionV16HISACausal(nn.Module):
         gv = npci_rotate_cuda(local_value, vd, theta_v, addend=addend_v)
         return gk, gv
 
-    def forward(self, x: torch.Tensor, kv_inject=None, *, valid_lengths=None, return_metadata: bool = False,
-                return_auxiliary: bool = False):
-        self._check_supported()
-        _lib.require_cuda(x)
-        if torch.is_grad_enabled() and (x.requires_grad or any(p.requires_grad for p in self.parameters())):
-            raise NotImplementedError("dwarf_v2_b200 is a forward (inference) engine; run under torch.no_grad()")
-        self.hisa_evidence_capture = None
-        self._routing_auxiliary_loss = None
+    def forward_parts(self, x: torch.Tensor, kv_inject, lengths: torch.Tensor):
+        """(W_o(attended), content-gate logits, top_chunk_idx): the forward up to the output gate.
+
+        The model fuses ``* sigmoid(gate)`` into its residual-add + RMSNorm kernel.
+        """
         B, T, _ = x.shape
-        if -(-T // self.chunk_size) > 128:
-            raise ValueError("the B200 HISA router supports up to 128 chunks (T <= 8192)")
         act = torch.bfloat16
         xb = x if x.dtype == act else x.to(act)
-        lengths = _as_valid_lengths(
-            valid_lengths if valid_lengths is not None else getattr(self, "_causal_control_valid_lengths", None),
-            batch_size=B, seq_len=T, device=x.device)
         qkvg = F.linear(xb, self.qkvg_proj.weight.to(act), self.qkvg_proj.bias.to(act))
         q, k, v, gate = qkvg.split(self.D, dim=-1)
         query = _to_heads(q, B, T, self.H, self.hd)
@@ -412,7 +404,25 @@ class HierarchicalSparseAttentionV16HISACausal(nn.Module):
         tile_attention(query, local_key, local_value, global_key, global_value, reps, top, scale, lengths,
                        out=_to_heads(attended, B, T, self.H, self.hd))
         self._last_token_selection_path = "enumerate_all"
-        output = gate_mul(F.linear(attended, self.W_o.weight.to(act)), gate)
+        return F.linear(attended, self.W_o.weight.to(act)), gate, top
+
+    def forward(self, x: torch.Tensor, kv_inject=None, *, valid_lengths=None, return_metadata: bool = False,
+                return_auxiliary: bool = False):
+        self._check_supported()
+        _lib.require_cuda(x)
+        if torch.is_grad_enabled() and (x.requires_grad or any(p.requires_grad for p in self.parameters())):
+            raise NotImplementedError("dwarf_v2_b200 is a forward (inference) engine; run under torch.no_grad()")
+        self.hisa_evidence_capture = None
+        self._routing_auxiliary_loss = None
+        B, T, _ = x.shape
+        if -(-T // self.chunk_size) > 128:
+            raise ValueError("the B200 HISA router supports up to 128 chunks (T <= 8192)")
+        lengths = _as_valid_lengths(
+            valid_lengths if valid_lengths is not None else getattr(self, "_causal_control_valid_lengths", None),
+            batch_size=B, seq_len=T, device=x.device)
+        projected, gate, top = self.forward_parts(x, kv_inject, lengths)
+        act = torch.bfloat16
+        output = gate_mul(projected, gate)
         if x.dtype != act:
             output = output.to(x.dtype)
         auxiliary = output.new_zeros(())

@@ -1,0 +1,308 @@
+"""DWARF-v2 model construction API and whole-model prefill on B200.
+
+Mirrors the model part of the reference trainer (train/train_dwarf.py:115-470):
+``DwarfConfig``, ``build_offset_groups``, ``RMSNorm``, ``SwiGLUFFN``,
+``InterferencePacket``, ``DSQGBlock``, ``GlobalMixerBlock`` and
+``DwarfForCausalLM`` with the same module tree, parameter names and shapes
+(55,348,728 parameters, 55,344,120 trainable) and the same seeded
+initialisation (``reset_parameters``), so reference state dicts load unchanged
+and a freshly built model holds bit-identical weights.
+
+``DwarfForCausalLM.forward`` runs the prefill through this engine's kernels:
+embedding + RMSNorm, per block the attention kernels, residual add fused with
+the next RMSNorm (and, after the HISA block, with its sigmoid output gate),
+SwiGLU, the EMA packet (three look-back scans + one epilogue kernel); GEMMs
+are cuBLAS bf16. Activations are bf16 with the reference's rounding points.
+``kv_cache="q6"`` runs every DSQG layer over the q6-quantised K/V cache.
+Eval mode only (dropout, HISA exploration and aux loss are training features).
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import Iterable
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from . import glue
+from .causal_ema_scan import bounded_ema_factor, causal_ema_scan, inverse_bounded_ema_factor
+from .dsqg_attention_v22 import ALL_OFFSETS, R_PLANES, DSQGAttentionV19
+from .hierarchical_sparse_attn_v18_hisa import HierarchicalSparseAttentionV16HISACausal
+
+EXPECTED_PARAMETERS = 55_348_728
+EXPECTED_TRAINABLE_PARAMETERS = 55_344_120
+LAYOUT: tuple[int | None, ...] = (0, 1, 2, None, 0, 1, 2, 0, 1, 2)  # None = the HISA global mixer
+
+
+@dataclass(frozen=True)
+class DwarfConfig:
+    """Model hyper-parameters (reference train/train_dwarf.py:115-151)."""
+
+    vocab_size: int = 32768
+    embedding_dim: int = 512
+    num_heads: int = 8
+    ffn_dim: int = 2400
+    seq_len: int = 2048
+    num_layers: int = 10
+    dropout: float = 0.05
+    min_offset_support: int = 64
+    hisa_chunk_size: int = 64
+    top_k_chunks: int = 4
+    hisa_top_m_tokens: int = 64
+    hisa_local_window: int = 64
+    hisa_selector_tile: int = 16
+    hisa_global_adapter_rank: int = 16
+    ema_timescales: tuple[float, ...] = (16.0, 64.0, 256.0)
+    init_seed: int = 42
+
+    def __post_init__(self) -> None:
+        if self.embedding_dim % self.num_heads:
+            raise ValueError("embedding_dim must be divisible by num_heads")
+        if self.num_layers != 10:
+            raise ValueError("the 55M DWARF topology has exactly ten blocks")
+        if self.seq_len < 65:
+            raise ValueError("seq_len must be at least 65")
+        head_dim = self.embedding_dim // self.num_heads
+        if head_dim & (head_dim - 1):
+            raise ValueError("HISA requires a power-of-two head dimension")
+
+    @property
+    def model_length(self) -> int:
+        return self.seq_len - 1
+
+    @property
+    def swiglu_dim(self) -> int:
+        return max(64, int(round((2.0 * self.ffn_dim / 3.0) / 64.0)) * 64)
+
+
+def build_offset_groups(config: DwarfConfig) -> tuple[tuple[int, ...], ...]:
+    """Offsets with >= min_offset_support sources at model length, dealt round-robin into 3 groups (reference :157-169)."""
+    offsets = tuple(sorted(int(v) for v in ALL_OFFSETS))
+    if len(offsets) != len(set(offsets)):
+        raise ValueError("canonical DSQG offsets must be unique")
+    live = tuple(d for d in offsets if config.model_length - d >= config.min_offset_support)
+    groups = tuple(tuple(live[i::3]) for i in range(3))
+    if any(not g for g in groups):
+        raise ValueError("offset pruning left an empty DSQG group")
+    return groups
+
+
+def _small_large_counts(offsets: Iterable[int]) -> tuple[int, int]:
+    values = tuple(int(v) for v in offsets)
+    small = sum(v <= 28 for v in values)
+    large = sum(v >= 48 for v in values)
+    if small + large != len(values):
+        raise ValueError("DSQG offsets must remain in the supported kernel bands")
+    return small, large
+
+
+def _act(t: torch.Tensor) -> torch.Tensor:
+    return t if t.dtype == torch.bfloat16 else t.to(torch.bfloat16)
+
+
+class RMSNorm(nn.Module):
+    def __init__(self, dimension: int, eps: float = 1e-6) -> None:
+        super().__init__()
+        self.weight = nn.Parameter(torch.ones(dimension))
+        self.eps = eps
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        return glue.rmsnorm(_act(x), self.weight.detach(), self.eps)
+
+
+class SwiGLUFFN(nn.Module):
+    def __init__(self, config: DwarfConfig) -> None:
+        super().__init__()
+        hidden = config.swiglu_dim
+        self.up_gate = nn.Linear(config.embedding_dim, 2 * hidden, bias=False)
+        self.down = nn.Linear(hidden, config.embedding_dim, bias=False)
+        self.dropout = nn.Dropout(config.dropout)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        """down(silu(gate) * up): two cuBLAS GEMMs around the ``dwarf_swiglu`` kernel."""
+        h = glue.swiglu(F.linear(_act(x), _act(self.up_gate.weight)))
+        return F.linear(h, _act(self.down.weight))
+
+
+class InterferencePacket(nn.Module):
+    """Causal EMA packet feeding HISA's global K/V (reference :243-284)."""
+
+    def __init__(self, config: DwarfConfig) -> None:
+        super().__init__()
+        self.heads = config.num_heads
+        self.head_dim = config.embedding_dim // config.num_heads
+        raw = [inverse_bounded_ema_factor(1.0 / v) for v in config.ema_timescales]
+        self.ema_raw = nn.Parameter(torch.tensor(raw, dtype=torch.float32))
+        self.mix_logits = nn.Parameter(torch.zeros(len(raw)))
+        self.gate_proj = nn.Linear(config.embedding_dim, config.embedding_dim)
+        self.kv_proj = nn.Linear(config.embedding_dim, 2 * config.embedding_dim, bias=False)
+        with torch.no_grad():
+            self.gate_proj.bias.fill_(-2.0)
+
+    @property
+    def ema_factors(self) -> torch.Tensor:
+        return bounded_ema_factor(self.ema_raw)
+
+    def forward(self, normalized: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        x = _act(normalized)
+        with torch.no_grad():
+            factors = self.ema_factors.detach()
+            mixture = torch.softmax(self.mix_logits.detach().float(), dim=0).to(torch.bfloat16).float().tolist()
+        scans = [causal_ema_scan(x, f.reshape(1)) for f in factors]
+        gate_pre = F.linear(x, _act(self.gate_proj.weight), _act(self.gate_proj.bias))
+        packet = glue.packet(scans, mixture, gate_pre)
+        kv = F.linear(packet, _act(self.kv_proj.weight))
+        B, T, D = x.shape
+        key_delta = kv[..., :D].reshape(B, T, self.heads, self.head_dim).permute(0, 2, 1, 3)
+        value_delta = kv[..., D:].reshape(B, T, self.heads, self.head_dim).permute(0, 2, 1, 3)
+        return key_delta, value_delta
+
+
+class DSQGBlock(nn.Module):
+    def __init__(self, config: DwarfConfig, offsets: tuple[int, ...], *, plane_shift: int,
+                 kv_cache: str = "bf16") -> None:
+        super().__init__()
+        small, large = _small_large_counts(offsets)
+        self.norm1 = RMSNorm(config.embedding_dim)
+        self.norm2 = RMSNorm(config.embedding_dim)
+        self.attn = DSQGAttentionV19(
+            config.embedding_dim, config.num_heads, offsets, small, large, seq_len=config.seq_len,
+            dropout=config.dropout, grouped_mode="baseline", plane_shift=plane_shift, pos_bias_scale=1.0,
+            movt_dynamic_rms_target=0.01, train_phase_probes=False, scale_embed_init_std=0.01,
+            npci_strength_tau=0.25, online_softmax=True, support_crop_projections=True,
+            support_crop_min_offset=64, kv_cache=kv_cache,
+        )
+        self.ffn = SwiGLUFFN(config)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        x, n2 = glue.add_rmsnorm(_act(x), self.norm2.weight.detach(), addend=self.attn(self.norm1(x)))
+        x, _ = glue.add_rmsnorm(x, self.norm2.weight.detach(), addend=self.ffn(n2))
+        return x
+
+
+class GlobalMixerBlock(nn.Module):
+    def __init__(self, config: DwarfConfig) -> None:
+        super().__init__()
+        self.norm1 = RMSNorm(config.embedding_dim)
+        self.norm2 = RMSNorm(config.embedding_dim)
+        self.attn = HierarchicalSparseAttentionV16HISACausal(
+            D=config.embedding_dim, H=config.num_heads, hd=config.embedding_dim // config.num_heads,
+            chunk_size=config.hisa_chunk_size, top_k_chunks=config.top_k_chunks,
+            hisa_top_m_tokens=config.hisa_top_m_tokens, local_window=config.hisa_local_window,
+            selector_tile_size=config.hisa_selector_tile, representative_mode="mean_max_blend",
+            representative_blend_alpha=0.5, route_prior_scale=0.1, route_aux_weight=0.01, route_aux_samples=4,
+            route_aux_temperature=1.0, exploration_probability=0.05,
+            global_adapter_rank=config.hisa_global_adapter_rank, npci_theta_max=0.25,
+            max_seq_len=config.model_length, local_backend="flex", collect_routing_diagnostics=False,
+        )
+        self.packet = InterferencePacket(config)
+        self.ffn = SwiGLUFFN(config)
+        self.dropout = nn.Dropout(config.dropout)
+
+    def forward(self, x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        normalized = self.norm1(x)
+        attended, auxiliary = self.attn(normalized, kv_inject=self.packet(normalized), return_auxiliary=True)
+        x, n2 = glue.add_rmsnorm(_act(x), self.norm2.weight.detach(), addend=attended)
+        x, _ = glue.add_rmsnorm(x, self.norm2.weight.detach(), addend=self.ffn(n2))
+        return x, auxiliary
+
+
+class DwarfForCausalLM(nn.Module):
+    """The 10-block DWARF-v2 language model (reference train/train_dwarf.py:367-470)."""
+
+    def __init__(self, config: DwarfConfig | None = None, *, kv_cache: str = "bf16") -> None:
+        super().__init__()
+        self.config = config or DwarfConfig()
+        config = self.config
+        self.kv_cache = kv_cache
+        self.offset_groups = build_offset_groups(config)
+        self.embedding = nn.Embedding(config.vocab_size, config.embedding_dim)
+        self.dropout = nn.Dropout(config.dropout)
+        blocks: list[nn.Module] = []
+        dsqg_index = 0
+        plane_segment = max(2, (config.embedding_dim // config.num_heads) // R_PLANES)
+        for group_index in LAYOUT:
+            if group_index is None:
+                blocks.append(GlobalMixerBlock(config))
+                continue
+            plane_shift = 2 * (dsqg_index % max(1, plane_segment // 2))
+            blocks.append(DSQGBlock(config, self.offset_groups[group_index], plane_shift=plane_shift,
+                                    kv_cache=kv_cache))
+            dsqg_index += 1
+        self.blocks = nn.ModuleList(blocks)
+        self.norm = RMSNorm(config.embedding_dim)
+        self.lm_head = nn.Linear(config.embedding_dim, config.vocab_size, bias=False)
+        self.lm_head.weight = self.embedding.weight
+        self.reset_parameters()
+
+    def reset_parameters(self) -> None:
+        """Seeded initialisation with the reference's draw order (reference :397-431)."""
+        state = torch.random.get_rng_state()
+        torch.manual_seed(self.config.init_seed + 20_001)
+        try:
+            for module in self.modules():
+                if isinstance(module, nn.Linear):
+                    nn.init.normal_(module.weight, mean=0.0, std=0.02)
+                    if module.bias is not None:
+                        nn.init.zeros_(module.bias)
+                elif isinstance(module, nn.Embedding):
+                    nn.init.normal_(module.weight, mean=0.0, std=0.02)
+            for module in self.modules():
+                if isinstance(module, DSQGAttentionV19):
+                    nn.init.normal_(module.phase_base, mean=0.0, std=0.01)
+                    nn.init.normal_(module.phase_gain, mean=0.0, std=module.movt_phase_gain_init_std)
+                    nn.init.zeros_(module.phase_gate)
+                    nn.init.normal_(module.scale_embed, mean=0.0, std=module.scale_embed_init_std)
+                    with torch.no_grad():
+                        module.scale_embed.sub_(module.scale_embed.mean(0, keepdim=True))
+                    module.reset_phase_probes_()
+                elif isinstance(module, HierarchicalSparseAttentionV16HISACausal):
+                    module.reset_global_adapters_()
+                elif isinstance(module, InterferencePacket):
+                    with torch.no_grad():
+                        module.gate_proj.bias.fill_(-2.0)
+        finally:
+            torch.random.set_rng_state(state)
+
+    def prepare_runtime(self, device) -> None:
+        for module in self.modules():
+            if isinstance(module, HierarchicalSparseAttentionV16HISACausal):
+                module.prepare_runtime(device, self.config.model_length)
+
+    def _check(self, input_ids: torch.Tensor) -> None:
+        if self.training:
+            raise NotImplementedError("the B200 engine is a forward engine; call .eval()")
+        if not input_ids.is_cuda:
+            raise RuntimeError("dwarf_v2_b200 runs on CUDA tensors only (no CPU fallback)")
+        if input_ids.ndim != 2:
+            raise ValueError("input_ids must be [B, T]")
+        if torch.is_grad_enabled() and any(p.requires_grad for p in self.parameters()):
+            raise NotImplementedError("dwarf_v2_b200 is a forward (inference) engine; run under torch.no_grad()")
+
+    def forward_hidden(self, input_ids: torch.Tensor, *, return_auxiliary: bool = False):
+        """Final RMSNorm'd hidden states [B, T, D] (bf16)."""
+        self._check(input_ids)
+        emb = _act(self.embedding.weight.detach()).contiguous()
+        blocks = list(self.blocks)
+        x, n = glue.embed_rmsnorm(input_ids, emb, blocks[0].norm1.weight.detach())
+        auxiliary = x.new_zeros(())
+        for i, block in enumerate(blocks):
+            next_norm = blocks[i + 1].norm1.weight if i + 1 < len(blocks) else self.norm.weight
+            if isinstance(block, GlobalMixerBlock):
+                attn = block.attn
+                kd, vd = block.packet(n)
+                lengths = torch.full((x.shape[0],), x.shape[1], dtype=torch.int32, device=x.device)
+                projected, gate, _ = attn.forward_parts(n, (kd, vd), lengths)
+                x, n2 = glue.add_rmsnorm(x, block.norm2.weight.detach(), addend=projected, gate=gate)
+            else:
+                x, n2 = glue.add_rmsnorm(x, block.norm2.weight.detach(), addend=block.attn(n))
+            x, n = glue.add_rmsnorm(x, next_norm.detach(), addend=block.ffn(n2), x_out=x)
+        return (n, auxiliary) if return_auxiliary else n
+
+    def forward(self, input_ids: torch.Tensor, *, return_hidden: bool = False, return_auxiliary: bool = False):
+        hidden, auxiliary = self.forward_hidden(input_ids, return_auxiliary=True)
+        output = hidden if return_hidden else F.linear(hidden, _act(self.embedding.weight.detach()))
+        return (output, auxiliary) if return_auxiliary else output

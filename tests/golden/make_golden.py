@@ -280,9 +280,64 @@ def make_hisa() -> None:
     save("hisa_module_eval", x=x, key_delta=kd, value_delta=vd, y=y, **state)
 
 
+def make_model() -> None:
+    """Whole-model prefill of the reference DwarfForCausalLM (seeded init), B=1, T=2048.
+
+    bf16 weights/activations on CPU (the BASELINE config-5 precision), plus the
+    same model in fp32, plus a q6 variant where every DSQG layer sees K/V
+    round-tripped through the q6 codec (oracle/q6.py), z_pre from unquantised K.
+    Stored: final hidden states at every 4th position, logits at 4 positions
+    and a parameter digest.
+    """
+    import hashlib
+
+    _import_reference()
+    sys.path.insert(0, str(HERE.parent.parent))
+    import dsqg_attention_v22 as ref_dsqg
+    import train_dwarf as td
+
+    from oracle import q6 as oq6
+
+    model = td.DwarfForCausalLM(td.DwarfConfig()).eval()
+    digest = hashlib.sha256()
+    for name, tensor in model.state_dict().items():
+        digest.update(name.encode())
+        digest.update(tensor.detach().float().numpy().tobytes())
+    g = torch.Generator().manual_seed(0)
+    ids = torch.randint(57, 32768, (1, 2048), generator=g)
+    positions = torch.tensor([1, 65, 1024, 2047])       # logits kept at these positions
+    rows = torch.arange(0, 2048, 4)                        # hidden states kept at these positions
+    out = {"input_ids": ids, "positions": positions, "rows": rows,
+           "param_count": sum(p.numel() for p in model.parameters()),
+           "param_sha256": np.frombuffer(digest.digest(), dtype=np.uint8)}
+    with torch.no_grad():
+        h32 = model(ids, return_hidden=True)
+        out["logits_f32"] = model.lm_head(h32)[0, positions]
+        m16 = model.to(torch.bfloat16)
+        h16 = m16(ids, return_hidden=True)
+        out["hidden_bf16"] = h16[0, rows]
+        out["logits_bf16"] = m16.lm_head(h16)[0, positions].float()
+        original = ref_dsqg.dsqg_attention_v18_grouped
+
+        def fake_q6(q, k, v, *args, **kwargs):
+            def rt(t):
+                codes, scales = oq6.pack(t.float().numpy())
+                return torch.from_numpy(oq6.unpack(codes, scales)).to(t.dtype)
+            return original(q, rt(k), rt(v), *args, **kwargs)
+
+        ref_dsqg.dsqg_attention_v18_grouped = fake_q6
+        try:
+            hq = m16(ids, return_hidden=True)
+        finally:
+            ref_dsqg.dsqg_attention_v18_grouped = original
+        out["hidden_bf16_q6"] = hq[0, rows]
+        out["logits_bf16_q6"] = m16.lm_head(hq)[0, positions].float()
+    save("model_prefill_b1_t2048", **out)
+
+
 def main(argv: list[str]) -> None:
     which = argv[1] if len(argv) > 1 else "all"
-    makers = {"ema": make_ema, "dsqg": make_dsqg, "hisa": make_hisa}
+    makers = {"ema": make_ema, "dsqg": make_dsqg, "hisa": make_hisa, "model": make_model}
     for name, maker in makers.items():
         if which in ("all", name):
             maker()

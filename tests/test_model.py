@@ -1,0 +1,78 @@
+"""Whole-model drop-in: construction API and prefill parity with the reference.
+
+CPU: DwarfForCausalLM builds the reference topology with bit-identical seeded
+weights (parameter count and a SHA-256 over the state dict, captured from the
+reference by tests/golden/make_golden.py). GPU: bf16 prefill of the reference
+config (B=1, T=2048) against the reference's own bf16 forward; logits within
+the north-star 2e-2 max-abs / 1e-2 mean-relative tolerance. The q6-KV variant
+is compared with the reference run on q6-round-tripped K/V.
+"""
+
+import hashlib
+
+import numpy as np
+import pytest
+import torch
+
+from tests._golden import load
+
+
+def test_construction_matches_reference_weights():
+    from dwarf_v2_b200.model import EXPECTED_PARAMETERS, EXPECTED_TRAINABLE_PARAMETERS, DwarfConfig, DwarfForCausalLM
+
+    g = load("model_prefill_b1_t2048")
+    model = DwarfForCausalLM(DwarfConfig())
+    assert sum(p.numel() for p in model.parameters()) == EXPECTED_PARAMETERS == int(g["param_count"])
+    assert sum(p.numel() for p in model.parameters() if p.requires_grad) == EXPECTED_TRAINABLE_PARAMETERS
+    digest = hashlib.sha256()
+    for name, tensor in model.state_dict().items():
+        digest.update(name.encode())
+        digest.update(tensor.detach().float().numpy().tobytes())
+    assert digest.digest() == bytes(g["param_sha256"].numpy().tolist())
+
+
+def test_topology():
+    from dwarf_v2_b200.model import DwarfForCausalLM, GlobalMixerBlock
+
+    model = DwarfForCausalLM()
+    kinds = ["HISA" if isinstance(b, GlobalMixerBlock) else "DSQG" for b in model.blocks]
+    assert kinds == ["DSQG"] * 3 + ["HISA"] + ["DSQG"] * 6
+    shifts = [b.attn.plane_shift for b in model.blocks if not isinstance(b, GlobalMixerBlock)]
+    assert shifts == [0, 2, 4, 6, 8, 10, 12, 14, 0]
+    assert [len(g) for g in model.offset_groups] == [29, 29, 29]
+    assert model.lm_head.weight is model.embedding.weight
+
+
+def test_forward_requires_cuda_and_eval():
+    from dwarf_v2_b200.model import DwarfForCausalLM
+
+    model = DwarfForCausalLM()
+    with pytest.raises(NotImplementedError):
+        model(torch.zeros(1, 8, dtype=torch.long))      # training mode
+    model.eval()
+    with torch.no_grad(), pytest.raises(RuntimeError):
+        model(torch.zeros(1, 8, dtype=torch.long))      # CPU tensor: no fallback
+
+
+def _close(out, ref, tol=2e-2, mean_rel=1e-2):
+    err = np.abs(np.asarray(out, np.float64) - np.asarray(ref, np.float64))
+    assert err.max() <= tol, err.max()
+    assert err.mean() / np.abs(ref).mean() <= mean_rel, err.mean() / np.abs(ref).mean()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("kv_cache", ["bf16", "q6"])
+def test_prefill_matches_reference(kv_cache):
+    from dwarf_v2_b200.model import DwarfForCausalLM
+
+    g = load("model_prefill_b1_t2048")
+    model = DwarfForCausalLM(kv_cache=kv_cache).eval().to(torch.bfloat16).cuda()
+    ids = g["input_ids"].cuda()
+    with torch.no_grad():
+        hidden = model(ids, return_hidden=True)
+        logits = model(ids)[0, g["positions"].cuda()].float().cpu().numpy()
+    suffix = "_q6" if kv_cache == "q6" else ""
+    rows = g["rows"]
+    _close(hidden[0, rows.cuda()].float().cpu().numpy(), g["hidden_bf16" + suffix].float().numpy(),
+           tol=0.5, mean_rel=2e-2)
+    _close(logits, g["logits_bf16" + suffix].numpy())
