@@ -1,0 +1,282 @@
+"""Benchmark: DWARF-v2 whole-model prefill on 1..8 B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...     (N > 1)
+
+Workload: DwarfForCausalLM (D=512, L=10, T=2048, vocab 32768, seeded bf16
+weights), q6 KV cache in every DSQG layer, global batch 256 uniform-random
+token ids in [57, 32768), split by batch rows across the ranks (strong scaling:
+the global batch is fixed). One step = prefill of the whole batch to logits
+plus an NCCL all-gather of every row's next-token logits to all ranks.
+
+Printed JSON line (rank 0):
+* value    tokens/s with inputs resident in HBM, timed with CUDA events over
+           exactly K steps between barriers, max over ranks;
+* e2e      the same step through the public API with the host->device copy of
+           the token ids (pinned) and the device->host read of the gathered
+           next-token logits inside the timed region;
+* roofline the dominant engine kernel (dwarf_dsqg_fwd): algorithmic bytes per
+           launch / its mean CUDA-event duration inside the timed region,
+           against the measured HBM copy bandwidth;
+* cpu_baseline  the CPU oracle port of the same prefill (oracle/model.py) on
+           one 2048-token row, host cores, rank 0 at N=1.
+``--impl reference`` times that CPU port alone (the reference is pure
+PyTorch/Triton and cannot be installed on the GPU box).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+METRIC = "prefill tok/s (D512 L10 T2048, q6 KV) at 1/2/4/8 B200; kernel HBM % of peak"
+GLOBAL_BATCH = 256
+SEQ_LEN = 2048
+VOCAB = 32768
+FALLBACK_HBM_GBS = 6650.0
+
+
+def _peaks() -> tuple[float, str]:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.is_file():
+        return float(json.loads(path.read_text())["hbm_gbs"]), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def _dist():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def _token_ids(rows: slice) -> torch.Tensor:
+    g = torch.Generator().manual_seed(0)
+    ids = torch.randint(57, VOCAB, (GLOBAL_BATCH, SEQ_LEN), generator=g)
+    return ids[rows].contiguous()
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during a timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            out, _ = self.proc.communicate(timeout=10)
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in getattr(self, "lines", []):
+            parts = [p.strip() for p in line.split(",")]
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except (ValueError, IndexError):
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cpu_baseline(sample_rows: int = 1) -> dict:
+    """Time the CPU oracle port of the prefill on `sample_rows` rows of the workload."""
+    sys.path.insert(0, str(ROOT))
+    from oracle import model as omodel
+
+    from dwarf_v2_b200.dsqg_attention_v22 import ALL_OFFSETS
+    from dwarf_v2_b200.model import DwarfForCausalLM
+
+    cores = len(os.sched_getaffinity(0))
+    torch.set_num_threads(cores)
+    state = DwarfForCausalLM().state_dict()
+    ids = _token_ids(slice(0, sample_rows))
+    t0 = time.perf_counter()
+    omodel.prefill(state, ids, all_offsets=ALL_OFFSETS)
+    dt = time.perf_counter() - t0
+    return {"value": sample_rows * SEQ_LEN / dt, "unit": "tok/s", "cores": cores, "kind": "port",
+            "sample": f"{sample_rows} row(s) x {SEQ_LEN} tokens of the config-5 batch through oracle/model.py "
+                      f"(fp32/fp64 CPU restatement of the reference forward), {dt:.1f} s"}
+
+
+def run_reference(args) -> None:
+    world, rank, _ = _dist()
+    if rank != 0:
+        return
+    for _ in range(args.warmup):
+        cpu_baseline(1) if args.warmup_full else None
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        r = cpu_baseline(1)
+        times.append(time.perf_counter() - t0)
+    value = SEQ_LEN * len(times) / sum(times)
+    line = {"metric": METRIC, "impl": "reference", "value": value, "unit": "tok/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * sum(times) / len(times),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded uniform token ids in [57,32768); seeded reference init)",
+            "config": {"workload": "config5: DWARF-v2 prefill, T=2048; each step a 1-row sample on host cores",
+                       "global_batch": GLOBAL_BATCH, "seq_len": SEQ_LEN},
+            "cpu_baseline": {**r, "value": value},
+            "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args) -> None:
+    import torch.distributed as dist
+
+    from dwarf_v2_b200 import _lib
+    from dwarf_v2_b200.model import DwarfForCausalLM
+
+    world, rank, local = _dist()
+    if world > 1:
+        dist.init_process_group("nccl", device_id=torch.device(f"cuda:{local}"))
+    torch.cuda.set_device(local)
+    dev = torch.device(f"cuda:{local}")
+    if GLOBAL_BATCH % world:
+        raise SystemExit(f"global batch {GLOBAL_BATCH} must divide by {world} ranks")
+    rows = GLOBAL_BATCH // world
+    model = DwarfForCausalLM(kv_cache="q6").eval().to(torch.bfloat16).to(dev)
+    ids_host = _token_ids(slice(rank * rows, (rank + 1) * rows)).pin_memory()
+    ids_dev = ids_host.to(dev)
+    gathered = torch.empty(GLOBAL_BATCH, VOCAB, dtype=torch.bfloat16, device=dev)
+    out_host = torch.empty(GLOBAL_BATCH, VOCAB, dtype=torch.bfloat16).pin_memory()
+
+    def step(ids):
+        logits = model(ids)
+        last = logits[:, -1].contiguous()
+        if world > 1:
+            dist.all_gather_into_tensor(gathered, last)
+        else:
+            gathered.copy_(last)
+        return gathered
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    with torch.no_grad():
+        for _ in range(max(args.warmup, 0)):
+            step(ids_dev)
+        # device-resident throughput
+        log = _lib.LaunchLog(timed=("dwarf_dsqg_fwd",))
+        barrier()
+        with ClockSampler(local) as clocks:
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            _lib.set_launch_log(log)
+            start.record()
+            for _ in range(args.steps):
+                step(ids_dev)
+            end.record()
+            _lib.set_launch_log(None)
+            barrier()
+        ms = max_over_ranks(start.elapsed_time(end) / args.steps)
+        dsqg_ms = log.mean_ms("dwarf_dsqg_fwd")
+        launches = log.count
+        # end to end through the public API: H2D ids, prefill + gather, D2H logits
+        barrier()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(args.steps):
+            ids_dev.copy_(ids_host, non_blocking=True)
+            out = step(ids_dev)
+            if rank == 0:
+                out_host.copy_(out, non_blocking=True)
+        end.record()
+        barrier()
+        e2e_ms = max_over_ranks(start.elapsed_time(end) / args.steps)
+
+    tokens = GLOBAL_BATCH * SEQ_LEN
+    hbm, hbm_kind = _peaks()
+    # dwarf_dsqg_fwd algorithmic bytes per launch (one DSQG layer over this rank's rows):
+    # Q bf16 + K/V q6 codes+scales + y_pre/z_pre fp32 + content gate bf16 + output bf16.
+    per_row = 8 * SEQ_LEN  # (head, token) rows per batch row
+    dsqg_bytes = rows * per_row * (64 * 2 + 2 * 50 + 2 * 16 + 64 * 2 + 64 * 2)
+    achieved = dsqg_bytes / (dsqg_ms * 1e-3) / 1e9 if dsqg_ms else None
+    traffic = None
+    prof = ROOT / "profiles" / "dsqg_fwd_traffic.json"
+    if prof.is_file():
+        info = json.loads(prof.read_text())
+        traffic = info["dram_bytes_per_row"] * rows
+    line = {
+        "metric": METRIC, "value": tokens / (ms * 1e-3), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: seeded uniform token ids in [57,32768); random-init weights (reference seeded init)",
+        "config": {"workload": "config5: full DWARF-v2 prefill D512 L10 T2048, q6 KV, batch rows sharded",
+                   "model": "DWARF-v2 55M (10 blocks: 9 DSQG + 1 HISA)", "global_batch": GLOBAL_BATCH,
+                   "seq_len": SEQ_LEN, "parallelism": f"dp{world}", "kv_cache": "q6",
+                   "l2": "no flush: every step's working set (>= 4 GB of activations per GPU) exceeds L2"},
+        "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": rows * SEQ_LEN * 8,
+                "d2h_bytes_per_step": GLOBAL_BATCH * VOCAB * 2 if rank == 0 else 0},
+        "gpu_launches": launches,
+        "roofline": {"kernel": "dwarf_dsqg_fwd", "bound": "hbm", "achieved": achieved, "peak": hbm,
+                     "peak_kind": hbm_kind, "unit": "GB/s", "frac": (achieved / hbm) if achieved else None,
+                     "traffic": traffic, "algorithmic_bytes_per_launch": dsqg_bytes, "mean_launch_ms": dsqg_ms},
+        "clocks": clocks.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(1)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--warmup-full", action="store_true", help="reference arm: full-size warm-up steps")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -248,10 +248,46 @@ _ENTRY_POINTS = {
 }
 
 
+class LaunchLog:
+    """Counts C-ABI launches and, for the entry points in `timed`, brackets each
+    with CUDA events on the launching (current) stream."""
+
+    def __init__(self, timed: tuple[str, ...] = ()):
+        self.count = 0
+        self.timed = set(timed)
+        self.events: dict[str, list[tuple[torch.cuda.Event, torch.cuda.Event]]] = {n: [] for n in timed}
+
+    def mean_ms(self, name: str) -> float | None:
+        pairs = self.events.get(name) or []
+        if not pairs:
+            return None
+        return sum(a.elapsed_time(b) for a, b in pairs) / len(pairs)
+
+
+_launch_log: LaunchLog | None = None
+
+
+def set_launch_log(log: LaunchLog | None) -> None:
+    global _launch_log
+    _launch_log = log
+
+
 def call(name: str, args: ctypes.Structure, device: torch.device) -> None:
     """Invoke a C entry point on the current stream of `device`; raise on error."""
     lib = load()
-    status = getattr(lib, name)(ctypes.byref(args), stream_handle(device))
+    log = _launch_log
+    if log is None:
+        status = getattr(lib, name)(ctypes.byref(args), stream_handle(device))
+    else:
+        log.count += 1
+        if name in log.timed:
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            start.record()
+            status = getattr(lib, name)(ctypes.byref(args), stream_handle(device))
+            end.record()
+            log.events[name].append((start, end))
+        else:
+            status = getattr(lib, name)(ctypes.byref(args), stream_handle(device))
     check(status, name)
 
 

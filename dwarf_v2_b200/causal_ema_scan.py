@@ -20,7 +20,6 @@ This is a forward (inference) engine: a call that would need autograd raises
 
 from __future__ import annotations
 
-import ctypes
 import math
 
 import torch
@@ -90,8 +89,7 @@ def _launch(x: torch.Tensor, out: torch.Tensor, alpha: torch.Tensor, per_channel
         workspace=ws.data_ptr(), workspace_bytes=ws.numel(),
         device_status=_lib.device_status_word(x.device).data_ptr(),
     )
-    status = lib.dwarf_ema_scan(ctypes.byref(args), _lib.stream_handle(x.device))
-    _lib.check(status, "dwarf_ema_scan")
+    _lib.call("dwarf_ema_scan", args, x.device)
 
 
 def _forward_only(*tensors: torch.Tensor) -> None:
