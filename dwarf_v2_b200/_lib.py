@@ -241,6 +241,7 @@ _ENTRY_POINTS = {
     "dwarf_packet": PacketArgs,
     "dwarf_npci_rotate": NpciArgs,
     "dwarf_ema_scan": EmaScanArgs,
+    "dwarf_ema_scan_noalloc": EmaScanArgs,
     "dwarf_q6_pack": Q6PackArgs,
     "dwarf_q6_unpack": Q6UnpackArgs,
     "dwarf_dsqg_fwd": DsqgFwdArgs,

@@ -378,3 +378,54 @@ extern "C" int dwarf_ema_scan(const dwarf_ema_scan_args* a, void* stream_) {
   return vector_ok ? launch_ema<__nv_bfloat16, 8, 16, 4>(a, p, stream)
                    : launch_ema<__nv_bfloat16, 1, 16, 4>(a, p, stream);
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant: the look-back scratch lives in a fixed device array
+// owned by the library, for callers that cannot allocate device memory at the
+// point of the call. See dwarf_ema_scan_noalloc in include/dwarf_b200.h.
+
+#include <mutex>
+
+namespace {
+
+static __device__ __align__(256) unsigned char g_ema_noalloc_scratch[DWARF_EMA_NOALLOC_SCRATCH_BYTES];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mutex;
+void* g_scratch_ptr[kMaxDevices] = {};
+
+// Device address of the scratch array on the current device (looked up once
+// per device; host code must never use the symbol itself as a pointer).
+int scratch_address(void** out) {
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= kMaxDevices) return DWARF_ERR_LAUNCH;
+  std::lock_guard<std::mutex> lock(g_scratch_mutex);
+  if (g_scratch_ptr[device] == nullptr) {
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_ema_noalloc_scratch) != cudaSuccess || ptr == nullptr) return DWARF_ERR_LAUNCH;
+    g_scratch_ptr[device] = ptr;
+  }
+  *out = g_scratch_ptr[device];
+  return DWARF_OK;
+}
+
+}  // namespace
+
+extern "C" int dwarf_ema_scan_noalloc(const dwarf_ema_scan_args* a, void* stream_) {
+  DWARF_CHECK_VERSION(a);
+  if (a->dtype != DWARF_F32 && a->dtype != DWARF_BF16) return DWARF_ERR_DTYPE;
+  if (a->batch < 0 || a->seq_len < 0 || a->width < 0) return DWARF_ERR_SHAPE;
+  if (a->batch == 0 || a->seq_len == 0 || a->width == 0) return DWARF_OK;
+  const int64_t need = workspace_bytes_any(a->batch, a->seq_len, a->width, a->dtype);
+  if (need > (int64_t)DWARF_EMA_NOALLOC_SCRATCH_BYTES) return DWARF_ERR_SCRATCH_LIMIT;
+  void* scratch = nullptr;
+  const int st = scratch_address(&scratch);
+  if (st != DWARF_OK) return st;
+  // Start from a zeroed header and zeroed records, whatever the last call left.
+  if (cudaMemsetAsync(scratch, 0, (size_t)need, static_cast<cudaStream_t>(stream_)) != cudaSuccess)
+    return DWARF_ERR_LAUNCH;
+  dwarf_ema_scan_args local = *a;
+  local.workspace = scratch;
+  local.workspace_bytes = DWARF_EMA_NOALLOC_SCRATCH_BYTES;
+  return dwarf_ema_scan(&local, stream_);
+}

@@ -13,6 +13,7 @@ extern "C" const char* dwarf_status_string(int status) {
     case DWARF_ERR_WORKSPACE: return "workspace missing or too small";
     case DWARF_ERR_LAUNCH: return "CUDA launch failed";
     case DWARF_ERR_VALUE: return "bad scalar argument";
+    case DWARF_ERR_SCRATCH_LIMIT: return "problem exceeds the library's built-in scratch size";
     default: return "unknown status";
   }
 }

@@ -41,7 +41,8 @@ typedef enum {
   DWARF_ERR_DTYPE = -6,        /* unsupported dtype code                      */
   DWARF_ERR_WORKSPACE = -7,    /* workspace missing or too small              */
   DWARF_ERR_LAUNCH = -8,       /* cudaGetLastError() after the launch         */
-  DWARF_ERR_VALUE = -9         /* bad scalar argument                         */
+  DWARF_ERR_VALUE = -9,        /* bad scalar argument                         */
+  DWARF_ERR_SCRATCH_LIMIT = -10 /* problem needs more than the built-in scratch */
 } dwarf_status;
 
 /* Device-side status words written by kernels with bounded waits. */
@@ -93,6 +94,34 @@ typedef struct {
 int64_t dwarf_ema_scan_workspace_bytes(int64_t batch, int64_t seq_len, int64_t width,
                                        int32_t dtype);
 int dwarf_ema_scan(const dwarf_ema_scan_args* args, void* stream);
+
+/* Causal EMA scan that allocates nothing and needs no caller workspace.
+ *
+ * No counterpart in the reference: this entry point exists for callers that
+ * cannot allocate device memory at the point of the call -- for example code
+ * running inside an allocator-less runtime, a plugin whose host forbids
+ * cudaMalloc on its hot path, or an embedder that pre-sizes all device memory
+ * up front. It computes exactly what dwarf_ema_scan computes (same kernel),
+ * but keeps its look-back scratch in a fixed array that lives inside the
+ * library (DWARF_EMA_NOALLOC_SCRATCH_BYTES per GPU that loads the library,
+ * held until the process exits). The caller still passes x, y and alpha;
+ * args->workspace and args->workspace_bytes are ignored.
+ *
+ *  - Size limit: problems whose scratch need (dwarf_ema_scan_workspace_bytes)
+ *    exceeds DWARF_EMA_NOALLOC_SCRATCH_BYTES are rejected with
+ *    DWARF_ERR_SCRATCH_LIMIT before anything is launched. 8 MiB covers e.g.
+ *    B=16, T=2048, D=512 in fp32 or bf16.
+ *  - Set-up: the first call on each device looks up the array's device
+ *    address (cudaGetSymbolAddress) with that device current; make that
+ *    first call before any stream capture begins.
+ *  - Sharing: every call on a device uses the same array. Each call clears
+ *    the part it uses (cudaMemsetAsync on its stream) before launching, so
+ *    calls ordered on one stream are independent, but calls that can overlap
+ *    on the GPU (different streams, or several host threads) race on the
+ *    array and must be serialised by the caller.
+ *  - Calls no cudaMalloc, cudaFree or other allocating routine. */
+#define DWARF_EMA_NOALLOC_SCRATCH_BYTES (8 * 1024 * 1024)
+int dwarf_ema_scan_noalloc(const dwarf_ema_scan_args* args, void* stream);
 
 
 /* ------------------------------------------------------------------------
