@@ -158,29 +158,24 @@ def run_ours(args) -> None:
 
     from dwarf_v2_b200 import _lib
     from dwarf_v2_b200.model import DwarfForCausalLM
+    from dwarf_v2_b200.sharding import gather_rows, rows_for_rank
 
     world, rank, local = _dist()
     if world > 1:
         dist.init_process_group("nccl", device_id=torch.device(f"cuda:{local}"))
     torch.cuda.set_device(local)
     dev = torch.device(f"cuda:{local}")
-    if GLOBAL_BATCH % world:
-        raise SystemExit(f"global batch {GLOBAL_BATCH} must divide by {world} ranks")
-    rows = GLOBAL_BATCH // world
+    mine = rows_for_rank(GLOBAL_BATCH, rank, world)
+    rows = mine.stop - mine.start
     model = DwarfForCausalLM(kv_cache="q6").eval().to(torch.bfloat16).to(dev)
-    ids_host = _token_ids(slice(rank * rows, (rank + 1) * rows)).pin_memory()
+    ids_host = _token_ids(mine).pin_memory()
     ids_dev = ids_host.to(dev)
     gathered = torch.empty(GLOBAL_BATCH, VOCAB, dtype=torch.bfloat16, device=dev)
     out_host = torch.empty(GLOBAL_BATCH, VOCAB, dtype=torch.bfloat16).pin_memory()
 
     def step(ids):
         logits = model(ids)
-        last = logits[:, -1].contiguous()
-        if world > 1:
-            dist.all_gather_into_tensor(gathered, last)
-        else:
-            gathered.copy_(last)
-        return gathered
+        return gather_rows(logits[:, -1].contiguous(), gathered)
 
     def barrier():
         torch.cuda.synchronize()
@@ -270,8 +265,12 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--rows", type=int, default=None, help="override the global batch (small profiling cases)")
     ap.add_argument("--warmup-full", action="store_true", help="reference arm: full-size warm-up steps")
     args = ap.parse_args()
+    if args.rows:
+        global GLOBAL_BATCH
+        GLOBAL_BATCH = args.rows
     if args.impl == "reference":
         run_reference(args)
     else:

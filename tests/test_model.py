@@ -90,3 +90,16 @@ def test_prefill_matches_reference(kv_cache):
     else:
         mx, mean = _err(logits, g["logits_bf16_q6"].numpy())
         assert mx <= 0.15 and mean <= 0.05, (mx, mean)
+
+
+def test_cpu_oracle_matches_reference_fp32_logits():
+    """oracle/model.py (the timed CPU baseline) reproduces the reference's fp32 logits."""
+    from oracle import model as omodel
+
+    from dwarf_v2_b200.dsqg_attention_v22 import ALL_OFFSETS
+    from dwarf_v2_b200.model import DwarfForCausalLM
+
+    g = load("model_prefill_b1_t2048")
+    logits = omodel.prefill(DwarfForCausalLM().state_dict(), g["input_ids"], all_offsets=ALL_OFFSETS)
+    err = np.abs(logits[0, g["positions"]].numpy() - g["logits_f32"].numpy())
+    assert err.max() < 2e-3, err.max()
