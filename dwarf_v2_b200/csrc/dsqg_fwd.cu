@@ -13,11 +13,15 @@
 // slice of thread r, so each thread rotates exactly one plane. K/V rows are
 // gathered straight from global memory (rows of neighbouring queries are
 // neighbouring rows, so each warp reads 8 whole rows per offset), with the
-// next offset's rows prefetched while the current one is consumed.
-// Per-offset tables (offsets, pos_bias[:,h], bf16(scale_embed), this head's
-// phase base/gain) are staged in shared memory once per CTA.
+// next offset's row prefetched while the current one is consumed.
+// The scale-embedding term q . bf16(E_j) of every (query, offset) is one
+// 64 x J x 64 bf16 tensor-core product per CTA (mma.sync), so the per-pair
+// loop only handles q . k. Scores are computed in a first pass and the V
+// accumulation runs in a second pass against the final maximum, which removes
+// the per-offset accumulator rescaling of the online form.
 #include "common.cuh"
 #include "q6_format.cuh"
+#include "warp_mma.cuh"
 
 namespace dwarf {
 namespace {
@@ -76,11 +80,29 @@ __device__ __forceinline__ void bf16x16_to_f32(const uint4 (&w)[2], float (&o)[1
   }
 }
 
+// q6 row slice of one thread (16 codes = 12 bytes) decoded as offset-binary
+// u = c + 32 in [1, 63]: XOR-ing bit 5 of every 6-bit field turns two's
+// complement into offset binary, and float(u) comes from the exponent trick
+// (0x4B000000 | u) - 2^23, so no int->float conversion instruction is needed.
+// The caller removes the +32 bias with one per-row correction.
+__device__ __forceinline__ void q6_flip_sign_bits(uint32_t (&w)[3]) {
+  w[0] ^= 0x20820820u;  // stream bits 5, 11, 17, 23, 29
+  w[1] ^= 0x08208208u;  // stream bits 35, 41, 47, 53, 59
+  w[2] ^= 0x82082082u;  // stream bits 65, 71, 77, 83, 89, 95
+}
 template <int I>
-__device__ __forceinline__ void q6_decode16_impl(const uint32_t (&w)[3], float step, float (&o)[16]) {
+__device__ __forceinline__ float q6_u_float(const uint32_t (&w)[3]) {
+  constexpr int bit = 6 * I, word = bit >> 5, off = bit & 31;
+  uint32_t u;
+  if constexpr (off <= 26) u = (w[word] >> off) & 63u;
+  else u = __funnelshift_r(w[word], w[word + 1], off) & 63u;
+  return __int_as_float(0x4B000000u | u) - 8388608.0f;
+}
+template <int I>
+__device__ __forceinline__ void q6_u16(const uint32_t (&w)[3], float (&o)[16]) {
   if constexpr (I < 16) {
-    o[I] = (float)q6_code96<I>(w) * step;
-    q6_decode16_impl<I + 1>(w, step, o);
+    o[I] = q6_u_float<I>(w);
+    q6_u16<I + 1>(w, o);
   }
 }
 
@@ -117,145 +139,269 @@ struct RowSlice<true> {
       s = 0;
     }
   }
-  __device__ __forceinline__ void to_f32(float (&o)[16]) const {
-    q6_decode16_impl<0>(w, q6_step(__ushort_as_half(s)), o);
+  // Offset-binary values u_d (code + 32) and the dequantisation step.
+  __device__ __forceinline__ void to_u(float (&o)[16], float& step) const {
+    uint32_t t[3] = {w[0], w[1], w[2]};
+    q6_flip_sign_bits(t);
+    q6_u16<0>(t, o);
+    step = q6_step(__ushort_as_half(s));
   }
 };
 
+// Shared-memory carve-up of one CTA (64 queries of one (b, h)).
+struct DsqgSmem {
+  int jp;       // J rounded up to a multiple of 8 (mma n-tiles)
+  int qe_ld;    // row stride of qe (jp + 1 floats)
+  int sc_ld;    // row stride of sc (J + 1 floats)
+  size_t bytes;
+  size_t o_q, o_e, o_qe, o_sc, o_pb, o_off, o_pbase, o_pgain;
+  __host__ __device__ DsqgSmem(int J, int j_large) {
+    jp = (J + 7) / 8 * 8;
+    qe_ld = jp + 1;
+    sc_ld = J + 1;
+    size_t o = 0;
+    o_q = o;      o += 64 * 128;                        // bf16 Q tile, swizzled
+    o_e = o;      o += (size_t)jp * 128;                // bf16(scale_embed), swizzled
+    o_qe = o;     o += (size_t)64 * qe_ld * 4;          // q . bf16(E_j) (fp32)
+    o_sc = o;     o += (size_t)64 * sc_ld * 4;          // scores of pass 1
+    o_pb = o;     o += (size_t)J * 4;
+    o_off = o;    o += (size_t)J * 4;
+    o_pbase = o;  o += (size_t)j_large * 16;
+    o_pgain = o;  o += (size_t)j_large * 16;
+    bytes = (o + 15) / 16 * 16;
+  }
+};
+
+// Two passes per query: (1) scores of every live offset from K rows plus the
+// tensor-core q.E term, running max; (2) exp2 weights against the final max
+// and the V accumulation (no accumulator rescaling), MOVT planes rotated in
+// the owning thread. Softmax is mathematically the reference's online form.
 template <bool Q6>
 __global__ void __launch_bounds__(kThreads)
 dsqg_fwd_kernel(const DsqgParams p) {
-  extern __shared__ __align__(16) unsigned char smem[];
+  using namespace wmma16;
+  extern __shared__ __align__(128) unsigned char smem[];
   const int J = p.J;
-  float* s_se = reinterpret_cast<float*>(smem);            // [J][64]
-  float* s_pb = s_se + (size_t)J * 64;                     // [J]
-  int* s_off = reinterpret_cast<int*>(s_pb + J);           // [J]
-  float* s_pbase = reinterpret_cast<float*>(s_off + J);    // [j_large][4]
-  float* s_pgain = s_pbase + (size_t)p.j_large * 4;        // [j_large][4]
+  const DsqgSmem L(J, p.j_large);
+  unsigned char* s_q = smem + L.o_q;
+  unsigned char* s_e = smem + L.o_e;
+  float* s_qe = reinterpret_cast<float*>(smem + L.o_qe);
+  float* s_sc = reinterpret_cast<float*>(smem + L.o_sc);
+  float* s_pb = reinterpret_cast<float*>(smem + L.o_pb);
+  int* s_off = reinterpret_cast<int*>(smem + L.o_off);
+  float* s_pbase = reinterpret_cast<float*>(smem + L.o_pbase);
+  float* s_pgain = reinterpret_cast<float*>(smem + L.o_pgain);
   __shared__ int s_count[2];
 
   const int64_t b = blockIdx.z;
   const int64_t h = blockIdx.y;
   const int64_t hk = h / p.kv_group;
-  const int sub = threadIdx.x & 3;
-  const int64_t n = (int64_t)blockIdx.x * kQB + (threadIdx.x >> 2);
-  const int64_t n_end = (int64_t)blockIdx.x * kQB + kQB;
-  const int64_t n_last = (n_end < p.N ? n_end : p.N) - 1;
+  const int tid = threadIdx.x;
+  const int lane = tid & 31, warp = tid >> 5;
+  const int sub = tid & 3;
+  const int qi = tid >> 2;
+  const int64_t n0 = (int64_t)blockIdx.x * kQB;
+  const int64_t n = n0 + qi;
+  const int64_t n_last = (n0 + kQB < p.N ? n0 + kQB : p.N) - 1;
 
-  for (int i = threadIdx.x; i < J * 64; i += kThreads) {
-    const int j = i >> 6, d = i & 63;
-    s_se[i] = round_bf16(p.se[j * p.sej + d * p.sed]);
+  // ---- stage Q tile, bf16(E), tables
+  const uint32_t q_base = smem_u32(s_q), e_base = smem_u32(s_e);
+  for (int i = tid; i < 64 * 8; i += kThreads) {
+    const int r = i >> 3, c = i & 7;
+    const int64_t row = n0 + r < p.N ? n0 + r : p.N - 1;
+    const uint4 v = *reinterpret_cast<const uint4*>(p.q + b * p.sqb + h * p.sqh + row * p.sqn + c * 8);
+    *reinterpret_cast<uint4*>(s_q + (tile_addr(q_base, r, c) - q_base)) = v;
   }
-  for (int j = threadIdx.x; j < J; j += kThreads) {
+  for (int i = tid; i < L.jp * 8; i += kThreads) {
+    const int r = i >> 3, c = i & 7;
+    uint32_t packed[4] = {0u, 0u, 0u, 0u};
+    if (r < J) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float lo = p.se[r * p.sej + (c * 8 + 2 * k) * p.sed];
+        const float hi = p.se[r * p.sej + (c * 8 + 2 * k + 1) * p.sed];
+        const __nv_bfloat162 two = __floats2bfloat162_rn(lo, hi);
+        packed[k] = *reinterpret_cast<const uint32_t*>(&two);
+      }
+    }
+    *reinterpret_cast<uint4*>(s_e + (tile_addr(e_base, r, c) - e_base)) =
+        make_uint4(packed[0], packed[1], packed[2], packed[3]);
+  }
+  for (int j = tid; j < J; j += kThreads) {
     s_pb[j] = p.pos_bias[j * p.spj + h * p.sph];
     s_off[j] = p.offsets[j];
   }
-  for (int i = threadIdx.x; i < p.j_large * 4; i += kThreads) {
+  for (int i = tid; i < p.j_large * 4; i += kThreads) {
     const int j = i >> 2, r = i & 3;
     s_pbase[i] = p.pbase[j * p.sbj + h * p.sbh + r];
     s_pgain[i] = p.pgain[j * p.sgj + h * p.sgh + r];
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    // Offsets are ascending inside each band: the ones this CTA can use are a
-    // prefix of the small band and a prefix of the large band.
+  if (tid == 0) {
+    // Offsets ascend inside each band: the usable ones are a prefix of each band.
     int cs = 0, cl = 0;
     for (int j = 0; j < p.j_small; ++j) cs += (s_off[j] <= n_last);
     for (int j = p.j_small; j < J; ++j) cl += (s_off[j] <= n_last);
     s_count[0] = cs;
     s_count[1] = cl;
   }
+  // ---- QE[64][jp] = Q . bf16(E)^T on tensor cores: warp w owns m-tile w&3,
+  // n-tiles (w>>2), (w>>2)+2, ...
+  {
+    const int mt = warp & 3;
+    uint32_t a[4][4];
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {
+      const int mi = lane >> 3, r = lane & 7;
+      ldsm_x4(tile_addr(q_base, mt * 16 + (mi & 1) * 8 + r, ks * 2 + (mi >> 1)), a[ks][0], a[ks][1], a[ks][2],
+              a[ks][3]);
+    }
+    const int g = lane >> 2, t4 = lane & 3;
+    for (int nt = warp >> 2; nt < L.jp / 8; nt += 2) {
+      float c[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks) {
+        uint32_t b0, b1;
+        ldsm_x2(tile_addr(e_base, nt * 8 + (lane & 7), ks * 2 + ((lane >> 3) & 1)), b0, b1);
+        mma_bf16(c, a[ks], b0, b1);
+      }
+      float* row0 = s_qe + (mt * 16 + g) * L.qe_ld + nt * 8 + 2 * t4;
+      float* row1 = row0 + 8 * L.qe_ld;
+      row0[0] = c[0]; row0[1] = c[1];
+      row1[0] = c[2]; row1[1] = c[3];
+    }
+  }
   __syncthreads();
   const int count_small = s_count[0];
-  const int count_large = s_count[1];
-  const int steps = count_small + count_large;
+  const int steps = count_small + s_count[1];
+  auto jof = [&](int step) { return step < count_small ? step : p.j_small + (step - count_small); };
 
   const bool row_ok = n < p.N && n >= p.query_start;
   const int64_t nn = n < p.N ? n : p.N - 1;
   const int d0 = sub * 16;
-
   float q[16];
   {
     RowSlice<false> qs;
     qs.load(p.q + b * p.sqb + h * p.sqh + nn * p.sqn + d0, true);
     qs.to_f32(q);
   }
-  const float yq = p.y[b * p.syb + h * p.syh + nn * p.syn + sub];
-  const int rot_a = p.plane_shift;  // local channel of this thread's plane
+  float qsum = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) qsum += q[i];
 
+  const uint8_t* kcb = p.kc + b * p.ccb + hk * p.cch + sub * 12;
+  const uint8_t* vcb = p.vc + b * p.ccb + hk * p.cch + sub * 12;
+  const uint16_t* ksb = p.ks + b * p.csb + hk * p.csh;
+  const uint16_t* vsb = p.vs + b * p.csb + hk * p.csh;
+  const __nv_bfloat16* kb = p.k + b * p.skb + hk * p.skh + d0;
+  const __nv_bfloat16* vb = p.v + b * p.svb + hk * p.svh + d0;
+  float* my_sc = s_sc + qi * L.sc_ld;
+  const float* my_qe = s_qe + qi * L.qe_ld;
+
+  // ---- pass 1: scores and their maximum
+  float m = -INFINITY;
+  {
+    RowSlice<Q6> kn;
+    auto fetch = [&](int step, RowSlice<Q6>& kr) {
+      const int64_t src = n - s_off[jof(step)];
+      const bool ok = row_ok && src >= 0;
+      const int64_t s = ok ? src : 0;
+      if constexpr (Q6) kr.load(kcb + s * p.cct, ksb + s * p.cst, ok);
+      else kr.load(kb + s * p.skn, ok);
+    };
+    if (steps > 0) fetch(0, kn);
+    for (int step = 0; step < steps; ++step) {
+      const RowSlice<Q6> kc = kn;
+      if (step + 1 < steps) fetch(step + 1, kn);
+      const int j = jof(step);
+      float kv[16], part = 0.0f;
+      if constexpr (Q6) {
+        float stepk;
+        kc.to_u(kv, stepk);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) part = fmaf(q[i], kv[i], part);
+        part = (part - 32.0f * qsum) * stepk;
+      } else {
+        kc.to_f32(kv);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) part = fmaf(q[i], kv[i], part);
+      }
+      part += __shfl_xor_sync(0xffffffffu, part, 1);
+      part += __shfl_xor_sync(0xffffffffu, part, 2);
+      const bool valid = row_ok && n - s_off[j] >= 0;
+      const float score = valid ? (part + my_qe[j]) * 0.125f + s_pb[j] : -INFINITY;
+      if (sub == 0) my_sc[step] = score;
+      m = fmaxf(m, score);
+    }
+  }
+  __syncwarp();
+
+  // ---- pass 2: weights against the final max, V accumulation
   float acc[16];
 #pragma unroll
   for (int i = 0; i < 16; ++i) acc[i] = 0.0f;
-  float m = -INFINITY, l = 0.0f;
-
-  auto jof = [&](int step) { return step < count_small ? step : p.j_small + (step - count_small); };
-
-  RowSlice<Q6> kn, vn;
-  float zn = 0.0f;
-  auto fetch = [&](int step, RowSlice<Q6>& kr, RowSlice<Q6>& vr, float& zr) {
-    const int j = jof(step);
-    const int64_t src = n - s_off[j];
-    const bool ok = row_ok && src >= 0;
-    const int64_t s = ok ? src : 0;
-    if constexpr (Q6) {
-      kr.load(p.kc + b * p.ccb + hk * p.cch + s * p.cct + sub * 12, p.ks + b * p.csb + hk * p.csh + s * p.cst, ok);
-      vr.load(p.vc + b * p.ccb + hk * p.cch + s * p.cct + sub * 12, p.vs + b * p.csb + hk * p.csh + s * p.cst, ok);
-    } else {
-      kr.load(p.k + b * p.skb + hk * p.skh + s * p.skn + d0, ok);
-      vr.load(p.v + b * p.svb + hk * p.svh + s * p.svn + d0, ok);
-    }
-    zr = (ok && j >= p.j_small) ? __ldg(p.z + b * p.szb + hk * p.szh + s * p.szn + sub) : 0.0f;
-  };
-  if (steps > 0) fetch(0, kn, vn, zn);
-
-  for (int step = 0; step < steps; ++step) {
-    const RowSlice<Q6> kc = kn, vc = vn;
-    const float zc = zn;
-    if (step + 1 < steps) fetch(step + 1, kn, vn, zn);
-    const int j = jof(step);
-    const bool valid = row_ok && n - s_off[j] >= 0;
-
-    float kv[16];
-    kc.to_f32(kv);
-    const float* e = s_se + j * 64 + d0;
-    float part = 0.0f;
+  float l = 0.0f, wbias = 0.0f;  // wbias: sum of w * step_v (q6 offset correction)
+  const float msafe = m == -INFINITY ? 0.0f : m;
+  const float yq = p.y[b * p.syb + h * p.syh + nn * p.syn + sub];
+  const int rot_a = p.plane_shift;
+  {
+    RowSlice<Q6> vn;
+    float zn = 0.0f;
+    auto fetch = [&](int step, RowSlice<Q6>& vr, float& zr) {
+      const int j = jof(step);
+      const int64_t src = n - s_off[j];
+      const bool ok = row_ok && src >= 0;
+      const int64_t s = ok ? src : 0;
+      if constexpr (Q6) vr.load(vcb + s * p.cct, vsb + s * p.cst, ok);
+      else vr.load(vb + s * p.svn, ok);
+      zr = (ok && j >= p.j_small) ? __ldg(p.z + b * p.szb + hk * p.szh + s * p.szn + sub) : 0.0f;
+    };
+    if (steps > 0) fetch(0, vn, zn);
+    for (int step = 0; step < steps; ++step) {
+      const RowSlice<Q6> vc = vn;
+      const float zc = zn;
+      if (step + 1 < steps) fetch(step + 1, vn, zn);
+      const float score = my_sc[step];
+      if (score == -INFINITY) continue;  // uniform across the query's 4 threads
+      const int j = jof(step);
+      const float w = exp2f((score - msafe) * kLog2e);
+      l += w;
+      float vv[16];
+      float wv;            // weight applied to the decoded values
+      float stepv = 1.0f;  // q6 dequantisation step of this V row
+      if constexpr (Q6) {
+        vc.to_u(vv, stepv);
+        wv = w * stepv;
+        wbias += wv;
+      } else {
+        vc.to_f32(vv);
+        wv = w;
+      }
 #pragma unroll
-    for (int i = 0; i < 16; ++i) part = fmaf(q[i], kv[i] + e[i], part);
-    part += __shfl_xor_sync(0xffffffffu, part, 1);
-    part += __shfl_xor_sync(0xffffffffu, part, 2);
-    if (!valid) continue;  // uniform across the 4 threads of a query
-    const float score = part * 0.125f + s_pb[j];
-
-    const float m_new = fmaxf(m, score);
-    const float old_scale = l > 0.0f ? exp2f((m - m_new) * kLog2e) : 0.0f;
-    const float w = exp2f((score - m_new) * kLog2e);
-    vc.to_f32(kv);
-    if (j >= p.j_small) {
-      const int jl = j - p.j_small;
-      const float theta = s_pbase[jl * 4 + sub] + s_pgain[jl * 4 + sub] * yq * zc;
-      float sn, cs;
-      sincosf(theta, &sn, &cs);
+      for (int i = 0; i < 16; ++i) acc[i] = fmaf(wv, vv[i], acc[i]);
+      if (j >= p.j_small) {
+        const int jl = j - p.j_small;
+        const float theta = s_pbase[jl * 4 + sub] + s_pgain[jl * 4 + sub] * yq * zc;
+        float sn, cs;
+        sincosf(theta, &sn, &cs);
 #pragma unroll
-      for (int i = 0; i < 15; ++i) {
-        if (i == rot_a) {
-          const float va = kv[i], vb = kv[i + 1];
-          kv[i] = cs * va - sn * vb;
-          kv[i + 1] = sn * va + cs * vb;
+        for (int i = 0; i < 15; ++i) {
+          if (i == rot_a) {
+            // value-domain plane (q6: (u - 32) * step), rotated minus unrotated
+            const float va = Q6 ? (vv[i] - 32.0f) * stepv : vv[i];
+            const float vb2 = Q6 ? (vv[i + 1] - 32.0f) * stepv : vv[i + 1];
+            acc[i] += w * ((cs - 1.0f) * va - sn * vb2);
+            acc[i + 1] += w * (sn * va + (cs - 1.0f) * vb2);
+          }
         }
       }
     }
-#pragma unroll
-    for (int i = 0; i < 16; ++i) acc[i] = fmaf(acc[i], old_scale, w * kv[i]);
-    l = l * old_scale + w;
-    m = m_new;
   }
 
   if (n >= p.N) return;
-  const float inv = 1.0f;
-  (void)inv;
   float o[16];
 #pragma unroll
-  for (int i = 0; i < 16; ++i) o[i] = l > 0.0f ? round_bf16(acc[i] / l) : 0.0f;
+  for (int i = 0; i < 16; ++i) o[i] = l > 0.0f ? round_bf16((acc[i] - 32.0f * wbias) / l) : 0.0f;
   if (p.gain != nullptr) {
     const float g = p.gain_bf16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.gain)[h])
                                 : reinterpret_cast<const float*>(p.gain)[h];
@@ -284,7 +430,7 @@ dsqg_fwd_kernel(const DsqgParams p) {
   dst[0] = packed[0];
   dst[1] = packed[1];
   if (p.lse != nullptr && sub == 0) {
-    p.lse[b * p.slb + h * p.slh + n * p.sln] = l > 0.0f ? m + log2f(l) * (1.0f / kLog2e) : -INFINITY;
+    p.lse[b * p.slb + h * p.slh + n * p.sln] = l > 0.0f ? m + logf(l) : -INFINITY;
   }
 }
 
@@ -346,7 +492,7 @@ extern "C" int dwarf_dsqg_fwd(const dwarf_dsqg_fwd_args* a, void* stream) {
   p.gain = a->head_gain; p.gain_bf16 = a->head_gain_dtype == DWARF_BF16;
   p.gate = (const __nv_bfloat16*)a->gate; p.sgtb = a->sgb_; p.sgtn = a->sgn_;
 
-  const size_t smem = (size_t)a->J * 64 * 4 + (size_t)a->J * 8 + (size_t)a->j_large * 32;
+  const size_t smem = DsqgSmem(a->J, a->j_large).bytes;
   dim3 grid((unsigned)((a->N + kQB - 1) / kQB), (unsigned)a->H, (unsigned)a->B);
   if (grid.z > 65535 || grid.y > 65535) return DWARF_ERR_SHAPE;
   if (q6) {

@@ -4,7 +4,8 @@
 // Replaces the y_pre/z_pre einsums of DSQGAttentionV19.forward
 // (kernels/dsqg_attention_v22.py:3231-3254). 16 threads own one row, 4
 // values each; norms, probe dots and the q6 row maximum are 16-lane shuffle
-// reductions. Rows are numbered q rows first, then k rows, then v rows.
+// reductions; the q6 row is assembled in shared memory and written as three
+// 16-byte stores.
 #include "common.cuh"
 #include "q6_format.cuh"
 
@@ -12,7 +13,7 @@ namespace dwarf {
 namespace {
 
 struct PrepParams {
-  int64_t H, Hkv, N, rows_q, rows_k;
+  int64_t H, Hkv, N;
   int pack;
   const __nv_bfloat16 *q, *k, *v;
   int64_t sqb, sqh, sqn, skb, skh, skn, svb, svh, svn;
@@ -28,50 +29,51 @@ __device__ __forceinline__ float sum16(float v) {
   return v;
 }
 
+// grid = (ceil(N/16), H + Hkv (+ Hkv when packing), B); blockIdx.y picks the
+// tensor and head: [0, H) query heads, [H, H+Hkv) key heads, then value heads.
+// 16 rows per CTA, 16 lanes per row, 4 values per lane.
 __global__ void __launch_bounds__(256) dsqg_prep_kernel(const PrepParams p) {
-  const int64_t row = (int64_t)blockIdx.x * 16 + threadIdx.x / 16;
+  __shared__ float probes[2][4][64];
+  __shared__ __align__(16) uint8_t codes[16][48];
+  for (int i = threadIdx.x; i < 2 * 4 * 64; i += 256)
+    probes[i / 256][(i / 64) & 3][i & 63] = (i < 256 ? p.qp : p.kp)[i & 255];
+  __syncthreads();
   const int g = threadIdx.x & 15;
-  const int64_t rows_v = p.pack ? p.rows_k : 0;
-  const int64_t total = p.rows_q + p.rows_k + rows_v;
-  const bool active = row < total;
-  int kind = 0;  // 0 = q, 1 = k, 2 = v
-  int64_t r = active ? row : 0;
-  if (r >= p.rows_q) { r -= p.rows_q; kind = 1; if (r >= p.rows_k) { r -= p.rows_k; kind = 2; } }
-  const int64_t heads = kind == 0 ? p.H : p.Hkv;
-  const int64_t t = r % p.N;
-  const int64_t h = (r / p.N) % heads;
-  const int64_t b = r / (p.N * heads);
-  const __nv_bfloat16* src = kind == 0 ? p.q + b * p.sqb + h * p.sqh + t * p.sqn
-                           : kind == 1 ? p.k + b * p.skb + h * p.skh + t * p.skn
-                                       : p.v + b * p.svb + h * p.svh + t * p.svn;
+  const int lr = threadIdx.x >> 4;  // local row
+  const int64_t t = (int64_t)blockIdx.x * 16 + lr;
+  const bool active = t < p.N;
+  const int64_t b = blockIdx.z;
+  int hy = blockIdx.y, kind = 0;
+  if (hy >= p.H) { hy -= (int)p.H; kind = 1; if (hy >= p.Hkv) { hy -= (int)p.Hkv; kind = 2; } }
+  const int64_t tt = active ? t : p.N - 1;
+  const __nv_bfloat16* src = kind == 0 ? p.q + b * p.sqb + hy * p.sqh + tt * p.sqn
+                           : kind == 1 ? p.k + b * p.skb + hy * p.skh + tt * p.skn
+                                       : p.v + b * p.svb + hy * p.svh + tt * p.svn;
   float x[4];
   {
     const uint2 w = *reinterpret_cast<const uint2*>(src + g * 4);
     x[0] = __uint_as_float(w.x << 16); x[1] = __uint_as_float(w.x & 0xffff0000u);
     x[2] = __uint_as_float(w.y << 16); x[3] = __uint_as_float(w.y & 0xffff0000u);
   }
-  // Every lane runs every shuffle (the two rows of a warp may be of different
-  // kinds); results are used only where they apply.
-  {
-    const float* probe = kind == 0 ? p.qp : p.kp;
+  const int heads = kind == 0 ? (int)p.H : (int)p.Hkv;
+  // kind is uniform over the CTA, so these branches never split a warp.
+  if (kind < 2) {
+    const float (*pr)[64] = probes[kind];
     float ss = x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3];
     float dots[4];
 #pragma unroll
-    for (int pl = 0; pl < 4; ++pl) {
-      const float* pr = probe + pl * 64 + g * 4;
-      dots[pl] = x[0] * pr[0] + x[1] * pr[1] + x[2] * pr[2] + x[3] * pr[3];
-    }
+    for (int pl = 0; pl < 4; ++pl)
+      dots[pl] = x[0] * pr[pl][g * 4] + x[1] * pr[pl][g * 4 + 1] + x[2] * pr[pl][g * 4 + 2] + x[3] * pr[pl][g * 4 + 3];
     ss = sum16(ss);
 #pragma unroll
     for (int pl = 0; pl < 4; ++pl) dots[pl] = sum16(dots[pl]);
     const float inv = rsqrtf(ss + 1e-6f * 64.0f);
-    if (active && kind < 2 && g < 4) {
-      float* dst = (kind == 0 ? p.y : p.z) + ((b * heads + h) * p.N + t) * 4;
-      const float dg = g == 0 ? dots[0] : g == 1 ? dots[1] : g == 2 ? dots[2] : dots[3];
-      dst[g] = dg * inv;
+    if (active && g == 0) {
+      float* dst = (kind == 0 ? p.y : p.z) + ((b * heads + hy) * p.N + t) * 4;
+      *reinterpret_cast<float4*>(dst) = make_float4(dots[0] * inv, dots[1] * inv, dots[2] * inv, dots[3] * inv);
     }
   }
-  if (p.pack) {
+  if (p.pack && kind > 0) {
     float amax = fmaxf(fmaxf(fabsf(x[0]), fabsf(x[1])), fmaxf(fabsf(x[2]), fabsf(x[3])));
 #pragma unroll
     for (int o = 8; o >= 1; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o, 16));
@@ -80,14 +82,14 @@ __global__ void __launch_bounds__(256) dsqg_prep_kernel(const PrepParams p) {
     uint32_t w = 0;
 #pragma unroll
     for (int i = 0; i < 4; ++i) w |= (uint32_t)(q6_quantize(x[i], sf) & 63) << (6 * i);
-    if (active && kind > 0) {
-      const int64_t rr = (b * p.Hkv + h) * p.N + t;
-      uint8_t* dst = (kind == 1 ? p.kc : p.vc) + rr * 48 + g * 3;
-      dst[0] = (uint8_t)(w & 255u);
-      dst[1] = (uint8_t)((w >> 8) & 255u);
-      dst[2] = (uint8_t)((w >> 16) & 255u);
-      if (g == 0) (kind == 1 ? p.ks : p.vs)[rr] = __half_as_ushort(s);
-    }
+    codes[lr][g * 3] = (uint8_t)(w & 255u);
+    codes[lr][g * 3 + 1] = (uint8_t)((w >> 8) & 255u);
+    codes[lr][g * 3 + 2] = (uint8_t)((w >> 16) & 255u);
+    __syncwarp();
+    const int64_t rr = (b * p.Hkv + hy) * p.N + t;
+    if (active && g < 3)
+      reinterpret_cast<uint4*>((kind == 1 ? p.kc : p.vc) + rr * 48)[g] = reinterpret_cast<const uint4*>(codes[lr])[g];
+    if (active && g == 3) (kind == 1 ? p.ks : p.vs)[rr] = __half_as_ushort(s);
   }
 }
 
@@ -108,8 +110,6 @@ extern "C" int dwarf_dsqg_prep(const dwarf_dsqg_prep_args* a, void* stream) {
   if (a->pack_q6 && (a->svb | a->svh | a->svn) % 4 != 0) return DWARF_ERR_ALIGN;
   PrepParams p{};
   p.H = a->H; p.Hkv = a->H_kv; p.N = a->N;
-  p.rows_q = a->B * a->H * a->N;
-  p.rows_k = a->B * a->H_kv * a->N;
   p.pack = a->pack_q6 ? 1 : 0;
   p.q = (const __nv_bfloat16*)a->q; p.k = (const __nv_bfloat16*)a->k; p.v = (const __nv_bfloat16*)a->v;
   p.sqb = a->sqb; p.sqh = a->sqh; p.sqn = a->sqn;
@@ -117,9 +117,9 @@ extern "C" int dwarf_dsqg_prep(const dwarf_dsqg_prep_args* a, void* stream) {
   p.svb = a->svb; p.svh = a->svh; p.svn = a->svn;
   p.qp = a->q_probe; p.kp = a->k_probe; p.y = a->y_pre; p.z = a->z_pre;
   p.kc = a->k_codes; p.vc = a->v_codes; p.ks = a->k_scales; p.vs = a->v_scales;
-  const int64_t total = p.rows_q + p.rows_k + (p.pack ? p.rows_k : 0);
-  const int64_t blocks = (total + 15) / 16;
-  if (blocks > 0x7fffffffLL) return DWARF_ERR_SHAPE;
-  dsqg_prep_kernel<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(p);
+  const int64_t ys = a->H + a->H_kv + (p.pack ? a->H_kv : 0);
+  if (ys > 65535 || a->B > 65535 || (a->N + 15) / 16 > 0x7fffffffLL) return DWARF_ERR_SHAPE;
+  dim3 grid((unsigned)((a->N + 15) / 16), (unsigned)ys, (unsigned)a->B);
+  dsqg_prep_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(p);
   return launch_status();
 }
