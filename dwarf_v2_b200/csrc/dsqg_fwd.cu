@@ -23,11 +23,13 @@
 #include "q6_format.cuh"
 #include "warp_mma.cuh"
 
+#include <cstdlib>
+#include <type_traits>
+
 namespace dwarf {
 namespace {
 
-constexpr int kQB = 64;       // queries per CTA
-constexpr int kThreads = 256;  // 4 per query
+constexpr int kThreads = 256;  // threads per CTA
 constexpr float kLog2e = 1.4426950408889634f;
 
 struct DsqgParams {
@@ -81,29 +83,44 @@ __device__ __forceinline__ void bf16x16_to_f32(const uint4 (&w)[2], float (&o)[1
 }
 
 // q6 row slice of one thread (16 codes = 12 bytes) decoded as offset-binary
-// u = c + 32 in [1, 63]: XOR-ing bit 5 of every 6-bit field turns two's
-// complement into offset binary, and float(u) comes from the exponent trick
-// (0x4B000000 | u) - 2^23, so no int->float conversion instruction is needed.
-// The caller removes the +32 bias with one per-row correction.
+// u = c + 32 in [1, 63]. XOR-ing bit 5 of every 6-bit field turns two's
+// complement into offset binary. Field i is then read in place, scaled by a
+// power of two 2^K_i: masking its 6 bits (at bit K_i <= 17, after at most one
+// shift of its word) into the mantissa of 2^23 and subtracting 2^23 gives
+// u_i * 2^K_i exactly, with one LOP3 and one FADD and no int->float
+// conversion. Callers pre-scale q by 2^-K_i (K path) or post-scale the
+// accumulator (V path), and remove the +32 bias with one per-row term.
 __device__ __forceinline__ void q6_flip_sign_bits(uint32_t (&w)[3]) {
   w[0] ^= 0x20820820u;  // stream bits 5, 11, 17, 23, 29
   w[1] ^= 0x08208208u;  // stream bits 35, 41, 47, 53, 59
   w[2] ^= 0x82082082u;  // stream bits 65, 71, 77, 83, 89, 95
 }
-template <int I>
-__device__ __forceinline__ float q6_u_float(const uint32_t (&w)[3]) {
-  constexpr int bit = 6 * I, word = bit >> 5, off = bit & 31;
-  uint32_t u;
-  if constexpr (off <= 26) u = (w[word] >> off) & 63u;
-  else u = __funnelshift_r(w[word], w[word + 1], off) & 63u;
-  return __int_as_float(0x4B000000u | u) - 8388608.0f;
+// Power-of-two placement K_i of field i (see q6_scaled16).
+__host__ __device__ constexpr int q6_field_shift(int i) {
+  constexpr int k[16] = {0, 6, 12, 6, 12, 0, 4, 10, 16, 10, 0, 2, 8, 14, 8, 14};
+  return k[i];
 }
-template <int I>
-__device__ __forceinline__ void q6_u16(const uint32_t (&w)[3], float (&o)[16]) {
-  if constexpr (I < 16) {
-    o[I] = q6_u_float<I>(w);
-    q6_u16<I + 1>(w, o);
-  }
+__device__ __forceinline__ float q6_field(uint32_t src, int k) {
+  return __int_as_float(0x4B000000u | (src & (63u << k))) - 8388608.0f;
+}
+// o[i] = u_i * 2^K_i for the 16 codes of a flipped 96-bit slice.
+__device__ __forceinline__ void q6_scaled16(const uint32_t (&w)[3], float (&o)[16]) {
+  const uint32_t w0s = w[0] >> 12, w1s = w[1] >> 12, w2s = w[2] >> 12;
+  const uint32_t f5 = __funnelshift_r(w[0], w[1], 30);
+  const uint32_t f10 = __funnelshift_r(w[1], w[2], 28);
+  o[0] = q6_field(w[0], 0);   o[1] = q6_field(w[0], 6);   o[2] = q6_field(w[0], 12);
+  o[3] = q6_field(w0s, 6);    o[4] = q6_field(w0s, 12);   o[5] = q6_field(f5, 0);
+  o[6] = q6_field(w[1], 4);   o[7] = q6_field(w[1], 10);  o[8] = q6_field(w[1], 16);
+  o[9] = q6_field(w1s, 10);   o[10] = q6_field(f10, 0);   o[11] = q6_field(w[2], 2);
+  o[12] = q6_field(w[2], 8);  o[13] = q6_field(w[2], 14); o[14] = q6_field(w2s, 8);
+  o[15] = q6_field(w2s, 14);
+}
+// Unscaled u of code i (runtime index) -- used for the two MOVT plane channels.
+__device__ __forceinline__ float q6_u_at(const uint32_t (&w)[3], int i) {
+  const int bit = 6 * i, word = bit >> 5, off = bit & 31;
+  const uint32_t lo = word == 0 ? w[0] : (word == 1 ? w[1] : w[2]);
+  const uint32_t hi = word == 0 ? w[1] : w[2];
+  return (float)(__funnelshift_r(lo, hi, off) & 63u);
 }
 
 // One gathered row slice: bf16 (2 x uint4) or q6 (3 x u32 + fp16 scale).
@@ -139,31 +156,34 @@ struct RowSlice<true> {
       s = 0;
     }
   }
-  // Offset-binary values u_d (code + 32) and the dequantisation step.
-  __device__ __forceinline__ void to_u(float (&o)[16], float& step) const {
-    uint32_t t[3] = {w[0], w[1], w[2]};
+  // Offset-binary values u_d * 2^K_d (see q6_scaled16), the flipped words
+  // and the dequantisation step.
+  __device__ __forceinline__ void to_scaled(float (&o)[16], uint32_t (&t)[3], float& step) const {
+    t[0] = w[0]; t[1] = w[1]; t[2] = w[2];
     q6_flip_sign_bits(t);
-    q6_u16<0>(t, o);
-    step = q6_step(__ushort_as_half(s));
+    q6_scaled16(t, o);
+    // float(s) / 31 up to one rounding (a reciprocal multiply instead of an
+    // IEEE division per gathered row; the attention tolerance absorbs it).
+    step = __half2float(__ushort_as_half(s)) * (1.0f / 31.0f);
   }
 };
 
-// Shared-memory carve-up of one CTA (64 queries of one (b, h)).
+// Shared-memory carve-up of one CTA (QB queries of one (b, h)).
 struct DsqgSmem {
   int jp;       // J rounded up to a multiple of 8 (mma n-tiles)
   int qe_ld;    // row stride of qe (jp + 1 floats)
   int sc_ld;    // row stride of sc (J + 1 floats)
   size_t bytes;
   size_t o_q, o_e, o_qe, o_sc, o_pb, o_off, o_pbase, o_pgain;
-  __host__ __device__ DsqgSmem(int J, int j_large) {
+  __host__ __device__ DsqgSmem(int J, int j_large, int qb) {
     jp = (J + 7) / 8 * 8;
     qe_ld = jp + 1;
     sc_ld = J + 1;
     size_t o = 0;
-    o_q = o;      o += 64 * 128;                        // bf16 Q tile, swizzled
+    o_q = o;      o += (size_t)qb * 128;                // bf16 Q tile, swizzled
     o_e = o;      o += (size_t)jp * 128;                // bf16(scale_embed), swizzled
-    o_qe = o;     o += (size_t)64 * qe_ld * 4;          // q . bf16(E_j) (fp32)
-    o_sc = o;     o += (size_t)64 * sc_ld * 4;          // scores of pass 1
+    o_qe = o;     o += (size_t)qb * qe_ld * 4;          // q . bf16(E_j) (fp32)
+    o_sc = o;     o += (size_t)qb * sc_ld * 4;          // scores of pass 1
     o_pb = o;     o += (size_t)J * 4;
     o_off = o;    o += (size_t)J * 4;
     o_pbase = o;  o += (size_t)j_large * 16;
@@ -175,14 +195,18 @@ struct DsqgSmem {
 // Two passes per query: (1) scores of every live offset from K rows plus the
 // tensor-core q.E term, running max; (2) exp2 weights against the final max
 // and the V accumulation (no accumulator rescaling), MOVT planes rotated in
-// the owning thread. Softmax is mathematically the reference's online form.
-template <bool Q6>
+// the owning thread. TPQ threads share a query, each owning 64/TPQ dims and
+// 4/TPQ MOVT planes; a CTA of 256 threads covers QB = 256/TPQ queries.
+template <bool Q6, int TPQ>
 __global__ void __launch_bounds__(kThreads)
 dsqg_fwd_kernel(const DsqgParams p) {
   using namespace wmma16;
+  constexpr int QB = kThreads / TPQ;       // queries per CTA
+  constexpr int NS = 4 / TPQ;              // 16-dim slices (and MOVT planes) per thread
+  constexpr int DIMS = 16 * NS;
   extern __shared__ __align__(128) unsigned char smem[];
   const int J = p.J;
-  const DsqgSmem L(J, p.j_large);
+  const DsqgSmem L(J, p.j_large, QB);
   unsigned char* s_q = smem + L.o_q;
   unsigned char* s_e = smem + L.o_e;
   float* s_qe = reinterpret_cast<float*>(smem + L.o_qe);
@@ -198,15 +222,15 @@ dsqg_fwd_kernel(const DsqgParams p) {
   const int64_t hk = h / p.kv_group;
   const int tid = threadIdx.x;
   const int lane = tid & 31, warp = tid >> 5;
-  const int sub = tid & 3;
-  const int qi = tid >> 2;
-  const int64_t n0 = (int64_t)blockIdx.x * kQB;
+  const int sub = tid % TPQ;
+  const int qi = tid / TPQ;
+  const int64_t n0 = (int64_t)blockIdx.x * QB;
   const int64_t n = n0 + qi;
-  const int64_t n_last = (n0 + kQB < p.N ? n0 + kQB : p.N) - 1;
+  const int64_t n_last = (n0 + QB < p.N ? n0 + QB : p.N) - 1;
 
   // ---- stage Q tile, bf16(E), tables
   const uint32_t q_base = smem_u32(s_q), e_base = smem_u32(s_e);
-  for (int i = tid; i < 64 * 8; i += kThreads) {
+  for (int i = tid; i < QB * 8; i += kThreads) {
     const int r = i >> 3, c = i & 7;
     const int64_t row = n0 + r < p.N ? n0 + r : p.N - 1;
     const uint4 v = *reinterpret_cast<const uint4*>(p.q + b * p.sqb + h * p.sqh + row * p.sqn + c * 8);
@@ -245,193 +269,267 @@ dsqg_fwd_kernel(const DsqgParams p) {
     s_count[0] = cs;
     s_count[1] = cl;
   }
-  // ---- QE[64][jp] = Q . bf16(E)^T on tensor cores: warp w owns m-tile w&3,
-  // n-tiles (w>>2), (w>>2)+2, ...
+  // ---- QE[QB][jp] = Q . bf16(E)^T on tensor cores (m16n8k16 tiles spread over the 8 warps)
   {
-    const int mt = warp & 3;
-    uint32_t a[4][4];
-#pragma unroll
-    for (int ks = 0; ks < 4; ++ks) {
-      const int mi = lane >> 3, r = lane & 7;
-      ldsm_x4(tile_addr(q_base, mt * 16 + (mi & 1) * 8 + r, ks * 2 + (mi >> 1)), a[ks][0], a[ks][1], a[ks][2],
-              a[ks][3]);
-    }
+    constexpr int MT = QB / 16;
     const int g = lane >> 2, t4 = lane & 3;
-    for (int nt = warp >> 2; nt < L.jp / 8; nt += 2) {
-      float c[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int mt = warp % MT; mt < MT; mt += 8) {
+      uint32_t a[4][4];
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks) {
-        uint32_t b0, b1;
-        ldsm_x2(tile_addr(e_base, nt * 8 + (lane & 7), ks * 2 + ((lane >> 3) & 1)), b0, b1);
-        mma_bf16(c, a[ks], b0, b1);
+        const int mi = lane >> 3, r = lane & 7;
+        ldsm_x4(tile_addr(q_base, mt * 16 + (mi & 1) * 8 + r, ks * 2 + (mi >> 1)), a[ks][0], a[ks][1], a[ks][2],
+                a[ks][3]);
       }
-      float* row0 = s_qe + (mt * 16 + g) * L.qe_ld + nt * 8 + 2 * t4;
-      float* row1 = row0 + 8 * L.qe_ld;
-      row0[0] = c[0]; row0[1] = c[1];
-      row1[0] = c[2]; row1[1] = c[3];
+      const int nstep = 8 / MT > 0 ? 8 / MT : 1;  // warps sharing this m-tile
+      for (int nt = MT >= 8 ? 0 : warp / MT; nt < L.jp / 8; nt += nstep) {
+        float c[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks) {
+          uint32_t b0, b1;
+          ldsm_x2(tile_addr(e_base, nt * 8 + (lane & 7), ks * 2 + ((lane >> 3) & 1)), b0, b1);
+          mma_bf16(c, a[ks], b0, b1);
+        }
+        float* row0 = s_qe + (mt * 16 + g) * L.qe_ld + nt * 8 + 2 * t4;
+        float* row1 = row0 + 8 * L.qe_ld;
+        row0[0] = c[0]; row0[1] = c[1];
+        row1[0] = c[2]; row1[1] = c[3];
+      }
     }
   }
   __syncthreads();
   const int count_small = s_count[0];
-  const int steps = count_small + s_count[1];
-  auto jof = [&](int step) { return step < count_small ? step : p.j_small + (step - count_small); };
+  const int count_large = s_count[1];
 
   const bool row_ok = n < p.N && n >= p.query_start;
-  const int64_t nn = n < p.N ? n : p.N - 1;
-  const int d0 = sub * 16;
-  float q[16];
-  {
-    RowSlice<false> qs;
-    qs.load(p.q + b * p.sqb + h * p.sqh + nn * p.sqn + d0, true);
-    qs.to_f32(q);
-  }
+  const int nq = (int)(n < p.N ? n : p.N - 1);
+  const int d0 = sub * DIMS;
+  float qs[DIMS];  // q, pre-scaled by 2^-K_i for the q6 field placement (exact)
   float qsum = 0.0f;
 #pragma unroll
-  for (int i = 0; i < 16; ++i) qsum += q[i];
+  for (int sl = 0; sl < NS; ++sl) {
+    RowSlice<false> qr;
+    qr.load(p.q + b * p.sqb + h * p.sqh + (int64_t)nq * p.sqn + d0 + 16 * sl, true);
+    float t[16];
+    qr.to_f32(t);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      qsum += t[i];
+      qs[16 * sl + i] = Q6 ? t[i] * __int_as_float((127 - q6_field_shift(i)) << 23) : t[i];
+    }
+  }
 
-  const uint8_t* kcb = p.kc + b * p.ccb + hk * p.cch + sub * 12;
-  const uint8_t* vcb = p.vc + b * p.ccb + hk * p.cch + sub * 12;
+  // Per-thread bases; row offsets below are 32-bit (the host checks N * stride < 2^31).
+  const uint8_t* kcb = p.kc + b * p.ccb + hk * p.cch + sub * (12 * NS);
+  const uint8_t* vcb = p.vc + b * p.ccb + hk * p.cch + sub * (12 * NS);
   const uint16_t* ksb = p.ks + b * p.csb + hk * p.csh;
   const uint16_t* vsb = p.vs + b * p.csb + hk * p.csh;
   const __nv_bfloat16* kb = p.k + b * p.skb + hk * p.skh + d0;
   const __nv_bfloat16* vb = p.v + b * p.svb + hk * p.svh + d0;
+  const float* zb = p.z + b * p.szb + hk * p.szh + sub * NS;
+  const int cct = (int)p.cct, cst = (int)p.cst, skn = (int)p.skn, svn = (int)p.svn, szn = (int)p.szn;
   float* my_sc = s_sc + qi * L.sc_ld;
   const float* my_qe = s_qe + qi * L.qe_ld;
+  const int nrow = row_ok ? nq : -1;  // src = nrow - off < 0 marks an invalid pair
 
-  // ---- pass 1: scores and their maximum
+  // ---- pass 1: scores of the live offsets (small band, then large band) and their max
   float m = -INFINITY;
-  {
-    RowSlice<Q6> kn;
-    auto fetch = [&](int step, RowSlice<Q6>& kr) {
-      const int64_t src = n - s_off[jof(step)];
-      const bool ok = row_ok && src >= 0;
-      const int64_t s = ok ? src : 0;
-      if constexpr (Q6) kr.load(kcb + s * p.cct, ksb + s * p.cst, ok);
-      else kr.load(kb + s * p.skn, ok);
-    };
-    if (steps > 0) fetch(0, kn);
-    for (int step = 0; step < steps; ++step) {
-      const RowSlice<Q6> kc = kn;
-      if (step + 1 < steps) fetch(step + 1, kn);
-      const int j = jof(step);
-      float kv[16], part = 0.0f;
-      if constexpr (Q6) {
-        float stepk;
-        kc.to_u(kv, stepk);
+  auto score_band = [&](int j_begin, int count, int slot0) {
+    RowSlice<Q6> kn[NS];
+    auto fetch = [&](int j, RowSlice<Q6> (&kr)[NS]) {
+      const int src = nrow - s_off[j];
+      const bool ok = src >= 0;
+      const int r = ok ? src : 0;
 #pragma unroll
-        for (int i = 0; i < 16; ++i) part = fmaf(q[i], kv[i], part);
-        part = (part - 32.0f * qsum) * stepk;
-      } else {
-        kc.to_f32(kv);
-#pragma unroll
-        for (int i = 0; i < 16; ++i) part = fmaf(q[i], kv[i], part);
+      for (int sl = 0; sl < NS; ++sl) {
+        if constexpr (Q6) kr[sl].load(kcb + r * cct + 12 * sl, ksb + r * cst, ok);
+        else kr[sl].load(kb + r * skn + 16 * sl, ok);
       }
-      part += __shfl_xor_sync(0xffffffffu, part, 1);
-      part += __shfl_xor_sync(0xffffffffu, part, 2);
-      const bool valid = row_ok && n - s_off[j] >= 0;
-      const float score = valid ? (part + my_qe[j]) * 0.125f + s_pb[j] : -INFINITY;
-      if (sub == 0) my_sc[step] = score;
+    };
+    if (count > 0) fetch(j_begin, kn);
+    for (int t = 0; t < count; ++t) {
+      const int j = j_begin + t;
+      RowSlice<Q6> kc[NS];
+#pragma unroll
+      for (int sl = 0; sl < NS; ++sl) kc[sl] = kn[sl];
+      if (t + 1 < count) fetch(j + 1, kn);
+      float p0 = 0.0f, p1 = 0.0f, stepk = 1.0f;
+#pragma unroll
+      for (int sl = 0; sl < NS; ++sl) {
+        float kv[16];
+        if constexpr (Q6) {
+          uint32_t w3[3];
+          kc[sl].to_scaled(kv, w3, stepk);
+        } else {
+          kc[sl].to_f32(kv);
+        }
+#pragma unroll
+        for (int i = 0; i < 16; i += 2) {
+          p0 = fmaf(qs[16 * sl + i], kv[i], p0);
+          p1 = fmaf(qs[16 * sl + i + 1], kv[i + 1], p1);
+        }
+      }
+      float part = Q6 ? ((p0 + p1) - 32.0f * qsum) * stepk : p0 + p1;
+#pragma unroll
+      for (int o = 1; o < TPQ; o <<= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+      const float score = nrow - s_off[j] >= 0 ? (part + my_qe[j]) * 0.125f + s_pb[j] : -INFINITY;
+      if (sub == 0) my_sc[slot0 + t] = score;
       m = fmaxf(m, score);
     }
-  }
+  };
+  score_band(0, count_small, 0);
+  score_band(p.j_small, count_large, count_small);
   __syncwarp();
 
   // ---- pass 2: weights against the final max, V accumulation
-  float acc[16];
+  float acc[DIMS];
 #pragma unroll
-  for (int i = 0; i < 16; ++i) acc[i] = 0.0f;
+  for (int i = 0; i < DIMS; ++i) acc[i] = 0.0f;
   float l = 0.0f, wbias = 0.0f;  // wbias: sum of w * step_v (q6 offset correction)
+  float corr_a[NS], corr_b[NS], yq[NS];
+#pragma unroll
+  for (int sl = 0; sl < NS; ++sl) {
+    corr_a[sl] = corr_b[sl] = 0.0f;
+    yq[sl] = p.y[b * p.syb + h * p.syh + (int64_t)nq * p.syn + sub * NS + sl];
+  }
   const float msafe = m == -INFINITY ? 0.0f : m;
-  const float yq = p.y[b * p.syb + h * p.syh + nn * p.syn + sub];
   const int rot_a = p.plane_shift;
-  {
-    RowSlice<Q6> vn;
-    float zn = 0.0f;
-    auto fetch = [&](int step, RowSlice<Q6>& vr, float& zr) {
-      const int j = jof(step);
-      const int64_t src = n - s_off[j];
-      const bool ok = row_ok && src >= 0;
-      const int64_t s = ok ? src : 0;
-      if constexpr (Q6) vr.load(vcb + s * p.cct, vsb + s * p.cst, ok);
-      else vr.load(vb + s * p.svn, ok);
-      zr = (ok && j >= p.j_small) ? __ldg(p.z + b * p.szb + hk * p.szh + s * p.szn + sub) : 0.0f;
+  auto value_band = [&](int j_begin, int count, int slot0, auto large_tag) {
+    constexpr bool kLarge = decltype(large_tag)::value;
+    RowSlice<Q6> vn[NS];
+    float zn[NS];
+    auto fetch = [&](int j, RowSlice<Q6> (&vr)[NS], float (&zr)[NS]) {
+      const int src = nrow - s_off[j];
+      const bool ok = src >= 0;
+      const int r = ok ? src : 0;
+#pragma unroll
+      for (int sl = 0; sl < NS; ++sl) {
+        if constexpr (Q6) vr[sl].load(vcb + r * cct + 12 * sl, vsb + r * cst, ok);
+        else vr[sl].load(vb + r * svn + 16 * sl, ok);
+        if constexpr (kLarge) zr[sl] = ok ? __ldg(zb + r * szn + sl) : 0.0f;
+      }
     };
-    if (steps > 0) fetch(0, vn, zn);
-    for (int step = 0; step < steps; ++step) {
-      const RowSlice<Q6> vc = vn;
-      const float zc = zn;
-      if (step + 1 < steps) fetch(step + 1, vn, zn);
-      const float score = my_sc[step];
-      if (score == -INFINITY) continue;  // uniform across the query's 4 threads
-      const int j = jof(step);
+    if (count > 0) fetch(j_begin, vn, zn);
+    for (int t = 0; t < count; ++t) {
+      const int j = j_begin + t;
+      RowSlice<Q6> vc[NS];
+      float zc[NS];
+#pragma unroll
+      for (int sl = 0; sl < NS; ++sl) { vc[sl] = vn[sl]; zc[sl] = zn[sl]; }
+      if (t + 1 < count) fetch(j + 1, vn, zn);
+      const float score = my_sc[slot0 + t];
+      if (score == -INFINITY) continue;  // uniform across the query's threads
       const float w = exp2f((score - msafe) * kLog2e);
       l += w;
-      float vv[16];
-      float wv;            // weight applied to the decoded values
-      float stepv = 1.0f;  // q6 dequantisation step of this V row
-      if constexpr (Q6) {
-        vc.to_u(vv, stepv);
-        wv = w * stepv;
-        wbias += wv;
-      } else {
-        vc.to_f32(vv);
-        wv = w;
-      }
 #pragma unroll
-      for (int i = 0; i < 16; ++i) acc[i] = fmaf(wv, vv[i], acc[i]);
-      if (j >= p.j_small) {
-        const int jl = j - p.j_small;
-        const float theta = s_pbase[jl * 4 + sub] + s_pgain[jl * 4 + sub] * yq * zc;
-        float sn, cs;
-        sincosf(theta, &sn, &cs);
+      for (int sl = 0; sl < NS; ++sl) {
+        float vv[16];
+        float va = 0.0f, vb2 = 0.0f;  // value-domain channels of this slice's MOVT plane
+        if constexpr (Q6) {
+          float stepv;
+          uint32_t w3[3];
+          vc[sl].to_scaled(vv, w3, stepv);
+          const float wv = w * stepv;
+          if (sl == 0) wbias += wv;
 #pragma unroll
-        for (int i = 0; i < 15; ++i) {
-          if (i == rot_a) {
-            // value-domain plane (q6: (u - 32) * step), rotated minus unrotated
-            const float va = Q6 ? (vv[i] - 32.0f) * stepv : vv[i];
-            const float vb2 = Q6 ? (vv[i + 1] - 32.0f) * stepv : vv[i + 1];
-            acc[i] += w * ((cs - 1.0f) * va - sn * vb2);
-            acc[i + 1] += w * (sn * va + (cs - 1.0f) * vb2);
+          for (int i = 0; i < 16; ++i) acc[16 * sl + i] = fmaf(wv, vv[i], acc[16 * sl + i]);
+          if constexpr (kLarge) {
+            va = (q6_u_at(w3, rot_a) - 32.0f) * stepv;
+            vb2 = (q6_u_at(w3, rot_a + 1) - 32.0f) * stepv;
+          }
+        } else {
+          vc[sl].to_f32(vv);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) acc[16 * sl + i] = fmaf(w, vv[i], acc[16 * sl + i]);
+          if constexpr (kLarge) {
+#pragma unroll
+            for (int i = 0; i < 15; ++i) {
+              if (i == rot_a) { va = vv[i]; vb2 = vv[i + 1]; }
+            }
           }
         }
+        if constexpr (kLarge) {
+          // MOVT: rotate this slice's plane; accumulate rotated-minus-unrotated.
+          const int jl = j - p.j_small;
+          const int plane = sub * NS + sl;
+          const float theta = s_pbase[jl * 4 + plane] + s_pgain[jl * 4 + plane] * yq[sl] * zc[sl];
+          float sn, cs;
+          __sincosf(theta, &sn, &cs);
+          corr_a[sl] += w * ((cs - 1.0f) * va - sn * vb2);
+          corr_b[sl] += w * (sn * va + (cs - 1.0f) * vb2);
+        }
       }
+    }
+  };
+  value_band(0, count_small, 0, std::false_type{});
+  value_band(p.j_small, count_large, count_small, std::true_type{});
+
+  // Fold the plane corrections in, undo the q6 field scaling and bias.
+  // (All slices of a row share one scale, so wbias is per row.)
+#pragma unroll
+  for (int sl = 0; sl < NS; ++sl) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      float v = Q6 ? acc[16 * sl + i] * __int_as_float((127 - q6_field_shift(i)) << 23) - 32.0f * wbias
+                   : acc[16 * sl + i];
+      if (i == rot_a) v += corr_a[sl];
+      if (i == rot_a + 1) v += corr_b[sl];
+      acc[16 * sl + i] = v;
     }
   }
 
   if (n >= p.N) return;
-  float o[16];
+  float gain = 1.0f;
+  if (p.gain != nullptr)
+    gain = p.gain_bf16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.gain)[h])
+                       : reinterpret_cast<const float*>(p.gain)[h];
 #pragma unroll
-  for (int i = 0; i < 16; ++i) o[i] = l > 0.0f ? round_bf16((acc[i] - 32.0f * wbias) / l) : 0.0f;
-  if (p.gain != nullptr) {
-    const float g = p.gain_bf16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.gain)[h])
-                                : reinterpret_cast<const float*>(p.gain)[h];
+  for (int sl = 0; sl < NS; ++sl) {
+    float o[16];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) o[i] = p.gain_bf16 ? round_bf16(o[i] * g) : o[i] * g;
-  }
-  if (p.gate != nullptr) {
-    RowSlice<false> gs;
-    gs.load(p.gate + b * p.sgtb + n * p.sgtn + h * 64 + d0, true);
-    float gv[16];
-    gs.to_f32(gv);
+    for (int i = 0; i < 16; ++i) o[i] = l > 0.0f ? round_bf16(acc[16 * sl + i] / l) : 0.0f;
+    if (p.gain != nullptr) {
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const float sg = round_bf16(1.0f / (1.0f + expf(-gv[i])));
-      o[i] = p.gain_bf16 || p.gain == nullptr ? round_bf16(o[i] * sg) : o[i] * sg;
+      for (int i = 0; i < 16; ++i) o[i] = p.gain_bf16 ? round_bf16(o[i] * gain) : o[i] * gain;
     }
-  }
-  uint4 packed[2];
-  uint32_t* pw = reinterpret_cast<uint32_t*>(packed);
+    if (p.gate != nullptr) {
+      RowSlice<false> gs;
+      gs.load(p.gate + b * p.sgtb + n * p.sgtn + h * 64 + d0 + 16 * sl, true);
+      float gv[16];
+      gs.to_f32(gv);
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const __nv_bfloat162 two = __floats2bfloat162_rn(o[2 * i], o[2 * i + 1]);
-    pw[i] = *reinterpret_cast<const uint32_t*>(&two);
+      for (int i = 0; i < 16; ++i) {
+        const float sg = round_bf16(1.0f / (1.0f + expf(-gv[i])));
+        o[i] = p.gain_bf16 || p.gain == nullptr ? round_bf16(o[i] * sg) : o[i] * sg;
+      }
+    }
+    uint4 packed[2];
+    uint32_t* pw = reinterpret_cast<uint32_t*>(packed);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const __nv_bfloat162 two = __floats2bfloat162_rn(o[2 * i], o[2 * i + 1]);
+      pw[i] = *reinterpret_cast<const uint32_t*>(&two);
+    }
+    uint4* dst = reinterpret_cast<uint4*>(p.out + b * p.sob + h * p.soh + n * p.son + d0 + 16 * sl);
+    dst[0] = packed[0];
+    dst[1] = packed[1];
   }
-  uint4* dst = reinterpret_cast<uint4*>(p.out + b * p.sob + h * p.soh + n * p.son + d0);
-  dst[0] = packed[0];
-  dst[1] = packed[1];
   if (p.lse != nullptr && sub == 0) {
     p.lse[b * p.slb + h * p.slh + n * p.sln] = l > 0.0f ? m + logf(l) : -INFINITY;
   }
+}
+
+template <bool Q6, int TPQ>
+int launch_dsqg(const DsqgParams& p, int64_t B, int64_t H, int64_t N, int J, int j_large, cudaStream_t stream) {
+  constexpr int QB = kThreads / TPQ;
+  const size_t smem = DsqgSmem(J, j_large, QB).bytes;
+  dim3 grid((unsigned)((N + QB - 1) / QB), (unsigned)H, (unsigned)B);
+  if (grid.z > 65535 || grid.y > 65535) return DWARF_ERR_SHAPE;
+  auto kernel = dsqg_fwd_kernel<Q6, TPQ>;
+  if (smem > 48 * 1024 && cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem))
+    return DWARF_ERR_LAUNCH;
+  kernel<<<grid, kThreads, smem, stream>>>(p);
+  return launch_status();
 }
 
 bool a16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -469,6 +567,11 @@ extern "C" int dwarf_dsqg_fwd(const dwarf_dsqg_fwd_args* a, void* stream) {
   if (a->head_gain != nullptr && a->head_gain_dtype != DWARF_F32 && a->head_gain_dtype != DWARF_BF16)
     return DWARF_ERR_DTYPE;
 
+  // Row offsets inside the kernel are 32-bit.
+  const int64_t lim = (int64_t)1 << 31;
+  if (a->N * (q6 ? (a->cct > a->cst ? a->cct : a->cst) : (a->skn > a->svn ? a->skn : a->svn)) >= lim ||
+      a->N * a->szn >= lim)
+    return DWARF_ERR_SHAPE;
   DsqgParams p{};
   p.H = a->H; p.Hkv = a->H_kv; p.N = a->N;
   p.J = a->J; p.j_small = a->j_small; p.j_large = a->j_large;
@@ -492,19 +595,16 @@ extern "C" int dwarf_dsqg_fwd(const dwarf_dsqg_fwd_args* a, void* stream) {
   p.gain = a->head_gain; p.gain_bf16 = a->head_gain_dtype == DWARF_BF16;
   p.gate = (const __nv_bfloat16*)a->gate; p.sgtb = a->sgb_; p.sgtn = a->sgn_;
 
-  const size_t smem = DsqgSmem(a->J, a->j_large).bytes;
-  dim3 grid((unsigned)((a->N + kQB - 1) / kQB), (unsigned)a->H, (unsigned)a->B);
-  if (grid.z > 65535 || grid.y > 65535) return DWARF_ERR_SHAPE;
-  if (q6) {
-    if (smem > 48 * 1024 &&
-        cudaFuncSetAttribute(dsqg_fwd_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem))
-      return DWARF_ERR_LAUNCH;
-    dsqg_fwd_kernel<true><<<grid, kThreads, smem, (cudaStream_t)stream>>>(p);
-  } else {
-    if (smem > 48 * 1024 &&
-        cudaFuncSetAttribute(dsqg_fwd_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem))
-      return DWARF_ERR_LAUNCH;
-    dsqg_fwd_kernel<false><<<grid, kThreads, smem, (cudaStream_t)stream>>>(p);
-  }
-  return launch_status();
+  // 2 threads per query (32 dims each): half the per-pair bookkeeping of the
+  // 4-thread layout. DWARF_DSQG_TPQ=4 selects the 4-thread layout.
+  static const int tpq = [] {
+    const char* e = getenv("DWARF_DSQG_TPQ");
+    return (e && e[0] == '4') ? 4 : 2;
+  }();
+  cudaStream_t st = (cudaStream_t)stream;
+  if (q6) return tpq == 4 ? launch_dsqg<true, 4>(p, a->B, a->H, a->N, a->J, a->j_large, st)
+                          : launch_dsqg<true, 2>(p, a->B, a->H, a->N, a->J, a->j_large, st);
+  return tpq == 4 ? launch_dsqg<false, 4>(p, a->B, a->H, a->N, a->J, a->j_large, st)
+                  : launch_dsqg<false, 2>(p, a->B, a->H, a->N, a->J, a->j_large, st);
 }
+

@@ -34,12 +34,8 @@ __device__ __forceinline__ void load4(const void* base, int64_t off, float (&v)[
 }
 
 template <typename T>
-__global__ void __launch_bounds__(256) npci_kernel(const NpciParams p) {
-  const int64_t rows = p.B * p.H * p.N;
-  const int64_t row = (int64_t)blockIdx.x * 16 + threadIdx.x / 16;
-  const int g = threadIdx.x & 15;
-  const int64_t r = row < rows ? row : rows - 1;
-  const int64_t n = r % p.N, h = (r / p.N) % p.H, b = r / (p.N * p.H);
+__device__ __forceinline__ void npci_row(const NpciParams& p, int64_t b, int64_t h, int64_t n, bool active_row,
+                                         int g) {
   float x[4], d[4];
   load4<T>(p.x, b * p.sxb + h * p.sxh + n * p.sxn + g * 4, x);
   if (p.add != nullptr) {
@@ -70,13 +66,27 @@ __global__ void __launch_bounds__(256) npci_kernel(const NpciParams p) {
   float sn, cs;
   sincosf(angle, &sn, &cs);
   const float inv_pn = 1.0f / fmaxf(pn, 1e-20f);
-  if (row >= rows) return;
+  if (!active_row) return;
   T* o = static_cast<T*>(p.out) + b * p.sob + h * p.soh + n * p.son + g * 4;
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const float dir = active ? perp[i] * inv_pn : 0.0f;
     const float rot = cs * x[i] + sn * norm * dir;
     o[i] = static_cast<T>(active ? rot : x[i]);
+  }
+}
+
+constexpr int kRowGroups = 8;  // 16-row groups per CTA
+
+// grid = (ceil(N / 128), H, B): each CTA rotates 128 consecutive tokens of one
+// (b, h), 16 lanes per 64-value row.
+template <typename T>
+__global__ void __launch_bounds__(256) npci_kernel(const NpciParams p) {
+  const int64_t h = blockIdx.y, b = blockIdx.z;
+  const int g = threadIdx.x & 15;
+  for (int grp = 0; grp < kRowGroups; ++grp) {
+    const int64_t row = ((int64_t)blockIdx.x * kRowGroups + grp) * 16 + threadIdx.x / 16;
+    npci_row<T>(p, b, h, row < p.N ? row : p.N - 1, row < p.N, g);
   }
 }
 
@@ -89,17 +99,17 @@ extern "C" int dwarf_npci_rotate(const dwarf_npci_rotate_args* a, void* stream) 
   DWARF_CHECK_VERSION(a);
   if (a->dtype != DWARF_BF16 && a->dtype != DWARF_F32) return DWARF_ERR_DTYPE;
   if (a->B < 0 || a->H <= 0 || a->N < 0) return DWARF_ERR_SHAPE;
-  const int64_t rows = a->B * a->H * a->N;
-  if (rows == 0) return DWARF_OK;
+  if (a->B == 0 || a->N == 0) return DWARF_OK;
   if (!a->x || !a->out || (a->delta && !a->theta)) return DWARF_ERR_NULL;
   if (!(a->tau > 0.0f)) return DWARF_ERR_VALUE;
   NpciParams p{a->B, a->H, a->N, a->x, a->sxb, a->sxh, a->sxn, a->addend, a->sab, a->sah, a->san,
                a->delta, a->sdb, a->sdh, a->sdn, a->theta, a->tau, a->out, a->sob, a->soh, a->son};
-  const int64_t blocks = (rows + 15) / 16;
-  if (blocks > 0x7fffffffLL) return DWARF_ERR_SHAPE;
+  const int64_t per_cta = 16 * kRowGroups;
+  if (a->H > 65535 || a->B > 65535 || (a->N + per_cta - 1) / per_cta > 0x7fffffffLL) return DWARF_ERR_SHAPE;
+  const dim3 blocks((unsigned)((a->N + per_cta - 1) / per_cta), (unsigned)a->H, (unsigned)a->B);
   if (a->dtype == DWARF_BF16)
-    npci_kernel<__nv_bfloat16><<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(p);
+    npci_kernel<__nv_bfloat16><<<blocks, 256, 0, (cudaStream_t)stream>>>(p);
   else
-    npci_kernel<float><<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(p);
+    npci_kernel<float><<<blocks, 256, 0, (cudaStream_t)stream>>>(p);
   return launch_status();
 }

@@ -3,7 +3,7 @@
 // The format is defined by this engine (the reference has no packed KV path;
 // kernels/dsqg_attention_v22.py:467,473-476 declares it unimplemented):
 //   amax = max_d |x_d| (fp32); s = fp16(min(amax, 65504)) (RNE);
-//   c_d  = clamp(rint((x_d * 31) / float(s)), -31, 31) (RNE, IEEE div; s == 0 -> 0);
+//   c_d  = clamp(rint(x_d * (31 / float(s))), -31, 31) (RNE, IEEE div once per row; s == 0 -> 0);
 //   group g of 4 codes -> 3 bytes little-endian of w = u0 | u1<<6 | u2<<12 | u3<<18,
 //   u = c & 63; dequant x^ = float(c) * (float(s) / 31).
 // 16 threads own one row, 4 values (one 3-byte group) each; the row maximum
@@ -38,10 +38,10 @@ __global__ void q6_pack_kernel(const T* __restrict__ x, int64_t B, int64_t H, in
 #pragma unroll
   for (int o = 8; o >= 1; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o, 16));
   const __half s = q6_scale_from_amax(amax);
-  const float sf = __half2float(s);
+  const float inv = q6_inv_step(__half2float(s));
   uint32_t w = 0;
 #pragma unroll
-  for (int i = 0; i < 4; ++i) w |= (uint32_t)(q6_quantize(v[i], sf) & 63) << (6 * i);
+  for (int i = 0; i < 4; ++i) w |= (uint32_t)(q6_quantize(v[i], inv) & 63) << (6 * i);
   if (active) {
     uint8_t* dst = codes + b * scb + h * sch + t * sct + g * 3;
     dst[0] = (uint8_t)(w & 255u);

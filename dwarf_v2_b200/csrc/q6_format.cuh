@@ -11,10 +11,12 @@ __device__ __forceinline__ __half q6_scale_from_amax(float amax) {
   return __float2half_rn(fminf(amax, 65504.0f));
 }
 
-// Code of one value: clamp(rint((x*31)/s), -31, 31); s == 0 -> 0.
-__device__ __forceinline__ int q6_quantize(float x, float s) {
-  if (!(s > 0.0f)) return 0;
-  float q = rintf(__fdiv_rn(__fmul_rn(x, 31.0f), s));
+// Per-row quantisation factor 31 / float(s) (IEEE division); 0 when s == 0.
+__device__ __forceinline__ float q6_inv_step(float s) { return s > 0.0f ? __fdiv_rn(31.0f, s) : 0.0f; }
+
+// Code of one value: clamp(rint(x * inv), -31, 31), inv = q6_inv_step(s).
+__device__ __forceinline__ int q6_quantize(float x, float inv) {
+  float q = rintf(__fmul_rn(x, inv));
   q = fminf(fmaxf(q, -31.0f), 31.0f);
   return (int)q;
 }

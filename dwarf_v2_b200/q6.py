@@ -3,7 +3,8 @@
 A row is one (b, h, t) head vector of 64 values:
 
 * ``s = fp16(min(max|x|, 65504))``
-* ``c = clamp(rint((x * 31) / float(s)), -31, 31)`` (round half to even; ``s == 0 -> c = 0``)
+* ``c = clamp(rint(x * (31 / float(s))), -31, 31)`` (one IEEE division per row, an fp32
+  multiply per value, round half to even; ``s == 0 -> c = 0``)
 * 16 groups of 4 codes, each group 3 bytes little-endian of
   ``u0 | u1 << 6 | u2 << 12 | u3 << 18`` with ``u = c & 63``: 48 bytes per row
 * dequantisation ``x^ = float(c) * (float(s) / 31)``

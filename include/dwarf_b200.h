@@ -131,7 +131,8 @@ int dwarf_ema_scan_noalloc(const dwarf_ema_scan_args* args, void* stream);
  * One row = one (b, h, t) head vector of 64 values.
  *   amax  = max_d |x_d|                         (fp32)
  *   s     = fp16(min(amax, 65504))              (round to nearest even)
- *   c_d   = clamp(rint((x_d * 31) / float(s)), -31, 31)   (RNE; s == 0 -> 0)
+ *   inv   = 31 / float(s)                       (IEEE fp32 division)
+ *   c_d   = clamp(rint(x_d * inv), -31, 31)     (fp32 multiply, RNE; s == 0 -> 0)
  *   bytes = 16 groups of 4 codes, each group 3 bytes little-endian:
  *           w = u0 | u1 << 6 | u2 << 12 | u3 << 18, u = c & 63 (6-bit two's
  *           complement); row = 48 bytes.

@@ -20,7 +20,8 @@ def pack(x: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
     scales = np.minimum(amax, np.float32(65504.0)).astype(np.float16)
     sf = scales.astype(np.float32)[..., None]
     with np.errstate(divide="ignore", invalid="ignore"):
-        q = np.rint((x * np.float32(31.0)) / sf)  # float32 multiply then divide, both RNE
+        inv = np.float32(31.0) / sf                # one float32 division per row (RNE)
+        q = np.rint(x * inv)                       # float32 multiply (RNE), round half to even
     q = np.where(sf > 0, q, np.float32(0.0))
     q = np.clip(q, -31, 31).astype(np.int32)
     u = (q & 63).astype(np.uint32).reshape(*x.shape[:-1], 16, 4)
