@@ -171,7 +171,7 @@ class DsqgFwdArgs(ctypes.Structure):
         phase_base:ptr, sbj:i64, sbh:i64, phase_gain:ptr, sgj:i64, sgh:i64,
         y_pre:ptr, syb:i64, syh:i64, syn:i64, z_pre:ptr, szb:i64, szh:i64, szn:i64,
         out:ptr, sob:i64, soh:i64, son:i64, lse:ptr, slb:i64, slh:i64, sln:i64,
-        head_gain:ptr, head_gain_dtype:i32, gate:ptr, sgb_:i64, sgn_:i64""")
+        head_gain:ptr, head_gain_dtype:i32, gate:ptr, sgb_:i64, sgn_:i64, device_status:ptr""")
 
 
 class DsqgPrepArgs(ctypes.Structure):

@@ -40,21 +40,31 @@ __global__ void __launch_bounds__(256) dsqg_prep_kernel(const PrepParams p) {
   for (int i = threadIdx.x; i < 2 * 4 * 64; i += 256)
     probes[i / 256][(i / 64) & 3][i & 63] = (i < 256 ? p.qp : p.kp)[i & 255];
   __syncthreads();
+  const int g = threadIdx.x & 15;
+  const int lr = threadIdx.x >> 4;  // local row
+  const int64_t b = blockIdx.z;
+  int hy = blockIdx.y, kind = 0;
+  if (hy >= p.H) { hy -= (int)p.H; kind = 1; if (hy >= p.Hkv) { hy -= (int)p.Hkv; kind = 2; } }
+  const __nv_bfloat16* base = kind == 0 ? p.q + b * p.sqb + hy * p.sqh
+                            : kind == 1 ? p.k + b * p.skb + hy * p.skh
+                                        : p.v + b * p.svb + hy * p.svh;
+  const int64_t srow = kind == 0 ? p.sqn : kind == 1 ? p.skn : p.svn;
+  // All eight groups' loads are issued before any math, so each thread keeps
+  // 64 B in flight (the loop below alone would expose one load latency per group).
+  uint2 xw[kRowGroups];
+#pragma unroll
   for (int grp = 0; grp < kRowGroups; ++grp) {
-    const int g = threadIdx.x & 15;
-    const int lr = threadIdx.x >> 4;  // local row
+    const int64_t t = ((int64_t)blockIdx.x * kRowGroups + grp) * 16 + lr;
+    const int64_t tt = t < p.N ? t : p.N - 1;
+    xw[grp] = __ldg(reinterpret_cast<const uint2*>(base + tt * srow + g * 4));
+  }
+#pragma unroll
+  for (int grp = 0; grp < kRowGroups; ++grp) {
     const int64_t t = ((int64_t)blockIdx.x * kRowGroups + grp) * 16 + lr;
     const bool active = t < p.N;
-    const int64_t b = blockIdx.z;
-    int hy = blockIdx.y, kind = 0;
-    if (hy >= p.H) { hy -= (int)p.H; kind = 1; if (hy >= p.Hkv) { hy -= (int)p.Hkv; kind = 2; } }
-    const int64_t tt = active ? t : p.N - 1;
-    const __nv_bfloat16* src = kind == 0 ? p.q + b * p.sqb + hy * p.sqh + tt * p.sqn
-                             : kind == 1 ? p.k + b * p.skb + hy * p.skh + tt * p.skn
-                                         : p.v + b * p.svb + hy * p.svh + tt * p.svn;
     float x[4];
     {
-      const uint2 w = *reinterpret_cast<const uint2*>(src + g * 4);
+      const uint2 w = xw[grp];
       x[0] = __uint_as_float(w.x << 16); x[1] = __uint_as_float(w.x & 0xffff0000u);
       x[2] = __uint_as_float(w.y << 16); x[3] = __uint_as_float(w.y & 0xffff0000u);
     }

@@ -230,6 +230,7 @@ typedef struct {
   int32_t head_gain_dtype;        /* DWARF_F32 or DWARF_BF16              */
   const void* gate;               /* optional bf16 [B, N, H*64] view      */
   int64_t sgb_, sgn_;             /* element strides (b, n); h*64+d is +1 */
+  int32_t* device_status;         /* optional; set to DWARF_DEVICE_TIMEOUT */
 } dwarf_dsqg_fwd_args;
 
 int dwarf_dsqg_fwd(const dwarf_dsqg_fwd_args* args, void* stream);

@@ -258,3 +258,93 @@ def test_kernel_config3_full_size_properties():
                                     pgain[:, h:h + 1].cpu().numpy(), y[b:b + 1, h:h + 1].cpu().numpy(),
                                     z[b:b + 1, h:h + 1].cpu().numpy(), ALL_OFFSETS, js, 0, 1)
         _assert_close(out[b:b + 1, h:h + 1].float().cpu().numpy(), ref)
+
+
+# ------------------------------------------------------------------ resident-K/V q6 kernel
+
+def _group_offsets():
+    from dwarf_v2_b200.dsqg_attention_v22 import ALL_OFFSETS
+    live = [d for d in sorted(ALL_OFFSETS) if 2047 - d >= 64]
+    g = live[0::3]
+    small = [d for d in g if d <= 28]
+    return small + [d for d in g if d >= 48], len(small)
+
+
+def _resident_case(B, H, Hkv, N, seed, q_scale=1.0):
+    gen = torch.Generator().manual_seed(seed)
+    offs, js = _group_offsets()
+    J = len(offs)
+    c = dict(
+        q=(torch.randn(B, H, N, 64, generator=gen) * q_scale).to(torch.bfloat16),
+        k=torch.randn(B, Hkv, N, 64, generator=gen).to(torch.bfloat16),
+        v=torch.randn(B, Hkv, N, 64, generator=gen).to(torch.bfloat16),
+        pos_bias=torch.randn(J, H, generator=gen) * 0.3 - torch.log1p(torch.tensor(offs, dtype=torch.float32))[:, None],
+        scale_embed=torch.randn(J, 64, generator=gen) * 0.05,
+        phase_base=torch.randn(J - js, H, 4, generator=gen) * 0.5,
+        phase_gain=torch.randn(J - js, H, 4, generator=gen) * 2.0,
+        y_pre=torch.randn(B, H, N, 4, generator=gen) * 0.2,
+        z_pre=torch.randn(B, Hkv, N, 4, generator=gen) * 0.2,
+    )
+    return c, offs, js
+
+
+def _run_q6(c, offs, js, plane_shift, query_start, path, monkeypatch, gain=None, gate=None):
+    from dwarf_v2_b200.dsqg_attention_v22 import _dsqg_launch, _prepare_tables
+    from dwarf_v2_b200.q6 import q6_pack
+
+    monkeypatch.setenv("DWARF_DSQG_PATH", path)
+    d = {k: v.cuda() for k, v in c.items()}
+    kc, ks = q6_pack(d["k"])
+    vc, vs = q6_pack(d["v"])
+    B, H, N, _ = d["q"].shape
+    J = len(offs)
+    offs_t = torch.tensor(offs, dtype=torch.int32, device="cuda")
+    pb, se, pbase, pgain, y32, z32, o = _prepare_tables(d["pos_bias"], d["scale_embed"], d["phase_base"],
+                                                        d["phase_gain"], d["y_pre"], d["z_pre"], offs_t,
+                                                        d["q"].device, J, J - js)
+    out = torch.empty(B, H, N, 64, dtype=torch.bfloat16, device="cuda")
+    lse = torch.empty(B, H, N, dtype=torch.float32, device="cuda")
+    _dsqg_launch(d["q"].contiguous(), kv=("q6", kc, ks, vc, vs), pos_bias=pb, scale_embed=se, phase_base=pbase,
+                 phase_gain=pgain, y_pre=y32, z_pre=z32, offsets=o, j_small=js, j_large=J - js,
+                 plane_shift=plane_shift, query_start=query_start, out=out, lse=lse, head_gain=gain, gate=gate)
+    torch.cuda.synchronize()
+    return out, lse, (kc, ks, vc, vs)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("B,H,Hkv,N,plane_shift,query_start,q_scale", [
+    (2, 4, 4, 2048, 0, 0, 1.0),      # model shape per head, MOVT pair in word 0
+    (1, 4, 2, 2048, 6, 37, 1.0),     # GQA, word 1, query_start
+    (2, 2, 2, 200, 14, 0, 1.0),      # partial last chunk (192 + 8 rows), word 2
+    (1, 2, 2, 8, 10, 0, 1.0),        # a single 8-row chunk
+    (1, 2, 2, 1024, 4, 0, 60.0),     # large |q|: near one-hot softmax, exponent scaling
+])
+def test_resident_q6_kernel_matches_oracle(B, H, Hkv, N, plane_shift, query_start, q_scale, monkeypatch):
+    c, offs, js = _resident_case(B, H, Hkv, N, seed=N + plane_shift, q_scale=q_scale)
+    out, lse, (kc, ks, vc, vs) = _run_q6(c, offs, js, plane_shift, query_start, "resident", monkeypatch)
+    gout, glse, _ = _run_q6(c, offs, js, plane_shift, query_start, "gather", monkeypatch)
+    k_hat = oq6.unpack(kc.cpu().numpy(), ks.cpu().numpy())
+    v_hat = oq6.unpack(vc.cpu().numpy(), vs.cpu().numpy())
+    ref, ref_lse = odsqg.dsqg_forward(_np(c["q"]), k_hat, v_hat, _np(c["pos_bias"]), _np(c["scale_embed"]),
+                                      _np(c["phase_base"]), _np(c["phase_gain"]), _np(c["y_pre"]),
+                                      _np(c["z_pre"]), offs, js, plane_shift, query_start)
+    _assert_close(out.float().cpu().numpy(), ref)
+    _assert_close(out.float().cpu().numpy(), gout.float().cpu().numpy())
+    lse, glse = lse.cpu().numpy(), glse.cpu().numpy()
+    fin = np.isfinite(ref_lse)
+    assert np.array_equal(fin, np.isfinite(lse))
+    assert np.abs(lse[fin] - ref_lse[fin]).max() < 1e-3 * max(1.0, q_scale)
+    assert np.abs(lse[fin] - glse[fin]).max() < 1e-3 * max(1.0, q_scale)
+    if query_start:
+        assert torch.all(out[:, :, :query_start] == 0)
+
+
+@pytest.mark.gpu
+def test_resident_q6_kernel_fused_gain_gate_matches_gather(monkeypatch):
+    c, offs, js = _resident_case(2, 4, 4, 2048, seed=3)
+    gen = torch.Generator().manual_seed(4)
+    gain = (torch.rand(4, generator=gen) + 0.5).to(torch.bfloat16).cuda()
+    gate = torch.randn(2, 2048, 4 * 64, generator=gen).to(torch.bfloat16).cuda()
+    out, _, _ = _run_q6(c, offs, js, 2, 0, "resident", monkeypatch, gain=gain, gate=gate)
+    gout, _, _ = _run_q6(c, offs, js, 2, 0, "gather", monkeypatch, gain=gain, gate=gate)
+    _assert_close(out.float().cpu().numpy(), gout.float().cpu().numpy(), tol=2e-2, mean_rel=5e-3)
