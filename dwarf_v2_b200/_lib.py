@@ -230,7 +230,16 @@ class PacketArgs(ctypes.Structure):
                 ("sgp", c_i64), ("out", c_ptr), ("so", c_i64)]
 
 
+class GemmArgs(ctypes.Structure):
+    _fields_ = _fields("""version:i32, epilogue:i32, M:i64, N:i64, K:i64, a:ptr, lda:i64, b:ptr, ldb:i64,
+        bias:ptr, bias_dtype:i32, swiglu_tile:i32, out:ptr, ldo:i64, device_status:ptr,
+        resid:ptr, ldr:i64, norm_w:ptr, norm_w_dtype:i32, eps:f32, n_out:ptr, ldn:i64,
+        T:i64, heads:i32, q_probe:ptr, k_probe:ptr, y_pre:ptr, z_pre:ptr, k_codes:ptr, k_scales:ptr,
+        v_codes:ptr, v_scales:ptr""")
+
+
 _ENTRY_POINTS = {
+    "dwarf_gemm_bf16": GemmArgs,
     "dwarf_hisa_reps": HisaRepsArgs,
     "dwarf_hisa_select": HisaSelectArgs,
     "dwarf_hisa_attn": HisaAttnArgs,

@@ -5,6 +5,8 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <stdint.h>
+#include <stdio.h>
+#include <stdlib.h>
 
 #include "../../include/dwarf_b200.h"
 
@@ -22,8 +24,11 @@ constexpr int kNumSMs = 148;
 // waiting CTA gives up and records DWARF_DEVICE_TIMEOUT.
 constexpr uint32_t kSpinLimit = 1u << 22;
 
+// Status of the last launch; with DWARF_DEBUG set, the CUDA error text goes to stderr.
 inline int launch_status() {
   cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess && getenv("DWARF_DEBUG") != nullptr)
+    fprintf(stderr, "dwarf_b200: launch failed: %s\n", cudaGetErrorString(e));
   return e == cudaSuccess ? DWARF_OK : DWARF_ERR_LAUNCH;
 }
 

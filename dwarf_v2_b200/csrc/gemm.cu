@@ -1,0 +1,734 @@
+// bf16 GEMM on the 5th-generation tensor cores with fused epilogues.
+//
+// out = epilogue(A . B^T), A [M, K] and B [N, K] both K-major bf16 (x and a
+// torch Linear weight), fp32 accumulation in tensor memory.
+//
+// Persistent, warp-specialised kernel, one CTA per SM:
+//   warp 0      TMA producer: A tile [128 x 64] and B tile [BN x 64] per
+//               k-block into an S-stage shared-memory ring (128-byte
+//               swizzle, one mbarrier pair per stage);
+//   warp 1      allocates tensor memory and issues tcgen05.mma
+//               (M = 128, N = BN, K = 16 per instruction) from one thread;
+//               tcgen05.commit frees a stage once its MMAs have read it and
+//               marks an accumulator full after the tile's last k-block;
+//   warps 2-5   epilogue: each thread owns one accumulator row (TMEM lane),
+//               reads it with tcgen05.ld, applies the epilogue and stores.
+// Two accumulator buffers (2 x BN columns of TMEM) let the epilogue of tile
+// i overlap the MMAs of tile i + 1. Tiles are walked M-block-major so the
+// CTAs working on one A block at a time share it through L2.
+//
+// Every mbarrier wait is bounded; a timeout sets a shared abort flag that
+// ends every role's loop, records DWARF_DEVICE_TIMEOUT, waits (bounded) for
+// the copies and MMAs already issued and releases tensor memory.
+#include "common.cuh"
+#include "q6_format.cuh"
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <type_traits>
+
+namespace dwarf {
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;  // bf16 elements per 128-byte swizzle row
+constexpr int kGemmThreads = 320;  // TMA warp, MMA warp, 8 epilogue warps
+constexpr uint32_t kWaitLimit = 1u << 24;
+
+enum : int {
+  kEpiStore = DWARF_GEMM_STORE,
+  kEpiSwiglu = DWARF_GEMM_SWIGLU,
+  kEpiRmsNorm = DWARF_GEMM_RESID_RMSNORM,
+  kEpiQkvg = DWARF_GEMM_QKVG_PREP
+};
+
+struct GemmEpi {
+  const void* bias;
+  int bias_bf16;
+  __nv_bfloat16* out;
+  int64_t ldo;
+  int32_t* status;
+  // residual + RMSNorm epilogue
+  const __nv_bfloat16* resid;
+  int64_t ldr;
+  const void* norm_w;
+  int norm_w_bf16;
+  float eps;
+  // qkvg + DSQG prep epilogue
+  int T, heads;
+  const float* q_probe;
+  const float* k_probe;
+  float* y_pre;
+  float* z_pre;
+  uint8_t* k_codes;
+  uint16_t* k_scales;
+  uint8_t* v_codes;
+  uint16_t* v_scales;
+};
+
+__device__ __forceinline__ uint32_t s32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile("{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\nselp.u32 %0, 1, 0, p;\n}"
+               : "=r"(done) : "r"(bar), "r"(parity) : "memory");
+  return done != 0;
+}
+// Bounded wait; gives up (and raises the CTA's abort flag) after kWaitLimit
+// polls or as soon as another role has aborted.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
+  for (uint32_t it = 0; it < kWaitLimit; ++it) {
+    if (mbar_try(bar, parity)) return true;
+    if (*abort_flag) return false;
+  }
+  *abort_flag = 1;
+  return false;
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+      ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar) : "memory");
+}
+
+// Shared-memory matrix descriptor: K-major operand, 128-byte swizzle, rows of
+// 128 bytes in 8-row (1024-byte) atoms.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+  d |= (uint64_t)(16 >> 4) << 16;    // leading byte offset (unused for swizzled K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;  // stride byte offset: next 8-row atom
+  d |= (uint64_t)1 << 46;            // descriptor version for sm_100
+  d |= (uint64_t)2 << 61;            // 128-byte swizzle
+  return d;
+}
+// Instruction descriptor, kind::f16: bf16 A and B (K-major), fp32 D.
+__host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile("{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\ntcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}"
+               ::"r"(tmem_d), "l"(a), "l"(b), "r"(idesc), "r"(acc) : "memory");
+}
+// 16 consecutive fp32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// 64 consecutive fp32 columns of this thread's TMEM lane: two x32 loads and
+// the wait in one asm statement, so no use of the registers can be scheduled
+// before they are valid.
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&v)[64]) {
+  uint32_t r[64];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%64];\n"
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%65];\n"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]), "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]), "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]), "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]), "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+      : "r"(taddr), "r"(taddr + 32) : "memory");
+#pragma unroll
+  for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(r[i]);
+}
+// Columns [c, c+16) and [c2, c2+16) (x16 each), one wait.
+__device__ __forceinline__ void tmem_ld16x2(uint32_t t1, uint32_t t2, float (&a)[16], float (&b)[16]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%32];\n"
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%33];\n"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(t1), "r"(t2) : "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) { a[i] = __uint_as_float(r[i]); b[i] = __uint_as_float(r[16 + i]); }
+}
+__device__ __forceinline__ void add_bias64(const void* bias, int bf16, int col, float (&v)[64]) {
+  if (bf16) {
+    const uint4* p = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(bias) + col);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint4 w = __ldg(p + j);
+      const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        v[8 * j + 2 * k] += __uint_as_float(u[k] << 16);
+        v[8 * j + 2 * k + 1] += __uint_as_float(u[k] & 0xffff0000u);
+      }
+    }
+  } else {
+    const float4* p = reinterpret_cast<const float4*>(static_cast<const float*>(bias) + col);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const float4 w = __ldg(p + j);
+      v[4 * j] += w.x; v[4 * j + 1] += w.y; v[4 * j + 2] += w.z; v[4 * j + 3] += w.w;
+    }
+  }
+}
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%1, %2}], [%3];"
+               ::"l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(src) : "memory");
+}
+
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  const __nv_bfloat162 t = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&t);
+}
+__device__ __forceinline__ void store16(__nv_bfloat16* dst, const float (&v)[16]) {
+  uint4 w0 = make_uint4(pack2(v[0], v[1]), pack2(v[2], v[3]), pack2(v[4], v[5]), pack2(v[6], v[7]));
+  uint4 w1 = make_uint4(pack2(v[8], v[9]), pack2(v[10], v[11]), pack2(v[12], v[13]), pack2(v[14], v[15]));
+  reinterpret_cast<uint4*>(dst)[0] = w0;
+  reinterpret_cast<uint4*>(dst)[1] = w1;
+}
+
+template <int BN>
+__host__ __device__ constexpr int gemm_stages() {
+  return BN >= 256 ? 4 : 6;
+}
+template <int BN>
+__host__ __device__ constexpr uint32_t gemm_tmem_cols() {
+  return 2 * BN <= 256 ? 256u : 512u;
+}
+template <int EPI>
+__host__ __device__ constexpr uint32_t gemm_staging_bytes() {
+  return EPI != DWARF_GEMM_SWIGLU ? 8 * 4096 : 0;  // one 32 x 64 bf16 box per epilogue warp
+}
+template <int BN, int EPI>
+__host__ __device__ constexpr size_t gemm_smem_bytes() {
+  // 1 KB alignment slack, stages, staging boxes, barriers (256 B) and the
+  // RMSNorm partial sums (8 warps x 32 rows of fp32).
+  return 1024 + (size_t)gemm_stages<BN>() * (kBM * 128 + BN * 128) + gemm_staging_bytes<EPI>() + 256 +
+         (EPI == DWARF_GEMM_RESID_RMSNORM ? 1024 : 0);
+}
+
+template <int BN, int EPI>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                 const __grid_constant__ CUtensorMap tmap_out, const __grid_constant__ CUtensorMap tmap_n,
+                 const int M, const int N, const int K, const GemmEpi epi) {
+  constexpr int S = gemm_stages<BN>();
+  constexpr uint32_t kStageA = kBM * 128, kStageB = BN * 128;
+  constexpr uint32_t kTmemCols = gemm_tmem_cols<BN>();
+  constexpr uint32_t kIdesc = idesc_bf16(kBM, BN);
+  extern __shared__ uint8_t gsm_raw[];
+  const uint32_t raw = s32(gsm_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;  // 1024-byte aligned swizzle atoms
+  uint8_t* gsm = gsm_raw + (base - raw);
+  const uint32_t sA = base, sB = base + S * kStageA;
+  const uint32_t sStage = base + S * (kStageA + kStageB);
+  uint8_t* ctl = gsm + S * (kStageA + kStageB) + gemm_staging_bytes<EPI>();
+  const uint32_t bar_full = s32(ctl), bar_empty = bar_full + 8 * S;
+  const uint32_t bar_tfull = bar_empty + 8 * S, bar_tempty = bar_tfull + 16, bar_drain = bar_tempty + 16;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ctl + 16 * S + 40);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(ctl + 16 * S + 44);
+  constexpr uint32_t kAccStride = kTmemCols / 2;  // accumulator buffer a at column a * kAccStride
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tiles_m = (M + kBM - 1) / kBM, tiles_n = N / BN;
+  const int tiles = tiles_m * tiles_n;
+  // i-th tile of this CTA. The RMSNorm epilogue needs whole rows, so there a
+  // CTA owns M blocks and walks their tiles_n column tiles back to back.
+  const int sub = EPI == kEpiRmsNorm ? tiles_n : 1;
+  auto tile_at = [&](int i) { return (blockIdx.x + (i / sub) * gridDim.x) * sub + i % sub; };
+  const int kblocks = (K + kBK - 1) / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(bar_full + 8 * s, 1);
+      mbar_init(bar_empty + 8 * s, 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(bar_tfull + 8 * a, 1);
+      mbar_init(bar_tempty + 8 * a, 8);  // one arrival per epilogue warp
+    }
+    mbar_init(bar_drain, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_a)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_b)) : "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(s32(tmem_slot)),
+                 "r"(kTmemCols) : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer
+    if (lane == 0) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (int i = 0; ok; ++i) {
+        const int t = tile_at(i);
+        if (t >= tiles) break;
+        const int m0 = (t / tiles_n) * kBM, n0 = (t % tiles_n) * BN;
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          const uint32_t s = it % S, ph = (it / S) & 1u;
+          if (!(ok = mbar_wait(bar_empty + 8 * s, ph ^ 1u, abort_flag))) break;
+          mbar_expect_tx(bar_full + 8 * s, kStageA + kStageB);
+          tma_load_2d(sA + s * kStageA, &tmap_a, kb * kBK, m0, bar_full + 8 * s);
+          tma_load_2d(sB + s * kStageB, &tmap_b, kb * kBK, n0, bar_full + 8 * s);
+        }
+      }
+      // Leave no copy in flight: the last S issued stages must have landed.
+      for (uint32_t j = it > (uint32_t)S ? it - S : 0; j < it; ++j) {
+        const uint32_t s = j % S, ph = (j / S) & 1u;
+        for (uint32_t w = 0; w < kWaitLimit && !mbar_try(bar_full + 8 * s, ph); ++w) {}
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ---------------- MMA issuer
+    if (lane == 0) {
+      uint32_t it = 0, tc = 0;
+      bool ok = true;
+      for (int i = 0; ok; ++i, ++tc) {
+        const int t = tile_at(i);
+        if (t >= tiles) break;
+        const uint32_t a = tc & 1u, aph = (tc >> 1) & 1u;
+        if (!(ok = mbar_wait(bar_tempty + 8 * a, aph ^ 1u, abort_flag))) break;
+        tc_fence_after();
+        const uint32_t d = tmem + a * kAccStride;
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          const uint32_t s = it % S, ph = (it / S) & 1u;
+          if (!(ok = mbar_wait(bar_full + 8 * s, ph, abort_flag))) break;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk)
+            tc_mma(d, smem_desc(sA + s * kStageA + kk * 32), smem_desc(sB + s * kStageB + kk * 32), kIdesc,
+                   (kb | kk) != 0);
+          tc_commit(bar_empty + 8 * s);
+        }
+        if (ok) tc_commit(bar_tfull + 8 * a);
+      }
+      // Drain: every MMA issued so far has completed once this commit lands.
+      tc_commit(bar_drain);
+      for (uint32_t w = 0; w < kWaitLimit && !mbar_try(bar_drain, 0); ++w) {}
+    }
+    __syncwarp();
+  } else {
+    // ---------------- epilogue: warps 2..9. TMEM lane quarter = warp % 4;
+    // the two warps of a quarter split the tile's columns.
+    const int e = warp - 2, quarter = warp & 3, half = e >> 2;
+    uint32_t tc = 0;
+    float ss = 0.0f;  // RMSNorm: running sum of squares of this thread's row slice
+    for (int i = 0;; ++i, ++tc) {
+      const int t = tile_at(i);
+      if (t >= tiles) break;
+      const uint32_t a = tc & 1u, aph = (tc >> 1) & 1u;
+      if (!mbar_wait(bar_tfull + 8 * a, aph, abort_flag)) break;
+      tc_fence_after();
+      const int m0 = (t / tiles_n) * kBM, n0 = (t % tiles_n) * BN;
+      const uint32_t tbase = tmem + ((uint32_t)(quarter * 32) << 16) + a * kAccStride;
+      if constexpr (EPI == kEpiRmsNorm) {
+        // Residual add + RMSNorm over whole rows (N <= 512, BN = 256): each
+        // warp owns 32 rows x 128 columns of every column tile. Pass 1 writes
+        // v = x + addend per 64-column chunk and accumulates the row's sum of
+        // squares; once the row is complete, pass 2 reads v back (L2) from
+        // the rows this warp itself stored and writes the normalised row.
+        constexpr int CW = BN / 2;
+        const uint32_t stg = sStage + e * 4096;
+        uint8_t* stg_p = gsm + (stg - base);
+        const int row = m0 + quarter * 32 + lane;
+        const int rrow = row < M ? row : M - 1;
+        auto stage_store = [&](const CUtensorMap* map, const uint32_t (&pk)[32], int col) {
+          if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+          __syncwarp();
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            *reinterpret_cast<uint4*>(stg_p + lane * 128 + ((q ^ (lane & 7)) << 4)) =
+                make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(map, stg, col, m0 + quarter * 32);
+            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+          }
+        };
+        auto add_part = [&](auto jc) {
+          constexpr int J = decltype(jc)::value;
+          if (J == 0) ss = 0.0f;
+#pragma unroll
+          for (int k = 0; k < CW / 64; ++k) {
+            const int c = half * CW + 64 * k;
+            float v[64];
+            tmem_ld64(tbase + c, v);
+            if (k == CW / 64 - 1) {
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(bar_tempty + 8 * a);
+            }
+            const uint4* rp = reinterpret_cast<const uint4*>(epi.resid + (int64_t)rrow * epi.ldr + n0 + c);
+            uint32_t pk[32];
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              const uint4 w = rp[q];  // plain load: out may alias resid
+              const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+              for (int h = 0; h < 4; ++h) {
+                float& lo = v[8 * q + 2 * h];
+                float& hi = v[8 * q + 2 * h + 1];
+                lo = round_bf16(__uint_as_float(u[h] << 16) + round_bf16(lo));
+                hi = round_bf16(__uint_as_float(u[h] & 0xffff0000u) + round_bf16(hi));
+                ss = fmaf(lo, lo, ss);
+                ss = fmaf(hi, hi, ss);
+                pk[4 * q + h] = pack2(lo, hi);
+              }
+            }
+            stage_store(&tmap_out, pk, n0 + c);
+          }
+        };
+        auto normalise = [&](auto jn) {
+          constexpr int JN = decltype(jn)::value;  // column tiles in the row
+          float* ssb = reinterpret_cast<float*>(ctl + 256);
+          ssb[e * 32 + lane] = ss;
+          asm volatile("bar.sync %0, 64;" ::"r"(1 + quarter) : "memory");
+          const float total = ssb[e * 32 + lane] + ssb[(e ^ 4) * 32 + lane];
+          asm volatile("bar.sync %0, 64;" ::"r"(1 + quarter) : "memory");
+          const float r = rsqrtf(total / (float)N + epi.eps);
+          // This warp's v stores must have landed before it reads them back.
+          if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;\nfence.proxy.async.global;" ::: "memory");
+          __syncwarp();
+          const __nv_bfloat16* vrow = epi.out + (int64_t)rrow * epi.ldo;
+#pragma unroll 1
+          for (int jj = 0; jj < JN; ++jj) {
+#pragma unroll 1
+            for (int k = 0; k < CW / 64; ++k) {
+              const int col = jj * BN + half * CW + 64 * k;
+              const uint4* vp = reinterpret_cast<const uint4*>(vrow + col);
+              uint32_t pk[32];
+#pragma unroll
+              for (int q = 0; q < 8; ++q) {
+                const uint4 w = vp[q];
+                const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                for (int h = 0; h < 4; ++h) {
+                  const int cc = col + 8 * q + 2 * h;
+                  float w0, w1;
+                  if (epi.norm_w_bf16) {
+                    const __nv_bfloat162 wb = __ldg(reinterpret_cast<const __nv_bfloat162*>(
+                        static_cast<const __nv_bfloat16*>(epi.norm_w) + cc));
+                    w0 = __low2float(wb); w1 = __high2float(wb);
+                  } else {
+                    const float2 wf = __ldg(reinterpret_cast<const float2*>(static_cast<const float*>(epi.norm_w) + cc));
+                    w0 = wf.x; w1 = wf.y;
+                  }
+                  pk[4 * q + h] = pack2((__uint_as_float(u[h] << 16) * r) * w0,
+                                        (__uint_as_float(u[h] & 0xffff0000u) * r) * w1);
+                }
+              }
+              stage_store(&tmap_n, pk, col);
+            }
+          }
+        };
+        const int j = t % tiles_n;
+        if (j == 0) add_part(std::integral_constant<int, 0>{});
+        else add_part(std::integral_constant<int, 1>{});
+        if (j == tiles_n - 1) {
+          if (tiles_n == 1) normalise(std::integral_constant<int, 1>{});
+          else normalise(std::integral_constant<int, 2>{});
+        }
+      } else if constexpr (EPI == kEpiQkvg) {
+        // One head (64 columns) per chunk; the tile lies inside one of the
+        // q | k | v | gate sections. q and gate rows go out through the
+        // staging box like epilogue 0; q and k rows give y / z (probe dots
+        // over the bf16 row, scaled by rsqrt(|row|^2 + 64e-6)); k and v rows
+        // are packed straight into the q6 cache.
+        const int D = epi.heads * 64;
+        const int sec = n0 / D;
+        const int row = m0 + quarter * 32 + lane;
+        const int b = row / epi.T, tt = row - b * epi.T;
+        const uint32_t stg = sStage + e * 4096;
+        uint8_t* stg_p = gsm + (stg - base);
+#pragma unroll 1
+        for (int k = 0; k < 2; ++k) {
+          const int c = half * 128 + 64 * k;
+          const int head = (n0 - sec * D + c) >> 6;
+          float v[64];
+          tmem_ld64(tbase + c, v);
+          if (k == 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar_tempty + 8 * a);
+          }
+          add_bias64(epi.bias, epi.bias_bf16, n0 + c, v);
+#pragma unroll
+          for (int i = 0; i < 64; ++i) v[i] = round_bf16(v[i]);
+          const int64_t hrow = ((int64_t)b * epi.heads + head) * epi.T + tt;
+          if (sec == 0 || sec == 3) {
+            if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+            __syncwarp();
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const uint4 w = make_uint4(pack2(v[8 * j], v[8 * j + 1]), pack2(v[8 * j + 2], v[8 * j + 3]),
+                                         pack2(v[8 * j + 4], v[8 * j + 5]), pack2(v[8 * j + 6], v[8 * j + 7]));
+              *reinterpret_cast<uint4*>(stg_p + lane * 128 + ((j ^ (lane & 7)) << 4)) = w;
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_2d(&tmap_out, stg, n0 + c, m0 + quarter * 32);
+              asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+            }
+          }
+          if (sec <= 1 && row < M) {
+            const float4* pr = reinterpret_cast<const float4*>(sec == 0 ? epi.q_probe : epi.k_probe);
+            float ssq = 0.0f, d[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int i4 = 0; i4 < 16; ++i4) {
+#pragma unroll
+              for (int r = 0; r < 4; ++r) {
+                const float4 p4 = __ldg(pr + r * 16 + i4);
+                d[r] = fmaf(v[4 * i4], p4.x, d[r]);
+                d[r] = fmaf(v[4 * i4 + 1], p4.y, d[r]);
+                d[r] = fmaf(v[4 * i4 + 2], p4.z, d[r]);
+                d[r] = fmaf(v[4 * i4 + 3], p4.w, d[r]);
+              }
+            }
+#pragma unroll
+            for (int i = 0; i < 64; ++i) ssq = fmaf(v[i], v[i], ssq);
+            const float inv = rsqrtf(ssq + 1e-6f * 64.0f);
+            float* dst = (sec == 0 ? epi.y_pre : epi.z_pre) + hrow * 4;
+            *reinterpret_cast<float4*>(dst) = make_float4(d[0] * inv, d[1] * inv, d[2] * inv, d[3] * inv);
+          }
+          if ((sec == 1 || sec == 2) && row < M) {
+            float amax = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 64; ++i) amax = fmaxf(amax, fabsf(v[i]));
+            const __half sh = q6_scale_from_amax(amax);
+            const float qinv = q6_inv_step(__half2float(sh));
+            uint32_t w[12];
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {
+              uint32_t cc[16];
+#pragma unroll
+              for (int i = 0; i < 16; ++i) cc[i] = (uint32_t)(q6_quantize(v[16 * g + i], qinv) & 63);
+              w[3 * g] = cc[0] | cc[1] << 6 | cc[2] << 12 | cc[3] << 18 | cc[4] << 24 | cc[5] << 30;
+              w[3 * g + 1] = cc[5] >> 2 | cc[6] << 4 | cc[7] << 10 | cc[8] << 16 | cc[9] << 22 | cc[10] << 28;
+              w[3 * g + 2] = cc[10] >> 4 | cc[11] << 2 | cc[12] << 8 | cc[13] << 14 | cc[14] << 20 | cc[15] << 26;
+            }
+            uint4* cd = reinterpret_cast<uint4*>((sec == 1 ? epi.k_codes : epi.v_codes) + hrow * 48);
+            cd[0] = make_uint4(w[0], w[1], w[2], w[3]);
+            cd[1] = make_uint4(w[4], w[5], w[6], w[7]);
+            cd[2] = make_uint4(w[8], w[9], w[10], w[11]);
+            (sec == 1 ? epi.k_scales : epi.v_scales)[hrow] = __half_as_ushort(sh);
+          }
+        }
+      } else if constexpr (EPI == kEpiStore) {
+        // 64-column chunks: TMEM -> registers (+bias) -> bf16 rows in this
+        // warp's 128-byte-swizzled staging box -> one TMA store of 32 x 64.
+        constexpr int CW = BN / 2;
+        const uint32_t stg = sStage + e * 4096;
+        uint8_t* stg_p = gsm + (stg - base);
+#pragma unroll 1
+        for (int c = half * CW; c < (half + 1) * CW; c += 64) {
+          float v[64];
+          tmem_ld64(tbase + c, v);
+          if (c + 64 == (half + 1) * CW) {  // last TMEM read of this tile by this warp
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar_tempty + 8 * a);
+          }
+          if (epi.bias != nullptr) add_bias64(epi.bias, epi.bias_bf16, n0 + c, v);
+          if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+          __syncwarp();
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const uint4 w = make_uint4(pack2(v[8 * j], v[8 * j + 1]), pack2(v[8 * j + 2], v[8 * j + 3]),
+                                       pack2(v[8 * j + 4], v[8 * j + 5]), pack2(v[8 * j + 6], v[8 * j + 7]));
+            *reinterpret_cast<uint4*>(stg_p + lane * 128 + ((j ^ (lane & 7)) << 4)) = w;
+          }
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmap_out, stg, n0 + c, m0 + quarter * 32);
+            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+          }
+        }
+      } else {
+        // Tile columns [0, H) are up, [H, 2H) the matching gate columns;
+        // 16-column chunks dealt alternately to the two warps of a quarter.
+        constexpr int H = BN / 2;
+        const int f0 = (t % tiles_n) * H;
+        const int row = m0 + quarter * 32 + lane;
+        constexpr int NCH = (H + 31) / 32;  // chunks per warp (the last may be absent for half 1)
+#pragma unroll
+        for (int k = 0; k < NCH; ++k) {
+          const int c0 = half * 16 + 32 * k;
+          const bool have = c0 < H;                      // warp-uniform
+          const bool last = have && c0 + 32 >= H;        // this warp's last TMEM read of the tile
+          float up[16], gt[16];
+          if (have) tmem_ld16x2(tbase + c0, tbase + H + c0, up, gt);
+          if (last) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar_tempty + 8 * a);
+          }
+          if (!have) break;
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            // silu in fp32 with the hardware exp2 and a fast divide (the bf16
+            // rounding after it absorbs the few-ulp fp32 difference).
+            const float u = round_bf16(up[i]), g = round_bf16(gt[i]);
+            up[i] = round_bf16(__fdividef(g, 1.0f + __expf(-g))) * u;
+          }
+          if (row < M) store16(epi.out + (int64_t)row * epi.ldo + f0 + c0, up);
+        }
+      }
+    }
+    if (EPI != kEpiSwiglu && lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    __syncwarp();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (*abort_flag && threadIdx.x == 0 && epi.status != nullptr) atomicExch(epi.status, DWARF_DEVICE_TIMEOUT);
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+  }
+}
+
+// ---------------------------------------------------------------- host side
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      p = nullptr;
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }();
+  return fn;
+}
+
+// 2-D bf16 tensor map over rows x cols (row stride ld elements), box box_rows x
+// box_cols (box_cols * 2 <= 128 bytes: one 128-byte swizzle row).
+bool make_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t K, int64_t ld, int box_rows, int box_cols) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+  const cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int num_sms() {
+  static int n = [] {
+    int dev = 0, v = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    return v > 0 ? v : kNumSMs;
+  }();
+  return n;
+}
+
+template <int BN, int EPI>
+int launch_gemm(const dwarf_gemm_args* a, const GemmEpi& epi, cudaStream_t stream) {
+  CUtensorMap ma, mb, mo;
+  if (!make_map(&ma, a->a, a->M, a->K, a->lda, kBM, kBK) || !make_map(&mb, a->b, a->N, a->K, a->ldb, BN, kBK))
+    return DWARF_ERR_LAUNCH;
+  CUtensorMap mn = ma;
+  // Output boxes of 32 rows x 64 columns (epilogues 0 and 2).
+  if (EPI != kEpiSwiglu && !make_map(&mo, a->out, a->M, a->N, a->ldo, 32, 64)) return DWARF_ERR_LAUNCH;
+  if (EPI == kEpiSwiglu) mo = ma;
+  if (EPI == kEpiRmsNorm && !make_map(&mn, a->n_out, a->M, a->N, a->ldn, 32, 64)) return DWARF_ERR_LAUNCH;
+  constexpr size_t smem = gemm_smem_bytes<BN, EPI>();
+  auto kernel = gemm_bf16_kernel<BN, EPI>;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    return launch_status();
+  // Work units: tiles, or whole M blocks for the RMSNorm epilogue.
+  const int64_t units = ((a->M + kBM - 1) / kBM) * (EPI == kEpiRmsNorm ? 1 : a->N / BN);
+  const int grid = (int)(units < num_sms() ? units : num_sms());
+  kernel<<<grid, kGemmThreads, smem, stream>>>(ma, mb, mo, mn, (int)a->M, (int)a->N, (int)a->K, epi);
+  return launch_status();
+}
+
+bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+}  // namespace dwarf
+
+using namespace dwarf;
+
+extern "C" int dwarf_gemm_bf16(const dwarf_gemm_args* a, void* stream) {
+  DWARF_CHECK_VERSION(a);
+  if (a->epilogue < DWARF_GEMM_STORE || a->epilogue > DWARF_GEMM_QKVG_PREP) return DWARF_ERR_VALUE;
+  if (a->M < 0 || a->N <= 0 || a->K <= 0 || a->K % 8 != 0) return DWARF_ERR_SHAPE;
+  if (a->M > 0x7fffffffLL || a->N > 0x7fffffffLL || a->K > 0x7fffffffLL) return DWARF_ERR_SHAPE;
+  if (a->M == 0) return DWARF_OK;
+  if (!a->a || !a->b || !a->out) return DWARF_ERR_NULL;
+  if (!al16(a->a) || !al16(a->b) || !al16(a->out) || a->lda % 8 || a->ldb % 8 || a->ldo % 8 || a->lda < a->K ||
+      a->ldb < a->K)
+    return DWARF_ERR_ALIGN;
+  if (a->bias != nullptr && a->bias_dtype != DWARF_F32 && a->bias_dtype != DWARF_BF16) return DWARF_ERR_DTYPE;
+  GemmEpi epi{a->bias, a->bias_dtype == DWARF_BF16, (__nv_bfloat16*)a->out, a->ldo, a->device_status,
+              (const __nv_bfloat16*)a->resid, a->ldr, a->norm_w, a->norm_w_dtype == DWARF_BF16, a->eps,
+              (int)a->T, a->heads, a->q_probe, a->k_probe, a->y_pre, a->z_pre, a->k_codes, a->k_scales,
+              a->v_codes, a->v_scales};
+  cudaStream_t st = (cudaStream_t)stream;
+  if (a->epilogue == DWARF_GEMM_QKVG_PREP) {
+    if (a->heads <= 0 || a->N != 256LL * a->heads || (64LL * a->heads) % 256 != 0) return DWARF_ERR_SHAPE;
+    if (a->T <= 0 || a->M % a->T != 0 || a->T > 0x7fffffffLL) return DWARF_ERR_SHAPE;
+    if (!a->bias || !a->q_probe || !a->k_probe || !a->y_pre || !a->z_pre || !a->k_codes || !a->k_scales ||
+        !a->v_codes || !a->v_scales)
+      return DWARF_ERR_NULL;
+    if (!al16(a->q_probe) || !al16(a->k_probe) || !al16(a->y_pre) || !al16(a->z_pre) || !al16(a->k_codes) ||
+        !al16(a->v_codes) || !al16(a->bias) || a->ldo < a->N)
+      return DWARF_ERR_ALIGN;
+    return launch_gemm<256, kEpiQkvg>(a, epi, st);
+  }
+  if (a->epilogue == DWARF_GEMM_RESID_RMSNORM) {
+    if (a->N != 256 && a->N != 512) return DWARF_ERR_SHAPE;
+    if (!a->resid || !a->norm_w || !a->n_out) return DWARF_ERR_NULL;
+    if (a->bias != nullptr) return DWARF_ERR_VALUE;
+    if (!al16(a->resid) || !al16(a->n_out) || !al16(a->norm_w) || a->ldr % 8 || a->ldn % 8 || a->ldo < a->N ||
+        a->ldr < a->N || a->ldn < a->N)
+      return DWARF_ERR_ALIGN;
+    if (a->norm_w_dtype != DWARF_F32 && a->norm_w_dtype != DWARF_BF16) return DWARF_ERR_DTYPE;
+    return launch_gemm<256, kEpiRmsNorm>(a, epi, st);
+  }
+  if (a->epilogue == DWARF_GEMM_STORE) {
+    if (a->ldo < a->N) return DWARF_ERR_SHAPE;
+    if (a->N % 256 == 0) return launch_gemm<256, kEpiStore>(a, epi, st);
+    if (a->N % 128 == 0) return launch_gemm<128, kEpiStore>(a, epi, st);
+    return DWARF_ERR_SHAPE;
+  }
+  if (a->bias != nullptr) return DWARF_ERR_VALUE;
+  const int h = a->swiglu_tile;
+  if (a->N % (2 * h) != 0 || a->ldo < a->N / 2) return DWARF_ERR_SHAPE;
+  if (h == 128) return launch_gemm<256, kEpiSwiglu>(a, epi, st);
+  if (h == 80) return launch_gemm<160, kEpiSwiglu>(a, epi, st);
+  if (h == 64) return launch_gemm<128, kEpiSwiglu>(a, epi, st);
+  return DWARF_ERR_SHAPE;
+}

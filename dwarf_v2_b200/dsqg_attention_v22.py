@@ -30,7 +30,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from . import _lib
+from . import _lib, gemm
 from .npci import npci_rotate_cuda
 
 R_PLANES = 4
@@ -495,10 +495,12 @@ def dsqg_prep(q, k, v, q_probe, k_probe, *, pack_q6: bool):
 class DSQGAttentionV19(nn.Module):
     """DSQG attention block with the reference's parameters and forward contract (reference :2780-3289).
 
-    Forward pipeline on the device: qkvg GEMM (cuBLAS) -> ``dwarf_dsqg_prep``
-    (probe projections, optional q6 pack) -> ``dwarf_dsqg_fwd`` with the
-    ``if_gain`` and ``sigmoid(content_gate)`` epilogue fused -> out_proj GEMM.
-    ``kv_cache="q6"`` runs the attention over the q6-quantised K/V cache.
+    Forward pipeline on the device. With ``kv_cache="q6"`` (no K/V injection):
+    the qkvg GEMM on tcgen05 with the probe projections and the q6 pack of K/V
+    fused into its epilogue (``dwarf_gemm_bf16`` epilogue 3) ->
+    ``dwarf_dsqg_fwd`` (resident-K/V kernel) with the ``if_gain`` and
+    ``sigmoid(content_gate)`` epilogue fused -> out_proj GEMM. Otherwise: qkvg
+    GEMM (cuBLAS) -> ``dwarf_dsqg_prep`` -> ``dwarf_dsqg_fwd`` -> out_proj.
     """
 
     def __init__(self, embedding_dim, num_heads, offsets, j_small, j_large, seq_len=2048, dropout=0.1,
@@ -699,6 +701,14 @@ class DSQGAttentionV19(nn.Module):
         act = torch.bfloat16
         xb = x if x.dtype == act else x.to(act)
         weight, bias = self.qkvg_proj.weight, self.qkvg_proj.bias
+        t = self._tables()
+        if kv_inject is None and self.kv_cache == "q6" and head_dim == 64 and dimension % 256 == 0:
+            # qkvg GEMM on tcgen05 with the prep pass (probes, q6 pack) in its epilogue.
+            qkvg, y_pre, z_pre, cache = gemm.qkvg_prep(xb, weight.to(act), bias.to(act), heads, t["q_probe"],
+                                                       t["k_probe"])
+            query = qkvg.view(batch, seq_len, 4, heads, head_dim)[:, :, 0].permute(0, 2, 1, 3)
+            return self._attend(x, query, ("q6", *cache), y_pre, z_pre, qkvg[:, :, 3 * dimension:], t,
+                                query_start)
         qkvg = F.linear(xb, weight.to(act), bias.to(act))  # [B, N, 4D]
         split = qkvg.view(batch, seq_len, 4, heads, head_dim)
         query = split[:, :, 0].permute(0, 2, 1, 3)
@@ -724,12 +734,18 @@ class DSQGAttentionV19(nn.Module):
                              strength_tau=self.npci_strength_tau)
             key = torch.cat((rk, key[:, :, key_end:]), dim=2) if key_end < seq_len else rk
             value = torch.cat((rv, value[:, :, key_end:]), dim=2) if key_end < seq_len else rv
-        t = self._tables()
         q6 = self.kv_cache == "q6"
         y_pre, z_pre, cache = dsqg_prep(query, key, value, t["q_probe"], t["k_probe"], pack_q6=q6)
+        kv = ("q6", *cache) if q6 else ("bf16", key, value)
+        return self._attend(x, query, kv, y_pre, z_pre, content_gate, t, query_start)
+
+    def _attend(self, x, query, kv, y_pre, z_pre, content_gate, t, query_start):
+        """DSQG kernel (if_gain and content-gate epilogue fused) followed by out_proj."""
+        act = torch.bfloat16
+        batch, heads, seq_len, head_dim = query.shape
+        dimension = heads * head_dim
         out = torch.empty(batch, seq_len, dimension, dtype=act, device=x.device)
         out_view = out.view(batch, seq_len, heads, head_dim).permute(0, 2, 1, 3)
-        kv = ("q6", *cache) if q6 else ("bf16", key, value)
         gain = self.if_gain if self.if_gain.dtype in (torch.bfloat16, torch.float32) else self.if_gain.float()
         _dsqg_launch(query, kv=kv, pos_bias=t["pos_bias"], scale_embed=t["scale_embed"],
                      phase_base=t["phase_base"], phase_gain=t["phase_gain"], y_pre=y_pre, z_pre=z_pre,

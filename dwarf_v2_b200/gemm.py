@@ -1,0 +1,150 @@
+"""Tensor-core GEMMs with fused epilogues (``dwarf_gemm_bf16``).
+
+Host mirror of the reference's ``F.linear`` calls (train/train_dwarf.py
+SwiGLUFFN and the attention projections): ``linear(x, w, bias)`` computes
+``x @ w.T + bias`` in bf16 with fp32 accumulation, and ``linear_swiglu``
+fuses SwiGLUFFN's ``silu(gate) * up`` into the up_gate projection.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+
+STORE = 0
+SWIGLU = 1
+RESID_RMSNORM = 2
+QKVG_PREP = 3
+SWIGLU_TILES = (128, 80, 64)
+
+
+def _rows2d(x: torch.Tensor) -> tuple[torch.Tensor, int]:
+    x2 = x.reshape(-1, x.shape[-1])
+    if x2.stride(-1) != 1:
+        x2 = x2.contiguous()
+    return x2, x2.stride(0)
+
+
+def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None,
+           out: torch.Tensor | None = None) -> torch.Tensor:
+    """bf16 ``x @ weight.T (+ bias)`` on tcgen05; weight [N, K] as nn.Linear stores it."""
+    _lib.require_cuda(x, weight, bias)
+    if x.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16:
+        raise TypeError("linear takes bf16 activations and weights")
+    N, K = weight.shape
+    x2, lda = _rows2d(x)
+    w = weight if weight.stride(-1) == 1 else weight.contiguous()
+    M = x2.shape[0]
+    if out is None:
+        out = torch.empty(*x.shape[:-1], N, dtype=torch.bfloat16, device=x.device)
+    o2 = out.view(-1, N)
+    args = _lib.GemmArgs(version=_lib.ABI_VERSION, epilogue=STORE, M=M, N=N, K=K, a=x2.data_ptr(), lda=lda,
+                         b=w.data_ptr(), ldb=w.stride(0), out=o2.data_ptr(), ldo=o2.stride(0))
+    if bias is not None:
+        b = bias.contiguous()
+        args.bias, args.bias_dtype = b.data_ptr(), _lib.dtype_code(b.dtype)
+    _lib.call("dwarf_gemm_bf16", args, x.device)
+    return out
+
+
+def swiglu_tile(hidden: int) -> int:
+    for h in SWIGLU_TILES:
+        if hidden % h == 0:
+            return h
+    raise ValueError(f"no SwiGLU tile width divides hidden={hidden} (supported {SWIGLU_TILES})")
+
+
+def interleave_up_gate(weight: torch.Tensor, tile: int | None = None) -> torch.Tensor:
+    """[2F, K] up_gate weight (up rows then gate rows) -> tile-interleaved rows for linear_swiglu."""
+    two_f, K = weight.shape
+    F = two_f // 2
+    h = tile or swiglu_tile(F)
+    up = weight[:F].reshape(F // h, h, K)
+    gate = weight[F:].reshape(F // h, h, K)
+    return torch.cat([up, gate], dim=1).reshape(two_f, K).contiguous()
+
+
+def linear_swiglu(x: torch.Tensor, weight_interleaved: torch.Tensor, tile: int,
+                  out: torch.Tensor | None = None) -> torch.Tensor:
+    """bf16(silu(bf16(x @ gate.T)) * bf16(x @ up.T)) with the reference rounding points."""
+    _lib.require_cuda(x, weight_interleaved)
+    if x.dtype != torch.bfloat16 or weight_interleaved.dtype != torch.bfloat16:
+        raise TypeError("linear_swiglu takes bf16 activations and weights")
+    N, K = weight_interleaved.shape
+    x2, lda = _rows2d(x)
+    M = x2.shape[0]
+    if out is None:
+        out = torch.empty(*x.shape[:-1], N // 2, dtype=torch.bfloat16, device=x.device)
+    o2 = out.view(-1, N // 2)
+    args = _lib.GemmArgs(version=_lib.ABI_VERSION, epilogue=SWIGLU, M=M, N=N, K=K, a=x2.data_ptr(), lda=lda,
+                         b=weight_interleaved.data_ptr(), ldb=weight_interleaved.stride(0), swiglu_tile=tile,
+                         out=o2.data_ptr(), ldo=o2.stride(0))
+    _lib.call("dwarf_gemm_bf16", args, x.device)
+    return out
+
+
+def linear_add_rmsnorm(x: torch.Tensor, weight: torch.Tensor, resid: torch.Tensor, norm_weight: torch.Tensor,
+                       eps: float = 1e-6, x_out: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """(v, n): v = bf16(resid + bf16(x @ weight.T)), n = RMSNorm(v) * norm_weight (dwarf_add_rmsnorm rounding).
+
+    Fuses the residual add and the next RMSNorm into the projection (N = 256 or 512);
+    ``x_out`` may be ``resid`` itself (in-place residual stream).
+    """
+    _lib.require_cuda(x, weight, resid, norm_weight)
+    if x.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16 or resid.dtype != torch.bfloat16:
+        raise TypeError("linear_add_rmsnorm takes bf16 activations, weights and residual")
+    N, K = weight.shape
+    x2, lda = _rows2d(x)
+    M = x2.shape[0]
+    r2 = resid.reshape(M, N)
+    if r2.stride(-1) != 1:
+        raise ValueError("resid rows must be contiguous")
+    if x_out is None:
+        x_out = torch.empty_like(resid)
+    n_out = torch.empty_like(resid)
+    o2, n2 = x_out.view(M, N), n_out.view(M, N)
+    nw = norm_weight.contiguous()
+    args = _lib.GemmArgs(version=_lib.ABI_VERSION, epilogue=RESID_RMSNORM, M=M, N=N, K=K, a=x2.data_ptr(),
+                         lda=lda, b=weight.data_ptr(), ldb=weight.stride(0), out=o2.data_ptr(), ldo=o2.stride(0),
+                         resid=r2.data_ptr(), ldr=r2.stride(0), norm_w=nw.data_ptr(),
+                         norm_w_dtype=_lib.dtype_code(nw.dtype), eps=float(eps), n_out=n2.data_ptr(),
+                         ldn=n2.stride(0))
+    _lib.call("dwarf_gemm_bf16", args, x.device)
+    return x_out, n_out
+
+
+def qkvg_prep(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, heads: int,
+              q_probe: torch.Tensor, k_probe: torch.Tensor):
+    """DSQG qkvg projection with the prep pass fused into its epilogue.
+
+    x [B, T, D] bf16; weight [4D, D], bias [4D]. Returns (qkvg, y_pre, z_pre,
+    (k_codes, k_scales, v_codes, v_scales)) where qkvg [B, T, 4D] holds valid
+    q and gate columns only (K and V exist only as the q6 cache).
+    """
+    _lib.require_cuda(x, weight, bias, q_probe, k_probe)
+    if x.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16:
+        raise TypeError("qkvg_prep takes bf16 activations and weights")
+    B, T, D = x.shape
+    N, K = weight.shape
+    if N != 4 * D or D != 64 * heads:
+        raise ValueError("qkvg_prep expects weight [4D, D] with D = 64 * heads")
+    dev = x.device
+    x2, lda = _rows2d(x)
+    qkvg = torch.empty(B, T, N, dtype=torch.bfloat16, device=dev)
+    y = torch.empty(B, heads, T, 4, dtype=torch.float32, device=dev)
+    z = torch.empty_like(y)
+    kc = torch.empty(B, heads, T, 48, dtype=torch.uint8, device=dev)
+    vc = torch.empty_like(kc)
+    ks = torch.empty(B, heads, T, dtype=torch.float16, device=dev)
+    vs = torch.empty_like(ks)
+    b = bias.contiguous()
+    qp, kp = q_probe.float().contiguous(), k_probe.float().contiguous()
+    args = _lib.GemmArgs(version=_lib.ABI_VERSION, epilogue=QKVG_PREP, M=B * T, N=N, K=K, a=x2.data_ptr(),
+                         lda=lda, b=weight.data_ptr(), ldb=weight.stride(0), bias=b.data_ptr(),
+                         bias_dtype=_lib.dtype_code(b.dtype), out=qkvg.data_ptr(), ldo=N, T=T, heads=heads,
+                         q_probe=qp.data_ptr(), k_probe=kp.data_ptr(), y_pre=y.data_ptr(), z_pre=z.data_ptr(),
+                         k_codes=kc.data_ptr(), k_scales=ks.data_ptr(), v_codes=vc.data_ptr(),
+                         v_scales=vs.data_ptr())
+    _lib.call("dwarf_gemm_bf16", args, dev)
+    return qkvg, y, z, (kc, ks, vc, vs)

@@ -27,7 +27,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from . import glue
+from . import gemm, glue
 from .causal_ema_scan import bounded_ema_factor, causal_ema_scan, inverse_bounded_ema_factor
 from .dsqg_attention_v22 import ALL_OFFSETS, R_PLANES, DSQGAttentionV19
 from .hierarchical_sparse_attn_v18_hisa import HierarchicalSparseAttentionV16HISACausal
@@ -121,9 +121,20 @@ class SwiGLUFFN(nn.Module):
         self.down = nn.Linear(hidden, config.embedding_dim, bias=False)
         self.dropout = nn.Dropout(config.dropout)
 
+    def _interleaved(self) -> tuple[torch.Tensor, int]:
+        """up_gate weight in the tile-interleaved order of the fused SwiGLU GEMM (cached per weight version)."""
+        w = self.up_gate.weight
+        key = (w.data_ptr(), w._version, w.device)
+        if getattr(self, "_il_key", None) != key:
+            tile = gemm.swiglu_tile(w.shape[0] // 2)
+            self._il = (gemm.interleave_up_gate(_act(w.detach()), tile), tile)
+            self._il_key = key
+        return self._il
+
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        """down(silu(gate) * up): two cuBLAS GEMMs around the ``dwarf_swiglu`` kernel."""
-        h = glue.swiglu(F.linear(_act(x), _act(self.up_gate.weight)))
+        """down(silu(gate) * up): the tcgen05 GEMM with the SwiGLU epilogue, then the down projection."""
+        w_il, tile = self._interleaved()
+        h = gemm.linear_swiglu(_act(x), w_il, tile)
         return F.linear(h, _act(self.down.weight))
 
 

@@ -442,6 +442,70 @@ int dwarf_swiglu(const dwarf_swiglu_args* args, void* stream);
 int dwarf_gate_mul(const dwarf_gate_mul_args* args, void* stream);
 int dwarf_packet(const dwarf_packet_args* args, void* stream);
 
+/* ------------------------------------------------------------------------
+ * bf16 GEMM on the 5th-generation tensor cores (tcgen05, TMA, TMEM) with
+ * fused epilogues: out = epilogue(A . B^T), A bf16 [M, K] (row stride lda),
+ * B bf16 [N, K] (row stride ldb; a torch Linear weight), fp32 accumulation.
+ *
+ * Replaces F.linear (+ the following row-wise op) of the reference blocks:
+ *   epilogue 0 (DWARF_GEMM_STORE):  out[M, N] = bf16(acc + bias)
+ *     -- nn.Linear (train/train_dwarf.py:230-240, 299-322, 325-364, 470);
+ *   epilogue 1 (DWARF_GEMM_SWIGLU): out[M, N/2] = SwiGLU of the pair
+ *     (up, gate) with dwarf_swiglu's rounding -- SwiGLUFFN.up_gate followed
+ *     by silu(gate) * up (train/train_dwarf.py:230-240). B must hold the
+ *     up_gate weight in tile-interleaved order: for tile t (of width 2h,
+ *     h = swiglu_tile), rows [2ht, 2ht+h) are up rows [ht, ht+h) and rows
+ *     [2ht+h, 2h(t+1)) are the matching gate rows (F + ht ...).
+ *   epilogue 2 (DWARF_GEMM_RESID_RMSNORM): the residual add and RMSNorm
+ *     that follow out_proj / down (train/train_dwarf.py:218-225, 320-322):
+ *     v = bf16(resid + bf16(acc)) -> out[M, N] (out may alias resid), and
+ *     n_out = bf16((v * rsqrt(mean(v^2) + eps)) * norm_w), as
+ *     dwarf_add_rmsnorm rounds them. N must be 256 or 512.
+ *   epilogue 3 (DWARF_GEMM_QKVG_PREP): the DSQG qkvg projection (+bias)
+ *     with dwarf_dsqg_prep fused in (dsqg_attention_v22.py:3218-3254):
+ *     N = 4 D (q | k | v | gate, D = 64 * heads, D % 256 == 0, M = B * T);
+ *     q and gate columns go to out (bf16, k/v columns are not written),
+ *     y_pre / z_pre come from the bf16 q / k rows and K / V are written
+ *     only as the q6 cache (dwarf_q6_pack layout, [B, heads, T] rows).
+ * Requirements: K % 8 == 0, 16-byte aligned A/B/out and row strides; N a
+ * multiple of the tile width (256 or 128 for epilogue 0, 2*swiglu_tile for
+ * epilogue 1 with swiglu_tile in {128, 80, 64}).
+ * ---------------------------------------------------------------------- */
+#define DWARF_GEMM_STORE 0
+#define DWARF_GEMM_SWIGLU 1
+#define DWARF_GEMM_RESID_RMSNORM 2
+#define DWARF_GEMM_QKVG_PREP 3
+
+typedef struct {
+  int32_t version;
+  int32_t epilogue;               /* DWARF_GEMM_*                          */
+  int64_t M, N, K;
+  const void* a;     int64_t lda; /* bf16 [M, K]                           */
+  const void* b;     int64_t ldb; /* bf16 [N, K]                           */
+  const void* bias;               /* optional [N] (epilogue 0)             */
+  int32_t bias_dtype;             /* DWARF_F32 or DWARF_BF16               */
+  int32_t swiglu_tile;            /* h of epilogue 1                       */
+  void* out;         int64_t ldo; /* bf16                                  */
+  int32_t* device_status;         /* optional; set to DWARF_DEVICE_TIMEOUT */
+  const void* resid; int64_t ldr; /* epilogue 2: bf16 residual [M, N]      */
+  const void* norm_w;             /* epilogue 2: [N]                       */
+  int32_t norm_w_dtype;           /* DWARF_F32 or DWARF_BF16               */
+  float eps;
+  void* n_out;       int64_t ldn; /* epilogue 2: bf16 [M, N]               */
+  int64_t T;                      /* epilogue 3: rows per batch entry      */
+  int32_t heads;                  /* epilogue 3: D / 64                    */
+  const float* q_probe;           /* epilogue 3: [4][64] unit probes       */
+  const float* k_probe;
+  float* y_pre;                   /* epilogue 3: [B, heads, T, 4]          */
+  float* z_pre;                   /* epilogue 3: [B, heads, T, 4]          */
+  uint8_t* k_codes;               /* epilogue 3: [B, heads, T, 48]         */
+  uint16_t* k_scales;             /* epilogue 3: [B, heads, T]             */
+  uint8_t* v_codes;
+  uint16_t* v_scales;
+} dwarf_gemm_args;
+
+int dwarf_gemm_bf16(const dwarf_gemm_args* args, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
