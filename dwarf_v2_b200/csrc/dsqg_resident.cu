@@ -5,26 +5,29 @@
 // _fwd_v22_online, kernels/dsqg_attention_v22.py:698-860, for the q6 cache of
 // _DSQGV18GroupedFn.forward, :2197-2352), for the layout the engine itself
 // produces: dwarf_q6_pack rows (48 code bytes, contiguous) and fp16 scales
-// (contiguous), N <= 2048 with N % 8 == 0, J <= 32.
+// (contiguous), N % 8 == 0 and small enough for the cache to fit (N <= 2176),
+// J <= 32.
 //
 // Why resident: every key row n - off_j is used by the J queries that reach
 // it, so the gather kernel reads each row ~J times through L2 and pays an L2
 // latency per (query, offset) pair. Here one CTA owns one (b, h): the 100 B
 // per row of K+V codes and scales (200 KB at N = 2048) arrive by bulk copies
-// (cp.async.bulk, one mbarrier per 192-row chunk, all issued at kernel start)
-// and every pair reads its row from shared memory. Rows of consecutive
-// queries are consecutive 48-B rows, which keeps the 64-bit shared loads of a
-// half-warp on 16 distinct bank pairs (conflict-free).
+// (cp.async.bulk, one mbarrier per 256-row chunk, all issued at kernel start)
+// and every pair reads its rows from shared memory. A warp's 32 queries read
+// 32 consecutive 48-B rows: the 16-B shared loads of each 8-lane phase fall
+// on 8 distinct bank groups (conflict-free).
 //
-// Work split: 384 threads = 12 warps; a round covers 192 queries (one chunk),
-// 2 threads per query (32 head dims each). Per round: wait for the round's
-// chunk, flip the sign bit of every 6-bit field in place (two's complement
-// -> offset binary, once per row instead of once per pair), then each warp
-// computes q . bf16(E_j) for its 16 queries on tensor cores (mma.sync) and
-// runs one online-softmax pass over the offsets with K and V of a pair
-// consumed together. The running maximum is only moved when a score exceeds
-// it by more than 2^8 in the exp2 domain, so accumulators are rescaled
-// rarely; weights stay below 2^8.
+// Work split: 256 threads = 8 warps, ONE thread per query (all 64 head dims
+// and all 4 MOVT planes), so the per-pair bookkeeping (score, softmax
+// update, loop control) is done once per pair. A round covers 256 queries
+// (one chunk): wait for the chunk, flip the sign bit of every 6-bit field in
+// place (two's complement -> offset binary, once per row instead of once
+// per pair), then each warp walks the offsets in groups of 8: q . bf16(E_j)
+// for its 32 queries x 8 offsets on tensor cores (mma.sync, through a small
+// per-warp transpose buffer into registers), then 8 unrolled pair steps of
+// one online-softmax pass with K and V of a pair consumed together. The
+// running maximum only moves when a score exceeds it by more than 2^8 in the
+// exp2 domain, so accumulators are rescaled rarely; weights stay below 2^8.
 //
 // Decoding without int->float: field i of a 96-bit slice is masked in place
 // at bit K_i <= 17 and read as an fp32 denormal, u_i * 2^(K_i - 149), exactly.
@@ -40,20 +43,21 @@ namespace {
 using namespace dsqg;
 using namespace wmma16;
 
-constexpr int kRThreads = 384;
-constexpr int kRQB = 192;  // queries per round == key rows per chunk
+constexpr int kRThreads = 256;
+constexpr int kRWarps = kRThreads / 32;
+constexpr int kRQB = 256;  // queries per round == key rows per chunk
 constexpr int kRMaxJ = 32;
 constexpr int kRSmemLimit = 232448;  // 227 KB opt-in shared memory per CTA
 constexpr float kRescaleLog2 = 8.0f;
 constexpr float kVPreScale = 1.2676506002282294e30f;  // 2^100
 constexpr int kVPreScaleLog2 = 100;
+constexpr int kQeLd = 9;  // row stride (floats) of the per-warp 32 x 8 q.E transpose buffer
 
 struct ResLayout {
-  int jp, qe_ld, chunks;
+  int jp, chunks;
   uint32_t o_kc, o_vc, o_ks, o_vs, o_e, o_qe, o_pb, o_off, o_pbase, o_pgain, o_bar, bytes;
   __host__ __device__ ResLayout(int N, int J, int jl) {
     jp = (J + 7) / 8 * 8;
-    qe_ld = J | 1;  // odd row stride: the 16 rows a warp reads sit in 16 banks
     chunks = (N + kRQB - 1) / kRQB;
     uint32_t o = 0;
     o_kc = o;    o += (uint32_t)N * 48;
@@ -61,7 +65,7 @@ struct ResLayout {
     o_ks = o;    o += (uint32_t)N * 2;
     o_vs = o;    o += (uint32_t)N * 2;
     o_e = o;     o += (uint32_t)jp * 128;
-    o_qe = o;    o += (uint32_t)kRQB * qe_ld * 4;
+    o_qe = o;    o += (uint32_t)kRWarps * 32 * kQeLd * 4;
     o_pb = o;    o += (uint32_t)J * 4;
     o_off = o;   o += (uint32_t)J * 4;
     o_pbase = o; o += (uint32_t)jl * 16;
@@ -97,6 +101,14 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
 }
 
 __device__ __forceinline__ float den(uint32_t bits) { return __uint_as_float(bits); }
+
+// 2^x on the SFU (arguments here are <= 8; results below 2^-126 flush to 0,
+// which only drops weights far below the running maximum).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 
 // sum_i q[i] * u_i * 2^(K_i - 149) over the 16 fields of a flipped slice,
 // q[i] pre-scaled by 2^(E - K_i): = 2^(E - 149) * sum_i q_i u_i.
@@ -144,6 +156,52 @@ __device__ __forceinline__ void axpy16(uint32_t w0, uint32_t w1, uint32_t w2, fl
   acc[15] = fmaf(wv, den(w2s & (63u << 14)), acc[15]);
 }
 
+// (a0, a1) += (q0, q1) * (x, y) as one packed fp32x2 FMA (sm_100).
+__device__ __forceinline__ void fma2v(float& a0, float& a1, float q0, float q1, float x, float y) {
+  asm("{\n.reg .b64 pa, pb, pc;\nmov.b64 pa, {%2, %3};\nmov.b64 pb, {%4, %5};\nmov.b64 pc, {%0, %1};\n"
+      "fma.rn.f32x2 pc, pa, pb, pc;\nmov.b64 {%0, %1}, pc;\n}"
+      : "+f"(a0), "+f"(a1)
+      : "f"(q0), "f"(q1), "f"(x), "f"(y));
+}
+
+// dot16 with packed fp32x2 FMAs (two running pairs).
+__device__ __forceinline__ float dot16x2(uint32_t w0, uint32_t w1, uint32_t w2, const float* q) {
+  const uint32_t w0s = w0 >> 12, w1s = w1 >> 12, w2s = w2 >> 12;
+  const uint32_t f5 = __funnelshift_r(w0, w1, 30), f10 = __funnelshift_r(w1, w2, 28);
+  float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
+  fma2v(a0, a1, q[0], q[1], den(w0 & 63u), den(w0 & (63u << 6)));
+  fma2v(b0, b1, q[2], q[3], den(w0 & (63u << 12)), den(w0s & (63u << 6)));
+  fma2v(a0, a1, q[4], q[5], den(w0s & (63u << 12)), den(f5 & 63u));
+  fma2v(b0, b1, q[6], q[7], den(w1 & (63u << 4)), den(w1 & (63u << 10)));
+  fma2v(a0, a1, q[8], q[9], den(w1 & (63u << 16)), den(w1s & (63u << 10)));
+  fma2v(b0, b1, q[10], q[11], den(f10 & 63u), den(w2 & (63u << 2)));
+  fma2v(a0, a1, q[12], q[13], den(w2 & (63u << 8)), den(w2 & (63u << 14)));
+  fma2v(b0, b1, q[14], q[15], den(w2s & (63u << 8)), den(w2s & (63u << 14)));
+  return (a0 + a1) + (b0 + b1);
+}
+
+// acc[2i], acc[2i+1] += w * (x, y) as one packed fp32x2 FMA (sm_100).
+__device__ __forceinline__ void fma2(float& a0, float& a1, float w, float x, float y) {
+  asm("{\n.reg .b64 pa, pb, pc;\nmov.b64 pa, {%2, %2};\nmov.b64 pb, {%3, %4};\nmov.b64 pc, {%0, %1};\n"
+      "fma.rn.f32x2 pc, pa, pb, pc;\nmov.b64 {%0, %1}, pc;\n}"
+      : "+f"(a0), "+f"(a1)
+      : "f"(w), "f"(x), "f"(y));
+}
+
+// axpy16 with packed fp32x2 FMAs.
+__device__ __forceinline__ void axpy16x2(uint32_t w0, uint32_t w1, uint32_t w2, float wv, float* acc) {
+  const uint32_t w0s = w0 >> 12, w1s = w1 >> 12, w2s = w2 >> 12;
+  const uint32_t f5 = __funnelshift_r(w0, w1, 30), f10 = __funnelshift_r(w1, w2, 28);
+  fma2(acc[0], acc[1], wv, den(w0 & 63u), den(w0 & (63u << 6)));
+  fma2(acc[2], acc[3], wv, den(w0 & (63u << 12)), den(w0s & (63u << 6)));
+  fma2(acc[4], acc[5], wv, den(w0s & (63u << 12)), den(f5 & 63u));
+  fma2(acc[6], acc[7], wv, den(w1 & (63u << 4)), den(w1 & (63u << 10)));
+  fma2(acc[8], acc[9], wv, den(w1 & (63u << 16)), den(w1s & (63u << 10)));
+  fma2(acc[10], acc[11], wv, den(f10 & 63u), den(w2 & (63u << 2)));
+  fma2(acc[12], acc[13], wv, den(w2 & (63u << 8)), den(w2 & (63u << 14)));
+  fma2(acc[14], acc[15], wv, den(w2s & (63u << 8)), den(w2s & (63u << 14)));
+}
+
 // Offset-binary fields rot and rot + 1 of a flipped slice minus the +32 bias.
 // PW = (6 * rot) / 32 is the word the pair starts in; off = (6 * rot) % 32.
 template <int PW>
@@ -155,12 +213,6 @@ __device__ __forceinline__ void movt_pair(uint32_t w0, uint32_t w1, uint32_t w2,
   a = __uint_as_float(0x4B000000u | (x & 63u)) - 8388640.0f;          // 2^23 + 32
   b = __uint_as_float(0x4B000000u | ((x >> 6) & 63u)) - 8388640.0f;
 }
-
-struct RState {
-  float acc[32];
-  float l, wbias, m;
-  float corr_a[2], corr_b[2];
-};
 
 template <int PW>
 __global__ void __launch_bounds__(kRThreads, 1) dsqg_resident_kernel(const DsqgParams p, int32_t* status) {
@@ -227,13 +279,12 @@ __global__ void __launch_bounds__(kRThreads, 1) dsqg_resident_kernel(const DsqgP
   const uint8_t* s_vc = smem + L.o_vc;
   const __half* s_ks = reinterpret_cast<const __half*>(smem + L.o_ks);
   const __half* s_vs = reinterpret_cast<const __half*>(smem + L.o_vs);
-  float* s_qe = reinterpret_cast<float*>(smem + L.o_qe);
-  const int sub = lane & 1;
+  float* qe_buf = reinterpret_cast<float*>(smem + L.o_qe) + warp * 32 * kQeLd;
   const int rot = p.plane_shift;
   const uint32_t rot_off = (uint32_t)(6 * rot) & 31u;
   const float c_score = 0.125f * kLog2e;
   const __nv_bfloat16* qbase = p.q + b * p.sqb + h * p.sqh;
-  const float* zbase = p.z + b * p.szb + hk * p.szh + sub * 2;
+  const float* zbase = p.z + b * p.szb + hk * p.szh;
   float gain = 1.0f;
   if (p.gain != nullptr)
     gain = p.gain_bf16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.gain)[h])
@@ -264,57 +315,22 @@ __global__ void __launch_bounds__(kRThreads, 1) dsqg_resident_kernel(const DsqgP
     }
     __syncthreads();
 
-    const int wn0 = n0 + warp * 16;
+    const int wn0 = n0 + warp * 32;
     if (wn0 >= N) continue;  // warp-uniform; no block barrier follows before the next round
 
-    // ---- q . bf16(E_j) for this warp's 16 queries (mma m16n8k16, A straight from global)
-    float* qe_w = s_qe + warp * 16 * L.qe_ld;
-    {
-      const int g = lane >> 2, t4 = lane & 3;
-      const int ra = wn0 + g < N ? wn0 + g : N - 1;
-      const int rb = wn0 + g + 8 < N ? wn0 + g + 8 : N - 1;
-      const __nv_bfloat16* qa = qbase + (int64_t)ra * p.sqn + 2 * t4;
-      const __nv_bfloat16* qb2 = qbase + (int64_t)rb * p.sqn + 2 * t4;
-      uint32_t a[4][4];
-#pragma unroll
-      for (int ks = 0; ks < 4; ++ks) {
-        a[ks][0] = __ldg(reinterpret_cast<const uint32_t*>(qa + ks * 16));
-        a[ks][1] = __ldg(reinterpret_cast<const uint32_t*>(qb2 + ks * 16));
-        a[ks][2] = __ldg(reinterpret_cast<const uint32_t*>(qa + ks * 16 + 8));
-        a[ks][3] = __ldg(reinterpret_cast<const uint32_t*>(qb2 + ks * 16 + 8));
-      }
-      for (int nt = 0; nt < L.jp / 8; ++nt) {
-        float c[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int ks = 0; ks < 4; ++ks) {
-          uint32_t b0, b1;
-          ldsm_x2(tile_addr(e_base, nt * 8 + (lane & 7), ks * 2 + ((lane >> 3) & 1)), b0, b1);
-          mma_bf16(c, a[ks], b0, b1);
-        }
-        const int col = nt * 8 + 2 * t4;
-        if (col < J) { qe_w[g * L.qe_ld + col] = c[0]; qe_w[(g + 8) * L.qe_ld + col] = c[2]; }
-        if (col + 1 < J) { qe_w[g * L.qe_ld + col + 1] = c[1]; qe_w[(g + 8) * L.qe_ld + col + 1] = c[3]; }
-      }
-    }
-    __syncwarp();
-
-    // ---- per-query state (2 threads per query, 32 dims each)
-    const int qi = lane >> 1;
-    const int n = wn0 + qi;
+    // ---- per-query state: this thread's query n, all 64 dims
+    const int n = wn0 + lane;
     const bool row_ok = n < N && n >= p.query_start;
     const int nq = n < N ? n : N - 1;
-    const float* my_qe = qe_w + qi * L.qe_ld;
-    float qs[32];
+    float qs[64];
     float qbias, c1;
     {
-      const uint4* src = reinterpret_cast<const uint4*>(qbase + (int64_t)nq * p.sqn + sub * 32);
-      uint4 w[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) w[i] = __ldg(src + i);
+      const uint4* src = reinterpret_cast<const uint4*>(qbase + (int64_t)nq * p.sqn);
       float qmax = 0.0f, qsum = 0.0f;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const uint32_t u[4] = {w[i].x, w[i].y, w[i].z, w[i].w};
+      for (int i = 0; i < 8; ++i) {
+        const uint4 w = __ldg(src + i);
+        const uint32_t u[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
           qs[8 * i + 2 * k] = __uint_as_float(u[k] << 16);
@@ -322,101 +338,120 @@ __global__ void __launch_bounds__(kRThreads, 1) dsqg_resident_kernel(const DsqgP
         }
       }
 #pragma unroll
-      for (int i = 0; i < 32; ++i) { qmax = fmaxf(qmax, fabsf(qs[i])); qsum += qs[i]; }
-      qmax = fmaxf(qmax, __shfl_xor_sync(0xffffffffu, qmax, 1));
+      for (int i = 0; i < 64; ++i) { qmax = fmaxf(qmax, fabsf(qs[i])); qsum += qs[i]; }
       const int e = (int)((__float_as_uint(qmax) >> 23) & 255u) - 127;  // floor(log2 qmax)
       int E = 125 - e;
       E = E > 100 ? 100 : (E < 22 ? 22 : E);
+      // 2^(E - K) for the nine field placements K = 0, 2, ..., 16.
+      float sc[9];
 #pragma unroll
-      for (int i = 0; i < 32; ++i) qs[i] *= __int_as_float((127 + E - q6_field_shift(i & 15)) << 23);
+      for (int k = 0; k < 9; ++k) sc[k] = __int_as_float((127 + E - 2 * k) << 23);
+#pragma unroll
+      for (int i = 0; i < 64; ++i) qs[i] *= sc[q6_field_shift(i & 15) / 2];
       c1 = __int_as_float((276 - E) << 23);  // 2^(149 - E)
       qbias = -32.0f * qsum;
     }
-    float yq[2];
+    float gy[4];  // y_pre of this query (multiplies phase_gain)
     {
-      const float2 y2 = *reinterpret_cast<const float2*>(p.y + b * p.syb + h * p.syh + (int64_t)nq * p.syn + sub * 2);
-      yq[0] = y2.x; yq[1] = y2.y;
+      const float4 y4 = *reinterpret_cast<const float4*>(p.y + b * p.syb + h * p.syh + (int64_t)nq * p.syn);
+      gy[0] = y4.x; gy[1] = y4.y; gy[2] = y4.z; gy[3] = y4.w;
     }
 
-    RState st;
+    float acc[64];
 #pragma unroll
-    for (int i = 0; i < 32; ++i) st.acc[i] = 0.0f;
-    st.l = 0.0f; st.wbias = 0.0f; st.m = -INFINITY;
-    st.corr_a[0] = st.corr_a[1] = st.corr_b[0] = st.corr_b[1] = 0.0f;
+    for (int i = 0; i < 64; ++i) acc[i] = 0.0f;
+    float l = 0.0f, wbias = 0.0f, m = -INFINITY;
+    float corr_a[4] = {0.f, 0.f, 0.f, 0.f}, corr_b[4] = {0.f, 0.f, 0.f, 0.f};
 
-    // One (query, offset) pair; returns the weight-times-step of the pair.
-    auto pair = [&](int j, bool valid, int src) -> float {
-      const uint32_t* kr = reinterpret_cast<const uint32_t*>(s_kc + src * 48 + sub * 24);
-      const uint2 k01 = *reinterpret_cast<const uint2*>(kr);
-      const uint2 k23 = *reinterpret_cast<const uint2*>(kr + 2);
-      const uint2 k45 = *reinterpret_cast<const uint2*>(kr + 4);
-      const float sk = __half2float(s_ks[src]) * (1.0f / 31.0f);
-      const float P = dot16(k01.x, k01.y, k23.x, qs) + dot16(k23.y, k45.x, k45.y, qs + 16);
-      float part = fmaf(P, c1, qbias) * sk;
-      part += __shfl_xor_sync(0xffffffffu, part, 1);
-      float s2 = fmaf(part + my_qe[j], c_score, s_pb[j]);
-      s2 = valid ? s2 : -INFINITY;
-      if (s2 > st.m + kRescaleLog2) {  // uniform within the query's two threads
-        const float f = exp2f(st.m - s2);
+    // Offsets in groups of 8: q . bf16(E_j) for the warp's 32 queries on
+    // tensor cores, transposed through qe_buf into this thread's qe[8].
+    const int g = lane >> 2, t4 = lane & 3;
+#pragma unroll 1
+    for (int j0 = 0; j0 < J; j0 += 8) {
+      {
+        __syncwarp();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) st.acc[i] *= f;
-        st.l *= f; st.wbias *= f;
-        st.corr_a[0] *= f; st.corr_a[1] *= f; st.corr_b[0] *= f; st.corr_b[1] *= f;
-        st.m = s2;
+        for (int mt = 0; mt < 2; ++mt) {
+          const int ra = min(wn0 + mt * 16 + g, N - 1), rb = min(wn0 + mt * 16 + g + 8, N - 1);
+          const __nv_bfloat16* qa = qbase + (int64_t)ra * p.sqn + 2 * t4;
+          const __nv_bfloat16* qb2 = qbase + (int64_t)rb * p.sqn + 2 * t4;
+          float c[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks) {
+            const uint32_t a[4] = {__ldg(reinterpret_cast<const uint32_t*>(qa + ks * 16)),
+                                   __ldg(reinterpret_cast<const uint32_t*>(qb2 + ks * 16)),
+                                   __ldg(reinterpret_cast<const uint32_t*>(qa + ks * 16 + 8)),
+                                   __ldg(reinterpret_cast<const uint32_t*>(qb2 + ks * 16 + 8))};
+            uint32_t b0, b1;
+            ldsm_x2(tile_addr(e_base, j0 + (lane & 7), ks * 2 + ((lane >> 3) & 1)), b0, b1);
+            mma_bf16(c, a, b0, b1);
+          }
+          float* r0p = qe_buf + (mt * 16 + g) * kQeLd + 2 * t4;
+          float* r1p = r0p + 8 * kQeLd;
+          r0p[0] = c[0]; r0p[1] = c[1];
+          r1p[0] = c[2]; r1p[1] = c[3];
+        }
+        __syncwarp();
       }
-      const float w = valid ? exp2f(s2 - st.m) : 0.0f;
-      const float sv = __half2float(s_vs[src]) * (1.0f / 31.0f);
-      const float wv = w * sv;
-      st.l += w;
-      st.wbias += wv;
-      const uint32_t* vr = reinterpret_cast<const uint32_t*>(s_vc + src * 48 + sub * 24);
-      const uint2 v01 = *reinterpret_cast<const uint2*>(vr);
-      const uint2 v23 = *reinterpret_cast<const uint2*>(vr + 2);
-      const uint2 v45 = *reinterpret_cast<const uint2*>(vr + 4);
-      const float wvs = wv * kVPreScale;
-      axpy16(v01.x, v01.y, v23.x, wvs, st.acc);
-      axpy16(v23.y, v45.x, v45.y, wvs, st.acc + 16);
-      return wv;
-    };
-
-    // Small band: no MOVT.
-    for (int j = 0; j < js; ++j) {
-      const int s = n - s_off[j];
-      const bool valid = row_ok && s >= 0;
-      (void)pair(j, valid, valid ? s : 0);
-    }
-    // Large band: MOVT plane rotation of the two planes this thread owns.
-    {
-      float2 zn = make_float2(0.f, 0.f);
-      if (js < J) {
-        const int s = nq - s_off[js];  // nq: rows past N must not index past the z rows
-        zn = *reinterpret_cast<const float2*>(zbase + (int64_t)(s >= 0 ? s : 0) * p.szn);
-      }
-      for (int j = js; j < J; ++j) {
+      const float* my_qe = qe_buf + lane * kQeLd;
+      const int jn = J - j0 < 8 ? J - j0 : 8;
+#pragma unroll 1
+      for (int jj = 0; jj < jn; ++jj) {
+        const int j = j0 + jj;
         const int s = n - s_off[j];
         const bool valid = row_ok && s >= 0;
         const int src = valid ? s : 0;
-        const float2 zc = zn;
-        if (j + 1 < J) {
-          const int s1 = nq - s_off[j + 1];
-          zn = *reinterpret_cast<const float2*>(zbase + (int64_t)(s1 >= 0 ? s1 : 0) * p.szn);
-        }
-        const float wv = pair(j, valid, src);
-        const uint32_t* vr = reinterpret_cast<const uint32_t*>(s_vc + src * 48 + sub * 24);
-        const int jl = j - js;
-        const float zz[2] = {zc.x, zc.y};
+        const bool large = j >= js;  // warp-uniform
+        float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (large) z4 = __ldg(reinterpret_cast<const float4*>(zbase + (int64_t)src * p.szn));
+
+        // score: q . k_src in the denormal domain, + q . bf16(E_j), + bias
+        const uint4* kr = reinterpret_cast<const uint4*>(s_kc + src * 48);
+        const uint4 k0 = kr[0], k1 = kr[1], k2 = kr[2];
+        const float sk = __half2float(s_ks[src]) * (1.0f / 31.0f);
+        const float P = (dot16x2(k0.x, k0.y, k0.z, qs) + dot16x2(k0.w, k1.x, k1.y, qs + 16)) +
+                        (dot16x2(k1.z, k1.w, k2.x, qs + 32) + dot16x2(k2.y, k2.z, k2.w, qs + 48));
+        const float part = fmaf(P, c1, qbias) * sk;
+        float s2 = fmaf(part + my_qe[jj], c_score, s_pb[j]);
+        s2 = valid ? s2 : -INFINITY;
+        if (s2 > m + kRescaleLog2) {
+          const float f = ex2_approx(m - s2);
 #pragma unroll
-        for (int sl = 0; sl < 2; ++sl) {
-          const uint32_t w0 = vr[3 * sl], w1 = vr[3 * sl + 1], w2 = vr[3 * sl + 2];
-          float fa, fb;
-          movt_pair<PW>(w0, w1, w2, rot_off, fa, fb);
-          const int plane = sub * 2 + sl;
-          const float theta = fmaf(s_pgain[jl * 4 + plane] * yq[sl], zz[sl], s_pbase[jl * 4 + plane]);
-          float sn, cs;
-          __sincosf(theta, &sn, &cs);
-          const float cm1 = cs - 1.0f;
-          st.corr_a[sl] = fmaf(wv, fmaf(cm1, fa, -sn * fb), st.corr_a[sl]);
-          st.corr_b[sl] = fmaf(wv, fmaf(sn, fa, cm1 * fb), st.corr_b[sl]);
+          for (int i = 0; i < 64; ++i) acc[i] *= f;
+          l *= f; wbias *= f;
+#pragma unroll
+          for (int pl = 0; pl < 4; ++pl) { corr_a[pl] *= f; corr_b[pl] *= f; }
+          m = s2;
+        }
+        const float w = valid ? ex2_approx(s2 - m) : 0.0f;
+        const float sv = __half2float(s_vs[src]) * (1.0f / 31.0f);
+        const float wv = w * sv;
+        l += w;
+        wbias += wv;
+        const uint4* vr = reinterpret_cast<const uint4*>(s_vc + src * 48);
+        const uint4 v0 = vr[0], v1 = vr[1], v2 = vr[2];
+        const float wvs = wv * kVPreScale;
+        axpy16x2(v0.x, v0.y, v0.z, wvs, acc);
+        axpy16x2(v0.w, v1.x, v1.y, wvs, acc + 16);
+        axpy16x2(v1.z, v1.w, v2.x, wvs, acc + 32);
+        axpy16x2(v2.y, v2.z, v2.w, wvs, acc + 48);
+        if (large) {
+          // MOVT: rotate plane r (channels 16 r + rot, + 1) by theta; keep
+          // rotated-minus-unrotated so the plain accumulation above stays.
+          const int jl = j - js;
+          const uint32_t vw[12] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w, v2.x, v2.y, v2.z, v2.w};
+          const float zz[4] = {z4.x, z4.y, z4.z, z4.w};
+#pragma unroll
+          for (int pl = 0; pl < 4; ++pl) {
+            float fa, fb;
+            movt_pair<PW>(vw[3 * pl], vw[3 * pl + 1], vw[3 * pl + 2], rot_off, fa, fb);
+            const float theta = fmaf(s_pgain[jl * 4 + pl] * gy[pl], zz[pl], s_pbase[jl * 4 + pl]);
+            float sn, cs;
+            __sincosf(theta, &sn, &cs);
+            const float cm1 = cs - 1.0f;
+            corr_a[pl] = fmaf(wv, fmaf(cm1, fa, -sn * fb), corr_a[pl]);
+            corr_b[pl] = fmaf(wv, fmaf(sn, fa, cm1 * fb), corr_b[pl]);
+          }
         }
       }
     }
@@ -424,31 +459,33 @@ __global__ void __launch_bounds__(kRThreads, 1) dsqg_resident_kernel(const DsqgP
     if (n >= N) continue;
     // ---- epilogue: undo the field scaling and the +32 bias, add MOVT
     // corrections, normalise, optional gain / gate, bf16 store.
-    const float bias = 32.0f * st.wbias;
-    const int d0 = sub * 32;
+    const float bias = 32.0f * wbias;
+    const float inv_l = l > 0.0f ? 1.0f / l : 0.0f;
+    __nv_bfloat16* orow = p.out + b * p.sob + h * p.soh + (int64_t)n * p.son;
+    const __nv_bfloat16* grow = p.gate != nullptr ? p.gate + b * p.sgtb + (int64_t)n * p.sgtn + h * 64 : nullptr;
 #pragma unroll
-    for (int sl = 0; sl < 2; ++sl) {
+    for (int sl = 0; sl < 4; ++sl) {
       float o[16];
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
-        float v = fmaf(st.acc[16 * sl + i], __int_as_float((127 + 149 - kVPreScaleLog2 - q6_field_shift(i)) << 23),
+        float v = fmaf(acc[16 * sl + i], __int_as_float((127 + 149 - kVPreScaleLog2 - q6_field_shift(i)) << 23),
                        -bias);
-        if (i == rot) v += st.corr_a[sl];
-        if (i == rot + 1) v += st.corr_b[sl];
-        o[i] = st.l > 0.0f ? round_bf16(v / st.l) : 0.0f;
+        if (i == rot) v += corr_a[sl];
+        if (i == rot + 1) v += corr_b[sl];
+        o[i] = round_bf16(v * inv_l);
       }
       if (p.gain != nullptr) {
 #pragma unroll
         for (int i = 0; i < 16; ++i) o[i] = p.gain_bf16 ? round_bf16(o[i] * gain) : o[i] * gain;
       }
-      if (p.gate != nullptr) {
-        const uint4* gp = reinterpret_cast<const uint4*>(p.gate + b * p.sgtb + (int64_t)n * p.sgtn + h * 64 + d0 + 16 * sl);
+      if (grow != nullptr) {
+        const uint4* gp = reinterpret_cast<const uint4*>(grow + 16 * sl);
         const uint4 gw[2] = {__ldg(gp), __ldg(gp + 1)};
         float gv[16];
         bf16x16_to_f32(gw, gv);
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          const float sg = round_bf16(1.0f / (1.0f + expf(-gv[i])));
+          const float sg = round_bf16(__frcp_rn(1.0f + __expf(-gv[i])));
           o[i] = p.gain_bf16 || p.gain == nullptr ? round_bf16(o[i] * sg) : o[i] * sg;
         }
       }
@@ -459,13 +496,12 @@ __global__ void __launch_bounds__(kRThreads, 1) dsqg_resident_kernel(const DsqgP
         const __nv_bfloat162 two = __floats2bfloat162_rn(o[2 * i], o[2 * i + 1]);
         pw[i] = *reinterpret_cast<const uint32_t*>(&two);
       }
-      uint4* dst = reinterpret_cast<uint4*>(p.out + b * p.sob + h * p.soh + (int64_t)n * p.son + d0 + 16 * sl);
+      uint4* dst = reinterpret_cast<uint4*>(orow + 16 * sl);
       dst[0] = packed[0];
       dst[1] = packed[1];
     }
-    if (p.lse != nullptr && sub == 0)
-      p.lse[b * p.slb + h * p.slh + (int64_t)n * p.sln] =
-          st.l > 0.0f ? st.m * 0.6931471805599453f + logf(st.l) : -INFINITY;
+    if (p.lse != nullptr)
+      p.lse[b * p.slb + h * p.slh + (int64_t)n * p.sln] = l > 0.0f ? m * 0.6931471805599453f + logf(l) : -INFINITY;
   }
 }
 
@@ -475,15 +511,15 @@ bool al(const void* ptr, uintptr_t a) { return (reinterpret_cast<uintptr_t>(ptr)
 
 int dsqg_resident_launch(const DsqgParams& p, int64_t B, cudaStream_t stream) {
   // Layout and size limits of the resident kernel; anything else goes to the gather kernel.
-  if (p.kc == nullptr || p.J > kRMaxJ || p.N > 2048 || p.N % 8 != 0 || p.cct != 48 || p.cst != 1) return kNotApplicable;
+  if (p.kc == nullptr || p.J > kRMaxJ || p.N % 8 != 0 || p.cct != 48 || p.cst != 1) return kNotApplicable;
   if (!al(p.kc, 16) || !al(p.vc, 16) || !al(p.ks, 16) || !al(p.vs, 16) || p.ccb % 16 || p.cch % 16 ||
       (p.csb * 2) % 16 || (p.csh * 2) % 16)
     return kNotApplicable;
-  if (!al(p.y, 8) || !al(p.z, 8) || p.syb % 2 || p.syh % 2 || p.syn % 2 || p.szb % 2 || p.szh % 2 || p.szn % 2)
+  if (!al(p.y, 16) || !al(p.z, 16) || p.syb % 4 || p.syh % 4 || p.syn % 4 || p.szb % 4 || p.szh % 4 || p.szn % 4)
     return kNotApplicable;
   if (p.gate != nullptr && p.sgtn % 8) return kNotApplicable;
   const ResLayout L((int)p.N, p.J, p.j_large);
-  if (L.bytes > (uint32_t)kRSmemLimit || B > 65535 || p.H > 0x7fffffff) return kNotApplicable;
+  if (p.N > 4096 || L.bytes > (uint32_t)kRSmemLimit || B > 65535 || p.H > 65535) return kNotApplicable;
   const int pw = (6 * p.plane_shift) >> 5;
   auto kernel = pw == 0 ? dsqg_resident_kernel<0> : (pw == 1 ? dsqg_resident_kernel<1> : dsqg_resident_kernel<2>);
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.bytes) != cudaSuccess)
