@@ -23,8 +23,7 @@
 #include "common.cuh"
 #include "q6_format.cuh"
 
-#include <cuda.h>
-#include <cudaTypedefs.h>
+#include "tma.cuh"
 
 #include <type_traits>
 
@@ -164,6 +163,50 @@ __device__ __forceinline__ void tmem_ld16x2(uint32_t t1, uint32_t t2, float (&a)
       : "r"(t1), "r"(t2) : "memory");
 #pragma unroll
   for (int i = 0; i < 16; ++i) { a[i] = __uint_as_float(r[i]); b[i] = __uint_as_float(r[16 + i]); }
+}
+// 32 fp32 columns of this thread's TMEM lane (load + wait in one asm).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr) : "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+// 32 bf16 of a row (64 bytes) as four 16-byte loads (plain loads: the row may be rewritten in place).
+__device__ __forceinline__ void load_row32(const __nv_bfloat16* p, uint4 (&w)[4]) {
+  const uint4* q = reinterpret_cast<const uint4*>(p);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) w[i] = q[i];
+}
+// 32 RMSNorm weights (fp32 or bf16) from column col.
+__device__ __forceinline__ void load_w32(const void* w, int bf16, int col, float (&o)[32]) {
+  if (bf16) {
+    const uint4* p = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(w) + col);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint4 v = __ldg(p + j);
+      const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        o[8 * j + 2 * k] = __uint_as_float(u[k] << 16);
+        o[8 * j + 2 * k + 1] = __uint_as_float(u[k] & 0xffff0000u);
+      }
+    }
+  } else {
+    const float4* p = reinterpret_cast<const float4*>(static_cast<const float*>(w) + col);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float4 v = __ldg(p + j);
+      o[4 * j] = v.x; o[4 * j + 1] = v.y; o[4 * j + 2] = v.z; o[4 * j + 3] = v.w;
+    }
+  }
 }
 __device__ __forceinline__ void add_bias64(const void* bias, int bf16, int col, float (&v)[64]) {
   if (bf16) {
@@ -342,70 +385,74 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
       const int t = tile_at(i);
       if (t >= tiles) break;
       const uint32_t a = tc & 1u, aph = (tc >> 1) & 1u;
+      const int m0 = (t / tiles_n) * kBM, n0 = (t % tiles_n) * BN;
+      // RMSNorm: the first residual chunk is loaded before waiting for the accumulator.
+      uint4 rbuf[2][4];
+      const int rrow = min(m0 + quarter * 32 + lane, M - 1);
+      if constexpr (EPI == kEpiRmsNorm) load_row32(epi.resid + (int64_t)rrow * epi.ldr + n0 + half * (BN / 2), rbuf[0]);
       if (!mbar_wait(bar_tfull + 8 * a, aph, abort_flag)) break;
       tc_fence_after();
-      const int m0 = (t / tiles_n) * kBM, n0 = (t % tiles_n) * BN;
       const uint32_t tbase = tmem + ((uint32_t)(quarter * 32) << 16) + a * kAccStride;
       if constexpr (EPI == kEpiRmsNorm) {
         // Residual add + RMSNorm over whole rows (N <= 512, BN = 256): each
-        // warp owns 32 rows x 128 columns of every column tile. Pass 1 writes
-        // v = x + addend per 64-column chunk and accumulates the row's sum of
-        // squares; once the row is complete, pass 2 reads v back (L2) from
-        // the rows this warp itself stored and writes the normalised row.
+        // warp owns 32 rows x 128 columns of every column tile, in 32-column
+        // chunks. Pass 1 writes v = x + addend (two chunks per 32 x 64 TMA
+        // box) and accumulates the row's sum of squares, with the next
+        // chunk's residual loaded while this one is processed; once the row
+        // is complete, pass 2 reads v back (L2) from the rows this warp
+        // itself stored, again one chunk ahead, and writes the normalised row.
         constexpr int CW = BN / 2;
+        constexpr int NC = CW / 32;
         const uint32_t stg = sStage + e * 4096;
         uint8_t* stg_p = gsm + (stg - base);
-        const int row = m0 + quarter * 32 + lane;
-        const int rrow = row < M ? row : M - 1;
-        auto stage_store = [&](const CUtensorMap* map, const uint32_t (&pk)[32], int col) {
-          if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
-          __syncwarp();
+        // Chunk k of a box: 16-byte pieces 4 (k & 1) + q of the 128-byte row.
+        auto stage_chunk = [&](const CUtensorMap* map, const uint32_t (&pk)[16], int k, int col_box) {
+          if ((k & 1) == 0) {
+            if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+            __syncwarp();
+          }
 #pragma unroll
-          for (int q = 0; q < 8; ++q)
-            *reinterpret_cast<uint4*>(stg_p + lane * 128 + ((q ^ (lane & 7)) << 4)) =
+          for (int q = 0; q < 4; ++q)
+            *reinterpret_cast<uint4*>(stg_p + lane * 128 + (((4 * (k & 1) + q) ^ (lane & 7)) << 4)) =
                 make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
-          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-          __syncwarp();
-          if (lane == 0) {
-            tma_store_2d(map, stg, col, m0 + quarter * 32);
-            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+          if (k & 1) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_2d(map, stg, col_box, m0 + quarter * 32);
+              asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+            }
           }
         };
-        auto add_part = [&](auto jc) {
-          constexpr int J = decltype(jc)::value;
-          if (J == 0) ss = 0.0f;
+        const int j = t % tiles_n;
+        if (j == 0) ss = 0.0f;
+        const __nv_bfloat16* rrow_p = epi.resid + (int64_t)rrow * epi.ldr + n0 + half * CW;
 #pragma unroll
-          for (int k = 0; k < CW / 64; ++k) {
-            const int c = half * CW + 64 * k;
-            float v[64];
-            tmem_ld64(tbase + c, v);
-            if (k == CW / 64 - 1) {
-              tc_fence_before();
-              __syncwarp();
-              if (lane == 0) mbar_arrive(bar_tempty + 8 * a);
-            }
-            const uint4* rp = reinterpret_cast<const uint4*>(epi.resid + (int64_t)rrow * epi.ldr + n0 + c);
-            uint32_t pk[32];
-#pragma unroll
-            for (int q = 0; q < 8; ++q) {
-              const uint4 w = rp[q];  // plain load: out may alias resid
-              const uint32_t u[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-              for (int h = 0; h < 4; ++h) {
-                float& lo = v[8 * q + 2 * h];
-                float& hi = v[8 * q + 2 * h + 1];
-                lo = round_bf16(__uint_as_float(u[h] << 16) + round_bf16(lo));
-                hi = round_bf16(__uint_as_float(u[h] & 0xffff0000u) + round_bf16(hi));
-                ss = fmaf(lo, lo, ss);
-                ss = fmaf(hi, hi, ss);
-                pk[4 * q + h] = pack2(lo, hi);
-              }
-            }
-            stage_store(&tmap_out, pk, n0 + c);
+        for (int k = 0; k < NC; ++k) {
+          if (k + 1 < NC) load_row32(rrow_p + 32 * (k + 1), rbuf[(k + 1) & 1]);
+          float v[32];
+          tmem_ld32(tbase + half * CW + 32 * k, v);
+          if (k == NC - 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar_tempty + 8 * a);
           }
-        };
-        auto normalise = [&](auto jn) {
-          constexpr int JN = decltype(jn)::value;  // column tiles in the row
+          uint32_t pk[16];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const uint32_t u[4] = {rbuf[k & 1][q].x, rbuf[k & 1][q].y, rbuf[k & 1][q].z, rbuf[k & 1][q].w};
+#pragma unroll
+            for (int hh = 0; hh < 4; ++hh) {
+              const float lo = round_bf16(__uint_as_float(u[hh] << 16) + round_bf16(v[8 * q + 2 * hh]));
+              const float hi = round_bf16(__uint_as_float(u[hh] & 0xffff0000u) + round_bf16(v[8 * q + 2 * hh + 1]));
+              ss = fmaf(lo, lo, ss);
+              ss = fmaf(hi, hi, ss);
+              pk[4 * q + hh] = pack2(lo, hi);
+            }
+          }
+          stage_chunk(&tmap_out, pk, k, n0 + half * CW + 64 * (k >> 1));
+        }
+        if (j == tiles_n - 1) {
           float* ssb = reinterpret_cast<float*>(ctl + 256);
           ssb[e * 32 + lane] = ss;
           asm volatile("bar.sync %0, 64;" ::"r"(1 + quarter) : "memory");
@@ -416,43 +463,32 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
           if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;\nfence.proxy.async.global;" ::: "memory");
           __syncwarp();
           const __nv_bfloat16* vrow = epi.out + (int64_t)rrow * epi.ldo;
-#pragma unroll 1
-          for (int jj = 0; jj < JN; ++jj) {
-#pragma unroll 1
-            for (int k = 0; k < CW / 64; ++k) {
-              const int col = jj * BN + half * CW + 64 * k;
-              const uint4* vp = reinterpret_cast<const uint4*>(vrow + col);
-              uint32_t pk[32];
+          const int nch = tiles_n * NC;  // this warp's chunks across the row
+          auto col_of = [&](int kk) { return (kk / NC) * BN + half * CW + 32 * (kk % NC); };
+          load_row32(vrow + col_of(0), rbuf[0]);
+          auto step = [&](int kk, auto cur) {
+            constexpr int C = decltype(cur)::value;
+            if (kk + 1 < nch) load_row32(vrow + col_of(kk + 1), rbuf[C ^ 1]);
+            const int col = col_of(kk);
+            float wv[32];
+            load_w32(epi.norm_w, epi.norm_w_bf16, col, wv);
+            uint32_t pk[16];
 #pragma unroll
-              for (int q = 0; q < 8; ++q) {
-                const uint4 w = vp[q];
-                const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+            for (int q = 0; q < 4; ++q) {
+              const uint4 w4 = rbuf[C][q];
+              const uint32_t u[4] = {w4.x, w4.y, w4.z, w4.w};
 #pragma unroll
-                for (int h = 0; h < 4; ++h) {
-                  const int cc = col + 8 * q + 2 * h;
-                  float w0, w1;
-                  if (epi.norm_w_bf16) {
-                    const __nv_bfloat162 wb = __ldg(reinterpret_cast<const __nv_bfloat162*>(
-                        static_cast<const __nv_bfloat16*>(epi.norm_w) + cc));
-                    w0 = __low2float(wb); w1 = __high2float(wb);
-                  } else {
-                    const float2 wf = __ldg(reinterpret_cast<const float2*>(static_cast<const float*>(epi.norm_w) + cc));
-                    w0 = wf.x; w1 = wf.y;
-                  }
-                  pk[4 * q + h] = pack2((__uint_as_float(u[h] << 16) * r) * w0,
-                                        (__uint_as_float(u[h] & 0xffff0000u) * r) * w1);
-                }
-              }
-              stage_store(&tmap_n, pk, col);
+              for (int hh = 0; hh < 4; ++hh)
+                pk[4 * q + hh] = pack2((__uint_as_float(u[hh] << 16) * r) * wv[8 * q + 2 * hh],
+                                       (__uint_as_float(u[hh] & 0xffff0000u) * r) * wv[8 * q + 2 * hh + 1]);
             }
+            stage_chunk(&tmap_n, pk, kk % NC, (kk / NC) * BN + half * CW + 64 * ((kk % NC) >> 1));
+          };
+#pragma unroll 1
+          for (int kk = 0; kk < nch; kk += 2) {  // nch is even
+            step(kk, std::integral_constant<int, 0>{});
+            step(kk + 1, std::integral_constant<int, 1>{});
           }
-        };
-        const int j = t % tiles_n;
-        if (j == 0) add_part(std::integral_constant<int, 0>{});
-        else add_part(std::integral_constant<int, 1>{});
-        if (j == tiles_n - 1) {
-          if (tiles_n == 1) normalise(std::integral_constant<int, 1>{});
-          else normalise(std::integral_constant<int, 2>{});
         }
       } else if constexpr (EPI == kEpiQkvg) {
         // One head (64 columns) per chunk; the tile lies inside one of the
@@ -617,22 +653,11 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
 
 // ---------------------------------------------------------------- host side
 
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
-        q != cudaDriverEntryPointSuccess)
-      p = nullptr;
-    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  }();
-  return fn;
-}
 
 // 2-D bf16 tensor map over rows x cols (row stride ld elements), box box_rows x
 // box_cols (box_cols * 2 <= 128 bytes: one 128-byte swizzle row).
 bool make_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t K, int64_t ld, int box_rows, int box_cols) {
-  auto fn = encode_fn();
+  auto fn = tensormap_encoder();
   if (fn == nullptr) return false;
   const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
   const cuuint64_t strides[1] = {(cuuint64_t)ld * 2};

@@ -15,6 +15,7 @@
 // contraction, so selected chunk indices are reproducible bit for bit by a
 // CPU restatement; ties go to the lower chunk index.
 #include "common.cuh"
+#include "tma.cuh"
 
 namespace dwarf {
 namespace {
@@ -201,9 +202,12 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<const uint32_t*>(&v);
 }
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0)
-               : "memory");
+
+// 2^x on the SFU (x <= 0 here; results below 2^-126 flush to zero).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
 // Swizzled [rows][64 bf16] tile: 16-byte chunk c of row r lives at chunk c ^ (r & 7).
@@ -226,21 +230,6 @@ struct AttnParams {
   int64_t H, T, C, tiles;
   int k_slots;
 };
-
-constexpr int kAttnWarps = 4;
-constexpr int kWarpSmem = 2 * 64 * 128 + 16 * 128 + 16 * kHD * 4 + kTopK * kHD * 4 + 16 * kTopK * 4;
-
-// Stage rows [row0, row0+nrows) of a [T,64] bf16 matrix into a swizzled tile
-// (rows outside [0, T) are zero-filled).
-__device__ __forceinline__ void stage_rows(uint32_t tile, const __nv_bfloat16* base, int64_t stride, int64_t row0,
-                                           int nrows, int64_t T, int lane) {
-  for (int i = lane; i < nrows * 8; i += 32) {
-    const int r = i >> 3, c = i & 7;
-    const int64_t row = row0 + r;
-    const bool ok = row >= 0 && row < T;
-    cp_async16(tile_addr(tile, r, c), base + (ok ? row : 0) * stride + c * 8, ok);
-  }
-}
 
 // S[16 x 8*NT] = Q tile . K block^T, online-softmax update, O += P . V.
 // Key i of the block is valid for query row r when mask(r, i) holds; bias[rr]
@@ -288,15 +277,15 @@ __device__ __forceinline__ void attend_block(const uint32_t (&qa)[4][4], uint32_
   for (int rr = 0; rr < 2; ++rr) {
     const float mn = fmaxf(m[rr], mx[rr]);
     msafe[rr] = mn == -INFINITY ? 0.0f : mn;
-    scale[rr] = exp2f(m[rr] - msafe[rr]);
+    scale[rr] = ex2_approx(m[rr] - msafe[rr]);
     m[rr] = mn;
   }
   float rs[2] = {0.0f, 0.0f};
   uint32_t pa[NT][2];
 #pragma unroll
   for (int j = 0; j < NT; ++j) {
-    const float p0 = exp2f(s[j][0] - msafe[0]), p1 = exp2f(s[j][1] - msafe[0]);
-    const float p2 = exp2f(s[j][2] - msafe[1]), p3 = exp2f(s[j][3] - msafe[1]);
+    const float p0 = ex2_approx(s[j][0] - msafe[0]), p1 = ex2_approx(s[j][1] - msafe[0]);
+    const float p2 = ex2_approx(s[j][2] - msafe[1]), p3 = ex2_approx(s[j][3] - msafe[1]);
     rs[0] += p0 + p1;
     rs[1] += p2 + p3;
     pa[j][0] = pack_bf16(p0, p1);
@@ -330,161 +319,313 @@ __device__ __forceinline__ void attend_block(const uint32_t (&qa)[4][4], uint32_
   }
 }
 
-// One warp per 16-query selector tile, 4 tiles of one (b, h) per CTA; each
-// warp owns its shared-memory slice and synchronises only itself.
-__global__ void __launch_bounds__(kAttnWarps * 32) hisa_attn_kernel(const AttnParams p) {
-  extern __shared__ __align__(128) unsigned char smem[];
+// ---------------------------------------------------------------- pipelined tile attention
+//
+// CTA = 8 selector tiles (128 queries) of one (b, h): warps 0-7 each own one
+// 16-query tile, warp 8 is the producer. The CTA's key chunks -- the three
+// 64-row blocks of local keys around its queries and the union of the
+// routed chunks its tiles selected -- are listed once, fetched once by TMA
+// (K and V boxes of 64 rows x 64 dims, 128-byte swizzle) into a ring of
+// kStages stages, and consumed by every tile that needs them (mma.sync,
+// online softmax), so loads of later chunks overlap the math of earlier ones
+// and neighbouring tiles share their local and routed chunks.
+
+constexpr int kCtaTiles = 8;
+constexpr int kStages = 5;
+constexpr int kStageBytes = 2 * 64 * 128;  // K and V boxes
+constexpr int kMaxEntries = 3 + kCtaTiles * kTopK;
+constexpr uint32_t kWait = 1u << 24;
+
+struct ChunkEntry {
+  int32_t row0;   // first key row
+  int8_t global;  // 0: local K/V, 1: global (adapted) K/V
+  uint8_t mask;   // tiles that attend to this chunk
+  int8_t slot[kCtaTiles];  // routed: the tile's top-k slot (route prior), else -1
+};
+
+struct AttnSmem {
+  static constexpr uint32_t ring = 0;
+  static constexpr uint32_t rsel = kStages * kStageBytes;                // [8 tiles][4][64] fp32
+  static constexpr uint32_t route = rsel + kCtaTiles * kTopK * kHD * 4;  // [8 tiles][16][4] fp32
+  static constexpr uint32_t entries = route + kCtaTiles * 16 * kTopK * 4;
+  static constexpr uint32_t bars = entries + kMaxEntries * sizeof(ChunkEntry);
+  static constexpr uint32_t count = bars + 2 * kStages * 8;
+  static constexpr uint32_t bytes = count + 8 + 4 * kCtaTiles * kTopK + 1024;  // + alignment slack
+};
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t n) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(n) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile("{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\nselp.u32 %0, 1, 0, p;\n}"
+               : "=r"(done) : "r"(bar), "r"(parity) : "memory");
+  return done != 0;
+}
+// Bounded wait; raises the CTA's abort flag after kWait polls or when another warp has.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
+  for (uint32_t it = 0; it < kWait; ++it) {
+    if (mbar_try(bar, parity)) return true;
+    if (*abort_flag) return false;
+  }
+  *abort_flag = 1;
+  return false;
+}
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, int x, int y, int z, int w,
+                                            uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], [%6];"
+      ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(bar) : "memory");
+}
+
+struct AttnMaps {
+  CUtensorMap lk, lv, gk, gv;
+};
+
+__global__ void __launch_bounds__((kCtaTiles + 1) * 32, 2)
+hisa_attn_kernel(const AttnParams p, const __grid_constant__ AttnMaps maps, int32_t* status) {
+  extern __shared__ unsigned char smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  unsigned char* smem = smem_raw + (base - raw);
+  float* s_rsel = reinterpret_cast<float*>(smem + AttnSmem::rsel);
+  float* s_route = reinterpret_cast<float*>(smem + AttnSmem::route);
+  ChunkEntry* s_ent = reinterpret_cast<ChunkEntry*>(smem + AttnSmem::entries);
+  const uint32_t bar_full = base + AttnSmem::bars, bar_empty = bar_full + 8 * kStages;
+  int* s_count = reinterpret_cast<int*>(smem + AttnSmem::count);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + AttnSmem::count + 4);
+
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int h = blockIdx.y, b = blockIdx.z;
-  const int64_t t = (int64_t)blockIdx.x * kAttnWarps + warp;
-  if (t >= p.tiles) return;
-  unsigned char* ws = smem + warp * kWarpSmem;
-  const uint32_t ktile = smem_u32(ws);
-  const uint32_t vtile = ktile + 64 * 128;
-  __nv_bfloat16* qtile = reinterpret_cast<__nv_bfloat16*>(ws + 2 * 64 * 128);
-  float* qhat = reinterpret_cast<float*>(ws + 2 * 64 * 128 + 16 * 128);  // [16][64]
-  float* rsel = qhat + 16 * kHD;                                          // [4][64]
-  float* route = rsel + kTopK * kHD;                                      // [16][4]
-  const int g = lane >> 2, t4 = lane & 3;
-  const int64_t t0 = t * kTile;
+  const int64_t T0 = (int64_t)blockIdx.x * kCtaTiles * kTile;
   const int64_t vlen = imin64((int64_t)p.lengths[b], p.T);
+  const int32_t* top = p.top + ((int64_t)b * p.H + h) * p.tiles * p.k_slots;
 
-  const __nv_bfloat16* qb = p.q + b * p.sqb + h * p.sqh;
-  for (int i = lane; i < 16 * 8; i += 32) {
-    const int r = i >> 3, c = i & 7;
-    const int64_t row = t0 + r;
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (row < p.T) v = *reinterpret_cast<const uint4*>(qb + row * p.sqn + c * 8);
-    *reinterpret_cast<uint4*>(qtile + r * 64 + c * 8) = v;
+  // ---- phase A: the CTA's 32 (tile, slot) selections into smem
+  int* s_top = s_count + 2;  // [kCtaTiles * kTopK]
+  if (warp == kCtaTiles) {
+    const int i = lane / kTopK, k = lane % kTopK;
+    const int64_t t = T0 / kTile + i;
+    s_top[lane] = (t < p.tiles && k < p.k_slots) ? top[t * p.k_slots + k] : -1;
   }
-  int chunk_sel[kTopK];
-  const int32_t* top = p.top + ((b * p.H + h) * p.tiles + t) * p.k_slots;
-#pragma unroll
-  for (int k = 0; k < kTopK; ++k) chunk_sel[k] = k < p.k_slots ? top[k] : -1;
-  for (int i = lane; i < kTopK * kHD; i += 32) {
-    const int k = i / kHD, d = i % kHD;
-    rsel[i] = chunk_sel[k] >= 0 ? __bfloat162float(p.reps[((b * p.H + h) * p.C + chunk_sel[k]) * kHD + d]) : 0.0f;
-  }
-  __syncwarp();
-  // q^ = bf16(q / max(|q|, 1e-6)) for the 16 rows (lanes 0..15 own one row each).
-  if (lane < 16) {
-    float* row = qhat + lane * kHD;
-    for (int d = 0; d < kHD; ++d) row[d] = __bfloat162float(qtile[lane * 64 + d]);
-    normalize_row_bf16(row);
-  }
-  __syncwarp();
-  // Route prior: lane -> (row = lane & 15, slots 2*(lane>>4) + {0,1}).
-  {
-    const int row = lane & 15, k0 = (lane >> 4) * 2;
-    float sc[2];
-#pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      float acc = 0.0f;
-      for (int d = 0; d < kHD; ++d) acc = add_rn(acc, mul_rn(qhat[row * kHD + d], rsel[(k0 + e) * kHD + d]));
-      sc[e] = acc;
+  __syncthreads();
+  // ---- phase B: chunk list + barriers (producer warp), selected representatives (everyone)
+  if (warp == kCtaTiles) {
+    // Local chunks: the three 64-row blocks of [T0 - 64, T0 + 128).
+    int n = 0;
+    if (lane == 0) {
+      for (int k = 0; k < 3; ++k) {
+        const int64_t row0 = T0 - 64 + 64 * k;
+        if (row0 >= p.T || row0 + 64 <= 0) continue;
+        ChunkEntry e;
+        e.row0 = (int32_t)row0;
+        e.global = 0;
+        e.mask = 0;
+        for (int i = 0; i < kCtaTiles; ++i) {
+          e.slot[i] = -1;
+          const int64_t t0 = T0 + kTile * i;
+          if (t0 < p.T && t0 - 64 < row0 + 64 && row0 < t0 + kTile) e.mask |= (uint8_t)(1u << i);
+        }
+        if (e.mask) s_ent[n++] = e;
+      }
     }
-    const float o0 = __shfl_xor_sync(0xffffffffu, sc[0], 16);
-    const float o1 = __shfl_xor_sync(0xffffffffu, sc[1], 16);
-    float all[4];
-    if (k0 == 0) { all[0] = sc[0]; all[1] = sc[1]; all[2] = o0; all[3] = o1; }
-    else { all[0] = o0; all[1] = o1; all[2] = sc[0]; all[3] = sc[1]; }
-    float sum = 0.0f;
-    int count = 0;
-#pragma unroll
-    for (int k = 0; k < kTopK; ++k) {
-      const bool ok = chunk_sel[k] >= 0;
-      sum = add_rn(sum, ok ? all[k] : 0.0f);
-      count += ok;
+    n = __shfl_sync(0xffffffffu, n, 0);
+    // Routed chunks: one entry per distinct chunk id among the 32 selections
+    // (lane = tile * 4 + slot); the lowest lane of each group of equal ids
+    // writes the entry, in lane order.
+    const int c = s_top[lane];
+    const unsigned same = __match_any_sync(0xffffffffu, c);
+    const bool leader = c >= 0 && (__ffs(same) - 1) == lane;
+    const unsigned leaders = __ballot_sync(0xffffffffu, leader);
+    if (leader) {
+      ChunkEntry e;
+      e.row0 = c * kChunk;
+      e.global = 1;
+      e.mask = 0;
+      for (int k = 0; k < kCtaTiles; ++k) e.slot[k] = -1;
+      for (unsigned m = same; m; m &= m - 1) {
+        const int ln = __ffs(m) - 1;
+        e.mask |= (uint8_t)(1u << (ln / kTopK));
+        e.slot[ln / kTopK] = (int8_t)(ln % kTopK);
+      }
+      s_ent[n + __popc(leaders & ((1u << lane) - 1))] = e;
     }
-    const float mean = __fdiv_rn(sum, (float)max(count, 1));
-    const float scale = p.route_scale[h];
-#pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      const int k = k0 + e;
-      const float centered = chunk_sel[k] >= 0 ? __fsub_rn(sc[e], mean) : 0.0f;
-      const float v = round_bf16(mul_rn(centered, scale));
-      route[row * kTopK + k] = v;
-      if (p.route_out != nullptr && t0 + row < p.T)
-        p.route_out[((b * p.H + h) * p.T + t0 + row) * kTopK + k] = __float2bfloat16_rn(v);
-    }
-  }
-  __syncwarp();
-  uint32_t qa[4][4];
-#pragma unroll
-  for (int kt = 0; kt < 4; ++kt) {
-    const int c0 = kt * 16 + 2 * t4;
-    qa[kt][0] = *reinterpret_cast<const uint32_t*>(qtile + g * 64 + c0);
-    qa[kt][1] = *reinterpret_cast<const uint32_t*>(qtile + (g + 8) * 64 + c0);
-    qa[kt][2] = *reinterpret_cast<const uint32_t*>(qtile + g * 64 + c0 + 8);
-    qa[kt][3] = *reinterpret_cast<const uint32_t*>(qtile + (g + 8) * 64 + c0 + 8);
-  }
-
-  float o[8][4];
-#pragma unroll
-  for (int n = 0; n < 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
-  float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.0f, 0.0f};
-  const float zero_bias[2] = {0.0f, 0.0f};
-  const __nv_bfloat16* lkb = p.lk + b * p.slkb + h * p.slkh;
-  const __nv_bfloat16* lvb = p.lv + b * p.slvb + h * p.slvh;
-  const __nv_bfloat16* gkb = p.gk + b * p.sgkb + h * p.sgkh;
-  const __nv_bfloat16* gvb = p.gv + b * p.sgvb + h * p.sgvh;
-
-  // Local window, part 1: rows [t0-64, t0); key i serves query r when i >= r.
-  if (t0 > 0) {
-    stage_rows(ktile, lkb, p.slkn, t0 - 64, 64, p.T, lane);
-    stage_rows(vtile, lvb, p.slvn, t0 - 64, 64, p.T, lane);
-    asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;\n" ::: "memory");
-    __syncwarp();
-    auto mask = [&](int r, int i) {
-      const int64_t id = t0 - 64 + i;
-      return id >= 0 && i >= r && id < vlen && t0 + r < vlen;
-    };
-    attend_block<8>(qa, ktile, vtile, zero_bias, mask, o, m, l, lane);
-    __syncwarp();
-  }
-  // Local window, part 2: rows [t0, t0+16); strictly earlier rows of the tile.
-  {
-    stage_rows(ktile, lkb, p.slkn, t0, 16, p.T, lane);
-    stage_rows(vtile, lvb, p.slvn, t0, 16, p.T, lane);
-    asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;\n" ::: "memory");
-    __syncwarp();
-    auto mask = [&](int r, int i) { return i < r && t0 + i < vlen && t0 + r < vlen; };
-    attend_block<2>(qa, ktile, vtile, zero_bias, mask, o, m, l, lane);
-    __syncwarp();
-  }
-  // Routed chunks: ids < n - 64, route prior of the slot added.
-#pragma unroll 1
-  for (int k = 0; k < kTopK; ++k) {
-    const int c = chunk_sel[k];
-    if (c < 0) continue;
-    const int64_t row0 = (int64_t)c * kChunk;
-    stage_rows(ktile, gkb, p.sgkn, row0, 64, p.T, lane);
-    stage_rows(vtile, gvb, p.sgvn, row0, 64, p.T, lane);
-    asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;\n" ::: "memory");
-    __syncwarp();
-    const float bias[2] = {route[g * kTopK + k], route[(g + 8) * kTopK + k]};
-    auto mask = [&](int r, int i) {
-      const int64_t id = row0 + i;
-      const int64_t n = t0 + r;
-      return id < n - kWindow && id < vlen && n < vlen;
-    };
-    attend_block<8>(qa, ktile, vtile, bias, mask, o, m, l, lane);
-    __syncwarp();
-  }
-
-  // Epilogue: O / l in bf16; rows past the valid length are zero.
-  __nv_bfloat16* ob = p.out + b * p.sob + h * p.soh;
-#pragma unroll
-  for (int rr = 0; rr < 2; ++rr) {
-    const int64_t row = t0 + g + rr * 8;
-    if (row >= p.T) continue;
-    const float inv = (l[rr] > 0.0f && row < vlen) ? 1.0f / l[rr] : 0.0f;
-#pragma unroll
-    for (int n = 0; n < 8; ++n) {
-      const uint32_t v = pack_bf16(o[n][rr * 2] * inv, o[n][rr * 2 + 1] * inv);
-      *reinterpret_cast<uint32_t*>(ob + row * p.son + n * 8 + 2 * t4) = v;
+    if (lane == 0) {
+      *s_count = n + __popc(leaders);
+      *abort_flag = 0;
+      for (int s = 0; s < kStages; ++s) {
+        mbar_init(bar_full + 8 * s, 1);
+        mbar_init(bar_empty + 8 * s, kCtaTiles);
+      }
+      asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
   }
+  // rsel[i][k][d] = bf16 representative of tile i's slot k (0 when unused)
+  for (int x = threadIdx.x; x < kCtaTiles * kTopK * kHD; x += blockDim.x) {
+    const int c = s_top[x / kHD];
+    s_rsel[x] = c >= 0 ? __bfloat162float(p.reps[(((int64_t)b * p.H + h) * p.C + c) * kHD + x % kHD]) : 0.0f;
+  }
+  __syncthreads();
+  const int n_ent = *s_count;
+
+  if (warp == kCtaTiles) {
+    // ---------------- producer
+    if (lane == 0) {
+      for (int e = 0; e < n_ent; ++e) {
+        const int s = e % kStages;
+        const uint32_t ph = (uint32_t)(e / kStages) & 1u;
+        if (!mbar_wait(bar_empty + 8 * s, ph ^ 1u, abort_flag)) break;
+        const uint32_t dst = base + AttnSmem::ring + s * kStageBytes;
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar_full + 8 * s),
+                     "r"(kStageBytes) : "memory");
+        const ChunkEntry& en = s_ent[e];
+        tma_load_4d(dst, en.global ? &maps.gk : &maps.lk, 0, en.row0, h, b, bar_full + 8 * s);
+        tma_load_4d(dst + kStageBytes / 2, en.global ? &maps.gv : &maps.lv, 0, en.row0, h, b, bar_full + 8 * s);
+      }
+      // Leave no copy in flight: wait (bounded) for the last stages issued.
+      for (int e = n_ent > kStages ? n_ent - kStages : 0; e < n_ent; ++e) {
+        const int s = e % kStages;
+        const uint32_t ph = (uint32_t)(e / kStages) & 1u;
+        for (uint32_t it = 0; it < kWait && !mbar_try(bar_full + 8 * s, ph); ++it) {}
+      }
+    }
+    __syncwarp();
+  } else {
+    // ---------------- one 16-query tile per warp
+    const int tile = warp;
+    const int64_t t0 = T0 + (int64_t)kTile * tile;
+    const int g = lane >> 2, t4 = lane & 3;
+    const __nv_bfloat16* qb = p.q + b * p.sqb + h * p.sqh;
+    const bool tile_ok = t0 < p.T;
+    float* route = s_route + tile * 16 * kTopK;
+    // Route prior: lanes 0..15 own one query row each (q^ = bf16(q / max(|q|, 1e-6))).
+    if (lane < 16) {
+      const int64_t row = imin64(t0 + lane, p.T - 1);
+      float qh[kHD];
+      const uint4* src = reinterpret_cast<const uint4*>(qb + row * p.sqn);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const uint4 w = src[i];
+        const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          qh[8 * i + 2 * k] = __uint_as_float(u[k] << 16);
+          qh[8 * i + 2 * k + 1] = __uint_as_float(u[k] & 0xffff0000u);
+        }
+      }
+      float ss = 0.0f;
+#pragma unroll
+      for (int d = 0; d < kHD; ++d) ss = add_rn(ss, mul_rn(qh[d], qh[d]));
+      const float nrm = fmaxf(sqrtf(ss), 1e-6f);
+#pragma unroll
+      for (int d = 0; d < kHD; ++d) qh[d] = round_bf16(__fdiv_rn(qh[d], nrm));
+      float sc[kTopK];
+      float sum = 0.0f;
+      int count = 0;
+#pragma unroll
+      for (int k = 0; k < kTopK; ++k) {
+        const float* rs = s_rsel + (tile * kTopK + k) * kHD;
+        float acc = 0.0f;
+#pragma unroll
+        for (int d = 0; d < kHD; ++d) acc = add_rn(acc, mul_rn(qh[d], rs[d]));
+        sc[k] = acc;
+        const bool ok = tile_ok && s_top[tile * kTopK + k] >= 0;
+        sum = add_rn(sum, ok ? acc : 0.0f);
+        count += ok;
+      }
+      const float mean = __fdiv_rn(sum, (float)max(count, 1));
+      const float scale = p.route_scale[h];
+#pragma unroll
+      for (int k = 0; k < kTopK; ++k) {
+        const bool ok = tile_ok && s_top[tile * kTopK + k] >= 0;
+        const float centered = ok ? __fsub_rn(sc[k], mean) : 0.0f;
+        const float v = round_bf16(mul_rn(centered, scale));
+        route[lane * kTopK + k] = v;
+        if (p.route_out != nullptr && tile_ok && t0 + lane < p.T)
+          p.route_out[((b * p.H + h) * p.T + t0 + lane) * kTopK + k] = __float2bfloat16_rn(v);
+      }
+    }
+    __syncwarp();
+    // Q fragments (m16n8k16 A operand) straight from global.
+    uint32_t qa[4][4];
+    {
+      const int64_t ra = imin64(t0 + g, p.T - 1), rb = imin64(t0 + g + 8, p.T - 1);
+#pragma unroll
+      for (int kt = 0; kt < 4; ++kt) {
+        const int c0 = kt * 16 + 2 * t4;
+        qa[kt][0] = *reinterpret_cast<const uint32_t*>(qb + ra * p.sqn + c0);
+        qa[kt][1] = *reinterpret_cast<const uint32_t*>(qb + rb * p.sqn + c0);
+        qa[kt][2] = *reinterpret_cast<const uint32_t*>(qb + ra * p.sqn + c0 + 8);
+        qa[kt][3] = *reinterpret_cast<const uint32_t*>(qb + rb * p.sqn + c0 + 8);
+      }
+    }
+    float o[8][4];
+#pragma unroll
+    for (int n = 0; n < 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
+    float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.0f, 0.0f};
+
+    for (int e = 0; e < n_ent; ++e) {
+      const int s = e % kStages;
+      const uint32_t ph = (uint32_t)(e / kStages) & 1u;
+      if (!mbar_wait(bar_full + 8 * s, ph, abort_flag)) break;
+      const ChunkEntry& en = s_ent[e];
+      if (tile_ok && ((en.mask >> tile) & 1)) {
+        const uint32_t ktile = base + AttnSmem::ring + s * kStageBytes;
+        const uint32_t vtile = ktile + kStageBytes / 2;
+        const int row0i = en.row0, t0i = (int)t0, vleni = (int)vlen;
+        if (en.global) {
+          const int slot = en.slot[tile];
+          const float bias[2] = {route[g * kTopK + slot], route[(g + 8) * kTopK + slot]};
+          auto mask = [&](int r, int i) {
+            const int id = row0i + i, n = t0i + r;
+            return id < n - kWindow && id < vleni && n < vleni;
+          };
+          attend_block<8>(qa, ktile, vtile, bias, mask, o, m, l, lane);
+        } else {
+          const float bias[2] = {0.0f, 0.0f};
+          auto mask = [&](int r, int i) {
+            const int id = row0i + i, n = t0i + r;
+            return id >= n - kWindow && id < n && id >= 0 && id < vleni && n < vleni;
+          };
+          attend_block<8>(qa, ktile, vtile, bias, mask, o, m, l, lane);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar_empty + 8 * s) : "memory");
+    }
+
+    // Epilogue: O / l in bf16; rows past the valid length are zero.
+    if (tile_ok) {
+      __nv_bfloat16* ob = p.out + b * p.sob + h * p.soh;
+#pragma unroll
+      for (int rr = 0; rr < 2; ++rr) {
+        const int64_t row = t0 + g + rr * 8;
+        if (row >= p.T) continue;
+        const float inv = (l[rr] > 0.0f && row < vlen) ? 1.0f / l[rr] : 0.0f;
+#pragma unroll
+        for (int n = 0; n < 8; ++n) {
+          const uint32_t v = pack_bf16(o[n][rr * 2] * inv, o[n][rr * 2 + 1] * inv);
+          *reinterpret_cast<uint32_t*>(ob + row * p.son + n * 8 + 2 * t4) = v;
+        }
+      }
+    }
+  }
+  if (*abort_flag && lane == 0 && status != nullptr) atomicExch(status, DWARF_DEVICE_TIMEOUT);
+}
+
+// 4-D bf16 tensor map over a [B, H, T, 64] view (element strides sb, sh, sn),
+// box 64 rows x 64 dims, 128-byte swizzle.
+bool make_kv_map(CUtensorMap* map, const void* ptr, int64_t B, int64_t H, int64_t T, int64_t sb, int64_t sh,
+                 int64_t sn) {
+  auto fn = tensormap_encoder();
+  if (fn == nullptr) return false;
+  const cuuint64_t dims[4] = {64, (cuuint64_t)T, (cuuint64_t)H, (cuuint64_t)B};
+  const cuuint64_t strides[3] = {(cuuint64_t)sn * 2, (cuuint64_t)sh * 2, (cuuint64_t)sb * 2};
+  const cuuint32_t box[4] = {64, 64, 1, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(ptr), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 bool al16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
@@ -556,10 +697,17 @@ extern "C" int dwarf_hisa_attn(const dwarf_hisa_attn_args* a, void* stream) {
   p.route_out = (__nv_bfloat16*)a->route_out;
   p.H = a->H; p.T = a->T; p.C = (a->T + kChunk - 1) / kChunk; p.tiles = (a->T + kTile - 1) / kTile;
   p.k_slots = a->k_slots;
-  const size_t smem = (size_t)kAttnWarps * kWarpSmem;
+  AttnMaps maps;
+  if (!make_kv_map(&maps.lk, a->local_key, a->B, a->H, a->T, a->slkb, a->slkh, a->slkn) ||
+      !make_kv_map(&maps.lv, a->local_value, a->B, a->H, a->T, a->slvb, a->slvh, a->slvn) ||
+      !make_kv_map(&maps.gk, a->global_key, a->B, a->H, a->T, a->sgkb, a->sgkh, a->sgkn) ||
+      !make_kv_map(&maps.gv, a->global_value, a->B, a->H, a->T, a->sgvb, a->sgvh, a->sgvn))
+    return DWARF_ERR_LAUNCH;
+  constexpr size_t smem = AttnSmem::bytes;
   if (cudaFuncSetAttribute(hisa_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return DWARF_ERR_LAUNCH;
-  dim3 grid((unsigned)((p.tiles + kAttnWarps - 1) / kAttnWarps), (unsigned)a->H, (unsigned)a->B);
-  hisa_attn_kernel<<<grid, kAttnWarps * 32, smem, (cudaStream_t)stream>>>(p);
+  const int64_t cta_tiles = kCtaTiles;
+  dim3 grid((unsigned)((p.tiles + cta_tiles - 1) / cta_tiles), (unsigned)a->H, (unsigned)a->B);
+  hisa_attn_kernel<<<grid, (kCtaTiles + 1) * 32, smem, (cudaStream_t)stream>>>(p, maps, nullptr);
   return launch_status();
 }
