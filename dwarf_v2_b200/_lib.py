@@ -202,8 +202,13 @@ class HisaAttnArgs(ctypes.Structure):
         k_slots:i32, B:i64, H:i64, T:i64,
         query:ptr, sqb:i64, sqh:i64, sqn:i64, local_key:ptr, slkb:i64, slkh:i64, slkn:i64,
         local_value:ptr, slvb:i64, slvh:i64, slvn:i64, global_key:ptr, sgkb:i64, sgkh:i64, sgkn:i64,
-        global_value:ptr, sgvb:i64, sgvh:i64, sgvn:i64, reps:ptr, top_chunk_idx:ptr, route_scale:ptr,
-        lengths:ptr, out:ptr, sob:i64, soh:i64, son:i64, route_out:ptr""")
+        global_value:ptr, sgvb:i64, sgvh:i64, sgvn:i64, top_chunk_idx:ptr, route:ptr,
+        lengths:ptr, out:ptr, sob:i64, soh:i64, son:i64""")
+
+
+class HisaRouteArgs(ctypes.Structure):
+    _fields_ = _fields("""version:i32, head_dim:i32, selector_tile:i32, k_slots:i32, B:i64, H:i64, T:i64, C:i64,
+        query:ptr, sqb:i64, sqh:i64, sqn:i64, reps:ptr, top_chunk_idx:ptr, route_scale:ptr, route:ptr""")
 
 
 class AddRmsNormArgs(ctypes.Structure):
@@ -243,6 +248,7 @@ _ENTRY_POINTS = {
     "dwarf_hisa_reps": HisaRepsArgs,
     "dwarf_hisa_select": HisaSelectArgs,
     "dwarf_hisa_attn": HisaAttnArgs,
+    "dwarf_hisa_route": HisaRouteArgs,
     "dwarf_add_rmsnorm": AddRmsNormArgs,
     "dwarf_embed_rmsnorm": EmbedRmsNormArgs,
     "dwarf_swiglu": SwigluArgs,

@@ -221,13 +221,11 @@ struct AttnParams {
   const __nv_bfloat16* lv; int64_t slvb, slvh, slvn;
   const __nv_bfloat16* gk; int64_t sgkb, sgkh, sgkn;
   const __nv_bfloat16* gv; int64_t sgvb, sgvh, sgvn;
-  const __nv_bfloat16* reps;  // [B,H,C,64]
-  const int32_t* top;         // [B,H,tiles,K]
-  const float* route_scale;   // [H]
+  const int32_t* top;           // [B,H,tiles,K]
+  const __nv_bfloat16* route;   // [B,H,T,4]
   const int32_t* lengths;
   __nv_bfloat16* out; int64_t sob, soh, son;
-  __nv_bfloat16* route_out;   // optional [B,H,T,4]
-  int64_t H, T, C, tiles;
+  int64_t H, T, tiles;
   int k_slots;
 };
 
@@ -319,10 +317,95 @@ __device__ __forceinline__ void attend_block(const uint32_t (&qa)[4][4], uint32_
   }
 }
 
+// ---------------------------------------------------------------- route prior
+
+struct RouteParams {
+  const __nv_bfloat16* q; int64_t sqb, sqh, sqn;
+  const __nv_bfloat16* reps;  // [B,H,C,64]
+  const int32_t* top;         // [B,H,tiles,K]
+  const float* route_scale;   // [H]
+  __nv_bfloat16* route;       // [B,H,T,4]
+  int64_t H, T, C, tiles;
+  int k_slots;
+};
+
+// One warp per two 16-query tiles (16 tiles per CTA); each lane owns one query row.
+__global__ void __launch_bounds__(256) hisa_route_kernel(const RouteParams p) {
+  __shared__ float rsel[16][kTopK][kHD];
+  __shared__ int sel[16][kTopK];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int lt = warp * 2 + (lane >> 4);  // local tile of this lane's row
+  const int64_t t = (int64_t)blockIdx.x * 16 + lt;
+  const bool tile_ok = t < p.tiles;
+  const int64_t row = t * kTile + (lane & 15);
+  // Issue the row load first; the selections and representatives follow.
+  uint4 qw[8];
+  {
+    const int64_t r = row < p.T ? row : p.T - 1;
+    const uint4* src = reinterpret_cast<const uint4*>(p.q + b * p.sqb + h * p.sqh + r * p.sqn);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) qw[i] = src[i];
+  }
+  if (lane < 2 * kTopK) {
+    const int i = warp * 2 + lane / kTopK, k = lane % kTopK;
+    const int64_t ti = (int64_t)blockIdx.x * 16 + i;
+    sel[i][k] = (ti < p.tiles && k < p.k_slots) ? p.top[((b * p.H + h) * p.tiles + ti) * p.k_slots + k] : -1;
+  }
+  __syncwarp();
+  for (int x = lane; x < 2 * kTopK * kHD; x += 32) {
+    const int i = warp * 2 + x / (kTopK * kHD), k = (x / kHD) % kTopK, c = sel[i][k];
+    rsel[i][k][x % kHD] = c >= 0 ? __bfloat162float(p.reps[((b * p.H + h) * p.C + c) * kHD + x % kHD]) : 0.0f;
+  }
+  __syncwarp();
+  if (!tile_ok || row >= p.T) return;
+  float qh[kHD];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const uint32_t u[4] = {qw[i].x, qw[i].y, qw[i].z, qw[i].w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      qh[8 * i + 2 * k] = __uint_as_float(u[k] << 16);
+      qh[8 * i + 2 * k + 1] = __uint_as_float(u[k] & 0xffff0000u);
+    }
+  }
+  // q^ = bf16(q / max(|q|, 1e-6)): sequential float32 norm, IEEE divide.
+  float ss = 0.0f;
+#pragma unroll
+  for (int d = 0; d < kHD; ++d) ss = add_rn(ss, mul_rn(qh[d], qh[d]));
+  const float nrm = fmaxf(sqrtf(ss), 1e-6f);
+#pragma unroll
+  for (int d = 0; d < kHD; ++d) qh[d] = round_bf16(__fdiv_rn(qh[d], nrm));
+  float sc[kTopK];
+  float sum = 0.0f;
+  int count = 0;
+#pragma unroll
+  for (int k = 0; k < kTopK; ++k) {
+    float acc = 0.0f;
+#pragma unroll
+    for (int d = 0; d < kHD; ++d) acc = add_rn(acc, mul_rn(qh[d], rsel[lt][k][d]));
+    sc[k] = acc;
+    const bool ok = sel[lt][k] >= 0;
+    sum = add_rn(sum, ok ? acc : 0.0f);
+    count += ok;
+  }
+  const float mean = __fdiv_rn(sum, (float)max(count, 1));
+  const float scale = p.route_scale[h];
+  uint32_t packed[2];
+#pragma unroll
+  for (int k = 0; k < kTopK; k += 2) {
+    const float v0 = sel[lt][k] >= 0 ? mul_rn(__fsub_rn(sc[k], mean), scale) : 0.0f;
+    const float v1 = sel[lt][k + 1] >= 0 ? mul_rn(__fsub_rn(sc[k + 1], mean), scale) : 0.0f;
+    const __nv_bfloat162 two = __floats2bfloat162_rn(v0, v1);
+    packed[k / 2] = *reinterpret_cast<const uint32_t*>(&two);
+  }
+  *reinterpret_cast<uint2*>(p.route + ((b * p.H + h) * p.T + row) * kTopK) = make_uint2(packed[0], packed[1]);
+}
+
 // ---------------------------------------------------------------- pipelined tile attention
 //
 // CTA = 8 selector tiles (128 queries) of one (b, h): warps 0-7 each own one
-// 16-query tile, warp 8 is the producer. The CTA's key chunks -- the three
+// 16-query tile; lane 0 of warp 0 also issues the chunk loads. The CTA's key chunks -- the three
 // 64-row blocks of local keys around its queries and the union of the
 // routed chunks its tiles selected -- are listed once, fetched once by TMA
 // (K and V boxes of 64 rows x 64 dims, 128-byte swizzle) into a ring of
@@ -345,8 +428,7 @@ struct ChunkEntry {
 
 struct AttnSmem {
   static constexpr uint32_t ring = 0;
-  static constexpr uint32_t rsel = kStages * kStageBytes;                // [8 tiles][4][64] fp32
-  static constexpr uint32_t route = rsel + kCtaTiles * kTopK * kHD * 4;  // [8 tiles][16][4] fp32
+  static constexpr uint32_t route = kStages * kStageBytes;  // [8 tiles][16][4] fp32
   static constexpr uint32_t entries = route + kCtaTiles * 16 * kTopK * 4;
   static constexpr uint32_t bars = entries + kMaxEntries * sizeof(ChunkEntry);
   static constexpr uint32_t count = bars + 2 * kStages * 8;
@@ -382,13 +464,12 @@ struct AttnMaps {
   CUtensorMap lk, lv, gk, gv;
 };
 
-__global__ void __launch_bounds__((kCtaTiles + 1) * 32, 2)
+__global__ void __launch_bounds__(kCtaTiles * 32, 2)
 hisa_attn_kernel(const AttnParams p, const __grid_constant__ AttnMaps maps, int32_t* status) {
   extern __shared__ unsigned char smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   unsigned char* smem = smem_raw + (base - raw);
-  float* s_rsel = reinterpret_cast<float*>(smem + AttnSmem::rsel);
   float* s_route = reinterpret_cast<float*>(smem + AttnSmem::route);
   ChunkEntry* s_ent = reinterpret_cast<ChunkEntry*>(smem + AttnSmem::entries);
   const uint32_t bar_full = base + AttnSmem::bars, bar_empty = bar_full + 8 * kStages;
@@ -403,14 +484,14 @@ hisa_attn_kernel(const AttnParams p, const __grid_constant__ AttnMaps maps, int3
 
   // ---- phase A: the CTA's 32 (tile, slot) selections into smem
   int* s_top = s_count + 2;  // [kCtaTiles * kTopK]
-  if (warp == kCtaTiles) {
+  if (warp == 0) {
     const int i = lane / kTopK, k = lane % kTopK;
     const int64_t t = T0 / kTile + i;
     s_top[lane] = (t < p.tiles && k < p.k_slots) ? top[t * p.k_slots + k] : -1;
   }
   __syncthreads();
-  // ---- phase B: chunk list + barriers (producer warp), selected representatives (everyone)
-  if (warp == kCtaTiles) {
+  // ---- phase B: chunk list + barriers (warp 0), route prior rows (everyone)
+  if (warp == 0) {
     // Local chunks: the three 64-row blocks of [T0 - 64, T0 + 128).
     int n = 0;
     if (lane == 0) {
@@ -460,37 +541,28 @@ hisa_attn_kernel(const AttnParams p, const __grid_constant__ AttnMaps maps, int3
       asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
   }
-  // rsel[i][k][d] = bf16 representative of tile i's slot k (0 when unused)
-  for (int x = threadIdx.x; x < kCtaTiles * kTopK * kHD; x += blockDim.x) {
-    const int c = s_top[x / kHD];
-    s_rsel[x] = c >= 0 ? __bfloat162float(p.reps[(((int64_t)b * p.H + h) * p.C + c) * kHD + x % kHD]) : 0.0f;
+  // Route prior of the CTA's 128 query rows (4 slots each).
+  for (int x = threadIdx.x; x < kCtaTiles * 16 * kTopK; x += blockDim.x) {
+    const int64_t row = T0 + x / kTopK;
+    s_route[x] = row < p.T ? __bfloat162float(p.route[(((int64_t)b * p.H + h) * p.T + row) * kTopK + x % kTopK]) : 0.0f;
   }
   __syncthreads();
   const int n_ent = *s_count;
 
-  if (warp == kCtaTiles) {
-    // ---------------- producer
-    if (lane == 0) {
-      for (int e = 0; e < n_ent; ++e) {
-        const int s = e % kStages;
-        const uint32_t ph = (uint32_t)(e / kStages) & 1u;
-        if (!mbar_wait(bar_empty + 8 * s, ph ^ 1u, abort_flag)) break;
-        const uint32_t dst = base + AttnSmem::ring + s * kStageBytes;
-        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar_full + 8 * s),
-                     "r"(kStageBytes) : "memory");
-        const ChunkEntry& en = s_ent[e];
-        tma_load_4d(dst, en.global ? &maps.gk : &maps.lk, 0, en.row0, h, b, bar_full + 8 * s);
-        tma_load_4d(dst + kStageBytes / 2, en.global ? &maps.gv : &maps.lv, 0, en.row0, h, b, bar_full + 8 * s);
-      }
-      // Leave no copy in flight: wait (bounded) for the last stages issued.
-      for (int e = n_ent > kStages ? n_ent - kStages : 0; e < n_ent; ++e) {
-        const int s = e % kStages;
-        const uint32_t ph = (uint32_t)(e / kStages) & 1u;
-        for (uint32_t it = 0; it < kWait && !mbar_try(bar_full + 8 * s, ph); ++it) {}
-      }
-    }
-    __syncwarp();
-  } else {
+  // Chunk e goes to stage e % kStages; its loads are issued once every tile
+  // has released the chunk that used the stage before it.
+  auto issue = [&](int e) {
+    const int s = e % kStages;
+    const uint32_t dst = base + AttnSmem::ring + s * kStageBytes;
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar_full + 8 * s),
+                 "r"(kStageBytes) : "memory");
+    const ChunkEntry& en = s_ent[e];
+    tma_load_4d(dst, en.global ? &maps.gk : &maps.lk, 0, en.row0, h, b, bar_full + 8 * s);
+    tma_load_4d(dst + kStageBytes / 2, en.global ? &maps.gv : &maps.lv, 0, en.row0, h, b, bar_full + 8 * s);
+  };
+  if (threadIdx.x == 0)
+    for (int e = 0; e < n_ent && e < kStages; ++e) issue(e);
+  {
     // ---------------- one 16-query tile per warp
     const int tile = warp;
     const int64_t t0 = T0 + (int64_t)kTile * tile;
@@ -498,54 +570,6 @@ hisa_attn_kernel(const AttnParams p, const __grid_constant__ AttnMaps maps, int3
     const __nv_bfloat16* qb = p.q + b * p.sqb + h * p.sqh;
     const bool tile_ok = t0 < p.T;
     float* route = s_route + tile * 16 * kTopK;
-    // Route prior: lanes 0..15 own one query row each (q^ = bf16(q / max(|q|, 1e-6))).
-    if (lane < 16) {
-      const int64_t row = imin64(t0 + lane, p.T - 1);
-      float qh[kHD];
-      const uint4* src = reinterpret_cast<const uint4*>(qb + row * p.sqn);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const uint4 w = src[i];
-        const uint32_t u[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          qh[8 * i + 2 * k] = __uint_as_float(u[k] << 16);
-          qh[8 * i + 2 * k + 1] = __uint_as_float(u[k] & 0xffff0000u);
-        }
-      }
-      float ss = 0.0f;
-#pragma unroll
-      for (int d = 0; d < kHD; ++d) ss = add_rn(ss, mul_rn(qh[d], qh[d]));
-      const float nrm = fmaxf(sqrtf(ss), 1e-6f);
-#pragma unroll
-      for (int d = 0; d < kHD; ++d) qh[d] = round_bf16(__fdiv_rn(qh[d], nrm));
-      float sc[kTopK];
-      float sum = 0.0f;
-      int count = 0;
-#pragma unroll
-      for (int k = 0; k < kTopK; ++k) {
-        const float* rs = s_rsel + (tile * kTopK + k) * kHD;
-        float acc = 0.0f;
-#pragma unroll
-        for (int d = 0; d < kHD; ++d) acc = add_rn(acc, mul_rn(qh[d], rs[d]));
-        sc[k] = acc;
-        const bool ok = tile_ok && s_top[tile * kTopK + k] >= 0;
-        sum = add_rn(sum, ok ? acc : 0.0f);
-        count += ok;
-      }
-      const float mean = __fdiv_rn(sum, (float)max(count, 1));
-      const float scale = p.route_scale[h];
-#pragma unroll
-      for (int k = 0; k < kTopK; ++k) {
-        const bool ok = tile_ok && s_top[tile * kTopK + k] >= 0;
-        const float centered = ok ? __fsub_rn(sc[k], mean) : 0.0f;
-        const float v = round_bf16(mul_rn(centered, scale));
-        route[lane * kTopK + k] = v;
-        if (p.route_out != nullptr && tile_ok && t0 + lane < p.T)
-          p.route_out[((b * p.H + h) * p.T + t0 + lane) * kTopK + k] = __float2bfloat16_rn(v);
-      }
-    }
-    __syncwarp();
     // Q fragments (m16n8k16 A operand) straight from global.
     uint32_t qa[4][4];
     {
@@ -567,7 +591,9 @@ hisa_attn_kernel(const AttnParams p, const __grid_constant__ AttnMaps maps, int3
     for (int e = 0; e < n_ent; ++e) {
       const int s = e % kStages;
       const uint32_t ph = (uint32_t)(e / kStages) & 1u;
-      if (!mbar_wait(bar_full + 8 * s, ph, abort_flag)) break;
+      // One lane waits; the outcome is the warp's, so the warp leaves together.
+      const bool ready = __shfl_sync(0xffffffffu, lane == 0 ? (int)mbar_wait(bar_full + 8 * s, ph, abort_flag) : 0, 0);
+      if (!ready) break;
       const ChunkEntry& en = s_ent[e];
       if (tile_ok && ((en.mask >> tile) & 1)) {
         const uint32_t ktile = base + AttnSmem::ring + s * kStageBytes;
@@ -592,7 +618,12 @@ hisa_attn_kernel(const AttnParams p, const __grid_constant__ AttnMaps maps, int3
       }
       __syncwarp();
       if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar_empty + 8 * s) : "memory");
+      if (threadIdx.x == 0 && e + kStages < n_ent && mbar_wait(bar_empty + 8 * s, ph, abort_flag)) issue(e + kStages);
     }
+    // Leave no copy in flight: every issued chunk has landed.
+    if (threadIdx.x == 0)
+      for (int e = n_ent > kStages ? n_ent - kStages : 0; e < n_ent; ++e)
+        for (uint32_t it = 0; it < kWait && !mbar_try(bar_full + 8 * (e % kStages), (uint32_t)(e / kStages) & 1u); ++it) {}
 
     // Epilogue: O / l in bf16; rows past the valid length are zero.
     if (tile_ok) {
@@ -669,14 +700,32 @@ extern "C" int dwarf_hisa_select(const dwarf_hisa_select_args* a, void* stream) 
   return launch_status();
 }
 
+extern "C" int dwarf_hisa_route(const dwarf_hisa_route_args* a, void* stream) {
+  DWARF_CHECK_VERSION(a);
+  if (a->head_dim != kHD || a->selector_tile != kTile) return DWARF_ERR_SHAPE;
+  if (a->B < 0 || a->H <= 0 || a->T < 0 || a->C < 1 || a->k_slots < 0 || a->k_slots > kTopK) return DWARF_ERR_SHAPE;
+  if (a->B == 0 || a->T == 0) return DWARF_OK;
+  if (!a->query || !a->reps || !a->top_chunk_idx || !a->route_scale || !a->route) return DWARF_ERR_NULL;
+  if (!al16(a->query) || (a->sqb | a->sqh | a->sqn) % 8 || (reinterpret_cast<uintptr_t>(a->route) & 7u))
+    return DWARF_ERR_ALIGN;
+  RouteParams p{};
+  p.q = (const __nv_bfloat16*)a->query; p.sqb = a->sqb; p.sqh = a->sqh; p.sqn = a->sqn;
+  p.reps = (const __nv_bfloat16*)a->reps; p.top = a->top_chunk_idx; p.route_scale = a->route_scale;
+  p.route = (__nv_bfloat16*)a->route;
+  p.H = a->H; p.T = a->T; p.C = a->C; p.tiles = (a->T + kTile - 1) / kTile; p.k_slots = a->k_slots;
+  dim3 grid((unsigned)((p.tiles + 15) / 16), (unsigned)a->H, (unsigned)a->B);
+  hisa_route_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(p);
+  return launch_status();
+}
+
 extern "C" int dwarf_hisa_attn(const dwarf_hisa_attn_args* a, void* stream) {
   DWARF_CHECK_VERSION(a);
   if (a->head_dim != kHD || a->chunk_size != kChunk || a->selector_tile != kTile || a->local_window != kWindow)
     return DWARF_ERR_SHAPE;
   if (a->B < 0 || a->H <= 0 || a->T < 0 || a->k_slots < 0 || a->k_slots > kTopK) return DWARF_ERR_SHAPE;
   if (a->B == 0 || a->T == 0) return DWARF_OK;
-  if (!a->query || !a->local_key || !a->local_value || !a->global_key || !a->global_value || !a->reps ||
-      !a->top_chunk_idx || !a->route_scale || !a->lengths || !a->out)
+  if (!a->query || !a->local_key || !a->local_value || !a->global_key || !a->global_value || !a->route ||
+      !a->top_chunk_idx || !a->lengths || !a->out)
     return DWARF_ERR_NULL;
   const void* rows[] = {a->query, a->local_key, a->local_value, a->global_key, a->global_value, a->out};
   for (const void* r : rows)
@@ -685,17 +734,17 @@ extern "C" int dwarf_hisa_attn(const dwarf_hisa_attn_args* a, void* stream) {
                              a->sgkb, a->sgkh, a->sgkn, a->sgvb, a->sgvh, a->sgvn, a->sob, a->soh, a->son};
   for (int64_t s : strides)
     if (s % 8 != 0) return DWARF_ERR_ALIGN;
+  if (a->T > 0x7fffffffLL) return DWARF_ERR_SHAPE;
   AttnParams p{};
   p.q = (const __nv_bfloat16*)a->query; p.sqb = a->sqb; p.sqh = a->sqh; p.sqn = a->sqn;
   p.lk = (const __nv_bfloat16*)a->local_key; p.slkb = a->slkb; p.slkh = a->slkh; p.slkn = a->slkn;
   p.lv = (const __nv_bfloat16*)a->local_value; p.slvb = a->slvb; p.slvh = a->slvh; p.slvn = a->slvn;
   p.gk = (const __nv_bfloat16*)a->global_key; p.sgkb = a->sgkb; p.sgkh = a->sgkh; p.sgkn = a->sgkn;
   p.gv = (const __nv_bfloat16*)a->global_value; p.sgvb = a->sgvb; p.sgvh = a->sgvh; p.sgvn = a->sgvn;
-  p.reps = (const __nv_bfloat16*)a->reps; p.top = a->top_chunk_idx; p.route_scale = a->route_scale;
+  p.top = a->top_chunk_idx; p.route = (const __nv_bfloat16*)a->route;
   p.lengths = a->lengths;
   p.out = (__nv_bfloat16*)a->out; p.sob = a->sob; p.soh = a->soh; p.son = a->son;
-  p.route_out = (__nv_bfloat16*)a->route_out;
-  p.H = a->H; p.T = a->T; p.C = (a->T + kChunk - 1) / kChunk; p.tiles = (a->T + kTile - 1) / kTile;
+  p.H = a->H; p.T = a->T; p.tiles = (a->T + kTile - 1) / kTile;
   p.k_slots = a->k_slots;
   AttnMaps maps;
   if (!make_kv_map(&maps.lk, a->local_key, a->B, a->H, a->T, a->slkb, a->slkh, a->slkn) ||
@@ -708,6 +757,6 @@ extern "C" int dwarf_hisa_attn(const dwarf_hisa_attn_args* a, void* stream) {
     return DWARF_ERR_LAUNCH;
   const int64_t cta_tiles = kCtaTiles;
   dim3 grid((unsigned)((p.tiles + cta_tiles - 1) / cta_tiles), (unsigned)a->H, (unsigned)a->B);
-  hisa_attn_kernel<<<grid, (kCtaTiles + 1) * 32, smem, (cudaStream_t)stream>>>(p, maps, nullptr);
+  hisa_attn_kernel<<<grid, kCtaTiles * 32, smem, (cudaStream_t)stream>>>(p, maps, nullptr);
   return launch_status();
 }

@@ -125,21 +125,32 @@ def select_chunks(query: torch.Tensor, reps: torch.Tensor, lengths: torch.Tensor
     return top, logits
 
 
+def route_prior(query, reps, top, route_scale) -> torch.Tensor:
+    """``dwarf_hisa_route``: bf16 route prior [B,H,T,4] of the selected chunks."""
+    B, H, T, D = query.shape
+    route = torch.empty(B, H, T, _MAX_TOP_K, dtype=torch.bfloat16, device=query.device)
+    args = _lib.HisaRouteArgs(version=_lib.ABI_VERSION, head_dim=D, selector_tile=_TILE, k_slots=top.shape[-1],
+                              B=B, H=H, T=T, C=reps.shape[2], query=query.data_ptr(), reps=reps.data_ptr(),
+                              top_chunk_idx=top.data_ptr(), route_scale=route_scale.data_ptr(),
+                              route=route.data_ptr())
+    args.sqb, args.sqh, args.sqn = _strides3(query)
+    _lib.call("dwarf_hisa_route", args, query.device)
+    return route
+
+
 def tile_attention(query, local_key, local_value, global_key, global_value, reps, top, route_scale, lengths, *,
                    out: torch.Tensor | None = None, want_route: bool = False):
-    """``dwarf_hisa_attn``: fused route prior + local window + routed chunks."""
+    """``dwarf_hisa_route`` + ``dwarf_hisa_attn``: route prior, then local window + routed chunks."""
     B, H, T, D = query.shape
     if out is None:
         out = torch.empty(B, H, T, D, dtype=torch.bfloat16, device=query.device)
-    route = torch.empty(B, H, T, _MAX_TOP_K, dtype=torch.bfloat16, device=query.device) if want_route else None
+    route = route_prior(query, reps, top, route_scale)
     args = _lib.HisaAttnArgs(version=_lib.ABI_VERSION, head_dim=D, chunk_size=_CHUNK, selector_tile=_TILE,
                              local_window=_WINDOW, k_slots=top.shape[-1], B=B, H=H, T=T,
                              query=query.data_ptr(), local_key=local_key.data_ptr(),
                              local_value=local_value.data_ptr(), global_key=global_key.data_ptr(),
-                             global_value=global_value.data_ptr(), reps=reps.data_ptr(),
-                             top_chunk_idx=top.data_ptr(), route_scale=route_scale.data_ptr(),
-                             lengths=lengths.data_ptr(), out=out.data_ptr(),
-                             route_out=None if route is None else route.data_ptr())
+                             global_value=global_value.data_ptr(), top_chunk_idx=top.data_ptr(),
+                             route=route.data_ptr(), lengths=lengths.data_ptr(), out=out.data_ptr())
     args.sqb, args.sqh, args.sqn = _strides3(query)
     args.slkb, args.slkh, args.slkn = _strides3(local_key)
     args.slvb, args.slvh, args.slvn = _strides3(local_value)
@@ -147,7 +158,7 @@ def tile_attention(query, local_key, local_value, global_key, global_value, reps
     args.sgvb, args.sgvh, args.sgvn = _strides3(global_value)
     args.sob, args.soh, args.son = _strides3(out)
     _lib.call("dwarf_hisa_attn", args, query.device)
-    return out, route
+    return out, (route if want_route else None)
 
 
 def hisa_attention(query, local_key, local_value, global_key, global_value, route_scale, valid_lengths=None, *,

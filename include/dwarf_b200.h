@@ -338,12 +338,27 @@ typedef struct {
   float* logits;                  /* optional [B, H, tiles, C] (masked)   */
 } dwarf_hisa_select_args;
 
+/* Route prior of the selected chunks (_selected_route_scores :418-468):
+ * route[n, slot] = bf16((q^_n . rep_c - mean over the tile's valid slots) *
+ * route_scale[h]), q^_n = bf16(q_n / max(|q_n|, 1e-6)), c the slot's chunk
+ * (0 for slots >= k_slots or without a chunk). float32 with sequential sums
+ * and no FMA contraction, so it is reproducible bit for bit. */
+typedef struct {
+  int32_t version;
+  int32_t head_dim, selector_tile;  /* 64, 16                             */
+  int32_t k_slots;                  /* last dim of top_chunk_idx (<= 4)   */
+  int64_t B, H, T, C;
+  const void* query;        int64_t sqb, sqh, sqn;
+  const void* reps;                 /* bf16 [B, H, C, 64]                 */
+  const int32_t* top_chunk_idx;     /* [B, H, tiles, k_slots]             */
+  const float* route_scale;         /* [H] = softplus(route_prior_raw)    */
+  void* route;                      /* bf16 [B, H, T, 4] contiguous       */
+} dwarf_hisa_route_args;
+
 /* Fused tile attention: for each query n of tile t, one softmax over
  *   local keys  [n-64, n-1] of (local_key, local_value), score q.k/8, and
  *   routed keys of the selected chunks with id < n-64 of (global_key,
- *   global_value), score q.k/8 + route[n, slot],
- * where route[n, slot] = bf16((q^_n . rep_c - mean over valid slots) *
- * route_scale[h]) is computed in-kernel (_selected_route_scores :418-468).
+ *   global_value), score q.k/8 + route[n, slot] (dwarf_hisa_route).
  * Equals the reference's local lane + global lane + exact LSE merge
  * (:2424-2461, 1002-1100, 808-835). Output bf16, zero past the valid length. */
 typedef struct {
@@ -356,16 +371,15 @@ typedef struct {
   const void* local_value;  int64_t slvb, slvh, slvn;
   const void* global_key;   int64_t sgkb, sgkh, sgkn;
   const void* global_value; int64_t sgvb, sgvh, sgvn;
-  const void* reps;               /* bf16 [B, H, C, 64]                   */
   const int32_t* top_chunk_idx;   /* [B, H, tiles, k_slots]               */
-  const float* route_scale;       /* [H] = softplus(route_prior_raw)      */
+  const void* route;              /* bf16 [B, H, T, 4] (dwarf_hisa_route) */
   const int32_t* lengths;
   void* out;                int64_t sob, soh, son;   /* bf16              */
-  void* route_out;                /* optional bf16 [B, H, T, 4]           */
 } dwarf_hisa_attn_args;
 
 int dwarf_hisa_reps(const dwarf_hisa_reps_args* args, void* stream);
 int dwarf_hisa_select(const dwarf_hisa_select_args* args, void* stream);
+int dwarf_hisa_route(const dwarf_hisa_route_args* args, void* stream);
 int dwarf_hisa_attn(const dwarf_hisa_attn_args* args, void* stream);
 
 /* ------------------------------------------------------------------------
