@@ -246,9 +246,10 @@ __device__ __forceinline__ void store16(__nv_bfloat16* dst, const float (&v)[16]
   reinterpret_cast<uint4*>(dst)[1] = w1;
 }
 
-template <int BN>
+template <int BN, int EPI>
 __host__ __device__ constexpr int gemm_stages() {
-  return BN >= 256 ? 4 : 6;
+  // The qkvg+prep epilogue keeps the two [4][64] probe tables in shared memory.
+  return EPI == DWARF_GEMM_QKVG_PREP ? 3 : (BN >= 256 ? 4 : 6);
 }
 template <int BN>
 __host__ __device__ constexpr uint32_t gemm_tmem_cols() {
@@ -262,8 +263,8 @@ template <int BN, int EPI>
 __host__ __device__ constexpr size_t gemm_smem_bytes() {
   // 1 KB alignment slack, stages, staging boxes, barriers (256 B) and the
   // RMSNorm partial sums (8 warps x 32 rows of fp32).
-  return 1024 + (size_t)gemm_stages<BN>() * (kBM * 128 + BN * 128) + gemm_staging_bytes<EPI>() + 256 +
-         (EPI == DWARF_GEMM_RESID_RMSNORM ? 1024 : 0);
+  return 1024 + (size_t)gemm_stages<BN, EPI>() * (kBM * 128 + BN * 128) + gemm_staging_bytes<EPI>() + 256 +
+         (EPI == DWARF_GEMM_RESID_RMSNORM ? 1024 : 0) + (EPI == DWARF_GEMM_QKVG_PREP ? 2048 : 0);
 }
 
 template <int BN, int EPI>
@@ -271,7 +272,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                  const __grid_constant__ CUtensorMap tmap_out, const __grid_constant__ CUtensorMap tmap_n,
                  const int M, const int N, const int K, const GemmEpi epi) {
-  constexpr int S = gemm_stages<BN>();
+  constexpr int S = gemm_stages<BN, EPI>();
   constexpr uint32_t kStageA = kBM * 128, kStageB = BN * 128;
   constexpr uint32_t kTmemCols = gemm_tmem_cols<BN>();
   constexpr uint32_t kIdesc = idesc_bf16(kBM, BN);
@@ -379,6 +380,13 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
     // ---------------- epilogue: warps 2..9. TMEM lane quarter = warp % 4;
     // the two warps of a quarter split the tile's columns.
     const int e = warp - 2, quarter = warp & 3, half = e >> 2;
+    if constexpr (EPI == kEpiQkvg) {
+      float* sp = reinterpret_cast<float*>(ctl + 256);
+      const int et = threadIdx.x - 64;  // 0..255 over the epilogue warps
+      sp[et] = epi.q_probe[et];
+      sp[256 + et] = epi.k_probe[et];
+      asm volatile("bar.sync 5, 256;" ::: "memory");
+    }
     uint32_t tc = 0;
     float ss = 0.0f;  // RMSNorm: running sum of squares of this thread's row slice
     for (int i = 0;; ++i, ++tc) {
@@ -498,6 +506,7 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
         // are packed straight into the q6 cache.
         const int D = epi.heads * 64;
         const int sec = n0 / D;
+        const float* s_probe = reinterpret_cast<const float*>(ctl + 256);  // [2][4][64]: q probes, k probes
         const int row = m0 + quarter * 32 + lane;
         const int b = row / epi.T, tt = row - b * epi.T;
         const uint32_t stg = sStage + e * 4096;
@@ -534,13 +543,13 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
             }
           }
           if (sec <= 1 && row < M) {
-            const float4* pr = reinterpret_cast<const float4*>(sec == 0 ? epi.q_probe : epi.k_probe);
+            const float4* pr = reinterpret_cast<const float4*>(s_probe + sec * 256);
             float ssq = 0.0f, d[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
             for (int i4 = 0; i4 < 16; ++i4) {
 #pragma unroll
               for (int r = 0; r < 4; ++r) {
-                const float4 p4 = __ldg(pr + r * 16 + i4);
+                const float4 p4 = pr[r * 16 + i4];  // shared-memory broadcast
                 d[r] = fmaf(v[4 * i4], p4.x, d[r]);
                 d[r] = fmaf(v[4 * i4 + 1], p4.y, d[r]);
                 d[r] = fmaf(v[4 * i4 + 2], p4.z, d[r]);
@@ -564,7 +573,11 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
             for (int g = 0; g < 4; ++g) {
               uint32_t cc[16];
 #pragma unroll
-              for (int i = 0; i < 16; ++i) cc[i] = (uint32_t)(q6_quantize(v[16 * g + i], qinv) & 63);
+              for (int i = 0; i < 16; ++i) {
+                // clamp(rint(x * inv), -31, 31), as q6_quantize, in integer form
+                const int qv = __float2int_rn(__fmul_rn(v[16 * g + i], qinv));
+                cc[i] = (uint32_t)(min(max(qv, -31), 31) & 63);
+              }
               w[3 * g] = cc[0] | cc[1] << 6 | cc[2] << 12 | cc[3] << 18 | cc[4] << 24 | cc[5] << 30;
               w[3 * g + 1] = cc[5] >> 2 | cc[6] << 4 | cc[7] << 10 | cc[8] << 16 | cc[9] << 22 | cc[10] << 28;
               w[3 * g + 2] = cc[10] >> 4 | cc[11] << 2 | cc[12] << 8 | cc[13] << 14 | cc[14] << 20 | cc[15] << 26;
