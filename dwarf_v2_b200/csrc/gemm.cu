@@ -116,6 +116,46 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
   return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
+// ---- CTA-pair (cluster of 2) helpers
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// shared::cluster address of the same variable in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t map_rank(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+// Arrive on a barrier of another CTA of the cluster (default .release.cta
+// semantics: the signal orders this thread's prior tensor-memory reads, which
+// tcgen05.wait::ld and the tcgen05 fence already completed; a cluster-scope
+// release would also wait for the thread's outstanding global stores).
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+// TMA load into this CTA's shared memory whose bytes complete on the
+// leader's (rank 0) barrier at the same offset.
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+      ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(map_rank(bar, 0)) : "memory");
+}
+__device__ __forceinline__ void tc_mma_pair(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5, %5, %5, %5, %5}, p;\n}"
+      ::"r"(tmem_d), "l"(a), "l"(b), "r"(idesc), "r"(acc), "r"(0u) : "memory");
+}
+// Arrives on the leader's own barrier once the pair's MMAs issued so far are done.
+__device__ __forceinline__ void tc_commit_pair(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_commit(uint32_t bar) {
@@ -246,10 +286,26 @@ __device__ __forceinline__ void store16(__nv_bfloat16* dst, const float (&v)[16]
   reinterpret_cast<uint4*>(dst)[1] = w1;
 }
 
-template <int BN, int EPI>
+// Shared-memory stage of one CTA: A tile [128 x 64] + its part of the B tile
+// (all BN rows alone, BN / 2 rows in a CTA pair).
+template <int BN, int CTAS>
+__host__ __device__ constexpr uint32_t gemm_stage_bytes() {
+  return kBM * 128 + (BN / CTAS) * 128;
+}
+template <int EPI>
+__host__ __device__ constexpr uint32_t gemm_table_bytes() {
+  // RMSNorm partial sums (8 warps x 32 rows fp32) or the qkvg [2][4][64] probe tables.
+  return EPI == DWARF_GEMM_RESID_RMSNORM ? 1024u : (EPI == DWARF_GEMM_QKVG_PREP ? 2048u : 0u);
+}
+template <int BN, int EPI, int CTAS>
 __host__ __device__ constexpr int gemm_stages() {
-  // The qkvg+prep epilogue keeps the two [4][64] probe tables in shared memory.
-  return EPI == DWARF_GEMM_QKVG_PREP ? 3 : (BN >= 256 ? 4 : 6);
+  // As many stages as fit (at most 8) beside the staging boxes, barriers and tables.
+  return (232448u - 1024u - 256u - gemm_table_bytes<EPI>() - (EPI != DWARF_GEMM_SWIGLU ? 8u * 4096u : 0u)) /
+                     gemm_stage_bytes<BN, CTAS>() > 8u
+             ? 8
+             : (int)((232448u - 1024u - 256u - gemm_table_bytes<EPI>() -
+                      (EPI != DWARF_GEMM_SWIGLU ? 8u * 4096u : 0u)) /
+                     gemm_stage_bytes<BN, CTAS>());
 }
 template <int BN>
 __host__ __device__ constexpr uint32_t gemm_tmem_cols() {
@@ -259,23 +315,32 @@ template <int EPI>
 __host__ __device__ constexpr uint32_t gemm_staging_bytes() {
   return EPI != DWARF_GEMM_SWIGLU ? 8 * 4096 : 0;  // one 32 x 64 bf16 box per epilogue warp
 }
-template <int BN, int EPI>
+template <int BN, int EPI, int CTAS>
 __host__ __device__ constexpr size_t gemm_smem_bytes() {
   // 1 KB alignment slack, stages, staging boxes, barriers (256 B) and the
-  // RMSNorm partial sums (8 warps x 32 rows of fp32).
-  return 1024 + (size_t)gemm_stages<BN, EPI>() * (kBM * 128 + BN * 128) + gemm_staging_bytes<EPI>() + 256 +
-         (EPI == DWARF_GEMM_RESID_RMSNORM ? 1024 : 0) + (EPI == DWARF_GEMM_QKVG_PREP ? 2048 : 0);
+  // epilogue tables (RMSNorm partial sums or qkvg probes, at most 2 KB).
+  return 1024 + (size_t)gemm_stages<BN, EPI, CTAS>() * gemm_stage_bytes<BN, CTAS>() + gemm_staging_bytes<EPI>() +
+         256 + gemm_table_bytes<EPI>();
 }
 
-template <int BN, int EPI>
+// CTAS = 2: a CTA pair (cluster of 2) computes 256 x BN tiles with
+// tcgen05.mma.cta_group::2 issued by the even CTA (the leader). Each CTA
+// loads its own 128 rows of A and BN / 2 rows of B; the operand halves stay in
+// their own shared memory and the MMA reads both. The leader's full barriers
+// count both CTAs' TMA bytes (the odd CTA's loads signal the leader's
+// barrier), its commits arrive on the matching barriers of both CTAs, and the
+// odd CTA's epilogue warps release the accumulator on the leader's barrier.
+// No load is multicast: every CTA fetches only the bytes it keeps.
+template <int BN, int EPI, int CTAS>
 __global__ void __launch_bounds__(kGemmThreads, 1)
 gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                  const __grid_constant__ CUtensorMap tmap_out, const __grid_constant__ CUtensorMap tmap_n,
                  const int M, const int N, const int K, const GemmEpi epi) {
-  constexpr int S = gemm_stages<BN, EPI>();
-  constexpr uint32_t kStageA = kBM * 128, kStageB = BN * 128;
+  constexpr int S = gemm_stages<BN, EPI, CTAS>();
+  constexpr uint32_t kStageA = kBM * 128, kStageB = (BN / CTAS) * 128;
   constexpr uint32_t kTmemCols = gemm_tmem_cols<BN>();
-  constexpr uint32_t kIdesc = idesc_bf16(kBM, BN);
+  constexpr uint32_t kIdesc = idesc_bf16(kBM * CTAS, BN);
+  constexpr int kTileM = kBM * CTAS;  // rows per tile (both CTAs)
   extern __shared__ uint8_t gsm_raw[];
   const uint32_t raw = s32(gsm_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;  // 1024-byte aligned swizzle atoms
@@ -290,12 +355,14 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
   constexpr uint32_t kAccStride = kTmemCols / 2;  // accumulator buffer a at column a * kAccStride
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tiles_m = (M + kBM - 1) / kBM, tiles_n = N / BN;
+  const int rank = CTAS == 2 ? (int)cluster_rank() : 0;  // 0 = leader
+  const int group = blockIdx.x / CTAS, groups = gridDim.x / CTAS;
+  const int tiles_m = (M + kTileM - 1) / kTileM, tiles_n = N / BN;
   const int tiles = tiles_m * tiles_n;
-  // i-th tile of this CTA. The RMSNorm epilogue needs whole rows, so there a
-  // CTA owns M blocks and walks their tiles_n column tiles back to back.
+  // i-th tile of this CTA (group). The RMSNorm epilogue needs whole rows, so
+  // there a group owns M blocks and walks their tiles_n column tiles back to back.
   const int sub = EPI == kEpiRmsNorm ? tiles_n : 1;
-  auto tile_at = [&](int i) { return (blockIdx.x + (i / sub) * gridDim.x) * sub + i % sub; };
+  auto tile_at = [&](int i) { return (group + (i / sub) * groups) * sub + i % sub; };
   const int kblocks = (K + kBK - 1) / kBK;
 
   if (threadIdx.x == 0) {
@@ -305,7 +372,7 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(bar_tfull + 8 * a, 1);
-      mbar_init(bar_tempty + 8 * a, 8);  // one arrival per epilogue warp
+      mbar_init(bar_tempty + 8 * a, 8 * CTAS);  // one arrival per epilogue warp of the group
     }
     mbar_init(bar_drain, 1);
     *abort_flag = 0;
@@ -314,42 +381,61 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_b)) : "memory");
   }
   if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(s32(tmem_slot)),
-                 "r"(kTmemCols) : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    if constexpr (CTAS == 2) {
+      asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(s32(tmem_slot)),
+                   "r"(kTmemCols) : "memory");
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    } else {
+      asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(s32(tmem_slot)),
+                   "r"(kTmemCols) : "memory");
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (CTAS == 2) cluster_sync();  // both CTAs' barriers exist before anyone signals them
+  else __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
-    // ---------------- TMA producer
+    // ---------------- TMA producer (both CTAs of a pair)
     if (lane == 0) {
       uint32_t it = 0;
       bool ok = true;
       for (int i = 0; ok; ++i) {
         const int t = tile_at(i);
         if (t >= tiles) break;
-        const int m0 = (t / tiles_n) * kBM, n0 = (t % tiles_n) * BN;
+        const int m0 = (t / tiles_n) * kTileM + kBM * rank, n0 = (t % tiles_n) * BN + (BN / CTAS) * rank;
         for (int kb = 0; kb < kblocks; ++kb, ++it) {
           const uint32_t s = it % S, ph = (it / S) & 1u;
           if (!(ok = mbar_wait(bar_empty + 8 * s, ph ^ 1u, abort_flag))) break;
-          mbar_expect_tx(bar_full + 8 * s, kStageA + kStageB);
-          tma_load_2d(sA + s * kStageA, &tmap_a, kb * kBK, m0, bar_full + 8 * s);
-          tma_load_2d(sB + s * kStageB, &tmap_b, kb * kBK, n0, bar_full + 8 * s);
+          if constexpr (CTAS == 2) {
+            // The MMA commit lands on the leader's empty barrier only; the
+            // leader passes each release on to the odd CTA's barrier.
+            if (rank == 0 && it >= (uint32_t)S) mbar_arrive_cluster(map_rank(bar_empty + 8 * s, 1));
+            // The leader's full barrier expects both CTAs' bytes.
+            if (rank == 0) mbar_expect_tx(bar_full + 8 * s, 2 * (kStageA + kStageB));
+            tma_load_2d_pair(sA + s * kStageA, &tmap_a, kb * kBK, m0, bar_full + 8 * s);
+            tma_load_2d_pair(sB + s * kStageB, &tmap_b, kb * kBK, n0, bar_full + 8 * s);
+          } else {
+            mbar_expect_tx(bar_full + 8 * s, kStageA + kStageB);
+            tma_load_2d(sA + s * kStageA, &tmap_a, kb * kBK, m0, bar_full + 8 * s);
+            tma_load_2d(sB + s * kStageB, &tmap_b, kb * kBK, n0, bar_full + 8 * s);
+          }
         }
       }
-      // Leave no copy in flight: the last S issued stages must have landed.
-      for (uint32_t j = it > (uint32_t)S ? it - S : 0; j < it; ++j) {
-        const uint32_t s = j % S, ph = (j / S) & 1u;
-        for (uint32_t w = 0; w < kWaitLimit && !mbar_try(bar_full + 8 * s, ph); ++w) {}
-      }
+      // Leave no copy in flight: the last S issued stages must have landed
+      // (in a pair the leader's full barriers count the odd CTA's copies too).
+      if (rank == 0)
+        for (uint32_t j = it > (uint32_t)S ? it - S : 0; j < it; ++j) {
+          const uint32_t s = j % S, ph = (j / S) & 1u;
+          for (uint32_t w = 0; w < kWaitLimit && !mbar_try(bar_full + 8 * s, ph); ++w) {}
+        }
     }
     __syncwarp();
   } else if (warp == 1) {
-    // ---------------- MMA issuer
-    if (lane == 0) {
+    // ---------------- MMA issuer (the leader of a pair)
+    if (lane == 0 && rank == 0) {
       uint32_t it = 0, tc = 0;
       bool ok = true;
       for (int i = 0; ok; ++i, ++tc) {
@@ -364,15 +450,22 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
           if (!(ok = mbar_wait(bar_full + 8 * s, ph, abort_flag))) break;
           tc_fence_after();
 #pragma unroll
-          for (int kk = 0; kk < kBK / 16; ++kk)
-            tc_mma(d, smem_desc(sA + s * kStageA + kk * 32), smem_desc(sB + s * kStageB + kk * 32), kIdesc,
-                   (kb | kk) != 0);
-          tc_commit(bar_empty + 8 * s);
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            const uint64_t da = smem_desc(sA + s * kStageA + kk * 32), db = smem_desc(sB + s * kStageB + kk * 32);
+            if constexpr (CTAS == 2) tc_mma_pair(d, da, db, kIdesc, (kb | kk) != 0);
+            else tc_mma(d, da, db, kIdesc, (kb | kk) != 0);
+          }
+          if constexpr (CTAS == 2) tc_commit_pair(bar_empty + 8 * s);
+          else tc_commit(bar_empty + 8 * s);
         }
-        if (ok) tc_commit(bar_tfull + 8 * a);
+        if (ok) {
+          if constexpr (CTAS == 2) tc_commit_pair(bar_tfull + 8 * a);
+          else tc_commit(bar_tfull + 8 * a);
+        }
       }
       // Drain: every MMA issued so far has completed once this commit lands.
-      tc_commit(bar_drain);
+      if constexpr (CTAS == 2) tc_commit_pair(bar_drain);
+      else tc_commit(bar_drain);
       for (uint32_t w = 0; w < kWaitLimit && !mbar_try(bar_drain, 0); ++w) {}
     }
     __syncwarp();
@@ -380,6 +473,11 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
     // ---------------- epilogue: warps 2..9. TMEM lane quarter = warp % 4;
     // the two warps of a quarter split the tile's columns.
     const int e = warp - 2, quarter = warp & 3, half = e >> 2;
+    // Accumulator release: on the leader's barrier (remote for the odd CTA of a pair).
+    auto release_acc = [&](uint32_t bar) {
+      if (CTAS == 2 && rank != 0) mbar_arrive_cluster(map_rank(bar, 0));
+      else mbar_arrive(bar);
+    };
     if constexpr (EPI == kEpiQkvg) {
       float* sp = reinterpret_cast<float*>(ctl + 256);
       const int et = threadIdx.x - 64;  // 0..255 over the epilogue warps
@@ -393,12 +491,14 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
       const int t = tile_at(i);
       if (t >= tiles) break;
       const uint32_t a = tc & 1u, aph = (tc >> 1) & 1u;
-      const int m0 = (t / tiles_n) * kBM, n0 = (t % tiles_n) * BN;
+      const int m0 = (t / tiles_n) * kTileM + kBM * rank, n0 = (t % tiles_n) * BN;
       // RMSNorm: the first residual chunk is loaded before waiting for the accumulator.
       uint4 rbuf[2][4];
       const int rrow = min(m0 + quarter * 32 + lane, M - 1);
       if constexpr (EPI == kEpiRmsNorm) load_row32(epi.resid + (int64_t)rrow * epi.ldr + n0 + half * (BN / 2), rbuf[0]);
       if (!mbar_wait(bar_tfull + 8 * a, aph, abort_flag)) break;
+      // The accumulator-full commit lands on the leader; pass it on to the odd CTA.
+      if (CTAS == 2 && rank == 0 && e == 0 && lane == 0) mbar_arrive_cluster(map_rank(bar_tfull + 8 * a, 1));
       tc_fence_after();
       const uint32_t tbase = tmem + ((uint32_t)(quarter * 32) << 16) + a * kAccStride;
       if constexpr (EPI == kEpiRmsNorm) {
@@ -443,7 +543,7 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
           if (k == NC - 1) {
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(bar_tempty + 8 * a);
+            if (lane == 0) release_acc(bar_tempty + 8 * a);
           }
           uint32_t pk[16];
 #pragma unroll
@@ -520,7 +620,7 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
           if (k == 1) {
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(bar_tempty + 8 * a);
+            if (lane == 0) release_acc(bar_tempty + 8 * a);
           }
           add_bias64(epi.bias, epi.bias_bf16, n0 + c, v);
 #pragma unroll
@@ -602,7 +702,7 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
           if (c + 64 == (half + 1) * CW) {  // last TMEM read of this tile by this warp
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(bar_tempty + 8 * a);
+            if (lane == 0) release_acc(bar_tempty + 8 * a);
           }
           if (epi.bias != nullptr) add_bias64(epi.bias, epi.bias_bf16, n0 + c, v);
           if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
@@ -637,7 +737,7 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
           if (last) {
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(bar_tempty + 8 * a);
+            if (lane == 0) release_acc(bar_tempty + 8 * a);
           }
           if (!have) break;
 #pragma unroll
@@ -656,11 +756,15 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
   }
 
   tc_fence_before();
-  __syncthreads();
+  if constexpr (CTAS == 2) cluster_sync();  // no CTA leaves while its peer may still signal it
+  else __syncthreads();
   if (*abort_flag && threadIdx.x == 0 && epi.status != nullptr) atomicExch(epi.status, DWARF_DEVICE_TIMEOUT);
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+    if constexpr (CTAS == 2)
+      asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+    else
+      asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
   }
 }
 
@@ -691,25 +795,49 @@ int num_sms() {
   return n;
 }
 
-template <int BN, int EPI>
-int launch_gemm(const dwarf_gemm_args* a, const GemmEpi& epi, cudaStream_t stream) {
+template <int BN, int EPI, int CTAS>
+int launch_gemm_impl(const dwarf_gemm_args* a, const GemmEpi& epi, cudaStream_t stream) {
   CUtensorMap ma, mb, mo;
-  if (!make_map(&ma, a->a, a->M, a->K, a->lda, kBM, kBK) || !make_map(&mb, a->b, a->N, a->K, a->ldb, BN, kBK))
+  if (!make_map(&ma, a->a, a->M, a->K, a->lda, kBM, kBK) ||
+      !make_map(&mb, a->b, a->N, a->K, a->ldb, BN / CTAS, kBK))
     return DWARF_ERR_LAUNCH;
   CUtensorMap mn = ma;
-  // Output boxes of 32 rows x 64 columns (epilogues 0 and 2).
+  // Output boxes of 32 rows x 64 columns (epilogues 0, 2 and 3).
   if (EPI != kEpiSwiglu && !make_map(&mo, a->out, a->M, a->N, a->ldo, 32, 64)) return DWARF_ERR_LAUNCH;
   if (EPI == kEpiSwiglu) mo = ma;
   if (EPI == kEpiRmsNorm && !make_map(&mn, a->n_out, a->M, a->N, a->ldn, 32, 64)) return DWARF_ERR_LAUNCH;
-  constexpr size_t smem = gemm_smem_bytes<BN, EPI>();
-  auto kernel = gemm_bf16_kernel<BN, EPI>;
+  constexpr size_t smem = gemm_smem_bytes<BN, EPI, CTAS>();
+  auto kernel = gemm_bf16_kernel<BN, EPI, CTAS>;
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return launch_status();
-  // Work units: tiles, or whole M blocks for the RMSNorm epilogue.
-  const int64_t units = ((a->M + kBM - 1) / kBM) * (EPI == kEpiRmsNorm ? 1 : a->N / BN);
-  const int grid = (int)(units < num_sms() ? units : num_sms());
-  kernel<<<grid, kGemmThreads, smem, stream>>>(ma, mb, mo, mn, (int)a->M, (int)a->N, (int)a->K, epi);
+  // Work units (per CTA group): tiles, or whole M blocks for the RMSNorm epilogue.
+  const int64_t tile_m = (int64_t)kBM * CTAS;
+  const int64_t units = ((a->M + tile_m - 1) / tile_m) * (EPI == kEpiRmsNorm ? 1 : a->N / BN);
+  const int64_t groups_max = num_sms() / CTAS;
+  const int groups = (int)(units < groups_max ? units : groups_max);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(groups * CTAS));
+  cfg.blockDim = dim3(kGemmThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = CTAS;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kernel, ma, mb, mo, mn, (int)a->M, (int)a->N, (int)a->K, epi) != cudaSuccess)
+    return launch_status();
   return launch_status();
+}
+
+// CTA pairs (cta_group::2) unless DWARF_GEMM_CTAS=1 (read on every call).
+template <int BN, int EPI>
+int launch_gemm(const dwarf_gemm_args* a, const GemmEpi& epi, cudaStream_t stream) {
+  const char* e = getenv("DWARF_GEMM_CTAS");
+  if (e != nullptr && e[0] == '1') return launch_gemm_impl<BN, EPI, 1>(a, epi, stream);
+  return launch_gemm_impl<BN, EPI, 2>(a, epi, stream);
 }
 
 bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }

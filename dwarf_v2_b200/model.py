@@ -137,6 +137,14 @@ class SwiGLUFFN(nn.Module):
         h = gemm.linear_swiglu(_act(x), w_il, tile)
         return F.linear(h, _act(self.down.weight))
 
+    def forward_add_rmsnorm(self, x: torch.Tensor, residual: torch.Tensor, norm_weight: torch.Tensor,
+                            eps: float = 1e-6) -> tuple[torch.Tensor, torch.Tensor]:
+        """(residual + ffn(x), RMSNorm of that * norm_weight) with the residual add and the next
+        norm fused into the down projection's epilogue; the residual stream is updated in place."""
+        w_il, tile = self._interleaved()
+        h = gemm.linear_swiglu(_act(x), w_il, tile)
+        return gemm.linear_add_rmsnorm(h, _act(self.down.weight), residual, norm_weight, eps=eps, x_out=residual)
+
 
 class InterferencePacket(nn.Module):
     """Causal EMA packet feeding HISA's global K/V (reference :243-284)."""
@@ -310,10 +318,10 @@ class DwarfForCausalLM(nn.Module):
                 x, n2 = glue.add_rmsnorm(x, block.norm2.weight.detach(), addend=projected, gate=gate)
             else:
                 x, n2 = glue.add_rmsnorm(x, block.norm2.weight.detach(), addend=block.attn(n))
-            x, n = glue.add_rmsnorm(x, next_norm.detach(), addend=block.ffn(n2), x_out=x)
+            x, n = block.ffn.forward_add_rmsnorm(n2, x, next_norm.detach())
         return (n, auxiliary) if return_auxiliary else n
 
     def forward(self, input_ids: torch.Tensor, *, return_hidden: bool = False, return_auxiliary: bool = False):
         hidden, auxiliary = self.forward_hidden(input_ids, return_auxiliary=True)
-        output = hidden if return_hidden else F.linear(hidden, _act(self.embedding.weight.detach()))
+        output = hidden if return_hidden else gemm.linear(hidden, _act(self.embedding.weight.detach()))
         return (output, auxiliary) if return_auxiliary else output
