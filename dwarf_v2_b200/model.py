@@ -121,29 +121,41 @@ class SwiGLUFFN(nn.Module):
         self.down = nn.Linear(hidden, config.embedding_dim, bias=False)
         self.dropout = nn.Dropout(config.dropout)
 
-    def _interleaved(self) -> tuple[torch.Tensor, int]:
-        """up_gate weight in the tile-interleaved order of the fused SwiGLU GEMM (cached per weight version)."""
-        w = self.up_gate.weight
-        key = (w.data_ptr(), w._version, w.device)
-        if getattr(self, "_il_key", None) != key:
-            tile = gemm.swiglu_tile(w.shape[0] // 2)
-            self._il = (gemm.interleave_up_gate(_act(w.detach()), tile), tile)
-            self._il_key = key
-        return self._il
+    def _fused_weights(self) -> tuple[torch.Tensor, torch.Tensor, int]:
+        """Weights of the fused FFN GEMMs, cached per weight version.
+
+        The hidden width is padded to a multiple of 128 with zero up/gate rows
+        and zero down columns (silu(0) * 0 = 0 and zero columns add exact zeros,
+        so results are unchanged), which lets the SwiGLU GEMM use 256-wide tiles
+        (128 up + 128 gate columns); the up_gate rows are tile-interleaved."""
+        w, wd = self.up_gate.weight, self.down.weight
+        key = (w.data_ptr(), w._version, wd.data_ptr(), wd._version, w.device)
+        if getattr(self, "_fw_key", None) != key:
+            hidden = w.shape[0] // 2
+            tile = 128
+            padded = -(-hidden // tile) * tile
+            up, gate = _act(w.detach()).chunk(2, dim=0)
+            pad_rows = up.new_zeros(padded - hidden, up.shape[1])
+            w_ug = torch.cat([up, pad_rows, gate, pad_rows], dim=0)
+            w_down = torch.cat([_act(wd.detach()), wd.new_zeros(wd.shape[0], padded - hidden, dtype=w_ug.dtype)],
+                               dim=1).contiguous()
+            self._fw = (gemm.interleave_up_gate(w_ug, tile), w_down, tile)
+            self._fw_key = key
+        return self._fw
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         """down(silu(gate) * up): the tcgen05 GEMM with the SwiGLU epilogue, then the down projection."""
-        w_il, tile = self._interleaved()
+        w_il, w_down, tile = self._fused_weights()
         h = gemm.linear_swiglu(_act(x), w_il, tile)
-        return F.linear(h, _act(self.down.weight))
+        return gemm.linear(h, w_down)
 
     def forward_add_rmsnorm(self, x: torch.Tensor, residual: torch.Tensor, norm_weight: torch.Tensor,
                             eps: float = 1e-6) -> tuple[torch.Tensor, torch.Tensor]:
         """(residual + ffn(x), RMSNorm of that * norm_weight) with the residual add and the next
         norm fused into the down projection's epilogue; the residual stream is updated in place."""
-        w_il, tile = self._interleaved()
+        w_il, w_down, tile = self._fused_weights()
         h = gemm.linear_swiglu(_act(x), w_il, tile)
-        return gemm.linear_add_rmsnorm(h, _act(self.down.weight), residual, norm_weight, eps=eps, x_out=residual)
+        return gemm.linear_add_rmsnorm(h, w_down, residual, norm_weight, eps=eps, x_out=residual)
 
 
 class InterferencePacket(nn.Module):
