@@ -53,18 +53,25 @@ __device__ __forceinline__ void npci_row(const NpciParams& p, int64_t b, int64_t
 #pragma unroll
   for (int i = 0; i < 4; ++i) xx += x[i] * x[i];
   const float norm = fmaxf(sqrtf(sum16(xx)), 1e-12f);
+  const float inv_norm = 1.0f / norm;
   float u[4], du = 0.f;
 #pragma unroll
-  for (int i = 0; i < 4; ++i) { u[i] = x[i] / norm; du += d[i] * u[i]; }
+  for (int i = 0; i < 4; ++i) { u[i] = x[i] * inv_norm; du += d[i] * u[i]; }
   du = sum16(du);
   float perp[4], pp = 0.f;
 #pragma unroll
   for (int i = 0; i < 4; ++i) { perp[i] = d[i] - du * u[i]; pp += perp[i] * perp[i]; }
   const float pn = sqrtf(sum16(pp));
   const bool active = pn > norm * 1e-7f;
-  const float angle = p.theta[h] * tanhf(pn / (p.tau * norm + 1e-12f));
+  // |angle| <= |theta| (0.25 rad in the DWARF blocks): there the SFU sine and
+  // cosine are accurate to a few 1e-7 absolute; larger angles take sincosf.
+  // tanh (of a non-negative argument) from the SFU exponential.
+  const float z = pn / (p.tau * norm + 1e-12f);
+  const float e2 = __expf(-2.0f * fminf(z, 40.0f));
+  const float angle = p.theta[h] * __fdividef(1.0f - e2, 1.0f + e2);
   float sn, cs;
-  sincosf(angle, &sn, &cs);
+  if (fabsf(angle) < 1.0f) __sincosf(angle, &sn, &cs);
+  else sincosf(angle, &sn, &cs);
   const float inv_pn = 1.0f / fmaxf(pn, 1e-20f);
   if (!active_row) return;
   T* o = static_cast<T*>(p.out) + b * p.sob + h * p.soh + n * p.son + g * 4;
