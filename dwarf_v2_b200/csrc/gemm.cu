@@ -275,6 +275,14 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t sr
                ::"l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(src) : "memory");
 }
 
+// (a0, a1) += (q0, q1) * (x, y) as one packed fp32x2 FMA (sm_100), each lane an IEEE fma.
+__device__ __forceinline__ void fma2v(float& a0, float& a1, float q0, float q1, float x, float y) {
+  asm("{\n.reg .b64 pa, pb, pc;\nmov.b64 pa, {%2, %3};\nmov.b64 pb, {%4, %5};\nmov.b64 pc, {%0, %1};\n"
+      "fma.rn.f32x2 pc, pa, pb, pc;\nmov.b64 {%0, %1}, pc;\n}"
+      : "+f"(a0), "+f"(a1)
+      : "f"(q0), "f"(q1), "f"(x), "f"(y));
+}
+
 __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   const __nv_bfloat162 t = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<const uint32_t*>(&t);
@@ -479,10 +487,13 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
       else mbar_arrive(bar);
     };
     if constexpr (EPI == kEpiQkvg) {
+      // [q | k][probe pair][dim][2]: (p_{2r}[i], p_{2r+1}[i]) adjacent for packed FMAs
       float* sp = reinterpret_cast<float*>(ctl + 256);
       const int et = threadIdx.x - 64;  // 0..255 over the epilogue warps
-      sp[et] = epi.q_probe[et];
-      sp[256 + et] = epi.k_probe[et];
+      const int pr = et >> 6, dim = et & 63;  // probe, dim
+      const int dst = ((pr >> 1) * 64 + dim) * 2 + (pr & 1);
+      sp[dst] = epi.q_probe[et];
+      sp[256 + dst] = epi.k_probe[et];
       asm volatile("bar.sync 5, 256;" ::: "memory");
     }
     uint32_t tc = 0;
@@ -643,18 +654,17 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
             }
           }
           if (sec <= 1 && row < M) {
+            // probes stored as pairs (p0[i], p1[i]), (p2[i], p3[i]): one packed FMA per two probes
             const float4* pr = reinterpret_cast<const float4*>(s_probe + sec * 256);
             float ssq = 0.0f, d[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-            for (int i4 = 0; i4 < 16; ++i4) {
-#pragma unroll
-              for (int r = 0; r < 4; ++r) {
-                const float4 p4 = pr[r * 16 + i4];  // shared-memory broadcast
-                d[r] = fmaf(v[4 * i4], p4.x, d[r]);
-                d[r] = fmaf(v[4 * i4 + 1], p4.y, d[r]);
-                d[r] = fmaf(v[4 * i4 + 2], p4.z, d[r]);
-                d[r] = fmaf(v[4 * i4 + 3], p4.w, d[r]);
-              }
+            for (int i2 = 0; i2 < 32; ++i2) {
+              const float4 p01 = pr[i2];       // (p0[2 i2], p1[2 i2], p0[2 i2 + 1], p1[2 i2 + 1])
+              const float4 p23 = pr[32 + i2];  // same for probes 2, 3
+              fma2v(d[0], d[1], v[2 * i2], v[2 * i2], p01.x, p01.y);
+              fma2v(d[0], d[1], v[2 * i2 + 1], v[2 * i2 + 1], p01.z, p01.w);
+              fma2v(d[2], d[3], v[2 * i2], v[2 * i2], p23.x, p23.y);
+              fma2v(d[2], d[3], v[2 * i2 + 1], v[2 * i2 + 1], p23.z, p23.w);
             }
 #pragma unroll
             for (int i = 0; i < 64; ++i) ssq = fmaf(v[i], v[i], ssq);
@@ -674,9 +684,11 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
               uint32_t cc[16];
 #pragma unroll
               for (int i = 0; i < 16; ++i) {
-                // clamp(rint(x * inv), -31, 31), as q6_quantize, in integer form
-                const int qv = __float2int_rn(__fmul_rn(v[16 * g + i], qinv));
-                cc[i] = (uint32_t)(min(max(qv, -31), 31) & 63);
+                // clamp(rint(x * inv), -31, 31) as q6_quantize (clamping first gives the same
+                // code): adding 1.5 * 2^23 rounds to nearest-even into the low mantissa bits,
+                // whose low six bits are the two's-complement code.
+                const float qf = fminf(fmaxf(__fmul_rn(v[16 * g + i], qinv), -31.0f), 31.0f);
+                cc[i] = __float_as_uint(__fadd_rn(qf, 12582912.0f)) & 63u;
               }
               w[3 * g] = cc[0] | cc[1] << 6 | cc[2] << 12 | cc[3] << 18 | cc[4] << 24 | cc[5] << 30;
               w[3 * g + 1] = cc[5] >> 2 | cc[6] << 4 | cc[7] << 10 | cc[8] << 16 | cc[9] << 22 | cc[10] << 28;
