@@ -177,11 +177,21 @@ class InterferencePacket(nn.Module):
     def ema_factors(self) -> torch.Tensor:
         return bounded_ema_factor(self.ema_raw)
 
+    def _constants(self) -> tuple[torch.Tensor, list[float]]:
+        """EMA factors (device) and the bf16 mixture weights (host floats), recomputed only when
+        ema_raw or mix_logits change, so a forward needs no device-to-host copy (CUDA-graph safe)."""
+        key = (self.ema_raw.data_ptr(), self.ema_raw._version, self.mix_logits.data_ptr(), self.mix_logits._version)
+        if getattr(self, "_const_key", None) != key:
+            with torch.no_grad():
+                factors = self.ema_factors.detach().clone()
+                mixture = torch.softmax(self.mix_logits.detach().float(), dim=0).to(torch.bfloat16).float().tolist()
+            self._const = (factors, mixture)
+            self._const_key = key
+        return self._const
+
     def forward(self, normalized: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
         x = _act(normalized)
-        with torch.no_grad():
-            factors = self.ema_factors.detach()
-            mixture = torch.softmax(self.mix_logits.detach().float(), dim=0).to(torch.bfloat16).float().tolist()
+        factors, mixture = self._constants()
         scans = [causal_ema_scan(x, f.reshape(1)) for f in factors]
         gate_pre = F.linear(x, _act(self.gate_proj.weight), _act(self.gate_proj.bias))
         packet = glue.packet(scans, mixture, gate_pre)
