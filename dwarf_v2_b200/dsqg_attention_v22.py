@@ -609,6 +609,51 @@ class DSQGAttentionV19(nn.Module):
     def centered_scale_embed(self) -> torch.Tensor:
         return self.scale_embed - self.scale_embed.mean(dim=0, keepdim=True)
 
+    def _migrate_legacy_keys(self, state_dict, prefix: str) -> None:
+        """Rewrites, in place, the reference's older checkpoint layouts (dsqg_attention_v22.py:3069-3142).
+
+        * separate ``qkv_proj`` / ``gate_proj`` weights and biases -> one ``qkvg_proj``
+          (a missing gate keeps this module's current gate rows, missing biases are zero);
+        * ``out_proj.bias`` is dropped (the projection is bias-free);
+        * the old free ``pos_bias`` [J, H] table -> ``pos_bias_residual`` against this
+          module's analytic slope, so the effective bias (analytic + residual) is unchanged;
+        * absent ``pos_bias_*`` entries keep this module's current values.
+        """
+        D = self.qkvg_proj.in_features
+        state_dict.pop(prefix + "out_proj.bias", None)
+        w_key, b_key = prefix + "qkvg_proj.weight", prefix + "qkvg_proj.bias"
+        if w_key not in state_dict and prefix + "qkv_proj.weight" in state_dict:
+            qkv_w = state_dict.pop(prefix + "qkv_proj.weight")
+            gate_w = state_dict.pop(prefix + "gate_proj.weight", None)
+            if gate_w is None:
+                gate_w = self.qkvg_proj.weight.detach()[3 * D:].clone()
+            qkv_b = state_dict.pop(prefix + "qkv_proj.bias", None)
+            if qkv_b is None:
+                qkv_b = qkv_w.new_zeros(3 * D)
+            gate_b = state_dict.pop(prefix + "gate_proj.bias", None)
+            if gate_b is None:
+                gate_b = qkv_b.new_zeros(D)
+            state_dict[w_key] = torch.cat((qkv_w, gate_w), dim=0)
+            state_dict[b_key] = torch.cat((qkv_b, gate_b), dim=0)
+        old_key, res_key, slope_key = prefix + "pos_bias", prefix + "pos_bias_residual", prefix + "pos_bias_log_slope"
+        if old_key in state_dict and res_key not in state_dict:
+            old = state_dict.pop(old_key)
+            slope = self.pos_bias_log_slope.detach().clone()
+            state_dict[slope_key] = slope
+            log_distance = torch.log1p(self.offsets_dev.to(device=old.device, dtype=old.dtype)).reshape(-1, 1)
+            analytic = -log_distance * F.softplus(slope.to(device=old.device, dtype=old.dtype)).reshape(1, -1)
+            state_dict[res_key] = old - analytic
+        current = self.state_dict()
+        for name in ("pos_bias_log_slope", "pos_bias_residual", "pos_bias_scale"):
+            if prefix + name not in state_dict:
+                state_dict[prefix + name] = current[name].detach().clone()
+
+    def _load_from_state_dict(self, state_dict, prefix, local_metadata, strict, missing_keys, unexpected_keys,
+                              error_msgs):
+        self._migrate_legacy_keys(state_dict, prefix)
+        super()._load_from_state_dict(state_dict, prefix, local_metadata, strict, missing_keys, unexpected_keys,
+                                      error_msgs)
+
     def _tables(self):
         """fp32 device tables the kernels read, recomputed only when a parameter changed."""
         params = (self.pos_bias_log_slope, self.pos_bias_residual, self.pos_bias_scale, self.scale_embed,

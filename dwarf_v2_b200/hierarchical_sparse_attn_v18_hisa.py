@@ -343,6 +343,50 @@ class HierarchicalSparseAttentionV16HISACausal(nn.Module):
             "flex_lse_api": "none",
         }
 
+    def _migrate_legacy_keys(self, state_dict, prefix: str) -> None:
+        """Rewrites, in place, the reference's older checkpoint layouts (hierarchical_sparse_attn_v18_hisa.py:2469-2544).
+
+        Separate ``W_q`` / ``W_k`` / ``W_v`` (+ biases, zero when absent) and the block's
+        ``gate_proj`` (or ``global_gate``; zero when absent) -> one ``qkvg_proj``; parameters
+        newer than the checkpoint (route prior, NPCI angles, global adapters) keep this
+        module's current values.
+        """
+        w_key, b_key = prefix + "qkvg_proj.weight", prefix + "qkvg_proj.bias"
+        if w_key not in state_dict:
+            qw, kw, vw = (state_dict.get(prefix + f"{n}.weight") for n in ("W_q", "W_k", "W_v"))
+            if qw is not None and kw is not None and vw is not None:
+                parent = prefix[: -len("attn.")] if prefix.endswith("attn.") else prefix
+                gw = state_dict.get(parent + "gate_proj.weight")
+                if gw is None:
+                    gw = state_dict.get(parent + "global_gate.weight")
+                if gw is None:
+                    gw = torch.zeros_like(qw)
+                qb = state_dict.get(prefix + "W_q.bias", qw.new_zeros(qw.shape[0]))
+                kb = state_dict.get(prefix + "W_k.bias", kw.new_zeros(kw.shape[0]))
+                vb = state_dict.get(prefix + "W_v.bias", vw.new_zeros(vw.shape[0]))
+                gb = state_dict.get(parent + "gate_proj.bias")
+                if gb is None:
+                    gb = state_dict.get(parent + "global_gate.bias")
+                if gb is None:
+                    gb = qw.new_zeros(qw.shape[0])
+                state_dict[w_key] = torch.cat((qw, kw, vw, gw), dim=0)
+                state_dict[b_key] = torch.cat((qb, kb, vb, gb), dim=0)
+                for n in ("W_q.weight", "W_q.bias", "W_k.weight", "W_k.bias", "W_v.weight", "W_v.bias"):
+                    state_dict.pop(prefix + n, None)
+                for n in ("gate_proj.weight", "gate_proj.bias", "global_gate.weight", "global_gate.bias"):
+                    state_dict.pop(parent + n, None)
+        current = self.state_dict()
+        for name in ("route_prior_raw", "npci_theta_k", "npci_theta_v", "global_k_down.weight",
+                     "global_k_up.weight", "global_v_down.weight", "global_v_up.weight"):
+            if name in current and prefix + name not in state_dict:
+                state_dict[prefix + name] = current[name].detach().clone()
+
+    def _load_from_state_dict(self, state_dict, prefix, local_metadata, strict, missing_keys, unexpected_keys,
+                              error_msgs):
+        self._migrate_legacy_keys(state_dict, prefix)
+        super()._load_from_state_dict(state_dict, prefix, local_metadata, strict, missing_keys, unexpected_keys,
+                                      error_msgs)
+
     def prepare_runtime(self, device, seq_len: int | None = None) -> None:
         """Nothing to prebuild: the fused kernel needs no block mask."""
         return None

@@ -4,7 +4,7 @@ Run in a container that has the reference checkout (path in DWARF_REFERENCE_DIR,
 default ``/root/reference``); the fixtures it writes are committed and the
 tests read only those files, so nothing at test time needs the reference.
 
-    python tests/golden/make_golden.py [ema|dsqg|hisa|model|all]
+    python tests/golden/make_golden.py [ema|dsqg|hisa|model|checkpoint|all]
 
 Each fixture is an ``.npz`` holding the seeded inputs and the reference output
 of one call, named for the reference function it exercises. bf16 tensors are
@@ -335,9 +335,74 @@ def make_model() -> None:
     save("model_prefill_b1_t2048", **out)
 
 
+def make_checkpoint() -> None:
+    """Legacy-key migration of the reference modules' _load_from_state_dict.
+
+    DSQG (dsqg_attention_v22.py:3069-3142): a V19/V20-style dict with separate
+    qkv_proj / gate_proj (+ an out_proj.bias and the old unconstrained pos_bias
+    table). HISA (hierarchical_sparse_attn_v18_hisa.py:2469-2544): separate
+    W_q / W_k / W_v with the block-level gate_proj, and no adapter / NPCI /
+    route-prior parameters. Stored: the legacy dict and the state the
+    reference module holds after loading it.
+    """
+    _import_reference()
+    import dsqg_attention_v22 as ref_dsqg
+    import hierarchical_sparse_attn_v18_hisa as ref_hisa
+
+    torch.manual_seed(5)
+    offsets = [1, 2, 3, 5, 8, 13, 21, 48, 64, 100]
+    src = ref_dsqg.DSQGAttentionV19(128, 2, offsets, 7, 3, seq_len=160, dropout=0.0, plane_shift=6)
+    _randomize_dsqg(src, 505)
+    sd = src.state_dict()
+    D = 128
+    legacy = {k: v.clone() for k, v in sd.items()
+              if not k.startswith(("qkvg_proj.", "pos_bias_log_slope", "pos_bias_residual", "pos_bias_scale"))}
+    legacy["qkv_proj.weight"] = sd["qkvg_proj.weight"][: 3 * D].clone()
+    legacy["qkv_proj.bias"] = sd["qkvg_proj.bias"][: 3 * D].clone()
+    legacy["gate_proj.weight"] = sd["qkvg_proj.weight"][3 * D:].clone()
+    legacy["gate_proj.bias"] = sd["qkvg_proj.bias"][3 * D:].clone()
+    legacy["out_proj.bias"] = torch.randn(D)
+    legacy["pos_bias"] = torch.randn(len(offsets), 2) * 0.5
+    torch.manual_seed(6)
+    dst = ref_dsqg.DSQGAttentionV19(128, 2, offsets, 7, 3, seq_len=160, dropout=0.0, plane_shift=6)
+    dst.load_state_dict({k: v.clone() for k, v in legacy.items()}, strict=True)
+    out = {f"legacy.{k}": v for k, v in legacy.items()}
+    out.update({f"loaded.{k}": v for k, v in dst.state_dict().items()})
+    save("checkpoint_dsqg_legacy", **out)
+
+    torch.manual_seed(7)
+    kwargs = dict(D=128, H=2, hd=64, chunk_size=64, top_k_chunks=4, hisa_top_m_tokens=64, local_window=64,
+                  selector_tile_size=16, representative_mode="mean_max_blend", representative_blend_alpha=0.5,
+                  route_prior_scale=0.1, global_adapter_rank=16, npci_theta_max=0.25, local_backend="flex")
+    src = ref_hisa.HierarchicalSparseAttentionV16HISACausal(**kwargs)
+    sd = src.state_dict()
+    gen = torch.Generator().manual_seed(77)
+    legacy = {}
+    for name in ("W_q", "W_k", "W_v"):
+        legacy[f"attn.{name}.weight"] = torch.randn(D, D, generator=gen) * 0.05
+        legacy[f"attn.{name}.bias"] = torch.randn(D, generator=gen) * 0.05
+    legacy["gate_proj.weight"] = torch.randn(D, D, generator=gen) * 0.05
+    legacy["gate_proj.bias"] = torch.randn(D, generator=gen) * 0.05
+    for k, v in sd.items():
+        if k.startswith(("qkvg_proj.", "route_prior_raw", "npci_theta_", "global_k_", "global_v_")):
+            continue
+        legacy[f"attn.{k}"] = v.clone()
+    torch.manual_seed(8)
+    dst = ref_hisa.HierarchicalSparseAttentionV16HISACausal(**kwargs)
+    block = torch.nn.Module()  # stands in for the block that owns the legacy gate_proj
+    block.attn = dst
+    # strict=False: the stand-in block has no module of its own for the legacy gate keys
+    result = block.load_state_dict({k: v.clone() for k, v in legacy.items()}, strict=False)
+    assert not result.missing_keys, result
+    out = {f"legacy.{k}": v for k, v in legacy.items()}
+    out.update({f"loaded.{k}": v for k, v in dst.state_dict().items()})
+    save("checkpoint_hisa_legacy", **out)
+
+
 def main(argv: list[str]) -> None:
     which = argv[1] if len(argv) > 1 else "all"
-    makers = {"ema": make_ema, "dsqg": make_dsqg, "hisa": make_hisa, "model": make_model}
+    makers = {"ema": make_ema, "dsqg": make_dsqg, "hisa": make_hisa, "model": make_model,
+              "checkpoint": make_checkpoint}
     for name, maker in makers.items():
         if which in ("all", name):
             maker()
