@@ -17,9 +17,11 @@
 //      while the current one is finished),
 //   2. scan each warp's TS tokens from a zero state -> warp end states,
 //   3. warp 0 combines them into the tile aggregate, publishes it, walks back
-//      over up to 8 predecessor tiles of the same series (7 aggregates + 1
-//      inclusive prefix) to get the carry-in, and publishes the inclusive
-//      prefix,
+//      over up to LB predecessor tiles of the same series (LB - 1 aggregates
+//      + 1 inclusive prefix) to get the carry-in, and publishes the inclusive
+//      prefix (LB = 1 with many series in flight: the window costs registers,
+//      hence occupancy, and the series themselves hide the chain's latency;
+//      LB = 2 with few series),
 //   4. each warp rescans its tokens from its true carry-in and writes y once.
 //
 // Publication without fences: every published channel value travels in one
@@ -42,7 +44,9 @@
 namespace dwarf {
 namespace {
 
-constexpr int kLookback = 8;
+constexpr int kLookbackFew = 2;   // look-back window with few series in flight
+constexpr int kLookbackMany = 1;  // ... and with many (>= kManySeries)
+constexpr int64_t kManySeries = 256;
 
 struct EmaWorkspace {
   uint32_t* header;  // [0] epoch, [32] exit counter (separate 128-B lines)
@@ -80,7 +84,7 @@ __device__ __forceinline__ void stage_row(T* smem, const T* gmem, bool valid) {
   }
 }
 
-template <typename T, int VEC, int TS, int WARPS>
+template <typename T, int VEC, int TS, int WARPS, int kLookback>
 __global__ void __launch_bounds__(WARPS * 32, 1)
 ema_scan_lookback_kernel(const T* __restrict__ x, T* __restrict__ y, int64_t seq_len, int64_t width,
                          int64_t sxb, int64_t sxn, int64_t sxd, int64_t syb, int64_t syn, int64_t syd,
@@ -184,9 +188,9 @@ ema_scan_lookback_kernel(const T* __restrict__ x, T* __restrict__ y, int64_t seq
 #pragma unroll
         for (int v = 0; v < VEC; ++v) st_rec(ws.incl + rec + v, agg[v], tag);
       } else {
-        // Window: aggregates of chunk-1 .. chunk-7 and, in the farthest slot,
-        // the inclusive prefix of chunk-8 (the aggregate of chunk 0 is its
-        // inclusive prefix, so a window that reaches chunk 0 uses it).
+        // Window: aggregates of chunk-1 .. chunk-(LB-1) and, in the farthest
+        // slot, the inclusive prefix of chunk-LB (the aggregate of chunk 0 is
+        // its inclusive prefix, so a window that reaches chunk 0 uses it).
         const int window = chunk < kLookback ? (int)chunk : kLookback;
         float val[kLookback][VEC];
 #pragma unroll
@@ -307,8 +311,8 @@ int64_t workspace_bytes_any(int64_t batch, int64_t seq_len, int64_t width, int d
   return a > b ? a : b;
 }
 
-template <typename T, int VEC, int TS, int WARPS>
-int launch_ema(const dwarf_ema_scan_args* a, const EmaPlan& p, cudaStream_t stream) {
+template <typename T, int VEC, int TS, int WARPS, int LB>
+int launch_ema_lb(const dwarf_ema_scan_args* a, const EmaPlan& p, cudaStream_t stream) {
   char* base = static_cast<char*>(a->workspace);
   EmaWorkspace ws;
   const int64_t C = 32 * VEC;
@@ -316,7 +320,7 @@ int launch_ema(const dwarf_ema_scan_args* a, const EmaPlan& p, cudaStream_t stre
   ws.agg = reinterpret_cast<uint2*>(base + kHeaderBytes);
   ws.incl = reinterpret_cast<uint2*>(base + kHeaderBytes + round_up(p.ntiles * C * 8, 256));
   const size_t smem = 2 * (size_t)WARPS * TS * C * sizeof(T);
-  auto kernel = ema_scan_lookback_kernel<T, VEC, TS, WARPS>;
+  auto kernel = ema_scan_lookback_kernel<T, VEC, TS, WARPS, LB>;
   if (smem > 48 * 1024 &&
       cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return DWARF_ERR_LAUNCH;
@@ -342,6 +346,12 @@ int launch_ema(const dwarf_ema_scan_args* a, const EmaPlan& p, cudaStream_t stre
                                   stream) != cudaSuccess)
     return DWARF_ERR_LAUNCH;
   return launch_status();
+}
+
+template <typename T, int VEC, int TS, int WARPS>
+int launch_ema(const dwarf_ema_scan_args* a, const EmaPlan& p, cudaStream_t stream) {
+  return p.nseries >= kManySeries ? launch_ema_lb<T, VEC, TS, WARPS, kLookbackMany>(a, p, stream)
+                                  : launch_ema_lb<T, VEC, TS, WARPS, kLookbackFew>(a, p, stream);
 }
 
 }  // namespace
