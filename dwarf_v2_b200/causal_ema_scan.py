@@ -70,7 +70,8 @@ def _workspace(device: torch.device, nbytes: int) -> torch.Tensor:
 
 
 def _launch(x: torch.Tensor, out: torch.Tensor, alpha: torch.Tensor, per_channel: bool,
-            clamp: bool, floor: float, ceiling: float) -> None:
+            clamp: bool, floor: float, ceiling: float, init_state: torch.Tensor | None = None,
+            final_state: torch.Tensor | None = None) -> None:
     lib = _lib.load()
     batch, seq_len, width = x.shape
     code = _lib.dtype_code(x.dtype)
@@ -88,6 +89,7 @@ def _launch(x: torch.Tensor, out: torch.Tensor, alpha: torch.Tensor, per_channel
         floor_=floor, ceiling=ceiling,
         workspace=ws.data_ptr(), workspace_bytes=ws.numel(),
         device_status=_lib.device_status_word(x.device).data_ptr(),
+        init_state=_lib.ptr(init_state), final_state=_lib.ptr(final_state),
     )
     _lib.call("dwarf_ema_scan", args, x.device)
 
@@ -106,8 +108,15 @@ def causal_ema_scan(
     ceiling: float = 0.5,
     *,
     reset_mask: torch.Tensor | None = None,
-) -> torch.Tensor:
-    """Scalar-alpha causal EMA over ``x[B,N,D]`` (reference causal_ema_scan.py:541-567)."""
+    initial_state: torch.Tensor | None = None,
+    return_final_state: bool = False,
+):
+    """Scalar-alpha causal EMA over ``x[B,N,D]`` (reference causal_ema_scan.py:541-567).
+
+    Engine extensions for incremental decoding: ``initial_state`` (fp32 [B, D]) is
+    y[-1] instead of zero, and ``return_final_state`` also returns the fp32 state
+    after the last token (the state a continuation starts from).
+    """
     if x.ndim != 3:
         raise ValueError(f"x must be [B,N,D], got {tuple(x.shape)}")
     if ema_factor.numel() != 1:
@@ -122,8 +131,15 @@ def causal_ema_scan(
         raise TypeError(f"causal_ema_scan supports float32/bfloat16 input, got {x.dtype}")
     alpha = ema_factor.detach().reshape(1).to(device=x.device, dtype=torch.float32)
     out = torch.empty(x.shape, dtype=x.dtype, device=x.device)
-    _launch(x, out, alpha, False, True, float(floor), float(ceiling))
-    return out
+    B, _, D = x.shape
+    if initial_state is not None:
+        if initial_state.shape != (B, D) or initial_state.dtype != torch.float32:
+            raise ValueError("initial_state must be float32 [B, D]")
+        _lib.require_cuda(initial_state)
+        initial_state = initial_state.contiguous()
+    final = torch.empty(B, D, dtype=torch.float32, device=x.device) if return_final_state else None
+    _launch(x, out, alpha, False, True, float(floor), float(ceiling), initial_state, final)
+    return (out, final) if return_final_state else out
 
 
 def causal_ema_scan_per_channel(x: torch.Tensor, alpha: torch.Tensor) -> torch.Tensor:

@@ -48,6 +48,7 @@ struct DsqgParams {
   const __nv_bfloat16* gate;
   int64_t sgtb, sgtn;
   int32_t* status;  // optional device status word (DWARF_DEVICE_TIMEOUT)
+  int64_t row_begin;  // first query row computed (gather kernel)
 };
 
 // 16 bf16 (two 16-B words) -> 16 floats.

@@ -142,8 +142,11 @@ dsqg_fwd_kernel(const DsqgParams p) {
   const int lane = tid & 31, warp = tid >> 5;
   const int sub = tid % TPQ;
   const int qi = tid / TPQ;
-  const int64_t n0 = (int64_t)blockIdx.x * QB;
+  // Queries [row_begin, N) (absolute positions); q, y, gate, out and lse rows
+  // are addressed relative to row_begin.
+  const int64_t n0 = p.row_begin + (int64_t)blockIdx.x * QB;
   const int64_t n = n0 + qi;
+  const int64_t rb = p.row_begin;
   const int64_t n_last = (n0 + QB < p.N ? n0 + QB : p.N) - 1;
 
   // ---- stage Q tile, bf16(E), tables
@@ -151,7 +154,7 @@ dsqg_fwd_kernel(const DsqgParams p) {
   for (int i = tid; i < QB * 8; i += kThreads) {
     const int r = i >> 3, c = i & 7;
     const int64_t row = n0 + r < p.N ? n0 + r : p.N - 1;
-    const uint4 v = *reinterpret_cast<const uint4*>(p.q + b * p.sqb + h * p.sqh + row * p.sqn + c * 8);
+    const uint4 v = *reinterpret_cast<const uint4*>(p.q + b * p.sqb + h * p.sqh + (row - rb) * p.sqn + c * 8);
     *reinterpret_cast<uint4*>(s_q + (tile_addr(q_base, r, c) - q_base)) = v;
   }
   for (int i = tid; i < L.jp * 8; i += kThreads) {
@@ -227,7 +230,7 @@ dsqg_fwd_kernel(const DsqgParams p) {
 #pragma unroll
   for (int sl = 0; sl < NS; ++sl) {
     RowSlice<false> qr;
-    qr.load(p.q + b * p.sqb + h * p.sqh + (int64_t)nq * p.sqn + d0 + 16 * sl, true);
+    qr.load(p.q + b * p.sqb + h * p.sqh + ((int64_t)nq - rb) * p.sqn + d0 + 16 * sl, true);
     float t[16];
     qr.to_f32(t);
 #pragma unroll
@@ -308,7 +311,7 @@ dsqg_fwd_kernel(const DsqgParams p) {
 #pragma unroll
   for (int sl = 0; sl < NS; ++sl) {
     corr_a[sl] = corr_b[sl] = 0.0f;
-    yq[sl] = p.y[b * p.syb + h * p.syh + (int64_t)nq * p.syn + sub * NS + sl];
+    yq[sl] = p.y[b * p.syb + h * p.syh + ((int64_t)nq - rb) * p.syn + sub * NS + sl];
   }
   const float msafe = m == -INFINITY ? 0.0f : m;
   const int rot_a = p.plane_shift;
@@ -412,7 +415,7 @@ dsqg_fwd_kernel(const DsqgParams p) {
     }
     if (p.gate != nullptr) {
       RowSlice<false> gs;
-      gs.load(p.gate + b * p.sgtb + n * p.sgtn + h * 64 + d0 + 16 * sl, true);
+      gs.load(p.gate + b * p.sgtb + (n - rb) * p.sgtn + h * 64 + d0 + 16 * sl, true);
       float gv[16];
       gs.to_f32(gv);
 #pragma unroll
@@ -428,12 +431,12 @@ dsqg_fwd_kernel(const DsqgParams p) {
       const __nv_bfloat162 two = __floats2bfloat162_rn(o[2 * i], o[2 * i + 1]);
       pw[i] = *reinterpret_cast<const uint32_t*>(&two);
     }
-    uint4* dst = reinterpret_cast<uint4*>(p.out + b * p.sob + h * p.soh + n * p.son + d0 + 16 * sl);
+    uint4* dst = reinterpret_cast<uint4*>(p.out + b * p.sob + h * p.soh + (n - rb) * p.son + d0 + 16 * sl);
     dst[0] = packed[0];
     dst[1] = packed[1];
   }
   if (p.lse != nullptr && sub == 0) {
-    p.lse[b * p.slb + h * p.slh + n * p.sln] = l > 0.0f ? m + logf(l) : -INFINITY;
+    p.lse[b * p.slb + h * p.slh + (n - rb) * p.sln] = l > 0.0f ? m + logf(l) : -INFINITY;
   }
 }
 
@@ -441,7 +444,7 @@ template <bool Q6, int TPQ>
 int launch_dsqg(const DsqgParams& p, int64_t B, int64_t H, int64_t N, int J, int j_large, cudaStream_t stream) {
   constexpr int QB = kThreads / TPQ;
   const size_t smem = DsqgSmem(J, j_large, QB).bytes;
-  dim3 grid((unsigned)((N + QB - 1) / QB), (unsigned)H, (unsigned)B);
+  dim3 grid((unsigned)((N - p.row_begin + QB - 1) / QB), (unsigned)H, (unsigned)B);
   if (grid.z > 65535 || grid.y > 65535) return DWARF_ERR_SHAPE;
   auto kernel = dsqg_fwd_kernel<Q6, TPQ>;
   if (smem > 48 * 1024 && cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem))
@@ -466,7 +469,8 @@ extern "C" int dwarf_dsqg_fwd(const dwarf_dsqg_fwd_args* a, void* stream) {
   if (a->J < 1 || a->j_small < 0 || a->j_large < 0 || a->j_small + a->j_large != a->J || a->J > 512)
     return DWARF_ERR_SHAPE;
   if (a->plane_shift < 0 || a->plane_shift > 14) return DWARF_ERR_VALUE;
-  if (a->B == 0 || a->N == 0) return DWARF_OK;
+  if (a->row_begin < 0 || a->row_begin > a->N) return DWARF_ERR_SHAPE;
+  if (a->B == 0 || a->N == 0 || a->row_begin == a->N) return DWARF_OK;
   if (!a->q || !a->out || !a->offsets || !a->pos_bias || !a->scale_embed || !a->y_pre || !a->z_pre)
     return DWARF_ERR_NULL;
   if (a->j_large > 0 && (!a->phase_base || !a->phase_gain)) return DWARF_ERR_NULL;
@@ -513,6 +517,7 @@ extern "C" int dwarf_dsqg_fwd(const dwarf_dsqg_fwd_args* a, void* stream) {
   p.gain = a->head_gain; p.gain_bf16 = a->head_gain_dtype == DWARF_BF16;
   p.gate = (const __nv_bfloat16*)a->gate; p.sgtb = a->sgb_; p.sgtn = a->sgn_;
   p.status = a->device_status;
+  p.row_begin = a->row_begin;
 
   // 2 threads per query (32 dims each): half the per-pair bookkeeping of the
   // 4-thread layout. DWARF_DSQG_TPQ=4 selects the 4-thread layout.
@@ -525,7 +530,7 @@ extern "C" int dwarf_dsqg_fwd(const dwarf_dsqg_fwd_args* a, void* stream) {
   // DWARF_DSQG_PATH=gather forces the gather kernel (read on every call).
   if (q6) {
     const char* path = getenv("DWARF_DSQG_PATH");
-    if (!(path && path[0] == 'g')) {
+    if (!(path && path[0] == 'g') && p.row_begin == 0) {
       const int rc = dsqg_resident_launch(p, a->B, st);
       if (rc != kNotApplicable) return rc;
     }

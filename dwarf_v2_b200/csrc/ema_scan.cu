@@ -90,7 +90,8 @@ ema_scan_lookback_kernel(const T* __restrict__ x, T* __restrict__ y, int64_t seq
                          int64_t sxb, int64_t sxn, int64_t sxd, int64_t syb, int64_t syn, int64_t syd,
                          const float* __restrict__ alpha, int alpha_per_channel, int clamp, float lo,
                          float hi, EmaWorkspace ws, int64_t nseries, int64_t ncb, int64_t ntiles,
-                         int32_t* device_status) {
+                         int32_t* device_status, const float* __restrict__ init_state,
+                         float* __restrict__ final_state) {
   constexpr int C = 32 * VEC;  // channels per series
   constexpr int CH = WARPS * TS;
   constexpr bool kAsync = VEC * sizeof(T) == 16;
@@ -185,12 +186,19 @@ ema_scan_lookback_kernel(const T* __restrict__ x, T* __restrict__ y, int64_t seq
 #pragma unroll
       for (int v = 0; v < VEC; ++v) st_rec(ws.agg + rec + v, agg[v], tag);
       if (chunk == 0) {
+        // Carry-in of the first chunk: the caller's initial state (decode
+        // continues a sequence) or zero.
+        if (init_state != nullptr && lane_active) {
 #pragma unroll
-        for (int v = 0; v < VEC; ++v) st_rec(ws.incl + rec + v, agg[v], tag);
+          for (int v = 0; v < VEC; ++v) carry[v] = init_state[b * width + c0 + v];
+        }
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) st_rec(ws.incl + rec + v, agg[v] + dch[v] * carry[v], tag);
       } else {
         // Window: aggregates of chunk-1 .. chunk-(LB-1) and, in the farthest
-        // slot, the inclusive prefix of chunk-LB (the aggregate of chunk 0 is
-        // its inclusive prefix, so a window that reaches chunk 0 uses it).
+        // slot, the inclusive prefix of chunk-LB; a window that reaches chunk 0
+        // reads its inclusive prefix (it holds the initial state's share and is
+        // published together with its aggregate).
         const int window = chunk < kLookback ? (int)chunk : kLookback;
         float val[kLookback][VEC];
 #pragma unroll
@@ -205,7 +213,7 @@ ema_scan_lookback_kernel(const T* __restrict__ x, T* __restrict__ y, int64_t seq
           for (int k = 0; k < kLookback; ++k) {
             if (k < window) {
               const int64_t pc = chunk - 1 - k;
-              const bool use_incl = (k == kLookback - 1) && pc > 0;
+              const bool use_incl = k == kLookback - 1 || pc == 0;
               const uint2* src = (use_incl ? ws.incl : ws.agg) + (pc * nseries + series) * C + lane * VEC;
 #pragma unroll
               for (int v = 0; v < VEC; ++v) {
@@ -256,6 +264,10 @@ ema_scan_lookback_kernel(const T* __restrict__ x, T* __restrict__ y, int64_t seq
 #pragma unroll
         for (int v = 0; v < VEC; ++v) s[v] = a[v] * xv[v] + d[v] * s[v];
         if (i < nvalid) VecIO<T, VEC>::store(yrow + i * syn, s);
+        if (final_state != nullptr && t0 + i == seq_len - 1) {
+#pragma unroll
+          for (int v = 0; v < VEC; ++v) final_state[b * width + c0 + v] = s[v];
+        }
       }
     }
 
@@ -340,8 +352,10 @@ int launch_ema_lb(const dwarf_ema_scan_args* a, const EmaPlan& p, cudaStream_t s
   float lo = a->floor_, hi = a->ceiling;
   int64_t nseries = p.nseries, ncb = p.ncb, ntiles = p.ntiles;
   int32_t* status = a->device_status;
+  const float* init = a->init_state;
+  float* fin = a->final_state;
   void* params[] = {&x, &y, &seq_len, &width, &sxb, &sxn, &sxd, &syb, &syn, &syd, &alpha,
-                    &per_channel, &clamp, &lo, &hi, &ws, &nseries, &ncb, &ntiles, &status};
+                    &per_channel, &clamp, &lo, &hi, &ws, &nseries, &ncb, &ntiles, &status, &init, &fin};
   if (cudaLaunchCooperativeKernel((const void*)kernel, dim3((unsigned)grid), dim3(WARPS * 32), params, smem,
                                   stream) != cudaSuccess)
     return DWARF_ERR_LAUNCH;

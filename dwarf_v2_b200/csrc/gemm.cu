@@ -56,6 +56,7 @@ struct GemmEpi {
   float eps;
   // qkvg + DSQG prep epilogue
   int T, heads;
+  int64_t cache_len;  // rows per (b, h) in y / z / codes / scales
   const float* q_probe;
   const float* k_probe;
   float* y_pre;
@@ -636,7 +637,7 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
           add_bias64(epi.bias, epi.bias_bf16, n0 + c, v);
 #pragma unroll
           for (int i = 0; i < 64; ++i) v[i] = round_bf16(v[i]);
-          const int64_t hrow = ((int64_t)b * epi.heads + head) * epi.T + tt;
+          const int64_t hrow = ((int64_t)b * epi.heads + head) * epi.cache_len + tt;
           if (sec == 0 || sec == 3) {
             if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
             __syncwarp();
@@ -872,8 +873,8 @@ extern "C" int dwarf_gemm_bf16(const dwarf_gemm_args* a, void* stream) {
   if (a->bias != nullptr && a->bias_dtype != DWARF_F32 && a->bias_dtype != DWARF_BF16) return DWARF_ERR_DTYPE;
   GemmEpi epi{a->bias, a->bias_dtype == DWARF_BF16, (__nv_bfloat16*)a->out, a->ldo, a->device_status,
               (const __nv_bfloat16*)a->resid, a->ldr, a->norm_w, a->norm_w_dtype == DWARF_BF16, a->eps,
-              (int)a->T, a->heads, a->q_probe, a->k_probe, a->y_pre, a->z_pre, a->k_codes, a->k_scales,
-              a->v_codes, a->v_scales};
+              (int)a->T, a->heads, a->cache_len > 0 ? a->cache_len : a->T, a->q_probe, a->k_probe, a->y_pre,
+              a->z_pre, a->k_codes, a->k_scales, a->v_codes, a->v_scales};
   cudaStream_t st = (cudaStream_t)stream;
   if (a->epilogue == DWARF_GEMM_QKVG_PREP) {
     if (a->heads <= 0 || a->N != 256LL * a->heads || (64LL * a->heads) % 256 != 0) return DWARF_ERR_SHAPE;

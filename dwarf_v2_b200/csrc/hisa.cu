@@ -107,6 +107,7 @@ struct SelectParams {
   int32_t* top;               // [B,H,tiles,K]
   float* logits;              // optional [B,H,tiles,C], masked (-inf)
   int64_t H, T, C, tiles;
+  int64_t tile_begin, tile_end;  // tiles [tile_begin, tile_end) are computed
   int k_slots;
   float temperature;
 };
@@ -128,14 +129,14 @@ __global__ void __launch_bounds__(256) hisa_select_kernel(const SelectParams p) 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int i = threadIdx.x; i < p.C * kHD; i += blockDim.x)
     reps[i / kHD][i % kHD] = __bfloat162float(p.reps[((b * p.H + h) * p.C) * kHD + i]);
-  const int64_t t = (int64_t)blockIdx.x * 8 + warp;
+  const int64_t t = p.tile_begin + (int64_t)blockIdx.x * 8 + warp;
   const int64_t start = t * kTile;
   const int64_t arow = imin64(start, p.T - 1);
   const __nv_bfloat16* qrow = p.q + b * p.sqb + h * p.sqh + arow * p.sqn;
   anchor[warp][lane] = __bfloat162float(qrow[lane]);
   anchor[warp][lane + 32] = __bfloat162float(qrow[lane + 32]);
   __syncthreads();
-  if (t >= p.tiles) return;
+  if (t >= p.tile_end) return;
   if (lane == 0) normalize_row_bf16(anchor[warp]);
   __syncwarp();
   const int64_t vlen = p.lengths[b];
@@ -226,6 +227,8 @@ struct AttnParams {
   const int32_t* lengths;
   __nv_bfloat16* out; int64_t sob, soh, son;
   int64_t H, T, tiles;
+  int64_t tile_begin, tile_end;  // tiles [tile_begin, tile_end) are computed
+  int64_t grid_begin;            // tile_begin rounded down to the CTA tile grid
   int k_slots;
 };
 
@@ -326,6 +329,7 @@ struct RouteParams {
   const float* route_scale;   // [H]
   __nv_bfloat16* route;       // [B,H,T,4]
   int64_t H, T, C, tiles;
+  int64_t tile_begin, tile_end;  // tiles [tile_begin, tile_end) are computed
   int k_slots;
 };
 
@@ -336,8 +340,8 @@ __global__ void __launch_bounds__(256) hisa_route_kernel(const RouteParams p) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int h = blockIdx.y, b = blockIdx.z;
   const int lt = warp * 2 + (lane >> 4);  // local tile of this lane's row
-  const int64_t t = (int64_t)blockIdx.x * 16 + lt;
-  const bool tile_ok = t < p.tiles;
+  const int64_t t = p.tile_begin + (int64_t)blockIdx.x * 16 + lt;
+  const bool tile_ok = t < p.tile_end;
   const int64_t row = t * kTile + (lane & 15);
   // Issue the row load first; the selections and representatives follow.
   uint4 qw[8];
@@ -349,8 +353,8 @@ __global__ void __launch_bounds__(256) hisa_route_kernel(const RouteParams p) {
   }
   if (lane < 2 * kTopK) {
     const int i = warp * 2 + lane / kTopK, k = lane % kTopK;
-    const int64_t ti = (int64_t)blockIdx.x * 16 + i;
-    sel[i][k] = (ti < p.tiles && k < p.k_slots) ? p.top[((b * p.H + h) * p.tiles + ti) * p.k_slots + k] : -1;
+    const int64_t ti = p.tile_begin + (int64_t)blockIdx.x * 16 + i;
+    sel[i][k] = (ti < p.tile_end && k < p.k_slots) ? p.top[((b * p.H + h) * p.tiles + ti) * p.k_slots + k] : -1;
   }
   __syncwarp();
   for (int x = lane; x < 2 * kTopK * kHD; x += 32) {
@@ -478,7 +482,11 @@ hisa_attn_kernel(const AttnParams p, const __grid_constant__ AttnMaps maps, int3
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int h = blockIdx.y, b = blockIdx.z;
-  const int64_t T0 = (int64_t)blockIdx.x * kCtaTiles * kTile;
+  // CTAs cover aligned groups of kCtaTiles tiles whatever the window, so a
+  // windowed launch visits each tile's chunks in the order a full launch does
+  // (bit-identical rows); tiles of a group outside the window stay idle.
+  const int64_t T0 = (p.grid_begin + (int64_t)blockIdx.x * kCtaTiles) * kTile;
+  auto in_window = [&](int64_t t) { return t >= p.tile_begin && t < p.tile_end; };
   const int64_t vlen = imin64((int64_t)p.lengths[b], p.T);
   const int32_t* top = p.top + ((int64_t)b * p.H + h) * p.tiles * p.k_slots;
 
@@ -487,7 +495,7 @@ hisa_attn_kernel(const AttnParams p, const __grid_constant__ AttnMaps maps, int3
   if (warp == 0) {
     const int i = lane / kTopK, k = lane % kTopK;
     const int64_t t = T0 / kTile + i;
-    s_top[lane] = (t < p.tiles && k < p.k_slots) ? top[t * p.k_slots + k] : -1;
+    s_top[lane] = (in_window(t) && k < p.k_slots) ? top[t * p.k_slots + k] : -1;
   }
   __syncthreads();
   // ---- phase B: chunk list + barriers (warp 0), route prior rows (everyone)
@@ -505,7 +513,8 @@ hisa_attn_kernel(const AttnParams p, const __grid_constant__ AttnMaps maps, int3
         for (int i = 0; i < kCtaTiles; ++i) {
           e.slot[i] = -1;
           const int64_t t0 = T0 + kTile * i;
-          if (t0 < p.T && t0 - 64 < row0 + 64 && row0 < t0 + kTile) e.mask |= (uint8_t)(1u << i);
+          if (t0 < p.T && in_window(t0 / kTile) && t0 - 64 < row0 + 64 && row0 < t0 + kTile)
+            e.mask |= (uint8_t)(1u << i);
         }
         if (e.mask) s_ent[n++] = e;
       }
@@ -513,11 +522,18 @@ hisa_attn_kernel(const AttnParams p, const __grid_constant__ AttnMaps maps, int3
     n = __shfl_sync(0xffffffffu, n, 0);
     // Routed chunks: one entry per distinct chunk id among the 32 selections
     // (lane = tile * 4 + slot); the lowest lane of each group of equal ids
-    // writes the entry, in lane order.
+    // writes the entry, in ascending chunk order -- so each tile meets its own
+    // chunks in the same order whichever tiles share the CTA (a windowed
+    // launch reproduces a full launch bit for bit).
     const int c = s_top[lane];
     const unsigned same = __match_any_sync(0xffffffffu, c);
     const bool leader = c >= 0 && (__ffs(same) - 1) == lane;
     const unsigned leaders = __ballot_sync(0xffffffffu, leader);
+    int rank = 0;
+    for (int j = 0; j < 32; ++j) {
+      const int cj = __shfl_sync(0xffffffffu, c, j);
+      rank += ((leaders >> j) & 1u) && cj < c;
+    }
     if (leader) {
       ChunkEntry e;
       e.row0 = c * kChunk;
@@ -529,7 +545,7 @@ hisa_attn_kernel(const AttnParams p, const __grid_constant__ AttnMaps maps, int3
         e.mask |= (uint8_t)(1u << (ln / kTopK));
         e.slot[ln / kTopK] = (int8_t)(ln % kTopK);
       }
-      s_ent[n + __popc(leaders & ((1u << lane) - 1))] = e;
+      s_ent[n + rank] = e;
     }
     if (lane == 0) {
       *s_count = n + __popc(leaders);
@@ -568,7 +584,7 @@ hisa_attn_kernel(const AttnParams p, const __grid_constant__ AttnMaps maps, int3
     const int64_t t0 = T0 + (int64_t)kTile * tile;
     const int g = lane >> 2, t4 = lane & 3;
     const __nv_bfloat16* qb = p.q + b * p.sqb + h * p.sqh;
-    const bool tile_ok = t0 < p.T;
+    const bool tile_ok = t0 < p.T && in_window(t0 / kTile);
     float* route = s_route + tile * 16 * kTopK;
     // Q fragments (m16n8k16 A operand) straight from global.
     uint32_t qa[4][4];
@@ -661,6 +677,16 @@ bool make_kv_map(CUtensorMap* map, const void* ptr, int64_t B, int64_t H, int64_
 
 bool al16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
 
+// Tile window [begin, begin + count) of `tiles` (count 0: to the end).
+bool tile_window(int64_t begin, int64_t count, int64_t tiles, int64_t* b, int64_t* e) {
+  if (begin < 0 || count < 0 || begin > tiles) return false;
+  const int64_t end = count == 0 ? tiles : begin + count;
+  if (end > tiles) return false;
+  *b = begin;
+  *e = end;
+  return true;
+}
+
 }  // namespace
 }  // namespace dwarf
 
@@ -695,7 +721,9 @@ extern "C" int dwarf_hisa_select(const dwarf_hisa_select_args* a, void* stream) 
   p.logits = a->logits; p.H = a->H; p.T = a->T; p.C = C; p.tiles = (a->T + kTile - 1) / kTile;
   p.k_slots = (int)(a->top_k < C ? a->top_k : C);
   p.temperature = a->temperature;
-  dim3 grid((unsigned)((p.tiles + 7) / 8), (unsigned)a->H, (unsigned)a->B);
+  if (!tile_window(a->tile_begin, a->tile_count, p.tiles, &p.tile_begin, &p.tile_end)) return DWARF_ERR_SHAPE;
+  if (p.tile_end == p.tile_begin) return DWARF_OK;
+  dim3 grid((unsigned)((p.tile_end - p.tile_begin + 7) / 8), (unsigned)a->H, (unsigned)a->B);
   hisa_select_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(p);
   return launch_status();
 }
@@ -713,7 +741,9 @@ extern "C" int dwarf_hisa_route(const dwarf_hisa_route_args* a, void* stream) {
   p.reps = (const __nv_bfloat16*)a->reps; p.top = a->top_chunk_idx; p.route_scale = a->route_scale;
   p.route = (__nv_bfloat16*)a->route;
   p.H = a->H; p.T = a->T; p.C = a->C; p.tiles = (a->T + kTile - 1) / kTile; p.k_slots = a->k_slots;
-  dim3 grid((unsigned)((p.tiles + 15) / 16), (unsigned)a->H, (unsigned)a->B);
+  if (!tile_window(a->tile_begin, a->tile_count, p.tiles, &p.tile_begin, &p.tile_end)) return DWARF_ERR_SHAPE;
+  if (p.tile_end == p.tile_begin) return DWARF_OK;
+  dim3 grid((unsigned)((p.tile_end - p.tile_begin + 15) / 16), (unsigned)a->H, (unsigned)a->B);
   hisa_route_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(p);
   return launch_status();
 }
@@ -756,7 +786,10 @@ extern "C" int dwarf_hisa_attn(const dwarf_hisa_attn_args* a, void* stream) {
   if (cudaFuncSetAttribute(hisa_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return DWARF_ERR_LAUNCH;
   const int64_t cta_tiles = kCtaTiles;
-  dim3 grid((unsigned)((p.tiles + cta_tiles - 1) / cta_tiles), (unsigned)a->H, (unsigned)a->B);
+  if (!tile_window(a->tile_begin, a->tile_count, p.tiles, &p.tile_begin, &p.tile_end)) return DWARF_ERR_SHAPE;
+  if (p.tile_end == p.tile_begin) return DWARF_OK;
+  p.grid_begin = p.tile_begin - p.tile_begin % cta_tiles;
+  dim3 grid((unsigned)((p.tile_end - p.grid_begin + cta_tiles - 1) / cta_tiles), (unsigned)a->H, (unsigned)a->B);
   hisa_attn_kernel<<<grid, kCtaTiles * 32, smem, (cudaStream_t)stream>>>(p, maps, nullptr);
   return launch_status();
 }

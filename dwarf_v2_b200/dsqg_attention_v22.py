@@ -305,15 +305,23 @@ def _strides3(t: torch.Tensor) -> tuple[int, int, int]:
 
 
 def _dsqg_launch(q, *, kv, pos_bias, scale_embed, phase_base, phase_gain, y_pre, z_pre, offsets,
-                 j_small, j_large, plane_shift, query_start, out, lse=None, head_gain=None, gate=None):
-    """Validate and launch dwarf_dsqg_fwd. ``kv`` is ("bf16", k, v) or ("q6", kc, ks, vc, vs)."""
+                 j_small, j_large, plane_shift, query_start, out, lse=None, head_gain=None, gate=None,
+                 seq_len=None, row_begin=0):
+    """Validate and launch dwarf_dsqg_fwd. ``kv`` is ("bf16", k, v) or ("q6", kc, ks, vc, vs).
+
+    With ``row_begin`` > 0 only queries [row_begin, seq_len) are computed and q, y_pre,
+    gate, out and lse hold those rows only (row 0 = position row_begin); K/V and z_pre
+    cover positions [0, seq_len). This is the decode step's single-row launch.
+    """
     B, H, N, HD = q.shape
+    if seq_len is not None:
+        N = int(seq_len)
     J = int(j_small) + int(j_large)
     if HD != 64:
         raise ValueError(f"the B200 DSQG kernel supports head_dim 64, got {HD}")
     args = _lib.DsqgFwdArgs(version=_lib.ABI_VERSION, B=B, H=H, N=N, head_dim=HD, J=J,
                             j_small=int(j_small), j_large=int(j_large), plane_shift=int(plane_shift),
-                            query_start=int(query_start))
+                            query_start=int(query_start), row_begin=int(row_begin))
     args.q = q.data_ptr()
     args.sqb, args.sqh, args.sqn = _strides3(q)
     if kv[0] == "bf16":
@@ -784,19 +792,52 @@ class DSQGAttentionV19(nn.Module):
         kv = ("q6", *cache) if q6 else ("bf16", key, value)
         return self._attend(x, query, kv, y_pre, z_pre, content_gate, t, query_start)
 
-    def _attend(self, x, query, kv, y_pre, z_pre, content_gate, t, query_start):
-        """DSQG kernel (if_gain and content-gate epilogue fused) followed by out_proj."""
+    def forward_cached(self, x: torch.Tensor, cache, row: int) -> torch.Tensor:
+        """Attention output for positions [row, row + T) of ``x`` [B,T,D], appending their
+        q6 K/V (and the K-side phase probes) to ``cache`` first.
+
+        ``cache`` = (y, z, k_codes, k_scales, v_codes, v_scales) of L positions per
+        (batch, head) (the layout ``gemm.qkvg_prep`` documents) holding positions
+        [0, row). row = 0 is a prefill; T = 1 is one decode step, whose DSQG launch
+        computes the single query row over the whole cache.
+        """
+        _lib.require_cuda(x)
+        _forward_only(x, *self.parameters())
+        if self.kv_cache != "q6" or self.head_dim != 64 or (self.num_heads * 64) % 256 != 0:
+            raise NotImplementedError("cached (incremental) DSQG runs on the q6 cache with head_dim 64")
+        batch, rows, dimension = x.shape
+        heads, head_dim = self.num_heads, self.head_dim
         act = torch.bfloat16
-        batch, heads, seq_len, head_dim = query.shape
+        xb = x if x.dtype == act else x.to(act)
+        t = self._tables()
+        qkvg, y_pre, _, _ = gemm.qkvg_prep(xb, self.qkvg_proj.weight.to(act), self.qkvg_proj.bias.to(act), heads,
+                                           t["q_probe"], t["k_probe"], cache=cache, row=row)
+        seq_len = row + rows
+        query_start = min(self.minimum_offset, seq_len)
+        if query_start >= seq_len:
+            return torch.zeros_like(x)
+        query = qkvg.view(batch, rows, 4, heads, head_dim)[:, :, 0].permute(0, 2, 1, 3)
+        _, z, kc, ks, vc, vs = cache
+        return self._attend(x, query, ("q6", kc, ks, vc, vs), y_pre, z, qkvg[:, :, 3 * dimension:], t,
+                            query_start, seq_len=seq_len, row_begin=row)
+
+    def _attend(self, x, query, kv, y_pre, z_pre, content_gate, t, query_start, *, seq_len=None, row_begin=0):
+        """DSQG kernel (if_gain and content-gate epilogue fused) followed by out_proj.
+
+        With ``row_begin`` > 0 ``query``/``y_pre``/``content_gate`` hold positions
+        [row_begin, seq_len) and K/V, z_pre positions [0, seq_len)."""
+        act = torch.bfloat16
+        batch, heads, rows, head_dim = query.shape
         dimension = heads * head_dim
-        out = torch.empty(batch, seq_len, dimension, dtype=act, device=x.device)
-        out_view = out.view(batch, seq_len, heads, head_dim).permute(0, 2, 1, 3)
+        out = torch.empty(batch, rows, dimension, dtype=act, device=x.device)
+        out_view = out.view(batch, rows, heads, head_dim).permute(0, 2, 1, 3)
         gain = self.if_gain if self.if_gain.dtype in (torch.bfloat16, torch.float32) else self.if_gain.float()
         _dsqg_launch(query, kv=kv, pos_bias=t["pos_bias"], scale_embed=t["scale_embed"],
                      phase_base=t["phase_base"], phase_gain=t["phase_gain"], y_pre=y_pre, z_pre=z_pre,
                      offsets=t["offsets"], j_small=self.j_small, j_large=self.j_large,
                      plane_shift=self.plane_shift, query_start=query_start, out=out_view,
-                     head_gain=gain.detach().contiguous(), gate=content_gate)
+                     head_gain=gain.detach().contiguous(), gate=content_gate, seq_len=seq_len,
+                     row_begin=row_begin)
         result = F.linear(out, self.out_proj.weight.to(act))
         return self.dropout(result).to(x.dtype) if x.dtype != act else self.dropout(result)
 

@@ -115,12 +115,17 @@ def linear_add_rmsnorm(x: torch.Tensor, weight: torch.Tensor, resid: torch.Tenso
 
 
 def qkvg_prep(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, heads: int,
-              q_probe: torch.Tensor, k_probe: torch.Tensor):
+              q_probe: torch.Tensor, k_probe: torch.Tensor, *, cache=None, row: int = 0):
     """DSQG qkvg projection with the prep pass fused into its epilogue.
 
     x [B, T, D] bf16; weight [4D, D], bias [4D]. Returns (qkvg, y_pre, z_pre,
     (k_codes, k_scales, v_codes, v_scales)) where qkvg [B, T, 4D] holds valid
     q and gate columns only (K and V exist only as the q6 cache).
+
+    ``cache`` = (y, z, k_codes, k_scales, v_codes, v_scales), contiguous buffers of
+    L >= row + T positions per (batch, head) ([B,H,L,4] fp32, [B,H,L,48] u8, [B,H,L]
+    fp16): the epilogue writes positions [row, row + T) there instead of allocating
+    (the decode cache). The returned tensors are then views of those rows.
     """
     _lib.require_cuda(x, weight, bias, q_probe, k_probe)
     if x.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16:
@@ -132,12 +137,26 @@ def qkvg_prep(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, heads: 
     dev = x.device
     x2, lda = _rows2d(x)
     qkvg = torch.empty(B, T, N, dtype=torch.bfloat16, device=dev)
-    y = torch.empty(B, heads, T, 4, dtype=torch.float32, device=dev)
-    z = torch.empty_like(y)
-    kc = torch.empty(B, heads, T, 48, dtype=torch.uint8, device=dev)
-    vc = torch.empty_like(kc)
-    ks = torch.empty(B, heads, T, dtype=torch.float16, device=dev)
-    vs = torch.empty_like(ks)
+    if cache is None:
+        y = torch.empty(B, heads, T, 4, dtype=torch.float32, device=dev)
+        z = torch.empty_like(y)
+        kc = torch.empty(B, heads, T, 48, dtype=torch.uint8, device=dev)
+        vc = torch.empty_like(kc)
+        ks = torch.empty(B, heads, T, dtype=torch.float16, device=dev)
+        vs = torch.empty_like(ks)
+        cache_len = T
+    else:
+        y, z, kc, ks, vc, vs = cache
+        cache_len = y.shape[2]
+        shapes = ((y, (B, heads, cache_len, 4), torch.float32), (z, (B, heads, cache_len, 4), torch.float32),
+                  (kc, (B, heads, cache_len, 48), torch.uint8), (vc, (B, heads, cache_len, 48), torch.uint8),
+                  (ks, (B, heads, cache_len), torch.float16), (vs, (B, heads, cache_len), torch.float16))
+        for t, shape, dtype in shapes:
+            if tuple(t.shape) != shape or t.dtype != dtype or not t.is_contiguous():
+                raise ValueError(f"cache buffer must be contiguous {dtype} {shape}, got {t.dtype} {tuple(t.shape)}")
+        if not 0 <= row <= cache_len - T:
+            raise ValueError(f"rows [{row}, {row + T}) exceed the cache length {cache_len}")
+        y, z, kc, ks, vc, vs = (t[:, :, row:row + T] for t in (y, z, kc, ks, vc, vs))
     b = bias.contiguous()
     qp, kp = q_probe.float().contiguous(), k_probe.float().contiguous()
     args = _lib.GemmArgs(version=_lib.ABI_VERSION, epilogue=QKVG_PREP, M=B * T, N=N, K=K, a=x2.data_ptr(),
@@ -145,6 +164,6 @@ def qkvg_prep(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, heads: 
                          bias_dtype=_lib.dtype_code(b.dtype), out=qkvg.data_ptr(), ldo=N, T=T, heads=heads,
                          q_probe=qp.data_ptr(), k_probe=kp.data_ptr(), y_pre=y.data_ptr(), z_pre=z.data_ptr(),
                          k_codes=kc.data_ptr(), k_scales=ks.data_ptr(), v_codes=vc.data_ptr(),
-                         v_scales=vs.data_ptr())
+                         v_scales=vs.data_ptr(), cache_len=cache_len)
     _lib.call("dwarf_gemm_bf16", args, dev)
     return qkvg, y, z, (kc, ks, vc, vs)

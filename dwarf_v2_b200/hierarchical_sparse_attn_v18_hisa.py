@@ -108,8 +108,12 @@ def chunk_representatives(global_key: torch.Tensor, lengths: torch.Tensor, *, bl
 
 
 def select_chunks(query: torch.Tensor, reps: torch.Tensor, lengths: torch.Tensor, *, top_k: int,
-                  temperature: float, want_logits: bool = False):
-    """``dwarf_hisa_select``: (top_chunk_idx int32 [B,H,tiles,K], optional masked logits)."""
+                  temperature: float, want_logits: bool = False, tile_begin: int = 0, tile_count: int = 0):
+    """``dwarf_hisa_select``: (top_chunk_idx int32 [B,H,tiles,K], optional masked logits).
+
+    ``tile_begin``/``tile_count`` restrict the launch to selector tiles
+    [tile_begin, tile_begin + tile_count) (count 0: every tile); other entries stay unset.
+    """
     B, H, T, D = query.shape
     C = reps.shape[2]
     tiles = -(-T // _TILE)
@@ -119,38 +123,44 @@ def select_chunks(query: torch.Tensor, reps: torch.Tensor, lengths: torch.Tensor
     args = _lib.HisaSelectArgs(version=_lib.ABI_VERSION, head_dim=D, chunk_size=_CHUNK, selector_tile=_TILE,
                                top_k=int(top_k), B=B, H=H, T=T, query=query.data_ptr(), reps=reps.data_ptr(),
                                lengths=lengths.data_ptr(), temperature=float(temperature),
-                               top_chunk_idx=top.data_ptr(), logits=None if logits is None else logits.data_ptr())
+                               top_chunk_idx=top.data_ptr(), logits=None if logits is None else logits.data_ptr(),
+                               tile_begin=int(tile_begin), tile_count=int(tile_count))
     args.sqb, args.sqh, args.sqn = _strides3(query)
     _lib.call("dwarf_hisa_select", args, query.device)
     return top, logits
 
 
-def route_prior(query, reps, top, route_scale) -> torch.Tensor:
+def route_prior(query, reps, top, route_scale, *, tile_begin: int = 0, tile_count: int = 0) -> torch.Tensor:
     """``dwarf_hisa_route``: bf16 route prior [B,H,T,4] of the selected chunks."""
     B, H, T, D = query.shape
     route = torch.empty(B, H, T, _MAX_TOP_K, dtype=torch.bfloat16, device=query.device)
     args = _lib.HisaRouteArgs(version=_lib.ABI_VERSION, head_dim=D, selector_tile=_TILE, k_slots=top.shape[-1],
                               B=B, H=H, T=T, C=reps.shape[2], query=query.data_ptr(), reps=reps.data_ptr(),
                               top_chunk_idx=top.data_ptr(), route_scale=route_scale.data_ptr(),
-                              route=route.data_ptr())
+                              route=route.data_ptr(), tile_begin=int(tile_begin), tile_count=int(tile_count))
     args.sqb, args.sqh, args.sqn = _strides3(query)
     _lib.call("dwarf_hisa_route", args, query.device)
     return route
 
 
 def tile_attention(query, local_key, local_value, global_key, global_value, reps, top, route_scale, lengths, *,
-                   out: torch.Tensor | None = None, want_route: bool = False):
-    """``dwarf_hisa_route`` + ``dwarf_hisa_attn``: route prior, then local window + routed chunks."""
+                   out: torch.Tensor | None = None, want_route: bool = False, tile_begin: int = 0,
+                   tile_count: int = 0):
+    """``dwarf_hisa_route`` + ``dwarf_hisa_attn``: route prior, then local window + routed chunks.
+
+    ``tile_begin``/``tile_count`` restrict both launches to the query rows of those selector
+    tiles (count 0: every tile); ``out`` rows of other tiles are left untouched."""
     B, H, T, D = query.shape
     if out is None:
         out = torch.empty(B, H, T, D, dtype=torch.bfloat16, device=query.device)
-    route = route_prior(query, reps, top, route_scale)
+    route = route_prior(query, reps, top, route_scale, tile_begin=tile_begin, tile_count=tile_count)
     args = _lib.HisaAttnArgs(version=_lib.ABI_VERSION, head_dim=D, chunk_size=_CHUNK, selector_tile=_TILE,
                              local_window=_WINDOW, k_slots=top.shape[-1], B=B, H=H, T=T,
                              query=query.data_ptr(), local_key=local_key.data_ptr(),
                              local_value=local_value.data_ptr(), global_key=global_key.data_ptr(),
                              global_value=global_value.data_ptr(), top_chunk_idx=top.data_ptr(),
-                             route=route.data_ptr(), lengths=lengths.data_ptr(), out=out.data_ptr())
+                             route=route.data_ptr(), lengths=lengths.data_ptr(), out=out.data_ptr(),
+                             tile_begin=int(tile_begin), tile_count=int(tile_count))
     args.sqb, args.sqh, args.sqn = _strides3(query)
     args.slkb, args.slkh, args.slkn = _strides3(local_key)
     args.slvb, args.slvh, args.slvn = _strides3(local_value)
@@ -460,6 +470,45 @@ class HierarchicalSparseAttentionV16HISACausal(nn.Module):
                        out=_to_heads(attended, B, T, self.H, self.hd))
         self._last_token_selection_path = "enumerate_all"
         return F.linear(attended, self.W_o.weight.to(act)), gate, top
+
+    def forward_parts_cached(self, x: torch.Tensor, kv_inject, cache, row: int):
+        """``forward_parts`` for positions [row, row + T) of ``x`` [B,T,D] over a cache.
+
+        ``cache`` = (query, local_key, local_value, global_key, global_value), bf16
+        [B,H,L,64] buffers holding positions [0, row); the new rows are written there
+        first. Every sequence is row + T long, so the router's chunk representatives
+        are rebuilt at that length and only the selector tiles holding the new rows
+        are selected, routed and attended (a partially filled tile is selected from
+        its present queries, exactly as a prefill of row + T tokens selects it).
+        Returns (W_o(attended) [B,T,D], content-gate logits [B,T,D]).
+        """
+        self._check_supported()
+        B, T, _ = x.shape
+        act = torch.bfloat16
+        xb = x if x.dtype == act else x.to(act)
+        qkvg = F.linear(xb, self.qkvg_proj.weight.to(act), self.qkvg_proj.bias.to(act))
+        q, k, v, gate = qkvg.split(self.D, dim=-1)
+        query = _to_heads(q, B, T, self.H, self.hd)
+        local_key = _to_heads(k, B, T, self.H, self.hd)
+        local_value = _to_heads(v, B, T, self.H, self.hd)
+        global_key, global_value = self.global_kv(xb, local_key, local_value, kv_inject)
+        seq_len = row + T
+        if seq_len > cache[0].shape[2]:
+            raise ValueError(f"rows [{row}, {seq_len}) exceed the cache length {cache[0].shape[2]}")
+        for buf, new in zip(cache, (query, local_key, local_value, global_key, global_value)):
+            buf[:, :, row:seq_len].copy_(new)
+        cq, clk, clv, cgk, cgv = (buf[:, :, :seq_len] for buf in cache)
+        lengths = torch.full((B,), seq_len, dtype=torch.int32, device=x.device)
+        tile0 = row // _TILE
+        tiles = -(-seq_len // _TILE) - tile0
+        reps = chunk_representatives(cgk, lengths, blend_alpha=self._blend_alpha)
+        top, _ = select_chunks(cq, reps, lengths, top_k=self.top_k_chunks, temperature=self.temperature,
+                               tile_begin=tile0, tile_count=tiles)
+        scale = self.route_prior_scale.detach().float().contiguous()
+        attended = torch.empty(B, seq_len, self.D, dtype=act, device=x.device)
+        tile_attention(cq, clk, clv, cgk, cgv, reps, top, scale, lengths,
+                       out=_to_heads(attended, B, seq_len, self.H, self.hd), tile_begin=tile0, tile_count=tiles)
+        return F.linear(attended[:, row:], self.W_o.weight.to(act)), gate
 
     def forward(self, x: torch.Tensor, kv_inject=None, *, valid_lengths=None, return_metadata: bool = False,
                 return_auxiliary: bool = False):

@@ -189,10 +189,20 @@ class InterferencePacket(nn.Module):
             self._const_key = key
         return self._const
 
-    def forward(self, normalized: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    def forward(self, normalized: torch.Tensor, ema_states: list | None = None):
+        """(key_delta, value_delta) [B,H,T,hd]. With ``ema_states`` (one fp32 [B,D] state per
+        timescale, or None entries for a zero start) the scans continue from those states and
+        the list is updated in place with the states after the last token."""
         x = _act(normalized)
         factors, mixture = self._constants()
-        scans = [causal_ema_scan(x, f.reshape(1)) for f in factors]
+        if ema_states is None:
+            scans = [causal_ema_scan(x, f.reshape(1)) for f in factors]
+        else:
+            scans = []
+            for i, f in enumerate(factors):
+                scan, ema_states[i] = causal_ema_scan(x, f.reshape(1), initial_state=ema_states[i],
+                                                      return_final_state=True)
+                scans.append(scan)
         gate_pre = F.linear(x, _act(self.gate_proj.weight), _act(self.gate_proj.bias))
         packet = glue.packet(scans, mixture, gate_pre)
         kv = F.linear(packet, _act(self.kv_proj.weight))
@@ -249,6 +259,21 @@ class GlobalMixerBlock(nn.Module):
         x, n2 = glue.add_rmsnorm(_act(x), self.norm2.weight.detach(), addend=attended)
         x, _ = glue.add_rmsnorm(x, self.norm2.weight.detach(), addend=self.ffn(n2))
         return x, auxiliary
+
+
+@dataclass
+class DecodeState:
+    """Per-sequence caches of an incremental decode, ``length`` positions filled.
+
+    ``layers[i]`` for a DSQG block: the q6 cache (y, z, k_codes, k_scales, v_codes,
+    v_scales) of ``max_len`` positions per (batch, head); for the HISA block:
+    ((query, local_key, local_value, global_key, global_value) bf16 [B,H,max_len,64],
+    the packet's fp32 EMA states [B,D] per timescale)."""
+
+    batch: int
+    max_len: int
+    length: int
+    layers: list
 
 
 class DwarfForCausalLM(nn.Module):
@@ -342,6 +367,70 @@ class DwarfForCausalLM(nn.Module):
                 x, n2 = glue.add_rmsnorm(x, block.norm2.weight.detach(), addend=block.attn(n))
             x, n = block.ffn.forward_add_rmsnorm(n2, x, next_norm.detach())
         return (n, auxiliary) if return_auxiliary else n
+
+    # ------------------------------------------------------------------ incremental decoding
+
+    def new_decode_state(self, batch: int, max_len: int | None = None, device=None) -> "DecodeState":
+        """Empty per-layer caches for ``batch`` sequences of up to ``max_len`` tokens."""
+        if self.kv_cache != "q6":
+            raise NotImplementedError("incremental decoding runs on the q6 KV cache (kv_cache='q6')")
+        config = self.config
+        max_len = int(max_len or config.model_length)
+        device = torch.device(device) if device is not None else self.embedding.weight.device
+        H, hd = config.num_heads, config.embedding_dim // config.num_heads
+        layers: list = []
+        for block in self.blocks:
+            if isinstance(block, GlobalMixerBlock):
+                kv = tuple(torch.empty(batch, H, max_len, hd, dtype=torch.bfloat16, device=device) for _ in range(5))
+                layers.append((kv, [None] * len(config.ema_timescales)))
+            else:
+                probes = torch.empty(batch, H, max_len, 4, dtype=torch.float32, device=device)
+                codes = torch.empty(batch, H, max_len, 48, dtype=torch.uint8, device=device)
+                scales = torch.empty(batch, H, max_len, dtype=torch.float16, device=device)
+                layers.append((probes, torch.empty_like(probes), codes, scales, torch.empty_like(codes),
+                               torch.empty_like(scales)))
+        return DecodeState(batch=batch, max_len=max_len, length=0, layers=layers)
+
+    def forward_cached(self, input_ids: torch.Tensor, state: "DecodeState") -> torch.Tensor:
+        """Final RMSNorm'd hidden states [B,T,D] of the T tokens following ``state.length``
+        cached positions; appends their caches and advances ``state.length`` by T."""
+        self._check(input_ids)
+        B, T = input_ids.shape
+        if B != state.batch:
+            raise ValueError(f"state holds {state.batch} sequences, input_ids {B}")
+        row = state.length
+        if row + T > state.max_len:
+            raise ValueError(f"{row} cached + {T} new tokens exceed the state's max_len {state.max_len}")
+        emb = _act(self.embedding.weight.detach()).contiguous()
+        blocks = list(self.blocks)
+        x, n = glue.embed_rmsnorm(input_ids, emb, blocks[0].norm1.weight.detach())
+        for i, block in enumerate(blocks):
+            next_norm = blocks[i + 1].norm1.weight if i + 1 < len(blocks) else self.norm.weight
+            layer = state.layers[i]
+            if isinstance(block, GlobalMixerBlock):
+                kv_cache, ema_states = layer
+                kd, vd = block.packet(n, ema_states)
+                projected, gate = block.attn.forward_parts_cached(n, (kd, vd), kv_cache, row)
+                x, n2 = glue.add_rmsnorm(x, block.norm2.weight.detach(), addend=projected, gate=gate)
+            else:
+                x, n2 = glue.add_rmsnorm(x, block.norm2.weight.detach(),
+                                         addend=block.attn.forward_cached(n, layer, row))
+            x, n = block.ffn.forward_add_rmsnorm(n2, x, next_norm.detach())
+        state.length = row + T
+        return n
+
+    def prefill(self, input_ids: torch.Tensor, max_len: int | None = None) -> tuple[torch.Tensor, "DecodeState"]:
+        """Prefill ``input_ids`` [B,T] into a new decode state; returns (logits of the last
+        token [B,V], state)."""
+        state = self.new_decode_state(input_ids.shape[0], max_len, input_ids.device)
+        hidden = self.forward_cached(input_ids, state)
+        return gemm.linear(hidden[:, -1].contiguous(), _act(self.embedding.weight.detach())), state
+
+    def decode_step(self, state: "DecodeState", token_ids: torch.Tensor) -> torch.Tensor:
+        """One incremental step: ``token_ids`` [B] at position ``state.length``; returns its
+        logits [B,V] (those of a prefill over the ``state.length + 1`` tokens at its last row)."""
+        hidden = self.forward_cached(token_ids.reshape(-1, 1), state)
+        return gemm.linear(hidden[:, 0].contiguous(), _act(self.embedding.weight.detach()))
 
     def forward(self, input_ids: torch.Tensor, *, return_hidden: bool = False, return_auxiliary: bool = False):
         hidden, auxiliary = self.forward_hidden(input_ids, return_auxiliary=True)

@@ -89,6 +89,9 @@ typedef struct {
   void* workspace;            /* dwarf_ema_scan_workspace_bytes() bytes     */
   int64_t workspace_bytes;
   int32_t* device_status;     /* optional; set to DWARF_DEVICE_TIMEOUT      */
+  const float* init_state;    /* optional fp32 [batch, width]: y[-1] (else 0) */
+  float* final_state;         /* optional fp32 [batch, width]: the fp32 state
+                                 after token seq_len-1 (may not alias init)  */
 } dwarf_ema_scan_args;
 
 int64_t dwarf_ema_scan_workspace_bytes(int64_t batch, int64_t seq_len, int64_t width,
@@ -231,6 +234,9 @@ typedef struct {
   const void* gate;               /* optional bf16 [B, N, H*64] view      */
   int64_t sgb_, sgn_;             /* element strides (b, n); h*64+d is +1 */
   int32_t* device_status;         /* optional; set to DWARF_DEVICE_TIMEOUT */
+  int64_t row_begin;              /* compute queries [row_begin, N) only; q,
+                                     y_pre, gate, out and lse rows are then
+                                     relative to row_begin (decode: N-1)  */
 } dwarf_dsqg_fwd_args;
 
 int dwarf_dsqg_fwd(const dwarf_dsqg_fwd_args* args, void* stream);
@@ -336,6 +342,8 @@ typedef struct {
   float temperature;
   int32_t* top_chunk_idx;         /* [B, H, ceil(T/16), min(top_k, C)]    */
   float* logits;                  /* optional [B, H, tiles, C] (masked)   */
+  int64_t tile_begin, tile_count; /* tiles computed (count 0: all from begin;
+                                     0, 0 = every tile); decode: one tile */
 } dwarf_hisa_select_args;
 
 /* Route prior of the selected chunks (_selected_route_scores :418-468):
@@ -353,6 +361,7 @@ typedef struct {
   const int32_t* top_chunk_idx;     /* [B, H, tiles, k_slots]             */
   const float* route_scale;         /* [H] = softplus(route_prior_raw)    */
   void* route;                      /* bf16 [B, H, T, 4] contiguous       */
+  int64_t tile_begin, tile_count;   /* as dwarf_hisa_select_args          */
 } dwarf_hisa_route_args;
 
 /* Fused tile attention: for each query n of tile t, one softmax over
@@ -375,6 +384,7 @@ typedef struct {
   const void* route;              /* bf16 [B, H, T, 4] (dwarf_hisa_route) */
   const int32_t* lengths;
   void* out;                int64_t sob, soh, son;   /* bf16              */
+  int64_t tile_begin, tile_count; /* as dwarf_hisa_select_args            */
 } dwarf_hisa_attn_args;
 
 int dwarf_hisa_reps(const dwarf_hisa_reps_args* args, void* stream);
@@ -516,6 +526,10 @@ typedef struct {
   uint16_t* k_scales;             /* epilogue 3: [B, heads, T]             */
   uint8_t* v_codes;
   uint16_t* v_scales;
+  int64_t cache_len;              /* epilogue 3: rows per (b, h) of y_pre,
+                                     z_pre and the q6 cache (0: T); with the
+                                     pointers offset by the first row, a
+                                     decode step appends into longer caches */
 } dwarf_gemm_args;
 
 int dwarf_gemm_bf16(const dwarf_gemm_args* args, void* stream);

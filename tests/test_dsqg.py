@@ -348,3 +348,30 @@ def test_resident_q6_kernel_fused_gain_gate_matches_gather(monkeypatch):
     out, _, _ = _run_q6(c, offs, js, 2, 0, "resident", monkeypatch, gain=gain, gate=gate)
     gout, _, _ = _run_q6(c, offs, js, 2, 0, "gather", monkeypatch, gain=gain, gate=gate)
     _assert_close(out.float().cpu().numpy(), gout.float().cpu().numpy(), tol=2e-2, mean_rel=5e-3)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("N,row_begin", [(300, 299), (300, 128), (2048, 2047), (2048, 1000)])
+def test_row_window_matches_full_launch(N, row_begin, monkeypatch):
+    """row_begin: queries [row_begin, N) over the full q6 cache, with q/y/out/lse rows
+    relative to row_begin, reproduce the full launch's rows (the decode step's launch)."""
+    from dwarf_v2_b200.dsqg_attention_v22 import _dsqg_launch, _prepare_tables
+
+    c, offs, js = _resident_case(1, 4, 2, N, seed=N + row_begin)
+    out, lse, (kc, ks, vc, vs) = _run_q6(c, offs, js, 6, 0, "gather", monkeypatch)
+    d = {k: v.cuda() for k, v in c.items()}
+    J = len(offs)
+    offs_t = torch.tensor(offs, dtype=torch.int32, device="cuda")
+    pb, se, pbase, pgain, y32, z32, o = _prepare_tables(d["pos_bias"], d["scale_embed"], d["phase_base"],
+                                                        d["phase_gain"], d["y_pre"], d["z_pre"], offs_t,
+                                                        d["q"].device, J, J - js)
+    rows = N - row_begin
+    w_out = torch.empty(1, 4, rows, 64, dtype=torch.bfloat16, device="cuda")
+    w_lse = torch.empty(1, 4, rows, dtype=torch.float32, device="cuda")
+    _dsqg_launch(d["q"][:, :, row_begin:].contiguous(), kv=("q6", kc, ks, vc, vs), pos_bias=pb, scale_embed=se,
+                 phase_base=pbase, phase_gain=pgain, y_pre=y32[:, :, row_begin:].contiguous(), z_pre=z32,
+                 offsets=o, j_small=js, j_large=J - js, plane_shift=6, query_start=0, out=w_out, lse=w_lse,
+                 seq_len=N, row_begin=row_begin)
+    torch.cuda.synchronize()
+    torch.testing.assert_close(w_out.float(), out[:, :, row_begin:].float(), atol=2e-2, rtol=2e-2)
+    torch.testing.assert_close(w_lse, lse[:, :, row_begin:], atol=1e-4, rtol=0)

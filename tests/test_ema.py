@@ -155,3 +155,22 @@ def test_kernel_causality_and_repeatability():
     y2 = causal_ema_scan(x2, a)
     assert torch.equal(y1[:, :700], y2[:, :700])
     assert torch.equal(y1, causal_ema_scan(x, a))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("split", [1, 37, 1024, 1499])
+def test_kernel_continuation_matches_one_pass(split):
+    """initial_state/final_state: scanning [0,split) then [split,N) from the carried
+    state reproduces the single pass (the decode path's EMA continuation)."""
+    from dwarf_v2_b200.causal_ema_scan import causal_ema_scan
+
+    g = torch.Generator().manual_seed(5)
+    x = torch.randn(2, 1500, 256, generator=g).cuda()
+    a = torch.tensor([0.07], device="cuda")
+    full, full_state = causal_ema_scan(x, a, return_final_state=True)
+    head, state = causal_ema_scan(x[:, :split].contiguous(), a, return_final_state=True)
+    tail, end_state = causal_ema_scan(x[:, split:].contiguous(), a, initial_state=state,
+                                      return_final_state=True)
+    torch.testing.assert_close(state, full[:, split - 1].float(), atol=1e-6, rtol=0)
+    torch.testing.assert_close(torch.cat([head, tail], 1), full, atol=1e-5, rtol=0)
+    torch.testing.assert_close(end_state, full_state, atol=1e-5, rtol=0)

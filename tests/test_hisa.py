@@ -153,3 +153,33 @@ def test_module_matches_reference_module():
         y = module(g["x"].to(torch.bfloat16).cuda(),
                    kv_inject=(g["key_delta"].to(torch.bfloat16).cuda(), g["value_delta"].to(torch.bfloat16).cuda()))
     _close(y.float().cpu().numpy(), f(g["y"]), tol=2e-2, mean_rel=3e-2)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("T,tile_begin,tile_count", [(2048, 127, 1), (1000, 40, 3), (333, 20, 1), (64, 0, 0)])
+def test_tile_window_matches_full_launch(T, tile_begin, tile_count):
+    """select/route/attn restricted to selector tiles [tile_begin, +count) reproduce the
+    full launch's rows there and leave every other output row untouched."""
+    from dwarf_v2_b200.hierarchical_sparse_attn_v18_hisa import (chunk_representatives, select_chunks,
+                                                                 tile_attention)
+
+    gen = torch.Generator().manual_seed(T + tile_begin)
+    B, H = 2, 4
+    q, lk, lv, gk, gv = ((torch.randn(B, H, T, 64, generator=gen) * 0.3).to(torch.bfloat16).cuda()
+                         for _ in range(5))
+    lengths = torch.tensor([T, max(1, T - 37)], dtype=torch.int32, device="cuda")
+    scale = torch.full((H,), 0.1, device="cuda")
+    reps = chunk_representatives(gk, lengths, blend_alpha=0.5)
+    top, _ = select_chunks(q, reps, lengths, top_k=4, temperature=1.0)
+    ref, _ = tile_attention(q, lk, lv, gk, gv, reps, top, scale, lengths)
+    wtop, _ = select_chunks(q, reps, lengths, top_k=4, temperature=1.0, tile_begin=tile_begin,
+                            tile_count=tile_count)
+    out = torch.full_like(ref, 7.0)
+    tile_attention(q, lk, lv, gk, gv, reps, wtop, scale, lengths, out=out, tile_begin=tile_begin,
+                   tile_count=tile_count)
+    torch.cuda.synchronize()
+    t_end = -(-T // 16) if tile_count == 0 else tile_begin + tile_count
+    r0, r1 = 16 * tile_begin, min(T, 16 * t_end)
+    assert torch.equal(wtop[:, :, tile_begin:t_end], top[:, :, tile_begin:t_end])
+    assert torch.equal(out[:, :, r0:r1], ref[:, :, r0:r1])
+    assert torch.all(out[:, :, :r0] == 7.0) and torch.all(out[:, :, r1:] == 7.0)
