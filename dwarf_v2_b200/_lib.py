@@ -241,11 +241,17 @@ class GemmArgs(ctypes.Structure):
         bias:ptr, bias_dtype:i32, swiglu_tile:i32, out:ptr, ldo:i64, device_status:ptr,
         resid:ptr, ldr:i64, norm_w:ptr, norm_w_dtype:i32, eps:f32, n_out:ptr, ldn:i64,
         T:i64, heads:i32, q_probe:ptr, k_probe:ptr, y_pre:ptr, z_pre:ptr, k_codes:ptr, k_scales:ptr,
-        v_codes:ptr, v_scales:ptr, cache_len:i64""")
+        v_codes:ptr, v_scales:ptr, cache_len:i64, lse_part:ptr, arg_part:ptr, targets:ptr, target_logit:ptr""")
+
+
+class LseReduceArgs(ctypes.Structure):
+    _fields_ = _fields("""version:i32, M:i64, parts:i64, vocab:i64, lse_part:ptr, arg_part:ptr, targets:ptr,
+        target_logit:ptr, ignore_index:i64, lse:ptr, argmax:ptr, loss:ptr""")
 
 
 _ENTRY_POINTS = {
     "dwarf_gemm_bf16": GemmArgs,
+    "dwarf_lse_reduce": LseReduceArgs,
     "dwarf_hisa_reps": HisaRepsArgs,
     "dwarf_hisa_select": HisaSelectArgs,
     "dwarf_hisa_attn": HisaAttnArgs,

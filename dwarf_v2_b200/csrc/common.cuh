@@ -51,6 +51,13 @@ __device__ __forceinline__ __nv_bfloat16 f32_to_bf16(float v) { return __float2b
 
 __device__ __forceinline__ float round_bf16(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
 
+// 2^x on the SFU (ex2.approx; results below 2^-126 flush to zero, 2^-inf = 0).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // Vector load/store of VEC consecutive elements as fp32.
 template <typename T, int VEC>
 struct VecIO;

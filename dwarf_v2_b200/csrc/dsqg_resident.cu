@@ -102,13 +102,8 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
 
 __device__ __forceinline__ float den(uint32_t bits) { return __uint_as_float(bits); }
 
-// 2^x on the SFU (arguments here are <= 8; results below 2^-126 flush to 0,
-// which only drops weights far below the running maximum).
-__device__ __forceinline__ float ex2_approx(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
+// ex2_approx (common.cuh): arguments here are <= 8; results below 2^-126
+// flush to 0, which only drops weights far below the running maximum.
 
 // sum_i q[i] * u_i * 2^(K_i - 149) over the 16 fields of a flipped slice,
 // q[i] pre-scaled by 2^(E - K_i): = 2^(E - 149) * sum_i q_i u_i.

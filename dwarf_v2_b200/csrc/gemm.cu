@@ -39,7 +39,8 @@ enum : int {
   kEpiStore = DWARF_GEMM_STORE,
   kEpiSwiglu = DWARF_GEMM_SWIGLU,
   kEpiRmsNorm = DWARF_GEMM_RESID_RMSNORM,
-  kEpiQkvg = DWARF_GEMM_QKVG_PREP
+  kEpiQkvg = DWARF_GEMM_QKVG_PREP,
+  kEpiLse = DWARF_GEMM_LSE
 };
 
 struct GemmEpi {
@@ -65,6 +66,11 @@ struct GemmEpi {
   uint16_t* k_scales;
   uint8_t* v_codes;
   uint16_t* v_scales;
+  // lm_head logsumexp / argmax epilogue
+  float2* lse_part;
+  float2* arg_part;
+  const int64_t* targets;
+  float* target_logit;
 };
 
 __device__ __forceinline__ uint32_t s32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -702,6 +708,55 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
             (sec == 1 ? epi.k_scales : epi.v_scales)[hrow] = __half_as_ushort(sh);
           }
         }
+      } else if constexpr (EPI == kEpiLse) {
+        // Online logsumexp and first-index argmax of this row's bf16-rounded
+        // logits over the warp's half of the tile, 64 columns at a time, one
+        // partial per (row, 128 columns): no exchange between the warps.
+        constexpr int CW = BN / 2;
+        constexpr float kLog2e = 1.4426950408889634f;
+        const int row = m0 + quarter * 32 + lane;
+        const int64_t tgt = (epi.targets != nullptr && row < M) ? epi.targets[row] : -1;
+        float mx = -INFINITY, sm = 0.0f, best = -INFINITY;
+        int bidx = 0;
+#pragma unroll 1
+        for (int c = half * CW; c < (half + 1) * CW; c += 64) {
+          float v[64];
+          tmem_ld64(tbase + c, v);
+          if (c + 64 == (half + 1) * CW) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) release_acc(bar_tempty + 8 * a);
+          }
+          float cm = -INFINITY;
+          int ci = 0;
+#pragma unroll
+          for (int j = 0; j < 64; ++j) {
+            v[j] = round_bf16(v[j]);
+            if (v[j] > cm) { cm = v[j]; ci = j; }
+          }
+          if (cm > best) { best = cm; bidx = n0 + c + ci; }
+          const float nm = fmaxf(mx, cm), nms = nm * kLog2e;
+          float acc0 = 0.0f, acc1 = 0.0f;
+#pragma unroll
+          for (int j = 0; j < 64; j += 2) {
+            acc0 += ex2_approx(fmaf(v[j], kLog2e, -nms));
+            acc1 += ex2_approx(fmaf(v[j + 1], kLog2e, -nms));
+          }
+          sm = sm * ex2_approx((mx - nm) * kLog2e) + (acc0 + acc1);
+          mx = nm;
+          if (tgt >= n0 + c && tgt < n0 + c + 64) {
+            const int k = (int)(tgt - n0 - c);
+            float tv = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 64; ++j) tv = j == k ? v[j] : tv;
+            epi.target_logit[row] = tv;
+          }
+        }
+        if (row < M) {
+          const int64_t slot = ((int64_t)row * tiles_n + (t % tiles_n)) * 2 + half;
+          epi.lse_part[slot] = make_float2(mx, sm);
+          epi.arg_part[slot] = make_float2(best, __int_as_float(bidx));
+        }
       } else if constexpr (EPI == kEpiStore) {
         // 64-column chunks: TMEM -> registers (+bias) -> bf16 rows in this
         // warp's 128-byte-swizzled staging box -> one TMA store of 32 x 64.
@@ -816,8 +871,9 @@ int launch_gemm_impl(const dwarf_gemm_args* a, const GemmEpi& epi, cudaStream_t 
     return DWARF_ERR_LAUNCH;
   CUtensorMap mn = ma;
   // Output boxes of 32 rows x 64 columns (epilogues 0, 2 and 3).
-  if (EPI != kEpiSwiglu && !make_map(&mo, a->out, a->M, a->N, a->ldo, 32, 64)) return DWARF_ERR_LAUNCH;
-  if (EPI == kEpiSwiglu) mo = ma;
+  if (EPI != kEpiSwiglu && EPI != kEpiLse && !make_map(&mo, a->out, a->M, a->N, a->ldo, 32, 64))
+    return DWARF_ERR_LAUNCH;
+  if (EPI == kEpiSwiglu || EPI == kEpiLse) mo = ma;  // unused
   if (EPI == kEpiRmsNorm && !make_map(&mn, a->n_out, a->M, a->N, a->ldn, 32, 64)) return DWARF_ERR_LAUNCH;
   constexpr size_t smem = gemm_smem_bytes<BN, EPI, CTAS>();
   auto kernel = gemm_bf16_kernel<BN, EPI, CTAS>;
@@ -862,20 +918,30 @@ using namespace dwarf;
 
 extern "C" int dwarf_gemm_bf16(const dwarf_gemm_args* a, void* stream) {
   DWARF_CHECK_VERSION(a);
-  if (a->epilogue < DWARF_GEMM_STORE || a->epilogue > DWARF_GEMM_QKVG_PREP) return DWARF_ERR_VALUE;
+  if (a->epilogue < DWARF_GEMM_STORE || a->epilogue > DWARF_GEMM_LSE) return DWARF_ERR_VALUE;
   if (a->M < 0 || a->N <= 0 || a->K <= 0 || a->K % 8 != 0) return DWARF_ERR_SHAPE;
   if (a->M > 0x7fffffffLL || a->N > 0x7fffffffLL || a->K > 0x7fffffffLL) return DWARF_ERR_SHAPE;
   if (a->M == 0) return DWARF_OK;
-  if (!a->a || !a->b || !a->out) return DWARF_ERR_NULL;
-  if (!al16(a->a) || !al16(a->b) || !al16(a->out) || a->lda % 8 || a->ldb % 8 || a->ldo % 8 || a->lda < a->K ||
-      a->ldb < a->K)
+  const bool lse = a->epilogue == DWARF_GEMM_LSE;  // writes partials, not out
+  if (!a->a || !a->b || (!lse && !a->out)) return DWARF_ERR_NULL;
+  if (!al16(a->a) || !al16(a->b) || a->lda % 8 || a->ldb % 8 || a->lda < a->K || a->ldb < a->K ||
+      (!lse && (!al16(a->out) || a->ldo % 8)))
     return DWARF_ERR_ALIGN;
   if (a->bias != nullptr && a->bias_dtype != DWARF_F32 && a->bias_dtype != DWARF_BF16) return DWARF_ERR_DTYPE;
   GemmEpi epi{a->bias, a->bias_dtype == DWARF_BF16, (__nv_bfloat16*)a->out, a->ldo, a->device_status,
               (const __nv_bfloat16*)a->resid, a->ldr, a->norm_w, a->norm_w_dtype == DWARF_BF16, a->eps,
               (int)a->T, a->heads, a->cache_len > 0 ? a->cache_len : a->T, a->q_probe, a->k_probe, a->y_pre,
-              a->z_pre, a->k_codes, a->k_scales, a->v_codes, a->v_scales};
+              a->z_pre, a->k_codes, a->k_scales, a->v_codes, a->v_scales, (float2*)a->lse_part,
+              (float2*)a->arg_part, a->targets, a->target_logit};
   cudaStream_t st = (cudaStream_t)stream;
+  if (lse) {
+    if (a->N % 256 != 0) return DWARF_ERR_SHAPE;
+    if (a->bias != nullptr) return DWARF_ERR_VALUE;
+    if (!a->lse_part || !a->arg_part || (a->targets && !a->target_logit)) return DWARF_ERR_NULL;
+    if ((reinterpret_cast<uintptr_t>(a->lse_part) | reinterpret_cast<uintptr_t>(a->arg_part)) & 7u)
+      return DWARF_ERR_ALIGN;
+    return launch_gemm<256, kEpiLse>(a, epi, st);
+  }
   if (a->epilogue == DWARF_GEMM_QKVG_PREP) {
     if (a->heads <= 0 || a->N != 256LL * a->heads || (64LL * a->heads) % 256 != 0) return DWARF_ERR_SHAPE;
     if (a->T <= 0 || a->M % a->T != 0 || a->T > 0x7fffffffLL) return DWARF_ERR_SHAPE;
@@ -910,4 +976,60 @@ extern "C" int dwarf_gemm_bf16(const dwarf_gemm_args* a, void* stream) {
   if (h == 80) return launch_gemm<160, kEpiSwiglu>(a, epi, st);
   if (h == 64) return launch_gemm<128, kEpiSwiglu>(a, epi, st);
   return DWARF_ERR_SHAPE;
+}
+
+namespace dwarf {
+namespace {
+
+// One warp per row: fold the row's (max, sum) and (max, first index) partials.
+__global__ void __launch_bounds__(256) lse_reduce_kernel(const dwarf_lse_reduce_args a) {
+  const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= a.M) return;
+  constexpr float kLog2e = 1.4426950408889634f;
+  const float2* lp = reinterpret_cast<const float2*>(a.lse_part) + row * a.parts;
+  const float2* ap = reinterpret_cast<const float2*>(a.arg_part) + row * a.parts;
+  float mx = -INFINITY, sm = 0.0f, best = -INFINITY;
+  int bidx = 0x7fffffff;
+  for (int64_t i = lane; i < a.parts; i += 32) {
+    const float2 l = lp[i], g = ap[i];
+    const float nm = fmaxf(mx, l.x);
+    sm = sm * ex2_approx((mx - nm) * kLog2e) + l.y * ex2_approx((l.x - nm) * kLog2e);
+    mx = nm;
+    const int gi = __float_as_int(g.y);
+    if (g.x > best || (g.x == best && gi < bidx)) { best = g.x; bidx = gi; }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float om = __shfl_xor_sync(0xffffffffu, mx, o), os = __shfl_xor_sync(0xffffffffu, sm, o);
+    const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bidx, o);
+    const float nm = fmaxf(mx, om);
+    sm = (mx == -INFINITY ? 0.0f : sm * ex2_approx((mx - nm) * kLog2e)) +
+         (om == -INFINITY ? 0.0f : os * ex2_approx((om - nm) * kLog2e));
+    mx = nm;
+    if (ob > best || (ob == best && oi < bidx)) { best = ob; bidx = oi; }
+  }
+  if (lane != 0) return;
+  const float lse = mx + logf(sm);
+  a.lse[row] = lse;
+  if (a.argmax) a.argmax[row] = bidx;
+  if (a.loss && a.targets) {
+    const int64_t t = a.targets[row];
+    a.loss[row] = t == a.ignore_index ? 0.0f : (t >= 0 && t < a.vocab ? lse - a.target_logit[row] : NAN);
+  }
+}
+
+}  // namespace
+}  // namespace dwarf
+
+extern "C" int dwarf_lse_reduce(const dwarf_lse_reduce_args* a, void* stream) {
+  DWARF_CHECK_VERSION(a);
+  if (a->M < 0 || a->parts <= 0 || a->vocab <= 0) return DWARF_ERR_SHAPE;
+  if (a->M == 0) return DWARF_OK;
+  if (!a->lse_part || !a->arg_part || !a->lse) return DWARF_ERR_NULL;
+  if (a->loss && (!a->targets || !a->target_logit)) return DWARF_ERR_NULL;
+  const unsigned blocks = (unsigned)((a->M + 7) / 8);
+  dwarf::lse_reduce_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(*a);
+  return dwarf::launch_status();
 }

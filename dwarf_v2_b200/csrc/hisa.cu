@@ -204,13 +204,6 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   return *reinterpret_cast<const uint32_t*>(&v);
 }
 
-// 2^x on the SFU (x <= 0 here; results below 2^-126 flush to zero).
-__device__ __forceinline__ float ex2_approx(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-
 // Swizzled [rows][64 bf16] tile: 16-byte chunk c of row r lives at chunk c ^ (r & 7).
 __device__ __forceinline__ uint32_t tile_addr(uint32_t base, int row, int chunk) {
   return base + row * 128 + ((chunk ^ (row & 7)) << 4);

@@ -16,6 +16,7 @@ STORE = 0
 SWIGLU = 1
 RESID_RMSNORM = 2
 QKVG_PREP = 3
+LSE = 4
 SWIGLU_TILES = (128, 80, 64)
 
 
@@ -46,6 +47,52 @@ def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = No
         args.bias, args.bias_dtype = b.data_ptr(), _lib.dtype_code(b.dtype)
     _lib.call("dwarf_gemm_bf16", args, x.device)
     return out
+
+
+def linear_lse(x: torch.Tensor, weight: torch.Tensor, targets: torch.Tensor | None = None, *,
+               ignore_index: int = -100):
+    """Row-wise logsumexp / argmax (/ cross entropy) of ``x @ weight.T`` without the logits.
+
+    The lm_head GEMM's epilogue reduces each row's bf16-rounded logits per
+    128 columns (online max / sum of exp2, first-index argmax, the target's
+    logit); ``dwarf_lse_reduce`` folds the partials. Returns (lse fp32 [M],
+    argmax int64 [M], loss fp32 [M] or None) over the rows of x; ``loss`` is
+    ``lse - logit[target]`` (0 where target == ignore_index).
+    """
+    _lib.require_cuda(x, weight, targets)
+    if x.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16:
+        raise TypeError("linear_lse takes bf16 activations and weights")
+    N, K = weight.shape
+    if N % 256 != 0:
+        raise ValueError(f"linear_lse needs a vocabulary that is a multiple of 256, got {N}")
+    x2, lda = _rows2d(x)
+    w = weight if weight.stride(-1) == 1 else weight.contiguous()
+    M = x2.shape[0]
+    dev = x.device
+    parts = N // 128
+    lse_part = torch.empty(M, parts, 2, dtype=torch.float32, device=dev)
+    arg_part = torch.empty(M, parts, 2, dtype=torch.float32, device=dev)
+    lse = torch.empty(M, dtype=torch.float32, device=dev)
+    argmax = torch.empty(M, dtype=torch.int64, device=dev)
+    args = _lib.GemmArgs(version=_lib.ABI_VERSION, epilogue=LSE, M=M, N=N, K=K, a=x2.data_ptr(), lda=lda,
+                         b=w.data_ptr(), ldb=w.stride(0), lse_part=lse_part.data_ptr(),
+                         arg_part=arg_part.data_ptr())
+    red = _lib.LseReduceArgs(version=_lib.ABI_VERSION, M=M, parts=parts, vocab=N, lse_part=lse_part.data_ptr(),
+                             arg_part=arg_part.data_ptr(), ignore_index=int(ignore_index), lse=lse.data_ptr(),
+                             argmax=argmax.data_ptr())
+    loss = None
+    if targets is not None:
+        t = targets.reshape(-1).to(device=dev, dtype=torch.int64).contiguous()
+        if t.numel() != M:
+            raise ValueError(f"targets must hold one label per row ({M}), got {t.numel()}")
+        target_logit = torch.zeros(M, dtype=torch.float32, device=dev)
+        loss = torch.empty(M, dtype=torch.float32, device=dev)
+        args.targets, args.target_logit = t.data_ptr(), target_logit.data_ptr()
+        red.targets, red.target_logit, red.loss = t.data_ptr(), target_logit.data_ptr(), loss.data_ptr()
+    if M:
+        _lib.call("dwarf_gemm_bf16", args, dev)
+        _lib.call("dwarf_lse_reduce", red, dev)
+    return lse, argmax, loss
 
 
 def swiglu_tile(hidden: int) -> int:

@@ -368,6 +368,16 @@ class DwarfForCausalLM(nn.Module):
             x, n = block.ffn.forward_add_rmsnorm(n2, x, next_norm.detach())
         return (n, auxiliary) if return_auxiliary else n
 
+    def forward_lse(self, input_ids: torch.Tensor, labels: torch.Tensor | None = None):
+        """Per-token (logsumexp, argmax, cross entropy vs ``labels`` or None), each [B, T], from the
+        lm_head GEMM's reducing epilogue: the [B, T, vocab] logits are never written."""
+        hidden = self.forward_hidden(input_ids)
+        B, T, _ = hidden.shape
+        lse, argmax, loss = gemm.linear_lse(hidden, _act(self.embedding.weight.detach()),
+                                            None if labels is None else labels.reshape(-1))
+        shape = (B, T)
+        return lse.view(shape), argmax.view(shape), None if loss is None else loss.view(shape)
+
     # ------------------------------------------------------------------ incremental decoding
 
     def new_decode_state(self, batch: int, max_len: int | None = None, device=None) -> "DecodeState":

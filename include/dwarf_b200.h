@@ -491,6 +491,14 @@ int dwarf_packet(const dwarf_packet_args* args, void* stream);
  *     q and gate columns go to out (bf16, k/v columns are not written),
  *     y_pre / z_pre come from the bf16 q / k rows and K / V are written
  *     only as the q6 cache (dwarf_q6_pack layout, [B, heads, T] rows).
+ *   epilogue 4 (DWARF_GEMM_LSE): lm_head without the logits -- the
+ *     forward of LigerFusedLinearCrossEntropyLoss (train/train_dwarf.py:1084,
+ *     1134-1138). Per row and 128 columns: (max, sum exp(l - max)) of the
+ *     bf16-rounded logits l -> lse_part [M, N/128] float2, (max, index of
+ *     its first occurrence) -> arg_part [M, N/128] float2 (index as int bits),
+ *     and, with targets [M] int64, target_logit[row] = l[targets[row]].
+ *     out is not written (may be NULL); no bias; N % 256 == 0.
+ *     dwarf_lse_reduce folds the partials into per-row lse / argmax / loss.
  * Requirements: K % 8 == 0, 16-byte aligned A/B/out and row strides; N a
  * multiple of the tile width (256 or 128 for epilogue 0, 2*swiglu_tile for
  * epilogue 1 with swiglu_tile in {128, 80, 64}).
@@ -499,6 +507,7 @@ int dwarf_packet(const dwarf_packet_args* args, void* stream);
 #define DWARF_GEMM_SWIGLU 1
 #define DWARF_GEMM_RESID_RMSNORM 2
 #define DWARF_GEMM_QKVG_PREP 3
+#define DWARF_GEMM_LSE 4
 
 typedef struct {
   int32_t version;
@@ -530,9 +539,34 @@ typedef struct {
                                      z_pre and the q6 cache (0: T); with the
                                      pointers offset by the first row, a
                                      decode step appends into longer caches */
+  void* lse_part;                 /* epilogue 4: float2 [M, N/128]         */
+  void* arg_part;                 /* epilogue 4: float2 [M, N/128]         */
+  const int64_t* targets;         /* epilogue 4: optional int64 [M]        */
+  float* target_logit;            /* epilogue 4: [M] (with targets)        */
 } dwarf_gemm_args;
 
 int dwarf_gemm_bf16(const dwarf_gemm_args* args, void* stream);
+
+/* Per-row reduction of DWARF_GEMM_LSE partials (parts = N/128 per row):
+ * lse[row] = log sum exp over the row's logits, argmax[row] = the first
+ * index of its maximum (torch.argmax), and with targets: loss[row] =
+ * lse - target_logit (0 where targets[row] == ignore_index), the per-token
+ * cross entropy Liger's loss averages (train/train_dwarf.py:1134-1138).
+ * Targets outside [0, vocab) other than ignore_index yield loss = NaN. */
+typedef struct {
+  int32_t version;
+  int64_t M, parts, vocab;
+  const void* lse_part;           /* float2 [M, parts]                     */
+  const void* arg_part;           /* float2 [M, parts]                     */
+  const int64_t* targets;         /* optional int64 [M]                    */
+  const float* target_logit;      /* [M] (with targets)                    */
+  int64_t ignore_index;
+  float* lse;                     /* [M]                                   */
+  int64_t* argmax;                /* optional [M]                          */
+  float* loss;                    /* optional [M] (with targets)           */
+} dwarf_lse_reduce_args;
+
+int dwarf_lse_reduce(const dwarf_lse_reduce_args* args, void* stream);
 
 #ifdef __cplusplus
 }
