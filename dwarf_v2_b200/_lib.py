@@ -82,7 +82,9 @@ def ptr(tensor: torch.Tensor | None) -> int | None:
 
 
 def stream_handle(device: torch.device) -> int:
-    return torch.cuda.current_stream(device).cuda_stream
+    """Raw handle of the current stream of ``device`` (what torch.cuda.current_stream returns)."""
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    return torch._C._cuda_getCurrentRawStream(index)
 
 
 def check(status: int, what: str) -> None:
@@ -171,7 +173,7 @@ class DsqgFwdArgs(ctypes.Structure):
         phase_base:ptr, sbj:i64, sbh:i64, phase_gain:ptr, sgj:i64, sgh:i64,
         y_pre:ptr, syb:i64, syh:i64, syn:i64, z_pre:ptr, szb:i64, szh:i64, szn:i64,
         out:ptr, sob:i64, soh:i64, son:i64, lse:ptr, slb:i64, slh:i64, sln:i64,
-        head_gain:ptr, head_gain_dtype:i32, gate:ptr, sgb_:i64, sgn_:i64, device_status:ptr, row_begin:i64""")
+        head_gain:ptr, head_gain_dtype:i32, gate:ptr, sgb_:i64, sgn_:i64, device_status:ptr, row_begin:i64, pos:ptr""")
 
 
 class DsqgPrepArgs(ctypes.Structure):
@@ -188,13 +190,13 @@ class NpciArgs(ctypes.Structure):
 
 class HisaRepsArgs(ctypes.Structure):
     _fields_ = _fields("""version:i32, head_dim:i32, chunk_size:i32, B:i64, H:i64, T:i64, key:ptr,
-        skb:i64, skh:i64, skn:i64, lengths:ptr, blend_alpha:f32, reps:ptr""")
+        skb:i64, skh:i64, skn:i64, lengths:ptr, blend_alpha:f32, reps:ptr, pos:ptr""")
 
 
 class HisaSelectArgs(ctypes.Structure):
     _fields_ = _fields("""version:i32, head_dim:i32, chunk_size:i32, selector_tile:i32, top_k:i32,
         B:i64, H:i64, T:i64, query:ptr, sqb:i64, sqh:i64, sqn:i64, reps:ptr, lengths:ptr, temperature:f32,
-        top_chunk_idx:ptr, logits:ptr, tile_begin:i64, tile_count:i64""")
+        top_chunk_idx:ptr, logits:ptr, tile_begin:i64, tile_count:i64, pos:ptr""")
 
 
 class HisaAttnArgs(ctypes.Structure):
@@ -203,13 +205,13 @@ class HisaAttnArgs(ctypes.Structure):
         query:ptr, sqb:i64, sqh:i64, sqn:i64, local_key:ptr, slkb:i64, slkh:i64, slkn:i64,
         local_value:ptr, slvb:i64, slvh:i64, slvn:i64, global_key:ptr, sgkb:i64, sgkh:i64, sgkn:i64,
         global_value:ptr, sgvb:i64, sgvh:i64, sgvn:i64, top_chunk_idx:ptr, route:ptr,
-        lengths:ptr, out:ptr, sob:i64, soh:i64, son:i64, tile_begin:i64, tile_count:i64""")
+        lengths:ptr, out:ptr, sob:i64, soh:i64, son:i64, tile_begin:i64, tile_count:i64, pos:ptr""")
 
 
 class HisaRouteArgs(ctypes.Structure):
     _fields_ = _fields("""version:i32, head_dim:i32, selector_tile:i32, k_slots:i32, B:i64, H:i64, T:i64, C:i64,
         query:ptr, sqb:i64, sqh:i64, sqn:i64, reps:ptr, top_chunk_idx:ptr, route_scale:ptr, route:ptr,
-        tile_begin:i64, tile_count:i64""")
+        tile_begin:i64, tile_count:i64, pos:ptr""")
 
 
 class AddRmsNormArgs(ctypes.Structure):
@@ -241,7 +243,7 @@ class GemmArgs(ctypes.Structure):
         bias:ptr, bias_dtype:i32, swiglu_tile:i32, out:ptr, ldo:i64, device_status:ptr,
         resid:ptr, ldr:i64, norm_w:ptr, norm_w_dtype:i32, eps:f32, n_out:ptr, ldn:i64,
         T:i64, heads:i32, q_probe:ptr, k_probe:ptr, y_pre:ptr, z_pre:ptr, k_codes:ptr, k_scales:ptr,
-        v_codes:ptr, v_scales:ptr, cache_len:i64, lse_part:ptr, arg_part:ptr, targets:ptr, target_logit:ptr""")
+        v_codes:ptr, v_scales:ptr, cache_len:i64, lse_part:ptr, arg_part:ptr, targets:ptr, target_logit:ptr, pos:ptr""")
 
 
 class LseReduceArgs(ctypes.Structure):

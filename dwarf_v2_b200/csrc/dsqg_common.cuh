@@ -49,6 +49,7 @@ struct DsqgParams {
   int64_t sgtb, sgtn;
   int32_t* status;  // optional device status word (DWARF_DEVICE_TIMEOUT)
   int64_t row_begin;  // first query row computed (gather kernel)
+  const int64_t* pos;  // optional device row_begin (decode kernel)
 };
 
 // 16 bf16 (two 16-B words) -> 16 floats.

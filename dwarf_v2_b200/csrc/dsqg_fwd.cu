@@ -440,6 +440,128 @@ dsqg_fwd_kernel(const DsqgParams p) {
   }
 }
 
+// Decode rows (a few query rows over a long q6 cache): one warp per (query
+// row, head), lane j owning offset j (J <= 32), so the J K/V row gathers of a
+// query are issued at once instead of one after another. Scores, a warp
+// softmax, then every lane's weighted (MOVT-rotated) V row goes through
+// shared memory and lane d sums dims d and d + 32. Same math as
+// dsqg_fwd_kernel up to fp32 summation order.
+constexpr int kDecodeWarps = 4;
+__global__ void __launch_bounds__(32 * kDecodeWarps) dsqg_decode_kernel(const DsqgParams p) {
+  __shared__ float s_v[kDecodeWarps][32][65];
+  __shared__ float s_q[kDecodeWarps][64];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t h = (int64_t)blockIdx.x * kDecodeWarps + warp;
+  if (h >= p.H) return;  // warp-uniform; the kernel has no block-wide barrier
+  const int64_t rb = p.pos != nullptr ? *p.pos : p.row_begin, n = rb + blockIdx.y, b = blockIdx.z;
+  const int64_t hk = h / p.kv_group;
+  const __nv_bfloat16* qrow = p.q + b * p.sqb + h * p.sqh + (n - rb) * p.sqn;
+  s_q[warp][lane] = __bfloat162float(qrow[lane]);
+  s_q[warp][lane + 32] = __bfloat162float(qrow[lane + 32]);
+  __syncwarp();
+  const float* q = s_q[warp];
+
+  const int j = lane;
+  const bool live = j < p.J;
+  const int64_t src = n - (live ? p.offsets[j] : 0);
+  const bool ok = live && src >= 0 && n >= p.query_start;
+  const int64_t srow = ok ? src : 0;
+  float score = -INFINITY;
+  if (ok) {
+    const uint32_t* kw = reinterpret_cast<const uint32_t*>(p.kc + b * p.ccb + hk * p.cch + srow * p.cct);
+    uint32_t w[13];
+#pragma unroll
+    for (int i = 0; i < 12; ++i) w[i] = __ldg(kw + i);
+    w[12] = 0u;
+    const float stepk = __half2float(__ushort_as_half(__ldg(p.ks + b * p.csb + hk * p.csh + srow * p.cst))) *
+                        (1.0f / 31.0f);
+    float d0 = 0.0f, d1 = 0.0f, e0 = 0.0f, e1 = 0.0f;
+    const float* se = p.se + (int64_t)j * p.sej;
+#pragma unroll
+    for (int d = 0; d < 64; ++d) {
+      const int bit = 6 * (d & 15), wd = 3 * (d >> 4) + (bit >> 5);
+      const uint32_t f = __funnelshift_r(w[wd], w[wd + 1], bit & 31) & 63u;
+      const float c = (float)((int)(f << 26) >> 26);
+      const float e = round_bf16(__ldg(se + d * p.sed));
+      if (d & 1) { d1 = fmaf(q[d], c, d1); e1 = fmaf(q[d], e, e1); }
+      else { d0 = fmaf(q[d], c, d0); e0 = fmaf(q[d], e, e0); }
+    }
+    score = ((d0 + d1) * stepk + (e0 + e1)) * 0.125f + __ldg(p.pos_bias + (int64_t)j * p.spj + h * p.sph);
+  }
+  float m = score;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  const float wgt = ok ? exp2f((score - m) * kLog2e) : 0.0f;
+  float l = wgt;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+
+  float* my_v = s_v[warp][lane];
+  if (ok) {
+    const uint32_t* vw = reinterpret_cast<const uint32_t*>(p.vc + b * p.ccb + hk * p.cch + srow * p.cct);
+    uint32_t w[13];
+#pragma unroll
+    for (int i = 0; i < 12; ++i) w[i] = __ldg(vw + i);
+    w[12] = 0u;
+    const float stepv = __half2float(__ushort_as_half(__ldg(p.vs + b * p.csb + hk * p.csh + srow * p.cst))) *
+                        (1.0f / 31.0f);
+    float vv[64];
+#pragma unroll
+    for (int d = 0; d < 64; ++d) {
+      const int bit = 6 * (d & 15), wd = 3 * (d >> 4) + (bit >> 5);
+      const uint32_t f = __funnelshift_r(w[wd], w[wd + 1], bit & 31) & 63u;
+      vv[d] = (float)((int)(f << 26) >> 26) * stepv;
+    }
+#pragma unroll
+    for (int d = 0; d < 64; ++d) my_v[d] = wgt * vv[d];
+    if (j >= p.j_small) {
+      // MOVT: rotate plane r (channels 16r + shift, 16r + shift + 1) of the
+      // weighted row in place (the rotation is linear).
+      const int jl = j - p.j_small;
+      // y_pre rows are absolute positions when row_begin comes from the device.
+      const float* yrow = p.y + b * p.syb + h * p.syh + (p.pos != nullptr ? n : n - rb) * p.syn;
+      const float* zrow = p.z + b * p.szb + hk * p.szh + srow * p.szn;
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const float theta = p.pbase[jl * p.sbj + h * p.sbh + r] + p.pgain[jl * p.sgj + h * p.sgh + r] * yrow[r] * zrow[r];
+        float sn, cs;
+        __sincosf(theta, &sn, &cs);
+        float* pa = my_v + 16 * r + p.plane_shift;
+        const float va = pa[0], vb = pa[1];
+        pa[0] = cs * va - sn * vb;
+        pa[1] = sn * va + cs * vb;
+      }
+    }
+  } else {
+#pragma unroll
+    for (int d = 0; d < 64; ++d) my_v[d] = 0.0f;
+  }
+  __syncwarp();
+  float acc[2] = {0.0f, 0.0f};
+  const int rows = p.J < 32 ? p.J : 32;
+  for (int r = 0; r < rows; ++r) {
+    acc[0] += s_v[warp][r][lane];
+    acc[1] += s_v[warp][r][lane + 32];
+  }
+  float gain = 1.0f;
+  if (p.gain != nullptr)
+    gain = p.gain_bf16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.gain)[h])
+                       : reinterpret_cast<const float*>(p.gain)[h];
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const int d = lane + 32 * k;
+    float o = l > 0.0f ? round_bf16(acc[k] / l) : 0.0f;
+    if (p.gain != nullptr) o = p.gain_bf16 ? round_bf16(o * gain) : o * gain;
+    if (p.gate != nullptr) {
+      const float gv = __bfloat162float(p.gate[b * p.sgtb + (n - rb) * p.sgtn + h * 64 + d]);
+      const float sg = round_bf16(1.0f / (1.0f + expf(-gv)));
+      o = p.gain_bf16 || p.gain == nullptr ? round_bf16(o * sg) : o * sg;
+    }
+    p.out[b * p.sob + h * p.soh + (n - rb) * p.son + d] = __float2bfloat16_rn(o);
+  }
+  if (p.lse != nullptr && lane == 0) p.lse[b * p.slb + h * p.slh + (n - rb) * p.sln] = l > 0.0f ? m + logf(l) : -INFINITY;
+}
+
 template <bool Q6, int TPQ>
 int launch_dsqg(const DsqgParams& p, int64_t B, int64_t H, int64_t N, int J, int j_large, cudaStream_t stream) {
   constexpr int QB = kThreads / TPQ;
@@ -518,6 +640,7 @@ extern "C" int dwarf_dsqg_fwd(const dwarf_dsqg_fwd_args* a, void* stream) {
   p.gate = (const __nv_bfloat16*)a->gate; p.sgtb = a->sgb_; p.sgtn = a->sgn_;
   p.status = a->device_status;
   p.row_begin = a->row_begin;
+  p.pos = a->pos;
 
   // 2 threads per query (32 dims each): half the per-pair bookkeeping of the
   // 4-thread layout. DWARF_DSQG_TPQ=4 selects the 4-thread layout.
@@ -530,9 +653,22 @@ extern "C" int dwarf_dsqg_fwd(const dwarf_dsqg_fwd_args* a, void* stream) {
   // DWARF_DSQG_PATH=gather forces the gather kernel (read on every call).
   if (q6) {
     const char* path = getenv("DWARF_DSQG_PATH");
-    if (!(path && path[0] == 'g') && p.row_begin == 0) {
+    if (!(path && path[0] == 'g') && p.row_begin == 0 && p.pos == nullptr) {
       const int rc = dsqg_resident_launch(p, a->B, st);
       if (rc != kNotApplicable) return rc;
+    }
+  }
+  // A few query rows (decode steps) over a q6 cache: the one-warp-per-row
+  // kernel (the only one that takes a device-side row_begin).
+  const bool decode_shape = q6 && a->J <= 32 && a->N - p.row_begin <= 16;
+  if (p.pos != nullptr && !decode_shape) return DWARF_ERR_VALUE;
+  if (decode_shape) {
+    const char* path = getenv("DWARF_DSQG_PATH");
+    if (p.pos != nullptr || !(path && path[0] == 'g')) {
+      dim3 grid((unsigned)((a->H + kDecodeWarps - 1) / kDecodeWarps), (unsigned)(a->N - p.row_begin), (unsigned)a->B);
+      if (grid.z > 65535) return DWARF_ERR_SHAPE;
+      dsqg_decode_kernel<<<grid, 32 * kDecodeWarps, 0, st>>>(p);
+      return launch_status();
     }
   }
   if (q6) return tpq == 4 ? launch_dsqg<true, 4>(p, a->B, a->H, a->N, a->J, a->j_large, st)

@@ -71,6 +71,7 @@ struct GemmEpi {
   float2* arg_part;
   const int64_t* targets;
   float* target_logit;
+  const int64_t* pos;  // qkvg: optional device row offset of the cache
 };
 
 __device__ __forceinline__ uint32_t s32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -505,6 +506,8 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
     }
     uint32_t tc = 0;
     float ss = 0.0f;  // RMSNorm: running sum of squares of this thread's row slice
+    // qkvg: device-side first cache row (a decode step replayed from a CUDA graph).
+    const int64_t cache_row0 = (EPI == kEpiQkvg && epi.pos != nullptr) ? *epi.pos : 0;
     for (int i = 0;; ++i, ++tc) {
       const int t = tile_at(i);
       if (t >= tiles) break;
@@ -643,7 +646,7 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
           add_bias64(epi.bias, epi.bias_bf16, n0 + c, v);
 #pragma unroll
           for (int i = 0; i < 64; ++i) v[i] = round_bf16(v[i]);
-          const int64_t hrow = ((int64_t)b * epi.heads + head) * epi.cache_len + tt;
+          const int64_t hrow = ((int64_t)b * epi.heads + head) * epi.cache_len + tt + cache_row0;
           if (sec == 0 || sec == 3) {
             if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
             __syncwarp();
@@ -932,7 +935,7 @@ extern "C" int dwarf_gemm_bf16(const dwarf_gemm_args* a, void* stream) {
               (const __nv_bfloat16*)a->resid, a->ldr, a->norm_w, a->norm_w_dtype == DWARF_BF16, a->eps,
               (int)a->T, a->heads, a->cache_len > 0 ? a->cache_len : a->T, a->q_probe, a->k_probe, a->y_pre,
               a->z_pre, a->k_codes, a->k_scales, a->v_codes, a->v_scales, (float2*)a->lse_part,
-              (float2*)a->arg_part, a->targets, a->target_logit};
+              (float2*)a->arg_part, a->targets, a->target_logit, a->pos};
   cudaStream_t st = (cudaStream_t)stream;
   if (lse) {
     if (a->N % 256 != 0) return DWARF_ERR_SHAPE;

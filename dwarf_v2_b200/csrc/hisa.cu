@@ -40,6 +40,7 @@ struct RepsParams {
   __nv_bfloat16* reps;  // [B,H,C,64] contiguous
   int64_t H, T, C;
   float alpha;
+  const int64_t* pos;   // optional: only chunk *pos / 64 (decode step)
 };
 
 // One CTA (64 threads) per (chunk, head, batch).
@@ -49,8 +50,10 @@ __global__ void __launch_bounds__(64) hisa_reps_kernel(const RepsParams p) {
   __shared__ float rep[kHD];
   __shared__ int best_row;
   __shared__ float norm;
-  const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int c = p.pos != nullptr ? (int)(*p.pos / kChunk) : (int)blockIdx.x;
+  const int h = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x;
+  if (c >= p.C) return;
   const int64_t vlen = imin64((int64_t)p.lengths[b], p.T);
   const __nv_bfloat16* base = p.k + b * p.skb + h * p.skh;
   for (int i = tid; i < kChunk * kHD; i += 64) {
@@ -100,6 +103,19 @@ __global__ void __launch_bounds__(64) hisa_reps_kernel(const RepsParams p) {
 
 // ---------------------------------------------------------------- router
 
+// The tile window of a launch: host-given, or [*pos / 16, + tile_count) read
+// from device memory (decode steps replayed from a CUDA graph).
+template <typename P>
+__device__ __forceinline__ void window_of(const P& p, int64_t& tb, int64_t& te) {
+  if (p.pos != nullptr) {
+    tb = *p.pos / kTile;
+    te = imin64(tb + p.tile_count, p.tiles);
+  } else {
+    tb = p.tile_begin;
+    te = p.tile_end;
+  }
+}
+
 struct SelectParams {
   const __nv_bfloat16* q; int64_t sqb, sqh, sqn;
   const __nv_bfloat16* reps;  // [B,H,C,64]
@@ -110,6 +126,8 @@ struct SelectParams {
   int64_t tile_begin, tile_end;  // tiles [tile_begin, tile_end) are computed
   int k_slots;
   float temperature;
+  const int64_t* pos;            // optional: window [*pos/16, +tile_count) (decode step)
+  int64_t tile_count;
 };
 
 // L2-normalise a 64-value row in place: float32 sequential norm, IEEE
@@ -129,14 +147,16 @@ __global__ void __launch_bounds__(256) hisa_select_kernel(const SelectParams p) 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int i = threadIdx.x; i < p.C * kHD; i += blockDim.x)
     reps[i / kHD][i % kHD] = __bfloat162float(p.reps[((b * p.H + h) * p.C) * kHD + i]);
-  const int64_t t = p.tile_begin + (int64_t)blockIdx.x * 8 + warp;
+  int64_t tb, te;
+  window_of(p, tb, te);
+  const int64_t t = tb + (int64_t)blockIdx.x * 8 + warp;
   const int64_t start = t * kTile;
   const int64_t arow = imin64(start, p.T - 1);
   const __nv_bfloat16* qrow = p.q + b * p.sqb + h * p.sqh + arow * p.sqn;
   anchor[warp][lane] = __bfloat162float(qrow[lane]);
   anchor[warp][lane + 32] = __bfloat162float(qrow[lane + 32]);
   __syncthreads();
-  if (t >= p.tile_end) return;
+  if (t >= te) return;
   if (lane == 0) normalize_row_bf16(anchor[warp]);
   __syncwarp();
   const int64_t vlen = p.lengths[b];
@@ -222,6 +242,8 @@ struct AttnParams {
   int64_t H, T, tiles;
   int64_t tile_begin, tile_end;  // tiles [tile_begin, tile_end) are computed
   int64_t grid_begin;            // tile_begin rounded down to the CTA tile grid
+  const int64_t* pos;            // optional: window [*pos/16, +tile_count) (decode step)
+  int64_t tile_count;
   int k_slots;
 };
 
@@ -324,6 +346,8 @@ struct RouteParams {
   int64_t H, T, C, tiles;
   int64_t tile_begin, tile_end;  // tiles [tile_begin, tile_end) are computed
   int k_slots;
+  const int64_t* pos;            // optional: window [*pos/16, +tile_count) (decode step)
+  int64_t tile_count;
 };
 
 // One warp per two 16-query tiles (16 tiles per CTA); each lane owns one query row.
@@ -333,8 +357,10 @@ __global__ void __launch_bounds__(256) hisa_route_kernel(const RouteParams p) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int h = blockIdx.y, b = blockIdx.z;
   const int lt = warp * 2 + (lane >> 4);  // local tile of this lane's row
-  const int64_t t = p.tile_begin + (int64_t)blockIdx.x * 16 + lt;
-  const bool tile_ok = t < p.tile_end;
+  int64_t tb, te;
+  window_of(p, tb, te);
+  const int64_t t = tb + (int64_t)blockIdx.x * 16 + lt;
+  const bool tile_ok = t < te;
   const int64_t row = t * kTile + (lane & 15);
   // Issue the row load first; the selections and representatives follow.
   uint4 qw[8];
@@ -346,8 +372,8 @@ __global__ void __launch_bounds__(256) hisa_route_kernel(const RouteParams p) {
   }
   if (lane < 2 * kTopK) {
     const int i = warp * 2 + lane / kTopK, k = lane % kTopK;
-    const int64_t ti = p.tile_begin + (int64_t)blockIdx.x * 16 + i;
-    sel[i][k] = (ti < p.tile_end && k < p.k_slots) ? p.top[((b * p.H + h) * p.tiles + ti) * p.k_slots + k] : -1;
+    const int64_t ti = tb + (int64_t)blockIdx.x * 16 + i;
+    sel[i][k] = (ti < te && k < p.k_slots) ? p.top[((b * p.H + h) * p.tiles + ti) * p.k_slots + k] : -1;
   }
   __syncwarp();
   for (int x = lane; x < 2 * kTopK * kHD; x += 32) {
@@ -478,8 +504,12 @@ hisa_attn_kernel(const AttnParams p, const __grid_constant__ AttnMaps maps, int3
   // CTAs cover aligned groups of kCtaTiles tiles whatever the window, so a
   // windowed launch visits each tile's chunks in the order a full launch does
   // (bit-identical rows); tiles of a group outside the window stay idle.
-  const int64_t T0 = (p.grid_begin + (int64_t)blockIdx.x * kCtaTiles) * kTile;
-  auto in_window = [&](int64_t t) { return t >= p.tile_begin && t < p.tile_end; };
+  int64_t tb, te;
+  window_of(p, tb, te);
+  const int64_t gb = p.pos != nullptr ? tb - tb % kCtaTiles : p.grid_begin;
+  const int64_t T0 = (gb + (int64_t)blockIdx.x * kCtaTiles) * kTile;
+  if (T0 / kTile >= te) return;  // whole CTA, before any barrier (device windows size the grid up)
+  auto in_window = [&](int64_t t) { return t >= tb && t < te; };
   const int64_t vlen = imin64((int64_t)p.lengths[b], p.T);
   const int32_t* top = p.top + ((int64_t)b * p.H + h) * p.tiles * p.k_slots;
 
@@ -680,6 +710,25 @@ bool tile_window(int64_t begin, int64_t count, int64_t tiles, int64_t* b, int64_
   return true;
 }
 
+// Host side of a launch's tile window: [begin, begin + count) checked against
+// the tile count, or with a device position the count alone (>= 1; the
+// kernel clips the window at the last tile).
+template <typename P>
+bool launch_window(int64_t begin, int64_t count, const int64_t* pos, P* p, int64_t* n_tiles) {
+  p->pos = pos;
+  p->tile_count = count;
+  if (pos != nullptr) {
+    if (count < 1 || count > p->tiles) return false;
+    p->tile_begin = 0;
+    p->tile_end = count;
+    *n_tiles = count;
+    return true;
+  }
+  if (!tile_window(begin, count, p->tiles, &p->tile_begin, &p->tile_end)) return false;
+  *n_tiles = p->tile_end - p->tile_begin;
+  return true;
+}
+
 }  // namespace
 }  // namespace dwarf
 
@@ -693,8 +742,8 @@ extern "C" int dwarf_hisa_reps(const dwarf_hisa_reps_args* a, void* stream) {
   if (!a->key || !a->lengths || !a->reps) return DWARF_ERR_NULL;
   if (!(a->blend_alpha >= 0.0f && a->blend_alpha <= 1.0f)) return DWARF_ERR_VALUE;
   RepsParams p{(const __nv_bfloat16*)a->key, a->skb, a->skh, a->skn, a->lengths, (__nv_bfloat16*)a->reps,
-               a->H, a->T, (a->T + kChunk - 1) / kChunk, a->blend_alpha};
-  dim3 grid((unsigned)p.C, (unsigned)a->H, (unsigned)a->B);
+               a->H, a->T, (a->T + kChunk - 1) / kChunk, a->blend_alpha, a->pos};
+  dim3 grid(a->pos != nullptr ? 1u : (unsigned)p.C, (unsigned)a->H, (unsigned)a->B);
   hisa_reps_kernel<<<grid, 64, 0, (cudaStream_t)stream>>>(p);
   return launch_status();
 }
@@ -714,9 +763,10 @@ extern "C" int dwarf_hisa_select(const dwarf_hisa_select_args* a, void* stream) 
   p.logits = a->logits; p.H = a->H; p.T = a->T; p.C = C; p.tiles = (a->T + kTile - 1) / kTile;
   p.k_slots = (int)(a->top_k < C ? a->top_k : C);
   p.temperature = a->temperature;
-  if (!tile_window(a->tile_begin, a->tile_count, p.tiles, &p.tile_begin, &p.tile_end)) return DWARF_ERR_SHAPE;
-  if (p.tile_end == p.tile_begin) return DWARF_OK;
-  dim3 grid((unsigned)((p.tile_end - p.tile_begin + 7) / 8), (unsigned)a->H, (unsigned)a->B);
+  int64_t n_tiles = 0;
+  if (!launch_window(a->tile_begin, a->tile_count, a->pos, &p, &n_tiles)) return DWARF_ERR_SHAPE;
+  if (n_tiles == 0) return DWARF_OK;
+  dim3 grid((unsigned)((n_tiles + 7) / 8), (unsigned)a->H, (unsigned)a->B);
   hisa_select_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(p);
   return launch_status();
 }
@@ -734,9 +784,10 @@ extern "C" int dwarf_hisa_route(const dwarf_hisa_route_args* a, void* stream) {
   p.reps = (const __nv_bfloat16*)a->reps; p.top = a->top_chunk_idx; p.route_scale = a->route_scale;
   p.route = (__nv_bfloat16*)a->route;
   p.H = a->H; p.T = a->T; p.C = a->C; p.tiles = (a->T + kTile - 1) / kTile; p.k_slots = a->k_slots;
-  if (!tile_window(a->tile_begin, a->tile_count, p.tiles, &p.tile_begin, &p.tile_end)) return DWARF_ERR_SHAPE;
-  if (p.tile_end == p.tile_begin) return DWARF_OK;
-  dim3 grid((unsigned)((p.tile_end - p.tile_begin + 15) / 16), (unsigned)a->H, (unsigned)a->B);
+  int64_t n_tiles = 0;
+  if (!launch_window(a->tile_begin, a->tile_count, a->pos, &p, &n_tiles)) return DWARF_ERR_SHAPE;
+  if (n_tiles == 0) return DWARF_OK;
+  dim3 grid((unsigned)((n_tiles + 15) / 16), (unsigned)a->H, (unsigned)a->B);
   hisa_route_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(p);
   return launch_status();
 }
@@ -779,10 +830,14 @@ extern "C" int dwarf_hisa_attn(const dwarf_hisa_attn_args* a, void* stream) {
   if (cudaFuncSetAttribute(hisa_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return DWARF_ERR_LAUNCH;
   const int64_t cta_tiles = kCtaTiles;
-  if (!tile_window(a->tile_begin, a->tile_count, p.tiles, &p.tile_begin, &p.tile_end)) return DWARF_ERR_SHAPE;
-  if (p.tile_end == p.tile_begin) return DWARF_OK;
+  int64_t n_tiles = 0;
+  if (!launch_window(a->tile_begin, a->tile_count, a->pos, &p, &n_tiles)) return DWARF_ERR_SHAPE;
+  if (n_tiles == 0) return DWARF_OK;
   p.grid_begin = p.tile_begin - p.tile_begin % cta_tiles;
-  dim3 grid((unsigned)((p.tile_end - p.grid_begin + cta_tiles - 1) / cta_tiles), (unsigned)a->H, (unsigned)a->B);
+  // A device window may straddle a CTA group boundary: one spare CTA (it exits at once).
+  const int64_t ctas = a->pos != nullptr ? (n_tiles == 1 ? 1 : (n_tiles + cta_tiles - 1) / cta_tiles + 1)
+                                         : (p.tile_end - p.grid_begin + cta_tiles - 1) / cta_tiles;
+  dim3 grid((unsigned)ctas, (unsigned)a->H, (unsigned)a->B);
   hisa_attn_kernel<<<grid, kCtaTiles * 32, smem, (cudaStream_t)stream>>>(p, maps, nullptr);
   return launch_status();
 }

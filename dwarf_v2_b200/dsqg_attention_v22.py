@@ -306,12 +306,14 @@ def _strides3(t: torch.Tensor) -> tuple[int, int, int]:
 
 def _dsqg_launch(q, *, kv, pos_bias, scale_embed, phase_base, phase_gain, y_pre, z_pre, offsets,
                  j_small, j_large, plane_shift, query_start, out, lse=None, head_gain=None, gate=None,
-                 seq_len=None, row_begin=0):
+                 seq_len=None, row_begin=0, pos=None):
     """Validate and launch dwarf_dsqg_fwd. ``kv`` is ("bf16", k, v) or ("q6", kc, ks, vc, vs).
 
     With ``row_begin`` > 0 only queries [row_begin, seq_len) are computed and q, y_pre,
     gate, out and lse hold those rows only (row 0 = position row_begin); K/V and z_pre
     cover positions [0, seq_len). This is the decode step's single-row launch.
+    ``pos`` (device int64 [1]) instead supplies row_begin at run time (a decode step
+    replayed from a CUDA graph); y_pre rows are then absolute positions like z_pre's.
     """
     B, H, N, HD = q.shape
     if seq_len is not None:
@@ -359,6 +361,8 @@ def _dsqg_launch(q, *, kv, pos_bias, scale_embed, phase_base, phase_gain, y_pre,
     if gate is not None:
         args.gate = gate.data_ptr()
         args.sgb_, args.sgn_ = gate.stride(0), gate.stride(1)
+    if pos is not None:
+        args.pos = pos.data_ptr()
     _lib.call("dwarf_dsqg_fwd", args, q.device)
 
 
@@ -744,7 +748,8 @@ class DSQGAttentionV19(nn.Module):
         if self.backend == "eager":
             raise NotImplementedError("the B200 engine has no eager backend; construct with backend='auto'")
         _lib.require_cuda(x)
-        _forward_only(x, *self.parameters())
+        if torch.is_grad_enabled():
+            _forward_only(x, *self.parameters())
         batch, seq_len, dimension = x.shape
         heads, head_dim = self.num_heads, self.head_dim
         query_start = min(self.minimum_offset, seq_len)
@@ -802,7 +807,8 @@ class DSQGAttentionV19(nn.Module):
         computes the single query row over the whole cache.
         """
         _lib.require_cuda(x)
-        _forward_only(x, *self.parameters())
+        if torch.is_grad_enabled():
+            _forward_only(x, *self.parameters())
         if self.kv_cache != "q6" or self.head_dim != 64 or (self.num_heads * 64) % 256 != 0:
             raise NotImplementedError("cached (incremental) DSQG runs on the q6 cache with head_dim 64")
         batch, rows, dimension = x.shape
@@ -821,7 +827,28 @@ class DSQGAttentionV19(nn.Module):
         return self._attend(x, query, ("q6", kc, ks, vc, vs), y_pre, z, qkvg[:, :, 3 * dimension:], t,
                             query_start, seq_len=seq_len, row_begin=row)
 
-    def _attend(self, x, query, kv, y_pre, z_pre, content_gate, t, query_start, *, seq_len=None, row_begin=0):
+    def forward_step(self, x: torch.Tensor, cache, pos: torch.Tensor) -> torch.Tensor:
+        """One new token per sequence (x [B,1,D]) at the device position ``pos`` (int64 [1]):
+        the q6 append and the DSQG launch both read the position from device memory, so
+        the step can be captured once in a CUDA graph and replayed at every position."""
+        if self.kv_cache != "q6" or self.head_dim != 64 or (self.num_heads * 64) % 256 != 0:
+            raise NotImplementedError("cached (incremental) DSQG runs on the q6 cache with head_dim 64")
+        batch, rows, dimension = x.shape
+        if rows != 1:
+            raise ValueError("forward_step takes one token per sequence")
+        heads, head_dim = self.num_heads, self.head_dim
+        act = torch.bfloat16
+        xb = x if x.dtype == act else x.to(act)
+        t = self._tables()
+        qkvg, _, _, _ = gemm.qkvg_prep(xb, self.qkvg_proj.weight.to(act), self.qkvg_proj.bias.to(act), heads,
+                                       t["q_probe"], t["k_probe"], cache=cache, pos=pos)
+        query = qkvg.view(batch, 1, 4, heads, head_dim)[:, :, 0].permute(0, 2, 1, 3)
+        y, z, kc, ks, vc, vs = cache
+        return self._attend(x, query, ("q6", kc, ks, vc, vs), y, z, qkvg[:, :, 3 * dimension:], t,
+                            self.minimum_offset, seq_len=1, pos=pos)
+
+    def _attend(self, x, query, kv, y_pre, z_pre, content_gate, t, query_start, *, seq_len=None, row_begin=0,
+                pos=None):
         """DSQG kernel (if_gain and content-gate epilogue fused) followed by out_proj.
 
         With ``row_begin`` > 0 ``query``/``y_pre``/``content_gate`` hold positions
@@ -837,7 +864,7 @@ class DSQGAttentionV19(nn.Module):
                      offsets=t["offsets"], j_small=self.j_small, j_large=self.j_large,
                      plane_shift=self.plane_shift, query_start=query_start, out=out_view,
                      head_gain=gain.detach().contiguous(), gate=content_gate, seq_len=seq_len,
-                     row_begin=row_begin)
+                     row_begin=row_begin, pos=pos)
         result = F.linear(out, self.out_proj.weight.to(act))
         return self.dropout(result).to(x.dtype) if x.dtype != act else self.dropout(result)
 

@@ -162,7 +162,8 @@ def linear_add_rmsnorm(x: torch.Tensor, weight: torch.Tensor, resid: torch.Tenso
 
 
 def qkvg_prep(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, heads: int,
-              q_probe: torch.Tensor, k_probe: torch.Tensor, *, cache=None, row: int = 0):
+              q_probe: torch.Tensor, k_probe: torch.Tensor, *, cache=None, row: int = 0,
+              pos: torch.Tensor | None = None):
     """DSQG qkvg projection with the prep pass fused into its epilogue.
 
     x [B, T, D] bf16; weight [4D, D], bias [4D]. Returns (qkvg, y_pre, z_pre,
@@ -173,6 +174,8 @@ def qkvg_prep(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, heads: 
     L >= row + T positions per (batch, head) ([B,H,L,4] fp32, [B,H,L,48] u8, [B,H,L]
     fp16): the epilogue writes positions [row, row + T) there instead of allocating
     (the decode cache). The returned tensors are then views of those rows.
+    ``pos`` (device int64 [1], with ``cache``) adds a run-time position to ``row``
+    (a decode step captured in a CUDA graph); the returned views then start at ``row``.
     """
     _lib.require_cuda(x, weight, bias, q_probe, k_probe)
     if x.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16:
@@ -201,6 +204,8 @@ def qkvg_prep(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, heads: 
         for t, shape, dtype in shapes:
             if tuple(t.shape) != shape or t.dtype != dtype or not t.is_contiguous():
                 raise ValueError(f"cache buffer must be contiguous {dtype} {shape}, got {t.dtype} {tuple(t.shape)}")
+        if pos is not None and (pos.dtype != torch.int64 or pos.numel() != 1 or not pos.is_cuda):
+            raise ValueError("pos must be a one-element int64 CUDA tensor")
         if not 0 <= row <= cache_len - T:
             raise ValueError(f"rows [{row}, {row + T}) exceed the cache length {cache_len}")
         y, z, kc, ks, vc, vs = (t[:, :, row:row + T] for t in (y, z, kc, ks, vc, vs))
@@ -211,6 +216,7 @@ def qkvg_prep(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, heads: 
                          bias_dtype=_lib.dtype_code(b.dtype), out=qkvg.data_ptr(), ldo=N, T=T, heads=heads,
                          q_probe=qp.data_ptr(), k_probe=kp.data_ptr(), y_pre=y.data_ptr(), z_pre=z.data_ptr(),
                          k_codes=kc.data_ptr(), k_scales=ks.data_ptr(), v_codes=vc.data_ptr(),
-                         v_scales=vs.data_ptr(), cache_len=cache_len)
+                         v_scales=vs.data_ptr(), cache_len=cache_len,
+                         pos=None if pos is None else pos.data_ptr())
     _lib.call("dwarf_gemm_bf16", args, dev)
     return qkvg, y, z, (kc, ks, vc, vs)

@@ -94,25 +94,33 @@ def _strides3(t):
     return t.stride(0), t.stride(1), t.stride(2)
 
 
-def chunk_representatives(global_key: torch.Tensor, lengths: torch.Tensor, *, blend_alpha: float) -> torch.Tensor:
-    """``dwarf_hisa_reps``: bf16 [B,H,ceil(T/64),64] normalised chunk representatives."""
+def chunk_representatives(global_key: torch.Tensor, lengths: torch.Tensor, *, blend_alpha: float,
+                          out: torch.Tensor | None = None, pos: torch.Tensor | None = None) -> torch.Tensor:
+    """``dwarf_hisa_reps``: bf16 [B,H,ceil(T/64),64] normalised chunk representatives.
+
+    With ``pos`` (device int64 [1]) only the chunk holding that position is rebuilt
+    in ``out`` (a decode step; the other chunks keep their values)."""
     B, H, T, D = global_key.shape
     C = max(1, -(-T // _CHUNK))
-    reps = torch.empty(B, H, C, D, dtype=torch.bfloat16, device=global_key.device)
+    reps = torch.empty(B, H, C, D, dtype=torch.bfloat16, device=global_key.device) if out is None else out
+    if tuple(reps.shape) != (B, H, C, D) or reps.dtype != torch.bfloat16 or not reps.is_contiguous():
+        raise ValueError(f"reps must be a contiguous bf16 {(B, H, C, D)} tensor")
     args = _lib.HisaRepsArgs(version=_lib.ABI_VERSION, head_dim=D, chunk_size=_CHUNK, B=B, H=H, T=T,
                              key=global_key.data_ptr(), lengths=lengths.data_ptr(), blend_alpha=float(blend_alpha),
-                             reps=reps.data_ptr())
+                             reps=reps.data_ptr(), pos=None if pos is None else pos.data_ptr())
     args.skb, args.skh, args.skn = _strides3(global_key)
     _lib.call("dwarf_hisa_reps", args, global_key.device)
     return reps
 
 
 def select_chunks(query: torch.Tensor, reps: torch.Tensor, lengths: torch.Tensor, *, top_k: int,
-                  temperature: float, want_logits: bool = False, tile_begin: int = 0, tile_count: int = 0):
+                  temperature: float, want_logits: bool = False, tile_begin: int = 0, tile_count: int = 0,
+                  pos: torch.Tensor | None = None):
     """``dwarf_hisa_select``: (top_chunk_idx int32 [B,H,tiles,K], optional masked logits).
 
     ``tile_begin``/``tile_count`` restrict the launch to selector tiles
     [tile_begin, tile_begin + tile_count) (count 0: every tile); other entries stay unset.
+    ``pos`` (device int64 [1]) starts the window at tile pos // 16 at run time instead.
     """
     B, H, T, D = query.shape
     C = reps.shape[2]
@@ -124,20 +132,23 @@ def select_chunks(query: torch.Tensor, reps: torch.Tensor, lengths: torch.Tensor
                                top_k=int(top_k), B=B, H=H, T=T, query=query.data_ptr(), reps=reps.data_ptr(),
                                lengths=lengths.data_ptr(), temperature=float(temperature),
                                top_chunk_idx=top.data_ptr(), logits=None if logits is None else logits.data_ptr(),
-                               tile_begin=int(tile_begin), tile_count=int(tile_count))
+                               tile_begin=int(tile_begin), tile_count=int(tile_count),
+                               pos=None if pos is None else pos.data_ptr())
     args.sqb, args.sqh, args.sqn = _strides3(query)
     _lib.call("dwarf_hisa_select", args, query.device)
     return top, logits
 
 
-def route_prior(query, reps, top, route_scale, *, tile_begin: int = 0, tile_count: int = 0) -> torch.Tensor:
+def route_prior(query, reps, top, route_scale, *, tile_begin: int = 0, tile_count: int = 0,
+                pos: torch.Tensor | None = None) -> torch.Tensor:
     """``dwarf_hisa_route``: bf16 route prior [B,H,T,4] of the selected chunks."""
     B, H, T, D = query.shape
     route = torch.empty(B, H, T, _MAX_TOP_K, dtype=torch.bfloat16, device=query.device)
     args = _lib.HisaRouteArgs(version=_lib.ABI_VERSION, head_dim=D, selector_tile=_TILE, k_slots=top.shape[-1],
                               B=B, H=H, T=T, C=reps.shape[2], query=query.data_ptr(), reps=reps.data_ptr(),
                               top_chunk_idx=top.data_ptr(), route_scale=route_scale.data_ptr(),
-                              route=route.data_ptr(), tile_begin=int(tile_begin), tile_count=int(tile_count))
+                              route=route.data_ptr(), tile_begin=int(tile_begin), tile_count=int(tile_count),
+                              pos=None if pos is None else pos.data_ptr())
     args.sqb, args.sqh, args.sqn = _strides3(query)
     _lib.call("dwarf_hisa_route", args, query.device)
     return route
@@ -145,7 +156,7 @@ def route_prior(query, reps, top, route_scale, *, tile_begin: int = 0, tile_coun
 
 def tile_attention(query, local_key, local_value, global_key, global_value, reps, top, route_scale, lengths, *,
                    out: torch.Tensor | None = None, want_route: bool = False, tile_begin: int = 0,
-                   tile_count: int = 0):
+                   tile_count: int = 0, pos: torch.Tensor | None = None):
     """``dwarf_hisa_route`` + ``dwarf_hisa_attn``: route prior, then local window + routed chunks.
 
     ``tile_begin``/``tile_count`` restrict both launches to the query rows of those selector
@@ -153,14 +164,15 @@ def tile_attention(query, local_key, local_value, global_key, global_value, reps
     B, H, T, D = query.shape
     if out is None:
         out = torch.empty(B, H, T, D, dtype=torch.bfloat16, device=query.device)
-    route = route_prior(query, reps, top, route_scale, tile_begin=tile_begin, tile_count=tile_count)
+    route = route_prior(query, reps, top, route_scale, tile_begin=tile_begin, tile_count=tile_count, pos=pos)
     args = _lib.HisaAttnArgs(version=_lib.ABI_VERSION, head_dim=D, chunk_size=_CHUNK, selector_tile=_TILE,
                              local_window=_WINDOW, k_slots=top.shape[-1], B=B, H=H, T=T,
                              query=query.data_ptr(), local_key=local_key.data_ptr(),
                              local_value=local_value.data_ptr(), global_key=global_key.data_ptr(),
                              global_value=global_value.data_ptr(), top_chunk_idx=top.data_ptr(),
                              route=route.data_ptr(), lengths=lengths.data_ptr(), out=out.data_ptr(),
-                             tile_begin=int(tile_begin), tile_count=int(tile_count))
+                             tile_begin=int(tile_begin), tile_count=int(tile_count),
+                             pos=None if pos is None else pos.data_ptr())
     args.sqb, args.sqh, args.sqn = _strides3(query)
     args.slkb, args.slkh, args.slkn = _strides3(local_key)
     args.slvb, args.slvh, args.slvn = _strides3(local_value)
@@ -509,6 +521,38 @@ class HierarchicalSparseAttentionV16HISACausal(nn.Module):
         tile_attention(cq, clk, clv, cgk, cgv, reps, top, scale, lengths,
                        out=_to_heads(attended, B, seq_len, self.H, self.hd), tile_begin=tile0, tile_count=tiles)
         return F.linear(attended[:, row:], self.W_o.weight.to(act)), gate
+
+    def forward_step(self, x: torch.Tensor, kv_inject, cache, reps: torch.Tensor, attended: torch.Tensor,
+                     pos: torch.Tensor, lengths: torch.Tensor):
+        """``forward_parts_cached`` for one new token per sequence at the device position
+        ``pos`` (int64 [1]); every launch takes the position from device memory, so the step
+        can be captured once in a CUDA graph and replayed at every position.
+
+        ``reps`` [B,H,L/64,64] holds the chunk representatives of the cached positions
+        (only the chunk holding ``pos`` changes), ``attended`` [B,L,D] is scratch and
+        ``lengths`` int32 [B] = pos + 1. Returns (W_o(attended) [B,1,D], gate logits).
+        """
+        self._check_supported()
+        B = x.shape[0]
+        act = torch.bfloat16
+        xb = x if x.dtype == act else x.to(act)
+        qkvg = F.linear(xb, self.qkvg_proj.weight.to(act), self.qkvg_proj.bias.to(act))
+        q, k, v, gate = qkvg.split(self.D, dim=-1)
+        query = _to_heads(q, B, 1, self.H, self.hd)
+        local_key = _to_heads(k, B, 1, self.H, self.hd)
+        local_value = _to_heads(v, B, 1, self.H, self.hd)
+        global_key, global_value = self.global_kv(xb, local_key, local_value, kv_inject)
+        for buf, new in zip(cache, (query, local_key, local_value, global_key, global_value)):
+            buf.index_copy_(2, pos, new)
+        cq, clk, clv, cgk, cgv = cache
+        L = cq.shape[2]
+        chunk_representatives(cgk, lengths, blend_alpha=self._blend_alpha, out=reps, pos=pos)
+        top, _ = select_chunks(cq, reps, lengths, top_k=self.top_k_chunks, temperature=self.temperature,
+                               tile_count=1, pos=pos)
+        scale = self.route_prior_scale.detach().float().contiguous()
+        tile_attention(cq, clk, clv, cgk, cgv, reps, top, scale, lengths,
+                       out=_to_heads(attended, B, L, self.H, self.hd), tile_count=1, pos=pos)
+        return F.linear(attended.index_select(1, pos), self.W_o.weight.to(act)), gate
 
     def forward(self, x: torch.Tensor, kv_inject=None, *, valid_lengths=None, return_metadata: bool = False,
                 return_auxiliary: bool = False):

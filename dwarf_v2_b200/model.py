@@ -30,7 +30,7 @@ import torch.nn.functional as F
 from . import gemm, glue
 from .causal_ema_scan import bounded_ema_factor, causal_ema_scan, inverse_bounded_ema_factor
 from .dsqg_attention_v22 import ALL_OFFSETS, R_PLANES, DSQGAttentionV19
-from .hierarchical_sparse_attn_v18_hisa import HierarchicalSparseAttentionV16HISACausal
+from .hierarchical_sparse_attn_v18_hisa import HierarchicalSparseAttentionV16HISACausal, chunk_representatives
 
 EXPECTED_PARAMETERS = 55_348_728
 EXPECTED_TRAINABLE_PARAMETERS = 55_344_120
@@ -190,18 +190,18 @@ class InterferencePacket(nn.Module):
         return self._const
 
     def forward(self, normalized: torch.Tensor, ema_states: list | None = None):
-        """(key_delta, value_delta) [B,H,T,hd]. With ``ema_states`` (one fp32 [B,D] state per
-        timescale, or None entries for a zero start) the scans continue from those states and
-        the list is updated in place with the states after the last token."""
+        """(key_delta, value_delta) [B,H,T,hd]. With ``ema_states`` (one fp32 [B,D] state tensor
+        per timescale) the scans continue from those states, which are then overwritten in
+        place with the states after the last token."""
         x = _act(normalized)
         factors, mixture = self._constants()
         if ema_states is None:
             scans = [causal_ema_scan(x, f.reshape(1)) for f in factors]
         else:
             scans = []
-            for i, f in enumerate(factors):
-                scan, ema_states[i] = causal_ema_scan(x, f.reshape(1), initial_state=ema_states[i],
-                                                      return_final_state=True)
+            for f, state in zip(factors, ema_states):
+                scan, final = causal_ema_scan(x, f.reshape(1), initial_state=state, return_final_state=True)
+                state.copy_(final)
                 scans.append(scan)
         gate_pre = F.linear(x, _act(self.gate_proj.weight), _act(self.gate_proj.bias))
         packet = glue.packet(scans, mixture, gate_pre)
@@ -262,18 +262,70 @@ class GlobalMixerBlock(nn.Module):
 
 
 @dataclass
+class HisaLayerCache:
+    """Decode cache of the HISA block: (query, local_key, local_value, global_key,
+    global_value) bf16 [B,H,L,64], chunk representatives [B,H,L/64,64], attention
+    scratch [B,L,D] and the packet's fp32 EMA states [B,D] (one per timescale)."""
+
+    kv: tuple
+    reps: torch.Tensor
+    attended: torch.Tensor
+    ema: list
+
+
+@dataclass
 class DecodeState:
     """Per-sequence caches of an incremental decode, ``length`` positions filled.
 
     ``layers[i]`` for a DSQG block: the q6 cache (y, z, k_codes, k_scales, v_codes,
-    v_scales) of ``max_len`` positions per (batch, head); for the HISA block:
-    ((query, local_key, local_value, global_key, global_value) bf16 [B,H,max_len,64],
-    the packet's fp32 EMA states [B,D] per timescale)."""
+    v_scales) of ``max_len`` positions per (batch, head); for the HISA block a
+    ``HisaLayerCache``. ``pos`` is ``length`` on the device (int64 [1]): decode steps
+    read it there, so one captured step replays at every position."""
 
     batch: int
     max_len: int
     length: int
     layers: list
+    pos: torch.Tensor
+
+
+class DecodeGraph:
+    """One decode step captured in a CUDA graph and replayed per token.
+
+    Every kernel of the step takes the position from ``state.pos`` on the device and
+    the step advances it there, so the same graph serves every position; the host only
+    copies the token ids in and replays (one launch instead of ~150). The state must not
+    be stepped by other means while a graph is in use, except ``state.length``, which
+    ``step`` keeps in sync.
+    """
+
+    def __init__(self, model: "DwarfForCausalLM", state: DecodeState) -> None:
+        if state.length >= state.max_len:
+            raise ValueError("the state is full")
+        self.model, self.state = model, state
+        device = state.pos.device
+        self.ids = torch.zeros(state.batch, dtype=torch.int64, device=device)
+        weight = _act(model.embedding.weight.detach()).contiguous()
+        self._weight = weight
+        torch.cuda.synchronize(device)
+        saved = state.pos.clone()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            hidden = model._step_hidden(self.ids, state)
+            self.logits = gemm.linear(hidden[:, 0].contiguous(), weight)
+        torch.cuda.synchronize(device)
+        state.pos.copy_(saved)  # capture records the step; it does not run it
+
+    def step(self, token_ids: torch.Tensor) -> torch.Tensor:
+        """Logits [B,V] of ``token_ids`` [B] at position ``state.length`` (a view of the
+        graph's output buffer, overwritten by the next step)."""
+        state = self.state
+        if state.length >= state.max_len:
+            raise ValueError(f"the state is full (max_len {state.max_len})")
+        self.ids.copy_(token_ids.reshape(-1), non_blocking=True)
+        self.graph.replay()
+        state.length += 1
+        return self.logits
 
 
 class DwarfForCausalLM(nn.Module):
@@ -386,20 +438,28 @@ class DwarfForCausalLM(nn.Module):
             raise NotImplementedError("incremental decoding runs on the q6 KV cache (kv_cache='q6')")
         config = self.config
         max_len = int(max_len or config.model_length)
+        if max_len < 1 or max_len > 128 * config.hisa_chunk_size:
+            raise ValueError(f"max_len must be in [1, {128 * config.hisa_chunk_size}]")
         device = torch.device(device) if device is not None else self.embedding.weight.device
-        H, hd = config.num_heads, config.embedding_dim // config.num_heads
+        D = config.embedding_dim
+        H, hd = config.num_heads, D // config.num_heads
         layers: list = []
         for block in self.blocks:
             if isinstance(block, GlobalMixerBlock):
-                kv = tuple(torch.empty(batch, H, max_len, hd, dtype=torch.bfloat16, device=device) for _ in range(5))
-                layers.append((kv, [None] * len(config.ema_timescales)))
+                kv = tuple(torch.zeros(batch, H, max_len, hd, dtype=torch.bfloat16, device=device) for _ in range(5))
+                chunks = -(-max_len // config.hisa_chunk_size)
+                reps = torch.zeros(batch, H, chunks, hd, dtype=torch.bfloat16, device=device)
+                attended = torch.zeros(batch, max_len, D, dtype=torch.bfloat16, device=device)
+                ema = [torch.zeros(batch, D, dtype=torch.float32, device=device) for _ in config.ema_timescales]
+                layers.append(HisaLayerCache(kv, reps, attended, ema))
             else:
-                probes = torch.empty(batch, H, max_len, 4, dtype=torch.float32, device=device)
-                codes = torch.empty(batch, H, max_len, 48, dtype=torch.uint8, device=device)
-                scales = torch.empty(batch, H, max_len, dtype=torch.float16, device=device)
-                layers.append((probes, torch.empty_like(probes), codes, scales, torch.empty_like(codes),
-                               torch.empty_like(scales)))
-        return DecodeState(batch=batch, max_len=max_len, length=0, layers=layers)
+                probes = torch.zeros(batch, H, max_len, 4, dtype=torch.float32, device=device)
+                codes = torch.zeros(batch, H, max_len, 48, dtype=torch.uint8, device=device)
+                scales = torch.zeros(batch, H, max_len, dtype=torch.float16, device=device)
+                layers.append((probes, torch.zeros_like(probes), codes, scales, torch.zeros_like(codes),
+                               torch.zeros_like(scales)))
+        pos = torch.zeros(1, dtype=torch.int64, device=device)
+        return DecodeState(batch=batch, max_len=max_len, length=0, layers=layers, pos=pos)
 
     def forward_cached(self, input_ids: torch.Tensor, state: "DecodeState") -> torch.Tensor:
         """Final RMSNorm'd hidden states [B,T,D] of the T tokens following ``state.length``
@@ -418,15 +478,41 @@ class DwarfForCausalLM(nn.Module):
             next_norm = blocks[i + 1].norm1.weight if i + 1 < len(blocks) else self.norm.weight
             layer = state.layers[i]
             if isinstance(block, GlobalMixerBlock):
-                kv_cache, ema_states = layer
-                kd, vd = block.packet(n, ema_states)
-                projected, gate = block.attn.forward_parts_cached(n, (kd, vd), kv_cache, row)
+                kd, vd = block.packet(n, layer.ema)
+                projected, gate = block.attn.forward_parts_cached(n, (kd, vd), layer.kv, row)
+                # the decode step's running chunk representatives over the whole cache
+                lengths = torch.full((B,), row + T, dtype=torch.int32, device=x.device)
+                chunk_representatives(layer.kv[3], lengths, blend_alpha=block.attn._blend_alpha, out=layer.reps)
                 x, n2 = glue.add_rmsnorm(x, block.norm2.weight.detach(), addend=projected, gate=gate)
             else:
                 x, n2 = glue.add_rmsnorm(x, block.norm2.weight.detach(),
                                          addend=block.attn.forward_cached(n, layer, row))
             x, n = block.ffn.forward_add_rmsnorm(n2, x, next_norm.detach())
         state.length = row + T
+        state.pos.fill_(state.length)
+        return n
+
+    def _step_hidden(self, token_ids: torch.Tensor, state: "DecodeState") -> torch.Tensor:
+        """One token per sequence at the device position ``state.pos`` (advanced by one on the
+        device); no host value of the position is used, so this is what a CUDA graph captures."""
+        B = token_ids.shape[0]
+        emb = _act(self.embedding.weight.detach()).contiguous()
+        blocks = list(self.blocks)
+        x, n = glue.embed_rmsnorm(token_ids.reshape(B, 1), emb, blocks[0].norm1.weight.detach())
+        pos = state.pos
+        lengths = (pos + 1).to(torch.int32).expand(B).contiguous()
+        for i, block in enumerate(blocks):
+            next_norm = blocks[i + 1].norm1.weight if i + 1 < len(blocks) else self.norm.weight
+            layer = state.layers[i]
+            if isinstance(block, GlobalMixerBlock):
+                kd, vd = block.packet(n, layer.ema)
+                projected, gate = block.attn.forward_step(n, (kd, vd), layer.kv, layer.reps, layer.attended, pos,
+                                                          lengths)
+                x, n2 = glue.add_rmsnorm(x, block.norm2.weight.detach(), addend=projected, gate=gate)
+            else:
+                x, n2 = glue.add_rmsnorm(x, block.norm2.weight.detach(), addend=block.attn.forward_step(n, layer, pos))
+            x, n = block.ffn.forward_add_rmsnorm(n2, x, next_norm.detach())
+        pos.add_(1)
         return n
 
     def prefill(self, input_ids: torch.Tensor, max_len: int | None = None) -> tuple[torch.Tensor, "DecodeState"]:
@@ -438,9 +524,20 @@ class DwarfForCausalLM(nn.Module):
 
     def decode_step(self, state: "DecodeState", token_ids: torch.Tensor) -> torch.Tensor:
         """One incremental step: ``token_ids`` [B] at position ``state.length``; returns its
-        logits [B,V] (those of a prefill over the ``state.length + 1`` tokens at its last row)."""
-        hidden = self.forward_cached(token_ids.reshape(-1, 1), state)
+        logits [B,V] (those of a prefill over the ``state.length + 1`` tokens at its last row,
+        up to the decode DSQG kernel's fp32 summation order)."""
+        self._check(token_ids.reshape(-1, 1))
+        if token_ids.numel() != state.batch:
+            raise ValueError(f"state holds {state.batch} sequences, got {token_ids.numel()} tokens")
+        if state.length >= state.max_len:
+            raise ValueError(f"the state is full (max_len {state.max_len})")
+        hidden = self._step_hidden(token_ids.reshape(-1), state)
+        state.length += 1
         return gemm.linear(hidden[:, 0].contiguous(), _act(self.embedding.weight.detach()))
+
+    def capture_decode(self, state: "DecodeState") -> "DecodeGraph":
+        """A CUDA graph of one decode step over ``state``'s buffers (see DecodeGraph)."""
+        return DecodeGraph(self, state)
 
     def forward(self, input_ids: torch.Tensor, *, return_hidden: bool = False, return_auxiliary: bool = False):
         hidden, auxiliary = self.forward_hidden(input_ids, return_auxiliary=True)

@@ -237,6 +237,12 @@ typedef struct {
   int64_t row_begin;              /* compute queries [row_begin, N) only; q,
                                      y_pre, gate, out and lse rows are then
                                      relative to row_begin (decode: N-1)  */
+  const int64_t* pos;             /* optional device int64 P (decode step):
+                                     row_begin = P at run time and N = P +
+                                     (N - row_begin) of the call; y_pre
+                                     rows are then absolute positions (it
+                                     lives in the cache); q6 K/V, J <= 32,
+                                     at most 16 rows                      */
 } dwarf_dsqg_fwd_args;
 
 int dwarf_dsqg_fwd(const dwarf_dsqg_fwd_args* args, void* stream);
@@ -322,6 +328,8 @@ typedef struct {
   const int32_t* lengths;         /* [B] valid lengths                    */
   float blend_alpha;
   void* reps;                     /* bf16 [B, H, ceil(T/64), 64] contiguous */
+  const int64_t* pos;             /* optional device int64 P (decode step):
+                                     only chunk P/64 is recomputed        */
 } dwarf_hisa_reps_args;
 
 /* Strict-causal top-k tile router: anchor q^ = bf16(normalize(q[16 t])),
@@ -344,6 +352,11 @@ typedef struct {
   float* logits;                  /* optional [B, H, tiles, C] (masked)   */
   int64_t tile_begin, tile_count; /* tiles computed (count 0: all from begin;
                                      0, 0 = every tile); decode: one tile */
+  const int64_t* pos;             /* optional device int64 P (decode step):
+                                     the tile window starts at tile P/16
+                                     (tile_begin ignored; tile_count >= 1
+                                     tiles), so a captured CUDA graph can
+                                     replay at every position             */
 } dwarf_hisa_select_args;
 
 /* Route prior of the selected chunks (_selected_route_scores :418-468):
@@ -362,6 +375,7 @@ typedef struct {
   const float* route_scale;         /* [H] = softplus(route_prior_raw)    */
   void* route;                      /* bf16 [B, H, T, 4] contiguous       */
   int64_t tile_begin, tile_count;   /* as dwarf_hisa_select_args          */
+  const int64_t* pos;               /* as dwarf_hisa_select_args          */
 } dwarf_hisa_route_args;
 
 /* Fused tile attention: for each query n of tile t, one softmax over
@@ -385,6 +399,7 @@ typedef struct {
   const int32_t* lengths;
   void* out;                int64_t sob, soh, son;   /* bf16              */
   int64_t tile_begin, tile_count; /* as dwarf_hisa_select_args            */
+  const int64_t* pos;             /* as dwarf_hisa_select_args            */
 } dwarf_hisa_attn_args;
 
 int dwarf_hisa_reps(const dwarf_hisa_reps_args* args, void* stream);
@@ -543,6 +558,8 @@ typedef struct {
   void* arg_part;                 /* epilogue 4: float2 [M, N/128]         */
   const int64_t* targets;         /* epilogue 4: optional int64 [M]        */
   float* target_logit;            /* epilogue 4: [M] (with targets)        */
+  const int64_t* pos;             /* epilogue 3: optional device int64 added
+                                     to the first cache row (decode step) */
 } dwarf_gemm_args;
 
 int dwarf_gemm_bf16(const dwarf_gemm_args* args, void* stream);
