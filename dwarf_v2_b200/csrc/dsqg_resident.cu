@@ -43,8 +43,6 @@ namespace {
 using namespace dsqg;
 using namespace wmma16;
 
-constexpr int kRThreads = 256;
-constexpr int kRWarps = kRThreads / 32;
 constexpr int kRQB = 256;  // queries per round == key rows per chunk
 constexpr int kRMaxJ = 32;
 constexpr int kRSmemLimit = 232448;  // 227 KB opt-in shared memory per CTA
@@ -65,7 +63,7 @@ struct ResLayout {
     o_ks = o;    o += (uint32_t)N * 2;
     o_vs = o;    o += (uint32_t)N * 2;
     o_e = o;     o += (uint32_t)jp * 128;
-    o_qe = o;    o += (uint32_t)kRWarps * 32 * kQeLd * 4;
+    o_qe = o;    o += (uint32_t)kRQB * kQeLd * 4;
     o_pb = o;    o += (uint32_t)J * 4;
     o_off = o;   o += (uint32_t)J * 4;
     o_pbase = o; o += (uint32_t)jl * 16;
@@ -209,12 +207,28 @@ __device__ __forceinline__ void movt_pair(uint32_t w0, uint32_t w1, uint32_t w2,
   b = __uint_as_float(0x4B000000u | ((x >> 6) & 63u)) - 8388640.0f;
 }
 
-template <int PW>
-__global__ void __launch_bounds__(kRThreads, 1) dsqg_resident_kernel(const DsqgParams p, int32_t* status) {
+// TPQ threads per query: 1 (all 64 dims in one thread; 256 threads, 8 warps)
+// or 2 (32 dims each, partial dot products combined with one shuffle; 512
+// threads, 16 warps). The per-pair score / softmax bookkeeping is repeated in
+// both threads of a pair with identical operands, so both hold the same
+// running maximum and weights. Two threads per query halve the registers of
+// a thread (q and the accumulator are 32 floats each), which doubles the
+// warps resident per SM: the kernel is bound by fixed-latency dependencies
+// (decode -> FMA chains) at 8 warps per SM.
+template <int PW, int TPQ>
+__global__ void __launch_bounds__(256 * TPQ, 1) dsqg_resident_kernel(const DsqgParams p, int32_t* status) {
+  constexpr int kThreads = 256 * TPQ;
+  constexpr int kQW = 32 / TPQ;       // queries per warp
+  constexpr int kD = 64 / TPQ;        // head dims per thread
+  constexpr int kSL = kD / 16;        // 16-field slices per thread
+  constexpr int kW = 3 * kSL;         // 32-bit code words per thread and row
+  constexpr int kPL = 4 / TPQ;        // MOVT planes per thread
+  constexpr int kMT = kQW / 16;       // m16 tiles of the q.E product per warp
   extern __shared__ __align__(128) unsigned char smem[];
   const int N = (int)p.N, J = p.J, js = p.j_small;
   const ResLayout L(N, J, p.j_large);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int qi = lane / TPQ, hf = lane % TPQ;
   const int64_t h = blockIdx.x, b = blockIdx.y;
   const int64_t hk = h / p.kv_group;
   const uint32_t sbase = smem_u32(smem);
@@ -240,7 +254,7 @@ __global__ void __launch_bounds__(kRThreads, 1) dsqg_resident_kernel(const DsqgP
     }
   }
   const uint32_t e_base = sbase + L.o_e;
-  for (int i = tid; i < L.jp * 8; i += kRThreads) {
+  for (int i = tid; i < L.jp * 8; i += kThreads) {
     const int r = i >> 3, c = i & 7;
     uint32_t packed[4] = {0u, 0u, 0u, 0u};
     if (r < J) {
@@ -259,11 +273,11 @@ __global__ void __launch_bounds__(kRThreads, 1) dsqg_resident_kernel(const DsqgP
   int* s_off = reinterpret_cast<int*>(smem + L.o_off);
   float* s_pbase = reinterpret_cast<float*>(smem + L.o_pbase);
   float* s_pgain = reinterpret_cast<float*>(smem + L.o_pgain);
-  for (int j = tid; j < J; j += kRThreads) {
+  for (int j = tid; j < J; j += kThreads) {
     s_pb[j] = p.pos_bias[j * p.spj + h * p.sph] * kLog2e;
     s_off[j] = p.offsets[j];
   }
-  for (int i = tid; i < p.j_large * 4; i += kRThreads) {
+  for (int i = tid; i < p.j_large * 4; i += kThreads) {
     const int j = i >> 2, r = i & 3;
     s_pbase[i] = p.pbase[j * p.sbj + h * p.sbh + r];
     s_pgain[i] = p.pgain[j * p.sgj + h * p.sgh + r];
@@ -274,12 +288,12 @@ __global__ void __launch_bounds__(kRThreads, 1) dsqg_resident_kernel(const DsqgP
   const uint8_t* s_vc = smem + L.o_vc;
   const __half* s_ks = reinterpret_cast<const __half*>(smem + L.o_ks);
   const __half* s_vs = reinterpret_cast<const __half*>(smem + L.o_vs);
-  float* qe_buf = reinterpret_cast<float*>(smem + L.o_qe) + warp * 32 * kQeLd;
+  float* qe_buf = reinterpret_cast<float*>(smem + L.o_qe) + warp * kQW * kQeLd;
   const int rot = p.plane_shift;
   const uint32_t rot_off = (uint32_t)(6 * rot) & 31u;
   const float c_score = 0.125f * kLog2e;
   const __nv_bfloat16* qbase = p.q + b * p.sqb + h * p.sqh;
-  const float* zbase = p.z + b * p.szb + hk * p.szh;
+  const float* zbase = p.z + b * p.szb + hk * p.szh + kPL * hf;
   float gain = 1.0f;
   if (p.gain != nullptr)
     gain = p.gain_bf16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.gain)[h])
@@ -301,7 +315,7 @@ __global__ void __launch_bounds__(kRThreads, 1) dsqg_resident_kernel(const DsqgP
       const int rows = N - n0 < kRQB ? N - n0 : kRQB;
       uint32_t* kw = reinterpret_cast<uint32_t*>(smem + L.o_kc) + n0 * 12;
       uint32_t* vw = reinterpret_cast<uint32_t*>(smem + L.o_vc) + n0 * 12;
-      for (int i = tid; i < rows * 12; i += kRThreads) {
+      for (int i = tid; i < rows * 12; i += kThreads) {
         const int k = i % 3;
         const uint32_t m = k == 0 ? 0x20820820u : (k == 1 ? 0x08208208u : 0x82082082u);
         kw[i] ^= m;
@@ -310,20 +324,20 @@ __global__ void __launch_bounds__(kRThreads, 1) dsqg_resident_kernel(const DsqgP
     }
     __syncthreads();
 
-    const int wn0 = n0 + warp * 32;
+    const int wn0 = n0 + warp * kQW;
     if (wn0 >= N) continue;  // warp-uniform; no block barrier follows before the next round
 
-    // ---- per-query state: this thread's query n, all 64 dims
-    const int n = wn0 + lane;
+    // ---- per-query state: query n, dims [kD * hf, kD * hf + kD)
+    const int n = wn0 + qi;
     const bool row_ok = n < N && n >= p.query_start;
     const int nq = n < N ? n : N - 1;
-    float qs[64];
+    float qs[kD];
     float qbias, c1;
     {
-      const uint4* src = reinterpret_cast<const uint4*>(qbase + (int64_t)nq * p.sqn);
+      const uint4* src = reinterpret_cast<const uint4*>(qbase + (int64_t)nq * p.sqn + kD * hf);
       float qmax = 0.0f, qsum = 0.0f;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
+      for (int i = 0; i < kD / 8; ++i) {
         const uint4 w = __ldg(src + i);
         const uint32_t u[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
@@ -333,7 +347,11 @@ __global__ void __launch_bounds__(kRThreads, 1) dsqg_resident_kernel(const DsqgP
         }
       }
 #pragma unroll
-      for (int i = 0; i < 64; ++i) { qmax = fmaxf(qmax, fabsf(qs[i])); qsum += qs[i]; }
+      for (int i = 0; i < kD; ++i) { qmax = fmaxf(qmax, fabsf(qs[i])); qsum += qs[i]; }
+      if constexpr (TPQ == 2) {
+        qmax = fmaxf(qmax, __shfl_xor_sync(0xffffffffu, qmax, 1));
+        qsum += __shfl_xor_sync(0xffffffffu, qsum, 1);
+      }
       const int e = (int)((__float_as_uint(qmax) >> 23) & 255u) - 127;  // floor(log2 qmax)
       int E = 125 - e;
       E = E > 100 ? 100 : (E < 22 ? 22 : E);
@@ -342,31 +360,46 @@ __global__ void __launch_bounds__(kRThreads, 1) dsqg_resident_kernel(const DsqgP
 #pragma unroll
       for (int k = 0; k < 9; ++k) sc[k] = __int_as_float((127 + E - 2 * k) << 23);
 #pragma unroll
-      for (int i = 0; i < 64; ++i) qs[i] *= sc[q6_field_shift(i & 15) / 2];
+      for (int i = 0; i < kD; ++i) qs[i] *= sc[q6_field_shift(i & 15) / 2];
       c1 = __int_as_float((276 - E) << 23);  // 2^(149 - E)
       qbias = -32.0f * qsum;
     }
-    float gy[4];  // y_pre of this query (multiplies phase_gain)
+    float gy[kPL];  // y_pre of this query (multiplies phase_gain)
     {
-      const float4 y4 = *reinterpret_cast<const float4*>(p.y + b * p.syb + h * p.syh + (int64_t)nq * p.syn);
-      gy[0] = y4.x; gy[1] = y4.y; gy[2] = y4.z; gy[3] = y4.w;
+      const float* yrow = p.y + b * p.syb + h * p.syh + (int64_t)nq * p.syn + kPL * hf;
+      if constexpr (TPQ == 1) {
+        const float4 y4 = *reinterpret_cast<const float4*>(yrow);
+        gy[0] = y4.x; gy[1] = y4.y; gy[2] = y4.z; gy[3] = y4.w;
+      } else {
+        const float2 y2 = *reinterpret_cast<const float2*>(yrow);
+        gy[0] = y2.x; gy[1] = y2.y;
+      }
     }
 
-    float acc[64];
+    float acc[kD];
 #pragma unroll
-    for (int i = 0; i < 64; ++i) acc[i] = 0.0f;
+    for (int i = 0; i < kD; ++i) acc[i] = 0.0f;
     float l = 0.0f, wbias = 0.0f, m = -INFINITY;
-    float corr_a[4] = {0.f, 0.f, 0.f, 0.f}, corr_b[4] = {0.f, 0.f, 0.f, 0.f};
+    float corr_a[kPL], corr_b[kPL];
+#pragma unroll
+    for (int pl = 0; pl < kPL; ++pl) { corr_a[pl] = 0.f; corr_b[pl] = 0.f; }
 
-    // Offsets in groups of 8: q . bf16(E_j) for the warp's 32 queries on
+    // Offsets in groups of 8: q . bf16(E_j) for the warp's queries on
     // tensor cores, transposed through qe_buf into this thread's qe[8].
     const int g = lane >> 2, t4 = lane & 3;
+    // Offsets whose source row is before token 0 for every query of the
+    // warp (off_j > last query) contribute nothing: skip them (warp-uniform).
+    const int wlast = wn0 + kQW - 1;
 #pragma unroll 1
     for (int j0 = 0; j0 < J; j0 += 8) {
+      const int jn = J - j0 < 8 ? J - j0 : 8;
+      bool any = false;
+      for (int jj = 0; jj < jn; ++jj) any |= s_off[j0 + jj] <= wlast;
+      if (!any) continue;
       {
         __syncwarp();
 #pragma unroll
-        for (int mt = 0; mt < 2; ++mt) {
+        for (int mt = 0; mt < kMT; ++mt) {
           const int ra = min(wn0 + mt * 16 + g, N - 1), rb = min(wn0 + mt * 16 + g + 8, N - 1);
           const __nv_bfloat16* qa = qbase + (int64_t)ra * p.sqn + 2 * t4;
           const __nv_bfloat16* qb2 = qbase + (int64_t)rb * p.sqn + 2 * t4;
@@ -388,34 +421,60 @@ __global__ void __launch_bounds__(kRThreads, 1) dsqg_resident_kernel(const DsqgP
         }
         __syncwarp();
       }
-      const float* my_qe = qe_buf + lane * kQeLd;
-      const int jn = J - j0 < 8 ? J - j0 : 8;
+      const float* my_qe = qe_buf + qi * kQeLd;
 #pragma unroll 1
       for (int jj = 0; jj < jn; ++jj) {
         const int j = j0 + jj;
+        if (s_off[j] > wlast) continue;
         const int s = n - s_off[j];
         const bool valid = row_ok && s >= 0;
         const int src = valid ? s : 0;
         const bool large = j >= js;  // warp-uniform
-        float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (large) z4 = __ldg(reinterpret_cast<const float4*>(zbase + (int64_t)src * p.szn));
+        float zz[kPL];
+#pragma unroll
+        for (int pl = 0; pl < kPL; ++pl) zz[pl] = 0.f;
+        if (large) {
+          if constexpr (TPQ == 1) {
+            const float4 z4 = __ldg(reinterpret_cast<const float4*>(zbase + (int64_t)src * p.szn));
+            zz[0] = z4.x; zz[1] = z4.y; zz[2] = z4.z; zz[3] = z4.w;
+          } else {
+            const float2 z2 = __ldg(reinterpret_cast<const float2*>(zbase + (int64_t)src * p.szn));
+            zz[0] = z2.x; zz[1] = z2.y;
+          }
+        }
 
         // score: q . k_src in the denormal domain, + q . bf16(E_j), + bias
-        const uint4* kr = reinterpret_cast<const uint4*>(s_kc + src * 48);
-        const uint4 k0 = kr[0], k1 = kr[1], k2 = kr[2];
+        uint32_t kw[kW];
+        if constexpr (TPQ == 1) {
+          const uint4* kr = reinterpret_cast<const uint4*>(s_kc + src * 48);
+          const uint4 k0 = kr[0], k1 = kr[1], k2 = kr[2];
+          kw[0] = k0.x; kw[1] = k0.y; kw[2] = k0.z; kw[3] = k0.w; kw[4] = k1.x; kw[5] = k1.y;
+          kw[6] = k1.z; kw[7] = k1.w; kw[8] = k2.x; kw[9] = k2.y; kw[10] = k2.z; kw[11] = k2.w;
+        } else {
+          const uint2* kr = reinterpret_cast<const uint2*>(s_kc + src * 48 + 24 * hf);
+          const uint2 k0 = kr[0], k1 = kr[1], k2 = kr[2];
+          kw[0] = k0.x; kw[1] = k0.y; kw[2] = k1.x; kw[3] = k1.y; kw[4] = k2.x; kw[5] = k2.y;
+        }
         const float sk = __half2float(s_ks[src]) * (1.0f / 31.0f);
-        const float P = (dot16x2(k0.x, k0.y, k0.z, qs) + dot16x2(k0.w, k1.x, k1.y, qs + 16)) +
-                        (dot16x2(k1.z, k1.w, k2.x, qs + 32) + dot16x2(k2.y, k2.z, k2.w, qs + 48));
+        float P;
+        if constexpr (TPQ == 1) {
+          P = (dot16x2(kw[0], kw[1], kw[2], qs) + dot16x2(kw[3], kw[4], kw[5], qs + 16)) +
+              (dot16x2(kw[6], kw[7], kw[8], qs + 32) + dot16x2(kw[9], kw[10], kw[11], qs + 48));
+        } else {
+          const float part = dot16x2(kw[0], kw[1], kw[2], qs) + dot16x2(kw[3], kw[4], kw[5], qs + 16);
+          const float other = __shfl_xor_sync(0xffffffffu, part, 1);
+          P = hf == 0 ? part + other : other + part;  // same sum order in both threads
+        }
         const float part = fmaf(P, c1, qbias) * sk;
         float s2 = fmaf(part + my_qe[jj], c_score, s_pb[j]);
         s2 = valid ? s2 : -INFINITY;
         if (s2 > m + kRescaleLog2) {
           const float f = ex2_approx(m - s2);
 #pragma unroll
-          for (int i = 0; i < 64; ++i) acc[i] *= f;
+          for (int i = 0; i < kD; ++i) acc[i] *= f;
           l *= f; wbias *= f;
 #pragma unroll
-          for (int pl = 0; pl < 4; ++pl) { corr_a[pl] *= f; corr_b[pl] *= f; }
+          for (int pl = 0; pl < kPL; ++pl) { corr_a[pl] *= f; corr_b[pl] *= f; }
           m = s2;
         }
         const float w = valid ? ex2_approx(s2 - m) : 0.0f;
@@ -423,24 +482,30 @@ __global__ void __launch_bounds__(kRThreads, 1) dsqg_resident_kernel(const DsqgP
         const float wv = w * sv;
         l += w;
         wbias += wv;
-        const uint4* vr = reinterpret_cast<const uint4*>(s_vc + src * 48);
-        const uint4 v0 = vr[0], v1 = vr[1], v2 = vr[2];
+        uint32_t vw[kW];
+        if constexpr (TPQ == 1) {
+          const uint4* vr = reinterpret_cast<const uint4*>(s_vc + src * 48);
+          const uint4 v0 = vr[0], v1 = vr[1], v2 = vr[2];
+          vw[0] = v0.x; vw[1] = v0.y; vw[2] = v0.z; vw[3] = v0.w; vw[4] = v1.x; vw[5] = v1.y;
+          vw[6] = v1.z; vw[7] = v1.w; vw[8] = v2.x; vw[9] = v2.y; vw[10] = v2.z; vw[11] = v2.w;
+        } else {
+          const uint2* vr = reinterpret_cast<const uint2*>(s_vc + src * 48 + 24 * hf);
+          const uint2 v0 = vr[0], v1 = vr[1], v2 = vr[2];
+          vw[0] = v0.x; vw[1] = v0.y; vw[2] = v1.x; vw[3] = v1.y; vw[4] = v2.x; vw[5] = v2.y;
+        }
         const float wvs = wv * kVPreScale;
-        axpy16x2(v0.x, v0.y, v0.z, wvs, acc);
-        axpy16x2(v0.w, v1.x, v1.y, wvs, acc + 16);
-        axpy16x2(v1.z, v1.w, v2.x, wvs, acc + 32);
-        axpy16x2(v2.y, v2.z, v2.w, wvs, acc + 48);
+#pragma unroll
+        for (int sl = 0; sl < kSL; ++sl) axpy16x2(vw[3 * sl], vw[3 * sl + 1], vw[3 * sl + 2], wvs, acc + 16 * sl);
         if (large) {
           // MOVT: rotate plane r (channels 16 r + rot, + 1) by theta; keep
           // rotated-minus-unrotated so the plain accumulation above stays.
           const int jl = j - js;
-          const uint32_t vw[12] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w, v2.x, v2.y, v2.z, v2.w};
-          const float zz[4] = {z4.x, z4.y, z4.z, z4.w};
 #pragma unroll
-          for (int pl = 0; pl < 4; ++pl) {
+          for (int pl = 0; pl < kPL; ++pl) {
+            const int gp = kPL * hf + pl;  // plane index in the head
             float fa, fb;
             movt_pair<PW>(vw[3 * pl], vw[3 * pl + 1], vw[3 * pl + 2], rot_off, fa, fb);
-            const float theta = fmaf(s_pgain[jl * 4 + pl] * gy[pl], zz[pl], s_pbase[jl * 4 + pl]);
+            const float theta = fmaf(s_pgain[jl * 4 + gp] * gy[pl], zz[pl], s_pbase[jl * 4 + gp]);
             float sn, cs;
             __sincosf(theta, &sn, &cs);
             const float cm1 = cs - 1.0f;
@@ -456,10 +521,11 @@ __global__ void __launch_bounds__(kRThreads, 1) dsqg_resident_kernel(const DsqgP
     // corrections, normalise, optional gain / gate, bf16 store.
     const float bias = 32.0f * wbias;
     const float inv_l = l > 0.0f ? 1.0f / l : 0.0f;
-    __nv_bfloat16* orow = p.out + b * p.sob + h * p.soh + (int64_t)n * p.son;
-    const __nv_bfloat16* grow = p.gate != nullptr ? p.gate + b * p.sgtb + (int64_t)n * p.sgtn + h * 64 : nullptr;
+    __nv_bfloat16* orow = p.out + b * p.sob + h * p.soh + (int64_t)n * p.son + kD * hf;
+    const __nv_bfloat16* grow =
+        p.gate != nullptr ? p.gate + b * p.sgtb + (int64_t)n * p.sgtn + h * 64 + kD * hf : nullptr;
 #pragma unroll
-    for (int sl = 0; sl < 4; ++sl) {
+    for (int sl = 0; sl < kSL; ++sl) {
       float o[16];
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
@@ -495,7 +561,7 @@ __global__ void __launch_bounds__(kRThreads, 1) dsqg_resident_kernel(const DsqgP
       dst[0] = packed[0];
       dst[1] = packed[1];
     }
-    if (p.lse != nullptr)
+    if (p.lse != nullptr && hf == 0)
       p.lse[b * p.slb + h * p.slh + (int64_t)n * p.sln] = l > 0.0f ? m * 0.6931471805599453f + logf(l) : -INFINITY;
   }
 }
@@ -516,11 +582,21 @@ int dsqg_resident_launch(const DsqgParams& p, int64_t B, cudaStream_t stream) {
   const ResLayout L((int)p.N, p.J, p.j_large);
   if (p.N > 4096 || L.bytes > (uint32_t)kRSmemLimit || B > 65535 || p.H > 65535) return kNotApplicable;
   const int pw = (6 * p.plane_shift) >> 5;
-  auto kernel = pw == 0 ? dsqg_resident_kernel<0> : (pw == 1 ? dsqg_resident_kernel<1> : dsqg_resident_kernel<2>);
+  // Threads per query: 2 by default; DWARF_DSQG_RES_TPQ=1 selects one thread per query.
+  static const int tpq = [] {
+    const char* e = getenv("DWARF_DSQG_RES_TPQ");
+    return (e && e[0] == '1') ? 1 : 2;
+  }();
+  using KernelFn = void (*)(const DsqgParams, int32_t*);
+  KernelFn kernel;
+  if (tpq == 1)
+    kernel = pw == 0 ? dsqg_resident_kernel<0, 1> : (pw == 1 ? dsqg_resident_kernel<1, 1> : dsqg_resident_kernel<2, 1>);
+  else
+    kernel = pw == 0 ? dsqg_resident_kernel<0, 2> : (pw == 1 ? dsqg_resident_kernel<1, 2> : dsqg_resident_kernel<2, 2>);
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.bytes) != cudaSuccess)
     return DWARF_ERR_LAUNCH;
   dim3 grid((unsigned)p.H, (unsigned)B);
-  kernel<<<grid, kRThreads, L.bytes, stream>>>(p, p.status);
+  kernel<<<grid, 256 * tpq, L.bytes, stream>>>(p, p.status);
   return launch_status();
 }
 
