@@ -154,6 +154,12 @@ def _fields(spec: str):
     return out
 
 
+class EmaGradAlphaArgs(ctypes.Structure):
+    _fields_ = _fields("""version:i32, dtype:i32, x:ptr, y:ptr, g:ptr, batch:i64, seq_len:i64, width:i64,
+        sxb:i64, sxn:i64, sxd:i64, syb:i64, syn:i64, syd:i64, sgb:i64, sgn:i64, sgd:i64,
+        alpha:ptr, alpha_per_channel:i32, pad_:i32, da:ptr""")
+
+
 class Q6PackArgs(ctypes.Structure):
     _fields_ = _fields("""version:i32, dtype:i32, x:ptr, B:i64, H:i64, T:i64, sxb:i64, sxh:i64, sxt:i64,
         codes:ptr, scb:i64, sch:i64, sct:i64, scales:ptr, ssb:i64, ssh:i64, sst:i64""")
@@ -266,6 +272,7 @@ _ENTRY_POINTS = {
     "dwarf_npci_rotate": NpciArgs,
     "dwarf_ema_scan": EmaScanArgs,
     "dwarf_ema_scan_noalloc": EmaScanArgs,
+    "dwarf_ema_scan_grad_alpha": EmaGradAlphaArgs,
     "dwarf_q6_pack": Q6PackArgs,
     "dwarf_q6_unpack": Q6UnpackArgs,
     "dwarf_dsqg_fwd": DsqgFwdArgs,

@@ -14,8 +14,11 @@ Extra entry point of this engine:
 
 The scan runs as one CUDA launch (``dwarf_ema_scan`` in the C ABI): a chunked
 scan chained by decoupled look-back, fp32 state, output in the dtype of ``x``.
-This is a forward (inference) engine: a call that would need autograd raises
-``NotImplementedError``; CPU tensors raise ``RuntimeError``.
+Both scans are differentiable (``_CausalEMAFn``, the counterpart of the
+reference's ``_CausalEMAFn`` :265-364): the input gradient is the same scan run
+over time-reversed ``dy`` (a negative time stride, no copy), and the alpha
+gradient is one fused reduction (``dwarf_ema_scan_grad_alpha``). CPU tensors
+raise ``RuntimeError``.
 """
 
 from __future__ import annotations
@@ -94,11 +97,96 @@ def _launch(x: torch.Tensor, out: torch.Tensor, alpha: torch.Tensor, per_channel
     _lib.call("dwarf_ema_scan", args, x.device)
 
 
-def _forward_only(*tensors: torch.Tensor) -> None:
-    if torch.is_grad_enabled() and any(t.requires_grad for t in tensors):
-        raise NotImplementedError(
-            "dwarf_v2_b200 is a forward (inference) engine; run under torch.no_grad()"
-        )
+def _needs_grad(*tensors: torch.Tensor) -> bool:
+    return torch.is_grad_enabled() and any(t.requires_grad for t in tensors)
+
+
+def _launch_reversed(src: torch.Tensor, dst: torch.Tensor, alpha: torch.Tensor, per_channel: bool) -> None:
+    """dst[t] = alpha*src[t] + (1-alpha)*dst[t+1] (dst[T] = 0): the forward scan
+    walked from the last token to the first through negative time strides."""
+    lib = _lib.load()
+    batch, seq_len, width = src.shape
+    code = _lib.dtype_code(src.dtype)
+    nbytes = int(lib.dwarf_ema_scan_workspace_bytes(batch, seq_len, width, code))
+    ws = _workspace(src.device, nbytes)
+    last = seq_len - 1
+    args = _lib.EmaScanArgs(
+        version=_lib.ABI_VERSION, dtype=code,
+        x=src.data_ptr() + last * src.stride(1) * src.element_size(),
+        y=dst.data_ptr() + last * dst.stride(1) * dst.element_size(),
+        batch=batch, seq_len=seq_len, width=width,
+        sxb=src.stride(0), sxn=-src.stride(1), sxd=src.stride(2),
+        syb=dst.stride(0), syn=-dst.stride(1), syd=dst.stride(2),
+        alpha=alpha.data_ptr(), alpha_per_channel=int(per_channel), clamp=0,
+        floor_=0.0, ceiling=1.0,
+        workspace=ws.data_ptr(), workspace_bytes=ws.numel(),
+        device_status=_lib.device_status_word(src.device).data_ptr(),
+        init_state=None, final_state=None,
+    )
+    _lib.call("dwarf_ema_scan", args, src.device)
+
+
+def _grad_alpha(x: torch.Tensor, y: torch.Tensor, g: torch.Tensor, alpha: torch.Tensor,
+                per_channel: bool) -> torch.Tensor:
+    """sum over (b, t) of (g / alpha) * (x[t] - y[t-1]) per channel (or in total)."""
+    da = torch.empty(x.shape[-1] if per_channel else 1, dtype=torch.float32, device=x.device)
+    args = _lib.EmaGradAlphaArgs(
+        version=_lib.ABI_VERSION, dtype=_lib.dtype_code(x.dtype),
+        x=x.data_ptr(), y=y.data_ptr(), g=g.data_ptr(),
+        batch=x.shape[0], seq_len=x.shape[1], width=x.shape[2],
+        sxb=x.stride(0), sxn=x.stride(1), sxd=x.stride(2),
+        syb=y.stride(0), syn=y.stride(1), syd=y.stride(2),
+        sgb=g.stride(0), sgn=g.stride(1), sgd=g.stride(2),
+        alpha=alpha.data_ptr(), alpha_per_channel=int(per_channel), pad_=0, da=da.data_ptr(),
+    )
+    _lib.call("dwarf_ema_scan_grad_alpha", args, x.device)
+    return da
+
+
+class _CausalEMAFn(torch.autograd.Function):
+    """Differentiable scan (reference _CausalEMAFn, causal_ema_scan.py:265-364).
+
+    backward: the reverse-time state s[t] = dy[t] + (1-alpha) s[t+1] gives
+    dx = alpha * s, which is the forward recurrence run backwards in time over
+    dy; d alpha = sum s[t] * (x[t] - y[t-1]). For the scalar API the clamp's
+    projected derivative is applied as the reference does (:355-363).
+    """
+
+    @staticmethod
+    def forward(ctx, x, alpha_input, floor, ceiling, per_channel):
+        x = x.contiguous()
+        if per_channel:
+            alpha = alpha_input.detach().reshape(-1).to(device=x.device, dtype=torch.float32).contiguous()
+        else:
+            alpha = alpha_input.detach().reshape(1).to(device=x.device, dtype=torch.float32)
+            alpha = alpha.clamp(float(floor), float(ceiling))
+        out = torch.empty_like(x)
+        _launch(x, out, alpha, per_channel, False, 0.0, 1.0)
+        ctx.save_for_backward(x, out, alpha_input, alpha)
+        ctx.floor, ctx.ceiling, ctx.per_channel = float(floor), float(ceiling), bool(per_channel)
+        return out
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, y, alpha_input, alpha = ctx.saved_tensors
+        dy = dy.contiguous()
+        need_da = bool(ctx.needs_input_grad[1])
+        if need_da and dy.dtype != torch.float32:
+            g = torch.empty(dy.shape, dtype=torch.float32, device=dy.device)
+            _launch_reversed(dy.float(), g, alpha, ctx.per_channel)
+            dx = g.to(dy.dtype)
+        else:
+            dx = torch.empty_like(dy)
+            _launch_reversed(dy, dx, alpha, ctx.per_channel)
+            g = dx
+        if not need_da:
+            return dx, None, None, None, None
+        da = _grad_alpha(x, y, g, alpha, ctx.per_channel)
+        da = da.reshape_as(alpha_input).to(alpha_input.dtype)
+        if not ctx.per_channel:
+            blocked = ((alpha_input <= ctx.floor) & (da > 0)) | ((alpha_input >= ctx.ceiling) & (da < 0))
+            da = torch.where(blocked, torch.zeros_like(da), da)
+        return dx, da, None, None, None
 
 
 def causal_ema_scan(
@@ -126,9 +214,12 @@ def causal_ema_scan(
     if reset_mask is not None:
         raise NotImplementedError("reset-aware EMA is not part of the prefill engine")
     _lib.require_cuda(x)
-    _forward_only(x, ema_factor)
     if x.dtype not in (torch.float32, torch.bfloat16):
         raise TypeError(f"causal_ema_scan supports float32/bfloat16 input, got {x.dtype}")
+    if _needs_grad(x, ema_factor):
+        if initial_state is not None or return_final_state:
+            raise NotImplementedError("initial_state / return_final_state are inference-only")
+        return _CausalEMAFn.apply(x, ema_factor, float(floor), float(ceiling), False)
     alpha = ema_factor.detach().reshape(1).to(device=x.device, dtype=torch.float32)
     out = torch.empty(x.shape, dtype=x.dtype, device=x.device)
     B, _, D = x.shape
@@ -152,9 +243,10 @@ def causal_ema_scan_per_channel(x: torch.Tensor, alpha: torch.Tensor) -> torch.T
     if alpha.numel() != x.shape[-1]:
         raise ValueError(f"alpha must have {x.shape[-1]} entries, got {alpha.numel()}")
     _lib.require_cuda(x)
-    _forward_only(x, alpha)
     if x.dtype not in (torch.float32, torch.bfloat16):
         raise TypeError(f"causal_ema_scan supports float32/bfloat16 input, got {x.dtype}")
+    if _needs_grad(x, alpha):
+        return _CausalEMAFn.apply(x, alpha, 0.0, 1.0, True)
     alpha32 = alpha.detach().reshape(-1).to(device=x.device, dtype=torch.float32).contiguous()
     out = torch.empty(x.shape, dtype=x.dtype, device=x.device)
     _launch(x, out, alpha32, True, False, 0.0, 1.0)

@@ -368,6 +368,156 @@ int launch_ema(const dwarf_ema_scan_args* a, const EmaPlan& p, cudaStream_t stre
                                   : launch_ema_lb<T, VEC, TS, WARPS, kLookbackFew>(a, p, stream);
 }
 
+
+// ---- d alpha: sum over (b, t) of g * (x[t] - y[t-1]), divided by alpha per channel.
+// Block = 128 threads across channels (4 each) x kGradGroups row groups of
+// kGradRowsPerThread consecutive tokens (kGradRows per block, one batch row);
+// y[t-1] is carried from the previous token inside a group, so x, y and g are
+// read once plus one y row per group. The groups are summed in shared memory,
+// then one atomic per channel (per-channel alpha) or per block (scalar alpha).
+__device__ __forceinline__ float to_f32(float v) { return v; }
+__device__ __forceinline__ float to_f32(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+constexpr int kGradThreads = 128;
+constexpr int kGradGroups = 8;
+constexpr int kGradRowsPerThread = 8;
+constexpr int kGradRows = kGradGroups * kGradRowsPerThread;
+
+template <typename T>
+struct Vec4;
+template <>
+struct Vec4<float> {
+  __device__ static void load(const float* p, float (&o)[4]) {
+    const float4 v = __ldg(reinterpret_cast<const float4*>(p));
+    o[0] = v.x; o[1] = v.y; o[2] = v.z; o[3] = v.w;
+  }
+};
+template <>
+struct Vec4<__nv_bfloat16> {
+  __device__ static void load(const __nv_bfloat16* p, float (&o)[4]) {
+    const uint2 v = __ldg(reinterpret_cast<const uint2*>(p));
+    o[0] = __uint_as_float(v.x << 16); o[1] = __uint_as_float(v.x & 0xffff0000u);
+    o[2] = __uint_as_float(v.y << 16); o[3] = __uint_as_float(v.y & 0xffff0000u);
+  }
+};
+
+// VECTOR: 4 consecutive channels per thread read as one 16-B (fp32) or 8-B
+// (bf16) load; requires unit channel strides, width % 4 == 0 and aligned rows.
+template <typename T, bool VECTOR>
+__global__ void __launch_bounds__(kGradThreads * kGradGroups) ema_grad_alpha_kernel(
+    const T* __restrict__ x, const T* __restrict__ y, const float* __restrict__ g, int64_t seq_len, int64_t width,
+    int64_t sxb, int64_t sxn, int64_t sxd, int64_t syb, int64_t syn, int64_t syd, int64_t sgb, int64_t sgn,
+    int64_t sgd, const float* __restrict__ alpha, int per_channel, float* __restrict__ da) {
+  constexpr int VEC = 4;
+  const int64_t c0 = ((int64_t)blockIdx.x * kGradThreads + threadIdx.x) * VEC;
+  const int64_t t0 = (int64_t)blockIdx.y * kGradRows + (int64_t)threadIdx.y * kGradRowsPerThread;
+  const int64_t b = blockIdx.z;
+  const bool active = c0 < width && t0 < seq_len;
+  float acc[VEC];
+#pragma unroll
+  for (int v = 0; v < VEC; ++v) acc[v] = 0.0f;
+  if (active) {
+    float prev[VEC];
+#pragma unroll
+    for (int v = 0; v < VEC; ++v) prev[v] = 0.0f;
+    const int64_t t1 = t0 + kGradRowsPerThread < seq_len ? t0 + kGradRowsPerThread : seq_len;
+    if constexpr (VECTOR) {
+      const T* xp = x + b * sxb + c0;
+      const T* yp = y + b * syb + c0;
+      const float* gp = g + b * sgb + c0;
+      if (t0 > 0) Vec4<T>::load(yp + (t0 - 1) * syn, prev);
+#pragma unroll
+      for (int i = 0; i < kGradRowsPerThread; ++i) {
+        const int64_t t = t0 + i;
+        if (t >= t1) break;
+        float xv[4], yv[4], gv[4];
+        Vec4<T>::load(xp + t * sxn, xv);
+        Vec4<T>::load(yp + t * syn, yv);
+        Vec4<float>::load(gp + t * sgn, gv);
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) {
+          acc[v] = fmaf(gv[v], xv[v] - prev[v], acc[v]);
+          prev[v] = yv[v];
+        }
+      }
+    } else {
+      if (t0 > 0) {
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) {
+          const int64_t c = c0 + v;
+          if (c < width) prev[v] = to_f32(y[b * syb + (t0 - 1) * syn + c * syd]);
+        }
+      }
+      for (int64_t t = t0; t < t1; ++t) {
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) {
+          const int64_t c = c0 + v;
+          if (c < width) {
+            const float xv = to_f32(x[b * sxb + t * sxn + c * sxd]);
+            const float gv = g[b * sgb + t * sgn + c * sgd];
+            acc[v] = fmaf(gv, xv - prev[v], acc[v]);
+            prev[v] = to_f32(y[b * syb + t * syn + c * syd]);
+          }
+        }
+      }
+    }
+  }
+  // Sum the row groups: thread (c, 0) ends with the block's partial for its channels.
+  __shared__ float red[kGradGroups][kGradThreads * VEC];
+#pragma unroll
+  for (int v = 0; v < VEC; ++v) red[threadIdx.y][threadIdx.x * VEC + v] = acc[v];
+  __syncthreads();
+  if (threadIdx.y != 0) return;
+#pragma unroll
+  for (int v = 0; v < VEC; ++v) {
+    float sum = 0.0f;
+#pragma unroll
+    for (int k = 0; k < kGradGroups; ++k) sum += red[k][threadIdx.x * VEC + v];
+    acc[v] = sum;
+  }
+  if (per_channel) {
+    if (c0 < width) {
+#pragma unroll
+      for (int v = 0; v < VEC; ++v)
+        if (c0 + v < width) atomicAdd(da + c0 + v, acc[v] / alpha[c0 + v]);
+    }
+    return;
+  }
+  float sum = 0.0f;
+#pragma unroll
+  for (int v = 0; v < VEC; ++v) sum += acc[v];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  __shared__ float part[kGradThreads / 32];
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = sum;
+  asm volatile("bar.sync 1, %0;" ::"n"(kGradThreads));  // the kGradThreads threads of row group 0
+  if (threadIdx.x == 0) {
+    float total = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kGradThreads / 32; ++w) total += part[w];
+    atomicAdd(da, total / alpha[0]);
+  }
+}
+
+template <typename T>
+int launch_grad_alpha(const dwarf_ema_grad_alpha_args* a, cudaStream_t stream) {
+  constexpr int VEC = 4;
+  const int64_t cblocks = (a->width + (int64_t)kGradThreads * VEC - 1) / ((int64_t)kGradThreads * VEC);
+  const int64_t tblocks = (a->seq_len + kGradRows - 1) / kGradRows;
+  if (cblocks > 2147483647LL || tblocks > 65535 || a->batch > 65535) return DWARF_ERR_SHAPE;
+  const int64_t ve = 16 / (int64_t)sizeof(T);  // elements per 16 B: x/y rows aligned to 16 B
+  const bool vector_ok = a->sxd == 1 && a->syd == 1 && a->sgd == 1 && a->width % VEC == 0 &&
+                         aligned16(a->x) && aligned16(a->y) && aligned16(a->g) && a->sxb % ve == 0 &&
+                         a->sxn % ve == 0 && a->syb % ve == 0 && a->syn % ve == 0 && a->sgb % 4 == 0 &&
+                         a->sgn % 4 == 0;
+  dim3 grid((unsigned)cblocks, (unsigned)tblocks, (unsigned)a->batch);
+  auto kernel = vector_ok ? ema_grad_alpha_kernel<T, true> : ema_grad_alpha_kernel<T, false>;
+  kernel<<<grid, dim3(kGradThreads, kGradGroups), 0, stream>>>(
+      static_cast<const T*>(a->x), static_cast<const T*>(a->y), a->g, a->seq_len, a->width, a->sxb, a->sxn,
+      a->sxd, a->syb, a->syn, a->syd, a->sgb, a->sgn, a->sgd, a->alpha, a->alpha_per_channel, a->da);
+  return launch_status();
+}
+
 }  // namespace
 }  // namespace dwarf
 
@@ -452,4 +602,18 @@ extern "C" int dwarf_ema_scan_noalloc(const dwarf_ema_scan_args* a, void* stream
   local.workspace = scratch;
   local.workspace_bytes = DWARF_EMA_NOALLOC_SCRATCH_BYTES;
   return dwarf_ema_scan(&local, stream_);
+}
+
+extern "C" int dwarf_ema_scan_grad_alpha(const dwarf_ema_grad_alpha_args* a, void* stream_) {
+  DWARF_CHECK_VERSION(a);
+  if (a->dtype != DWARF_F32 && a->dtype != DWARF_BF16) return DWARF_ERR_DTYPE;
+  if (a->batch < 0 || a->seq_len < 0 || a->width < 0) return DWARF_ERR_SHAPE;
+  if (!a->da || !a->alpha) return DWARF_ERR_NULL;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  const size_t out_bytes = (a->alpha_per_channel ? (size_t)a->width : 1u) * sizeof(float);
+  if (cudaMemsetAsync(a->da, 0, out_bytes, stream) != cudaSuccess) return DWARF_ERR_LAUNCH;
+  if (a->batch == 0 || a->seq_len == 0 || a->width == 0) return DWARF_OK;
+  if (!a->x || !a->y || !a->g) return DWARF_ERR_NULL;
+  if (a->dtype == DWARF_F32) return launch_grad_alpha<float>(a, stream);
+  return launch_grad_alpha<__nv_bfloat16>(a, stream);
 }

@@ -98,6 +98,38 @@ int64_t dwarf_ema_scan_workspace_bytes(int64_t batch, int64_t seq_len, int64_t w
                                        int32_t dtype);
 int dwarf_ema_scan(const dwarf_ema_scan_args* args, void* stream);
 
+/* Gradient of the causal EMA scan with respect to alpha.
+ *
+ * Replaces the COMPUTE_DA part of _bwd_apply (kernels/causal_ema_scan.py:204-260,
+ * launched by _CausalEMAFn.backward :315-364):
+ *     da[d] = sum_{b,t} s[b,t,d] * (x[b,t,d] - y[b,t-1,d]),   y[b,-1,d] = 0
+ * where s is the reverse-time state s[t] = dy[t] + (1 - alpha_d) s[t+1].
+ * The caller passes g = alpha_d * s, which is exactly the input gradient dx
+ * (dwarf_ema_scan run over time-reversed dy), in fp32; the kernel divides each
+ * channel's partial sum by alpha_d. x and y (the forward output) are in
+ * `dtype`. alpha_per_channel = 0: one alpha and one output value (summed over
+ * channels too); 1: `width` alphas and `width` outputs. `da` is overwritten
+ * (zeroed on the stream, then accumulated with atomics, so the summation order
+ * and the last bits vary between runs).
+ * ---------------------------------------------------------------------- */
+typedef struct {
+  int32_t version;
+  int32_t dtype;              /* dtype of x and y: DWARF_F32 or DWARF_BF16  */
+  const void* x;              /* [batch, seq_len, width]                    */
+  const void* y;              /* [batch, seq_len, width] forward output     */
+  const float* g;             /* [batch, seq_len, width] fp32 alpha * state */
+  int64_t batch, seq_len, width;
+  int64_t sxb, sxn, sxd;      /* element strides of x                       */
+  int64_t syb, syn, syd;      /* element strides of y                       */
+  int64_t sgb, sgn, sgd;      /* element strides of g                       */
+  const float* alpha;         /* fp32: 1 value or `width` values            */
+  int32_t alpha_per_channel;
+  int32_t pad_;
+  float* da;                  /* fp32 [1] or [width]                        */
+} dwarf_ema_grad_alpha_args;
+
+int dwarf_ema_scan_grad_alpha(const dwarf_ema_grad_alpha_args* args, void* stream);
+
 /* Causal EMA scan that allocates nothing and needs no caller workspace.
  *
  * No counterpart in the reference: this entry point exists for callers that

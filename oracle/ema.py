@@ -31,3 +31,29 @@ def ema_scan(x: np.ndarray, alpha, *, clamp: tuple[float, float] | None = None) 
 def ema_scan_decay_form(x: np.ndarray, decay_a: np.ndarray) -> np.ndarray:
     """``y_t = a*y_{t-1} + (1-a)*x_t`` per channel: the same scan with alpha = 1 - a."""
     return ema_scan(x, 1.0 - np.asarray(decay_a, dtype=np.float64))
+
+
+def ema_scan_backward(x: np.ndarray, y: np.ndarray, dy: np.ndarray, alpha, *, per_channel: bool = False):
+    """Gradients of ``ema_scan`` (reference _bwd_local/_bwd_carry/_bwd_apply,
+    kernels/causal_ema_scan.py:157-260; _CausalEMAFn.backward :315-364).
+
+    ``alpha`` is the (already clamped) scalar or per-channel factor, ``y`` the
+    forward output. Reverse-time state ``s[t] = dy[t] + (1-alpha) s[t+1]``,
+    ``dx = alpha * s`` and ``d alpha = sum s[t] * (x[t] - y[t-1])`` (y[-1] = 0),
+    summed over (b, t) per channel, and over channels too for a scalar alpha.
+    Returns fp64 (dx [B,N,D], d_alpha [D] or scalar); the clamp's projected
+    derivative (:355-363) is the caller's.
+    """
+    xf, yf, g = (np.asarray(a, dtype=np.float64) for a in (x, y, dy))
+    a = np.asarray(alpha, dtype=np.float64).reshape(-1)
+    a = np.broadcast_to(a, (xf.shape[2],))
+    decay = 1.0 - a
+    state = np.zeros((xf.shape[0], xf.shape[2]), dtype=np.float64)
+    dx = np.empty_like(xf)
+    da = np.zeros(xf.shape[2], dtype=np.float64)
+    for t in range(xf.shape[1] - 1, -1, -1):
+        state = g[:, t] + decay * state
+        dx[:, t] = a * state
+        prev = yf[:, t - 1] if t > 0 else 0.0
+        da += (state * (xf[:, t] - prev)).sum(axis=0)
+    return dx, (da if per_channel else da.sum())

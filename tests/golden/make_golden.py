@@ -86,6 +86,46 @@ def make_ema() -> None:
     save("ema_per_channel_f32", x=x, decay=decay, y=y)
 
 
+def make_ema_backward() -> None:
+    """Backward golden vectors: autograd through the reference's own oracle
+    ``_reference`` (kernels/causal_ema_scan.py:511-538), the function the
+    reference's gradcheck (:570-581) validates its kernels against."""
+    _import_reference()
+    import causal_ema_scan as ref
+
+    def grads(x, alpha, dy, floor, ceiling):
+        x = x.clone().requires_grad_(True)
+        alpha = alpha.clone().requires_grad_(True)
+        y = ref._reference(x, alpha, floor, ceiling)
+        dx, da = torch.autograd.grad(y, (x, alpha), dy)
+        return y.detach(), dx, da
+
+    # The reference __main__ shape, fp64, alpha = 0.05 inside the bounds.
+    torch.manual_seed(1)
+    x = torch.randn(2, 9, 7, dtype=torch.float64)
+    alpha = ref.bounded_ema_factor(torch.tensor(ref.inverse_bounded_ema_factor(0.05), dtype=torch.float64))
+    alpha = alpha.reshape(1)
+    dy = torch.randn(2, 9, 7, dtype=torch.float64)
+    y, dx, da = grads(x, alpha, dy, 1e-5, 0.5)
+    save("ema_bwd_scalar_f64", x=x, alpha=alpha, dy=dy, y=y, dx=dx, da=da)
+
+    # fp32, ragged sizes, alpha = 1/64 (the model's second packet scale).
+    g = torch.Generator().manual_seed(21)
+    x = torch.randn(3, 200, 96, generator=g, dtype=torch.float32)
+    dy = torch.randn(3, 200, 96, generator=g, dtype=torch.float32)
+    alpha = torch.tensor([1.0 / 64.0], dtype=torch.float32)
+    y, dx, da = grads(x, alpha, dy, 1e-5, 0.5)
+    save("ema_bwd_scalar_f32", x=x, alpha=alpha, dy=dy, y=y, dx=dx, da=da)
+
+    # Per-channel alpha = 1 - sigmoid(N(0,1)) with bounds that never bind.
+    g = torch.Generator().manual_seed(22)
+    x = torch.randn(2, 300, 64, generator=g, dtype=torch.float32)
+    dy = torch.randn(2, 300, 64, generator=g, dtype=torch.float32)
+    alpha = 1.0 - torch.sigmoid(torch.randn(64, generator=g))
+    y, dx, da = grads(x, alpha, dy, 1e-12, 1.0 - 1e-12)
+    save("ema_bwd_per_channel_f32", x=x, alpha=alpha, dy=dy, y=y, dx=dx, da=da)
+
+
 def _dsqg_case(module, q, k, v):
     """Reference tables + probe projections exactly as DSQGAttentionV19.forward builds them."""
     import torch.nn.functional as F
@@ -401,7 +441,7 @@ def make_checkpoint() -> None:
 
 def main(argv: list[str]) -> None:
     which = argv[1] if len(argv) > 1 else "all"
-    makers = {"ema": make_ema, "dsqg": make_dsqg, "hisa": make_hisa, "model": make_model,
+    makers = {"ema": make_ema, "ema_bwd": make_ema_backward, "dsqg": make_dsqg, "hisa": make_hisa, "model": make_model,
               "checkpoint": make_checkpoint}
     for name, maker in makers.items():
         if which in ("all", name):
