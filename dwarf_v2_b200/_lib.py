@@ -182,6 +182,13 @@ class DsqgFwdArgs(ctypes.Structure):
         head_gain:ptr, head_gain_dtype:i32, gate:ptr, sgb_:i64, sgn_:i64, device_status:ptr, row_begin:i64, pos:ptr""")
 
 
+class DsqgBwdArgs(ctypes.Structure):
+    _fields_ = _fields("""version:i32, J:i32, j_small:i32, j_large:i32, plane_shift:i32, query_start:i32,
+        B:i64, H:i64, H_kv:i64, N:i64, q:ptr, k:ptr, v:ptr, out:ptr, dout:ptr, lse:ptr, offsets:ptr,
+        pos_bias:ptr, scale_embed:ptr, phase_base:ptr, phase_gain:ptr, y_pre:ptr, z_pre:ptr,
+        dq:ptr, dk:ptr, dv:ptr, dy_pre:ptr, dz_pre:ptr, ds:ptr, delta:ptr, d_phase_base:ptr, d_phase_gain:ptr""")
+
+
 class DsqgPrepArgs(ctypes.Structure):
     _fields_ = _fields("""version:i32, pack_q6:i32, B:i64, H:i64, H_kv:i64, N:i64,
         q:ptr, sqb:i64, sqh:i64, sqn:i64, k:ptr, skb:i64, skh:i64, skn:i64, v:ptr, svb:i64, svh:i64, svn:i64,
@@ -276,6 +283,7 @@ _ENTRY_POINTS = {
     "dwarf_q6_pack": Q6PackArgs,
     "dwarf_q6_unpack": Q6UnpackArgs,
     "dwarf_dsqg_fwd": DsqgFwdArgs,
+    "dwarf_dsqg_bwd": DsqgBwdArgs,
     "dwarf_dsqg_prep": DsqgPrepArgs,
 }
 

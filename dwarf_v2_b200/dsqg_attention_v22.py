@@ -402,6 +402,76 @@ def _forward_only(*tensors) -> None:
         raise NotImplementedError("dwarf_v2_b200 is a forward (inference) engine; run under torch.no_grad()")
 
 
+def _needs_grad(*tensors) -> bool:
+    return torch.is_grad_enabled() and any(isinstance(t, torch.Tensor) and t.requires_grad for t in tensors)
+
+
+class _DSQGFn(torch.autograd.Function):
+    """Differentiable DSQG over bf16 K/V (reference _DSQGV18GroupedFn,
+    dsqg_attention_v22.py:2197-2552): forward by ``dwarf_dsqg_fwd`` (which also
+    writes the natural-log lse), backward by ``dwarf_dsqg_bwd`` (dq, dk, dv,
+    dy_pre, dz_pre, phase-table gradients and the per-pair ds), then
+    d pos_bias = sum_{b,n} ds and d scale_embed = (1/8) sum ds q."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, pos_bias, scale_embed, phase_base, phase_gain, y_pre, z_pre,
+                offsets, j_small, j_large, plane_shift, query_start):
+        B, H, N, HD = q.shape
+        qb, kb, vb = (t.to(torch.bfloat16).contiguous() for t in (q, k, v))
+        J = int(j_small) + int(j_large)
+        pb, se, pbase, pgain, y32, z32, offs = _prepare_tables(
+            pos_bias, scale_embed, phase_base, phase_gain, y_pre, z_pre, offsets, q.device, J, int(j_large))
+        out = torch.empty(B, H, N, HD, dtype=torch.bfloat16, device=q.device)
+        lse = torch.empty(B, H, N, dtype=torch.float32, device=q.device)
+        _dsqg_launch(qb, kv=("bf16", kb, vb), pos_bias=pb, scale_embed=se, phase_base=pbase, phase_gain=pgain,
+                     y_pre=y32, z_pre=z32, offsets=offs, j_small=j_small, j_large=j_large,
+                     plane_shift=plane_shift, query_start=query_start, out=out, lse=lse)
+        ctx.save_for_backward(qb, kb, vb, out, lse, pb, se, pbase, pgain, y32, z32, offs)
+        ctx.meta = (int(j_small), int(j_large), int(plane_shift), int(query_start))
+        ctx.in_dtypes = tuple(t.dtype for t in (q, k, v, pos_bias, scale_embed, phase_base, phase_gain,
+                                                  y_pre, z_pre))
+        ctx.phase_shape = tuple(phase_base.shape)
+        return out if q.dtype == torch.bfloat16 else out.to(q.dtype)
+
+    @staticmethod
+    def backward(ctx, dout):
+        qb, kb, vb, out, lse, pb, se, pbase, pgain, y32, z32, offs = ctx.saved_tensors
+        j_small, j_large, plane_shift, query_start = ctx.meta
+        B, H, N, HD = qb.shape
+        H_kv = kb.shape[1]
+        J = j_small + j_large
+        dev = qb.device
+        dob = dout.to(torch.bfloat16).contiguous()
+        dq, dk, dv = torch.empty_like(qb), torch.empty_like(kb), torch.empty_like(vb)
+        dy, dz = torch.empty_like(y32), torch.empty_like(z32)
+        ds = torch.zeros(B, H, N, J, dtype=torch.float32, device=dev)
+        delta = torch.empty(B, H, N, dtype=torch.float32, device=dev)
+        dpbase = torch.zeros(max(j_large, 1), H, 4, dtype=torch.float32, device=dev)
+        dpgain = torch.zeros_like(dpbase)
+        pbase_c = pbase[:j_large].contiguous()
+        pgain_c = pgain[:j_large].contiguous()
+        args = _lib.DsqgBwdArgs(version=_lib.ABI_VERSION, J=J, j_small=j_small, j_large=j_large,
+                                plane_shift=plane_shift, query_start=query_start, B=B, H=H, H_kv=H_kv, N=N)
+        for name, t in (("q", qb), ("k", kb), ("v", vb), ("out", out), ("dout", dob), ("lse", lse),
+                        ("offsets", offs), ("pos_bias", pb), ("scale_embed", se), ("phase_base", pbase_c),
+                        ("phase_gain", pgain_c), ("y_pre", y32), ("z_pre", z32), ("dq", dq), ("dk", dk),
+                        ("dv", dv), ("dy_pre", dy), ("dz_pre", dz), ("ds", ds), ("delta", delta),
+                        ("d_phase_base", dpbase), ("d_phase_gain", dpgain)):
+            setattr(args, name, t.data_ptr())
+        _lib.call("dwarf_dsqg_bwd", args, dev)
+        d_pos_bias = ds.sum(dim=(0, 2)).transpose(0, 1)
+        d_scale_embed = torch.einsum("bhnj,bhnd->jd", ds, qb.float()) * 0.125
+        (q_dt, k_dt, v_dt, pb_dt, se_dt, pbase_dt, pgain_dt, y_dt, z_dt) = ctx.in_dtypes
+        d_pbase = torch.zeros(ctx.phase_shape, dtype=torch.float32, device=dev)
+        d_pgain = torch.zeros_like(d_pbase)
+        if j_large > 0:
+            d_pbase[:j_large] = dpbase
+            d_pgain[:j_large] = dpgain
+        return (dq.to(q_dt), dk.to(k_dt), dv.to(v_dt), d_pos_bias.to(pb_dt), d_scale_embed.to(se_dt),
+                d_pbase.to(pbase_dt), d_pgain.to(pgain_dt), dy.to(y_dt), dz.to(z_dt),
+                None, None, None, None, None)
+
+
 def _bf16_rows(t: torch.Tensor) -> torch.Tensor:
     """bf16 view usable by the kernels: dim stride 1 and 16-byte aligned rows."""
     t = t if t.dtype == torch.bfloat16 else t.to(torch.bfloat16)
@@ -430,12 +500,18 @@ def dsqg_attention_v18_grouped(
     if backend == "eager":
         raise NotImplementedError("the B200 engine has no eager backend; use backend='auto'")
     _lib.require_cuda(q, k, v)
-    _forward_only(q, k, v, pos_bias, scale_embed, phase_base, phase_gain, y_pre, z_pre)
     _check_common(q, k, v, y_pre, z_pre)
     if int(j_val) != int(j_small) + int(j_large):
         raise ValueError("j_val must equal j_small + j_large")
     B, H, N, HD = q.shape
     query_start = max(0, min(int(query_start), N))
+    if _needs_grad(q, k, v, pos_bias, scale_embed, phase_base, phase_gain, y_pre, z_pre):
+        if HD != 64:
+            raise ValueError(f"the B200 DSQG kernel supports head_dim 64, got {HD}")
+        if not 0 <= int(plane_shift) <= 14:
+            raise ValueError("plane_shift must be in [0, 14] for the backward kernel")
+        return _DSQGFn.apply(q, k, v, pos_bias, scale_embed, phase_base, phase_gain, y_pre, z_pre,
+                             offsets_dev, int(j_small), int(j_large), int(plane_shift), query_start)
     original_dtype = q.dtype
     qb, kb, vb = _bf16_rows(q), _bf16_rows(k), _bf16_rows(v)
     pb, se, pbase, pgain, y32, z32, offsets = _prepare_tables(

@@ -280,6 +280,60 @@ typedef struct {
 int dwarf_dsqg_fwd(const dwarf_dsqg_fwd_args* args, void* stream);
 
 /* ------------------------------------------------------------------------
+ * DSQG lattice attention backward (bf16 K/V).
+ *
+ * Replaces _DSQGV18GroupedFn.backward (kernels/dsqg_attention_v22.py:2354-2552)
+ * with its kernels _compute_D_v18_grouped, _bwd_dq_v18_grouped and
+ * _bwd_dkdv_v18_grouped (:1263-2196): given dO and the forward's output and
+ * natural-log lse, with p = exp(score - lse), dp = dO . v~ (v~ the MOVT-rotated
+ * value), delta = dO . O and ds = p (dp - delta):
+ *   dq[n]  = (1/8) sum_j ds (k[n-off_j] + bf16(E_j))
+ *   dk[s]  = (1/8) sum_j ds q[s+off_j]          (over the query heads of s's KV head)
+ *   dv[s]  = sum_j p R(theta)^T dO[s+off_j]
+ *   dtheta = p (dO_b v~_a - dO_a v~_b) per plane (a, b); dy_pre[n,r] += dtheta *
+ *   gain * z, dz_pre[s,r] += dtheta * gain * y, d phase_base += dtheta,
+ *   d phase_gain += dtheta * y * z;
+ * ds itself is written to `ds` [B, H, N, J] (0 for invalid pairs; pairs whose
+ * offset reaches before token 0 for a whole warp of queries are not written,
+ * so the caller zero-fills ds) for the caller's d pos_bias = sum_{b,n} ds and
+ * d scale_embed = (1/8) sum_{b,h,n} ds q.
+ * Layout: every tensor contiguous; head_dim 64; plane_shift <= 14; tables fp32
+ * as in dwarf_dsqg_fwd_args (pos_bias [J,H], scale_embed [J,64], phase tables
+ * [j_large,H,4]). Two launches: the query-side kernel (dq, dy_pre, ds, delta,
+ * phase-table gradients; d_phase_* are zeroed on the stream first) then the
+ * key-side kernel (dk, dv, dz_pre), each output written by one thread.
+ * ---------------------------------------------------------------------- */
+typedef struct {
+  int32_t version;
+  int32_t J, j_small, j_large, plane_shift, query_start;
+  int64_t B, H, H_kv, N;
+  const void* q;              /* bf16 [B, H, N, 64]                         */
+  const void* k;              /* bf16 [B, H_kv, N, 64]                      */
+  const void* v;              /* bf16 [B, H_kv, N, 64]                      */
+  const void* out;            /* bf16 [B, H, N, 64] forward output          */
+  const void* dout;           /* bf16 [B, H, N, 64]                         */
+  const float* lse;           /* [B, H, N] natural-log lse of the forward   */
+  const int32_t* offsets;     /* [J]                                        */
+  const float* pos_bias;      /* [J, H]                                     */
+  const float* scale_embed;   /* [J, 64]                                    */
+  const float* phase_base;    /* [j_large, H, 4]                            */
+  const float* phase_gain;    /* [j_large, H, 4]                            */
+  const float* y_pre;         /* [B, H, N, 4]                               */
+  const float* z_pre;         /* [B, H_kv, N, 4]                            */
+  void* dq;                   /* bf16 [B, H, N, 64]                         */
+  void* dk;                   /* bf16 [B, H_kv, N, 64]                      */
+  void* dv;                   /* bf16 [B, H_kv, N, 64]                      */
+  float* dy_pre;              /* [B, H, N, 4]                               */
+  float* dz_pre;              /* [B, H_kv, N, 4]                            */
+  float* ds;                  /* [B, H, N, J], zero-filled by the caller    */
+  float* delta;               /* [B, H, N] written (dO . O)                 */
+  float* d_phase_base;        /* [j_large, H, 4] overwritten                */
+  float* d_phase_gain;        /* [j_large, H, 4] overwritten                */
+} dwarf_dsqg_bwd_args;
+
+int dwarf_dsqg_bwd(const dwarf_dsqg_bwd_args* args, void* stream);
+
+/* ------------------------------------------------------------------------
  * DSQG QKV prep: the per-row work between the qkvg projection and the DSQG
  * kernel, fused into one pass over the projection output.
  *

@@ -105,3 +105,61 @@ def derived_tables(offsets, pos_bias_log_slope, pos_bias_residual, pos_bias_scal
     se = se - se.mean(0, keepdims=True)
     gate = 1.0 / (1.0 + np.exp(-np.asarray(phase_gate, np.float64)))[:, None, None]
     return pb, se, np.asarray(phase_base, np.float64) * gate, np.asarray(phase_gain, np.float64) * gate
+
+
+def dsqg_forward_torch(q, k, v, pos_bias, scale_embed, phase_base, phase_gain, y_pre, z_pre, offsets,
+                       j_small: int, plane_shift: int = 0, query_start: int = 0, round_scale_embed: bool = True):
+    """``dsqg_forward`` restated on CPU torch tensors (any float dtype; use float64)
+    so autograd can differentiate it: the oracle of the backward pass, whose
+    gradients are those of ``_eager_dsqg_attention`` (dsqg_attention_v22.py:2602-2688)
+    and of the reference backward kernels (:1263-2196, 2354-2552)."""
+    import torch
+
+    B, H, N, D = q.shape
+    group = H // k.shape[1]
+    kx, vx, zx = (t.repeat_interleave(group, dim=1) for t in (k, v, z_pre))
+    se = scale_embed
+    if round_scale_embed:
+        se = se + (torch.from_numpy(bf16_round(scale_embed.detach().numpy())).to(se.dtype) - se).detach()
+    n = torch.arange(N)
+    pairs = plane_channels(D, plane_shift)
+    scores, values = [], []
+    for j, delta in enumerate(int(o) for o in offsets):
+        src = n - delta
+        valid = (src >= 0) & (n >= query_start)
+        s = src.clamp(0, N - 1)
+        ks, vs = kx[:, :, s], vx[:, :, s]
+        sc = (q * (ks + se[j])).sum(-1) / math.sqrt(D) + pos_bias[j][None, :, None]
+        scores.append(torch.where(valid[None, None], sc, torch.full_like(sc, -math.inf)))
+        if j >= j_small:
+            jl = j - j_small
+            zs = zx[:, :, s]
+            cols = list(vs.unbind(-1))
+            for r, (a, b) in enumerate(pairs):
+                theta = phase_base[jl, :, r][None, :, None] + phase_gain[jl, :, r][None, :, None] * y_pre[..., r] * zs[..., r]
+                c, sn = torch.cos(theta), torch.sin(theta)
+                va, vb = cols[a], cols[b]
+                cols[a], cols[b] = c * va - sn * vb, sn * va + c * vb
+            vs = torch.stack(cols, -1)
+        values.append(vs)
+    sc = torch.stack(scores, -1)
+    any_valid = torch.isfinite(sc).any(-1, keepdim=True)
+    p = torch.softmax(torch.where(any_valid, sc, torch.zeros_like(sc)), -1)
+    p = torch.where(torch.isfinite(sc), p, torch.zeros_like(p))
+    return (p.unsqueeze(-1) * torch.stack(values, -2)).sum(-2)
+
+
+def dsqg_backward(inputs: dict, dout, offsets, j_small: int, plane_shift: int = 0, query_start: int = 0,
+                  round_scale_embed: bool = True) -> dict:
+    """Gradients (float64) of ``dsqg_forward_torch`` for dO = ``dout``; ``inputs``
+    maps q, k, v, pos_bias, scale_embed, phase_base, phase_gain, y_pre, z_pre to
+    tensors. Returns {'d_' + name: gradient}."""
+    import torch
+
+    names = ("q", "k", "v", "pos_bias", "scale_embed", "phase_base", "phase_gain", "y_pre", "z_pre")
+    leaves = {n: torch.as_tensor(inputs[n]).double().clone().requires_grad_(True) for n in names}
+    out = dsqg_forward_torch(*(leaves[n] for n in names), offsets, j_small, plane_shift, query_start,
+                             round_scale_embed)
+    grads = torch.autograd.grad(out, [leaves[n] for n in names], torch.as_tensor(dout).double(),
+                                allow_unused=True)
+    return {f"d_{n}": (g if g is not None else torch.zeros_like(leaves[n])) for n, g in zip(names, grads)}

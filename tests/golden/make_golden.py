@@ -248,6 +248,28 @@ def make_dsqg(with_triton: bool = True) -> None:
     save("dsqg_module_eval", x=x, y=y, **state)
 
 
+def make_dsqg_backward() -> None:
+    """Backward golden vectors: fp64 autograd through the reference's own eager
+    oracle ``_eager_dsqg_attention`` (kernels/dsqg_attention_v22.py:2602-2688)
+    on the inputs of the committed forward fixtures, with a seeded dO."""
+    _import_reference()
+    import dsqg_attention_v22 as ref
+
+    sys.path.insert(0, str(HERE.parent.parent))
+    from tests._golden import load
+
+    names = ("q", "k", "v", "pos_bias", "scale_embed", "phase_base", "phase_gain", "y_pre", "z_pre")
+    for src, dst, seed in (("dsqg_config1", "dsqg_bwd_config1", 31), ("dsqg_gqa_ragged", "dsqg_bwd_gqa_ragged", 32)):
+        g = load(src)
+        leaves = {n: g[n].double().clone().requires_grad_(True) for n in names}
+        out = ref._eager_dsqg_attention(*(leaves[n] for n in names), g["offsets"], int(g["j_small"]),
+                                        plane_shift=int(g["plane_shift"]))
+        dout = torch.randn(out.shape, generator=torch.Generator().manual_seed(seed), dtype=torch.float64)
+        dout = dout.to(torch.bfloat16)
+        grads = torch.autograd.grad(out, [leaves[n] for n in names], dout.double())
+        save(dst, dout=dout, out=out.detach().float(), **{f"d_{n}": gr.float() for n, gr in zip(names, grads)})
+
+
 def make_hisa() -> None:
     _import_reference()
     import torch.nn.functional as F
@@ -441,7 +463,7 @@ def make_checkpoint() -> None:
 
 def main(argv: list[str]) -> None:
     which = argv[1] if len(argv) > 1 else "all"
-    makers = {"ema": make_ema, "ema_bwd": make_ema_backward, "dsqg": make_dsqg, "hisa": make_hisa, "model": make_model,
+    makers = {"ema": make_ema, "ema_bwd": make_ema_backward, "dsqg": make_dsqg, "dsqg_bwd": make_dsqg_backward, "hisa": make_hisa, "model": make_model,
               "checkpoint": make_checkpoint}
     for name, maker in makers.items():
         if which in ("all", name):
