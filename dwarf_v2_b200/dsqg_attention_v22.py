@@ -31,7 +31,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from . import _lib, gemm
-from .npci import npci_rotate_cuda
+from .npci import npci_rotate_autograd, npci_rotate_cuda
 
 R_PLANES = 4
 NPCI_THETA_MAX = 0.25
@@ -824,8 +824,8 @@ class DSQGAttentionV19(nn.Module):
         if self.backend == "eager":
             raise NotImplementedError("the B200 engine has no eager backend; construct with backend='auto'")
         _lib.require_cuda(x)
-        if torch.is_grad_enabled():
-            _forward_only(x, *self.parameters())
+        if _needs_grad(x, *self.parameters()) or (self.training and self.dropout.p > 0):
+            return self._forward_autograd(x, kv_inject)
         batch, seq_len, dimension = x.shape
         heads, head_dim = self.num_heads, self.head_dim
         query_start = min(self.minimum_offset, seq_len)
@@ -872,6 +872,57 @@ class DSQGAttentionV19(nn.Module):
         y_pre, z_pre, cache = dsqg_prep(query, key, value, t["q_probe"], t["k_probe"], pack_q6=q6)
         kv = ("q6", *cache) if q6 else ("bf16", key, value)
         return self._attend(x, query, kv, y_pre, z_pre, content_gate, t, query_start)
+
+    def _forward_autograd(self, x: torch.Tensor, kv_inject=None) -> torch.Tensor:
+        """Differentiable forward (training): the reference forward (:3144-3289,
+        without the support-crop projection schedule, which computes the same
+        values) with the projections, probes and tables as torch ops and the
+        attention on ``dwarf_dsqg_fwd`` / ``dwarf_dsqg_bwd`` (bf16 K/V)."""
+        batch, seq_len, dimension = x.shape
+        heads, head_dim = self.num_heads, self.head_dim
+        query_start = min(self.minimum_offset, seq_len)
+        key_end = max(0, seq_len - query_start)
+        if query_start >= seq_len:
+            return torch.zeros_like(x)
+        q_flat, k_flat, v_flat, content_gate = self.qkvg_proj(x).split(dimension, dim=-1)
+        query = q_flat.reshape(batch, seq_len, heads, head_dim).permute(0, 2, 1, 3)
+        key = k_flat.reshape(batch, seq_len, heads, head_dim).permute(0, 2, 1, 3)
+        value = v_flat.reshape(batch, seq_len, heads, head_dim).permute(0, 2, 1, 3)
+        if kv_inject is not None:
+            key_delta, value_delta = kv_inject
+            full = key.shape
+            prefix = (batch, heads, key_end, head_dim)
+            if key_delta.shape == full and value_delta.shape == full:
+                kd, vd = key_delta[:, :, :key_end], value_delta[:, :, :key_end]
+            elif key_delta.shape == prefix and value_delta.shape == prefix:
+                kd, vd = key_delta, value_delta
+            else:
+                raise ValueError(
+                    "kv_inject must contain full [B,H,N,HD] tensors or the "
+                    "exact live source prefix [B,H,N-min_offset,HD]"
+                )
+            rk = npci_rotate_autograd(key[:, :, :key_end], kd, NPCI_THETA_MAX * torch.tanh(self.npci_theta_k),
+                                      strength_tau=self.npci_strength_tau)
+            rv = npci_rotate_autograd(value[:, :, :key_end], vd, NPCI_THETA_MAX * torch.tanh(self.npci_theta_v),
+                                      strength_tau=self.npci_strength_tau)
+            key = torch.cat((rk, key[:, :, key_end:]), dim=2) if key_end < seq_len else rk
+            value = torch.cat((rv, value[:, :, key_end:]), dim=2) if key_end < seq_len else rv
+        query_probe = F.normalize(self.query_probes.float(), dim=-1)
+        key_probe = F.normalize(self.key_probes.float(), dim=-1)
+        qf, kf = query.float(), key.float()
+        eps = 1e-6 * head_dim
+        y_pre = (torch.einsum("bhnd,rd->bhnr", qf, query_probe)
+                 * torch.rsqrt(qf.square().sum(-1, keepdim=True) + eps)).contiguous()
+        z_pre = (torch.einsum("bhnd,rd->bhnr", kf, key_probe)
+                 * torch.rsqrt(kf.square().sum(-1, keepdim=True) + eps)).contiguous()
+        phase_gate = torch.sigmoid(self.phase_gate)[:, None, None]
+        output = dsqg_attention_v18_grouped(
+            query, key, value, self.pos_bias, self.centered_scale_embed, self.phase_base * phase_gate,
+            self.phase_gain * phase_gate, y_pre, z_pre, self.j_val, self.j_small, self.j_large, self.offsets_dev,
+            None, None, None, None, None, self.k_group_size, 0, False, 0, self.plane_shift, query_start)
+        output = output.to(x.dtype) * self.if_gain.reshape(1, heads, 1, 1).to(x.dtype)
+        flattened = output.permute(0, 2, 1, 3).reshape(batch, seq_len, dimension)
+        return self.dropout(self.out_proj(flattened * torch.sigmoid(content_gate)))
 
     def forward_cached(self, x: torch.Tensor, cache, row: int) -> torch.Tensor:
         """Attention output for positions [row, row + T) of ``x`` [B,T,D], appending their

@@ -52,3 +52,26 @@ def npci_rotate_cuda(x: torch.Tensor, x_delta: torch.Tensor | None, theta_h: tor
             raise ValueError("npci rotation needs a unit stride on the head dimension")
     _lib.call("dwarf_npci_rotate", args, x.device)
     return out
+
+
+def npci_rotate_autograd(x: torch.Tensor, x_delta: torch.Tensor, theta_h: torch.Tensor, *,
+                         strength_tau: float = 0.25) -> torch.Tensor:
+    """The same rotation as differentiable elementwise ops on the device, for the
+    training path (the reference's ``npci_rotate`` is itself such an op chain,
+    kernels/dsqg_attention_v22.py:235-254, differentiated by autograd)."""
+    tau = float(strength_tau)
+    if not math.isfinite(tau) or tau <= 0:
+        raise ValueError("strength_tau must be finite and positive")
+    _lib.require_cuda(x, x_delta)
+    xf, df = x.float(), x_delta.float()
+    theta = theta_h.float().reshape(1, -1, 1, 1)
+    norm = xf.norm(dim=-1, keepdim=True).clamp_min(1e-12)
+    unit = xf / norm
+    perpendicular = df - (df * unit).sum(dim=-1, keepdim=True) * unit
+    perpendicular_norm = perpendicular.norm(dim=-1, keepdim=True)
+    active = perpendicular_norm > norm * 1e-7
+    direction = torch.where(active, perpendicular / perpendicular_norm.clamp_min(1e-20),
+                            torch.zeros_like(perpendicular))
+    angle = theta * torch.tanh(perpendicular_norm / (tau * norm + 1e-12))
+    rotated = torch.cos(angle) * xf + torch.sin(angle) * norm * direction
+    return torch.where(active, rotated, xf).to(x.dtype)

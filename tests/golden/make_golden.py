@@ -270,6 +270,37 @@ def make_dsqg_backward() -> None:
         save(dst, dout=dout, out=out.detach().float(), **{f"d_{n}": gr.float() for n, gr in zip(names, grads)})
 
 
+def make_dsqg_module_grad() -> None:
+    """Training-mode gradients of the reference DSQGAttentionV19 (CPU, fp32 eager
+    path, dropout 0): every parameter's gradient and dx for a seeded dy, with
+    and without a kv_inject packet (NPCI path)."""
+    _import_reference()
+    import dsqg_attention_v22 as ref
+
+    torch.manual_seed(4)
+    module = ref.DSQGAttentionV19(128, 2, [1, 2, 3, 5, 8, 13, 21, 48, 64, 100], 7, 3, seq_len=160,
+                                  dropout=0.0, plane_shift=6).train()
+    _randomize_dsqg(module, 404)
+    g = torch.Generator().manual_seed(405)
+    x = torch.randn(2, 150, 128, generator=g).to(torch.bfloat16).float()
+    kd = torch.randn(2, 2, 150, 64, generator=g) * 0.5
+    vd = torch.randn(2, 2, 150, 64, generator=g) * 0.5
+    dy = torch.randn(2, 150, 128, generator=g)
+    state = {f"state.{k}": val for k, val in module.state_dict().items()}
+    out = {}
+    for tag, inject in (("plain", None), ("inject", (kd, vd))):
+        module.zero_grad()
+        xl = x.clone().requires_grad_(True)
+        y = module(xl, inject)
+        y.backward(dy)
+        out[f"{tag}.y"] = y.detach()
+        out[f"{tag}.dx"] = xl.grad
+        for name, p in module.named_parameters():
+            if p.grad is not None:
+                out[f"{tag}.grad.{name}"] = p.grad.clone()
+    save("dsqg_module_grad", x=x, kd=kd, vd=vd, dy=dy, **state, **out)
+
+
 def make_hisa() -> None:
     _import_reference()
     import torch.nn.functional as F
@@ -463,7 +494,7 @@ def make_checkpoint() -> None:
 
 def main(argv: list[str]) -> None:
     which = argv[1] if len(argv) > 1 else "all"
-    makers = {"ema": make_ema, "ema_bwd": make_ema_backward, "dsqg": make_dsqg, "dsqg_bwd": make_dsqg_backward, "hisa": make_hisa, "model": make_model,
+    makers = {"ema": make_ema, "ema_bwd": make_ema_backward, "dsqg": make_dsqg, "dsqg_bwd": make_dsqg_backward, "dsqg_module_grad": make_dsqg_module_grad, "hisa": make_hisa, "model": make_model,
               "checkpoint": make_checkpoint}
     for name, maker in makers.items():
         if which in ("all", name):

@@ -115,3 +115,31 @@ def test_engine_backward_properties_batch():
     _, g1 = _engine_grads(row, dout[3:4], offsets, js, jl, 0, 0)
     for n in ("d_q", "d_k", "d_v", "d_y_pre", "d_z_pre"):
         assert torch.equal(grads[n][3:4], g1[n]), n
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("tag", ["plain", "inject"])
+def test_module_training_gradients_match_reference(tag):
+    """DSQGAttentionV19 in training mode (fp32 parameters, bf16 attention on the
+    engine) against the reference module's CPU fp32 gradients: dx and every
+    parameter gradient, with and without a kv_inject packet."""
+    from dwarf_v2_b200.dsqg_attention_v22 import DSQGAttentionV19
+
+    g = load("dsqg_module_grad")
+    module = DSQGAttentionV19(128, 2, [1, 2, 3, 5, 8, 13, 21, 48, 64, 100], 7, 3, seq_len=160, dropout=0.0,
+                              plane_shift=6).train()
+    module.load_state_dict({k[len("state."):]: v for k, v in g.items() if k.startswith("state.")})
+    module = module.cuda()
+    x = g["x"].cuda().requires_grad_(True)
+    inject = (g["kd"].cuda(), g["vd"].cuda()) if tag == "inject" else None
+    y = module(x, inject)
+    y.backward(g["dy"].cuda())
+    _assert_grad_close(y, g[f"{tag}.y"], "y")
+    _assert_grad_close(x.grad, g[f"{tag}.dx"], "dx")
+    prefix = f"{tag}.grad."
+    names = [k[len(prefix):] for k in g if k.startswith(prefix)]
+    assert "qkvg_proj.weight" in names and "pos_bias_residual" in names
+    params = dict(module.named_parameters())
+    for name in names:
+        assert params[name].grad is not None, name
+        _assert_grad_close(params[name].grad, g[prefix + name], name)
