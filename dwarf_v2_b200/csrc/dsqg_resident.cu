@@ -17,15 +17,20 @@
 // 32 consecutive 48-B rows: the 16-B shared loads of each 8-lane phase fall
 // on 8 distinct bank groups (conflict-free).
 //
-// Work split: 256 threads = 8 warps, ONE thread per query (all 64 head dims
-// and all 4 MOVT planes), so the per-pair bookkeeping (score, softmax
-// update, loop control) is done once per pair. A round covers 256 queries
-// (one chunk): wait for the chunk, flip the sign bit of every 6-bit field in
-// place (two's complement -> offset binary, once per row instead of once
-// per pair), then each warp walks the offsets in groups of 8: q . bf16(E_j)
-// for its 32 queries x 8 offsets on tensor cores (mma.sync, through a small
-// per-warp transpose buffer into registers), then 8 unrolled pair steps of
-// one online-softmax pass with K and V of a pair consumed together. The
+// Work split: 512 threads = 16 warps, TWO threads per query (32 head dims and
+// two MOVT planes each; the K dot product is completed with one shuffle and
+// both threads repeat the per-pair softmax bookkeeping on identical values).
+// 122 registers per thread, so 16 warps fit on an SM: at 8 warps (one thread
+// per query, 235 registers; still selectable) the kernel stalls on
+// fixed-latency dependencies. A round covers 256 queries (one chunk): wait
+// for the chunk, flip the sign bit of every 6-bit field in place (two's
+// complement -> offset binary, once per row instead of once per pair), then
+// each warp walks the offsets in groups of 8: q . bf16(E_j) for its 16
+// queries x 8 offsets on tensor cores (mma.sync, through a small per-warp
+// transpose buffer into registers), then the group's pairs, one
+// online-softmax pass with K and V of a pair consumed together. Offsets that
+// reach before token 0 for all of a warp's queries are skipped
+// (warp-uniform): at T = 2048 that is ~40% of the (query, offset) grid. The
 // running maximum only moves when a score exceeds it by more than 2^8 in the
 // exp2 domain, so accumulators are rescaled rarely; weights stay below 2^8.
 //
