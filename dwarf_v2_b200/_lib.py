@@ -189,6 +189,12 @@ class DsqgBwdArgs(ctypes.Structure):
         dq:ptr, dk:ptr, dv:ptr, dy_pre:ptr, dz_pre:ptr, ds:ptr, delta:ptr, d_phase_base:ptr, d_phase_gain:ptr""")
 
 
+class HisaAttnBwdArgs(ctypes.Structure):
+    _fields_ = _fields("""version:i32, k_slots:i32, B:i64, H:i64, T:i64, query:ptr, local_key:ptr, local_value:ptr,
+        global_key:ptr, global_value:ptr, top_chunk_idx:ptr, route:ptr, lengths:ptr, out:ptr, dout:ptr,
+        dq:ptr, d_local_key:ptr, d_local_value:ptr, d_global_key:ptr, d_global_value:ptr, d_route:ptr""")
+
+
 class DsqgPrepArgs(ctypes.Structure):
     _fields_ = _fields("""version:i32, pack_q6:i32, B:i64, H:i64, H_kv:i64, N:i64,
         q:ptr, sqb:i64, sqh:i64, sqn:i64, k:ptr, skb:i64, skh:i64, skn:i64, v:ptr, svb:i64, svh:i64, svn:i64,
@@ -270,6 +276,7 @@ _ENTRY_POINTS = {
     "dwarf_hisa_reps": HisaRepsArgs,
     "dwarf_hisa_select": HisaSelectArgs,
     "dwarf_hisa_attn": HisaAttnArgs,
+    "dwarf_hisa_attn_bwd": HisaAttnBwdArgs,
     "dwarf_hisa_route": HisaRouteArgs,
     "dwarf_add_rmsnorm": AddRmsNormArgs,
     "dwarf_embed_rmsnorm": EmbedRmsNormArgs,

@@ -183,6 +183,84 @@ def tile_attention(query, local_key, local_value, global_key, global_value, reps
     return out, (route if want_route else None)
 
 
+def _attn_launch(query, local_key, local_value, global_key, global_value, top, route, lengths, out):
+    """``dwarf_hisa_attn`` with a given bf16 route prior [B,H,T,4]."""
+    B, H, T, D = query.shape
+    args = _lib.HisaAttnArgs(version=_lib.ABI_VERSION, head_dim=D, chunk_size=_CHUNK, selector_tile=_TILE,
+                             local_window=_WINDOW, k_slots=top.shape[-1], B=B, H=H, T=T,
+                             query=query.data_ptr(), local_key=local_key.data_ptr(),
+                             local_value=local_value.data_ptr(), global_key=global_key.data_ptr(),
+                             global_value=global_value.data_ptr(), top_chunk_idx=top.data_ptr(),
+                             route=route.data_ptr(), lengths=lengths.data_ptr(), out=out.data_ptr(),
+                             tile_begin=0, tile_count=0, pos=None)
+    args.sqb, args.sqh, args.sqn = _strides3(query)
+    args.slkb, args.slkh, args.slkn = _strides3(local_key)
+    args.slvb, args.slvh, args.slvn = _strides3(local_value)
+    args.sgkb, args.sgkh, args.sgkn = _strides3(global_key)
+    args.sgvb, args.sgvh, args.sgvn = _strides3(global_value)
+    args.sob, args.soh, args.son = _strides3(out)
+    _lib.call("dwarf_hisa_attn", args, query.device)
+
+
+class _HisaAttnFn(torch.autograd.Function):
+    """Differentiable fused tile attention: forward ``dwarf_hisa_attn``, backward
+    ``dwarf_hisa_attn_bwd`` (the reference trains the same function as
+    _GlobalHISATritonFn + autograd through the local lane and the LSE merge,
+    hierarchical_sparse_attn_v18_hisa.py:1897-2027, 2424-2461, 808-835).
+    Differentiable in query, the local and global K/V and the route prior;
+    top_chunk_idx and lengths are routing decisions (no gradient)."""
+
+    @staticmethod
+    def forward(ctx, query, local_key, local_value, global_key, global_value, route, top, lengths):
+        ins = [t.to(torch.bfloat16).contiguous() for t in (query, local_key, local_value, global_key, global_value,
+                                                          route)]
+        top = top.to(torch.int32).contiguous()
+        B, H, T, D = ins[0].shape
+        out = torch.empty(B, H, T, D, dtype=torch.bfloat16, device=query.device)
+        _attn_launch(*ins[:5], top, ins[5], lengths, out)
+        ctx.save_for_backward(*ins, top, lengths, out)
+        ctx.dtypes = tuple(t.dtype for t in (query, local_key, local_value, global_key, global_value, route))
+        return out if query.dtype == torch.bfloat16 else out.to(query.dtype)
+
+    @staticmethod
+    def backward(ctx, dout):
+        q, lk, lv, gk, gv, route, top, lengths, out = ctx.saved_tensors
+        B, H, T, D = q.shape
+        dob = dout.to(torch.bfloat16).contiguous()
+        f32 = dict(dtype=torch.float32, device=q.device)
+        dq = torch.empty(B, H, T, D, **f32)
+        dlk, dlv, dgk, dgv = (torch.zeros(B, H, T, D, **f32) for _ in range(4))
+        droute = torch.empty(B, H, T, route.shape[-1], **f32)
+        args = _lib.HisaAttnBwdArgs(version=_lib.ABI_VERSION, k_slots=top.shape[-1], B=B, H=H, T=T,
+                                    query=q.data_ptr(), local_key=lk.data_ptr(), local_value=lv.data_ptr(),
+                                    global_key=gk.data_ptr(), global_value=gv.data_ptr(),
+                                    top_chunk_idx=top.data_ptr(), route=route.data_ptr(), lengths=lengths.data_ptr(),
+                                    out=out.data_ptr(), dout=dob.data_ptr(), dq=dq.data_ptr(),
+                                    d_local_key=dlk.data_ptr(), d_local_value=dlv.data_ptr(),
+                                    d_global_key=dgk.data_ptr(), d_global_value=dgv.data_ptr(),
+                                    d_route=droute.data_ptr())
+        _lib.call("dwarf_hisa_attn_bwd", args, q.device)
+        grads = (dq, dlk, dlv, dgk, dgv, droute)
+        return (*(g.to(dt) for g, dt in zip(grads, ctx.dtypes)), None, None)
+
+
+def hisa_tile_attention(query, local_key, local_value, global_key, global_value, route, top_chunk_idx,
+                        valid_lengths=None):
+    """Fused tile attention with a given route prior [B,H,T,4] (differentiable when
+    its inputs require grad): one softmax over the strict local window (64) and the
+    routed chunks of ``top_chunk_idx`` with ids < n - 64, route added per slot."""
+    _lib.require_cuda(query, local_key, local_value, global_key, global_value, route)
+    B, H, T, D = query.shape
+    if D != _HD:
+        raise ValueError(f"the B200 HISA kernels support head_dim 64, got {D}")
+    if route.shape != (B, H, T, _MAX_TOP_K) or top_chunk_idx.shape[:3] != (B, H, -(-T // _TILE)):
+        raise ValueError("route must be [B,H,T,4] and top_chunk_idx [B,H,ceil(T/16),K]")
+    if top_chunk_idx.shape[-1] > _MAX_TOP_K:
+        raise ValueError("at most 4 routed chunks per tile")
+    lengths = _as_valid_lengths(valid_lengths, batch_size=B, seq_len=T, device=query.device)
+    return _HisaAttnFn.apply(query, local_key, local_value, global_key, global_value, route, top_chunk_idx, lengths)
+
+
 def hisa_attention(query, local_key, local_value, global_key, global_value, route_scale, valid_lengths=None, *,
                    top_k: int = 4, temperature: float = 1.0, blend_alpha: float = 0.5, want_route: bool = False):
     """Router + fused attention on head tensors [B,H,T,64] (bf16).

@@ -493,6 +493,46 @@ int dwarf_hisa_select(const dwarf_hisa_select_args* args, void* stream);
 int dwarf_hisa_route(const dwarf_hisa_route_args* args, void* stream);
 int dwarf_hisa_attn(const dwarf_hisa_attn_args* args, void* stream);
 
+/* Backward of the fused tile attention (dwarf_hisa_attn). Replaces
+ * _GlobalHISATritonFn.backward -> _global_lane_backward_kernel
+ * (hierarchical_sparse_attn_v18_hisa.py:1982-2027, 1103-1246) together with
+ * autograd through the local lane and the LSE merge (:2424-2461, 808-835):
+ * with P the joint softmax over the tile's local window and routed chunks,
+ * dP = dO . v, delta = dO . O and dS = P (dP - delta):
+ *   dq = (1/8) sum dS k,   dk += (1/8) dS q,   dv += P dO   (local or global K/V),
+ *   d_route[n, slot] = sum of dS over the slot's chunk.
+ * One CTA per (b, h, selector tile): the tile's keys (local rows
+ * [t0 - 64, t0 + 15) and the routed chunks) in blocks of 32 staged in shared
+ * memory; a first pass recomputes each query's lse. dq and d_route have one
+ * writer per row; the K/V gradients (each key row feeds several tiles) are
+ * accumulated with float4 atomics, so the caller zero-fills them and their
+ * last bits vary between runs. Tensors contiguous, head_dim 64, chunk 64,
+ * tile 16, window 64.
+ * ---------------------------------------------------------------------- */
+typedef struct {
+  int32_t version;
+  int32_t k_slots;                /* last dim of top_chunk_idx (<= 4)     */
+  int64_t B, H, T;
+  const void* query;              /* bf16 [B, H, T, 64]                   */
+  const void* local_key;          /* bf16 [B, H, T, 64]                   */
+  const void* local_value;
+  const void* global_key;
+  const void* global_value;
+  const int32_t* top_chunk_idx;   /* [B, H, tiles, k_slots]               */
+  const void* route;              /* bf16 [B, H, T, 4]                    */
+  const int32_t* lengths;         /* [B]                                  */
+  const void* out;                /* bf16 [B, H, T, 64] forward output    */
+  const void* dout;               /* bf16 [B, H, T, 64]                   */
+  float* dq;                      /* [B, H, T, 64] written                */
+  float* d_local_key;             /* [B, H, T, 64] accumulated            */
+  float* d_local_value;
+  float* d_global_key;
+  float* d_global_value;
+  float* d_route;                 /* [B, H, T, 4] written                 */
+} dwarf_hisa_attn_bwd_args;
+
+int dwarf_hisa_attn_bwd(const dwarf_hisa_attn_bwd_args* args, void* stream);
+
 /* ------------------------------------------------------------------------
  * Row-wise block glue (one warp per row of `width` values, width % 256 == 0
  * and <= 1024), with the reference's bf16 rounding points

@@ -168,3 +168,63 @@ def attention(query, local_key, local_value, global_key, global_value, route, to
             w = np.exp(s - s.max())
             out[b, h, n] = (w[:, None] * np.concatenate(vs)).sum(0) / w.sum()
     return out
+
+
+def attention_torch(query, local_key, local_value, global_key, global_value, route, top_idx, valid_lengths, *,
+                    chunk_size: int = 64, selector_tile: int = 16, local_window: int = 64):
+    """``attention`` restated on CPU torch tensors, one selector tile at a time
+    (its 16 queries against the tile's local window and routed chunks, masked),
+    so autograd gives the gradients of the reference's lanes + merge
+    (hierarchical_sparse_attn_v18_hisa.py:688-835; backward kernels :1103-1246).
+    Differentiable in query, the four K/V tensors and route."""
+    import torch
+
+    B, H, T, D = query.shape
+    scale = 1.0 / math.sqrt(D)
+    lengths = torch.as_tensor(valid_lengths).reshape(B, 1, 1, 1).long()
+    top = torch.as_tensor(top_idx).long()
+    K = top.shape[-1]
+    outs = []
+    for t in range(-(-T // selector_tile)):
+        n0, n1 = t * selector_tile, min((t + 1) * selector_tile, T)
+        n = torch.arange(n0, n1)
+        q = query[:, :, n0:n1]
+        qv = n.reshape(1, 1, -1, 1) < lengths
+        lids = torch.arange(n0 - local_window, n1 - 1)
+        lmask = ((lids >= 0) & (lids[None] < n[:, None]) & (lids[None] >= n[:, None] - local_window))
+        lmask = lmask.reshape(1, 1, n.numel(), -1) & (lids.reshape(1, 1, 1, -1) < lengths) & qv
+        safe = lids.clamp(0, T - 1)
+        s_loc = torch.einsum("bhqd,bhkd->bhqk", q, local_key[:, :, safe]) * scale
+        c = top[:, :, t]                                              # [B,H,K]
+        gids = c[..., None] * chunk_size + torch.arange(chunk_size)   # [B,H,K,C]
+        gids = gids.reshape(B, H, K * chunk_size)
+        gvalid = (c >= 0).repeat_interleave(chunk_size, dim=-1)
+        gsafe = gids.clamp(0, T - 1)
+        idx = gsafe[..., None].expand(-1, -1, -1, D)
+        gk = torch.gather(global_key, 2, idx)
+        gv = torch.gather(global_value, 2, idx)
+        prior = route[:, :, n0:n1].repeat_interleave(chunk_size, dim=-1)
+        s_glb = torch.einsum("bhqd,bhkd->bhqk", q, gk) * scale + prior
+        gmask = (gvalid[:, :, None] & (gids[:, :, None] < n.reshape(1, 1, -1, 1) - local_window)
+                 & (gids[:, :, None] < lengths) & qv)
+        s = torch.cat([s_loc.expand(B, H, -1, -1), s_glb], -1)
+        mask = torch.cat([lmask.expand(B, H, -1, -1), gmask], -1)
+        s = s.masked_fill(~mask, float("-inf"))
+        any_valid = mask.any(-1, keepdim=True)
+        p = torch.softmax(torch.where(any_valid, s, torch.zeros_like(s)), -1)
+        p = torch.where(mask, p, torch.zeros_like(p))
+        v = torch.cat([local_value[:, :, safe].expand(B, H, -1, -1), gv], 2)
+        outs.append(torch.einsum("bhqk,bhkd->bhqd", p, v))
+    return torch.cat(outs, 2)
+
+
+def attention_backward(inputs: dict, dout, top_idx, valid_lengths, **kw) -> dict:
+    """float64 gradients of ``attention_torch`` for dO = ``dout``; ``inputs`` maps
+    query, local_key, local_value, global_key, global_value, route to tensors."""
+    import torch
+
+    names = ("query", "local_key", "local_value", "global_key", "global_value", "route")
+    leaves = {n: torch.as_tensor(inputs[n]).double().clone().requires_grad_(True) for n in names}
+    out = attention_torch(*(leaves[n] for n in names), top_idx, valid_lengths, **kw)
+    grads = torch.autograd.grad(out, [leaves[n] for n in names], torch.as_tensor(dout).double())
+    return {f"d_{n}": g for n, g in zip(names, grads)}

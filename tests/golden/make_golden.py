@@ -373,6 +373,37 @@ def make_hisa() -> None:
     save("hisa_module_eval", x=x, key_delta=kd, value_delta=vd, y=y, **state)
 
 
+def make_hisa_backward() -> None:
+    """Backward golden vectors: fp64 autograd through the reference's own eager
+    lanes and merge (_eager_local_lane, _eager_global_lane, _merge_attention_lanes,
+    hierarchical_sparse_attn_v18_hisa.py:688-835) on the committed router/lanes
+    inputs, route a differentiable input, metadata from the reference router."""
+    _import_reference()
+    import hierarchical_sparse_attn_v18_hisa as ref
+
+    sys.path.insert(0, str(HERE.parent.parent))
+    from tests._golden import load
+
+    g = load("hisa_router_lanes")
+    T = g["q"].shape[2]
+    meta = ref.HISAMetadata(top_chunk_idx=g["top_chunk_idx"], token_idx=torch.empty(0, dtype=torch.int32),
+                            token_scores=torch.empty(0), tile_starts=torch.arange(-(-T // 16), dtype=torch.int32) * 16,
+                            valid_lengths=g["valid_lengths"], chunk_size=64, selector_tile_size=16,
+                            enumerate_all=True)
+    names = ("q", "local_key", "local_value", "global_key", "global_value", "route")
+    leaves = {n: g[n].double().clone().requires_grad_(True) for n in names}
+    lo, llse = ref._eager_local_lane(leaves["q"], leaves["local_key"], leaves["local_value"], g["valid_lengths"],
+                                     local_window=64, selector_tile_size=16)
+    go, glse = ref._eager_global_lane(leaves["q"], leaves["global_key"], leaves["global_value"], leaves["route"],
+                                      meta, local_window=64)
+    merged, _ = ref._merge_attention_lanes(lo, llse, go, glse)
+    dout = torch.randn(merged.shape, generator=torch.Generator().manual_seed(51), dtype=torch.float64)
+    dout = dout.to(torch.bfloat16)
+    grads = torch.autograd.grad(merged, [leaves[n] for n in names], dout.double())
+    save("hisa_bwd_lanes", dout=dout, merged=merged.detach().float(),
+         **{f"d_{n}": gr.float() for n, gr in zip(names, grads)})
+
+
 def make_model() -> None:
     """Whole-model prefill of the reference DwarfForCausalLM (seeded init), B=1, T=2048.
 
@@ -494,7 +525,7 @@ def make_checkpoint() -> None:
 
 def main(argv: list[str]) -> None:
     which = argv[1] if len(argv) > 1 else "all"
-    makers = {"ema": make_ema, "ema_bwd": make_ema_backward, "dsqg": make_dsqg, "dsqg_bwd": make_dsqg_backward, "dsqg_module_grad": make_dsqg_module_grad, "hisa": make_hisa, "model": make_model,
+    makers = {"ema": make_ema, "ema_bwd": make_ema_backward, "dsqg": make_dsqg, "dsqg_bwd": make_dsqg_backward, "dsqg_module_grad": make_dsqg_module_grad, "hisa": make_hisa, "hisa_bwd": make_hisa_backward, "model": make_model,
               "checkpoint": make_checkpoint}
     for name, maker in makers.items():
         if which in ("all", name):
