@@ -6,7 +6,7 @@ V18) with ``forward(x, kv_inject=None, *, valid_lengths=None,
 return_metadata=False, return_auxiliary=False)`` and ``prepare_runtime``;
 ``HISAMetadata``; ``HISASelectionCapture``.
 
-Device pipeline of one forward (eval mode):
+Device pipeline of one inference forward (eval mode, no gradients):
 qkvg GEMM and the rank-16 adapter GEMMs (cuBLAS) -> ``dwarf_npci_rotate``
 (adapter add + EMA/NPCI rotation of global K and V, one pass each) ->
 ``dwarf_hisa_reps`` (chunk representatives) -> ``dwarf_hisa_select`` (tile
@@ -19,8 +19,14 @@ window 64, top_k <= 4, hisa_top_m_tokens >= chunk (the reference's
 ``enumerate_all`` path), representative modes mean_max_blend / mean / max_l2.
 Metadata requested with ``return_metadata=True`` carries the routed chunk
 indices with ``enumerate_all=True`` (every token of a routed chunk is used,
-the same token set the reference's canonical listing names). Training mode
-(exploration slot, router auxiliary loss) raises: this is a forward engine.
+the same token set the reference's canonical listing names).
+
+Training mode, or any forward whose inputs or parameters need gradients, takes
+``_forward_autograd``: the projections, adapters, NPCI rotation, chunk
+representatives, route prior, exploration slot and router auxiliary loss as
+torch ops on the device, the chunk selection on ``dwarf_hisa_select`` and the
+attention on ``dwarf_hisa_attn`` / ``dwarf_hisa_attn_bwd``. Routing
+diagnostics (entropy, attention mass) are not computed.
 """
 
 from __future__ import annotations
@@ -35,7 +41,7 @@ import torch.nn.functional as F
 
 from . import _lib
 from .glue import gate_mul
-from .npci import npci_rotate_cuda
+from .npci import npci_rotate_autograd, npci_rotate_cuda
 
 _HD = 64
 _CHUNK = 64
@@ -259,6 +265,130 @@ def hisa_tile_attention(query, local_key, local_value, global_key, global_value,
         raise ValueError("at most 4 routed chunks per tile")
     lengths = _as_valid_lengths(valid_lengths, batch_size=B, seq_len=T, device=query.device)
     return _HisaAttnFn.apply(query, local_key, local_value, global_key, global_value, route, top_chunk_idx, lengths)
+
+
+# ---------------------------------------------------------------------------
+# Training-path router: differentiable device ops. The chunk selection itself
+# comes from ``dwarf_hisa_select`` (integer decisions, no gradient); what the
+# loss differentiates through -- the chunk representatives, the route prior of
+# the selected chunks and the router's auxiliary loss -- is small next to the
+# attention and is written here as torch ops on the device, as the reference
+# writes it (its own training path is these ops under autograd).
+
+
+def _chunk_view(key: torch.Tensor, lengths: torch.Tensor):
+    """(chunks [B,H,C,64,D], token_valid [B,1,C,64], chunk_valid [B,C]) (reference :148-168)."""
+    B, H, T, D = key.shape
+    C = max(1, -(-T // _CHUNK))
+    padded = F.pad(key, (0, 0, 0, C * _CHUNK - T)) if C * _CHUNK > T else key
+    ids = torch.arange(C * _CHUNK, device=key.device, dtype=torch.int32).reshape(1, 1, C, _CHUNK)
+    token_valid = ids < lengths.reshape(B, 1, 1, 1)
+    starts = torch.arange(C, device=key.device, dtype=torch.int32) * _CHUNK
+    chunk_valid = starts.reshape(1, C) < lengths.reshape(B, 1)
+    return padded.reshape(B, H, C, _CHUNK, D), token_valid, chunk_valid
+
+
+def representatives_autograd(global_key: torch.Tensor, lengths: torch.Tensor, blend_alpha: float) -> torch.Tensor:
+    """Chunk representatives as differentiable ops: (1 - a) * mean + a * (row of largest
+    squared norm, first on ties), L2-normalised (eps 1e-6), zero for chunks starting at
+    or past the valid length, in the key's dtype (reference
+    ``_completed_chunk_representatives``, hierarchical_sparse_attn_v18_hisa.py:171-219;
+    a = 0 is its "mean" mode, a = 1 its "max_l2" mode)."""
+    chunks, token_valid, chunk_valid = _chunk_view(global_key, lengths)
+    values = chunks.float()
+    weight = token_valid.unsqueeze(-1).to(values.dtype)
+    mean = (values * weight).sum(3) / weight.sum(3).clamp_min(1.0)
+    energy = values.detach().square().sum(-1).masked_fill(~token_valid, float("-inf"))
+    best = energy.argmax(-1, keepdim=True)
+    peak = torch.gather(values, 3, best.unsqueeze(-1).expand(-1, -1, -1, 1, values.shape[-1])).squeeze(3)
+    rep = F.normalize((1.0 - blend_alpha) * mean + blend_alpha * peak, dim=-1, eps=1e-6)
+    return rep.masked_fill(~chunk_valid[:, None, :, None], 0.0).to(global_key.dtype)
+
+
+def _eligible(tiles: int, num_chunks: int, lengths: torch.Tensor) -> torch.Tensor:
+    """bool [B, tiles, C]: chunk complete before the tile starts, chunk and tile inside the
+    valid length (reference ``_eligibility``, :222-237)."""
+    device = lengths.device
+    tile_starts = torch.arange(tiles, device=device, dtype=torch.int32) * _TILE
+    chunk_starts = torch.arange(num_chunks, device=device, dtype=torch.int32) * _CHUNK
+    tile_valid = tile_starts.reshape(1, -1) < lengths.reshape(-1, 1)
+    chunk_valid = chunk_starts.reshape(1, -1) < lengths.reshape(-1, 1)
+    completed = (chunk_starts + _CHUNK).reshape(1, 1, -1) <= tile_starts.reshape(1, -1, 1)
+    return completed & chunk_valid[:, None, :] & tile_valid[:, :, None]
+
+
+def inject_exploration(top: torch.Tensor, eligible: torch.Tensor, probability: float) -> torch.Tensor:
+    """With probability ``probability`` per (b, h, tile), the last slot of ``top`` is
+    replaced by a uniformly drawn eligible chunk that is not selected yet (reference
+    ``_inject_exploration_slot``, :240-287: the same draws, ``torch.rand`` over
+    [B,H,tiles,C] then over [B,H,tiles], on the device)."""
+    if probability <= 0.0 or top.shape[-1] == 0:
+        return top
+    B, H, tiles, slots = top.shape
+    valid = top >= 0
+    counts = torch.zeros(B, H, tiles, eligible.shape[-1], dtype=torch.int32, device=top.device)
+    counts.scatter_add_(-1, top.clamp_min(0).long(), valid.to(torch.int32))
+    candidate = eligible[:, None].expand(-1, H, -1, -1) & ~(counts > 0)
+    random_scores = torch.rand(candidate.shape, device=top.device).masked_fill(~candidate, -1.0)
+    best_value, best_choice = random_scores.max(-1)
+    replace = (torch.rand(B, H, tiles, device=top.device) < probability) & (best_value >= 0.0)
+    result = top.clone()
+    result[..., slots - 1] = torch.where(replace, best_choice.to(result.dtype), result[..., slots - 1])
+    return result.contiguous()
+
+
+def selected_route_scores(query_normalized: torch.Tensor, reps: torch.Tensor, top: torch.Tensor,
+                          route_scale: torch.Tensor) -> torch.Tensor:
+    """Route prior [B,H,T,4] of the selected chunks as differentiable ops: per query and
+    slot, q̂ . rep minus the mean over the tile's valid slots, times the head's scale; 0
+    for invalid and padding slots; in the query's dtype (reference ``_selected_route_scores``,
+    :418-468)."""
+    B, H, T, D = query_normalized.shape
+    tiles, K = top.shape[2], top.shape[3]
+    padded = tiles * _TILE
+    q = F.pad(query_normalized, (0, 0, 0, padded - T)) if padded > T else query_normalized
+    q = q.reshape(B, H, tiles, _TILE, D)
+    b_idx = torch.arange(B, device=top.device).reshape(B, 1, 1, 1)
+    h_idx = torch.arange(H, device=top.device).reshape(1, H, 1, 1)
+    selected = reps[b_idx, h_idx, top.clamp_min(0).long()]
+    scores = torch.einsum("bhtsd,bhtkd->bhtsk", q.float(), selected.float())
+    valid = (top >= 0)[..., None, :]
+    count = valid.sum(-1, keepdim=True).clamp_min(1)
+    mean = (scores * valid).sum(-1, keepdim=True) / count
+    centred = torch.where(valid, scores - mean, torch.zeros_like(scores))
+    scaled = centred * route_scale.reshape(1, H, 1, 1, 1).float()
+    route = scaled.reshape(B, H, padded, K)[:, :, :T].to(query_normalized.dtype)
+    return F.pad(route, (0, _MAX_TOP_K - K)) if K < _MAX_TOP_K else route
+
+
+def router_auxiliary_loss(anchor_logits: torch.Tensor, anchor_query: torch.Tensor, global_key: torch.Tensor,
+                          lengths: torch.Tensor, *, samples: int, temperature: float) -> torch.Tensor:
+    """Cross entropy of the anchor routing against the token-level chunk evidence
+    (logsumexp over each eligible chunk's q . k / 8) of up to ``samples`` selector tiles
+    drawn without replacement (all of them when that covers every candidate tile)
+    (reference ``_router_auxiliary_loss``, :471-531)."""
+    if samples <= 0:
+        return anchor_logits.sum() * 0.0
+    B, H, tiles, C = anchor_logits.shape
+    eligible_all = _eligible(tiles, C, lengths)
+    first_useful = -(-_CHUNK // _TILE)
+    candidates = max(0, tiles - first_useful)
+    if candidates == 0:
+        return anchor_logits.sum() * 0.0
+    count = min(int(samples), candidates)
+    useful = torch.arange(first_useful, tiles, device=anchor_logits.device, dtype=torch.long)
+    tile_ids = useful if count == candidates else useful[torch.randperm(candidates, device=anchor_logits.device)[:count]]
+    chunks, token_valid, _ = _chunk_view(global_key, lengths)
+    query = anchor_query[:, :, tile_ids].float()
+    token_scores = torch.einsum("bhsd,bhcmd->bhscm", query, chunks.float()) / math.sqrt(global_key.shape[-1])
+    eligible = eligible_all[:, tile_ids]
+    mask = token_valid[:, :, None] & eligible[:, None, :, :, None]
+    evidence = torch.logsumexp(token_scores.masked_fill(~mask, -1e9), dim=-1)
+    route = anchor_logits[:, :, tile_ids].float().masked_fill(~eligible[:, None], -1e9)
+    target = torch.softmax((evidence / float(temperature)).detach(), dim=-1)
+    per_row = -(target * torch.log_softmax(route, dim=-1)).sum(-1)
+    valid_rows = eligible.any(-1)[:, None].expand(-1, H, -1)
+    return (per_row * valid_rows).sum() / valid_rows.sum().clamp_min(1)
 
 
 def hisa_attention(query, local_key, local_value, global_key, global_value, route_scale, valid_lengths=None, *,
@@ -508,8 +638,6 @@ class HierarchicalSparseAttentionV16HISACausal(nn.Module):
             raise NotImplementedError("representative_mode='top2_blend' is not implemented on B200")
         if self.backend == "eager":
             raise NotImplementedError("the B200 engine has no eager backend")
-        if self.training:
-            raise NotImplementedError("the B200 engine is a forward engine; call .eval() (no exploration/aux loss)")
 
     @property
     def _blend_alpha(self) -> float:
@@ -632,12 +760,73 @@ class HierarchicalSparseAttentionV16HISACausal(nn.Module):
                        out=_to_heads(attended, B, L, self.H, self.hd), tile_count=1, pos=pos)
         return F.linear(attended.index_select(1, pos), self.W_o.weight.to(act)), gate
 
+    def _forward_autograd(self, x: torch.Tensor, kv_inject, lengths: torch.Tensor):
+        """Differentiable forward (training, or any call that needs gradients): the
+        reference forward (hierarchical_sparse_attn_v18_hisa.py:2546-2787) with the
+        projections, the global adapters, the NPCI rotation, the chunk representatives,
+        the route prior and the router's auxiliary loss as torch ops on the device, the
+        chunk selection on ``dwarf_hisa_select`` (plus the training-mode exploration
+        slot) and the attention on ``dwarf_hisa_attn`` / ``dwarf_hisa_attn_bwd``.
+        Returns (output [B,T,D] in x's dtype, top_chunk_idx, auxiliary loss)."""
+        B, T, _ = x.shape
+        q, k, v, gate = self.qkvg_proj(x).split(self.D, dim=-1)
+        query = _to_heads(q, B, T, self.H, self.hd)
+        local_key = _to_heads(k, B, T, self.H, self.hd)
+        local_value = _to_heads(v, B, T, self.H, self.hd)
+        global_key, global_value = local_key, local_value
+        if self.global_adapter_rank:
+            global_key = global_key + _to_heads(self.global_k_up(self.global_k_down(x)), B, T, self.H, self.hd)
+            global_value = global_value + _to_heads(self.global_v_up(self.global_v_down(x)), B, T, self.H, self.hd)
+        if kv_inject is not None:
+            kd, vd = kv_inject
+            if kd.shape != global_key.shape or vd.shape != global_value.shape:
+                raise ValueError("kv_inject must contain [B,H,N,HD] tensors")
+            global_key = npci_rotate_autograd(global_key, kd, self.npci_theta_max * torch.tanh(self.npci_theta_k))
+            global_value = npci_rotate_autograd(global_value, vd,
+                                                self.npci_theta_max * torch.tanh(self.npci_theta_v))
+        reps = representatives_autograd(global_key, lengths, self._blend_alpha)
+        query_normalized = F.normalize(query.float(), dim=-1, eps=1e-6).to(query.dtype)
+        tiles = -(-T // self.selector_tile_size)
+        starts = (torch.arange(tiles, device=x.device) * self.selector_tile_size).clamp_max(T - 1)
+        anchor = query_normalized[:, :, starts]
+        anchor_logits = torch.matmul(anchor.float(), reps.float().transpose(-2, -1)) / self.temperature
+        act = torch.bfloat16
+        top, _ = select_chunks(query.detach().to(act).contiguous(), reps.detach().to(act).contiguous(), lengths,
+                               top_k=self.top_k_chunks, temperature=self.temperature)
+        if self.training and self.exploration_probability > 0.0:
+            top = inject_exploration(top, _eligible(tiles, reps.shape[2], lengths), self.exploration_probability)
+        route = selected_route_scores(query_normalized, reps, top, self.route_prior_scale)
+        auxiliary = None
+        if self.training and self.route_aux_weight > 0.0:
+            auxiliary = router_auxiliary_loss(anchor_logits, anchor, global_key, lengths,
+                                              samples=self.route_aux_samples,
+                                              temperature=self.route_aux_temperature) * self.route_aux_weight
+            self._routing_auxiliary_loss = auxiliary
+            self.hisa_evidence_capture = HISASelectionCapture(anchor_logits=anchor_logits,
+                                                              metadata=self._metadata(top, lengths),
+                                                              auxiliary_loss=auxiliary)
+        self._last_token_selection_path = "enumerate_all"
+        attended = hisa_tile_attention(query, local_key, local_value, global_key, global_value, route, top, lengths)
+        merged = attended.to(x.dtype).permute(0, 2, 1, 3).reshape(B, T, self.D)
+        output = self.W_o(merged) * torch.sigmoid(gate)
+        if auxiliary is None:
+            auxiliary = output.sum() * 0.0
+        return output, top, auxiliary
+
+    def _metadata(self, top: torch.Tensor, lengths: torch.Tensor) -> HISAMetadata:
+        tiles = top.shape[2]
+        return HISAMetadata(
+            top_chunk_idx=top,
+            token_idx=torch.empty(0, dtype=torch.int32, device=top.device),
+            token_scores=torch.empty(0, dtype=torch.float32, device=top.device),
+            tile_starts=torch.arange(tiles, device=top.device, dtype=torch.int32) * self.selector_tile_size,
+            valid_lengths=lengths, chunk_size=self.chunk_size, selector_tile_size=self.selector_tile_size,
+            enumerate_all=True)
+
     def forward(self, x: torch.Tensor, kv_inject=None, *, valid_lengths=None, return_metadata: bool = False,
                 return_auxiliary: bool = False):
         self._check_supported()
         _lib.require_cuda(x)
-        if torch.is_grad_enabled() and (x.requires_grad or any(p.requires_grad for p in self.parameters())):
-            raise NotImplementedError("dwarf_v2_b200 is a forward (inference) engine; run under torch.no_grad()")
         self.hisa_evidence_capture = None
         self._routing_auxiliary_loss = None
         B, T, _ = x.shape
@@ -646,21 +835,17 @@ class HierarchicalSparseAttentionV16HISACausal(nn.Module):
         lengths = _as_valid_lengths(
             valid_lengths if valid_lengths is not None else getattr(self, "_causal_control_valid_lengths", None),
             batch_size=B, seq_len=T, device=x.device)
-        projected, gate, top = self.forward_parts(x, kv_inject, lengths)
-        act = torch.bfloat16
-        output = gate_mul(projected, gate)
-        if x.dtype != act:
-            output = output.to(x.dtype)
-        auxiliary = output.new_zeros(())
+        grad = torch.is_grad_enabled() and (x.requires_grad or any(p.requires_grad for p in self.parameters()))
+        if grad or self.training:
+            output, top, auxiliary = self._forward_autograd(x, kv_inject, lengths)
+        else:
+            projected, gate, top = self.forward_parts(x, kv_inject, lengths)
+            output = gate_mul(projected, gate)
+            if x.dtype != torch.bfloat16:
+                output = output.to(x.dtype)
+            auxiliary = output.new_zeros(())
         if return_metadata:
-            tiles = top.shape[2]
-            metadata = HISAMetadata(
-                top_chunk_idx=top,
-                token_idx=torch.empty(0, dtype=torch.int32, device=x.device),
-                token_scores=torch.empty(0, dtype=torch.float32, device=x.device),
-                tile_starts=torch.arange(tiles, device=x.device, dtype=torch.int32) * self.selector_tile_size,
-                valid_lengths=lengths, chunk_size=self.chunk_size, selector_tile_size=self.selector_tile_size,
-                enumerate_all=True)
+            metadata = self._metadata(top, lengths)
             return (output, metadata, auxiliary) if return_auxiliary else (output, metadata)
         return (output, auxiliary) if return_auxiliary else output
 

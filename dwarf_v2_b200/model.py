@@ -14,7 +14,10 @@ the next RMSNorm (and, after the HISA block, with its sigmoid output gate),
 SwiGLU, the EMA packet (three look-back scans + one epilogue kernel); GEMMs
 are cuBLAS bf16. Activations are bf16 with the reference's rounding points.
 ``kv_cache="q6"`` runs every DSQG layer over the q6-quantised K/V cache.
-Eval mode only (dropout, HISA exploration and aux loss are training features).
+Calls that need gradients (training mode, or autograd on with parameters that
+require grad) take the reference's own block formulas as torch ops over the
+engine's differentiable DSQG, HISA and EMA-scan functions (forward and backward
+kernels); ``forward_lse`` and the decode entry points are inference-only.
 """
 
 from __future__ import annotations
@@ -103,6 +106,18 @@ def _act(t: torch.Tensor) -> torch.Tensor:
     return t if t.dtype == torch.bfloat16 else t.to(torch.bfloat16)
 
 
+def _wants_grad(module: nn.Module, *tensors: torch.Tensor) -> bool:
+    """True when a forward must be differentiable (or apply training-mode randomness):
+    the module is training, or autograd is on and an input or a parameter requires grad.
+    Such calls take the reference's own formulas as torch ops, with the engine's
+    differentiable attention / scan functions; the rest take the fused inference kernels."""
+    if module.training:
+        return True
+    if not torch.is_grad_enabled():
+        return False
+    return any(t.requires_grad for t in tensors) or any(p.requires_grad for p in module.parameters())
+
+
 class RMSNorm(nn.Module):
     def __init__(self, dimension: int, eps: float = 1e-6) -> None:
         super().__init__()
@@ -110,6 +125,10 @@ class RMSNorm(nn.Module):
         self.eps = eps
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if _wants_grad(self, x):  # reference train/train_dwarf.py:224-227
+            xf = x.float()
+            normalized = xf * torch.rsqrt(xf.square().mean(-1, keepdim=True) + self.eps)
+            return (normalized * self.weight.float()).to(x.dtype)
         return glue.rmsnorm(_act(x), self.weight.detach(), self.eps)
 
 
@@ -145,6 +164,9 @@ class SwiGLUFFN(nn.Module):
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         """down(silu(gate) * up): the tcgen05 GEMM with the SwiGLU epilogue, then the down projection."""
+        if _wants_grad(self, x):  # reference train/train_dwarf.py:238-240
+            up, gate = self.up_gate(x).chunk(2, dim=-1)
+            return self.down(self.dropout(F.silu(gate) * up))
         w_il, w_down, tile = self._fused_weights()
         h = gemm.linear_swiglu(_act(x), w_il, tile)
         return gemm.linear(h, w_down)
@@ -193,6 +215,8 @@ class InterferencePacket(nn.Module):
         """(key_delta, value_delta) [B,H,T,hd]. With ``ema_states`` (one fp32 [B,D] state tensor
         per timescale) the scans continue from those states, which are then overwritten in
         place with the states after the last token."""
+        if ema_states is None and _wants_grad(self, normalized):
+            return self._forward_autograd(normalized)
         x = _act(normalized)
         factors, mixture = self._constants()
         if ema_states is None:
@@ -212,6 +236,29 @@ class InterferencePacket(nn.Module):
         return key_delta, value_delta
 
 
+def _packet_autograd(self, normalized: torch.Tensor):
+    """Differentiable packet (reference train/train_dwarf.py:260-284): the three EMA
+    scans on ``causal_ema_scan``'s autograd path, the rest as torch ops."""
+    scan_input = normalized.to(torch.bfloat16)
+    scans = [causal_ema_scan(scan_input, factor.reshape(1)) for factor in self.ema_factors]
+    mixture = torch.softmax(self.mix_logits.float(), dim=0)
+    pooled = sum(weight.to(scans[0].dtype) * scan for weight, scan in zip(mixture, scans))
+    pooled_float = pooled.float()
+    rms = pooled_float.square().mean(-1, keepdim=True).sqrt()
+    direction = pooled_float * torch.rsqrt(pooled_float.square().mean(-1, keepdim=True) + 1e-6)
+    confidence = torch.tanh(rms / 0.25)
+    gate = torch.sigmoid(self.gate_proj(normalized).float())
+    packet = (direction * confidence * gate).to(normalized.dtype)
+    key_delta, value_delta = self.kv_proj(packet).chunk(2, dim=-1)
+    B, T, _ = normalized.shape
+    key_delta = key_delta.reshape(B, T, self.heads, self.head_dim).permute(0, 2, 1, 3)
+    value_delta = value_delta.reshape(B, T, self.heads, self.head_dim).permute(0, 2, 1, 3)
+    return key_delta, value_delta
+
+
+InterferencePacket._forward_autograd = _packet_autograd
+
+
 class DSQGBlock(nn.Module):
     def __init__(self, config: DwarfConfig, offsets: tuple[int, ...], *, plane_shift: int,
                  kv_cache: str = "bf16") -> None:
@@ -229,6 +276,9 @@ class DSQGBlock(nn.Module):
         self.ffn = SwiGLUFFN(config)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if _wants_grad(self, x):  # reference train/train_dwarf.py:320-322
+            x = x + self.attn(self.norm1(x))
+            return x + self.ffn(self.norm2(x))
         x, n2 = glue.add_rmsnorm(_act(x), self.norm2.weight.detach(), addend=self.attn(self.norm1(x)))
         x, _ = glue.add_rmsnorm(x, self.norm2.weight.detach(), addend=self.ffn(n2))
         return x
@@ -256,6 +306,9 @@ class GlobalMixerBlock(nn.Module):
     def forward(self, x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
         normalized = self.norm1(x)
         attended, auxiliary = self.attn(normalized, kv_inject=self.packet(normalized), return_auxiliary=True)
+        if _wants_grad(self, x):  # reference train/train_dwarf.py:356-364
+            x = x + self.dropout(attended)
+            return x + self.ffn(self.norm2(x)), auxiliary
         x, n2 = glue.add_rmsnorm(_act(x), self.norm2.weight.detach(), addend=attended)
         x, _ = glue.add_rmsnorm(x, self.norm2.weight.detach(), addend=self.ffn(n2))
         return x, auxiliary
@@ -390,19 +443,37 @@ class DwarfForCausalLM(nn.Module):
             if isinstance(module, HierarchicalSparseAttentionV16HISACausal):
                 module.prepare_runtime(device, self.config.model_length)
 
-    def _check(self, input_ids: torch.Tensor) -> None:
-        if self.training:
-            raise NotImplementedError("the B200 engine is a forward engine; call .eval()")
+    def _check(self, input_ids: torch.Tensor, *, inference_only: bool = False) -> None:
         if not input_ids.is_cuda:
             raise RuntimeError("dwarf_v2_b200 runs on CUDA tensors only (no CPU fallback)")
         if input_ids.ndim != 2:
             raise ValueError("input_ids must be [B, T]")
-        if torch.is_grad_enabled() and any(p.requires_grad for p in self.parameters()):
-            raise NotImplementedError("dwarf_v2_b200 is a forward (inference) engine; run under torch.no_grad()")
+        if inference_only and _wants_grad(self):
+            raise NotImplementedError("this entry point is inference-only: call .eval() and run under "
+                                      "torch.no_grad()")
+
+    def _forward_hidden_autograd(self, input_ids: torch.Tensor):
+        """Differentiable forward (training): the reference's forward_hidden
+        (train/train_dwarf.py:439-459) -- bf16 activations, as the reference casts them
+        on CUDA (its trainer runs under torch.autocast bf16, which these GEMMs expect
+        too) -- through the blocks' differentiable paths."""
+        x = self.embedding(input_ids).to(torch.bfloat16)
+        x = self.dropout(x)
+        auxiliary = x.sum() * 0.0
+        for block in self.blocks:
+            if isinstance(block, GlobalMixerBlock):
+                x, block_auxiliary = block(x)
+                auxiliary = auxiliary + block_auxiliary
+            else:
+                x = block(x)
+        return self.norm(x).to(torch.bfloat16), auxiliary
 
     def forward_hidden(self, input_ids: torch.Tensor, *, return_auxiliary: bool = False):
         """Final RMSNorm'd hidden states [B, T, D] (bf16)."""
         self._check(input_ids)
+        if _wants_grad(self):
+            hidden, auxiliary = self._forward_hidden_autograd(input_ids)
+            return (hidden, auxiliary) if return_auxiliary else hidden
         emb = _act(self.embedding.weight.detach()).contiguous()
         blocks = list(self.blocks)
         x, n = glue.embed_rmsnorm(input_ids, emb, blocks[0].norm1.weight.detach())
@@ -423,6 +494,7 @@ class DwarfForCausalLM(nn.Module):
     def forward_lse(self, input_ids: torch.Tensor, labels: torch.Tensor | None = None):
         """Per-token (logsumexp, argmax, cross entropy vs ``labels`` or None), each [B, T], from the
         lm_head GEMM's reducing epilogue: the [B, T, vocab] logits are never written."""
+        self._check(input_ids, inference_only=True)
         hidden = self.forward_hidden(input_ids)
         B, T, _ = hidden.shape
         lse, argmax, loss = gemm.linear_lse(hidden, _act(self.embedding.weight.detach()),
@@ -464,7 +536,7 @@ class DwarfForCausalLM(nn.Module):
     def forward_cached(self, input_ids: torch.Tensor, state: "DecodeState") -> torch.Tensor:
         """Final RMSNorm'd hidden states [B,T,D] of the T tokens following ``state.length``
         cached positions; appends their caches and advances ``state.length`` by T."""
-        self._check(input_ids)
+        self._check(input_ids, inference_only=True)
         B, T = input_ids.shape
         if B != state.batch:
             raise ValueError(f"state holds {state.batch} sequences, input_ids {B}")
@@ -526,7 +598,7 @@ class DwarfForCausalLM(nn.Module):
         """One incremental step: ``token_ids`` [B] at position ``state.length``; returns its
         logits [B,V] (those of a prefill over the ``state.length + 1`` tokens at its last row,
         up to the decode DSQG kernel's fp32 summation order)."""
-        self._check(token_ids.reshape(-1, 1))
+        self._check(token_ids.reshape(-1, 1), inference_only=True)
         if token_ids.numel() != state.batch:
             raise ValueError(f"state holds {state.batch} sequences, got {token_ids.numel()} tokens")
         if state.length >= state.max_len:
@@ -541,5 +613,10 @@ class DwarfForCausalLM(nn.Module):
 
     def forward(self, input_ids: torch.Tensor, *, return_hidden: bool = False, return_auxiliary: bool = False):
         hidden, auxiliary = self.forward_hidden(input_ids, return_auxiliary=True)
-        output = hidden if return_hidden else gemm.linear(hidden, _act(self.embedding.weight.detach()))
+        if return_hidden:
+            output = hidden
+        elif hidden.requires_grad:
+            output = self.lm_head(hidden)  # reference train/train_dwarf.py:469
+        else:
+            output = gemm.linear(hidden, _act(self.embedding.weight.detach()))
         return (output, auxiliary) if return_auxiliary else output

@@ -19,6 +19,7 @@ from pathlib import Path
 
 import numpy as np
 import torch
+import torch.nn.functional as F
 
 HERE = Path(__file__).resolve().parent
 REFERENCE = Path(os.environ.get("DWARF_REFERENCE_DIR", "/root/reference"))
@@ -400,8 +401,133 @@ def make_hisa_backward() -> None:
     dout = torch.randn(merged.shape, generator=torch.Generator().manual_seed(51), dtype=torch.float64)
     dout = dout.to(torch.bfloat16)
     grads = torch.autograd.grad(merged, [leaves[n] for n in names], dout.double())
+    # Router auxiliary loss on the same inputs (every candidate tile, so no draw).
+    import torch.nn.functional as F
+    qn = F.normalize(g["q"].float(), dim=-1, eps=1e-6).to(g["q"].dtype)
+    anchor = qn[:, :, (torch.arange(-(-T // 16)) * 16).clamp_max(T - 1)]
+    logits = torch.matmul(anchor.float(), g["reps"].float().transpose(-2, -1))
+    aux = ref._router_auxiliary_loss(logits, anchor, g["global_key"], meta, samples=64, temperature=1.0)
     save("hisa_bwd_lanes", dout=dout, merged=merged.detach().float(),
-         **{f"d_{n}": gr.float() for n, gr in zip(names, grads)})
+         **{f"d_{n}": gr.float() for n, gr in zip(names, grads)}, aux=aux)
+
+
+def make_hisa_module_grad() -> None:
+    """Training-mode gradients of the reference HISA module (CPU, fp32, exploration
+    off, the router auxiliary loss over every candidate tile so that no tile is drawn
+    at random): output, auxiliary loss, dx and every parameter's gradient of
+    sum(y * dy) + aux, with and without a kv_inject packet. T=300 (the last chunk
+    partial) with valid lengths 300 / 250; at most four chunks are eligible, so the
+    routed set does not hinge on near-ties of the anchor logits."""
+    _import_reference()
+    import hierarchical_sparse_attn_v18_hisa as ref
+
+    torch.manual_seed(5)
+    module = ref.HierarchicalSparseAttentionV16HISACausal(
+        D=128, H=2, hd=64, chunk_size=64, top_k_chunks=4, hisa_top_m_tokens=64, local_window=64,
+        selector_tile_size=16, representative_mode="mean_max_blend", representative_blend_alpha=0.5,
+        route_prior_scale=0.1, route_aux_weight=0.01, route_aux_samples=64, route_aux_temperature=1.0,
+        exploration_probability=0.0, global_adapter_rank=16, npci_theta_max=0.25, local_backend="flex").train()
+    gen = torch.Generator().manual_seed(55)
+    with torch.no_grad():
+        module.qkvg_proj.weight.mul_(4.0)
+        for p in (module.global_k_up.weight, module.global_v_up.weight):
+            p.copy_(torch.randn(p.shape, generator=gen) * 0.05)
+        module.route_prior_raw.copy_(torch.tensor([-1.0, 0.5]))
+        module.npci_theta_k.copy_(torch.tensor([1.5, -0.7]))
+        module.npci_theta_v.copy_(torch.tensor([0.4, 2.0]))
+    B, T = 2, 300
+    x = torch.randn(B, T, 128, generator=gen).to(torch.bfloat16).float()
+    kd = torch.randn(B, 2, T, 64, generator=gen) * 0.5
+    vd = torch.randn(B, 2, T, 64, generator=gen) * 0.5
+    dy = torch.randn(B, T, 128, generator=gen)
+    lengths = torch.tensor([300, 250], dtype=torch.int32)
+    state = {f"state.{k}": val for k, val in module.state_dict().items()}
+
+    # A second run with the attention lanes fed and read at the bf16 points of a
+    # bf16 attention kernel (q, K/V and the route prior rounded on the way in,
+    # the merged output rounded on the way out, its incoming gradient rounded to
+    # bf16; gradients to the inputs pass straight through): the reference's
+    # fp32 maths otherwise unchanged.
+    class _Round(torch.autograd.Function):
+        @staticmethod
+        def forward(ctx, t, round_grad):
+            ctx.round_grad = round_grad
+            return t.to(torch.bfloat16).to(t.dtype)
+
+        @staticmethod
+        def backward(ctx, grad):
+            return (grad.to(torch.bfloat16).to(grad.dtype) if ctx.round_grad else grad), None
+
+    local_lane, global_lane, merge = module._local_lane, ref._eager_global_lane, ref._merge_attention_lanes
+
+    def bf16_local(q, k, v, lengths_):
+        return local_lane(*(_Round.apply(t, False) for t in (q, k, v)), lengths_)
+
+    def bf16_global(q, k, v, route, meta, **kw):
+        return global_lane(*(_Round.apply(t, False) for t in (q, k, v, route)), meta, **kw)
+
+    def bf16_merge(*args):
+        merged, lse = merge(*args)
+        return _Round.apply(merged, True), lse
+
+    out = {}
+    for points in ("", "bf16."):
+        if points:
+            module._local_lane = bf16_local
+            ref._eager_global_lane, ref._merge_attention_lanes = bf16_global, bf16_merge
+        for tag, inject in (("plain", None), ("inject", (kd, vd))):
+            module.zero_grad()
+            xl = x.clone().requires_grad_(True)
+            y, aux = module(xl, kv_inject=inject, valid_lengths=lengths, return_auxiliary=True)
+            ((y * dy).sum() + aux).backward()
+            out[f"{points}{tag}.y"] = y.detach()
+            out[f"{points}{tag}.aux"] = aux.detach()
+            out[f"{points}{tag}.dx"] = xl.grad
+            for name, p in module.named_parameters():
+                if p.grad is not None:
+                    out[f"{points}{tag}.grad.{name}"] = p.grad.clone()
+    module._local_lane = local_lane
+    ref._eager_global_lane, ref._merge_attention_lanes = global_lane, merge
+    save("hisa_module_grad", x=x, kd=kd, vd=vd, dy=dy, valid_lengths=lengths, **state, **out)
+
+
+def make_model_train() -> None:
+    """One training step of the reference DwarfForCausalLM (small config: vocab 1024,
+    D=128, H=2, FFN 384, T=256, B=2; seeded init; train mode, dropout 0, HISA
+    exploration off and its auxiliary loss over every candidate tile, so the step
+    has no random draws): loss = cross entropy of the next token + auxiliary loss.
+    Run in fp32 (gradients stored rounded to bf16, loss, aux, logits at a few
+    positions) and in bf16 (its per-parameter cosine and relative norm shift
+    against the fp32 run, the spread that bf16 arithmetic alone causes)."""
+    _import_reference()
+    import train_dwarf as td
+
+    cfg = td.DwarfConfig(vocab_size=1024, embedding_dim=128, num_heads=2, ffn_dim=384, seq_len=257, dropout=0.0)
+    ids = torch.randint(57, 1024, (2, 256), generator=torch.Generator().manual_seed(0))
+    positions = torch.tensor([0, 17, 100, 255])
+    runs = {}
+    for dtype in (torch.float32, torch.bfloat16):
+        model = td.DwarfForCausalLM(cfg).to(dtype).train()
+        for module in model.modules():
+            if hasattr(module, "exploration_probability"):
+                module.exploration_probability = 0.0
+                module.route_aux_samples = 64
+        logits, aux = model(ids, return_auxiliary=True)
+        ce = F.cross_entropy(logits.reshape(-1, cfg.vocab_size).float(), ids.roll(-1, 1).reshape(-1))
+        (ce + aux).backward()
+        runs[dtype] = (logits.detach().float(), ce.detach(), aux.detach(),
+                       {n: p.grad.detach().double() for n, p in model.named_parameters() if p.grad is not None})
+    logits, ce, aux, grads = runs[torch.float32]
+    _, ce16, aux16, grads16 = runs[torch.bfloat16]
+    out = {"input_ids": ids, "positions": positions, "logits": logits[:, positions], "ce": ce, "aux": aux,
+           "ce_bf16": ce16, "aux_bf16": aux16}
+    for name, g32 in grads.items():
+        g16 = grads16[name]
+        out["grad." + name] = g32.to(torch.bfloat16)
+        norm = float(g32.norm())
+        out["cos_bf16." + name] = torch.tensor(float((g32 * g16).sum()) / max(norm * float(g16.norm()), 1e-30))
+        out["norm_shift_bf16." + name] = torch.tensor(abs(float(g16.norm()) - norm) / max(norm, 1e-30))
+    save("model_train_step", **out)
 
 
 def make_model() -> None:
@@ -525,7 +651,7 @@ def make_checkpoint() -> None:
 
 def main(argv: list[str]) -> None:
     which = argv[1] if len(argv) > 1 else "all"
-    makers = {"ema": make_ema, "ema_bwd": make_ema_backward, "dsqg": make_dsqg, "dsqg_bwd": make_dsqg_backward, "dsqg_module_grad": make_dsqg_module_grad, "hisa": make_hisa, "hisa_bwd": make_hisa_backward, "model": make_model,
+    makers = {"ema": make_ema, "ema_bwd": make_ema_backward, "dsqg": make_dsqg, "dsqg_bwd": make_dsqg_backward, "dsqg_module_grad": make_dsqg_module_grad, "hisa": make_hisa, "hisa_bwd": make_hisa_backward, "hisa_module_grad": make_hisa_module_grad, "model": make_model, "model_train": make_model_train,
               "checkpoint": make_checkpoint}
     for name, maker in makers.items():
         if which in ("all", name):

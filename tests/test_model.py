@@ -51,12 +51,14 @@ def test_topology():
     assert model.lm_head.weight is model.embedding.weight
 
 
-def test_forward_requires_cuda_and_eval():
+def test_forward_requires_cuda():
     from dwarf_v2_b200.model import DwarfForCausalLM
 
     model = DwarfForCausalLM()
-    with pytest.raises(NotImplementedError):
-        model(torch.zeros(1, 8, dtype=torch.long))      # training mode
+    with pytest.raises(RuntimeError):
+        model(torch.zeros(1, 8, dtype=torch.long))      # training mode, CPU tensor: no fallback
+    with pytest.raises(RuntimeError):
+        model.forward_lse(torch.zeros(1, 8, dtype=torch.long))
     model.eval()
     with torch.no_grad(), pytest.raises(RuntimeError):
         model(torch.zeros(1, 8, dtype=torch.long))      # CPU tensor: no fallback
