@@ -1,0 +1,279 @@
+"""Per-kernel measurements at the benchmark configuration shapes.
+
+``python -m dwarf_v2_b200.kernel_bench [--case NAME ...] [--iters K] [--warmup W]``
+prints one JSON line per case: the mean device time of each engine entry point
+the case launches (CUDA events around every launch on the launching stream,
+``_lib.LaunchLog``), the algorithmic bytes (and FLOPs where they matter) of the
+case's main kernel, and the achieved rate against the measured HBM peak in
+``MEASURED_PEAKS.json`` (repository root) or, when that file is absent, the
+pool's earlier measurement (6650 GB/s, marked "fallback").
+
+Inputs are synthetic, seeded, with the shapes and distributions of the named
+configurations (config 2: causal EMA scan B=16 T=2048 D=512 fp32; config 3:
+DSQG over a q6 KV cache B=32 H=8 T=2048 J=96; config 4: HISA B=32 H=8 T=2048,
+Q/K/V ~ N(0, 0.125^2)); the backward cases use the same shapes. Before every
+timed iteration a 512 MB buffer is written, so no input starts in the 126 MB L2.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+from pathlib import Path
+
+import torch
+
+from . import _lib
+
+FALLBACK_HBM_GBS = 6650.0
+
+
+def _hbm_peak() -> tuple[float, str]:
+    path = Path(__file__).resolve().parent.parent / "MEASURED_PEAKS.json"
+    if path.is_file():
+        return float(json.loads(path.read_text())["hbm_gbs"]), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def _nbytes(*tensors: torch.Tensor) -> int:
+    return sum(t.numel() * t.element_size() for t in tensors)
+
+
+class _Timer:
+    """Runs ``fn`` ``warmup`` times untimed, then ``iters`` times with an L2 flush before
+    each and every engine launch timed with CUDA events."""
+
+    def __init__(self, warmup: int, iters: int):
+        self.warmup, self.iters = warmup, iters
+        self.flush = torch.empty(512 << 20, dtype=torch.uint8, device="cuda")
+
+    def __call__(self, fn, names: tuple[str, ...]) -> dict[str, float]:
+        for _ in range(self.warmup):
+            fn()
+        torch.cuda.synchronize()
+        log = _lib.LaunchLog(timed=names)
+        for _ in range(self.iters):
+            self.flush.fill_(1)
+            _lib.set_launch_log(log)
+            try:
+                fn()
+            finally:
+                _lib.set_launch_log(None)
+        torch.cuda.synchronize()
+        return {n: log.mean_ms(n) for n in names if log.mean_ms(n) is not None}
+
+
+def _rate(nbytes: int, ms: float, peak: float) -> dict:
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    return {"algorithmic_bytes": nbytes, "achieved_gbs": round(gbs, 1), "frac_of_hbm_peak": round(gbs / peak, 4)}
+
+
+def case_ema_config2(timer, peak):
+    """Config 2: per-channel EMA scan, fp32 [16, 2048, 512] -> fp32."""
+    from .causal_ema_scan import causal_ema_scan_per_channel
+
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(16, 2048, 512, generator=g).cuda()
+    alpha = (1.0 - torch.sigmoid(torch.randn(512, generator=g))).cuda()
+    out = {}
+    times = timer(lambda: out.__setitem__("y", causal_ema_scan_per_channel(x, alpha)), ("dwarf_ema_scan",))
+    ms = times["dwarf_ema_scan"]
+    return {"kernel": "dwarf_ema_scan", "ms": ms, **_rate(2 * _nbytes(x), ms, peak)}
+
+
+def case_ema_model_bf16(timer, peak):
+    """The model's packet scans: scalar alpha, bf16 [32, 2048, 512] (32 rows = one GPU's
+    share of the 256-row prefill batch at 8 GPUs)."""
+    from .causal_ema_scan import causal_ema_scan
+
+    g = torch.Generator().manual_seed(1)
+    x = torch.randn(32, 2048, 512, generator=g).to(torch.bfloat16).cuda()
+    alpha = torch.tensor([1.0 / 16.0], device="cuda")
+    times = timer(lambda: causal_ema_scan(x, alpha), ("dwarf_ema_scan",))
+    ms = times["dwarf_ema_scan"]
+    return {"kernel": "dwarf_ema_scan", "ms": ms, **_rate(2 * _nbytes(x), ms, peak)}
+
+
+def case_ema_bwd_config2(timer, peak):
+    """Config-2 backward: dx (the scan over time-reversed dy) and d alpha (one pass over
+    x, y and dx)."""
+    from .causal_ema_scan import causal_ema_scan_per_channel
+
+    g = torch.Generator().manual_seed(2)
+    x = torch.randn(16, 2048, 512, generator=g).cuda().requires_grad_(True)
+    alpha = (1.0 - torch.sigmoid(torch.randn(512, generator=g))).cuda().requires_grad_(True)
+    dy = torch.randn(16, 2048, 512, generator=g).cuda()
+    y = causal_ema_scan_per_channel(x, alpha)
+
+    def step():
+        x.grad = alpha.grad = None
+        torch.autograd.backward(y, dy, retain_graph=True)
+
+    times = timer(step, ("dwarf_ema_scan", "dwarf_ema_scan_grad_alpha"))
+    return {"kernels": times,
+            "dwarf_ema_scan": _rate(2 * _nbytes(x), times["dwarf_ema_scan"], peak),
+            "dwarf_ema_scan_grad_alpha": _rate(3 * _nbytes(x), times["dwarf_ema_scan_grad_alpha"], peak)}
+
+
+def case_q6_pack_config3(timer, peak):
+    """Config-3 K (or V) cache quantisation: bf16 [32, 8, 2048, 64] -> codes + fp16 scales."""
+    from .q6 import q6_pack
+
+    g = torch.Generator().manual_seed(3)
+    k = torch.randn(32, 8, 2048, 64, generator=g).to(torch.bfloat16).cuda()
+    res = {}
+    times = timer(lambda: res.__setitem__("c", q6_pack(k)), ("dwarf_q6_pack",))
+    codes, scales = res["c"]
+    ms = times["dwarf_q6_pack"]
+    return {"kernel": "dwarf_q6_pack", "ms": ms, **_rate(_nbytes(k, codes, scales), ms, peak)}
+
+
+def _dsqg_tables(J: int, js: int, H: int, offsets, g):
+    pb = torch.randn(J, H, generator=g) * 0.3 - torch.log1p(torch.tensor(offsets, dtype=torch.float32))[:, None]
+    return (pb.cuda(), (torch.randn(J, 64, generator=g) * 0.05).cuda(),
+            (torch.randn(J - js, H, 4, generator=g) * 0.5).cuda(), (torch.randn(J - js, H, 4, generator=g) * 2.0).cuda())
+
+
+def case_dsqg_q6_config3(timer, peak):
+    """Config 3: DSQG over a q6 KV cache, B=32 H=8 T=2048, the full 96-offset lattice."""
+    from .dsqg_attention_v22 import ALL_OFFSETS, dsqg_attention_q6
+    from .q6 import q6_pack
+
+    g = torch.Generator().manual_seed(4)
+    B, H, N, J, js = 32, 8, 2048, len(ALL_OFFSETS), 17
+    q = torch.randn(B, H, N, 64, generator=g).to(torch.bfloat16).cuda()
+    kc, ks = q6_pack(torch.randn(B, H, N, 64, generator=g).to(torch.bfloat16).cuda())
+    vc, vs = q6_pack(torch.randn(B, H, N, 64, generator=g).to(torch.bfloat16).cuda())
+    pb, se, pbase, pgain = _dsqg_tables(J, js, H, ALL_OFFSETS, g)
+    y = (torch.randn(B, H, N, 4, generator=g) * 0.2).cuda()
+    z = (torch.randn(B, H, N, 4, generator=g) * 0.2).cuda()
+    offs = torch.tensor(ALL_OFFSETS, dtype=torch.int32, device="cuda")
+    res = {}
+    times = timer(lambda: res.__setitem__("o", dsqg_attention_q6(q, kc, ks, vc, vs, pb, se, pbase, pgain, y, z,
+                                                                  offs, js, J - js, 0, 1)), ("dwarf_dsqg_fwd",))
+    ms = times["dwarf_dsqg_fwd"]
+    valid_pairs = sum(max(0, N - d) for d in ALL_OFFSETS) * B * H
+    flops = valid_pairs * 4 * 64  # q.k and p.v: 2 x 64 FMAs per (query, offset) pair
+    return {"kernel": "dwarf_dsqg_fwd (q6, 96 offsets)", "ms": ms,
+            **_rate(_nbytes(q, kc, ks, vc, vs, y, z, res["o"]), ms, peak),
+            "valid_pairs": valid_pairs, "fp32_tflops": round(flops / (ms * 1e-3) / 1e12, 2)}
+
+
+def case_dsqg_bwd_model_group(timer, peak):
+    """DSQG backward at the config-3 shape (B=32 H=8 T=2048) with bf16 K/V and the model's
+    first 29-offset group (one training layer): query-side and key-side gather kernels."""
+    from .dsqg_attention_v22 import ALL_OFFSETS, dsqg_attention_v18_grouped
+
+    offsets = [o for o in sorted(ALL_OFFSETS) if 2048 - o >= 64][0::3]
+    js = sum(1 for o in offsets if o <= 28)
+    J = len(offsets)
+    g = torch.Generator().manual_seed(5)
+    B, H, N = 32, 8, 2048
+    r = lambda *s, std=1.0: (torch.randn(*s, generator=g) * std).cuda()  # noqa: E731
+    leaves = [r(B, H, N, 64).bfloat16(), r(B, H, N, 64).bfloat16(), r(B, H, N, 64).bfloat16(), r(J, H, std=0.3),
+              r(J, 64, std=0.3), r(J - js, H, 4, std=0.7), r(J - js, H, 4, std=2.0),
+              r(B, H, N, 4, std=0.5).clamp(-1, 1), r(B, H, N, 4, std=0.5).clamp(-1, 1)]
+    for t in leaves:
+        t.requires_grad_(True)
+    dout = r(B, H, N, 64).bfloat16()
+    offs = torch.tensor(offsets, dtype=torch.int32, device="cuda")
+    e = torch.empty(0, dtype=torch.int32, device="cuda")
+
+    def step():
+        for t in leaves:
+            t.grad = None
+        out = dsqg_attention_v18_grouped(*leaves, J, js, J - js, offs, e, e, e, e, e, 3, 0, False, 0, 0, 0)
+        out.backward(dout)
+
+    times = timer(step, ("dwarf_dsqg_fwd", "dwarf_dsqg_bwd"))
+    q = leaves[0]
+    # per (b,h,t) row: q, k, v, O, dO read, dq, dk, dv written (bf16 in, fp32 gradients out)
+    row_bytes = 5 * 128 + 3 * 256
+    return {"kernels": times, "offsets": J,
+            "dwarf_dsqg_bwd": _rate(row_bytes * B * H * N, times["dwarf_dsqg_bwd"], peak)}
+
+
+def _hisa_inputs(seed: int):
+    g = torch.Generator().manual_seed(seed)
+    B, H, T = 32, 8, 2048
+    return [(torch.randn(B, H, T, 64, generator=g) * 0.125).to(torch.bfloat16).cuda() for _ in range(3)]
+
+
+def case_hisa_config4(timer, peak):
+    """Config 4: HISA router + fused tile attention, B=32 H=8 T=2048, local = global K/V."""
+    from .hierarchical_sparse_attn_v18_hisa import hisa_attention
+
+    q, k, v = _hisa_inputs(6)
+    scale = torch.full((8,), 0.1)
+    res = {}
+    names = ("dwarf_hisa_reps", "dwarf_hisa_select", "dwarf_hisa_route", "dwarf_hisa_attn")
+    times = timer(lambda: res.__setitem__("r", hisa_attention(q, k, v, k, v, scale, want_route=True)), names)
+    out, top, route = res["r"]
+    ms = times["dwarf_hisa_attn"]
+    B, H, T = q.shape[:3]
+    tiles = -(-T // 16)
+    keys = 80 + 4 * 64  # the tile's local window rows and four routed chunks
+    flops = tiles * B * H * 16 * keys * 64 * 4
+    return {"kernels": times, "dwarf_hisa_attn": {**_rate(_nbytes(q, k, v, out, route, top), ms, peak),
+                                                  "dense_tile_tflops": round(flops / (ms * 1e-3) / 1e12, 1)}}
+
+
+def case_hisa_bwd_config4(timer, peak):
+    """HISA fused tile attention backward at the config-4 shape (distinct local and global
+    K/V, route prior requiring grad)."""
+    from .hierarchical_sparse_attn_v18_hisa import chunk_representatives, hisa_tile_attention, route_prior
+    from .hierarchical_sparse_attn_v18_hisa import select_chunks
+
+    q, lk, lv = _hisa_inputs(7)
+    _, gk, gv = _hisa_inputs(8)
+    B, H, T = q.shape[:3]
+    lengths = torch.full((B,), T, dtype=torch.int32, device="cuda")
+    reps = chunk_representatives(gk, lengths, blend_alpha=0.5)
+    top, _ = select_chunks(q, reps, lengths, top_k=4, temperature=1.0)
+    route = route_prior(q, reps, top, torch.full((H,), 0.1, device="cuda")).float()
+    leaves = [t.clone().requires_grad_(True) for t in (q, lk, lv, gk, gv, route)]
+    dout = torch.randn(B, H, T, 64, device="cuda").to(torch.bfloat16)
+
+    def step():
+        for t in leaves:
+            t.grad = None
+        out = hisa_tile_attention(*leaves, top)
+        out.backward(dout)
+
+    times = timer(step, ("dwarf_hisa_attn", "dwarf_hisa_attn_bwd"))
+    # reads q, O, dO and each key row touched (k, v of the local window and routed chunks:
+    # counted once per tensor), writes dq and the four K/V gradients in fp32 and d route
+    nbytes = 7 * _nbytes(q) + 5 * 2 * _nbytes(q) + B * H * T * 4 * 4
+    return {"kernels": times, "dwarf_hisa_attn_bwd": _rate(nbytes, times["dwarf_hisa_attn_bwd"], peak)}
+
+
+CASES = {
+    "ema_config2": case_ema_config2,
+    "ema_model_bf16": case_ema_model_bf16,
+    "ema_bwd_config2": case_ema_bwd_config2,
+    "q6_pack_config3": case_q6_pack_config3,
+    "dsqg_q6_config3": case_dsqg_q6_config3,
+    "dsqg_bwd_model_group": case_dsqg_bwd_model_group,
+    "hisa_config4": case_hisa_config4,
+    "hisa_bwd_config4": case_hisa_bwd_config4,
+}
+
+
+def main(argv=None) -> None:
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--case", action="append", choices=sorted(CASES), help="cases to run (default: all)")
+    ap.add_argument("--iters", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    args = ap.parse_args(argv)
+    if not torch.cuda.is_available():
+        raise SystemExit("kernel_bench needs a CUDA device")
+    peak, peak_kind = _hbm_peak()
+    timer = _Timer(args.warmup, args.iters)
+    for name in args.case or list(CASES):
+        result = CASES[name](timer, peak)
+        print(json.dumps({"case": name, **result, "hbm_peak_gbs": peak, "peak": peak_kind}), flush=True)
+        torch.cuda.empty_cache()
+
+
+if __name__ == "__main__":
+    main()
