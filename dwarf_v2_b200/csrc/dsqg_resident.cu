@@ -49,7 +49,7 @@ using namespace dsqg;
 using namespace wmma16;
 
 constexpr int kRQB = 256;  // queries per round == key rows per chunk
-constexpr int kRMaxJ = 32;
+constexpr int kRMaxJ = 96;  // the canonical lattice; the shared-memory layout check bounds the rest
 constexpr int kRSmemLimit = 232448;  // 227 KB opt-in shared memory per CTA
 constexpr float kRescaleLog2 = 8.0f;
 constexpr float kVPreScale = 1.2676506002282294e30f;  // 2^100
