@@ -192,7 +192,8 @@ class DsqgBwdArgs(ctypes.Structure):
 class HisaAttnBwdArgs(ctypes.Structure):
     _fields_ = _fields("""version:i32, k_slots:i32, B:i64, H:i64, T:i64, query:ptr, local_key:ptr, local_value:ptr,
         global_key:ptr, global_value:ptr, top_chunk_idx:ptr, route:ptr, lengths:ptr, out:ptr, dout:ptr,
-        dq:ptr, d_local_key:ptr, d_local_value:ptr, d_global_key:ptr, d_global_value:ptr, d_route:ptr""")
+        dq:ptr, d_local_key:ptr, d_local_value:ptr, d_global_key:ptr, d_global_value:ptr, d_route:ptr,
+        lse:ptr, delta:ptr""")
 
 
 class DsqgPrepArgs(ctypes.Structure):

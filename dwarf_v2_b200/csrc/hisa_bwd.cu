@@ -2,239 +2,429 @@
 // gradients of the reference's local lane + global lane + exact LSE merge
 // (kernels/hierarchical_sparse_attn_v18_hisa.py:688-835, 1103-1246, 1982-2027).
 //
-// One CTA of 256 threads per (b, h, 16-query selector tile). The tile's key
-// set is dense: the local window rows [t0 - 64, t0 + 15) of (local_key,
-// local_value) and the 64 rows of each routed chunk of (global_key,
-// global_value). Keys go through shared memory in blocks of 32 (fp32, rows
-// padded to 65 floats so the per-key dot products are bank-conflict-free):
-// pass 1 recomputes each query's lse (online max / sum), pass 2 forms P, dP,
-// dS and accumulates dq in registers, d_route per slot, and the block's dK/dV
-// rows, which are added to the fp32 gradient buffers with float4 atomics.
+// With P the joint softmax of a query over its local window (keys n-64..n-1 of
+// local K/V) and its tile's routed chunks (keys of global K/V with id < n-64,
+// score + the slot's route prior), dP = dO . v, delta = dO . O, dS = P (dP - delta):
+//   dq = (1/8) sum dS k,  dk = (1/8) sum dS q,  dv = sum P dO,
+//   d_route[n, slot] = sum of dS over the slot's chunk.
+// All products run on bf16 tensor cores (mma.sync m16n8k16, fp32 accumulate),
+// the structure of a FlashAttention-2 backward:
+//  1. query side, one warp per 16-query selector tile (4 per CTA): pass 1 builds
+//     the row lse over the tile's key blocks of 16, pass 2 forms P, dP, dS and
+//     accumulates dq (dS in bf16 times K) and d_route; it also stores each row's
+//     lse (log2 domain) and delta for step 2;
+//  2. key side, one CTA per 64 key rows (4 warps x 16 keys), separately for the
+//     local K/V (query tiles of the rows' windows) and the global K/V (the tiles
+//     that routed the chunk, found by scanning top_chunk_idx): S^T = K Q^T from
+//     the stored lse gives P^T and dS^T, then dV = P^T dO and dK = dS^T Q.
+// Every gradient row has one writer: no atomics, no zero-fill, and repeated
+// runs are bit-identical.
 #include "common.cuh"
+#include "warp_mma.cuh"
 
 namespace dwarf {
 namespace {
+using namespace wmma16;
 
-constexpr int kHT = 256;       // threads
-constexpr int kHQ = 16;        // queries per tile
-constexpr int kHKB = 32;       // keys per block
-constexpr int kHChunk = 64;
-constexpr int kHWindow = 64;
-constexpr int kHLd = 65;       // padded row length (floats)
-constexpr int kHMaxBlocks = 3 + 2 * 4;
-constexpr float kHScale = 0.125f;
+constexpr int kBT = 16;        // queries per selector tile
+constexpr int kBChunk = 64;    // chunk rows == key rows per key-side CTA
+constexpr int kBWindow = 64;
+constexpr int kBSlots = 4;
+constexpr int kBWarps = 4;
+constexpr float kBScale = 0.125f;
+constexpr float kBLog2e = 1.4426950408889634f;
 
-struct KeyBlock {
-  int64_t row0;
-  int rows;
-  int slot;  // -1: local window block, else the routed slot
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+__device__ __forceinline__ float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+
+// A fragments (m16n8k16, row-major 16 x 64) of rows r0..r0+15 of a contiguous
+// [T][64] bf16 matrix; rows outside [0, T) read row 0 (their products are masked).
+__device__ __forceinline__ void load_a(const __nv_bfloat16* m, int64_t r0, int64_t T, int lane, uint32_t (&a)[4][4]) {
+  const int g = lane >> 2, t4 = lane & 3;
+  int64_t ra = r0 + g, rb = r0 + g + 8;
+  ra = (ra >= 0 && ra < T) ? ra : 0;
+  rb = (rb >= 0 && rb < T) ? rb : 0;
+#pragma unroll
+  for (int kt = 0; kt < 4; ++kt) {
+    const int c0 = kt * 16 + 2 * t4;
+    a[kt][0] = *reinterpret_cast<const uint32_t*>(m + ra * 64 + c0);
+    a[kt][1] = *reinterpret_cast<const uint32_t*>(m + rb * 64 + c0);
+    a[kt][2] = *reinterpret_cast<const uint32_t*>(m + ra * 64 + c0 + 8);
+    a[kt][3] = *reinterpret_cast<const uint32_t*>(m + rb * 64 + c0 + 8);
+  }
+}
+
+// 16 rows r0.. of a contiguous [T][64] bf16 matrix -> swizzled smem tile (zero
+// rows outside [0, T)); called by the 32 lanes of one warp or by `nthreads` threads.
+__device__ __forceinline__ void stage16(uint32_t tile, const __nv_bfloat16* m, int64_t r0, int64_t T, int tid,
+                                        int nthreads) {
+  for (int i = tid; i < 16 * 8; i += nthreads) {
+    const int r = i >> 3, c = i & 7;
+    const int64_t row = r0 + r;
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (row >= 0 && row < T) v = *reinterpret_cast<const uint4*>(m + row * 64 + c * 8);
+    asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(tile_addr(tile, r, c)), "r"(v.x), "r"(v.y), "r"(v.z),
+                 "r"(v.w) : "memory");
+  }
+}
+
+// C[16 x 16] = A[16 x 64] . M^T for the 16-row smem tile M (rows = the n index).
+__device__ __forceinline__ void mma_abt(const uint32_t (&a)[4][4], uint32_t tile, int lane, float (&c)[2][4]) {
+#pragma unroll
+  for (int j = 0; j < 2; ++j) c[j][0] = c[j][1] = c[j][2] = c[j][3] = 0.0f;
+  const int mtx = lane >> 3, r = lane & 7;
+#pragma unroll
+  for (int kt = 0; kt < 4; ++kt) {
+    uint32_t b0, b1, b2, b3;
+    ldsm_x4(tile_addr(tile, (mtx >> 1) * 8 + r, kt * 2 + (mtx & 1)), b0, b1, b2, b3);
+    mma_bf16(c[0], a[kt], b0, b1);
+    mma_bf16(c[1], a[kt], b2, b3);
+  }
+}
+
+// acc[16 x 64] += P[16 x 16] . M for the 16-row smem tile M (rows = the k index);
+// P comes as the bf16 A fragment built from a 16 x 16 accumulator pair.
+__device__ __forceinline__ void mma_pm(const uint32_t (&pa)[4], uint32_t tile, int lane, float (&acc)[8][4]) {
+  const int mtx = lane >> 3, r = lane & 7;
+#pragma unroll
+  for (int n = 0; n < 8; n += 2) {
+    uint32_t b0, b1, b2, b3;
+    ldsm_x4_t(tile_addr(tile, (mtx & 1) * 8 + r, n + (mtx >> 1)), b0, b1, b2, b3);
+    mma_bf16(acc[n], pa, b0, b1);
+    mma_bf16(acc[n + 1], pa, b2, b3);
+  }
+}
+
+__device__ __forceinline__ void a_from_acc(const float (&c)[2][4], uint32_t (&pa)[4]) {
+  pa[0] = pack2(c[0][0], c[0][1]);
+  pa[1] = pack2(c[0][2], c[0][3]);
+  pa[2] = pack2(c[1][0], c[1][1]);
+  pa[3] = pack2(c[1][2], c[1][3]);
+}
+
+struct BwdParams {
+  const __nv_bfloat16 *q, *lk, *lv, *gk, *gv, *out, *dout, *route;
+  const int32_t *top, *lengths;
+  float *dq, *dlk, *dlv, *dgk, *dgv, *droute, *lse, *delta;
+  int64_t H, T, tiles;
+  int k_slots;
 };
 
-__device__ __forceinline__ float half_warp_sum(float x) {
-#pragma unroll
-  for (int o = 8; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
-  return x;
-}
-__device__ __forceinline__ float half_warp_max(float x) {
-#pragma unroll
-  for (int o = 8; o > 0; o >>= 1) x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, o));
-  return x;
-}
-
-// `rows` x 64 bf16 rows of src (row stride 64) -> fp32 dst[CAP][kHLd]; zero past `rows`.
-template <int CAP>
-__device__ __forceinline__ void stage_rows(float (*dst)[kHLd], const __nv_bfloat16* src, int rows, int tid) {
-  for (int i = tid; i < CAP * 16; i += kHT) {
-    const int r = i >> 4, c = (i & 15) * 4;
-    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (r < rows) {
-      const uint2 w = *reinterpret_cast<const uint2*>(src + (int64_t)r * 64 + c);
-      v = make_float4(__uint_as_float(w.x << 16), __uint_as_float(w.x & 0xffff0000u),
-                      __uint_as_float(w.y << 16), __uint_as_float(w.y & 0xffff0000u));
-    }
-    dst[r][c] = v.x; dst[r][c + 1] = v.y; dst[r][c + 2] = v.z; dst[r][c + 3] = v.w;
-  }
-}
-
-__global__ void __launch_bounds__(kHT) hisa_attn_bwd_kernel(const dwarf_hisa_attn_bwd_args a) {
-  __shared__ float sQ[kHQ][kHLd], sdO[kHQ][kHLd];
-  __shared__ float sK[kHKB][kHLd], sV[kHKB][kHLd];
-  __shared__ float sP[kHQ][kHKB + 1], sdS[kHQ][kHKB + 1];
-  __shared__ float s_delta[kHQ], s_route[kHQ][4], s_droute[kHQ][4];
-  __shared__ KeyBlock s_blk[kHMaxBlocks];
-  __shared__ int s_nblk;
-
-  const int tid = threadIdx.x;
-  const int64_t t = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  const int64_t T = a.T;
-  const int64_t n0 = t * kHQ;
-  const int64_t len = a.lengths[b] < T ? a.lengths[b] : T;
-  const int64_t bh = (b * a.H + h) * T;
-  const __nv_bfloat16* Q = static_cast<const __nv_bfloat16*>(a.query) + bh * 64;
-  const __nv_bfloat16* LK = static_cast<const __nv_bfloat16*>(a.local_key) + bh * 64;
-  const __nv_bfloat16* LV = static_cast<const __nv_bfloat16*>(a.local_value) + bh * 64;
-  const __nv_bfloat16* GK = static_cast<const __nv_bfloat16*>(a.global_key) + bh * 64;
-  const __nv_bfloat16* GV = static_cast<const __nv_bfloat16*>(a.global_value) + bh * 64;
-  const int nq = (int)(T - n0 < kHQ ? T - n0 : kHQ);
-
-  // ---- tile inputs: Q, dO (fp32), delta = dO . O, route, block list
-  stage_rows<kHQ>(sQ, Q + n0 * 64, nq, tid);
-  __syncthreads();
+// ---------------------------------------------------------------- 1. query side
+// Key block kb of a tile: kb < 5 local blocks of 16 rows from t0 - 64, then
+// 4 blocks per routed slot.
+__global__ void __launch_bounds__(kBWarps * 32) hisa_bwd_query_kernel(const BwdParams p) {
+  __shared__ __align__(128) unsigned char s_kv[kBWarps][2][16 * 128];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t4 = lane & 3;
+  const int64_t h = blockIdx.y, b = blockIdx.z;
+  const int64_t t = (int64_t)blockIdx.x * kBWarps + warp;
+  if (t >= p.tiles) return;  // warp-uniform; no CTA-wide barrier below
+  const int64_t T = p.T, t0 = t * kBT;
+  const int64_t len = p.lengths[b] < T ? p.lengths[b] : T;
+  const int64_t bh = (b * p.H + h) * T;
+  const uint32_t ktile = smem_u32(s_kv[warp][0]), vtile = smem_u32(s_kv[warp][1]);
+  int slot_chunk[kBSlots];
   {
-    const int qi = tid >> 4, d4 = (tid & 15) * 4;
-    const int64_t n = n0 + qi;
-    float dsum = 0.f;
-    float o[4] = {0.f, 0.f, 0.f, 0.f}, g[4] = {0.f, 0.f, 0.f, 0.f};
-    if (qi < nq) {
-      const uint2 wo = *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(a.out) + (bh + n) * 64 + d4);
-      const uint2 wg = *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(a.dout) + (bh + n) * 64 + d4);
-      o[0] = __uint_as_float(wo.x << 16); o[1] = __uint_as_float(wo.x & 0xffff0000u);
-      o[2] = __uint_as_float(wo.y << 16); o[3] = __uint_as_float(wo.y & 0xffff0000u);
-      g[0] = __uint_as_float(wg.x << 16); g[1] = __uint_as_float(wg.x & 0xffff0000u);
-      g[2] = __uint_as_float(wg.y << 16); g[3] = __uint_as_float(wg.y & 0xffff0000u);
-    }
+    const int32_t* top = p.top + ((b * p.H + h) * p.tiles + t) * p.k_slots;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      dsum = fmaf(g[i], o[i], dsum);
-      sdO[qi][d4 + i] = g[i];
-    }
-    dsum = half_warp_sum(dsum);
-    if ((tid & 15) == 0) s_delta[qi] = dsum;
-    if (tid < kHQ * 4) {
-      const int q = tid >> 2, k = tid & 3;
-      float r = 0.f;
-      if (q < nq && k < a.k_slots)
-        r = __bfloat162float(static_cast<const __nv_bfloat16*>(a.route)[(bh + n0 + q) * 4 + k]);
-      s_route[q][k] = r;
-      s_droute[q][k] = 0.f;
-    }
-    if (tid == 0) {
-      int nb = 0;
-      const int64_t lo = n0 - kHWindow > 0 ? n0 - kHWindow : 0;
-      const int64_t hi = n0 + nq - 1;  // exclusive: the last query's last local key is hi - 1
-      for (int64_t r = lo; r < hi; r += kHKB) s_blk[nb++] = KeyBlock{r, (int)(hi - r < kHKB ? hi - r : kHKB), -1};
-      const int32_t* top = a.top_chunk_idx + ((b * a.H + h) * ((T + kHQ - 1) / kHQ) + t) * a.k_slots;
-      for (int k = 0; k < a.k_slots; ++k) {
-        const int c = top[k];
-        if (c < 0) continue;
-        for (int64_t r = (int64_t)c * kHChunk; r < (int64_t)(c + 1) * kHChunk && r < T; r += kHKB) {
-          const int64_t end = (int64_t)(c + 1) * kHChunk < T ? (int64_t)(c + 1) * kHChunk : T;
-          s_blk[nb++] = KeyBlock{r, (int)(end - r < kHKB ? end - r : kHKB), k};
-        }
+    for (int s = 0; s < kBSlots; ++s) slot_chunk[s] = s < p.k_slots ? top[s] : -1;
+  }
+  uint32_t qa[4][4], ga[4][4];
+  load_a(p.q + bh * 64, t0, T, lane, qa);
+  load_a(p.dout + bh * 64, t0, T, lane, ga);
+  // delta = dO . O per row (rows g and g + 8 of the tile), fp32 of the bf16 values
+  float delta[2], route[2][kBSlots];
+  {
+    uint32_t oa[4][4];
+    load_a(p.out + bh * 64, t0, T, lane, oa);
+    delta[0] = delta[1] = 0.0f;
+#pragma unroll
+    for (int kt = 0; kt < 4; ++kt)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float d = bf_lo(ga[kt][i]) * bf_lo(oa[kt][i]) + bf_hi(ga[kt][i]) * bf_hi(oa[kt][i]);
+        delta[i & 1] += d;
       }
-      s_nblk = nb;
+#pragma unroll
+    for (int rr = 0; rr < 2; ++rr) {
+      delta[rr] += __shfl_xor_sync(0xffffffffu, delta[rr], 1);
+      delta[rr] += __shfl_xor_sync(0xffffffffu, delta[rr], 2);
+      const int64_t n = t0 + g + 8 * rr;
+#pragma unroll
+      for (int s = 0; s < kBSlots; ++s)
+        route[rr][s] = (n < T && s < p.k_slots) ? __bfloat162float(p.route[(bh + n) * kBSlots + s]) : 0.0f;
     }
   }
-  __syncthreads();
-
-  // Score thread layout: query qi = tid / 16 (a half warp per query), keys kk, kk + 1.
-  const int qi = tid >> 4, kk = (tid & 15) * 2;
-  const int64_t n = n0 + qi;
-  const bool qvalid = qi < nq && n < len;
-  auto score = [&](const KeyBlock& blk, int e, float& s, bool& ok) {
-    const int k = kk + e;
-    const int64_t r = blk.row0 + k;
-    float acc = 0.f;
-#pragma unroll 16
-    for (int d = 0; d < 64; ++d) acc = fmaf(sQ[qi][d], sK[k][d], acc);
-    if (blk.slot < 0) ok = qvalid && k < blk.rows && r < n && r >= n - kHWindow;
-    else ok = qvalid && k < blk.rows && r < n - kHWindow && r < len;
-    s = blk.slot < 0 ? acc * kHScale : fmaf(acc, kHScale, s_route[qi][blk.slot]);
+  const int n_blocks = 5 + 4 * kBSlots;
+  // key block -> (first row, slot or -1); false when the block does not exist
+  auto block = [&](int kb, int64_t& r0, int& slot) -> bool {
+    if (kb < 5) {
+      r0 = t0 - kBWindow + 16 * kb;
+      slot = -1;
+      return r0 + 16 > 0 && r0 < T;
+    }
+    slot = (kb - 5) >> 2;
+    int c = -1;
+#pragma unroll
+    for (int q = 0; q < kBSlots; ++q) c = q == slot ? slot_chunk[q] : c;
+    r0 = (int64_t)c * kBChunk + 16 * ((kb - 5) & 3);
+    return c >= 0 && r0 < T;
+  };
+  // log2-domain scores of the block for rows g, g + 8 (-inf where masked)
+  auto scores = [&](float (&s)[2][4], int64_t r0, int slot) {
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int rr = e >> 1;
+        const int64_t n = t0 + g + 8 * rr, k = r0 + j * 8 + 2 * t4 + (e & 1);
+        const bool ok = n < len && k >= 0 && (slot < 0 ? (k < n && k >= n - kBWindow) : (k < n - kBWindow && k < len));
+        float bias = 0.0f;
+#pragma unroll
+        for (int q = 0; q < kBSlots; ++q) bias = q == slot ? route[rr][q] : bias;  // register select
+        s[j][e] = ok ? (s[j][e] * kBScale + bias) * kBLog2e : -INFINITY;
+      }
   };
 
-  // ---- pass 1: lse per query
-  float m = -INFINITY, l = 0.f;
-  const int nblk = s_nblk;
-  for (int bi = 0; bi < nblk; ++bi) {
-    const KeyBlock blk = s_blk[bi];
-    __syncthreads();
-    stage_rows<kHKB>(sK, (blk.slot < 0 ? LK : GK) + blk.row0 * 64, blk.rows, tid);
-    __syncthreads();
-    float s0, s1;
-    bool ok0, ok1;
-    score(blk, 0, s0, ok0);
-    score(blk, 1, s1, ok1);
-    float bm = fmaxf(ok0 ? s0 : -INFINITY, ok1 ? s1 : -INFINITY);
-    bm = half_warp_max(bm);
-    // nm is uniform over a half warp only: every shuffle stays outside the
-    // branch so that both halves of the warp take part.
-    const float nm = fmaxf(m, bm);
-    float add = (ok0 ? __expf(s0 - nm) : 0.f) + (ok1 ? __expf(s1 - nm) : 0.f);
-    add = half_warp_sum(add);
-    if (nm > -INFINITY) {
-      l = (m > -INFINITY ? l * __expf(m - nm) : 0.f) + add;
-      m = nm;
+  // ---- pass 1: row max and sum (log2 domain)
+  float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.0f, 0.0f};
+  for (int kb = 0; kb < n_blocks; ++kb) {
+    int64_t r0;
+    int slot;
+    if (!block(kb, r0, slot)) continue;  // warp-uniform
+    const __nv_bfloat16* kbase = (slot < 0 ? p.lk : p.gk) + bh * 64;
+    __syncwarp();
+    stage16(ktile, kbase, r0, T, lane, 32);
+    __syncwarp();
+    float s[2][4];
+    mma_abt(qa, ktile, lane, s);
+    scores(s, r0, slot);
+#pragma unroll
+    for (int rr = 0; rr < 2; ++rr) {
+      float mx = fmaxf(fmaxf(s[0][2 * rr], s[0][2 * rr + 1]), fmaxf(s[1][2 * rr], s[1][2 * rr + 1]));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      const float mn = fmaxf(m[rr], mx);
+      const float ms = mn == -INFINITY ? 0.0f : mn;
+      float add = ex2_approx(s[0][2 * rr] - ms) + ex2_approx(s[0][2 * rr + 1] - ms) + ex2_approx(s[1][2 * rr] - ms) +
+                  ex2_approx(s[1][2 * rr + 1] - ms);
+      add += __shfl_xor_sync(0xffffffffu, add, 1);
+      add += __shfl_xor_sync(0xffffffffu, add, 2);
+      l[rr] = l[rr] * ex2_approx(m[rr] - ms) + add;
+      m[rr] = mn;
     }
   }
-  const float lse = l > 0.f ? m + __logf(l) : INFINITY;  // +inf: no keys, P = 0
-  const float delta = s_delta[qi];
+  float lse[2];
+#pragma unroll
+  for (int rr = 0; rr < 2; ++rr) lse[rr] = l[rr] > 0.0f ? m[rr] + __log2f(l[rr]) : INFINITY;
 
-  // ---- pass 2: gradients
-  float dq[4] = {0.f, 0.f, 0.f, 0.f};
-  const int dq_q = tid >> 4, dq_d = (tid & 15) * 4;      // dq ownership (same query as the score thread)
-  const int kv_k = tid >> 3, kv_d = (tid & 7) * 8;       // dK / dV ownership
-  for (int bi = 0; bi < nblk; ++bi) {
-    const KeyBlock blk = s_blk[bi];
-    __syncthreads();
-    stage_rows<kHKB>(sK, (blk.slot < 0 ? LK : GK) + blk.row0 * 64, blk.rows, tid);
-    stage_rows<kHKB>(sV, (blk.slot < 0 ? LV : GV) + blk.row0 * 64, blk.rows, tid);
-    __syncthreads();
-    float rsum = 0.f;
+  // ---- pass 2: P, dP, dS; dq and d_route
+  float dq[8][4];
 #pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      float s;
-      bool ok;
-      score(blk, e, s, ok);
-      const float p = ok ? __expf(s - lse) : 0.f;
-      float dp = 0.f;
-#pragma unroll 16
-      for (int d = 0; d < 64; ++d) dp = fmaf(sdO[qi][d], sV[kk + e][d], dp);
-      const float ds = p * (dp - delta);
-      sP[qi][kk + e] = p;
-      sdS[qi][kk + e] = ds;
-      rsum += ds;
-    }
-    if (blk.slot >= 0) {
-      rsum = half_warp_sum(rsum);
-      if ((tid & 15) == 0) s_droute[qi][blk.slot] += rsum;
-    }
-    __syncthreads();
-#pragma unroll 8
-    for (int k = 0; k < kHKB; ++k) {
-      const float ds = sdS[dq_q][k];
+  for (int n = 0; n < 8; ++n) dq[n][0] = dq[n][1] = dq[n][2] = dq[n][3] = 0.0f;
+  float droute[2][kBSlots];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) dq[i] = fmaf(ds, sK[k][dq_d + i], dq[i]);
-    }
-    if (kv_k < blk.rows) {
-      float dk[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f}, dv[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      bool any = false;
+  for (int rr = 0; rr < 2; ++rr)
 #pragma unroll
-      for (int q = 0; q < kHQ; ++q) {
-        const float ds = sdS[q][kv_k], p = sP[q][kv_k];
-        any |= p != 0.f;
+    for (int s = 0; s < kBSlots; ++s) droute[rr][s] = 0.0f;
+  for (int kb = 0; kb < n_blocks; ++kb) {
+    int64_t r0;
+    int slot;
+    if (!block(kb, r0, slot)) continue;
+    const int64_t off = bh * 64;
+    __syncwarp();
+    stage16(ktile, (slot < 0 ? p.lk : p.gk) + off, r0, T, lane, 32);
+    stage16(vtile, (slot < 0 ? p.lv : p.gv) + off, r0, T, lane, 32);
+    __syncwarp();
+    float s[2][4], dp[2][4];
+    mma_abt(qa, ktile, lane, s);
+    scores(s, r0, slot);
+    mma_abt(ga, vtile, lane, dp);
+    float rsum[2] = {0.0f, 0.0f};
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          dk[i] = fmaf(ds, sQ[q][kv_d + i], dk[i]);
-          dv[i] = fmaf(p, sdO[q][kv_d + i], dv[i]);
-        }
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int rr = e >> 1;
+        const float pr = ex2_approx(s[j][e] - lse[rr]);
+        const float ds = pr * (dp[j][e] - delta[rr]);
+        s[j][e] = ds;
+        rsum[rr] += ds;
       }
-      if (any) {
-        const int64_t row = bh + blk.row0 + kv_k;
-        float* gk = (blk.slot < 0 ? a.d_local_key : a.d_global_key) + row * 64 + kv_d;
-        float* gv = (blk.slot < 0 ? a.d_local_value : a.d_global_value) + row * 64 + kv_d;
-        atomicAdd(reinterpret_cast<float4*>(gk), make_float4(dk[0] * kHScale, dk[1] * kHScale, dk[2] * kHScale, dk[3] * kHScale));
-        atomicAdd(reinterpret_cast<float4*>(gk + 4), make_float4(dk[4] * kHScale, dk[5] * kHScale, dk[6] * kHScale, dk[7] * kHScale));
-        atomicAdd(reinterpret_cast<float4*>(gv), make_float4(dv[0], dv[1], dv[2], dv[3]));
-        atomicAdd(reinterpret_cast<float4*>(gv + 4), make_float4(dv[4], dv[5], dv[6], dv[7]));
+    uint32_t pa[4];
+    a_from_acc(s, pa);
+    mma_pm(pa, ktile, lane, dq);
+#pragma unroll
+    for (int q = 0; q < kBSlots; ++q)
+#pragma unroll
+      for (int rr = 0; rr < 2; ++rr) droute[rr][q] += q == slot ? rsum[rr] : 0.0f;
+  }
+  // ---- stores: dq, d_route (rows g, g + 8), lse and delta for the key side
+#pragma unroll
+  for (int rr = 0; rr < 2; ++rr) {
+    const int64_t n = t0 + g + 8 * rr;
+#pragma unroll
+    for (int s = 0; s < kBSlots; ++s) {
+      droute[rr][s] += __shfl_xor_sync(0xffffffffu, droute[rr][s], 1);
+      droute[rr][s] += __shfl_xor_sync(0xffffffffu, droute[rr][s], 2);
+    }
+    if (n < T) {
+#pragma unroll
+      for (int nn = 0; nn < 8; ++nn)
+        *reinterpret_cast<float2*>(p.dq + (bh + n) * 64 + nn * 8 + 2 * t4) =
+            make_float2(dq[nn][2 * rr] * kBScale, dq[nn][2 * rr + 1] * kBScale);
+      if (t4 == 0) {
+        *reinterpret_cast<float4*>(p.droute + (bh + n) * kBSlots) =
+            make_float4(droute[rr][0], droute[rr][1], droute[rr][2], droute[rr][3]);
+        p.lse[bh + n] = lse[rr];
+        p.delta[bh + n] = delta[rr];
       }
     }
   }
-  __syncthreads();
-  if (dq_q < nq) {
-    *reinterpret_cast<float4*>(a.dq + (bh + n0 + dq_q) * 64 + dq_d) =
-        make_float4(dq[0] * kHScale, dq[1] * kHScale, dq[2] * kHScale, dq[3] * kHScale);
+}
+
+// ---------------------------------------------------------------- 2. key side
+// CTA = 64 key rows [k0, k0 + 64) of one (b, h); warp w owns rows k0 + 16 w ...
+// GLOBAL = false: local K/V, query tiles whose windows reach the rows;
+// GLOBAL = true: global K/V rows of chunk k0 / 64, query tiles that routed it.
+constexpr int kBMaxTiles = 512;  // T <= 8192 (128 chunks): at most 512 selector tiles
+
+template <bool GLOBAL>
+__global__ void __launch_bounds__(kBWarps * 32) hisa_bwd_key_kernel(const BwdParams p) {
+  __shared__ __align__(128) unsigned char s_tile[2][16 * 128];  // the query tile's Q and dO
+  __shared__ float s_lse[16], s_delta[16], s_bias[16];
+  __shared__ int16_t s_list[kBMaxTiles];
+  __shared__ int8_t s_slot[kBMaxTiles];
+  __shared__ int s_count;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, t4 = lane & 3;
+  const int64_t h = blockIdx.y, b = blockIdx.z;
+  const int64_t T = p.T, k0 = (int64_t)blockIdx.x * kBChunk;
+  const int64_t len = p.lengths[b] < T ? p.lengths[b] : T;
+  const int64_t bh = (b * p.H + h) * T;
+  const uint32_t qtile = smem_u32(s_tile[0]), gtile = smem_u32(s_tile[1]);
+
+  // ---- the query tiles that see these rows
+  if (GLOBAL) {
+    if (tid == 0) s_count = 0;
+    __syncthreads();
+    const int c = (int)blockIdx.x;
+    const int32_t* top = p.top + (b * p.H + h) * p.tiles * p.k_slots;
+    // tiles in ascending order: each warp takes 32 consecutive tiles per pass
+    for (int64_t base = 0; base < p.tiles; base += kBWarps * 32) {
+      const int64_t t = base + tid;
+      int slot = -1;
+      if (t < p.tiles)
+        for (int q = 0; q < p.k_slots; ++q) slot = top[t * p.k_slots + q] == c ? q : slot;
+      // a chunk is routed at most once per tile; tiles starting before the
+      // chunk's end + 64 have no query that may use it (ids < n - 64)
+      const bool hit = slot >= 0 && t * kBT + kBT - 1 - kBWindow > k0;
+      const unsigned mask = __ballot_sync(0xffffffffu, hit);
+      __shared__ int s_warp_n[kBWarps];
+      if (lane == 0) s_warp_n[warp] = __popc(mask);
+      __syncthreads();
+      int before = s_count;
+      for (int w = 0; w < warp; ++w) before += s_warp_n[w];
+      if (hit) {
+        const int at = before + __popc(mask & ((1u << lane) - 1u));
+        s_list[at] = (int16_t)t;
+        s_slot[at] = (int8_t)slot;
+      }
+      __syncthreads();
+      if (tid == 0) for (int w = 0; w < kBWarps; ++w) s_count += s_warp_n[w];
+      __syncthreads();
+    }
+  } else {
+    // queries n in [k0 + 1, k0 + 64 + 63] see some row of [k0, k0 + 64)
+    if (tid == 0) {
+      const int64_t t_first = (k0 + 1) / kBT;
+      int64_t t_last = (k0 + kBChunk - 1 + kBWindow) / kBT;
+      if (t_last > p.tiles - 1) t_last = p.tiles - 1;
+      int n = 0;
+      for (int64_t t = t_first; t <= t_last; ++t) {
+        s_list[n] = (int16_t)t;
+        s_slot[n] = -1;
+        ++n;
+      }
+      s_count = n;
+    }
+    __syncthreads();
   }
-  if (tid < kHQ * 4 && (tid >> 2) < nq) a.d_route[(bh + n0) * 4 + tid] = s_droute[tid >> 2][tid & 3];
+  const int n_tiles = s_count;
+
+  // ---- this warp's 16 key rows as A fragments (K and V)
+  const int64_t r0 = k0 + 16 * warp;
+  const __nv_bfloat16* kmat = (GLOBAL ? p.gk : p.lk) + bh * 64;
+  const __nv_bfloat16* vmat = (GLOBAL ? p.gv : p.lv) + bh * 64;
+  uint32_t ka[4][4], va[4][4];
+  load_a(kmat, r0, T, lane, ka);
+  load_a(vmat, r0, T, lane, va);
+  float dk[8][4], dv[8][4];
+#pragma unroll
+  for (int n = 0; n < 8; ++n) dk[n][0] = dk[n][1] = dk[n][2] = dk[n][3] = dv[n][0] = dv[n][1] = dv[n][2] = dv[n][3] = 0.0f;
+
+  for (int i = 0; i < n_tiles; ++i) {
+    const int64_t t0 = (int64_t)s_list[i] * kBT;
+    const int slot = s_slot[i];
+    __syncthreads();  // the previous tile's smem is no longer read
+    stage16(qtile, p.q + bh * 64, t0, T, tid, kBWarps * 32);
+    stage16(gtile, p.dout + bh * 64, t0, T, tid, kBWarps * 32);
+    if (tid < 16) {
+      const int64_t n = t0 + tid;
+      const bool ok = n < T;
+      s_lse[tid] = ok ? p.lse[bh + n] : INFINITY;
+      s_delta[tid] = ok ? p.delta[bh + n] : 0.0f;
+      s_bias[tid] = (ok && slot >= 0) ? __bfloat162float(p.route[(bh + n) * kBSlots + slot]) : 0.0f;
+    }
+    __syncthreads();
+    // S^T [16 keys x 16 queries], dP^T likewise
+    float s[2][4], dp[2][4];
+    mma_abt(ka, qtile, lane, s);
+    mma_abt(va, gtile, lane, dp);
+    float ds[2][4];
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int64_t k = r0 + g + 8 * (e >> 1);
+        const int qi = j * 8 + 2 * t4 + (e & 1);
+        const int64_t n = t0 + qi;
+        const bool ok = n < len && k < T &&
+                        (GLOBAL ? (k < n - kBWindow && k < len) : (k < n && k >= n - kBWindow));
+        const float x = ok ? (s[j][e] * kBScale + s_bias[qi]) * kBLog2e : -INFINITY;
+        const float pr = ex2_approx(x - s_lse[qi]);
+        s[j][e] = pr;
+        ds[j][e] = pr * (dp[j][e] - s_delta[qi]);
+      }
+    uint32_t pa[4], da[4];
+    a_from_acc(s, pa);
+    a_from_acc(ds, da);
+    mma_pm(pa, gtile, lane, dv);  // dV += P^T dO
+    mma_pm(da, qtile, lane, dk);  // dK += dS^T Q
+  }
+  // ---- one writer per row
+  float* dkm = (GLOBAL ? p.dgk : p.dlk) + bh * 64;
+  float* dvm = (GLOBAL ? p.dgv : p.dlv) + bh * 64;
+#pragma unroll
+  for (int rr = 0; rr < 2; ++rr) {
+    const int64_t k = r0 + g + 8 * rr;
+    if (k >= T) continue;
+#pragma unroll
+    for (int nn = 0; nn < 8; ++nn) {
+      *reinterpret_cast<float2*>(dkm + k * 64 + nn * 8 + 2 * t4) =
+          make_float2(dk[nn][2 * rr] * kBScale, dk[nn][2 * rr + 1] * kBScale);
+      *reinterpret_cast<float2*>(dvm + k * 64 + nn * 8 + 2 * t4) = make_float2(dv[nn][2 * rr], dv[nn][2 * rr + 1]);
+    }
+  }
 }
 
 }  // namespace
@@ -244,21 +434,33 @@ using namespace dwarf;
 
 extern "C" int dwarf_hisa_attn_bwd(const dwarf_hisa_attn_bwd_args* a, void* stream) {
   DWARF_CHECK_VERSION(a);
-  if (a->B < 0 || a->H <= 0 || a->T < 0 || a->k_slots < 0 || a->k_slots > 4) return DWARF_ERR_SHAPE;
-  if (a->B > 65535 || a->H > 65535) return DWARF_ERR_SHAPE;
+  if (a->B < 0 || a->H <= 0 || a->T < 0 || a->k_slots < 0 || a->k_slots > kBSlots) return DWARF_ERR_SHAPE;
+  if (a->B > 65535 || a->H > 65535 || a->T > (int64_t)kBMaxTiles * kBT) return DWARF_ERR_SHAPE;
   if (a->B == 0 || a->T == 0) return DWARF_OK;
   if (!a->query || !a->local_key || !a->local_value || !a->global_key || !a->global_value || !a->route ||
       !a->lengths || !a->out || !a->dout || !a->dq || !a->d_local_key || !a->d_local_value ||
-      !a->d_global_key || !a->d_global_value || !a->d_route || (a->k_slots > 0 && !a->top_chunk_idx))
+      !a->d_global_key || !a->d_global_value || !a->d_route || !a->lse || !a->delta ||
+      (a->k_slots > 0 && !a->top_chunk_idx))
     return DWARF_ERR_NULL;
   const void* rows[] = {a->query, a->local_key, a->local_value, a->global_key, a->global_value, a->out, a->dout,
-                        a->dq, a->d_local_key, a->d_local_value, a->d_global_key, a->d_global_value};
+                        a->dq, a->d_local_key, a->d_local_value, a->d_global_key, a->d_global_value, a->d_route};
   for (const void* r : rows)
     if (!aligned16(r)) return DWARF_ERR_ALIGN;
   if (reinterpret_cast<uintptr_t>(a->route) & 7u) return DWARF_ERR_ALIGN;
-  const int64_t tiles = (a->T + kHQ - 1) / kHQ;
-  if (tiles > 2147483647LL) return DWARF_ERR_SHAPE;
-  hisa_attn_bwd_kernel<<<dim3((unsigned)tiles, (unsigned)a->H, (unsigned)a->B), kHT, 0,
-                         static_cast<cudaStream_t>(stream)>>>(*a);
+  BwdParams p;
+  p.q = (const __nv_bfloat16*)a->query; p.lk = (const __nv_bfloat16*)a->local_key;
+  p.lv = (const __nv_bfloat16*)a->local_value; p.gk = (const __nv_bfloat16*)a->global_key;
+  p.gv = (const __nv_bfloat16*)a->global_value; p.out = (const __nv_bfloat16*)a->out;
+  p.dout = (const __nv_bfloat16*)a->dout; p.route = (const __nv_bfloat16*)a->route;
+  p.top = a->top_chunk_idx; p.lengths = a->lengths;
+  p.dq = a->dq; p.dlk = a->d_local_key; p.dlv = a->d_local_value; p.dgk = a->d_global_key;
+  p.dgv = a->d_global_value; p.droute = a->d_route; p.lse = a->lse; p.delta = a->delta;
+  p.H = a->H; p.T = a->T; p.tiles = (a->T + kBT - 1) / kBT; p.k_slots = a->k_slots;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  hisa_bwd_query_kernel<<<dim3((unsigned)((p.tiles + kBWarps - 1) / kBWarps), (unsigned)a->H, (unsigned)a->B),
+                          kBWarps * 32, 0, st>>>(p);
+  const unsigned blocks = (unsigned)((a->T + kBChunk - 1) / kBChunk);
+  hisa_bwd_key_kernel<false><<<dim3(blocks, (unsigned)a->H, (unsigned)a->B), kBWarps * 32, 0, st>>>(p);
+  hisa_bwd_key_kernel<true><<<dim3(blocks, (unsigned)a->H, (unsigned)a->B), kBWarps * 32, 0, st>>>(p);
   return launch_status();
 }

@@ -234,9 +234,9 @@ class _HisaAttnFn(torch.autograd.Function):
         B, H, T, D = q.shape
         dob = dout.to(torch.bfloat16).contiguous()
         f32 = dict(dtype=torch.float32, device=q.device)
-        dq = torch.empty(B, H, T, D, **f32)
-        dlk, dlv, dgk, dgv = (torch.zeros(B, H, T, D, **f32) for _ in range(4))
+        dq, dlk, dlv, dgk, dgv = (torch.empty(B, H, T, D, **f32) for _ in range(5))
         droute = torch.empty(B, H, T, route.shape[-1], **f32)
+        lse, delta = torch.empty(2, B, H, T, **f32)
         args = _lib.HisaAttnBwdArgs(version=_lib.ABI_VERSION, k_slots=top.shape[-1], B=B, H=H, T=T,
                                     query=q.data_ptr(), local_key=lk.data_ptr(), local_value=lv.data_ptr(),
                                     global_key=gk.data_ptr(), global_value=gv.data_ptr(),
@@ -244,7 +244,7 @@ class _HisaAttnFn(torch.autograd.Function):
                                     out=out.data_ptr(), dout=dob.data_ptr(), dq=dq.data_ptr(),
                                     d_local_key=dlk.data_ptr(), d_local_value=dlv.data_ptr(),
                                     d_global_key=dgk.data_ptr(), d_global_value=dgv.data_ptr(),
-                                    d_route=droute.data_ptr())
+                                    d_route=droute.data_ptr(), lse=lse.data_ptr(), delta=delta.data_ptr())
         _lib.call("dwarf_hisa_attn_bwd", args, q.device)
         grads = (dq, dlk, dlv, dgk, dgv, droute)
         return (*(g.to(dt) for g, dt in zip(grads, ctx.dtypes)), None, None)

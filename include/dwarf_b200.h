@@ -499,15 +499,14 @@ int dwarf_hisa_attn(const dwarf_hisa_attn_args* args, void* stream);
  * autograd through the local lane and the LSE merge (:2424-2461, 808-835):
  * with P the joint softmax over the tile's local window and routed chunks,
  * dP = dO . v, delta = dO . O and dS = P (dP - delta):
- *   dq = (1/8) sum dS k,   dk += (1/8) dS q,   dv += P dO   (local or global K/V),
+ *   dq = (1/8) sum dS k,   dk = (1/8) sum dS q,   dv = sum P dO   (local or global K/V),
  *   d_route[n, slot] = sum of dS over the slot's chunk.
- * One CTA per (b, h, selector tile): the tile's keys (local rows
- * [t0 - 64, t0 + 15) and the routed chunks) in blocks of 32 staged in shared
- * memory; a first pass recomputes each query's lse. dq and d_route have one
- * writer per row; the K/V gradients (each key row feeds several tiles) are
- * accumulated with float4 atomics, so the caller zero-fills them and their
- * last bits vary between runs. Tensors contiguous, head_dim 64, chunk 64,
- * tile 16, window 64.
+ * Three launches on bf16 tensor cores: a query-side kernel (one warp per
+ * selector tile: lse, dq, d_route; it writes each row's lse and delta to the
+ * caller's scratch planes) and two key-side kernels (64 rows of local / global
+ * K/V per CTA: dk, dv). Every output row has exactly one writer: no zero-fill
+ * is needed and results are bit-identical between runs. Tensors contiguous,
+ * head_dim 64, chunk 64, tile 16, window 64, T <= 8192.
  * ---------------------------------------------------------------------- */
 typedef struct {
   int32_t version;
@@ -524,11 +523,13 @@ typedef struct {
   const void* out;                /* bf16 [B, H, T, 64] forward output    */
   const void* dout;               /* bf16 [B, H, T, 64]                   */
   float* dq;                      /* [B, H, T, 64] written                */
-  float* d_local_key;             /* [B, H, T, 64] accumulated            */
+  float* d_local_key;             /* [B, H, T, 64] written                */
   float* d_local_value;
   float* d_global_key;
   float* d_global_value;
   float* d_route;                 /* [B, H, T, 4] written                 */
+  float* lse;                     /* scratch [B, H, T]: row lse (log2)    */
+  float* delta;                   /* scratch [B, H, T]: row dO . O        */
 } dwarf_hisa_attn_bwd_args;
 
 int dwarf_hisa_attn_bwd(const dwarf_hisa_attn_bwd_args* args, void* stream);

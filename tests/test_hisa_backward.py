@@ -77,6 +77,7 @@ def test_engine_backward_full_length():
     ref = oracle_hisa.attention_backward(inputs, dout, g["top_chunk_idx"], g["valid_lengths"])
     for n in NAMES:
         _assert_grad_close(grads["d_" + n], ref["d_" + n], n)
-    # single-writer outputs are reproducible bit for bit
+    # every gradient row has one writer: runs are reproducible bit for bit
     _, again = _engine(inputs, dout, g["top_chunk_idx"], g["valid_lengths"])
-    assert torch.equal(grads["d_query"], again["d_query"]) and torch.equal(grads["d_route"], again["d_route"])
+    for n in NAMES:
+        assert torch.equal(grads["d_" + n], again["d_" + n]), n
