@@ -245,6 +245,7 @@ struct AttnParams {
   const int64_t* pos;            // optional: window [*pos/16, +tile_count) (decode step)
   int64_t tile_count;
   int k_slots;
+  float* lse;                    // optional [B,H,T]: row log-sum-exp, log2 domain
 };
 
 // S[16 x 8*NT] = Q tile . K block^T, online-softmax update, O += P . V.
@@ -672,6 +673,8 @@ hisa_attn_kernel(const AttnParams p, const __grid_constant__ AttnMaps maps, int3
         const int64_t row = t0 + g + rr * 8;
         if (row >= p.T) continue;
         const float inv = (l[rr] > 0.0f && row < vlen) ? 1.0f / l[rr] : 0.0f;
+        if (p.lse != nullptr && t4 == 0)
+          p.lse[((int64_t)b * p.H + h) * p.T + row] = (l[rr] > 0.0f && row < vlen) ? m[rr] + __log2f(l[rr]) : INFINITY;
 #pragma unroll
         for (int n = 0; n < 8; ++n) {
           const uint32_t v = pack_bf16(o[n][rr * 2] * inv, o[n][rr * 2 + 1] * inv);
@@ -818,6 +821,7 @@ extern "C" int dwarf_hisa_attn(const dwarf_hisa_attn_args* a, void* stream) {
   p.top = a->top_chunk_idx; p.route = (const __nv_bfloat16*)a->route;
   p.lengths = a->lengths;
   p.out = (__nv_bfloat16*)a->out; p.sob = a->sob; p.soh = a->soh; p.son = a->son;
+  p.lse = (float*)a->lse;
   p.H = a->H; p.T = a->T; p.tiles = (a->T + kTile - 1) / kTile;
   p.k_slots = a->k_slots;
   AttnMaps maps;

@@ -9,10 +9,10 @@
 //   d_route[n, slot] = sum of dS over the slot's chunk.
 // All products run on bf16 tensor cores (mma.sync m16n8k16, fp32 accumulate),
 // the structure of a FlashAttention-2 backward:
-//  1. query side, one warp per 16-query selector tile (4 per CTA): pass 1 builds
-//     the row lse over the tile's key blocks of 16, pass 2 forms P, dP, dS and
-//     accumulates dq (dS in bf16 times K) and d_route; it also stores each row's
-//     lse (log2 domain) and delta for step 2;
+//  1. query side, one warp per 16-query selector tile (4 per CTA): with the row
+//     lse the forward launch stored (log2 domain), it forms P, dP, dS over the
+//     tile's key blocks of 16 (a three-stage cp.async pipeline) and accumulates
+//     dq (dS in bf16 times K) and d_route; it stores each row's delta for step 2;
 //  2. key side, one CTA per 64 key rows (4 warps x 16 keys), separately for the
 //     local K/V (query tiles of the rows' windows) and the global K/V (the tiles
 //     that routed the chunk, found by scanning top_chunk_idx): S^T = K Q^T from
@@ -31,6 +31,7 @@ constexpr int kBChunk = 64;    // chunk rows == key rows per key-side CTA
 constexpr int kBWindow = 64;
 constexpr int kBSlots = 4;
 constexpr int kBWarps = 4;
+constexpr int kBStages = 3;  // query-side key-block pipeline depth
 constexpr float kBScale = 0.125f;
 constexpr float kBLog2e = 1.4426950408889634f;
 
@@ -76,6 +77,23 @@ __device__ __forceinline__ void stage16(uint32_t tile, const __nv_bfloat16* m, i
   }
 }
 
+// stage16 through cp.async (16-byte copies, zero-filled outside [0, T)); the
+// caller commits and waits.
+__device__ __forceinline__ void stage16_async(uint32_t tile, const __nv_bfloat16* m, int64_t r0, int64_t T, int tid,
+                                              int nthreads) {
+  for (int i = tid; i < 16 * 8; i += nthreads) {
+    const int r = i >> 3, c = i & 7;
+    const int64_t row = r0 + r;
+    const bool ok = row >= 0 && row < T;
+    const __nv_bfloat16* src = m + (ok ? row : 0) * 64 + c * 8;
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(tile_addr(tile, r, c)), "l"(src),
+                 "r"(ok ? 16 : 0) : "memory");
+  }
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
 // C[16 x 16] = A[16 x 64] . M^T for the 16-row smem tile M (rows = the n index).
 __device__ __forceinline__ void mma_abt(const uint32_t (&a)[4][4], uint32_t tile, int lane, float (&c)[2][4]) {
 #pragma unroll
@@ -113,7 +131,8 @@ __device__ __forceinline__ void a_from_acc(const float (&c)[2][4], uint32_t (&pa
 struct BwdParams {
   const __nv_bfloat16 *q, *lk, *lv, *gk, *gv, *out, *dout, *route;
   const int32_t *top, *lengths;
-  float *dq, *dlk, *dlv, *dgk, *dgv, *droute, *lse, *delta;
+  float *dq, *dlk, *dlv, *dgk, *dgv, *droute, *delta;
+  const float* lse;  // the forward's row lse (log2 domain)
   int64_t H, T, tiles;
   int k_slots;
 };
@@ -122,7 +141,7 @@ struct BwdParams {
 // Key block kb of a tile: kb < 5 local blocks of 16 rows from t0 - 64, then
 // 4 blocks per routed slot.
 __global__ void __launch_bounds__(kBWarps * 32) hisa_bwd_query_kernel(const BwdParams p) {
-  __shared__ __align__(128) unsigned char s_kv[kBWarps][2][16 * 128];
+  __shared__ __align__(128) unsigned char s_kv[kBWarps][kBStages][2][16 * 128];  // [warp][stage][K, V]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t4 = lane & 3;
   const int64_t h = blockIdx.y, b = blockIdx.z;
@@ -131,7 +150,7 @@ __global__ void __launch_bounds__(kBWarps * 32) hisa_bwd_query_kernel(const BwdP
   const int64_t T = p.T, t0 = t * kBT;
   const int64_t len = p.lengths[b] < T ? p.lengths[b] : T;
   const int64_t bh = (b * p.H + h) * T;
-  const uint32_t ktile = smem_u32(s_kv[warp][0]), vtile = smem_u32(s_kv[warp][1]);
+  const uint32_t kv0 = smem_u32(s_kv[warp][0][0]);  // buffer x: K at kv0 + x * 4096, V 2048 above
   int slot_chunk[kBSlots];
   {
     const int32_t* top = p.top + ((b * p.H + h) * p.tiles + t) * p.k_slots;
@@ -179,55 +198,41 @@ __global__ void __launch_bounds__(kBWarps * 32) hisa_bwd_query_kernel(const BwdP
     r0 = (int64_t)c * kBChunk + 16 * ((kb - 5) & 3);
     return c >= 0 && r0 < T;
   };
-  // log2-domain scores of the block for rows g, g + 8 (-inf where masked)
-  auto scores = [&](float (&s)[2][4], int64_t r0, int slot) {
+  // log2-domain scores of the block for rows g, g + 8 (-inf where masked);
+  // 32-bit positions (T <= 8192)
+  const int ti = (int)t0, leni = (int)len;
+  auto scores = [&](float (&s)[2][4], int r0, int slot) {
 #pragma unroll
     for (int j = 0; j < 2; ++j)
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int rr = e >> 1;
-        const int64_t n = t0 + g + 8 * rr, k = r0 + j * 8 + 2 * t4 + (e & 1);
-        const bool ok = n < len && k >= 0 && (slot < 0 ? (k < n && k >= n - kBWindow) : (k < n - kBWindow && k < len));
+        const int n = ti + g + 8 * rr, k = r0 + j * 8 + 2 * t4 + (e & 1);
+        const bool ok = n < leni && k >= 0 && (slot < 0 ? (k < n && k >= n - kBWindow) : (k < n - kBWindow && k < leni));
         float bias = 0.0f;
 #pragma unroll
         for (int q = 0; q < kBSlots; ++q) bias = q == slot ? route[rr][q] : bias;  // register select
         s[j][e] = ok ? (s[j][e] * kBScale + bias) * kBLog2e : -INFINITY;
       }
   };
-
-  // ---- pass 1: row max and sum (log2 domain)
-  float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.0f, 0.0f};
-  for (int kb = 0; kb < n_blocks; ++kb) {
-    int64_t r0;
-    int slot;
-    if (!block(kb, r0, slot)) continue;  // warp-uniform
-    const __nv_bfloat16* kbase = (slot < 0 ? p.lk : p.gk) + bh * 64;
-    __syncwarp();
-    stage16(ktile, kbase, r0, T, lane, 32);
-    __syncwarp();
-    float s[2][4];
-    mma_abt(qa, ktile, lane, s);
-    scores(s, r0, slot);
-#pragma unroll
-    for (int rr = 0; rr < 2; ++rr) {
-      float mx = fmaxf(fmaxf(s[0][2 * rr], s[0][2 * rr + 1]), fmaxf(s[1][2 * rr], s[1][2 * rr + 1]));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-      const float mn = fmaxf(m[rr], mx);
-      const float ms = mn == -INFINITY ? 0.0f : mn;
-      float add = ex2_approx(s[0][2 * rr] - ms) + ex2_approx(s[0][2 * rr + 1] - ms) + ex2_approx(s[1][2 * rr] - ms) +
-                  ex2_approx(s[1][2 * rr + 1] - ms);
-      add += __shfl_xor_sync(0xffffffffu, add, 1);
-      add += __shfl_xor_sync(0xffffffffu, add, 2);
-      l[rr] = l[rr] * ex2_approx(m[rr] - ms) + add;
-      m[rr] = mn;
-    }
-  }
+  // Row lse (log2 domain) from the forward launch.
   float lse[2];
 #pragma unroll
-  for (int rr = 0; rr < 2; ++rr) lse[rr] = l[rr] > 0.0f ? m[rr] + __log2f(l[rr]) : INFINITY;
-
-  // ---- pass 2: P, dP, dS; dq and d_route
+  for (int rr = 0; rr < 2; ++rr) {
+    const int64_t n = t0 + g + 8 * rr;
+    lse[rr] = n < T ? p.lse[bh + n] : INFINITY;
+  }
+  // Three-stage cp.async pipeline over the 21 key-block positions (absent blocks
+  // issue nothing and compute nothing): block kb uses buffer kb % 3, and the
+  // copies of blocks kb + 1 and kb + 2 are in flight while kb is computed.
+  auto issue = [&](int kb) {
+    int64_t r0;
+    int slot;
+    if (!block(kb, r0, slot)) return;
+    const uint32_t kt = kv0 + (kb % kBStages) * 4096;
+    stage16_async(kt, (slot < 0 ? p.lk : p.gk) + bh * 64, r0, T, lane, 32);
+    stage16_async(kt + 2048, (slot < 0 ? p.lv : p.gv) + bh * 64, r0, T, lane, 32);
+  };
   float dq[8][4];
 #pragma unroll
   for (int n = 0; n < 8; ++n) dq[n][0] = dq[n][1] = dq[n][2] = dq[n][3] = 0.0f;
@@ -235,40 +240,46 @@ __global__ void __launch_bounds__(kBWarps * 32) hisa_bwd_query_kernel(const BwdP
 #pragma unroll
   for (int rr = 0; rr < 2; ++rr)
 #pragma unroll
-    for (int s = 0; s < kBSlots; ++s) droute[rr][s] = 0.0f;
+    for (int q = 0; q < kBSlots; ++q) droute[rr][q] = 0.0f;
+  issue(0);
+  cp_commit();
+  issue(1);
+  cp_commit();
   for (int kb = 0; kb < n_blocks; ++kb) {
-    int64_t r0;
+    if (kb + 2 < n_blocks) issue(kb + 2);
+    cp_commit();
+    cp_wait<2>();
+    __syncwarp();
+    int64_t r0l;
     int slot;
-    if (!block(kb, r0, slot)) continue;
-    const int64_t off = bh * 64;
-    __syncwarp();
-    stage16(ktile, (slot < 0 ? p.lk : p.gk) + off, r0, T, lane, 32);
-    stage16(vtile, (slot < 0 ? p.lv : p.gv) + off, r0, T, lane, 32);
-    __syncwarp();
-    float s[2][4], dp[2][4];
-    mma_abt(qa, ktile, lane, s);
-    scores(s, r0, slot);
-    mma_abt(ga, vtile, lane, dp);
-    float rsum[2] = {0.0f, 0.0f};
+    if (block(kb, r0l, slot)) {  // warp-uniform
+      const uint32_t ktile = kv0 + (kb % kBStages) * 4096, vtile = ktile + 2048;
+      float s[2][4], dp[2][4];
+      mma_abt(qa, ktile, lane, s);
+      scores(s, (int)r0l, slot);
+      mma_abt(ga, vtile, lane, dp);
+      float rsum[2] = {0.0f, 0.0f};
 #pragma unroll
-    for (int j = 0; j < 2; ++j)
+      for (int j = 0; j < 2; ++j)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int rr = e >> 1;
-        const float pr = ex2_approx(s[j][e] - lse[rr]);
-        const float ds = pr * (dp[j][e] - delta[rr]);
-        s[j][e] = ds;
-        rsum[rr] += ds;
-      }
-    uint32_t pa[4];
-    a_from_acc(s, pa);
-    mma_pm(pa, ktile, lane, dq);
+        for (int e = 0; e < 4; ++e) {
+          const int rr = e >> 1;
+          const float pr = ex2_approx(s[j][e] - lse[rr]);
+          const float ds = pr * (dp[j][e] - delta[rr]);
+          s[j][e] = ds;
+          rsum[rr] += ds;
+        }
+      uint32_t pa[4];
+      a_from_acc(s, pa);
+      mma_pm(pa, ktile, lane, dq);
 #pragma unroll
-    for (int q = 0; q < kBSlots; ++q)
+      for (int q = 0; q < kBSlots; ++q)
 #pragma unroll
-      for (int rr = 0; rr < 2; ++rr) droute[rr][q] += q == slot ? rsum[rr] : 0.0f;
+        for (int rr = 0; rr < 2; ++rr) droute[rr][q] += q == slot ? rsum[rr] : 0.0f;
+    }
+    __syncwarp();  // buffer kb % 3 is refilled by the issue of the next iteration
   }
-  // ---- stores: dq, d_route (rows g, g + 8), lse and delta for the key side
+  // ---- stores: dq, d_route (rows g, g + 8), delta for the key side
 #pragma unroll
   for (int rr = 0; rr < 2; ++rr) {
     const int64_t n = t0 + g + 8 * rr;
@@ -285,7 +296,6 @@ __global__ void __launch_bounds__(kBWarps * 32) hisa_bwd_query_kernel(const BwdP
       if (t4 == 0) {
         *reinterpret_cast<float4*>(p.droute + (bh + n) * kBSlots) =
             make_float4(droute[rr][0], droute[rr][1], droute[rr][2], droute[rr][3]);
-        p.lse[bh + n] = lse[rr];
         p.delta[bh + n] = delta[rr];
       }
     }
@@ -300,8 +310,8 @@ constexpr int kBMaxTiles = 512;  // T <= 8192 (128 chunks): at most 512 selector
 
 template <bool GLOBAL>
 __global__ void __launch_bounds__(kBWarps * 32) hisa_bwd_key_kernel(const BwdParams p) {
-  __shared__ __align__(128) unsigned char s_tile[2][16 * 128];  // the query tile's Q and dO
-  __shared__ float s_lse[16], s_delta[16], s_bias[16];
+  __shared__ __align__(128) unsigned char s_tile[2][2][16 * 128];  // [buffer][Q, dO] of a query tile
+  __shared__ float s_lse[2][16], s_delta[2][16], s_bias[2][16];
   __shared__ int16_t s_list[kBMaxTiles];
   __shared__ int8_t s_slot[kBMaxTiles];
   __shared__ int s_count;
@@ -311,7 +321,7 @@ __global__ void __launch_bounds__(kBWarps * 32) hisa_bwd_key_kernel(const BwdPar
   const int64_t T = p.T, k0 = (int64_t)blockIdx.x * kBChunk;
   const int64_t len = p.lengths[b] < T ? p.lengths[b] : T;
   const int64_t bh = (b * p.H + h) * T;
-  const uint32_t qtile = smem_u32(s_tile[0]), gtile = smem_u32(s_tile[1]);
+  const uint32_t tiles0 = smem_u32(s_tile[0][0]);  // buffer x: Q at tiles0 + x * 4096, dO 2048 above
 
   // ---- the query tiles that see these rows
   if (GLOBAL) {
@@ -372,20 +382,40 @@ __global__ void __launch_bounds__(kBWarps * 32) hisa_bwd_key_kernel(const BwdPar
 #pragma unroll
   for (int n = 0; n < 8; ++n) dk[n][0] = dk[n][1] = dk[n][2] = dk[n][3] = dv[n][0] = dv[n][1] = dv[n][2] = dv[n][3] = 0.0f;
 
-  for (int i = 0; i < n_tiles; ++i) {
+  // Double-buffered: tile i + 1's Q / dO copies (cp.async) and its per-row lse,
+  // delta and route prior (registers of threads 0..15) load while tile i computes.
+  float nl = INFINITY, nd = 0.0f, nb = 0.0f;
+  auto issue = [&](int i, int buf) {
     const int64_t t0 = (int64_t)s_list[i] * kBT;
     const int slot = s_slot[i];
-    __syncthreads();  // the previous tile's smem is no longer read
-    stage16(qtile, p.q + bh * 64, t0, T, tid, kBWarps * 32);
-    stage16(gtile, p.dout + bh * 64, t0, T, tid, kBWarps * 32);
+    stage16_async(tiles0 + buf * 4096, p.q + bh * 64, t0, T, tid, kBWarps * 32);
+    stage16_async(tiles0 + buf * 4096 + 2048, p.dout + bh * 64, t0, T, tid, kBWarps * 32);
     if (tid < 16) {
       const int64_t n = t0 + tid;
       const bool ok = n < T;
-      s_lse[tid] = ok ? p.lse[bh + n] : INFINITY;
-      s_delta[tid] = ok ? p.delta[bh + n] : 0.0f;
-      s_bias[tid] = (ok && slot >= 0) ? __bfloat162float(p.route[(bh + n) * kBSlots + slot]) : 0.0f;
+      nl = ok ? p.lse[bh + n] : INFINITY;
+      nd = ok ? p.delta[bh + n] : 0.0f;
+      nb = (ok && slot >= 0) ? __bfloat162float(p.route[(bh + n) * kBSlots + slot]) : 0.0f;
     }
-    __syncthreads();
+  };
+  if (n_tiles > 0) issue(0, 0);
+  cp_commit();
+  for (int i = 0; i < n_tiles; ++i) {
+    const int buf = i & 1;
+    const int64_t t0 = (int64_t)s_list[i] * kBT;
+    if (tid < 16) {
+      s_lse[buf][tid] = nl;
+      s_delta[buf][tid] = nd;
+      s_bias[buf][tid] = nb;
+    }
+    if (i + 1 < n_tiles) issue(i + 1, buf ^ 1);
+    cp_commit();
+    cp_wait<1>();
+    __syncthreads();  // tile i visible to every warp
+    const uint32_t qtile = tiles0 + buf * 4096, gtile = qtile + 2048;
+    const float* s_lse_b = s_lse[buf];
+    const float* s_delta_b = s_delta[buf];
+    const float* s_bias_b = s_bias[buf];
     // S^T [16 keys x 16 queries], dP^T likewise
     float s[2][4], dp[2][4];
     mma_abt(ka, qtile, lane, s);
@@ -400,16 +430,17 @@ __global__ void __launch_bounds__(kBWarps * 32) hisa_bwd_key_kernel(const BwdPar
         const int64_t n = t0 + qi;
         const bool ok = n < len && k < T &&
                         (GLOBAL ? (k < n - kBWindow && k < len) : (k < n && k >= n - kBWindow));
-        const float x = ok ? (s[j][e] * kBScale + s_bias[qi]) * kBLog2e : -INFINITY;
-        const float pr = ex2_approx(x - s_lse[qi]);
+        const float x = ok ? (s[j][e] * kBScale + s_bias_b[qi]) * kBLog2e : -INFINITY;
+        const float pr = ex2_approx(x - s_lse_b[qi]);
         s[j][e] = pr;
-        ds[j][e] = pr * (dp[j][e] - s_delta[qi]);
+        ds[j][e] = pr * (dp[j][e] - s_delta_b[qi]);
       }
     uint32_t pa[4], da[4];
     a_from_acc(s, pa);
     a_from_acc(ds, da);
     mma_pm(pa, gtile, lane, dv);  // dV += P^T dO
     mma_pm(da, qtile, lane, dk);  // dK += dS^T Q
+    __syncthreads();  // buffer buf is refilled by the next iteration's issue
   }
   // ---- one writer per row
   float* dkm = (GLOBAL ? p.dgk : p.dlk) + bh * 64;

@@ -189,8 +189,9 @@ def tile_attention(query, local_key, local_value, global_key, global_value, reps
     return out, (route if want_route else None)
 
 
-def _attn_launch(query, local_key, local_value, global_key, global_value, top, route, lengths, out):
-    """``dwarf_hisa_attn`` with a given bf16 route prior [B,H,T,4]."""
+def _attn_launch(query, local_key, local_value, global_key, global_value, top, route, lengths, out, lse=None):
+    """``dwarf_hisa_attn`` with a given bf16 route prior [B,H,T,4]; ``lse`` (fp32
+    [B,H,T], optional) receives the row log-sum-exp (log2 units) the backward reads."""
     B, H, T, D = query.shape
     args = _lib.HisaAttnArgs(version=_lib.ABI_VERSION, head_dim=D, chunk_size=_CHUNK, selector_tile=_TILE,
                              local_window=_WINDOW, k_slots=top.shape[-1], B=B, H=H, T=T,
@@ -198,7 +199,7 @@ def _attn_launch(query, local_key, local_value, global_key, global_value, top, r
                              local_value=local_value.data_ptr(), global_key=global_key.data_ptr(),
                              global_value=global_value.data_ptr(), top_chunk_idx=top.data_ptr(),
                              route=route.data_ptr(), lengths=lengths.data_ptr(), out=out.data_ptr(),
-                             tile_begin=0, tile_count=0, pos=None)
+                             tile_begin=0, tile_count=0, pos=None, lse=None if lse is None else lse.data_ptr())
     args.sqb, args.sqh, args.sqn = _strides3(query)
     args.slkb, args.slkh, args.slkn = _strides3(local_key)
     args.slvb, args.slvh, args.slvn = _strides3(local_value)
@@ -223,20 +224,21 @@ class _HisaAttnFn(torch.autograd.Function):
         top = top.to(torch.int32).contiguous()
         B, H, T, D = ins[0].shape
         out = torch.empty(B, H, T, D, dtype=torch.bfloat16, device=query.device)
-        _attn_launch(*ins[:5], top, ins[5], lengths, out)
-        ctx.save_for_backward(*ins, top, lengths, out)
+        lse = torch.empty(B, H, T, dtype=torch.float32, device=query.device)
+        _attn_launch(*ins[:5], top, ins[5], lengths, out, lse)
+        ctx.save_for_backward(*ins, top, lengths, out, lse)
         ctx.dtypes = tuple(t.dtype for t in (query, local_key, local_value, global_key, global_value, route))
         return out if query.dtype == torch.bfloat16 else out.to(query.dtype)
 
     @staticmethod
     def backward(ctx, dout):
-        q, lk, lv, gk, gv, route, top, lengths, out = ctx.saved_tensors
+        q, lk, lv, gk, gv, route, top, lengths, out, lse = ctx.saved_tensors
         B, H, T, D = q.shape
         dob = dout.to(torch.bfloat16).contiguous()
         f32 = dict(dtype=torch.float32, device=q.device)
         dq, dlk, dlv, dgk, dgv = (torch.empty(B, H, T, D, **f32) for _ in range(5))
         droute = torch.empty(B, H, T, route.shape[-1], **f32)
-        lse, delta = torch.empty(2, B, H, T, **f32)
+        delta = torch.empty(B, H, T, **f32)
         args = _lib.HisaAttnBwdArgs(version=_lib.ABI_VERSION, k_slots=top.shape[-1], B=B, H=H, T=T,
                                     query=q.data_ptr(), local_key=lk.data_ptr(), local_value=lv.data_ptr(),
                                     global_key=gk.data_ptr(), global_value=gv.data_ptr(),

@@ -486,6 +486,11 @@ typedef struct {
   void* out;                int64_t sob, soh, son;   /* bf16              */
   int64_t tile_begin, tile_count; /* as dwarf_hisa_select_args            */
   const int64_t* pos;             /* as dwarf_hisa_select_args            */
+  float* lse;                     /* optional fp32 [B, H, T] (contiguous):
+                                     row log-sum-exp of the joint softmax in
+                                     log2 units (scores x log2 e), +inf for rows
+                                     with no key: the input dwarf_hisa_attn_bwd
+                                     needs. NULL: not written                */
 } dwarf_hisa_attn_args;
 
 int dwarf_hisa_reps(const dwarf_hisa_reps_args* args, void* stream);
@@ -502,9 +507,9 @@ int dwarf_hisa_attn(const dwarf_hisa_attn_args* args, void* stream);
  *   dq = (1/8) sum dS k,   dk = (1/8) sum dS q,   dv = sum P dO   (local or global K/V),
  *   d_route[n, slot] = sum of dS over the slot's chunk.
  * Three launches on bf16 tensor cores: a query-side kernel (one warp per
- * selector tile: lse, dq, d_route; it writes each row's lse and delta to the
- * caller's scratch planes) and two key-side kernels (64 rows of local / global
- * K/V per CTA: dk, dv). Every output row has exactly one writer: no zero-fill
+ * selector tile: dq, d_route; it writes each row's delta to the caller's
+ * scratch plane) and two key-side kernels (64 rows of local / global K/V per
+ * CTA: dk, dv). The row lse comes from the forward launch (its lse output). Every output row has exactly one writer: no zero-fill
  * is needed and results are bit-identical between runs. Tensors contiguous,
  * head_dim 64, chunk 64, tile 16, window 64, T <= 8192.
  * ---------------------------------------------------------------------- */
@@ -528,7 +533,7 @@ typedef struct {
   float* d_global_key;
   float* d_global_value;
   float* d_route;                 /* [B, H, T, 4] written                 */
-  float* lse;                     /* scratch [B, H, T]: row lse (log2)    */
+  const float* lse;               /* [B, H, T]: the forward's lse output  */
   float* delta;                   /* scratch [B, H, T]: row dO . O        */
 } dwarf_hisa_attn_bwd_args;
 
