@@ -11,8 +11,9 @@ pool's earlier measurement (6650 GB/s, marked "fallback").
 Inputs are synthetic, seeded, with the shapes and distributions of the named
 configurations (config 2: causal EMA scan B=16 T=2048 D=512 fp32; config 3:
 DSQG over a q6 KV cache B=32 H=8 T=2048 J=96; config 4: HISA B=32 H=8 T=2048,
-Q/K/V ~ N(0, 0.125^2)); the backward cases use the same shapes. Before every
-timed iteration a 512 MB buffer is written, so no input starts in the 126 MB L2.
+Q/K/V ~ N(0, 0.125^2)); the backward cases use the same shapes; the training
+step case runs the full model on 8 x 2048 tokens. Before every timed iteration
+a 512 MB buffer is written, so no input starts in the 126 MB L2.
 """
 
 from __future__ import annotations
@@ -247,6 +248,44 @@ def case_hisa_bwd_config4(timer, peak):
     return {"kernels": times, "dwarf_hisa_attn_bwd": _rate(nbytes, times["dwarf_hisa_attn_bwd"], peak)}
 
 
+def case_model_train_step(timer, peak):
+    """One training step of the full model (DwarfConfig(): D=512, L=10, vocab 32768, bf16
+    weights, train mode) on B=8 x T=2048 tokens: forward, next-token cross entropy + the
+    HISA auxiliary loss, backward. Whole-step time with CUDA events; the engine kernels'
+    per-launch times inside the step."""
+    import torch.nn.functional as F
+
+    from .model import DwarfConfig, DwarfForCausalLM
+
+    model = DwarfForCausalLM(DwarfConfig()).to(torch.bfloat16).cuda().train()
+    g = torch.Generator().manual_seed(9)
+    B, T = 8, 2048
+    ids = torch.randint(57, 32768, (B, T), generator=g).cuda()
+    labels = ids.roll(-1, 1).reshape(-1)
+
+    def step():
+        model.zero_grad(set_to_none=True)
+        logits, aux = model(ids, return_auxiliary=True)
+        loss = F.cross_entropy(logits.reshape(-1, logits.shape[-1]).float(), labels) + aux
+        loss.backward()
+
+    for _ in range(2):
+        step()
+    torch.cuda.synchronize()
+    iters = 3
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(iters):
+        step()
+    end.record()
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(end) / iters
+    names = ("dwarf_dsqg_fwd", "dwarf_dsqg_bwd", "dwarf_hisa_attn", "dwarf_hisa_attn_bwd", "dwarf_ema_scan",
+             "dwarf_ema_scan_grad_alpha")
+    return {"tokens_per_step": B * T, "ms_per_step": round(ms, 3), "train_tok_per_s": round(B * T / (ms * 1e-3)),
+            "kernels_mean_ms": timer(step, names)}
+
+
 CASES = {
     "ema_config2": case_ema_config2,
     "ema_model_bf16": case_ema_model_bf16,
@@ -256,6 +295,7 @@ CASES = {
     "dsqg_bwd_model_group": case_dsqg_bwd_model_group,
     "hisa_config4": case_hisa_config4,
     "hisa_bwd_config4": case_hisa_bwd_config4,
+    "model_train_step": case_model_train_step,
 }
 
 
