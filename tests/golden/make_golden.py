@@ -530,6 +530,56 @@ def make_model_train() -> None:
     save("model_train_step", **out)
 
 
+def make_hisa_backward_edges() -> None:
+    """HISA attention backward at the edges, each case from the reference's own
+    router (representatives, anchor logits, top-4) and fp64 autograd through its
+    eager lanes + merge: T=64 (one chunk, so no tile has a routed chunk),
+    T=1 (row 0 has no key), T=83 with valid lengths [83, 0] (a row of length 0
+    and a partial last tile), T=200 with lengths [130, 199]."""
+    _import_reference()
+    import torch.nn.functional as F
+
+    import hierarchical_sparse_attn_v18_hisa as ref
+
+    out = {}
+    cases = [("t64", 64, [64, 64]), ("t1", 1, [1, 1]), ("t83", 83, [83, 0]), ("t200", 200, [130, 199])]
+    for i, (tag, T, lens) in enumerate(cases):
+        g = torch.Generator().manual_seed(700 + i)
+        B, H, D = 2, 2, 64
+        q = (torch.randn(B, H, T, D, generator=g) * 0.5).to(torch.bfloat16)
+        lk = (torch.randn(B, H, T, D, generator=g) * 0.5).to(torch.bfloat16)
+        lv = torch.randn(B, H, T, D, generator=g).to(torch.bfloat16)
+        gk = (lk.float() + 0.3 * torch.randn(B, H, T, D, generator=g)).to(torch.bfloat16)
+        gv = (lv.float() + 0.3 * torch.randn(B, H, T, D, generator=g)).to(torch.bfloat16)
+        lengths = torch.tensor(lens, dtype=torch.int32)
+        reps = ref._completed_chunk_representatives(gk, chunk_size=64, valid_lengths=lengths,
+                                                    representative_mode="mean_max_blend", blend_alpha=0.5)
+        qn = F.normalize(q.float(), dim=-1, eps=1e-6).to(q.dtype)
+        anchor = qn[:, :, (torch.arange(-(-T // 16)) * 16).clamp_max(T - 1)]
+        logits = torch.matmul(anchor.float(), reps.float().transpose(-2, -1))
+        meta = ref._build_causal_tile_metadata(anchor, gk, logits, chunk_size=64, top_k_chunks=4, top_m_tokens=64,
+                                               selector_tile_size=16, valid_lengths=lengths,
+                                               canonical_token_order=False, exploration_probability=0.0)
+        route = ref._selected_route_scores(qn, reps, meta, torch.tensor([0.1, 0.3]))
+        names = ("q", "local_key", "local_value", "global_key", "global_value", "route")
+        leaves = {n: t.double().clone().requires_grad_(True) for n, t in zip(names, (q, lk, lv, gk, gv, route))}
+        lo, llse = ref._eager_local_lane(leaves["q"], leaves["local_key"], leaves["local_value"], lengths,
+                                         local_window=64, selector_tile_size=16)
+        go, glse = ref._eager_global_lane(leaves["q"], leaves["global_key"], leaves["global_value"],
+                                          leaves["route"], meta, local_window=64)
+        merged, _ = ref._merge_attention_lanes(lo, llse, go, glse)
+        dout = torch.randn(merged.shape, generator=g, dtype=torch.float64).to(torch.bfloat16)
+        grads = torch.autograd.grad(merged, [leaves[n] for n in names], dout.double(), allow_unused=True)
+        out.update({f"{tag}.{n}": t for n, t in zip(names, (q, lk, lv, gk, gv, route))})
+        out[f"{tag}.valid_lengths"] = lengths
+        out[f"{tag}.top_chunk_idx"] = meta.top_chunk_idx
+        out[f"{tag}.dout"] = dout
+        out[f"{tag}.merged"] = merged.detach().float()
+        for n, gr in zip(names, grads):
+            out[f"{tag}.d_{n}"] = (torch.zeros_like(leaves[n]) if gr is None else gr).float()
+    save("hisa_bwd_edges", **out)
+
+
 def make_model() -> None:
     """Whole-model prefill of the reference DwarfForCausalLM (seeded init), B=1, T=2048.
 
@@ -651,7 +701,7 @@ def make_checkpoint() -> None:
 
 def main(argv: list[str]) -> None:
     which = argv[1] if len(argv) > 1 else "all"
-    makers = {"ema": make_ema, "ema_bwd": make_ema_backward, "dsqg": make_dsqg, "dsqg_bwd": make_dsqg_backward, "dsqg_module_grad": make_dsqg_module_grad, "hisa": make_hisa, "hisa_bwd": make_hisa_backward, "hisa_module_grad": make_hisa_module_grad, "model": make_model, "model_train": make_model_train,
+    makers = {"ema": make_ema, "ema_bwd": make_ema_backward, "dsqg": make_dsqg, "dsqg_bwd": make_dsqg_backward, "dsqg_module_grad": make_dsqg_module_grad, "hisa": make_hisa, "hisa_bwd": make_hisa_backward, "hisa_bwd_edges": make_hisa_backward_edges, "hisa_module_grad": make_hisa_module_grad, "model": make_model, "model_train": make_model_train,
               "checkpoint": make_checkpoint}
     for name, maker in makers.items():
         if which in ("all", name):
