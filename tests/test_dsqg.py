@@ -386,3 +386,22 @@ def test_row_window_matches_full_launch(N, row_begin, path, monkeypatch):
         fin = torch.isfinite(lse[:, :, row_begin:])
         assert torch.equal(fin, torch.isfinite(w_lse))
         assert (w_lse[fin] - lse[:, :, row_begin:][fin]).abs().max().item() < 1e-3
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("path", ["resident", "gather"])
+def test_kernel_causality_prefix_unchanged(path, monkeypatch):
+    """Perturbing Q/K/V and the probes at positions >= 700 leaves every output row
+    before 700 bit-identical (the reference's causality check,
+    dsqg_attention_v22.py:3315-3321), on both q6 kernels."""
+    c, offs, js = _resident_case(2, 4, 4, 1024, seed=71)
+    out, _, _ = _run_q6(c, offs, js, 6, 0, path, monkeypatch)
+    gen = torch.Generator().manual_seed(72)
+    d = dict(c)
+    for name in ("q", "k", "v", "y_pre", "z_pre"):
+        t = d[name].clone()
+        t[:, :, 700:] = torch.randn(t[:, :, 700:].shape, generator=gen).to(t.dtype)
+        d[name] = t
+    out2, _, _ = _run_q6(d, offs, js, 6, 0, path, monkeypatch)
+    assert torch.equal(out[:, :, :700], out2[:, :, :700])
+    assert not torch.equal(out[:, :, 700:], out2[:, :, 700:])

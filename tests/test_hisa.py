@@ -183,3 +183,27 @@ def test_tile_window_matches_full_launch(T, tile_begin, tile_count):
     assert torch.equal(wtop[:, :, tile_begin:t_end], top[:, :, tile_begin:t_end])
     assert torch.equal(out[:, :, r0:r1], ref[:, :, r0:r1])
     assert torch.all(out[:, :, :r0] == 7.0) and torch.all(out[:, :, r1:] == 7.0)
+
+
+@pytest.mark.gpu
+def test_router_and_attention_causality_prefix_unchanged():
+    """Perturbing Q/K/V at positions >= 300 leaves the routed chunk indices of every
+    tile starting before 300 and every output row before 300 bit-identical (the
+    reference's causality check, hierarchical_sparse_attn_v18_hisa.py:2816-2822):
+    the router only sees chunks completed before a tile starts, and each tile's
+    chunk order does not depend on the tiles sharing its CTA."""
+    from dwarf_v2_b200.hierarchical_sparse_attn_v18_hisa import hisa_attention
+
+    gen = torch.Generator().manual_seed(81)
+    B, H, T = 2, 4, 1024
+    q, k, v = ((torch.randn(B, H, T, 64, generator=gen) * 0.5).to(torch.bfloat16) for _ in range(3))
+    scale = torch.full((H,), 0.1)
+    out, top, _ = hisa_attention(q.cuda(), k.cuda(), v.cuda(), k.cuda(), v.cuda(), scale)
+    q2, k2, v2 = q.clone(), k.clone(), v.clone()
+    for t in (q2, k2, v2):
+        t[:, :, 300:] = (torch.randn(t[:, :, 300:].shape, generator=gen) * 0.5).to(t.dtype)
+    out2, top2, _ = hisa_attention(q2.cuda(), k2.cuda(), v2.cuda(), k2.cuda(), v2.cuda(), scale)
+    torch.cuda.synchronize()
+    assert torch.equal(top[:, :, : 300 // 16 + 1], top2[:, :, : 300 // 16 + 1])
+    assert torch.equal(out[:, :, :300], out2[:, :, :300])
+    assert not torch.equal(out[:, :, 300:], out2[:, :, 300:])
