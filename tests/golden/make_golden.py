@@ -407,8 +407,19 @@ def make_hisa_backward() -> None:
     anchor = qn[:, :, (torch.arange(-(-T // 16)) * 16).clamp_max(T - 1)]
     logits = torch.matmul(anchor.float(), g["reps"].float().transpose(-2, -1))
     aux = ref._router_auxiliary_loss(logits, anchor, g["global_key"], meta, samples=64, temperature=1.0)
+    # The random training paths under fixed CPU seeds: the auxiliary loss over 4
+    # sampled tiles (torch.randperm) and the exploration slot (two torch.rand draws).
+    torch.manual_seed(123)
+    aux_sampled = ref._router_auxiliary_loss(logits, anchor, g["global_key"], meta, samples=4, temperature=1.0)
+    tiles = -(-T // 16)
+    eligible = ref._eligibility(torch.arange(tiles, dtype=torch.int32) * 16, g["reps"].shape[2], 64,
+                                g["valid_lengths"])
+    top3 = g["top_chunk_idx"][..., :3].contiguous()
+    torch.manual_seed(124)
+    explored, _ = ref._inject_exploration_slot(top3.long(), top3 >= 0, eligible, 0.5)
     save("hisa_bwd_lanes", dout=dout, merged=merged.detach().float(),
-         **{f"d_{n}": gr.float() for n, gr in zip(names, grads)}, aux=aux)
+         **{f"d_{n}": gr.float() for n, gr in zip(names, grads)}, aux=aux, aux_sampled=aux_sampled,
+         explored=explored.to(torch.int32))
 
 
 def make_hisa_module_grad() -> None:

@@ -133,3 +133,24 @@ def test_training_exploration_changes_only_the_last_slot():
     top, ref = meta.top_chunk_idx.cpu(), base.top_chunk_idx.cpu()
     assert torch.equal(top[..., :-1], ref[..., :-1])
     assert (top[..., -1] >= -1).all() and (top[..., -1] < 5).all()
+
+
+def test_random_training_paths_match_reference_draws():
+    """With the same CPU seed, the sampled auxiliary loss (4 of 15 candidate tiles,
+    torch.randperm) and the exploration slot (probability 0.5, two torch.rand draws)
+    reproduce the reference's own outputs exactly: the restatements draw in the
+    reference's order and shapes."""
+    g, gb = load("hisa_router_lanes"), load("hisa_bwd_lanes")
+    T = g["q"].shape[2]
+    qn = F.normalize(g["q"].float(), dim=-1, eps=1e-6).to(g["q"].dtype)
+    anchor = qn[:, :, (torch.arange(-(-T // 16)) * 16).clamp_max(T - 1)]
+    logits = torch.matmul(anchor.float(), g["reps"].float().transpose(-2, -1))
+    torch.manual_seed(123)
+    aux = hisa.router_auxiliary_loss(logits, anchor, g["global_key"], g["valid_lengths"], samples=4, temperature=1.0)
+    assert float(aux) == float(gb["aux_sampled"])
+    top3 = g["top_chunk_idx"][..., :3].contiguous()
+    eligible = hisa._eligible(top3.shape[2], g["reps"].shape[2], g["valid_lengths"])
+    torch.manual_seed(124)
+    explored = hisa.inject_exploration(top3, eligible, 0.5)
+    assert torch.equal(explored, gb["explored"])
+    assert not torch.equal(explored, top3)
