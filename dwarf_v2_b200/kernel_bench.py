@@ -160,6 +160,36 @@ def case_dsqg_q6_config3(timer, peak):
             "valid_pairs": valid_pairs, "fp32_tflops": round(flops / (ms * 1e-3) / 1e12, 2)}
 
 
+def case_dsqg_q6_model_group(timer, peak):
+    """One model DSQG layer over a q6 KV cache at the config-3 shape (B=32 H=8 T=2048) with
+    the model's first 29-offset group (6 small, 23 large), the q6 cache layout the qkvg
+    epilogue writes."""
+    from .dsqg_attention_v22 import dsqg_attention_q6
+    from .model import DwarfConfig, build_offset_groups
+    from .q6 import q6_pack
+
+    offsets = list(build_offset_groups(DwarfConfig())[0])
+    js = sum(1 for o in offsets if o <= 28)
+    g = torch.Generator().manual_seed(10)
+    B, H, N, J = 32, 8, 2048, len(offsets)
+    q = torch.randn(B, H, N, 64, generator=g).to(torch.bfloat16).cuda()
+    kc, ks = q6_pack(torch.randn(B, H, N, 64, generator=g).to(torch.bfloat16).cuda())
+    vc, vs = q6_pack(torch.randn(B, H, N, 64, generator=g).to(torch.bfloat16).cuda())
+    pb, se, pbase, pgain = _dsqg_tables(J, js, H, offsets, g)
+    y = (torch.randn(B, H, N, 4, generator=g) * 0.2).cuda()
+    z = (torch.randn(B, H, N, 4, generator=g) * 0.2).cuda()
+    offs = torch.tensor(offsets, dtype=torch.int32, device="cuda")
+    res = {}
+    times = timer(lambda: res.__setitem__("o", dsqg_attention_q6(q, kc, ks, vc, vs, pb, se, pbase, pgain, y, z,
+                                                                  offs, js, J - js, 0, 1)), ("dwarf_dsqg_fwd",))
+    ms = times["dwarf_dsqg_fwd"]
+    valid_pairs = sum(max(0, N - d) for d in offsets) * B * H
+    return {"kernel": "dwarf_dsqg_fwd (q6, model group 0)", "ms": ms,
+            **_rate(_nbytes(q, kc, ks, vc, vs, y, z, res["o"]), ms, peak), "valid_pairs": valid_pairs,
+            "fp32_tflops": round(valid_pairs * 4 * 64 / (ms * 1e-3) / 1e12, 2),
+            "ns_per_pair_per_sm": round(ms * 1e6 * 148 / valid_pairs, 3)}
+
+
 def case_dsqg_bwd_model_group(timer, peak):
     """DSQG backward at the config-3 shape (B=32 H=8 T=2048) with bf16 K/V and the model's
     first 29-offset group (one training layer): query-side and key-side gather kernels."""
@@ -292,6 +322,7 @@ CASES = {
     "ema_bwd_config2": case_ema_bwd_config2,
     "q6_pack_config3": case_q6_pack_config3,
     "dsqg_q6_config3": case_dsqg_q6_config3,
+    "dsqg_q6_model_group": case_dsqg_q6_model_group,
     "dsqg_bwd_model_group": case_dsqg_bwd_model_group,
     "hisa_config4": case_hisa_config4,
     "hisa_bwd_config4": case_hisa_bwd_config4,
