@@ -17,11 +17,17 @@ Printed JSON line (rank 0):
            next-token logits inside the timed region;
 * roofline the dominant engine kernel (dwarf_dsqg_fwd): algorithmic bytes per
            launch / its mean CUDA-event duration inside the timed region,
-           against the measured HBM copy bandwidth;
+           against the measured HBM copy bandwidth; ``fma`` beside it: the
+           kernel's FP32 pair FMAs (2 x 64 per valid (query, offset) pair) per
+           second against the derived CUDA-core peak (148 SMs x 128 lanes x 2
+           x the sampled SM clock);
+* device_status the status word of the kernels' bounded waits after the
+           timed region (non-zero: a wait ran out and the line is invalid);
 * cpu_baseline  the CPU oracle port of the same prefill (oracle/model.py) on
            one 2048-token row, host cores, rank 0 at N=1.
-``--impl reference`` times that CPU port alone (the reference is pure
-PyTorch/Triton and cannot be installed on the GPU box).
+``--impl reference`` times that CPU port alone on the host cores (the
+reference's own code is pure PyTorch/Triton under a source tree that is not
+present on the GPU box), with the port built once outside the timed steps.
 """
 
 from __future__ import annotations
@@ -110,8 +116,9 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def cpu_baseline(sample_rows: int = 1) -> dict:
-    """Time the CPU oracle port of the prefill on `sample_rows` rows of the workload."""
+def _cpu_port():
+    """The CPU restatement of the prefill (oracle/model.py), its seeded reference-init
+    state dict and the offset lattice; built once, outside any timed region."""
     sys.path.insert(0, str(ROOT))
     from oracle import model as omodel
 
@@ -120,12 +127,25 @@ def cpu_baseline(sample_rows: int = 1) -> dict:
 
     cores = len(os.sched_getaffinity(0))
     torch.set_num_threads(cores)
-    state = DwarfForCausalLM().state_dict()
-    ids = _token_ids(slice(0, sample_rows))
+    with torch.no_grad():
+        state = {k: v.clone() for k, v in DwarfForCausalLM().state_dict().items()}
+    return omodel, state, ALL_OFFSETS, cores
+
+
+def _cpu_sample(port, ids) -> float:
+    omodel, state, offsets, _ = port
     t0 = time.perf_counter()
-    omodel.prefill(state, ids, all_offsets=ALL_OFFSETS)
-    dt = time.perf_counter() - t0
-    return {"value": sample_rows * SEQ_LEN / dt, "unit": "tok/s", "cores": cores, "kind": "port",
+    omodel.prefill(state, ids, all_offsets=offsets)
+    return time.perf_counter() - t0
+
+
+def cpu_baseline(sample_rows: int = 1) -> dict:
+    """Time the CPU oracle port of the prefill on `sample_rows` rows of the workload
+    (model construction outside the timed call)."""
+    port = _cpu_port()
+    ids = _token_ids(slice(0, sample_rows))
+    dt = _cpu_sample(port, ids)
+    return {"value": sample_rows * SEQ_LEN / dt, "unit": "tok/s", "cores": port[3], "kind": "port",
             "sample": f"{sample_rows} row(s) x {SEQ_LEN} tokens of the config-5 batch through oracle/model.py "
                       f"(fp32/fp64 CPU restatement of the reference forward), {dt:.1f} s"}
 
@@ -134,14 +154,15 @@ def run_reference(args) -> None:
     world, rank, _ = _dist()
     if rank != 0:
         return
+    port = _cpu_port()
+    ids = _token_ids(slice(0, 1))
     for _ in range(args.warmup):
-        cpu_baseline(1) if args.warmup_full else None
-    times = []
-    for _ in range(args.steps):
-        t0 = time.perf_counter()
-        r = cpu_baseline(1)
-        times.append(time.perf_counter() - t0)
+        _cpu_sample(port, ids)
+    times = [_cpu_sample(port, ids) for _ in range(args.steps)]
     value = SEQ_LEN * len(times) / sum(times)
+    r = {"unit": "tok/s", "cores": port[3], "kind": "port",
+         "sample": f"each step: 1 row x {SEQ_LEN} tokens of the config-5 batch through oracle/model.py "
+                   "(fp32/fp64 CPU restatement of the reference forward; model built once, untimed)"}
     line = {"metric": METRIC, "impl": "reference", "value": value, "unit": "tok/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * sum(times) / len(times),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
@@ -221,6 +242,7 @@ def run_ours(args) -> None:
         barrier()
         e2e_ms = max_over_ranks(start.elapsed_time(end) / args.steps)
 
+    device_status = _lib.read_and_clear_device_status(dev)
     tokens = GLOBAL_BATCH * SEQ_LEN
     hbm, hbm_kind = _peaks()
     # dwarf_dsqg_fwd algorithmic bytes per launch (one DSQG layer over this rank's rows):
@@ -228,6 +250,19 @@ def run_ours(args) -> None:
     per_row = 8 * SEQ_LEN  # (head, token) rows per batch row
     dsqg_bytes = rows * per_row * (64 * 2 + 2 * 50 + 2 * 16 + 64 * 2 + 64 * 2)
     achieved = dsqg_bytes / (dsqg_ms * 1e-3) / 1e9 if dsqg_ms else None
+    # FP32 work of one dwarf_dsqg_fwd launch, averaged over the model's DSQG layers:
+    # 2 x 64 FMAs (q.k and p.v) per valid (query, offset) pair.
+    from dwarf_v2_b200.model import DSQGBlock
+
+    layer_groups = [blk.attn.offsets for blk in model.blocks if isinstance(blk, DSQGBlock)]
+    pairs = sum(sum(max(0, SEQ_LEN - d) for d in g) for g in layer_groups) / len(layer_groups)
+    dsqg_flops = rows * 8 * pairs * 2 * 64 * 2
+    clock = clocks.summary()
+    sm_mhz = clock["sm_mhz"] or 1965.0
+    fma_peak = 148 * 128 * 2 * sm_mhz * 1e6 / 1e12
+    fma = ({"achieved": dsqg_flops / (dsqg_ms * 1e-3) / 1e12, "peak": fma_peak, "unit": "TFLOP/s",
+            "frac": dsqg_flops / (dsqg_ms * 1e-3) / 1e12 / fma_peak, "flops_per_launch": dsqg_flops,
+            "peak_kind": "derived: 148 SMs x 128 FP32 lanes x 2 x median sampled SM clock"} if dsqg_ms else None)
     traffic = None
     prof = ROOT / "profiles" / "dsqg_fwd_traffic.json"
     if prof.is_file():
@@ -247,15 +282,21 @@ def run_ours(args) -> None:
         "gpu_launches": launches,
         "roofline": {"kernel": "dwarf_dsqg_fwd", "bound": "hbm", "achieved": achieved, "peak": hbm,
                      "peak_kind": hbm_kind, "unit": "GB/s", "frac": (achieved / hbm) if achieved else None,
-                     "traffic": traffic, "algorithmic_bytes_per_launch": dsqg_bytes, "mean_launch_ms": dsqg_ms},
-        "clocks": clocks.summary(),
+                     "traffic": traffic, "algorithmic_bytes_per_launch": dsqg_bytes, "mean_launch_ms": dsqg_ms,
+                     "fma": fma},
+        "clocks": clock,
+        "device_status": device_status,
     }
+    if device_status != 0:
+        line["invalid"] = "a kernel's bounded wait ran out (DWARF_DEVICE_TIMEOUT) during the timed steps"
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(1)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
+    if device_status != 0:
+        sys.exit(3)
 
 
 def main() -> None:
@@ -266,7 +307,6 @@ def main() -> None:
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--rows", type=int, default=None, help="override the global batch (small profiling cases)")
-    ap.add_argument("--warmup-full", action="store_true", help="reference arm: full-size warm-up steps")
     args = ap.parse_args()
     if args.rows:
         global GLOBAL_BATCH

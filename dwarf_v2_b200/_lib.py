@@ -128,6 +128,29 @@ def read_and_clear_device_status(device: torch.device) -> int:
     return value
 
 
+class DeviceTimeoutError(RuntimeError):
+    """A kernel's bounded wait ran out (DWARF_DEVICE_TIMEOUT): its outputs are not valid."""
+
+
+def check_device_status(device: torch.device | None = None) -> None:
+    """Read and clear the device status word(s); raise DeviceTimeoutError if a kernel
+    recorded a timed-out wait since the last check. Synchronises with the device.
+
+    ``device=None`` checks every device that has a status word."""
+    if device is None:
+        indices = sorted(_status_words)
+    else:
+        indices = [device.index if device.index is not None else torch.cuda.current_device()]
+    bad = []
+    for index in indices:
+        if index in _status_words and read_and_clear_device_status(torch.device("cuda", index)) != 0:
+            bad.append(index)
+    if bad:
+        raise DeviceTimeoutError(
+            f"a dwarf_b200 kernel on cuda:{bad} hit its bounded-wait limit (DWARF_DEVICE_TIMEOUT); "
+            "the results of the launches since the last check are not valid")
+
+
 class EmaScanArgs(ctypes.Structure):
     _fields_ = [
         ("version", c_i32), ("dtype", c_i32),
@@ -139,6 +162,7 @@ class EmaScanArgs(ctypes.Structure):
         ("floor_", c_f32), ("ceiling", c_f32),
         ("workspace", c_ptr), ("workspace_bytes", c_i64),
         ("device_status", c_ptr), ("init_state", c_ptr), ("final_state", c_ptr),
+        ("wait_limit", ctypes.c_uint32), ("test_tag_skew", c_i32),
     ]
 
 
@@ -322,8 +346,14 @@ def set_launch_log(log: LaunchLog | None) -> None:
 
 
 def call(name: str, args: ctypes.Structure, device: torch.device) -> None:
-    """Invoke a C entry point on the current stream of `device`; raise on error."""
+    """Invoke a C entry point on the current stream of `device`; raise on error.
+
+    Entry points with a ``device_status`` field get the device's status word
+    when the caller left it null, so every kernel with bounded waits reports a
+    timeout where ``check_device_status`` can see it."""
     lib = load()
+    if hasattr(args, "device_status") and not args.device_status:
+        args.device_status = device_status_word(device).data_ptr()
     log = _launch_log
     if log is None:
         status = getattr(lib, name)(ctypes.byref(args), stream_handle(device))

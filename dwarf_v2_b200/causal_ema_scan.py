@@ -74,7 +74,7 @@ def _workspace(device: torch.device, nbytes: int) -> torch.Tensor:
 
 def _launch(x: torch.Tensor, out: torch.Tensor, alpha: torch.Tensor, per_channel: bool,
             clamp: bool, floor: float, ceiling: float, init_state: torch.Tensor | None = None,
-            final_state: torch.Tensor | None = None) -> None:
+            final_state: torch.Tensor | None = None, *, wait_limit: int = 0, test_tag_skew: int = 0) -> None:
     lib = _lib.load()
     batch, seq_len, width = x.shape
     code = _lib.dtype_code(x.dtype)
@@ -93,6 +93,7 @@ def _launch(x: torch.Tensor, out: torch.Tensor, alpha: torch.Tensor, per_channel
         workspace=ws.data_ptr(), workspace_bytes=ws.numel(),
         device_status=_lib.device_status_word(x.device).data_ptr(),
         init_state=_lib.ptr(init_state), final_state=_lib.ptr(final_state),
+        wait_limit=int(wait_limit), test_tag_skew=int(test_tag_skew),
     )
     _lib.call("dwarf_ema_scan", args, x.device)
 

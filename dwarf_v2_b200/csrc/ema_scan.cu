@@ -25,15 +25,15 @@
 //   4. each warp rescans its tokens from its true carry-in and writes y once.
 //
 // Publication without fences: every published channel value travels in one
-// 64-bit word {value bits, tag}, written and read as a single-copy-atomic
-// 8-byte access, where tag identifies this launch. A reader spins until the
+// 64-bit scalar {value bits, tag}, written and read as one single-copy-atomic
+// b64 access, where tag identifies this launch. A reader spins until the
 // tag matches, so no __threadfence/flag pair is needed. The launch tag is kept
 // in the workspace header: each launch uses tag = header.epoch + 1 and the last
 // CTA to exit advances header.epoch, so consecutive launches never see each
 // other's records and the workspace needs zero-filling only once, before its
 // first use.
 //
-// Waits are bounded (kSpinLimit); a timed-out wait records
+// Waits are bounded (kSpinLimit polls, or the caller's wait_limit); a timed-out wait records
 // DWARF_DEVICE_TIMEOUT and continues with a zero carry instead of hanging.
 // Summation order in the look-back is fixed, so results are bitwise
 // reproducible run to run.
@@ -57,14 +57,18 @@ struct EmaWorkspace {
 inline int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
 constexpr int64_t kHeaderBytes = 256;
 
+// A record is ONE 64-bit scalar (value bits in the low word, tag in the high
+// word), stored and loaded with a single b64 access: the PTX memory model
+// makes a scalar access single-copy atomic, whereas the two halves of a
+// .v2.u32 access may be observed separately (a new tag with a stale value).
 __device__ __forceinline__ void st_rec(uint2* p, float v, uint32_t tag) {
-  asm volatile("st.relaxed.gpu.global.v2.u32 [%0], {%1, %2};" ::"l"(p), "r"(__float_as_uint(v)), "r"(tag)
-               : "memory");
+  const unsigned long long w = (unsigned long long)__float_as_uint(v) | ((unsigned long long)tag << 32);
+  asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
 }
 __device__ __forceinline__ uint2 ld_rec(const uint2* p) {
-  uint2 r;
-  asm volatile("ld.relaxed.gpu.global.v2.u32 {%0, %1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p) : "memory");
-  return r;
+  unsigned long long w;
+  asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+  return make_uint2((uint32_t)w, (uint32_t)(w >> 32));
 }
 
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
@@ -91,7 +95,7 @@ ema_scan_lookback_kernel(const T* __restrict__ x, T* __restrict__ y, int64_t seq
                          const float* __restrict__ alpha, int alpha_per_channel, int clamp, float lo,
                          float hi, EmaWorkspace ws, int64_t nseries, int64_t ncb, int64_t ntiles,
                          int32_t* device_status, const float* __restrict__ init_state,
-                         float* __restrict__ final_state) {
+                         float* __restrict__ final_state, uint32_t spin_limit, uint32_t tag_skew) {
   constexpr int C = 32 * VEC;  // channels per series
   constexpr int CH = WARPS * TS;
   constexpr bool kAsync = VEC * sizeof(T) == 16;
@@ -218,13 +222,13 @@ ema_scan_lookback_kernel(const T* __restrict__ x, T* __restrict__ y, int64_t seq
 #pragma unroll
               for (int v = 0; v < VEC; ++v) {
                 const uint2 r = ld_rec(src + v);
-                if (r.y == tag) val[k][v] = __uint_as_float(r.x);
+                if (r.y == tag + tag_skew) val[k][v] = __uint_as_float(r.x);
                 else ready = false;
               }
             }
           }
           if (__all_sync(0xffffffffu, ready)) break;
-          if (++spins > kSpinLimit) { timed_out = true; break; }
+          if (++spins > spin_limit) { timed_out = true; break; }
           __nanosleep(20);
         }
         float f[VEC];
@@ -354,8 +358,10 @@ int launch_ema_lb(const dwarf_ema_scan_args* a, const EmaPlan& p, cudaStream_t s
   int32_t* status = a->device_status;
   const float* init = a->init_state;
   float* fin = a->final_state;
-  void* params[] = {&x, &y, &seq_len, &width, &sxb, &sxn, &sxd, &syb, &syn, &syd, &alpha,
-                    &per_channel, &clamp, &lo, &hi, &ws, &nseries, &ncb, &ntiles, &status, &init, &fin};
+  uint32_t spin_limit = a->wait_limit != 0 ? a->wait_limit : kSpinLimit;
+  uint32_t tag_skew = a->test_tag_skew != 0 ? 1u : 0u;
+  void* params[] = {&x, &y, &seq_len, &width, &sxb, &sxn, &sxd, &syb, &syn, &syd, &alpha, &per_channel,
+                    &clamp, &lo, &hi, &ws, &nseries, &ncb, &ntiles, &status, &init, &fin, &spin_limit, &tag_skew};
   if (cudaLaunchCooperativeKernel((const void*)kernel, dim3((unsigned)grid), dim3(WARPS * 32), params, smem,
                                   stream) != cudaSuccess)
     return DWARF_ERR_LAUNCH;

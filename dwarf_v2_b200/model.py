@@ -30,7 +30,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from . import gemm, glue
+from . import _lib, gemm, glue
 from .causal_ema_scan import bounded_ema_factor, causal_ema_scan, inverse_bounded_ema_factor
 from .dsqg_attention_v22 import ALL_OFFSETS, R_PLANES, DSQGAttentionV19
 from .hierarchical_sparse_attn_v18_hisa import HierarchicalSparseAttentionV16HISACausal, chunk_representatives
@@ -610,6 +610,12 @@ class DwarfForCausalLM(nn.Module):
     def capture_decode(self, state: "DecodeState") -> "DecodeGraph":
         """A CUDA graph of one decode step over ``state``'s buffers (see DecodeGraph)."""
         return DecodeGraph(self, state)
+
+    def check_device_status(self) -> None:
+        """Raise ``DeviceTimeoutError`` if a kernel of this model's device hit its bounded-wait
+        limit since the last check (the outputs of the launches since then are invalid).
+        Synchronises with the device; call it after a forward, not inside a captured graph."""
+        _lib.check_device_status(self.embedding.weight.device)
 
     def forward(self, input_ids: torch.Tensor, *, return_hidden: bool = False, return_auxiliary: bool = False):
         hidden, auxiliary = self.forward_hidden(input_ids, return_auxiliary=True)

@@ -92,6 +92,14 @@ typedef struct {
   const float* init_state;    /* optional fp32 [batch, width]: y[-1] (else 0) */
   float* final_state;         /* optional fp32 [batch, width]: the fp32 state
                                  after token seq_len-1 (may not alias init)  */
+  uint32_t wait_limit;        /* polls before a look-back wait gives up and
+                                 records DWARF_DEVICE_TIMEOUT (0: the default,
+                                 about 0.3-1 s)                              */
+  int32_t test_tag_skew;      /* testing only, 0 in normal use: nonzero makes
+                                 readers expect a record tag that no writer
+                                 produces, so every look-back wait runs out
+                                 (exercises the bounded-wait path without a
+                                 fault; the output is then not valid)        */
 } dwarf_ema_scan_args;
 
 int64_t dwarf_ema_scan_workspace_bytes(int64_t batch, int64_t seq_len, int64_t width,

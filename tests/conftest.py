@@ -21,3 +21,19 @@ def pytest_collection_modifyitems(config, items):
     for item in items:
         if "gpu" in item.keywords:
             item.add_marker(skip)
+
+
+@pytest.fixture(autouse=True)
+def _device_status_stays_clear(request):
+    """After every GPU test: no kernel hit its bounded-wait limit (the device status
+    word is read and cleared; a timeout fails the test at teardown)."""
+    yield
+    if "gpu" not in request.keywords:
+        return
+    import torch
+
+    if not torch.cuda.is_available():
+        return
+    from dwarf_v2_b200 import _lib
+
+    _lib.check_device_status()

@@ -76,3 +76,32 @@ def test_model_payload_round_trip_and_validation():
         load_weights(dst, {"kind": KIND, "model": wrong})
     for k, v in dst.state_dict().items():  # nothing was loaded by the failed calls
         assert torch.equal(v, snapshot[k]), k
+
+
+def test_resume_payload_is_held_to_the_reference_checks():
+    """A dwarf-55m-resume-v1 payload: a tensor whose dtype differs from the model's is
+    refused (restore_checkpoint, train/train_dwarf.py:999-1002) unless cast=True; a
+    stray key and a legacy-layout key are refused before any migration (the reference
+    compares the key sets first, :996-997); a bare state dict still migrates legacy keys."""
+    from dwarf_v2_b200.checkpoint import KIND, load_weights
+    from dwarf_v2_b200.model import DwarfConfig, DwarfForCausalLM
+
+    src = DwarfForCausalLM(DwarfConfig(init_seed=3))
+    dst = DwarfForCausalLM()
+    snapshot = {k: v.clone() for k, v in dst.state_dict().items()}
+    half = {k: v.to(torch.bfloat16) if v.is_floating_point() else v for k, v in src.state_dict().items()}
+    with pytest.raises(ValueError, match="tensor does not match"):
+        load_weights(dst, {"kind": KIND, "model": half})
+    stray = dict(src.state_dict())
+    stray["blocks.0.attn.not_a_parameter"] = torch.zeros(1)
+    with pytest.raises(ValueError, match="keys do not match"):
+        load_weights(dst, {"kind": KIND, "model": stray})
+    legacy = dict(src.state_dict())
+    legacy["blocks.0.attn.qkv_proj.weight"] = legacy.pop("blocks.0.attn.qkvg_proj.weight")
+    with pytest.raises(ValueError, match="keys do not match"):
+        load_weights(dst, {"kind": KIND, "model": legacy})
+    for k, v in dst.state_dict().items():  # nothing was loaded by the refused payloads
+        assert torch.equal(v, snapshot[k]), k
+    load_weights(dst, {"kind": KIND, "model": half}, cast=True)
+    for k, v in dst.state_dict().items():
+        assert torch.equal(v, half[k].to(v.dtype)), k

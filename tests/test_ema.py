@@ -174,3 +174,26 @@ def test_kernel_continuation_matches_one_pass(split):
     torch.testing.assert_close(state, full[:, split - 1].float(), atol=1e-6, rtol=0)
     torch.testing.assert_close(torch.cat([head, tail], 1), full, atol=1e-5, rtol=0)
     torch.testing.assert_close(end_state, full_state, atol=1e-5, rtol=0)
+
+
+@pytest.mark.gpu
+def test_lookback_wait_runs_out_reports_timeout_and_context_stays_usable():
+    """Bounded-wait path without a fault: with test_tag_skew the look-back waits for
+    records that no writer produces, gives up after the host-set poll limit and records
+    DWARF_DEVICE_TIMEOUT in the status word; check_device_status raises and clears it,
+    and the next scan on the same context is exact."""
+    from dwarf_v2_b200 import _lib, check_device_status
+    from dwarf_v2_b200.causal_ema_scan import _launch, causal_ema_scan_per_channel
+
+    g = torch.Generator().manual_seed(11)
+    x = torch.randn(2, 1024, 256, generator=g).cuda()
+    alpha = torch.rand(256, generator=g).cuda()
+    check_device_status(x.device)  # a clean start
+    out = torch.empty_like(x)
+    _launch(x, out, alpha, True, False, 0.0, 1.0, wait_limit=64, test_tag_skew=1)
+    with pytest.raises(_lib.DeviceTimeoutError):
+        check_device_status(x.device)
+    y = causal_ema_scan_per_channel(x, alpha).cpu()
+    ref = oracle_ema.ema_scan(x.cpu().numpy(), alpha.cpu().numpy())
+    assert np.abs(y.numpy() - ref).max() < 1e-5
+    check_device_status(x.device)
