@@ -478,18 +478,39 @@ class DwarfForCausalLM(nn.Module):
         blocks = list(self.blocks)
         x, n = glue.embed_rmsnorm(input_ids, emb, blocks[0].norm1.weight.detach())
         auxiliary = x.new_zeros(())
-        for i, block in enumerate(blocks):
-            next_norm = blocks[i + 1].norm1.weight if i + 1 < len(blocks) else self.norm.weight
-            if isinstance(block, GlobalMixerBlock):
-                attn = block.attn
-                kd, vd = block.packet(n)
-                lengths = torch.full((x.shape[0],), x.shape[1], dtype=torch.int32, device=x.device)
-                projected, gate, _ = attn.forward_parts(n, (kd, vd), lengths)
-                x, n2 = glue.add_rmsnorm(x, block.norm2.weight.detach(), addend=projected, gate=gate)
-            else:
-                x, n2 = glue.add_rmsnorm(x, block.norm2.weight.detach(), addend=block.attn(n))
-            x, n = block.ffn.forward_add_rmsnorm(n2, x, next_norm.detach())
+        for i in range(len(blocks)):
+            x, n = self._prefill_block(i, x, n)
         return (n, auxiliary) if return_auxiliary else n
+
+    def _prefill_block(self, i: int, x: torch.Tensor, n: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        """Block ``i`` of the inference prefill: residual stream ``x`` and its norm1 output ``n``
+        in; the block output (``x`` is updated in place) and the next norm's output out."""
+        blocks = self.blocks
+        block = blocks[i]
+        next_norm = blocks[i + 1].norm1.weight if i + 1 < len(blocks) else self.norm.weight
+        if isinstance(block, GlobalMixerBlock):
+            attn = block.attn
+            kd, vd = block.packet(n)
+            lengths = torch.full((x.shape[0],), x.shape[1], dtype=torch.int32, device=x.device)
+            projected, gate, _ = attn.forward_parts(n, (kd, vd), lengths)
+            x, n2 = glue.add_rmsnorm(x, block.norm2.weight.detach(), addend=projected, gate=gate)
+        else:
+            x, n2 = glue.add_rmsnorm(x, block.norm2.weight.detach(), addend=block.attn(n))
+        return block.ffn.forward_add_rmsnorm(n2, x, next_norm.detach())
+
+    def prefill_block(self, index: int, x: torch.Tensor) -> torch.Tensor:
+        """Output of block ``index`` (reference train/train_dwarf.py:320-322 / :356-364) for the
+        residual-stream input ``x`` [B, T, D] bf16, through the fused kernels ``forward_hidden``
+        runs (inference only): per-block, teacher-forced parity with the reference's blocks."""
+        if not x.is_cuda:
+            raise RuntimeError("dwarf_v2_b200 runs on CUDA tensors only (no CPU fallback)")
+        if _wants_grad(self):
+            raise NotImplementedError("prefill_block is inference-only: call .eval() and run under torch.no_grad()")
+        if x.dtype != torch.bfloat16 or x.dim() != 3:
+            raise ValueError("prefill_block takes the bf16 residual stream [B, T, D]")
+        x = x.contiguous().clone()
+        n = glue.rmsnorm(x, self.blocks[index].norm1.weight.detach())
+        return self._prefill_block(index, x, n)[0]
 
     def forward_lse(self, input_ids: torch.Tensor, labels: torch.Tensor | None = None):
         """Per-token (logsumexp, argmax, cross entropy vs ``labels`` or None), each [B, T], from the

@@ -1,10 +1,10 @@
 """Generates the golden fixtures in tests/golden/ by running the REFERENCE code.
 
-Run in a container that has the reference checkout (path in DWARF_REFERENCE_DIR,
-default ``/root/reference``); the fixtures it writes are committed and the
-tests read only those files, so nothing at test time needs the reference.
+Run where a checkout of the reference exists, with its path in the required
+environment variable DWARF_REFERENCE_DIR; the fixtures it writes are committed
+and the tests read only those files, so nothing at test time needs the reference.
 
-    python tests/golden/make_golden.py [ema|dsqg|hisa|model|checkpoint|all]
+    DWARF_REFERENCE_DIR=<checkout> python tests/golden/make_golden.py [ema|dsqg|hisa|model|model_blocks|checkpoint|all]
 
 Each fixture is an ``.npz`` holding the seeded inputs and the reference output
 of one call, named for the reference function it exercises. bf16 tensors are
@@ -22,10 +22,12 @@ import torch
 import torch.nn.functional as F
 
 HERE = Path(__file__).resolve().parent
-REFERENCE = Path(os.environ.get("DWARF_REFERENCE_DIR", "/root/reference"))
+REFERENCE = Path(os.environ["DWARF_REFERENCE_DIR"]) if os.environ.get("DWARF_REFERENCE_DIR") else None
 
 
 def _import_reference():
+    if REFERENCE is None or not (REFERENCE / "kernels").is_dir():
+        raise SystemExit("set DWARF_REFERENCE_DIR to a checkout of the reference (kernels/, train/)")
     for sub in ("kernels", "train"):
         path = str(REFERENCE / sub)
         if path not in sys.path:
@@ -353,6 +355,17 @@ def make_hisa() -> None:
          top_chunk_idx=meta.top_chunk_idx, route=route)
 
     # Whole module (eval, fp32, with an EMA/NPCI kv_inject packet), head_dim 64.
+    module, x, kd, vd = _hisa_module_case(ref)
+    with torch.no_grad():
+        y = module(x, kv_inject=(kd, vd))
+    state = {f"state.{k}": val for k, val in module.state_dict().items()}
+    save("hisa_module_eval", x=x, key_delta=kd, value_delta=vd, y=y, **state)
+    make_hisa_module_bf16()
+
+
+def _hisa_module_case(ref):
+    """The module-level HISA case: seeded module with non-trivial adapters, route prior and
+    NPCI angles, a bf16-valued input and an fp32 kv_inject packet."""
     torch.manual_seed(4)
     module = ref.HierarchicalSparseAttentionV16HISACausal(
         D=128, H=2, hd=64, chunk_size=64, top_k_chunks=4, hisa_top_m_tokens=64, local_window=64,
@@ -368,10 +381,20 @@ def make_hisa() -> None:
     x = torch.randn(2, 200, 128, generator=gen).to(torch.bfloat16).float()
     kd = torch.randn(2, 2, 200, 64, generator=gen) * 0.5
     vd = torch.randn(2, 2, 200, 64, generator=gen) * 0.5
+    return module, x, kd, vd
+
+
+def make_hisa_module_bf16() -> None:
+    """The module-level HISA case run by the reference in bf16 (module.to(bfloat16), bf16
+    input and packet), the precision the engine computes in: hisa_module_eval_bf16."""
+    _import_reference()
+    import hierarchical_sparse_attn_v18_hisa as ref
+
+    module, x, kd, vd = _hisa_module_case(ref)
+    module = module.to(torch.bfloat16)
     with torch.no_grad():
-        y = module(x, kv_inject=(kd, vd))
-    state = {f"state.{k}": val for k, val in module.state_dict().items()}
-    save("hisa_module_eval", x=x, key_delta=kd, value_delta=vd, y=y, **state)
+        y = module(x.to(torch.bfloat16), kv_inject=(kd.to(torch.bfloat16), vd.to(torch.bfloat16)))
+    save("hisa_module_eval_bf16", y=y)
 
 
 def make_hisa_backward() -> None:
@@ -646,6 +669,68 @@ def make_model() -> None:
     save("model_prefill_b1_t2048", **out)
 
 
+BLOCK_ROWS = slice(15, 2048, 16)  # output rows kept per block (128 rows, the last row included)
+
+
+def make_model_blocks() -> None:
+    """Per-block parity fixtures of the reference DwarfForCausalLM (seeded init), B=1, T=2048.
+
+    Each of the 10 blocks (train/train_dwarf.py:320-322 DSQG, :356-364 HISA) runs
+    on its own seeded input, randn(seed 100 + i) times the RMS of the block's real
+    input in the reference bf16 prefill of the model_prefill token ids (the
+    residual stream grows from 0.02 to ~0.3 over the blocks), cast to bf16.
+    Stored per block, at rows BLOCK_ROWS: the bf16 model's block output, the fp32
+    model's block output on the same (bf16-valued) input, and the bf16 model's
+    block output with q6 round-tripped K/V in its DSQG attention (oracle/q6.py;
+    DSQG blocks only). The inputs are regenerated by the test from the stored
+    RMS, so the fixture stays small.
+    """
+    _import_reference()
+    sys.path.insert(0, str(HERE.parent.parent))
+    import dsqg_attention_v22 as ref_dsqg
+    import train_dwarf as td
+
+    from oracle import q6 as oq6
+
+    torch.set_num_threads(max(1, os.cpu_count() or 1))
+    m32 = td.DwarfForCausalLM(td.DwarfConfig()).eval()
+    m16 = td.DwarfForCausalLM(td.DwarfConfig()).eval().to(torch.bfloat16)
+    g = torch.Generator().manual_seed(0)
+    ids = torch.randint(57, 32768, (1, 2048), generator=g)
+    out = {"rows": torch.arange(2048)[BLOCK_ROWS]}
+    original = ref_dsqg.dsqg_attention_v18_grouped
+
+    def fake_q6(q, k, v, *args, **kwargs):
+        def rt(t):
+            codes, scales = oq6.pack(t.float().numpy())
+            return torch.from_numpy(oq6.unpack(codes, scales)).to(t.dtype)
+        return original(q, rt(k), rt(v), *args, **kwargs)
+
+    def run(block, x):
+        y = block(x)
+        return y[0] if isinstance(y, tuple) else y
+
+    with torch.no_grad():
+        x = m16.embedding(ids)
+        rms = []
+        for block in m16.blocks:
+            rms.append(float(x.float().square().mean().sqrt()))
+            x = run(block, x)
+        out["input_rms"] = torch.tensor(rms, dtype=torch.float64)
+        for i, (b16, b32) in enumerate(zip(m16.blocks, m32.blocks)):
+            xin = (torch.randn(1, 2048, 512, generator=torch.Generator().manual_seed(100 + i)) * rms[i])
+            xin = xin.to(torch.bfloat16)
+            out[f"block{i}_bf16"] = run(b16, xin)[0, BLOCK_ROWS]
+            out[f"block{i}_f32"] = run(b32, xin.float())[0, BLOCK_ROWS]
+            if not isinstance(b16, td.GlobalMixerBlock):
+                ref_dsqg.dsqg_attention_v18_grouped = fake_q6
+                try:
+                    out[f"block{i}_bf16_q6"] = run(b16, xin)[0, BLOCK_ROWS]
+                finally:
+                    ref_dsqg.dsqg_attention_v18_grouped = original
+    save("model_blocks_b1_t2048", **out)
+
+
 def make_checkpoint() -> None:
     """Legacy-key migration of the reference modules' _load_from_state_dict.
 
@@ -712,7 +797,7 @@ def make_checkpoint() -> None:
 
 def main(argv: list[str]) -> None:
     which = argv[1] if len(argv) > 1 else "all"
-    makers = {"ema": make_ema, "ema_bwd": make_ema_backward, "dsqg": make_dsqg, "dsqg_bwd": make_dsqg_backward, "dsqg_module_grad": make_dsqg_module_grad, "hisa": make_hisa, "hisa_bwd": make_hisa_backward, "hisa_bwd_edges": make_hisa_backward_edges, "hisa_module_grad": make_hisa_module_grad, "model": make_model, "model_train": make_model_train,
+    makers = {"ema": make_ema, "ema_bwd": make_ema_backward, "dsqg": make_dsqg, "dsqg_bwd": make_dsqg_backward, "dsqg_module_grad": make_dsqg_module_grad, "hisa": make_hisa, "hisa_module_bf16": make_hisa_module_bf16, "hisa_bwd": make_hisa_backward, "hisa_bwd_edges": make_hisa_backward_edges, "hisa_module_grad": make_hisa_module_grad, "model": make_model, "model_blocks": make_model_blocks, "model_train": make_model_train,
               "checkpoint": make_checkpoint}
     for name, maker in makers.items():
         if which in ("all", name):

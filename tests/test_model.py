@@ -105,3 +105,39 @@ def test_cpu_oracle_matches_reference_fp32_logits():
     logits = omodel.prefill(DwarfForCausalLM().state_dict(), g["input_ids"], all_offsets=ALL_OFFSETS)
     err = np.abs(logits[0, g["positions"]].numpy() - g["logits_f32"].numpy())
     assert err.max() < 2e-3, err.max()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("kv_cache", ["bf16", "q6"])
+def test_each_block_matches_the_reference_block_at_the_north_star_bar(kv_cache):
+    """Teacher-forced per-block parity (reference train/train_dwarf.py:320-322 DSQG,
+    :356-364 HISA; fixture tests/golden/model_blocks_b1_t2048.npz): every engine block
+    gets the input its reference block got (seeded randn scaled to the RMS of that
+    block's real input in the reference bf16 prefill, T=2048) and its output must be
+    within 2e-2 max-abs and 1e-2 mean-relative of the reference bf16 block's output;
+    on the q6 cache, of the reference block run on q6-round-tripped K/V. The computed
+    part (output - input) must also stay within 2x the reference bf16 block's own
+    error against its fp32 run (+ 2e-3), i.e. no worse than the reference's bf16 path."""
+    from dwarf_v2_b200.model import DwarfForCausalLM
+
+    g = load("model_blocks_b1_t2048")
+    model = DwarfForCausalLM(kv_cache=kv_cache).eval().to(torch.bfloat16).cuda()
+    rows = g["rows"]
+    report = []
+    with torch.no_grad():
+        for i in range(len(model.blocks)):
+            gen = torch.Generator().manual_seed(100 + i)
+            xin = (torch.randn(1, 2048, 512, generator=gen) * float(g["input_rms"][i])).to(torch.bfloat16)
+            out = model.prefill_block(i, xin.cuda())[0, rows.cuda()].float().cpu().numpy()
+            key = f"block{i}_bf16_q6" if kv_cache == "q6" and f"block{i}_bf16_q6" in g else f"block{i}_bf16"
+            ref = g[key].float().numpy()
+            mx, mean = _err(out, ref)
+            x0 = xin[0, rows].float().numpy()
+            d_out, d_ref16, d_ref32 = out - x0, g[f"block{i}_bf16"].float().numpy() - x0, g[f"block{i}_f32"].numpy() - x0
+            report.append((i, round(mx, 5), round(mean, 5)))
+            assert mx <= 2e-2 and mean <= 1e-2, (kv_cache, i, mx, mean)
+            if kv_cache == "bf16":
+                e_out, e_ref = np.abs(d_out - d_ref32), np.abs(d_ref16 - d_ref32)
+                assert e_out.max() <= 2 * e_ref.max() + 2e-3, (i, e_out.max(), e_ref.max())
+                assert e_out.mean() <= 2 * e_ref.mean() + 2e-4, (i, e_out.mean(), e_ref.mean())
+    print(kv_cache, report)
