@@ -250,7 +250,7 @@ class HisaAttnArgs(ctypes.Structure):
         local_value:ptr, slvb:i64, slvh:i64, slvn:i64, global_key:ptr, sgkb:i64, sgkh:i64, sgkn:i64,
         global_value:ptr, sgvb:i64, sgvh:i64, sgvn:i64, top_chunk_idx:ptr, route:ptr,
         lengths:ptr, out:ptr, sob:i64, soh:i64, son:i64, tile_begin:i64, tile_count:i64, pos:ptr,
-        lse:ptr""")
+        lse:ptr, device_status:ptr""")
 
 
 class HisaRouteArgs(ctypes.Structure):

@@ -686,6 +686,412 @@ hisa_attn_kernel(const AttnParams p, const __grid_constant__ AttnMaps maps, int3
   if (*abort_flag && lane == 0 && status != nullptr) atomicExch(status, DWARF_DEVICE_TIMEOUT);
 }
 
+// ---------------------------------------------------------------- tcgen05 tile attention
+//
+// The same CTA (8 selector tiles = 128 queries of one (b, h)) and chunk list
+// as hisa_attn_kernel, with the dense tile products on the 5th-generation
+// tensor cores and their accumulators in tensor memory:
+//   warp 0      chunk list (once), then TMA producer: the Q tile (128 rows)
+//               once, and each chunk's K and V boxes (64 rows x 64 dims,
+//               128-byte swizzle) into a kTcStages ring;
+//   warp 1      allocates 256 TMEM columns and issues, from one thread,
+//                 S_e = Q . K_e^T   (M = 128 queries, N = 64 keys, K = 64)
+//                 into S[e % 2] (columns 0 / 64), and, once the softmax has
+//                 written P_e, O_e = P_e . V_e (M = 128, N = 64 dims,
+//                 K = 64 keys; V read in place as an MN-major operand) into
+//                 O[e % 2] (columns 128 / 192);
+//   warps 2-5   one query row per thread (TMEM lane = row): read S_e with
+//               tcgen05.ld, apply the lane masks, the route prior and the
+//               scale, run the online-softmax update, write P_e (bf16) to a
+//               swizzled shared-memory tile, and fold O_e into the fp32 row
+//               accumulator in registers (O = alpha_e * O + O_e) one chunk
+//               behind, so S_{e+1} and O_e overlap the softmax of chunk e.
+// A warp skips the chunks none of its 32 rows attend, and a row folds only
+// the chunks it attended: a tile meets its own chunks in list order whichever
+// tiles share the CTA, as in hisa_attn_kernel (windowed launches reproduce
+// full ones bit for bit).
+// Every wait is bounded; a timeout aborts all roles, drains the copies and
+// MMAs in flight, frees tensor memory and records DWARF_DEVICE_TIMEOUT.
+constexpr int kTcStages = 3;
+constexpr int kTcThreads = 192;
+constexpr uint32_t kTcCols = 256;
+
+struct TcSmem {
+  static constexpr uint32_t q = 0;                                 // 128 rows x 128 B
+  static constexpr uint32_t ring = q + 128 * 128;                  // stages: K box, V box
+  static constexpr uint32_t pbuf = ring + kTcStages * kStageBytes;  // P[2]: 128 rows x 128 B
+  static constexpr uint32_t route = pbuf + 2 * 128 * 128;          // [128 rows][4] fp32
+  static constexpr uint32_t entries = route + 128 * kTopK * 4;
+  static constexpr uint32_t bars = (entries + kMaxEntries * sizeof(ChunkEntry) + 7) / 8 * 8;
+  // q, full[S], empty[S], s_full[2], p_full[2], o_full[2], o_empty[2], drain
+  static constexpr uint32_t misc = bars + (2 + 2 * kTcStages + 8) * 8;
+  static constexpr uint32_t bytes = misc + 16 + 4 * 32 + 1024;  // + alignment slack
+};
+
+__device__ __forceinline__ uint64_t tc_desc(uint32_t saddr) {
+  // 128-byte swizzle, 8-row (1024-byte) atoms; for the K-major operands the
+  // stride field steps between 8-row groups of M/N, for the MN-major V between
+  // 8-row groups of K (keys). The leading field is unused (one atom along
+  // K for K-major, one 64-element atom along N for MN-major).
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+  d |= (uint64_t)1 << 16;
+  d |= (uint64_t)(1024 >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+// kind::f16 instruction descriptor: bf16 A and B, fp32 D, M x N; b_mn: B is MN-major.
+__host__ __device__ constexpr uint32_t tc_idesc(int M, int N, bool b_mn) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | (b_mn ? (1u << 16) : 0u) | ((uint32_t)(N >> 3) << 17) |
+         ((uint32_t)(M >> 4) << 24);
+}
+__device__ __forceinline__ void tc_mma1(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile("{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\ntcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}"
+               ::"r"(tmem_d), "l"(a), "l"(b), "r"(idesc), "r"(acc) : "memory");
+}
+__device__ __forceinline__ void tc_commit1(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void tc_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void mbar_arrive1(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+// 32 consecutive fp32 columns of this thread's TMEM lane (load and wait in one statement).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+      "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr) : "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// (d0, d1) = (a0, a1) * (b0, b1) + (c0, c1) as one packed fp32x2 FMA.
+__device__ __forceinline__ void ffma2(float& d0, float& d1, float a0, float a1, float b0, float b1, float c0,
+                                      float c1) {
+  asm("{\n.reg .b64 pa, pb, pc;\nmov.b64 pa, {%2, %3};\nmov.b64 pb, {%4, %5};\nmov.b64 pc, {%6, %7};\n"
+      "fma.rn.f32x2 pc, pa, pb, pc;\nmov.b64 {%0, %1}, pc;\n}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+}
+
+struct TcMaps {
+  CUtensorMap q, lk, lv, gk, gv;
+};
+
+__global__ void __launch_bounds__(kTcThreads, 2)
+hisa_attn_tc_kernel(const AttnParams p, const __grid_constant__ TcMaps maps, int32_t* status) {
+  extern __shared__ unsigned char smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  unsigned char* smem = smem_raw + (base - raw);
+  float* s_route = reinterpret_cast<float*>(smem + TcSmem::route);
+  ChunkEntry* s_ent = reinterpret_cast<ChunkEntry*>(smem + TcSmem::entries);
+  const uint32_t bar_q = base + TcSmem::bars;
+  const uint32_t bar_full = bar_q + 8, bar_empty = bar_full + 8 * kTcStages;
+  const uint32_t bar_sfull = bar_empty + 8 * kTcStages, bar_pfull = bar_sfull + 16;
+  const uint32_t bar_ofull = bar_pfull + 16, bar_oempty = bar_ofull + 16, bar_drain = bar_oempty + 16;
+  int* s_count = reinterpret_cast<int*>(smem + TcSmem::misc);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + TcSmem::misc + 4);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + TcSmem::misc + 8);
+  int* s_top = reinterpret_cast<int*>(smem + TcSmem::misc + 16);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int h = blockIdx.y, b = blockIdx.z;
+  int64_t tb, te;
+  window_of(p, tb, te);
+  const int64_t gb = p.pos != nullptr ? tb - tb % kCtaTiles : p.grid_begin;
+  const int64_t T0 = (gb + (int64_t)blockIdx.x * kCtaTiles) * kTile;
+  if (T0 / kTile >= te) return;  // whole CTA, before any barrier or allocation
+  auto in_window = [&](int64_t t) { return t >= tb && t < te; };
+  const int64_t vlen = imin64((int64_t)p.lengths[b], p.T);
+  const int32_t* top = p.top + ((int64_t)b * p.H + h) * p.tiles * p.k_slots;
+
+  // ---- the CTA's 32 (tile, slot) selections, then its chunk list (as hisa_attn_kernel)
+  if (warp == 0) {
+    const int i = lane / kTopK, k = lane % kTopK;
+    const int64_t t = T0 / kTile + i;
+    s_top[lane] = (in_window(t) && k < p.k_slots) ? top[t * p.k_slots + k] : -1;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    int n = 0;
+    if (lane == 0) {
+      for (int k = 0; k < 3; ++k) {
+        const int64_t row0 = T0 - 64 + 64 * k;
+        if (row0 >= p.T || row0 + 64 <= 0) continue;
+        ChunkEntry e;
+        e.row0 = (int32_t)row0;
+        e.global = 0;
+        e.mask = 0;
+        for (int i = 0; i < kCtaTiles; ++i) {
+          e.slot[i] = -1;
+          const int64_t t0 = T0 + kTile * i;
+          if (t0 < p.T && in_window(t0 / kTile) && t0 - 64 < row0 + 64 && row0 < t0 + kTile)
+            e.mask |= (uint8_t)(1u << i);
+        }
+        if (e.mask) s_ent[n++] = e;
+      }
+    }
+    n = __shfl_sync(0xffffffffu, n, 0);
+    const int c = s_top[lane];
+    const unsigned same = __match_any_sync(0xffffffffu, c);
+    const bool leader = c >= 0 && (__ffs(same) - 1) == lane;
+    const unsigned leaders = __ballot_sync(0xffffffffu, leader);
+    int rank = 0;
+    for (int j = 0; j < 32; ++j) {
+      const int cj = __shfl_sync(0xffffffffu, c, j);
+      rank += ((leaders >> j) & 1u) && cj < c;
+    }
+    if (leader) {
+      ChunkEntry e;
+      e.row0 = c * kChunk;
+      e.global = 1;
+      e.mask = 0;
+      for (int k = 0; k < kCtaTiles; ++k) e.slot[k] = -1;
+      for (unsigned m = same; m; m &= m - 1) {
+        const int ln = __ffs(m) - 1;
+        e.mask |= (uint8_t)(1u << (ln / kTopK));
+        e.slot[ln / kTopK] = (int8_t)(ln % kTopK);
+      }
+      s_ent[n + rank] = e;
+    }
+    if (lane == 0) {
+      *s_count = n + __popc(leaders);
+      *abort_flag = 0;
+      mbar_init(bar_q, 1);
+      for (int s = 0; s < kTcStages; ++s) {
+        mbar_init(bar_full + 8 * s, 1);
+        mbar_init(bar_empty + 8 * s, 1);
+      }
+      for (int i = 0; i < 2; ++i) {
+        mbar_init(bar_sfull + 8 * i, 1);
+        mbar_init(bar_pfull + 8 * i, 128);
+        mbar_init(bar_ofull + 8 * i, 1);
+        mbar_init(bar_oempty + 8 * i, 128);
+      }
+      mbar_init(bar_drain, 1);
+      asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+  } else if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kTcCols) : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  for (int x = threadIdx.x; x < kCtaTiles * 16 * kTopK; x += blockDim.x) {
+    const int64_t row = T0 + x / kTopK;
+    s_route[x] = row < p.T ? __bfloat162float(p.route[(((int64_t)b * p.H + h) * p.T + row) * kTopK + x % kTopK]) : 0.0f;
+  }
+  tc_before();
+  __syncthreads();
+  tc_after();
+  const int n_ent = *s_count;
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer
+    if (lane == 0) {
+      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar_q), "r"(128 * 128) : "memory");
+      tma_load_4d(base + TcSmem::q, &maps.q, 0, (int)T0, h, b, bar_q);
+      tma_load_4d(base + TcSmem::q + 64 * 128, &maps.q, 0, (int)T0 + 64, h, b, bar_q);
+      int issued = 0;
+      for (int e = 0; e < n_ent; ++e) {
+        const int s = e % kTcStages;
+        if (!mbar_wait(bar_empty + 8 * s, ((uint32_t)(e / kTcStages) & 1u) ^ 1u, abort_flag)) break;
+        const uint32_t dst = base + TcSmem::ring + s * kStageBytes;
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar_full + 8 * s),
+                     "r"(kStageBytes) : "memory");
+        const ChunkEntry& en = s_ent[e];
+        tma_load_4d(dst, en.global ? &maps.gk : &maps.lk, 0, en.row0, h, b, bar_full + 8 * s);
+        tma_load_4d(dst + kStageBytes / 2, en.global ? &maps.gv : &maps.lv, 0, en.row0, h, b, bar_full + 8 * s);
+        issued = e + 1;
+      }
+      // Leave no copy in flight: the Q tile and the last kTcStages issued chunks
+      // (every earlier one was consumed, hence landed) have arrived.
+      for (uint32_t it = 0; it < kWait && !mbar_try(bar_q, 0); ++it) {}
+      for (int e = issued > kTcStages ? issued - kTcStages : 0; e < issued; ++e)
+        for (uint32_t it = 0; it < kWait && !mbar_try(bar_full + 8 * (e % kTcStages), (uint32_t)(e / kTcStages) & 1u);
+             ++it) {}
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ---------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t kIdS = tc_idesc(128, 64, false), kIdO = tc_idesc(128, 64, true);
+      const uint32_t q_s = base + TcSmem::q;
+      bool ok = mbar_wait(bar_q, 0, abort_flag);
+      auto issue_s = [&](int e) -> bool {
+        const int s = e % kTcStages;
+        if (!mbar_wait(bar_full + 8 * s, (uint32_t)(e / kTcStages) & 1u, abort_flag)) return false;
+        tc_after();
+        const uint32_t k_s = base + TcSmem::ring + s * kStageBytes;
+        const uint32_t d = tmem + (uint32_t)(e & 1) * 64u;
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) tc_mma1(d, tc_desc(q_s + kk * 32), tc_desc(k_s + kk * 32), kIdS, kk != 0);
+        tc_commit1(bar_sfull + 8 * (e & 1));
+        return true;
+      };
+      if (ok) tc_after();
+      for (int e = 0; ok && e < n_ent && e < 2; ++e) ok = issue_s(e);
+      for (int e = 0; ok && e < n_ent; ++e) {
+        const int buf = e & 1;
+        const uint32_t ph = (uint32_t)(e >> 1) & 1u;
+        if (!(ok = mbar_wait(bar_pfull + 8 * buf, ph, abort_flag))) break;
+        if (!(ok = mbar_wait(bar_oempty + 8 * buf, ph ^ 1u, abort_flag))) break;
+        tc_after();
+        const int s = e % kTcStages;
+        const uint32_t v_s = base + TcSmem::ring + s * kStageBytes + kStageBytes / 2;
+        const uint32_t p_s = base + TcSmem::pbuf + buf * 128 * 128;
+        const uint32_t d = tmem + 128u + (uint32_t)buf * 64u;
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) tc_mma1(d, tc_desc(p_s + kk * 32), tc_desc(v_s + kk * 2048), kIdO, kk != 0);
+        tc_commit1(bar_ofull + 8 * buf);
+        tc_commit1(bar_empty + 8 * s);
+        if (e + 2 < n_ent) ok = issue_s(e + 2);  // S[e % 2] was read before P_e was published
+      }
+      // Drain: every MMA issued so far has completed once this commit lands.
+      tc_commit1(bar_drain);
+      for (uint32_t it = 0; it < kWait && !mbar_try(bar_drain, 0); ++it) {}
+    }
+    __syncwarp();
+  } else {
+    // ---------------- softmax / accumulation: one query row per thread
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const int tile = row >> 4;
+    const int64_t n = T0 + row;
+    const bool tile_ok = T0 + kTile * tile < p.T && in_window((T0 + kTile * tile) / kTile);
+    const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
+    const int ni = (int)n, vleni = (int)vlen;
+    float o[64];
+#pragma unroll
+    for (int i = 0; i < 64; ++i) o[i] = 0.0f;
+    float m = -INFINITY, l = 0.0f, alpha_prev = 1.0f;
+    bool act_prev = false, ok = true;
+    constexpr float kC1 = 0.125f * kLog2e;
+    // Waits and tensor-memory loads are warp-wide (tcgen05.ld is .sync.aligned):
+    // every lane polls, and the warp goes on only if all of them saw the phase.
+    auto warp_wait = [&](uint32_t bar, uint32_t parity) -> bool {
+      return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag));
+    };
+    // O = alpha_e * O + O_e for rows that attended chunk e, then free O[e % 2].
+    auto fold = [&](int e) -> bool {
+      const int buf = e & 1;
+      if (!warp_wait(bar_ofull + 8 * buf, (uint32_t)(e >> 1) & 1u)) return false;
+      tc_after();
+      if (__any_sync(0xffffffffu, act_prev)) {
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          float v[32];
+          tmem_ld32(lane_addr + 128u + (uint32_t)buf * 64u + half * 32, v);
+          if (act_prev) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 2)
+              ffma2(o[half * 32 + i], o[half * 32 + i + 1], alpha_prev, alpha_prev, o[half * 32 + i],
+                    o[half * 32 + i + 1], v[i], v[i + 1]);
+          }
+        }
+      }
+      tc_before();
+      mbar_arrive1(bar_oempty + 8 * buf);
+      return true;
+    };
+    for (int e = 0; e < n_ent; ++e) {
+      const int buf = e & 1;
+      if (!(ok = warp_wait(bar_sfull + 8 * buf, (uint32_t)(e >> 1) & 1u))) break;
+      tc_after();
+      const ChunkEntry& en = s_ent[e];
+      int lo, hi;  // valid keys of this row: index i of the chunk in [lo, hi)
+      float bias = 0.0f;
+      if (en.global) {
+        lo = 0;
+        hi = min(ni - kWindow, vleni) - en.row0;
+        bias = s_route[row * kTopK + (en.slot[tile] >= 0 ? en.slot[tile] : 0)];
+      } else {
+        lo = max(ni - kWindow, 0) - en.row0;
+        hi = min(ni, vleni) - en.row0;
+      }
+      const bool want = tile_ok && ((en.mask >> tile) & 1) && ni < vleni && hi > lo && hi > 0 && lo < 64;
+      float alpha = 1.0f;
+      if (__any_sync(0xffffffffu, want)) {  // warp-uniform: the whole warp loads its 32 rows
+        float sv[64];
+        tmem_ld32(lane_addr + (uint32_t)buf * 64u, *reinterpret_cast<float(*)[32]>(sv));
+        tmem_ld32(lane_addr + (uint32_t)buf * 64u + 32, *reinterpret_cast<float(*)[32]>(sv + 32));
+        if (want) {
+          const float c2 = bias * kLog2e;
+#pragma unroll
+          for (int i = 0; i < 64; i += 2) ffma2(sv[i], sv[i + 1], sv[i], sv[i + 1], kC1, kC1, c2, c2);
+          if (lo > 0 || hi < 64) {
+#pragma unroll
+            for (int i = 0; i < 64; ++i)
+              if ((unsigned)(i - lo) >= (unsigned)(hi - lo)) sv[i] = -INFINITY;
+          }
+          float mx = sv[0];
+#pragma unroll
+          for (int i = 1; i < 64; ++i) mx = fmaxf(mx, sv[i]);
+          const float mn = fmaxf(m, mx);
+          alpha = ex2_approx(m - mn);  // m = -inf on the row's first chunk: 0
+          m = mn;
+          float rs0 = 0.0f, rs1 = 0.0f;
+          // P row (bf16) -> swizzled tile: 16-byte chunk c of row r at chunk c ^ (r & 7)
+          unsigned char* prow = smem + TcSmem::pbuf + buf * 128 * 128 + (row >> 3) * 1024 + (row & 7) * 128;
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            uint32_t w[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const float p0 = ex2_approx(sv[8 * c + 2 * k] - mn), p1 = ex2_approx(sv[8 * c + 2 * k + 1] - mn);
+              rs0 += p0;
+              rs1 += p1;
+              w[k] = pack_bf16(p0, p1);
+            }
+            *reinterpret_cast<uint4*>(prow + ((c ^ (row & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+          }
+          l = l * alpha + (rs0 + rs1);
+        }
+      }
+      // Rows that skip chunk e leave their (stale) P row: fold() does not read their O_e.
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      tc_before();
+      mbar_arrive1(bar_pfull + 8 * buf);
+      if (e >= 1 && !(ok = fold(e - 1))) break;
+      alpha_prev = alpha;
+      act_prev = want;
+    }
+    if (ok && n_ent > 0) ok = fold(n_ent - 1);
+    if (ok && !*abort_flag && tile_ok && n < p.T) {
+      const float inv = (l > 0.0f && n < vlen) ? 1.0f / l : 0.0f;
+      __nv_bfloat16* orow = p.out + (int64_t)b * p.sob + (int64_t)h * p.soh + n * p.son;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        uint4 w;
+        w.x = pack_bf16(o[8 * c] * inv, o[8 * c + 1] * inv);
+        w.y = pack_bf16(o[8 * c + 2] * inv, o[8 * c + 3] * inv);
+        w.z = pack_bf16(o[8 * c + 4] * inv, o[8 * c + 5] * inv);
+        w.w = pack_bf16(o[8 * c + 6] * inv, o[8 * c + 7] * inv);
+        *reinterpret_cast<uint4*>(orow + 8 * c) = w;
+      }
+      if (p.lse != nullptr)
+        p.lse[((int64_t)b * p.H + h) * p.T + n] = (l > 0.0f && n < vlen) ? m + __log2f(l) : INFINITY;
+    }
+  }
+  tc_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTcCols) : "memory");
+  }
+  if (*abort_flag && threadIdx.x == 0 && status != nullptr) atomicExch(status, DWARF_DEVICE_TIMEOUT);
+}
+
 // 4-D bf16 tensor map over a [B, H, T, 64] view (element strides sb, sh, sn),
 // box 64 rows x 64 dims, 128-byte swizzle.
 bool make_kv_map(CUtensorMap* map, const void* ptr, int64_t B, int64_t H, int64_t T, int64_t sb, int64_t sh,
@@ -824,14 +1230,20 @@ extern "C" int dwarf_hisa_attn(const dwarf_hisa_attn_args* a, void* stream) {
   p.lse = (float*)a->lse;
   p.H = a->H; p.T = a->T; p.tiles = (a->T + kTile - 1) / kTile;
   p.k_slots = a->k_slots;
-  AttnMaps maps;
+  TcMaps maps;
   if (!make_kv_map(&maps.lk, a->local_key, a->B, a->H, a->T, a->slkb, a->slkh, a->slkn) ||
       !make_kv_map(&maps.lv, a->local_value, a->B, a->H, a->T, a->slvb, a->slvh, a->slvn) ||
       !make_kv_map(&maps.gk, a->global_key, a->B, a->H, a->T, a->sgkb, a->sgkh, a->sgkn) ||
-      !make_kv_map(&maps.gv, a->global_value, a->B, a->H, a->T, a->sgvb, a->sgvh, a->sgvn))
+      !make_kv_map(&maps.gv, a->global_value, a->B, a->H, a->T, a->sgvb, a->sgvh, a->sgvn) ||
+      !make_kv_map(&maps.q, a->query, a->B, a->H, a->T, a->sqb, a->sqh, a->sqn))
     return DWARF_ERR_LAUNCH;
-  constexpr size_t smem = AttnSmem::bytes;
-  if (cudaFuncSetAttribute(hisa_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+  // The tensor-core kernel by default; DWARF_HISA_ATTN=mma selects the mma.sync
+  // form (read on every call).
+  const char* which = getenv("DWARF_HISA_ATTN");
+  const bool tc = !(which != nullptr && which[0] == 'm');
+  const size_t smem = tc ? (size_t)TcSmem::bytes : (size_t)AttnSmem::bytes;
+  if (cudaFuncSetAttribute(tc ? (const void*)hisa_attn_tc_kernel : (const void*)hisa_attn_kernel,
+                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return DWARF_ERR_LAUNCH;
   const int64_t cta_tiles = kCtaTiles;
   int64_t n_tiles = 0;
@@ -842,6 +1254,11 @@ extern "C" int dwarf_hisa_attn(const dwarf_hisa_attn_args* a, void* stream) {
   const int64_t ctas = a->pos != nullptr ? (n_tiles == 1 ? 1 : (n_tiles + cta_tiles - 1) / cta_tiles + 1)
                                          : (p.tile_end - p.grid_begin + cta_tiles - 1) / cta_tiles;
   dim3 grid((unsigned)ctas, (unsigned)a->H, (unsigned)a->B);
-  hisa_attn_kernel<<<grid, kCtaTiles * 32, smem, (cudaStream_t)stream>>>(p, maps, nullptr);
+  if (tc) {
+    hisa_attn_tc_kernel<<<grid, kTcThreads, smem, (cudaStream_t)stream>>>(p, maps, a->device_status);
+  } else {
+    const AttnMaps m4{maps.lk, maps.lv, maps.gk, maps.gv};
+    hisa_attn_kernel<<<grid, kCtaTiles * 32, smem, (cudaStream_t)stream>>>(p, m4, a->device_status);
+  }
   return launch_status();
 }

@@ -499,6 +499,7 @@ typedef struct {
                                      log2 units (scores x log2 e), +inf for rows
                                      with no key: the input dwarf_hisa_attn_bwd
                                      needs. NULL: not written                */
+  int32_t* device_status;         /* optional; set to DWARF_DEVICE_TIMEOUT */
 } dwarf_hisa_attn_args;
 
 int dwarf_hisa_reps(const dwarf_hisa_reps_args* args, void* stream);
