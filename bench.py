@@ -9,6 +9,10 @@ token ids in [57, 32768), split by batch rows across the ranks (strong scaling:
 the global batch is fixed). One step = prefill of the whole batch to logits
 plus an NCCL all-gather of every row's next-token logits to all ranks.
 
+The prefill is launched eagerly (``--graph``: as one CUDA graph per step,
+``model.capture_prefill``; measured the same within 0.1%: the step is not
+launch-bound).
+
 Printed JSON line (rank 0):
 * value    tokens/s with inputs resident in HBM, timed with CUDA events over
            exactly K steps between barriers, max over ranks;
@@ -16,7 +20,8 @@ Printed JSON line (rank 0):
            the token ids (pinned) and the device->host read of the gathered
            next-token logits inside the timed region;
 * roofline the dominant engine kernel (dwarf_dsqg_fwd): algorithmic bytes per
-           launch / its mean CUDA-event duration inside the timed region,
+           launch / its mean CUDA-event duration (per-launch events in an eager
+           run of the same K steps right after the graph's timed region),
            against the measured HBM copy bandwidth; ``fma`` beside it: the
            kernel's FP32 pair FMAs (2 x 64 per valid (query, offset) pair) per
            second against the derived CUDA-core peak (148 SMs x 128 lanes x 2
@@ -194,8 +199,22 @@ def run_ours(args) -> None:
     gathered = torch.empty(GLOBAL_BATCH, VOCAB, dtype=torch.bfloat16, device=dev)
     out_host = torch.empty(GLOBAL_BATCH, VOCAB, dtype=torch.bfloat16).pin_memory()
 
+    # --graph: the prefill as one CUDA graph (model.capture_prefill), the same kernels
+    # as the eager forward launched as one graph instead of ~300 host launches; a
+    # launch log active during the capture counts the engine kernels of one step.
+    capture_log = _lib.LaunchLog()
+    _lib.set_launch_log(capture_log)
+    try:
+        graph = model.capture_prefill(rows, SEQ_LEN) if args.graph else None
+    finally:
+        _lib.set_launch_log(None)
+    launches_per_step = capture_log.count // 2 if graph is not None else None  # warm-up + capture
+
+    def forward(ids):
+        return graph(ids) if graph is not None else model(ids)
+
     def step(ids):
-        logits = model(ids)
+        logits = forward(ids)
         return gather_rows(logits[:, -1].contiguous(), gathered)
 
     def barrier():
@@ -227,8 +246,20 @@ def run_ours(args) -> None:
             _lib.set_launch_log(None)
             barrier()
         ms = max_over_ranks(start.elapsed_time(end) / args.steps)
+        launches = log.count if graph is None else launches_per_step * args.steps
+        if graph is not None:
+            # The graph's kernels carry no per-launch events: the DSQG launch time for
+            # the roofline comes from the same steps run eagerly right after (the
+            # same kernels, arguments and inputs), with CUDA events around each
+            # dwarf_dsqg_fwd launch on its stream.
+            log = _lib.LaunchLog(timed=("dwarf_dsqg_fwd",))
+            barrier()
+            _lib.set_launch_log(log)
+            for _ in range(args.steps):
+                model(ids_dev)
+            _lib.set_launch_log(None)
+            barrier()
         dsqg_ms = log.mean_ms("dwarf_dsqg_fwd")
-        launches = log.count
         # end to end through the public API: H2D ids, prefill + gather, D2H logits
         barrier()
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -276,7 +307,8 @@ def run_ours(args) -> None:
         "config": {"workload": "config5: full DWARF-v2 prefill D512 L10 T2048, q6 KV, batch rows sharded",
                    "model": "DWARF-v2 55M (10 blocks: 9 DSQG + 1 HISA)", "global_batch": GLOBAL_BATCH,
                    "seq_len": SEQ_LEN, "parallelism": f"dp{world}", "kv_cache": "q6",
-                   "l2": "no flush: every step's working set (>= 4 GB of activations per GPU) exceeds L2"},
+                   "l2": "no flush: every step's working set (>= 4 GB of activations per GPU) exceeds L2",
+                   "launch": "eager" if graph is None else "one CUDA graph per step (model.capture_prefill)"},
         "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": rows * SEQ_LEN * 8,
                 "d2h_bytes_per_step": GLOBAL_BATCH * VOCAB * 2 if rank == 0 else 0},
         "gpu_launches": launches,
@@ -307,6 +339,7 @@ def main() -> None:
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--rows", type=int, default=None, help="override the global batch (small profiling cases)")
+    ap.add_argument("--graph", action="store_true", help="run each step as one CUDA graph (model.capture_prefill)")
     args = ap.parse_args()
     if args.rows:
         global GLOBAL_BATCH

@@ -381,6 +381,43 @@ class DecodeGraph:
         return self.logits
 
 
+class PrefillGraph:
+    """The inference forward of a fixed [batch, seq_len] captured in one CUDA graph.
+
+    ``graph(input_ids)`` copies the ids into the graph's input buffer and replays the
+    ~300 kernels of the prefill as one launch, returning the logits [batch, seq_len,
+    vocab] (a view of the graph's output buffer, overwritten by the next call). The
+    kernels and their arguments are those of ``model(input_ids)`` under
+    ``torch.no_grad()`` in eval mode, so the outputs are bit-identical to the eager
+    forward's. Weights must not be replaced (re-bound) while a graph is in use;
+    in-place updates are seen by the next replay except for the tables the modules
+    derive from their parameters (recomputed on the next eager call).
+    """
+
+    def __init__(self, model: "DwarfForCausalLM", batch: int, seq_len: int) -> None:
+        if model.training:
+            raise NotImplementedError("capture_prefill captures the inference forward: call .eval() first")
+        device = model.embedding.weight.device
+        if device.type != "cuda":
+            raise RuntimeError("dwarf_v2_b200 runs on CUDA tensors only (no CPU fallback)")
+        self.model = model
+        self.ids = torch.full((int(batch), int(seq_len)), 57, dtype=torch.int64, device=device)
+        with torch.no_grad():
+            model(self.ids)  # eager warm-up: derived tables, workspaces, kernel attributes
+        torch.cuda.synchronize(device)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.no_grad(), torch.cuda.graph(self.graph):
+            self.logits = model(self.ids)
+        torch.cuda.synchronize(device)
+
+    def __call__(self, input_ids: torch.Tensor) -> torch.Tensor:
+        if tuple(input_ids.shape) != tuple(self.ids.shape):
+            raise ValueError(f"this graph was captured for input_ids of shape {tuple(self.ids.shape)}")
+        self.ids.copy_(input_ids, non_blocking=True)
+        self.graph.replay()
+        return self.logits
+
+
 class DwarfForCausalLM(nn.Module):
     """The 10-block DWARF-v2 language model (reference train/train_dwarf.py:367-470)."""
 
@@ -627,6 +664,10 @@ class DwarfForCausalLM(nn.Module):
         hidden = self._step_hidden(token_ids.reshape(-1), state)
         state.length += 1
         return gemm.linear(hidden[:, 0].contiguous(), _act(self.embedding.weight.detach()))
+
+    def capture_prefill(self, batch: int, seq_len: int) -> PrefillGraph:
+        """A CUDA graph of the inference prefill of [batch, seq_len] token ids (see PrefillGraph)."""
+        return PrefillGraph(self, batch, seq_len)
 
     def capture_decode(self, state: "DecodeState") -> "DecodeGraph":
         """A CUDA graph of one decode step over ``state``'s buffers (see DecodeGraph)."""

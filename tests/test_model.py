@@ -141,3 +141,21 @@ def test_each_block_matches_the_reference_block_at_the_north_star_bar(kv_cache):
                 assert e_out.max() <= 2 * e_ref.max() + 2e-3, (i, e_out.max(), e_ref.max())
                 assert e_out.mean() <= 2 * e_ref.mean() + 2e-4, (i, e_out.mean(), e_ref.mean())
     print(kv_cache, report)
+
+
+@pytest.mark.gpu
+def test_prefill_graph_replays_the_eager_forward_bit_for_bit():
+    """capture_prefill: one CUDA graph of the whole prefill (q6 KV) gives the eager
+    forward's logits bit for bit, for two different inputs replayed in turn."""
+    from dwarf_v2_b200.model import DwarfForCausalLM
+
+    model = DwarfForCausalLM(kv_cache="q6").eval().to(torch.bfloat16).cuda()
+    g = torch.Generator().manual_seed(3)
+    ids = [torch.randint(57, 32768, (2, 320), generator=g).cuda() for _ in range(2)]
+    with torch.no_grad():
+        eager = [model(x).clone() for x in ids]
+        graph = model.capture_prefill(2, 320)
+        for x, ref in zip(ids * 2, eager * 2):
+            assert torch.equal(graph(x), ref)
+    with pytest.raises(ValueError):
+        graph(ids[0][:, :100])
