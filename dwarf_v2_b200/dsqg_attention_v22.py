@@ -16,7 +16,7 @@ Engine additions: ``dsqg_attention_q6`` (DSQG over a q6 KV cache) and the
 module option ``kv_cache="q6"``.
 
 Everything on the device runs in this engine's CUDA kernels (``dwarf_dsqg_prep``,
-``dwarf_dsqg_fwd``, ``dwarf_npci_rotate``) and cuBLAS GEMMs; there is no
+``dwarf_dsqg_fwd``, ``dwarf_npci_rotate``) and its tcgen05 GEMM (``dwarf_gemm_bf16``); there is no
 Triton, no eager fallback and no CPU path (CPU tensors raise). Every grouped
 mode computes the same function, so all of them run the one online kernel.
 """
@@ -588,7 +588,7 @@ class DSQGAttentionV19(nn.Module):
     fused into its epilogue (``dwarf_gemm_bf16`` epilogue 3) ->
     ``dwarf_dsqg_fwd`` (resident-K/V kernel) with the ``if_gain`` and
     ``sigmoid(content_gate)`` epilogue fused -> out_proj GEMM. Otherwise: qkvg
-    GEMM (cuBLAS) -> ``dwarf_dsqg_prep`` -> ``dwarf_dsqg_fwd`` -> out_proj.
+    GEMM (tcgen05) -> ``dwarf_dsqg_prep`` -> ``dwarf_dsqg_fwd`` -> out_proj (tcgen05).
     """
 
     def __init__(self, embedding_dim, num_heads, offsets, j_small, j_large, seq_len=2048, dropout=0.1,
@@ -843,7 +843,7 @@ class DSQGAttentionV19(nn.Module):
             query = qkvg.view(batch, seq_len, 4, heads, head_dim)[:, :, 0].permute(0, 2, 1, 3)
             return self._attend(x, query, ("q6", *cache), y_pre, z_pre, qkvg[:, :, 3 * dimension:], t,
                                 query_start)
-        qkvg = F.linear(xb, weight.to(act), bias.to(act))  # [B, N, 4D]
+        qkvg = gemm.linear(xb, weight.to(act), bias.to(act))  # [B, N, 4D]
         split = qkvg.view(batch, seq_len, 4, heads, head_dim)
         query = split[:, :, 0].permute(0, 2, 1, 3)
         key = split[:, :, 1].permute(0, 2, 1, 3)
@@ -992,7 +992,7 @@ class DSQGAttentionV19(nn.Module):
                      plane_shift=self.plane_shift, query_start=query_start, out=out_view,
                      head_gain=gain.detach().contiguous(), gate=content_gate, seq_len=seq_len,
                      row_begin=row_begin, pos=pos)
-        result = F.linear(out, self.out_proj.weight.to(act))
+        result = gemm.linear(out, self.out_proj.weight.to(act))
         return self.dropout(result).to(x.dtype) if x.dtype != act else self.dropout(result)
 
 

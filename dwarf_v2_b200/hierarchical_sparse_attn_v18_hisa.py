@@ -7,12 +7,15 @@ return_metadata=False, return_auxiliary=False)`` and ``prepare_runtime``;
 ``HISAMetadata``; ``HISASelectionCapture``.
 
 Device pipeline of one inference forward (eval mode, no gradients):
-qkvg GEMM and the rank-16 adapter GEMMs (cuBLAS) -> ``dwarf_npci_rotate``
+one tcgen05 GEMM for qkvg and the adapters' rank-16 down-projections (one
+weight, rows padded to 256), the two rank-16 up-projections (tcgen05, K = 16)
+-> ``dwarf_npci_rotate``
 (adapter add + EMA/NPCI rotation of global K and V, one pass each) ->
 ``dwarf_hisa_reps`` (chunk representatives) -> ``dwarf_hisa_select`` (tile
-anchor logits, strict-causal top-k) -> ``dwarf_hisa_attn`` (route prior, local
-window and routed chunks in one tensor-core softmax) -> W_o GEMM ->
-``dwarf_gate_mul``.
+anchor logits, strict-causal top-k) -> ``dwarf_hisa_route`` -> ``dwarf_hisa_attn``
+(route prior, local window and routed chunks in one softmax, S and P.V on
+tcgen05 with TMEM accumulators) -> W_o GEMM (tcgen05) -> ``dwarf_gate_mul``
+(the model fuses this gate into its residual add + RMSNorm).
 
 Supported configuration: head_dim 64, chunk 64, selector tile 16, local
 window 64, top_k <= 4, hisa_top_m_tokens >= chunk (the reference's
@@ -39,7 +42,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from . import _lib
+from . import _lib, gemm
 from .glue import gate_mul
 from .npci import npci_rotate_autograd, npci_rotate_cuda
 
@@ -645,16 +648,52 @@ class HierarchicalSparseAttentionV16HISACausal(nn.Module):
     def _blend_alpha(self) -> float:
         return {"mean": 0.0, "max_l2": 1.0}.get(self.representative_mode, self.representative_blend_alpha)
 
-    def global_kv(self, x, local_key, local_value, kv_inject):
-        """Global K/V = local + low-rank adapter, NPCI-rotated toward the packet deltas when given."""
+    def _projection_weights(self) -> tuple[torch.Tensor, torch.Tensor]:
+        """One bf16 weight [qkvg_proj ; global_k_down ; global_v_down ; zero rows] (rows padded
+        to a multiple of 256, the GEMM's wide tile) and its bias (zeros past qkvg), rebuilt only
+        when a parameter changes: the input projection and the adapters' down-projections in
+        one GEMM."""
+        params = [self.qkvg_proj.weight, self.qkvg_proj.bias]
+        if self.global_adapter_rank:
+            params += [self.global_k_down.weight, self.global_v_down.weight]
+        key = tuple((t.data_ptr(), t._version, t.dtype, t.device) for t in params)
+        if getattr(self, "_proj_key", None) != key:
+            with torch.no_grad():
+                act = torch.bfloat16
+                w = [self.qkvg_proj.weight.to(act)]
+                b = [self.qkvg_proj.bias.to(act)]
+                if self.global_adapter_rank:
+                    w += [self.global_k_down.weight.to(act), self.global_v_down.weight.to(act)]
+                    b.append(torch.zeros(2 * self.global_adapter_rank, dtype=act, device=b[0].device))
+                rows = sum(t.shape[0] for t in w)
+                pad = -rows % 256
+                if pad:
+                    w.append(torch.zeros(pad, w[0].shape[1], dtype=act, device=w[0].device))
+                    b.append(torch.zeros(pad, dtype=act, device=b[0].device))
+                self._proj = (torch.cat(w).contiguous(), torch.cat(b).contiguous())
+            self._proj_key = key
+        return self._proj
+
+    def _project(self, xb: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor | None]:
+        """(qkvg [B,T,4D], adapter down-projections [B,T,2r] or None) from one tcgen05 GEMM;
+        both are column views of the GEMM's output."""
+        weight, bias = self._projection_weights()
+        out = gemm.linear(xb, weight, bias)
+        D, r = self.D, self.global_adapter_rank
+        return out[..., : 4 * D], (out[..., 4 * D: 4 * D + 2 * r] if r else None)
+
+    def global_kv(self, x, local_key, local_value, kv_inject, down=None):
+        """Global K/V = local + low-rank adapter, NPCI-rotated toward the packet deltas when given.
+        ``down``: the adapters' down-projections of x when the caller already has them."""
         B, T, _ = x.shape
         act = torch.bfloat16
         addend_k = addend_v = None
         if self.global_adapter_rank:
             r = self.global_adapter_rank
-            down = F.linear(x, torch.cat((self.global_k_down.weight, self.global_v_down.weight)).to(act))
-            addend_k = _to_heads(F.linear(down[..., :r], self.global_k_up.weight.to(act)), B, T, self.H, self.hd)
-            addend_v = _to_heads(F.linear(down[..., r:], self.global_v_up.weight.to(act)), B, T, self.H, self.hd)
+            if down is None:  # callers outside the fused projection (N = 2r is below the GEMM's 128-column tile)
+                down = F.linear(x, torch.cat((self.global_k_down.weight, self.global_v_down.weight)).to(act))
+            addend_k = _to_heads(gemm.linear(down[..., :r], self.global_k_up.weight.to(act)), B, T, self.H, self.hd)
+            addend_v = _to_heads(gemm.linear(down[..., r:], self.global_v_up.weight.to(act)), B, T, self.H, self.hd)
         kd = vd = None
         if kv_inject is not None:
             kd, vd = kv_inject
@@ -676,12 +715,12 @@ class HierarchicalSparseAttentionV16HISACausal(nn.Module):
         B, T, _ = x.shape
         act = torch.bfloat16
         xb = x if x.dtype == act else x.to(act)
-        qkvg = F.linear(xb, self.qkvg_proj.weight.to(act), self.qkvg_proj.bias.to(act))
+        qkvg, down = self._project(xb)
         q, k, v, gate = qkvg.split(self.D, dim=-1)
         query = _to_heads(q, B, T, self.H, self.hd)
         local_key = _to_heads(k, B, T, self.H, self.hd)
         local_value = _to_heads(v, B, T, self.H, self.hd)
-        global_key, global_value = self.global_kv(xb, local_key, local_value, kv_inject)
+        global_key, global_value = self.global_kv(xb, local_key, local_value, kv_inject, down)
         attended = torch.empty(B, T, self.D, dtype=act, device=x.device)
         reps = chunk_representatives(global_key, lengths, blend_alpha=self._blend_alpha)
         top, _ = select_chunks(query, reps, lengths, top_k=self.top_k_chunks, temperature=self.temperature)
@@ -689,7 +728,7 @@ class HierarchicalSparseAttentionV16HISACausal(nn.Module):
         tile_attention(query, local_key, local_value, global_key, global_value, reps, top, scale, lengths,
                        out=_to_heads(attended, B, T, self.H, self.hd))
         self._last_token_selection_path = "enumerate_all"
-        return F.linear(attended, self.W_o.weight.to(act)), gate, top
+        return gemm.linear(attended, self.W_o.weight.to(act)), gate, top
 
     def forward_parts_cached(self, x: torch.Tensor, kv_inject, cache, row: int):
         """``forward_parts`` for positions [row, row + T) of ``x`` [B,T,D] over a cache.
@@ -706,12 +745,12 @@ class HierarchicalSparseAttentionV16HISACausal(nn.Module):
         B, T, _ = x.shape
         act = torch.bfloat16
         xb = x if x.dtype == act else x.to(act)
-        qkvg = F.linear(xb, self.qkvg_proj.weight.to(act), self.qkvg_proj.bias.to(act))
+        qkvg, down = self._project(xb)
         q, k, v, gate = qkvg.split(self.D, dim=-1)
         query = _to_heads(q, B, T, self.H, self.hd)
         local_key = _to_heads(k, B, T, self.H, self.hd)
         local_value = _to_heads(v, B, T, self.H, self.hd)
-        global_key, global_value = self.global_kv(xb, local_key, local_value, kv_inject)
+        global_key, global_value = self.global_kv(xb, local_key, local_value, kv_inject, down)
         seq_len = row + T
         if seq_len > cache[0].shape[2]:
             raise ValueError(f"rows [{row}, {seq_len}) exceed the cache length {cache[0].shape[2]}")
@@ -728,7 +767,7 @@ class HierarchicalSparseAttentionV16HISACausal(nn.Module):
         attended = torch.empty(B, seq_len, self.D, dtype=act, device=x.device)
         tile_attention(cq, clk, clv, cgk, cgv, reps, top, scale, lengths,
                        out=_to_heads(attended, B, seq_len, self.H, self.hd), tile_begin=tile0, tile_count=tiles)
-        return F.linear(attended[:, row:], self.W_o.weight.to(act)), gate
+        return gemm.linear(attended[:, row:], self.W_o.weight.to(act)), gate
 
     def forward_step(self, x: torch.Tensor, kv_inject, cache, reps: torch.Tensor, attended: torch.Tensor,
                      pos: torch.Tensor, lengths: torch.Tensor):
@@ -744,12 +783,12 @@ class HierarchicalSparseAttentionV16HISACausal(nn.Module):
         B = x.shape[0]
         act = torch.bfloat16
         xb = x if x.dtype == act else x.to(act)
-        qkvg = F.linear(xb, self.qkvg_proj.weight.to(act), self.qkvg_proj.bias.to(act))
+        qkvg, down = self._project(xb)
         q, k, v, gate = qkvg.split(self.D, dim=-1)
         query = _to_heads(q, B, 1, self.H, self.hd)
         local_key = _to_heads(k, B, 1, self.H, self.hd)
         local_value = _to_heads(v, B, 1, self.H, self.hd)
-        global_key, global_value = self.global_kv(xb, local_key, local_value, kv_inject)
+        global_key, global_value = self.global_kv(xb, local_key, local_value, kv_inject, down)
         for buf, new in zip(cache, (query, local_key, local_value, global_key, global_value)):
             buf.index_copy_(2, pos, new)
         cq, clk, clv, cgk, cgv = cache
@@ -760,7 +799,7 @@ class HierarchicalSparseAttentionV16HISACausal(nn.Module):
         scale = self.route_prior_scale.detach().float().contiguous()
         tile_attention(cq, clk, clv, cgk, cgv, reps, top, scale, lengths,
                        out=_to_heads(attended, B, L, self.H, self.hd), tile_count=1, pos=pos)
-        return F.linear(attended.index_select(1, pos), self.W_o.weight.to(act)), gate
+        return gemm.linear(attended.index_select(1, pos), self.W_o.weight.to(act)), gate
 
     def _forward_autograd(self, x: torch.Tensor, kv_inject, lengths: torch.Tensor):
         """Differentiable forward (training, or any call that needs gradients): the

@@ -11,8 +11,10 @@ and a freshly built model holds bit-identical weights.
 ``DwarfForCausalLM.forward`` runs the prefill through this engine's kernels:
 embedding + RMSNorm, per block the attention kernels, residual add fused with
 the next RMSNorm (and, after the HISA block, with its sigmoid output gate),
-SwiGLU, the EMA packet (three look-back scans + one epilogue kernel); GEMMs
-are cuBLAS bf16. Activations are bf16 with the reference's rounding points.
+SwiGLU, the EMA packet (three look-back scans + one epilogue kernel); every
+GEMM runs on the engine's tcgen05 GEMM (``dwarf_gemm_bf16``, fused epilogues
+for qkvg + DSQG prep, SwiGLU and residual + RMSNorm). Activations are bf16 with
+the reference's rounding points.
 ``kv_cache="q6"`` runs every DSQG layer over the q6-quantised K/V cache.
 Calls that need gradients (training mode, or autograd on with parameters that
 require grad) take the reference's own block formulas as torch ops over the
@@ -227,9 +229,9 @@ class InterferencePacket(nn.Module):
                 scan, final = causal_ema_scan(x, f.reshape(1), initial_state=state, return_final_state=True)
                 state.copy_(final)
                 scans.append(scan)
-        gate_pre = F.linear(x, _act(self.gate_proj.weight), _act(self.gate_proj.bias))
+        gate_pre = gemm.linear(x, _act(self.gate_proj.weight), _act(self.gate_proj.bias))
         packet = glue.packet(scans, mixture, gate_pre)
-        kv = F.linear(packet, _act(self.kv_proj.weight))
+        kv = gemm.linear(packet, _act(self.kv_proj.weight))
         B, T, D = x.shape
         key_delta = kv[..., :D].reshape(B, T, self.heads, self.head_dim).permute(0, 2, 1, 3)
         value_delta = kv[..., D:].reshape(B, T, self.heads, self.head_dim).permute(0, 2, 1, 3)
