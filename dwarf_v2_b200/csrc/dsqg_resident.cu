@@ -5,8 +5,9 @@
 // _fwd_v22_online, kernels/dsqg_attention_v22.py:698-860, for the q6 cache of
 // _DSQGV18GroupedFn.forward, :2197-2352), for the layout the engine itself
 // produces: dwarf_q6_pack rows (48 code bytes, contiguous) and fp16 scales
-// (contiguous), N % 8 == 0 and small enough for the cache to fit (N <= 2176),
-// J <= 32.
+// (contiguous), N % 8 == 0 and small enough for the cache and the tables to
+// fit in shared memory (N <= 2176 at the model's 29 offsets; the full
+// 96-offset lattice fits at N = 2048).
 //
 // Why resident: every key row n - off_j is used by the J queries that reach
 // it, so the gather kernel reads each row ~J times through L2 and pays an L2

@@ -600,8 +600,9 @@ hisa_attn_kernel(const AttnParams p, const __grid_constant__ AttnMaps maps, int3
     tma_load_4d(dst, en.global ? &maps.gk : &maps.lk, 0, en.row0, h, b, bar_full + 8 * s);
     tma_load_4d(dst + kStageBytes / 2, en.global ? &maps.gv : &maps.lv, 0, en.row0, h, b, bar_full + 8 * s);
   };
+  int issued = 0;  // thread 0: entries whose loads were issued
   if (threadIdx.x == 0)
-    for (int e = 0; e < n_ent && e < kStages; ++e) issue(e);
+    for (int e = 0; e < n_ent && e < kStages; ++e) { issue(e); issued = e + 1; }
   {
     // ---------------- one 16-query tile per warp
     const int tile = warp;
@@ -658,11 +659,16 @@ hisa_attn_kernel(const AttnParams p, const __grid_constant__ AttnMaps maps, int3
       }
       __syncwarp();
       if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar_empty + 8 * s) : "memory");
-      if (threadIdx.x == 0 && e + kStages < n_ent && mbar_wait(bar_empty + 8 * s, ph, abort_flag)) issue(e + kStages);
+      if (threadIdx.x == 0 && e + kStages < n_ent && mbar_wait(bar_empty + 8 * s, ph, abort_flag)) {
+        issue(e + kStages);
+        issued = e + kStages + 1;
+      }
     }
-    // Leave no copy in flight: every issued chunk has landed.
+    // Leave no copy in flight: of the issued entries, all but the last kStages
+    // were released by every tile (so they landed); wait for those kStages,
+    // whether the loop finished or an abort ended it early.
     if (threadIdx.x == 0)
-      for (int e = n_ent > kStages ? n_ent - kStages : 0; e < n_ent; ++e)
+      for (int e = issued > kStages ? issued - kStages : 0; e < issued; ++e)
         for (uint32_t it = 0; it < kWait && !mbar_try(bar_full + 8 * (e % kStages), (uint32_t)(e / kStages) & 1u); ++it) {}
 
     // Epilogue: O / l in bf16; rows past the valid length are zero.

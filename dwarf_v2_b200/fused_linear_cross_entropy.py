@@ -8,7 +8,8 @@ labels.flatten())``): the mean over non-ignored labels of
 fp32. On B200 the lm_head GEMM reduces the logits in its epilogue
 (``gemm.linear_lse``); nothing of size [rows, vocab] is written.
 
-Forward (inference / evaluation) only: the engine has no backward kernels.
+Forward (inference / evaluation) only: this loss has no backward here. Training
+runs the reference's own loss formula over the model's differentiable path.
 """
 
 from __future__ import annotations

@@ -571,8 +571,12 @@ class HierarchicalSparseAttentionV16HISACausal(nn.Module):
         return {
             "backend": self.backend,
             "local_backend": "dwarf_hisa_attn",
+            "attention_kernel": "mma.sync" if os.environ.get("DWARF_HISA_ATTN", "").startswith("m") else "tcgen05",
             "triton_block_q": self.triton_block_q,
             "backward_impl": self.backward_impl,
+            # the two reference settings above are validated and echoed but select
+            # nothing here: one forward and one backward kernel serve every value
+            "ignored_settings": ("triton_block_q", "backward_impl"),
             "collect_routing_diagnostics": self.collect_routing_diagnostics,
             "flex_attention_available": False,
             "flex_lse_api": "none",
