@@ -129,6 +129,18 @@ def case_q6_pack_config3(timer, peak):
     return {"kernel": "dwarf_q6_pack", "ms": ms, **_rate(_nbytes(k, codes, scales), ms, peak)}
 
 
+def case_q6_unpack_config3(timer, peak):
+    """Config-3 K (or V) cache dequantisation: codes + fp16 scales -> bf16 [32, 8, 2048, 64]."""
+    from .q6 import q6_pack, q6_unpack
+
+    g = torch.Generator().manual_seed(3)
+    codes, scales = q6_pack(torch.randn(32, 8, 2048, 64, generator=g).to(torch.bfloat16).cuda())
+    res = {}
+    times = timer(lambda: res.__setitem__("x", q6_unpack(codes, scales, torch.bfloat16)), ("dwarf_q6_unpack",))
+    ms = times["dwarf_q6_unpack"]
+    return {"kernel": "dwarf_q6_unpack", "ms": ms, **_rate(_nbytes(codes, scales, res["x"]), ms, peak)}
+
+
 def _dsqg_tables(J: int, js: int, H: int, offsets, g):
     pb = torch.randn(J, H, generator=g) * 0.3 - torch.log1p(torch.tensor(offsets, dtype=torch.float32))[:, None]
     return (pb.cuda(), (torch.randn(J, 64, generator=g) * 0.05).cuda(),
@@ -321,6 +333,7 @@ CASES = {
     "ema_model_bf16": case_ema_model_bf16,
     "ema_bwd_config2": case_ema_bwd_config2,
     "q6_pack_config3": case_q6_pack_config3,
+    "q6_unpack_config3": case_q6_unpack_config3,
     "dsqg_q6_config3": case_dsqg_q6_config3,
     "dsqg_q6_model_group": case_dsqg_q6_model_group,
     "dsqg_bwd_model_group": case_dsqg_bwd_model_group,
