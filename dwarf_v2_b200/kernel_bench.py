@@ -95,6 +95,40 @@ def case_ema_model_bf16(timer, peak):
     return {"kernel": "dwarf_ema_scan", "ms": ms, **_rate(2 * _nbytes(x), ms, peak)}
 
 
+def case_copy_config2(timer, peak):
+    """Reference point, not an engine kernel: a device-to-device copy of the config-2 tensor
+    (fp32 [16, 2048, 512], 67 MB read + 67 MB written, the EMA scan's bytes), timed with
+    CUDA events after the same L2 flush: what a plain stream of this size reaches here."""
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(16, 2048, 512, generator=g).cuda()
+    y = torch.empty_like(x)
+    for _ in range(timer.warmup):
+        y.copy_(x)
+    times = []
+    for _ in range(timer.iters):
+        timer.flush.fill_(1)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        y.copy_(x)
+        b.record()
+        times.append((a, b))
+    torch.cuda.synchronize()
+    ms = sum(a.elapsed_time(b) for a, b in times) / len(times)
+    return {"kernel": "torch copy_ (reference point)", "ms": ms, **_rate(2 * _nbytes(x), ms, peak)}
+
+
+def case_ema_model_bf16_b256(timer, peak):
+    """The packet scans of the config-5 prefill on one GPU: scalar alpha, bf16 [256, 2048, 512]."""
+    from .causal_ema_scan import causal_ema_scan
+
+    g = torch.Generator().manual_seed(1)
+    x = torch.randn(256, 2048, 512, generator=g).to(torch.bfloat16).cuda()
+    alpha = torch.tensor([1.0 / 16.0], device="cuda")
+    times = timer(lambda: causal_ema_scan(x, alpha), ("dwarf_ema_scan",))
+    ms = times["dwarf_ema_scan"]
+    return {"kernel": "dwarf_ema_scan", "ms": ms, **_rate(2 * _nbytes(x), ms, peak)}
+
+
 def case_ema_bwd_config2(timer, peak):
     """Config-2 backward: dx (the scan over time-reversed dy) and d alpha (one pass over
     x, y and dx)."""
@@ -331,6 +365,8 @@ def case_model_train_step(timer, peak):
 CASES = {
     "ema_config2": case_ema_config2,
     "ema_model_bf16": case_ema_model_bf16,
+    "ema_model_bf16_b256": case_ema_model_bf16_b256,
+    "copy_config2": case_copy_config2,
     "ema_bwd_config2": case_ema_bwd_config2,
     "q6_pack_config3": case_q6_pack_config3,
     "q6_unpack_config3": case_q6_unpack_config3,
