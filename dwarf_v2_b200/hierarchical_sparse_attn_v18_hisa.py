@@ -20,9 +20,12 @@ tcgen05 with TMEM accumulators) -> W_o GEMM (tcgen05) -> ``dwarf_gate_mul``
 Supported configuration: head_dim 64, chunk 64, selector tile 16, local
 window 64, top_k <= 4, hisa_top_m_tokens >= chunk (the reference's
 ``enumerate_all`` path), representative modes mean_max_blend / mean / max_l2.
-Metadata requested with ``return_metadata=True`` carries the routed chunk
-indices with ``enumerate_all=True`` (every token of a routed chunk is used,
-the same token set the reference's canonical listing names).
+Metadata requested with ``return_metadata=True`` is the reference's canonical
+listing: the routed chunk indices and, per (tile, slot), the chunk's valid
+tokens in descending order of the tile anchor's score (``token_idx`` /
+``token_scores``, ``enumerate_all=False``), built on the device from the same
+router inputs; the attention itself attends every valid token of a routed
+chunk either way.
 
 Training mode, or any forward whose inputs or parameters need gradients, takes
 ``_forward_autograd``: the projections, adapters, NPCI rotation, chunk
@@ -711,10 +714,11 @@ class HierarchicalSparseAttentionV16HISACausal(nn.Module):
         gv = npci_rotate_cuda(local_value, vd, theta_v, addend=addend_v)
         return gk, gv
 
-    def forward_parts(self, x: torch.Tensor, kv_inject, lengths: torch.Tensor):
+    def forward_parts(self, x: torch.Tensor, kv_inject, lengths: torch.Tensor, *, router_inputs: list | None = None):
         """(W_o(attended), content-gate logits, top_chunk_idx): the forward up to the output gate.
 
         The model fuses ``* sigmoid(gate)`` into its residual-add + RMSNorm kernel.
+        ``router_inputs``: a list that receives (query, global_key) for the metadata listing.
         """
         B, T, _ = x.shape
         act = torch.bfloat16
@@ -732,6 +736,8 @@ class HierarchicalSparseAttentionV16HISACausal(nn.Module):
         tile_attention(query, local_key, local_value, global_key, global_value, reps, top, scale, lengths,
                        out=_to_heads(attended, B, T, self.H, self.hd))
         self._last_token_selection_path = "enumerate_all"
+        if router_inputs is not None:
+            router_inputs.extend((query, global_key))
         return gemm.linear(attended, self.W_o.weight.to(act)), gate, top
 
     def forward_parts_cached(self, x: torch.Tensor, kv_inject, cache, row: int):
@@ -805,7 +811,8 @@ class HierarchicalSparseAttentionV16HISACausal(nn.Module):
                        out=_to_heads(attended, B, L, self.H, self.hd), tile_count=1, pos=pos)
         return gemm.linear(attended.index_select(1, pos), self.W_o.weight.to(act)), gate
 
-    def _forward_autograd(self, x: torch.Tensor, kv_inject, lengths: torch.Tensor):
+    def _forward_autograd(self, x: torch.Tensor, kv_inject, lengths: torch.Tensor, *,
+                          router_inputs: list | None = None):
         """Differentiable forward (training, or any call that needs gradients): the
         reference forward (hierarchical_sparse_attn_v18_hisa.py:2546-2787) with the
         projections, the global adapters, the NPCI rotation, the chunk representatives,
@@ -838,6 +845,8 @@ class HierarchicalSparseAttentionV16HISACausal(nn.Module):
         act = torch.bfloat16
         top, _ = select_chunks(query.detach().to(act).contiguous(), reps.detach().to(act).contiguous(), lengths,
                                top_k=self.top_k_chunks, temperature=self.temperature)
+        if router_inputs is not None:
+            router_inputs.extend((query.detach(), global_key.detach()))
         if self.training and self.exploration_probability > 0.0:
             top = inject_exploration(top, _eligible(tiles, reps.shape[2], lengths), self.exploration_probability)
         route = selected_route_scores(query_normalized, reps, top, self.route_prior_scale)
@@ -857,6 +866,43 @@ class HierarchicalSparseAttentionV16HISACausal(nn.Module):
         if auxiliary is None:
             auxiliary = output.sum() * 0.0
         return output, top, auxiliary
+
+    def _canonical_metadata(self, query: torch.Tensor, global_key: torch.Tensor, top: torch.Tensor,
+                            lengths: torch.Tensor) -> HISAMetadata:
+        """The metadata the reference returns when asked for it: the routed chunks and, per
+        (tile, slot), the chunk's tokens in descending order of the tile anchor's score
+        q^_anchor . k / sqrt(hd), invalid tokens (past the valid length, at or after the
+        tile start, or of an empty slot) as -1 / -inf (reference
+        _build_causal_tile_metadata with canonical_token_order, :290-397; the module
+        asks for it whenever return_metadata is set, :2625). The attention does not
+        depend on this listing: with top_m_tokens == chunk_size every valid token of a
+        routed chunk is attended either way."""
+        with torch.no_grad():
+            B, H, T, D = query.shape
+            tiles, k_slots = top.shape[2], top.shape[3]
+            chunk = self.chunk_size
+            starts = torch.arange(tiles, device=query.device, dtype=torch.int32) * self.selector_tile_size
+            qn = F.normalize(query.float(), dim=-1, eps=1e-6).to(query.dtype)
+            anchor = qn[:, :, starts.long().clamp_max(T - 1)]
+            chunks = -(-T // chunk)
+            keys = F.pad(global_key, (0, 0, 0, chunks * chunk - T)).reshape(B, H, chunks, chunk, D)
+            bi = torch.arange(B, device=query.device).view(B, 1, 1, 1)
+            hi = torch.arange(H, device=query.device).view(1, H, 1, 1)
+            picked = keys[bi, hi, top.clamp_min(0).long()]                       # [B,H,tiles,K,chunk,D]
+            within = torch.arange(chunk, device=query.device, dtype=torch.int32).view(1, 1, 1, 1, chunk)
+            absolute = top[..., None] * chunk + within
+            valid = ((top[..., None] >= 0) & (absolute < lengths.view(B, 1, 1, 1, 1))
+                     & (absolute < starts.view(1, 1, tiles, 1, 1)))
+            scores = torch.einsum("bhtd,bhtkmd->bhtkm", anchor.float(), picked.float()) / math.sqrt(D)
+            scores = scores.masked_fill(~valid, float("-inf"))
+            token_scores, local = scores.topk(min(self.hisa_top_m_tokens, chunk), dim=-1)
+            finite = torch.isfinite(token_scores) & (top[..., None] >= 0)
+            token_idx = torch.where(finite, top[..., None] * chunk + local.to(torch.int32),
+                                    torch.full_like(local, -1, dtype=torch.int32)).to(torch.int32)
+            token_scores = torch.where(finite, token_scores, torch.full_like(token_scores, float("-inf")))
+        return HISAMetadata(top_chunk_idx=top, token_idx=token_idx, token_scores=token_scores.float(),
+                            tile_starts=starts, valid_lengths=lengths, chunk_size=self.chunk_size,
+                            selector_tile_size=self.selector_tile_size, enumerate_all=False)
 
     def _metadata(self, top: torch.Tensor, lengths: torch.Tensor) -> HISAMetadata:
         tiles = top.shape[2]
@@ -881,16 +927,18 @@ class HierarchicalSparseAttentionV16HISACausal(nn.Module):
             valid_lengths if valid_lengths is not None else getattr(self, "_causal_control_valid_lengths", None),
             batch_size=B, seq_len=T, device=x.device)
         grad = torch.is_grad_enabled() and (x.requires_grad or any(p.requires_grad for p in self.parameters()))
+        router_inputs: list = []
         if grad or self.training:
-            output, top, auxiliary = self._forward_autograd(x, kv_inject, lengths)
+            output, top, auxiliary = self._forward_autograd(x, kv_inject, lengths, router_inputs=router_inputs)
         else:
-            projected, gate, top = self.forward_parts(x, kv_inject, lengths)
+            projected, gate, top = self.forward_parts(x, kv_inject, lengths,
+                                                      router_inputs=router_inputs if return_metadata else None)
             output = gate_mul(projected, gate)
             if x.dtype != torch.bfloat16:
                 output = output.to(x.dtype)
             auxiliary = output.new_zeros(())
         if return_metadata:
-            metadata = self._metadata(top, lengths)
+            metadata = self._canonical_metadata(*router_inputs, top, lengths)
             return (output, metadata, auxiliary) if return_auxiliary else (output, metadata)
         return (output, auxiliary) if return_auxiliary else output
 

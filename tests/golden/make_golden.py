@@ -394,7 +394,10 @@ def make_hisa_module_bf16() -> None:
     module = module.to(torch.bfloat16)
     with torch.no_grad():
         y = module(x.to(torch.bfloat16), kv_inject=(kd.to(torch.bfloat16), vd.to(torch.bfloat16)))
-    save("hisa_module_eval_bf16", y=y)
+        _, meta = module(x.to(torch.bfloat16), kv_inject=(kd.to(torch.bfloat16), vd.to(torch.bfloat16)),
+                         return_metadata=True)
+    save("hisa_module_eval_bf16", y=y, top_chunk_idx=meta.top_chunk_idx, token_idx=meta.token_idx,
+         token_scores=meta.token_scores, enumerate_all=np.asarray(meta.enumerate_all))
 
 
 def make_hisa_backward() -> None:

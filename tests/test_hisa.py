@@ -166,6 +166,38 @@ def test_module_matches_reference_module():
 
 
 @pytest.mark.gpu
+def test_module_metadata_is_the_reference_canonical_listing():
+    """return_metadata=True gives the reference's canonical listing
+    (_build_causal_tile_metadata with canonical_token_order, hierarchical_sparse_attn_v18_hisa.py:290-397):
+    per (tile, slot) the routed chunk's valid tokens in descending anchor-score order,
+    -1 / -inf elsewhere. Against the reference module's bf16 run: the same routed
+    chunks, the same token set per (tile, slot), scores within 2e-2 (bf16 keys), and
+    each listing sorted by its own scores."""
+    from dwarf_v2_b200.hierarchical_sparse_attn_v18_hisa import HierarchicalSparseAttentionV16HISACausal
+
+    g, r = load("hisa_module_eval"), load("hisa_module_eval_bf16")
+    module = HierarchicalSparseAttentionV16HISACausal(
+        D=128, H=2, hd=64, chunk_size=64, top_k_chunks=4, hisa_top_m_tokens=64, local_window=64,
+        selector_tile_size=16, route_prior_scale=0.1, global_adapter_rank=16).eval()
+    module.load_state_dict({k[len("state."):]: val for k, val in g.items() if k.startswith("state.")})
+    module = module.cuda()
+    with torch.no_grad():
+        _, meta = module(g["x"].to(torch.bfloat16).cuda(), return_metadata=True,
+                         kv_inject=(g["key_delta"].to(torch.bfloat16).cuda(), g["value_delta"].to(torch.bfloat16).cuda()))
+    assert not meta.enumerate_all
+    top = meta.top_chunk_idx.cpu()
+    assert torch.equal(top, r["top_chunk_idx"])
+    idx, sc = meta.token_idx.cpu(), meta.token_scores.cpu()
+    assert idx.shape == r["token_idx"].shape
+    assert torch.equal(idx.sort(-1).values, r["token_idx"].sort(-1).values)
+    fin = torch.isfinite(r["token_scores"])
+    assert torch.equal(fin, torch.isfinite(sc)) and torch.equal(fin, idx >= 0)
+    assert (sc[fin] - r["token_scores"][fin]).abs().max() < 2e-2
+    later = sc[..., 1:]
+    assert ((sc[..., :-1] >= later) | ~torch.isfinite(later)).all()
+
+
+@pytest.mark.gpu
 @pytest.mark.parametrize("T,tile_begin,tile_count", [(2048, 127, 1), (1000, 40, 3), (333, 20, 1), (64, 0, 0)])
 def test_tile_window_matches_full_launch(T, tile_begin, tile_count):
     """select/route/attn restricted to selector tiles [tile_begin, +count) reproduce the
