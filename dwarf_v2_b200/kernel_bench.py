@@ -175,6 +175,23 @@ def case_q6_unpack_config3(timer, peak):
     return {"kernel": "dwarf_q6_unpack", "ms": ms, **_rate(_nbytes(codes, scales, res["x"]), ms, peak)}
 
 
+def case_npci_model_b256(timer, peak):
+    """The DSQG key rotation at the model's single-GPU shape (B=256, H=8, T=2048): key is the
+    strided view of the fused qkvg projection, delta the strided view of the packet's kv output."""
+    from .npci import npci_rotate_cuda
+
+    g = torch.Generator(device="cuda").manual_seed(5)
+    B, H, T = 256, 8, 2048
+    qkvg = torch.randn(B, T, 4, H, 64, generator=g, device="cuda", dtype=torch.bfloat16)
+    kv = torch.randn(B, T, 2, H, 64, generator=g, device="cuda", dtype=torch.bfloat16) * 0.3
+    key, delta = qkvg[:, :, 1].permute(0, 2, 1, 3), kv[:, :, 0].permute(0, 2, 1, 3)
+    theta = torch.full((H,), 0.2, device="cuda")
+    out = torch.empty(B, H, T, 64, device="cuda", dtype=torch.bfloat16)
+    times = timer(lambda: npci_rotate_cuda(key, delta, theta, out=out), ("dwarf_npci_rotate",))
+    ms = times["dwarf_npci_rotate"]
+    return {"kernel": "dwarf_npci_rotate", "ms": ms, **_rate(3 * _nbytes(out), ms, peak)}
+
+
 def _dsqg_tables(J: int, js: int, H: int, offsets, g):
     pb = torch.randn(J, H, generator=g) * 0.3 - torch.log1p(torch.tensor(offsets, dtype=torch.float32))[:, None]
     return (pb.cuda(), (torch.randn(J, 64, generator=g) * 0.05).cuda(),
@@ -370,6 +387,7 @@ CASES = {
     "ema_bwd_config2": case_ema_bwd_config2,
     "q6_pack_config3": case_q6_pack_config3,
     "q6_unpack_config3": case_q6_unpack_config3,
+    "npci_model_b256": case_npci_model_b256,
     "dsqg_q6_config3": case_dsqg_q6_config3,
     "dsqg_q6_model_group": case_dsqg_q6_model_group,
     "dsqg_bwd_model_group": case_dsqg_bwd_model_group,
