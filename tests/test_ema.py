@@ -123,6 +123,54 @@ def test_kernel_per_channel_shapes(shape, dtype, strided):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize(
+    "shape,dtype,per_channel",
+    [
+        ((160, 300, 32), torch.float32, True),     # one 32-channel block per row, a partial chunk
+        ((150, 1000, 96), torch.float32, False),   # scalar alpha, three blocks per row
+        ((40, 517, 264), torch.bfloat16, True),    # a 16-byte width edge (8 of 64 channels)
+        ((160, 2048, 512), torch.bfloat16, False),  # the model's packet scan at 160 rows
+    ],
+)
+def test_kernel_many_series_shapes(shape, dtype, per_channel):
+    """Many independent (row, channel block) series with partial last tiles, a 16-byte
+    width edge and both alpha forms, against the oracle."""
+    from dwarf_v2_b200.causal_ema_scan import causal_ema_scan, causal_ema_scan_per_channel
+
+    g = torch.Generator().manual_seed(sum(shape))
+    B, N, D = shape
+    x = torch.randn(B, N, D, generator=g).to(dtype)
+    if per_channel:
+        decay = torch.sigmoid(torch.randn(D, generator=g))
+        y = causal_ema_scan_per_channel(x.cuda(), (1.0 - decay).cuda())
+        ref = oracle_ema.ema_scan_decay_form(x.float().numpy(), decay.double().numpy())
+    else:
+        alpha = torch.tensor([0.03])
+        y = causal_ema_scan(x.cuda(), alpha.cuda())
+        ref = oracle_ema.ema_scan(x.float().numpy(), alpha.double().numpy(), clamp=(1e-5, 0.5))
+    torch.cuda.synchronize()
+    _tol_check(y, ref, dtype)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("split", [1, 300, 1499])
+def test_kernel_many_series_continuation(split):
+    """initial_state/final_state with many series in flight (160 rows x 256 channels)."""
+    from dwarf_v2_b200.causal_ema_scan import causal_ema_scan
+
+    g = torch.Generator().manual_seed(9)
+    x = torch.randn(160, 1500, 256, generator=g).cuda()
+    a = torch.tensor([0.07], device="cuda")
+    full, full_state = causal_ema_scan(x, a, return_final_state=True)
+    head, state = causal_ema_scan(x[:, :split].contiguous(), a, return_final_state=True)
+    tail, end_state = causal_ema_scan(x[:, split:].contiguous(), a, initial_state=state,
+                                      return_final_state=True)
+    torch.testing.assert_close(state, full[:, split - 1].float(), atol=1e-6, rtol=0)
+    torch.testing.assert_close(torch.cat([head, tail], 1), full, atol=1e-5, rtol=0)
+    torch.testing.assert_close(end_state, full_state, atol=1e-5, rtol=0)
+
+
+@pytest.mark.gpu
 def test_kernel_config2_full_size_properties():
     """BASELINE config 2 at full size: B=16, T=2048, D=512 fp32, a = sigmoid(N(0,1))."""
     from dwarf_v2_b200.causal_ema_scan import causal_ema_scan_per_channel
