@@ -295,6 +295,13 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   const __nv_bfloat162 t = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<const uint32_t*>(&t);
 }
+
+// (a, b) rounded to bf16 and back with one packed conversion.
+__device__ __forceinline__ void round_bf16_2(float& a, float& b) {
+  const uint32_t w = pack2(a, b);
+  a = __uint_as_float(w << 16);
+  b = __uint_as_float(w & 0xffff0000u);
+}
 __device__ __forceinline__ void store16(__nv_bfloat16* dst, const float (&v)[16]) {
   uint4 w0 = make_uint4(pack2(v[0], v[1]), pack2(v[2], v[3]), pack2(v[4], v[5]), pack2(v[6], v[7]));
   uint4 w1 = make_uint4(pack2(v[8], v[9]), pack2(v[10], v[11]), pack2(v[12], v[13]), pack2(v[14], v[15]));
@@ -572,8 +579,10 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
             const uint32_t u[4] = {rbuf[k & 1][q].x, rbuf[k & 1][q].y, rbuf[k & 1][q].z, rbuf[k & 1][q].w};
 #pragma unroll
             for (int hh = 0; hh < 4; ++hh) {
-              const float lo = round_bf16(__uint_as_float(u[hh] << 16) + round_bf16(v[8 * q + 2 * hh]));
-              const float hi = round_bf16(__uint_as_float(u[hh] & 0xffff0000u) + round_bf16(v[8 * q + 2 * hh + 1]));
+              float a0 = v[8 * q + 2 * hh], a1 = v[8 * q + 2 * hh + 1];
+              round_bf16_2(a0, a1);
+              float lo = __uint_as_float(u[hh] << 16) + a0, hi = __uint_as_float(u[hh] & 0xffff0000u) + a1;
+              round_bf16_2(lo, hi);
               ss = fmaf(lo, lo, ss);
               ss = fmaf(hi, hi, ss);
               pk[4 * q + hh] = pack2(lo, hi);
@@ -644,16 +653,22 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
             if (lane == 0) release_acc(bar_tempty + 8 * a);
           }
           add_bias64(epi.bias, epi.bias_bf16, n0 + c, v);
+          // bf16 rounding once, as packed pairs: the words are the stored row and,
+          // unpacked, the values every later step works on.
+          uint32_t pw[32];
 #pragma unroll
-          for (int i = 0; i < 64; ++i) v[i] = round_bf16(v[i]);
+          for (int i = 0; i < 32; ++i) {
+            pw[i] = pack2(v[2 * i], v[2 * i + 1]);
+            v[2 * i] = __uint_as_float(pw[i] << 16);
+            v[2 * i + 1] = __uint_as_float(pw[i] & 0xffff0000u);
+          }
           const int64_t hrow = ((int64_t)b * epi.heads + head) * epi.cache_len + tt + cache_row0;
           if (sec == 0 || sec == 3) {
             if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
             __syncwarp();
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
-              const uint4 w = make_uint4(pack2(v[8 * j], v[8 * j + 1]), pack2(v[8 * j + 2], v[8 * j + 3]),
-                                         pack2(v[8 * j + 4], v[8 * j + 5]), pack2(v[8 * j + 6], v[8 * j + 7]));
+              const uint4 w = make_uint4(pw[4 * j], pw[4 * j + 1], pw[4 * j + 2], pw[4 * j + 3]);
               *reinterpret_cast<uint4*>(stg_p + lane * 128 + ((j ^ (lane & 7)) << 4)) = w;
             }
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -688,17 +703,29 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
             for (int i = 0; i < 64; ++i) amax = fmaxf(amax, fabsf(v[i]));
             const __half sh = q6_scale_from_amax(amax);
             const float qinv = q6_inv_step(__half2float(sh));
+            // Rounding is monotonic, so when amax * inv (rounded) is below 31.5 every
+            // product on the row rounds to |code| <= 31 and the clamp is the identity:
+            // the common case (any fp16-normal scale) skips it. (The multiply and the
+            // add stay separate scalar IEEE ops: a fused or packed pair rounds once and
+            // can land on the other side of a .5 tie.)
+            const bool clamp = !(__fmul_rn(amax, qinv) < 31.5f);
             uint32_t w[12];
 #pragma unroll
             for (int g = 0; g < 4; ++g) {
               uint32_t cc[16];
+              // clamp(rint(x * inv), -31, 31) as q6_quantize (clamping first gives the same
+              // code): adding 1.5 * 2^23 rounds to nearest-even into the low mantissa bits,
+              // whose low six bits are the two's-complement code.
+              if (!clamp) {
 #pragma unroll
-              for (int i = 0; i < 16; ++i) {
-                // clamp(rint(x * inv), -31, 31) as q6_quantize (clamping first gives the same
-                // code): adding 1.5 * 2^23 rounds to nearest-even into the low mantissa bits,
-                // whose low six bits are the two's-complement code.
-                const float qf = fminf(fmaxf(__fmul_rn(v[16 * g + i], qinv), -31.0f), 31.0f);
-                cc[i] = __float_as_uint(__fadd_rn(qf, 12582912.0f)) & 63u;
+                for (int i = 0; i < 16; ++i)
+                  cc[i] = __float_as_uint(__fadd_rn(__fmul_rn(v[16 * g + i], qinv), 12582912.0f)) & 63u;
+              } else {
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                  const float qf = fminf(fmaxf(__fmul_rn(v[16 * g + i], qinv), -31.0f), 31.0f);
+                  cc[i] = __float_as_uint(__fadd_rn(qf, 12582912.0f)) & 63u;
+                }
               }
               w[3 * g] = cc[0] | cc[1] << 6 | cc[2] << 12 | cc[3] << 18 | cc[4] << 24 | cc[5] << 30;
               w[3 * g + 1] = cc[5] >> 2 | cc[6] << 4 | cc[7] << 10 | cc[8] << 16 | cc[9] << 22 | cc[10] << 28;
@@ -733,8 +760,9 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
           float cm = -INFINITY;
           int ci = 0;
 #pragma unroll
+          for (int j = 0; j < 64; j += 2) round_bf16_2(v[j], v[j + 1]);
+#pragma unroll
           for (int j = 0; j < 64; ++j) {
-            v[j] = round_bf16(v[j]);
             if (v[j] > cm) { cm = v[j]; ci = j; }
           }
           if (cm > best) { best = cm; bidx = n0 + c + ci; }
@@ -812,11 +840,16 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
           }
           if (!have) break;
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
+          for (int i = 0; i < 16; i += 2) {
             // silu in fp32 with the hardware exp2 and a fast divide (the bf16
             // rounding after it absorbs the few-ulp fp32 difference).
-            const float u = round_bf16(up[i]), g = round_bf16(gt[i]);
-            up[i] = round_bf16(__fdividef(g, 1.0f + __expf(-g))) * u;
+            float u0 = up[i], u1 = up[i + 1], g0 = gt[i], g1 = gt[i + 1];
+            round_bf16_2(u0, u1);
+            round_bf16_2(g0, g1);
+            float s0 = __fdividef(g0, 1.0f + __expf(-g0)), s1 = __fdividef(g1, 1.0f + __expf(-g1));
+            round_bf16_2(s0, s1);
+            up[i] = s0 * u0;
+            up[i + 1] = s1 * u1;
           }
           if (row < M) store16(epi.out + (int64_t)row * epi.ldo + f0 + c0, up);
         }

@@ -192,6 +192,46 @@ def case_npci_model_b256(timer, peak):
     return {"kernel": "dwarf_npci_rotate", "ms": ms, **_rate(3 * _nbytes(out), ms, peak)}
 
 
+def case_gemm_model_epilogues(timer, peak):
+    """The model's fused-epilogue GEMMs (M = 128 x 2048 rows) beside the same GEMM with a
+    plain store: qkvg + probes + q6 pack (N=2048, K=512), up_gate + SwiGLU (N=3200,
+    K=512), down + residual + RMSNorm (N=512, K=1600), out_proj (N=512, K=512)."""
+    from . import gemm
+    from .dsqg_attention_v22 import R_PLANES, _orthogonal_phase_probes
+
+    g = torch.Generator(device="cuda").manual_seed(7)
+    B, T, D, H = 128, 2048, 512, 8
+    M = B * T
+
+    def rnd(*shape, scale=1.0):
+        return torch.randn(*shape, generator=g, device="cuda", dtype=torch.bfloat16) * scale
+
+    x = rnd(B, T, D)
+    h = rnd(B, T, 1600)
+    out = {}
+    qp, kp = (t.cuda() for t in _orthogonal_phase_probes(R_PLANES, 64))
+    w_qkvg, b_qkvg = rnd(4 * D, D, scale=0.04), rnd(4 * D, scale=0.01)
+    w_ug = gemm.interleave_up_gate(rnd(3200, D, scale=0.04))
+    tile = gemm.swiglu_tile(1600)
+    w_down, w_out = rnd(D, 1600, scale=0.025), rnd(D, D, scale=0.04)
+    resid, nw = rnd(B, T, D), torch.ones(D, device="cuda")
+    cases = {
+        "qkvg_prep": (lambda: gemm.qkvg_prep(x, w_qkvg, b_qkvg, H, qp, kp), 2 * M * 4 * D * D),
+        "qkvg_plain": (lambda: out.__setitem__("a", gemm.linear(x, w_qkvg, b_qkvg)), 2 * M * 4 * D * D),
+        "up_gate_swiglu": (lambda: out.__setitem__("b", gemm.linear_swiglu(x, w_ug, tile)), 2 * M * 3200 * D),
+        "up_gate_plain": (lambda: out.__setitem__("b", gemm.linear(x, w_ug)), 2 * M * 3200 * D),
+        "down_rmsnorm": (lambda: gemm.linear_add_rmsnorm(h, w_down, resid, nw, x_out=resid), 2 * M * D * 1600),
+        "down_plain": (lambda: out.__setitem__("c", gemm.linear(h, w_down)), 2 * M * D * 1600),
+        "out_proj_plain": (lambda: out.__setitem__("d", gemm.linear(x, w_out)), 2 * M * D * D),
+    }
+    res = {}
+    for name, (fn, flops) in cases.items():
+        ms = timer(fn, ("dwarf_gemm_bf16",))["dwarf_gemm_bf16"]
+        res[name] = {"ms": round(ms, 4), "tflops": round(flops / (ms * 1e-3) / 1e12, 1)}
+        out.clear()
+    return {"rows": M, "gemms": res}
+
+
 def _dsqg_tables(J: int, js: int, H: int, offsets, g):
     pb = torch.randn(J, H, generator=g) * 0.3 - torch.log1p(torch.tensor(offsets, dtype=torch.float32))[:, None]
     return (pb.cuda(), (torch.randn(J, 64, generator=g) * 0.05).cuda(),
@@ -388,6 +428,7 @@ CASES = {
     "q6_pack_config3": case_q6_pack_config3,
     "q6_unpack_config3": case_q6_unpack_config3,
     "npci_model_b256": case_npci_model_b256,
+    "gemm_model_epilogues": case_gemm_model_epilogues,
     "dsqg_q6_config3": case_dsqg_q6_config3,
     "dsqg_q6_model_group": case_dsqg_q6_model_group,
     "dsqg_bwd_model_group": case_dsqg_bwd_model_group,

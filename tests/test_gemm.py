@@ -129,3 +129,33 @@ def test_qkvg_prep_matches_unfused(B, T, heads):
     assert torch.equal(ks, rks) and torch.equal(vs, rvs)
     assert (y - ry).abs().max().item() < 1e-5
     assert (z - rz).abs().max().item() < 1e-5
+
+
+@pytest.mark.gpu
+def test_qkvg_prep_q6_codes_with_subnormal_scales():
+    """Rows whose K/V amax is far below the fp16 normal range (zero inputs, bias ~1e-7):
+    their fp16 scales are subnormal, the rounded scale can sit well below amax, and the
+    codes depend on the clamp to +-31; they must still equal the unfused pack's."""
+    import torch.nn.functional as F
+
+    from dwarf_v2_b200.dsqg_attention_v22 import dsqg_prep
+    from dwarf_v2_b200.gemm import linear, qkvg_prep
+
+    B, T, heads = 2, 300, 4
+    D = 64 * heads
+    g = torch.Generator(device="cuda").manual_seed(17)
+    x = torch.randn(B, T, D, device="cuda", generator=g).to(torch.bfloat16)
+    x[:, ::3] = 0.0
+    w = (torch.randn(4 * D, D, device="cuda", generator=g) / D ** 0.5).to(torch.bfloat16)
+    bias = torch.randn(4 * D, device="cuda", generator=g) * 0.1
+    bias[D:3 * D] = torch.randn(2 * D, device="cuda", generator=g) * 1e-7
+    bias = bias.to(torch.bfloat16)
+    qp = F.normalize(torch.randn(4, 64, device="cuda", generator=g), dim=-1)
+    kp = F.normalize(torch.randn(4, 64, device="cuda", generator=g), dim=-1)
+    _, _, _, (kc, ks, vc, vs) = qkvg_prep(x, w, bias, heads, qp, kp)
+    ref = linear(x, w, bias).view(B, T, 4, heads, 64)
+    q, k, v = (ref[:, :, i].permute(0, 2, 1, 3) for i in range(3))
+    _, _, (rkc, rks, rvc, rvs) = dsqg_prep(q, k, v, qp, kp, pack_q6=True)
+    assert bool((rks[:, :, ::3].float() < 6.1e-5).all())  # the zero rows have subnormal scales
+    assert torch.equal(kc, rkc) and torch.equal(vc, rvc)
+    assert torch.equal(ks, rks) and torch.equal(vs, rvs)
