@@ -141,12 +141,18 @@ __global__ void __launch_bounds__(256) q6_pack_vec_kernel(const T* __restrict__ 
     amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
     const __half s = q6_scale_from_amax(amax);
     const float inv = q6_inv_step(__half2float(s));
+    const bool clamp = q6_needs_clamp(amax, inv);
     uint32_t g[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       g[j] = 0;
+      if (!clamp) {
 #pragma unroll
-      for (int i = 0; i < 4; ++i) g[j] |= (uint32_t)(q6_quantize(v[4 * j + i], inv) & 63) << (6 * i);
+        for (int i = 0; i < 4; ++i) g[j] |= q6_bits(v[4 * j + i], inv, false) << (6 * i);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) g[j] |= q6_bits(v[4 * j + i], inv, true) << (6 * i);
+      }
     }
     if (t < T_) {
       // four 24-bit groups -> three little-endian 32-bit words

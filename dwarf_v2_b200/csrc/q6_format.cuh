@@ -21,6 +21,19 @@ __device__ __forceinline__ int q6_quantize(float x, float inv) {
   return (int)q;
 }
 
+// The low six bits of the code of x (two's complement), as q6_quantize: adding
+// 1.5 * 2^23 to the (clamped) product rounds it to nearest-even into the low
+// mantissa bits. `clamp` may be false only when fmul_rn(amax, inv) < 31.5 for
+// the row's amax: rounding is monotonic, so no product then reaches 31.5 and the
+// clamp is the identity. Multiply and add stay separate IEEE operations (a fused
+// pair rounds once and can resolve a .5 tie differently).
+__device__ __forceinline__ uint32_t q6_bits(float x, float inv, bool clamp) {
+  float q = __fmul_rn(x, inv);
+  if (clamp) q = fminf(fmaxf(q, -31.0f), 31.0f);
+  return __float_as_uint(__fadd_rn(q, 12582912.0f)) & 63u;
+}
+__device__ __forceinline__ bool q6_needs_clamp(float amax, float inv) { return !(__fmul_rn(amax, inv) < 31.5f); }
+
 // Dequantisation step float(s) / 31 (IEEE division).
 __device__ __forceinline__ float q6_step(__half s) { return __fdiv_rn(__half2float(s), 31.0f); }
 

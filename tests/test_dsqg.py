@@ -172,6 +172,8 @@ def test_q6_pack_unpack_bit_exact(shape, dtype):
     x = (torch.randn(shape, generator=gen) * torch.rand(shape[:-1] + (1,), generator=gen) * 4).to(dtype)
     x[0, 0, 0] = 0.0                       # zero row
     x[0, 0, 1, 3] = 1e6 if dtype == torch.float32 else 3e5  # saturated scale
+    x[0, 0, 2] = (x[0, 0, 2].float() * 3e-7).to(dtype)  # fp16-subnormal scales: the clamp is live
+    x[0, 0, 3] = (x[0, 0, 3].float() * 2e-8).to(dtype)
     codes, scales = q6_pack(x.cuda())
     ref_codes, ref_scales = oq6.pack(x.float().numpy())
     assert np.array_equal(codes.cpu().numpy(), ref_codes)
