@@ -194,8 +194,9 @@ def case_npci_model_b256(timer, peak):
 
 def case_gemm_model_epilogues(timer, peak):
     """The model's fused-epilogue GEMMs (M = 128 x 2048 rows) beside the same GEMM with a
-    plain store: qkvg + probes + q6 pack (N=2048, K=512), up_gate + SwiGLU (N=3200,
-    K=512), down + residual + RMSNorm (N=512, K=1600), out_proj (N=512, K=512)."""
+    plain store: qkvg + probes + q6 pack (N=2048, K=512), up_gate + SwiGLU (the model's
+    hidden width padded to 1664: N=3328, K=512), down + residual + RMSNorm (N=512,
+    K=1664), out_proj (N=512, K=512). FLOPs count the padded shapes the GEMMs run."""
     from . import gemm
     from .dsqg_attention_v22 import R_PLANES, _orthogonal_phase_probes
 
@@ -207,21 +208,24 @@ def case_gemm_model_epilogues(timer, peak):
         return torch.randn(*shape, generator=g, device="cuda", dtype=torch.bfloat16) * scale
 
     x = rnd(B, T, D)
-    h = rnd(B, T, 1600)
     out = {}
     qp, kp = (t.cuda() for t in _orthogonal_phase_probes(R_PLANES, 64))
     w_qkvg, b_qkvg = rnd(4 * D, D, scale=0.04), rnd(4 * D, scale=0.01)
-    w_ug = gemm.interleave_up_gate(rnd(3200, D, scale=0.04))
-    tile = gemm.swiglu_tile(1600)
-    w_down, w_out = rnd(D, 1600, scale=0.025), rnd(D, D, scale=0.04)
+    from .model import DwarfConfig, SwiGLUFFN
+
+    ffn = SwiGLUFFN(DwarfConfig()).cuda()  # the model's own padded, interleaved FFN weights
+    w_ug, w_down, tile = ffn._fused_weights()
+    h = rnd(B, T, w_down.shape[1])
+    w_out = rnd(D, D, scale=0.04)
     resid, nw = rnd(B, T, D), torch.ones(D, device="cuda")
     cases = {
         "qkvg_prep": (lambda: gemm.qkvg_prep(x, w_qkvg, b_qkvg, H, qp, kp), 2 * M * 4 * D * D),
         "qkvg_plain": (lambda: out.__setitem__("a", gemm.linear(x, w_qkvg, b_qkvg)), 2 * M * 4 * D * D),
-        "up_gate_swiglu": (lambda: out.__setitem__("b", gemm.linear_swiglu(x, w_ug, tile)), 2 * M * 3200 * D),
-        "up_gate_plain": (lambda: out.__setitem__("b", gemm.linear(x, w_ug)), 2 * M * 3200 * D),
-        "down_rmsnorm": (lambda: gemm.linear_add_rmsnorm(h, w_down, resid, nw, x_out=resid), 2 * M * D * 1600),
-        "down_plain": (lambda: out.__setitem__("c", gemm.linear(h, w_down)), 2 * M * D * 1600),
+        "up_gate_swiglu": (lambda: out.__setitem__("b", gemm.linear_swiglu(x, w_ug, tile)), 2 * M * w_ug.shape[0] * D),
+        "up_gate_plain": (lambda: out.__setitem__("b", gemm.linear(x, w_ug)), 2 * M * w_ug.shape[0] * D),
+        "down_rmsnorm": (lambda: gemm.linear_add_rmsnorm(h, w_down, resid, nw, x_out=resid),
+                         2 * M * D * w_down.shape[1]),
+        "down_plain": (lambda: out.__setitem__("c", gemm.linear(h, w_down)), 2 * M * D * w_down.shape[1]),
         "out_proj_plain": (lambda: out.__setitem__("d", gemm.linear(x, w_out)), 2 * M * D * D),
     }
     res = {}
