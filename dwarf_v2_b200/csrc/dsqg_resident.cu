@@ -428,28 +428,23 @@ __global__ void __launch_bounds__(256 * TPQ, 1) dsqg_resident_kernel(const DsqgP
         __syncwarp();
       }
       const float* my_qe = qe_buf + qi * kQeLd;
-#pragma unroll 1
-      for (int jj = 0; jj < jn; ++jj) {
+      // Score of pair (n, j): the K row of the source token from shared memory,
+      // q . k in the denormal domain (+ the other thread's half), + q . bf16(E_j),
+      // + the position bias. z_pre is loaded for every offset (used by large
+      // ones only) so that the function has no branch: two calls in a row form
+      // one basic block and their dependency chains interleave.
+      auto pair_score = [&](int jj, int& src, bool& valid, float (&zz)[kPL]) -> float {
         const int j = j0 + jj;
-        if (s_off[j] > wlast) continue;
         const int s = n - s_off[j];
-        const bool valid = row_ok && s >= 0;
-        const int src = valid ? s : 0;
-        const bool large = j >= js;  // warp-uniform
-        float zz[kPL];
-#pragma unroll
-        for (int pl = 0; pl < kPL; ++pl) zz[pl] = 0.f;
-        if (large) {
-          if constexpr (TPQ == 1) {
-            const float4 z4 = __ldg(reinterpret_cast<const float4*>(zbase + (int64_t)src * p.szn));
-            zz[0] = z4.x; zz[1] = z4.y; zz[2] = z4.z; zz[3] = z4.w;
-          } else {
-            const float2 z2 = __ldg(reinterpret_cast<const float2*>(zbase + (int64_t)src * p.szn));
-            zz[0] = z2.x; zz[1] = z2.y;
-          }
+        valid = row_ok && s >= 0;
+        src = valid ? s : 0;
+        if constexpr (TPQ == 1) {
+          const float4 z4 = __ldg(reinterpret_cast<const float4*>(zbase + (int64_t)src * p.szn));
+          zz[0] = z4.x; zz[1] = z4.y; zz[2] = z4.z; zz[3] = z4.w;
+        } else {
+          const float2 z2 = __ldg(reinterpret_cast<const float2*>(zbase + (int64_t)src * p.szn));
+          zz[0] = z2.x; zz[1] = z2.y;
         }
-
-        // score: q . k_src in the denormal domain, + q . bf16(E_j), + bias
         uint32_t kw[kW];
         if constexpr (TPQ == 1) {
           const uint4* kr = reinterpret_cast<const uint4*>(s_kc + src * 48);
@@ -472,8 +467,13 @@ __global__ void __launch_bounds__(256 * TPQ, 1) dsqg_resident_kernel(const DsqgP
           P = hf == 0 ? part + other : other + part;  // same sum order in both threads
         }
         const float part = fmaf(P, c1, qbias) * sk;
-        float s2 = fmaf(part + my_qe[jj], c_score, s_pb[j]);
-        s2 = valid ? s2 : -INFINITY;
+        const float s2 = fmaf(part + my_qe[jj], c_score, s_pb[j]);
+        return valid ? s2 : -INFINITY;
+      };
+      // Online-softmax update and V accumulation (+ MOVT for large offsets) of one pair.
+      auto pair_update = [&](int jj, float s2, int src, bool valid, const float (&zz)[kPL]) {
+        const int j = j0 + jj;
+        const bool large = j >= js;  // warp-uniform
         if (s2 > m + kRescaleLog2) {
           const float f = ex2_approx(m - s2);
 #pragma unroll
@@ -518,6 +518,29 @@ __global__ void __launch_bounds__(256 * TPQ, 1) dsqg_resident_kernel(const DsqgP
             corr_a[pl] = fmaf(wv, fmaf(cm1, fa, -sn * fb), corr_a[pl]);
             corr_b[pl] = fmaf(wv, fmaf(sn, fa, cm1 * fb), corr_b[pl]);
           }
+        }
+      };
+      // Two pairs per step: both scores first (independent chains), then the two
+      // updates in offset order, so results equal the one-pair-at-a-time loop.
+#pragma unroll 1
+      for (int jj = 0; jj < jn; jj += 2) {
+        const bool use1 = s_off[j0 + jj] <= wlast;                      // warp-uniform
+        const bool use2 = jj + 1 < jn && s_off[j0 + jj + 1] <= wlast;  // warp-uniform
+        if (use1 && use2) {
+          int src1, src2;
+          bool v1, v2;
+          float z1[kPL], z2[kPL];
+          const float s1 = pair_score(jj, src1, v1, z1);
+          const float s2 = pair_score(jj + 1, src2, v2, z2);
+          pair_update(jj, s1, src1, v1, z1);
+          pair_update(jj + 1, s2, src2, v2, z2);
+        } else if (use1 || use2) {
+          const int jx = use1 ? jj : jj + 1;
+          int src;
+          bool v;
+          float z[kPL];
+          const float s = pair_score(jx, src, v, z);
+          pair_update(jx, s, src, v, z);
         }
       }
     }
