@@ -196,7 +196,7 @@ def case_gemm_model_epilogues(timer, peak):
     """The model's fused-epilogue GEMMs (M = 128 x 2048 rows) beside the same GEMM with a
     plain store: qkvg + probes + q6 pack (N=2048, K=512), up_gate + SwiGLU (the model's
     hidden width padded to 1664: N=3328, K=512), down + residual + RMSNorm (N=512,
-    K=1664), out_proj (N=512, K=512). FLOPs count the padded shapes the GEMMs run."""
+    K=1664), out_proj (N=512, K=512), lm_head (N=32768, K=512). FLOPs count the padded shapes the GEMMs run."""
     from . import gemm
     from .dsqg_attention_v22 import R_PLANES, _orthogonal_phase_probes
 
@@ -217,6 +217,7 @@ def case_gemm_model_epilogues(timer, peak):
     w_ug, w_down, tile = ffn._fused_weights()
     h = rnd(B, T, w_down.shape[1])
     w_out = rnd(D, D, scale=0.04)
+    w_vocab = rnd(32768, D, scale=0.02)
     resid, nw = rnd(B, T, D), torch.ones(D, device="cuda")
     cases = {
         "qkvg_prep": (lambda: gemm.qkvg_prep(x, w_qkvg, b_qkvg, H, qp, kp), 2 * M * 4 * D * D),
@@ -227,6 +228,7 @@ def case_gemm_model_epilogues(timer, peak):
                          2 * M * D * w_down.shape[1]),
         "down_plain": (lambda: out.__setitem__("c", gemm.linear(h, w_down)), 2 * M * D * w_down.shape[1]),
         "out_proj_plain": (lambda: out.__setitem__("d", gemm.linear(x, w_out)), 2 * M * D * D),
+        "lm_head_plain": (lambda: out.__setitem__("e", gemm.linear(x, w_vocab)), 2 * M * 32768 * D),
     }
     res = {}
     for name, (fn, flops) in cases.items():
