@@ -471,19 +471,22 @@ __global__ void __launch_bounds__(256 * TPQ, 1) dsqg_resident_kernel(const DsqgP
         return valid ? s2 : -INFINITY;
       };
       // Online-softmax update and V accumulation (+ MOVT for large offsets) of one pair.
-      auto pair_update = [&](int jj, float s2, int src, bool valid, const float (&zz)[kPL]) {
-        const int j = j0 + jj;
-        const bool large = j >= js;  // warp-uniform
-        if (s2 > m + kRescaleLog2) {
-          const float f = ex2_approx(m - s2);
+      // Lazy running maximum: rescale only when a score exceeds it by 2^8.
+      auto rescale_to = [&](float smax) {
+        if (smax > m + kRescaleLog2) {
+          const float f = ex2_approx(m - smax);
 #pragma unroll
           for (int i = 0; i < kD; ++i) acc[i] *= f;
           l *= f; wbias *= f;
 #pragma unroll
           for (int pl = 0; pl < kPL; ++pl) { corr_a[pl] *= f; corr_b[pl] *= f; }
-          m = s2;
+          m = smax;
         }
-        const float w = valid ? ex2_approx(s2 - m) : 0.0f;
+      };
+      // Weight w of one pair folded into l, the V accumulator and MOVT.
+      auto pair_update = [&](int jj, float w, int src, const float (&zz)[kPL]) {
+        const int j = j0 + jj;
+        const bool large = j >= js;  // warp-uniform
         const float sv = __half2float(s_vs[src]) * (1.0f / 31.0f);
         const float wv = w * sv;
         l += w;
@@ -520,8 +523,8 @@ __global__ void __launch_bounds__(256 * TPQ, 1) dsqg_resident_kernel(const DsqgP
           }
         }
       };
-      // Two pairs per step: both scores first (independent chains), then the two
-      // updates in offset order, so results equal the one-pair-at-a-time loop.
+      // Two pairs per step: both scores first (independent chains), one lazy
+      // rescale to the larger, then both weights and the two accumulations.
 #pragma unroll 1
       for (int jj = 0; jj < jn; jj += 2) {
         const bool use1 = s_off[j0 + jj] <= wlast;                      // warp-uniform
@@ -532,15 +535,18 @@ __global__ void __launch_bounds__(256 * TPQ, 1) dsqg_resident_kernel(const DsqgP
           float z1[kPL], z2[kPL];
           const float s1 = pair_score(jj, src1, v1, z1);
           const float s2 = pair_score(jj + 1, src2, v2, z2);
-          pair_update(jj, s1, src1, v1, z1);
-          pair_update(jj + 1, s2, src2, v2, z2);
+          rescale_to(fmaxf(s1, s2));  // one maximum for both: the two weights are independent
+          const float w1 = v1 ? ex2_approx(s1 - m) : 0.0f, w2 = v2 ? ex2_approx(s2 - m) : 0.0f;
+          pair_update(jj, w1, src1, z1);
+          pair_update(jj + 1, w2, src2, z2);
         } else if (use1 || use2) {
           const int jx = use1 ? jj : jj + 1;
           int src;
           bool v;
           float z[kPL];
           const float s = pair_score(jx, src, v, z);
-          pair_update(jx, s, src, v, z);
+          rescale_to(s);
+          pair_update(jx, v ? ex2_approx(s - m) : 0.0f, src, z);
         }
       }
     }
