@@ -130,16 +130,13 @@ struct SelectParams {
   int64_t tile_count;
 };
 
-// L2-normalise a 64-value row in place: float32 sequential norm, IEEE
-// divide, bf16 rounding (F.normalize(x.float(), eps=1e-6).to(bf16)).
-__device__ __forceinline__ void normalize_row_bf16(float* row) {
-  float ss = 0.0f;
-  for (int d = 0; d < kHD; ++d) ss = add_rn(ss, mul_rn(row[d], row[d]));
-  const float nrm = fmaxf(sqrtf(ss), 1e-6f);
-  for (int d = 0; d < kHD; ++d) row[d] = round_bf16(__fdiv_rn(row[d], nrm));
-}
+// Each warp takes one selector tile at a time, kSelRounds tiles in all: the
+// CTA's (b, h) representatives are staged in shared memory once for
+// kSelRounds * 8 tiles. Arithmetic and summation order are those of the
+// reference: the anchor's squares are summed in dimension order (every lane
+// runs the same chain), then each lane divides two of its elements.
+constexpr int kSelRounds = 4;
 
-// One warp per selector tile; the CTA's (b, h) representatives sit in smem.
 __global__ void __launch_bounds__(256) hisa_select_kernel(const SelectParams p) {
   __shared__ float reps[kMaxChunks][kHD + 1];
   __shared__ float anchor[8][kHD];
@@ -147,55 +144,69 @@ __global__ void __launch_bounds__(256) hisa_select_kernel(const SelectParams p) 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int i = threadIdx.x; i < p.C * kHD; i += blockDim.x)
     reps[i / kHD][i % kHD] = __bfloat162float(p.reps[((b * p.H + h) * p.C) * kHD + i]);
+  __syncthreads();
   int64_t tb, te;
   window_of(p, tb, te);
-  const int64_t t = tb + (int64_t)blockIdx.x * 8 + warp;
-  const int64_t start = t * kTile;
-  const int64_t arow = imin64(start, p.T - 1);
-  const __nv_bfloat16* qrow = p.q + b * p.sqb + h * p.sqh + arow * p.sqn;
-  anchor[warp][lane] = __bfloat162float(qrow[lane]);
-  anchor[warp][lane + 32] = __bfloat162float(qrow[lane + 32]);
-  __syncthreads();
-  if (t >= te) return;
-  if (lane == 0) normalize_row_bf16(anchor[warp]);
-  __syncwarp();
   const int64_t vlen = p.lengths[b];
-  float val[kMaxChunks / 32];
+  for (int r = 0; r < kSelRounds; ++r) {
+    const int64_t t = tb + ((int64_t)blockIdx.x * kSelRounds + r) * 8 + warp;
+    if (t >= te) break;  // warp-uniform; no block barrier follows
+    const int64_t start = t * kTile;
+    const int64_t arow = imin64(start, p.T - 1);
+    const __nv_bfloat16* qrow = p.q + b * p.sqb + h * p.sqh + arow * p.sqn;
+    // F.normalize(anchor.float(), eps=1e-6).to(bf16): float32 sequential norm,
+    // IEEE divide, bf16 rounding
+    const float x0 = __bfloat162float(qrow[lane]), x1 = __bfloat162float(qrow[lane + 32]);
+    __syncwarp();  // the previous round's readers of anchor[warp] are done
+    anchor[warp][lane] = mul_rn(x0, x0);
+    anchor[warp][lane + 32] = mul_rn(x1, x1);
+    __syncwarp();
+    float ss = 0.0f;
 #pragma unroll
-  for (int i = 0; i < kMaxChunks / 32; ++i) {
-    const int c = lane + 32 * i;
-    float s = -INFINITY;
-    if (c < p.C) {
-      float acc = 0.0f;
-      for (int d = 0; d < kHD; ++d) acc = add_rn(acc, mul_rn(anchor[warp][d], reps[c][d]));
-      acc = __fdiv_rn(acc, p.temperature);
-      const bool eligible = ((int64_t)(c + 1) * kChunk <= start) && ((int64_t)c * kChunk < vlen) && (start < vlen);
-      s = eligible ? acc : -INFINITY;
-      if (p.logits) p.logits[((b * p.H + h) * p.tiles + t) * p.C + c] = s;
-    }
-    val[i] = s;
-  }
-  // k rounds of warp argmax: larger value first, lower index on ties.
-  int32_t* out = p.top + ((b * p.H + h) * p.tiles + t) * p.k_slots;
-  for (int k = 0; k < p.k_slots; ++k) {
-    float bv = -INFINITY;
-    int bi = 0x7fffffff;
+    for (int d = 0; d < kHD; ++d) ss = add_rn(ss, anchor[warp][d]);
+    const float nrm = fmaxf(sqrtf(ss), 1e-6f);
+    __syncwarp();
+    anchor[warp][lane] = round_bf16(__fdiv_rn(x0, nrm));
+    anchor[warp][lane + 32] = round_bf16(__fdiv_rn(x1, nrm));
+    __syncwarp();
+    float val[kMaxChunks / 32];
 #pragma unroll
     for (int i = 0; i < kMaxChunks / 32; ++i) {
       const int c = lane + 32 * i;
-      if (c < p.C && !isnan(val[i]) && (val[i] > bv || (val[i] == bv && c < bi))) { bv = val[i]; bi = c; }
-    }
+      float s = -INFINITY;
+      if (c < p.C) {
+        float acc = 0.0f;
 #pragma unroll
-    for (int o = 16; o >= 1; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-      if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+        for (int d = 0; d < kHD; ++d) acc = add_rn(acc, mul_rn(anchor[warp][d], reps[c][d]));
+        acc = __fdiv_rn(acc, p.temperature);
+        const bool eligible = ((int64_t)(c + 1) * kChunk <= start) && ((int64_t)c * kChunk < vlen) && (start < vlen);
+        s = eligible ? acc : -INFINITY;
+        if (p.logits) p.logits[((b * p.H + h) * p.tiles + t) * p.C + c] = s;
+      }
+      val[i] = s;
     }
-    if (lane == 0) out[k] = (bi != 0x7fffffff && isfinite(bv)) ? bi : -1;
-    // retire the winner (NaN marks "taken")
+    // k rounds of warp argmax: larger value first, lower index on ties.
+    int32_t* out = p.top + ((b * p.H + h) * p.tiles + t) * p.k_slots;
+    for (int k = 0; k < p.k_slots; ++k) {
+      float bv = -INFINITY;
+      int bi = 0x7fffffff;
 #pragma unroll
-    for (int i = 0; i < kMaxChunks / 32; ++i)
-      if (lane + 32 * i == bi) val[i] = NAN;
+      for (int i = 0; i < kMaxChunks / 32; ++i) {
+        const int c = lane + 32 * i;
+        if (c < p.C && !isnan(val[i]) && (val[i] > bv || (val[i] == bv && c < bi))) { bv = val[i]; bi = c; }
+      }
+#pragma unroll
+      for (int o = 16; o >= 1; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+      }
+      if (lane == 0) out[k] = (bi != 0x7fffffff && isfinite(bv)) ? bi : -1;
+      // retire the winner (NaN marks "taken")
+#pragma unroll
+      for (int i = 0; i < kMaxChunks / 32; ++i)
+        if (lane + 32 * i == bi) val[i] = NAN;
+    }
   }
 }
 
@@ -1181,7 +1192,8 @@ extern "C" int dwarf_hisa_select(const dwarf_hisa_select_args* a, void* stream) 
   int64_t n_tiles = 0;
   if (!launch_window(a->tile_begin, a->tile_count, a->pos, &p, &n_tiles)) return DWARF_ERR_SHAPE;
   if (n_tiles == 0) return DWARF_OK;
-  dim3 grid((unsigned)((n_tiles + 7) / 8), (unsigned)a->H, (unsigned)a->B);
+  const int64_t per_cta = 8 * kSelRounds;
+  dim3 grid((unsigned)((n_tiles + per_cta - 1) / per_cta), (unsigned)a->H, (unsigned)a->B);
   hisa_select_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(p);
   return launch_status();
 }
