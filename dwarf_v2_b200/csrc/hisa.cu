@@ -43,61 +43,84 @@ struct RepsParams {
   const int64_t* pos;   // optional: only chunk *pos / 64 (decode step)
 };
 
-// One CTA (64 threads) per (chunk, head, batch).
+// One CTA (64 threads) per (chunk, head, batch). Operations and summation
+// orders are those of the reference; only the serial steps are spread out:
+// the chunk arrives by 16-byte loads (8 threads per 128-byte row) when rows are
+// aligned, the first-maximum row comes from a shuffle reduction (ties to the
+// lower row, as the sequential scan), and the representative's squares are
+// formed in parallel and summed in dimension order by every thread.
 __global__ void __launch_bounds__(64) hisa_reps_kernel(const RepsParams p) {
   __shared__ float xs[kChunk][kHD + 1];
-  __shared__ float energy[kChunk];
-  __shared__ float rep[kHD];
-  __shared__ int best_row;
-  __shared__ float norm;
+  __shared__ float rep2[kHD];
+  __shared__ float wmax[2];
+  __shared__ int widx[2];
   const int c = p.pos != nullptr ? (int)(*p.pos / kChunk) : (int)blockIdx.x;
   const int h = blockIdx.y, b = blockIdx.z;
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   if (c >= p.C) return;
   const int64_t vlen = imin64((int64_t)p.lengths[b], p.T);
   const __nv_bfloat16* base = p.k + b * p.skb + h * p.skh;
-  for (int i = tid; i < kChunk * kHD; i += 64) {
-    const int r = i / kHD, d = i % kHD;
-    const int64_t t = (int64_t)c * kChunk + r;
-    xs[r][d] = t < p.T ? __bfloat162float(base[t * p.skn + d]) : 0.0f;
-  }
-  __syncthreads();
-  // Row energies (row = tid), masked to -inf past the valid length.
-  {
-    float e = 0.0f;
-    for (int d = 0; d < kHD; ++d) e = add_rn(e, mul_rn(xs[tid][d], xs[tid][d]));
-    energy[tid] = ((int64_t)c * kChunk + tid < vlen) ? e : -INFINITY;
-  }
-  __syncthreads();
-  if (tid == 0) {
-    int bi = 0;
-    float bv = energy[0];
-    for (int r = 1; r < kChunk; ++r)
-      if (energy[r] > bv) { bv = energy[r]; bi = r; }  // first maximum wins
-    best_row = bi;
-  }
-  __syncthreads();
-  // Masked mean of dim d (= tid) and the blend.
-  {
-    float s = 0.0f;
-    int count = 0;
-    for (int r = 0; r < kChunk; ++r) {
-      const bool ok = (int64_t)c * kChunk + r < vlen;
-      s = add_rn(s, ok ? xs[r][tid] : 0.0f);
-      count += ok;
+  const bool vec = (reinterpret_cast<uintptr_t>(base) & 15u) == 0 && p.skn % 8 == 0;
+  if (vec) {
+    const int piece = tid & 7;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int r = k * 8 + (tid >> 3);
+      const int64_t t = (int64_t)c * kChunk + r;
+      uint4 w = make_uint4(0u, 0u, 0u, 0u);
+      if (t < p.T) w = *reinterpret_cast<const uint4*>(base + t * p.skn + piece * 8);
+      const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        xs[r][piece * 8 + 2 * i] = __uint_as_float(u[i] << 16);
+        xs[r][piece * 8 + 2 * i + 1] = __uint_as_float(u[i] & 0xffff0000u);
+      }
     }
-    const float mean = __fdiv_rn(s, (float)max(count, 1));
-    rep[tid] = add_rn(mul_rn(1.0f - p.alpha, mean), mul_rn(p.alpha, xs[best_row][tid]));
+  } else {
+    for (int i = tid; i < kChunk * kHD; i += 64) {
+      const int r = i / kHD, d = i % kHD;
+      const int64_t t = (int64_t)c * kChunk + r;
+      xs[r][d] = t < p.T ? __bfloat162float(base[t * p.skn + d]) : 0.0f;
+    }
   }
   __syncthreads();
-  if (tid == 0) {
-    float ss = 0.0f;
-    for (int d = 0; d < kHD; ++d) ss = add_rn(ss, mul_rn(rep[d], rep[d]));
-    norm = fmaxf(sqrtf(ss), 1e-6f);
+  // Row energies (row = tid), masked to -inf past the valid length; the first
+  // maximum over the rows.
+  float e = 0.0f;
+#pragma unroll 16
+  for (int d = 0; d < kHD; ++d) e = add_rn(e, mul_rn(xs[tid][d], xs[tid][d]));
+  e = ((int64_t)c * kChunk + tid < vlen) ? e : -INFINITY;
+  float bv = e;
+  int bi = tid;
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
   }
+  if (lane == 0) { wmax[warp] = bv; widx[warp] = bi; }
   __syncthreads();
+  // Rows 0-31 come before rows 32-63: the second warp wins only when strictly larger.
+  const int best_row = wmax[1] > wmax[0] ? widx[1] : widx[0];
+  // Masked mean of dim d (= tid) and the blend.
+  float s = 0.0f;
+  int count = 0;
+#pragma unroll 16
+  for (int r = 0; r < kChunk; ++r) {
+    const bool ok = (int64_t)c * kChunk + r < vlen;
+    s = add_rn(s, ok ? xs[r][tid] : 0.0f);
+    count += ok;
+  }
+  const float mean = __fdiv_rn(s, (float)max(count, 1));
+  const float rep = add_rn(mul_rn(1.0f - p.alpha, mean), mul_rn(p.alpha, xs[best_row][tid]));
+  rep2[tid] = mul_rn(rep, rep);
+  __syncthreads();
+  float ss = 0.0f;
+#pragma unroll 16
+  for (int d = 0; d < kHD; ++d) ss = add_rn(ss, rep2[d]);
+  const float norm = fmaxf(sqrtf(ss), 1e-6f);
   const bool chunk_valid = (int64_t)c * kChunk < vlen;
-  const float v = chunk_valid ? __fdiv_rn(rep[tid], norm) : 0.0f;
+  const float v = chunk_valid ? __fdiv_rn(rep, norm) : 0.0f;
   p.reps[((b * p.H + h) * p.C + c) * kHD + tid] = __float2bfloat16_rn(v);
 }
 
