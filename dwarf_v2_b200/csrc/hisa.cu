@@ -385,41 +385,41 @@ struct RouteParams {
   int64_t tile_count;
 };
 
-// One warp per two 16-query tiles (16 tiles per CTA); each lane owns one query row.
+// One warp per 16-query tile (8 tiles per CTA); two lanes per query row, lane
+// 2i + hf holding dims [32 hf, 32 hf + 32) of row i. Every float32 sum keeps the
+// reference's order over the 64 dims: the even lane sums dims 0-31 and hands its
+// partial to the odd lane (one shuffle), which continues with dims 32-63.
 __global__ void __launch_bounds__(256) hisa_route_kernel(const RouteParams p) {
-  __shared__ float rsel[16][kTopK][kHD];
-  __shared__ int sel[16][kTopK];
+  __shared__ float rsel[8][kTopK][kHD];
+  __shared__ int sel[8][kTopK];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int hf = lane & 1, ri = lane >> 1;
   const int h = blockIdx.y, b = blockIdx.z;
-  const int lt = warp * 2 + (lane >> 4);  // local tile of this lane's row
   int64_t tb, te;
   window_of(p, tb, te);
-  const int64_t t = tb + (int64_t)blockIdx.x * 16 + lt;
+  const int64_t t = tb + (int64_t)blockIdx.x * 8 + warp;
   const bool tile_ok = t < te;
-  const int64_t row = t * kTile + (lane & 15);
-  // Issue the row load first; the selections and representatives follow.
-  uint4 qw[8];
+  const int64_t row = t * kTile + ri;
+  // Issue the half-row load first; the selections and representatives follow.
+  uint4 qw[4];
   {
     const int64_t r = row < p.T ? row : p.T - 1;
-    const uint4* src = reinterpret_cast<const uint4*>(p.q + b * p.sqb + h * p.sqh + r * p.sqn);
+    const uint4* src = reinterpret_cast<const uint4*>(p.q + b * p.sqb + h * p.sqh + r * p.sqn + 32 * hf);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) qw[i] = src[i];
+    for (int i = 0; i < 4; ++i) qw[i] = src[i];
   }
-  if (lane < 2 * kTopK) {
-    const int i = warp * 2 + lane / kTopK, k = lane % kTopK;
-    const int64_t ti = tb + (int64_t)blockIdx.x * 16 + i;
-    sel[i][k] = (ti < te && k < p.k_slots) ? p.top[((b * p.H + h) * p.tiles + ti) * p.k_slots + k] : -1;
+  if (lane < kTopK) sel[warp][lane] = (tile_ok && lane < p.k_slots) ? p.top[((b * p.H + h) * p.tiles + t) * p.k_slots + lane] : -1;
+  __syncwarp();
+  for (int x = lane; x < kTopK * kHD; x += 32) {
+    const int k = x / kHD, c = sel[warp][k];
+    rsel[warp][k][x % kHD] = c >= 0 ? __bfloat162float(p.reps[((b * p.H + h) * p.C + c) * kHD + x % kHD]) : 0.0f;
   }
   __syncwarp();
-  for (int x = lane; x < 2 * kTopK * kHD; x += 32) {
-    const int i = warp * 2 + x / (kTopK * kHD), k = (x / kHD) % kTopK, c = sel[i][k];
-    rsel[i][k][x % kHD] = c >= 0 ? __bfloat162float(p.reps[((b * p.H + h) * p.C + c) * kHD + x % kHD]) : 0.0f;
-  }
-  __syncwarp();
-  if (!tile_ok || row >= p.T) return;
-  float qh[kHD];
+  if (!tile_ok) return;  // warp-uniform
+  const bool row_ok = row < p.T;
+  float qh[32];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
+  for (int i = 0; i < 4; ++i) {
     const uint32_t u[4] = {qw[i].x, qw[i].y, qw[i].z, qw[i].w};
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
@@ -427,24 +427,46 @@ __global__ void __launch_bounds__(256) hisa_route_kernel(const RouteParams p) {
       qh[8 * i + 2 * k + 1] = __uint_as_float(u[k] & 0xffff0000u);
     }
   }
+  const unsigned pair = 0xffffffffu;
+  const int even = lane & ~1;
   // q^ = bf16(q / max(|q|, 1e-6)): sequential float32 norm, IEEE divide.
   float ss = 0.0f;
+  if (hf == 0) {
 #pragma unroll
-  for (int d = 0; d < kHD; ++d) ss = add_rn(ss, mul_rn(qh[d], qh[d]));
+    for (int d = 0; d < 32; ++d) ss = add_rn(ss, mul_rn(qh[d], qh[d]));
+  }
+  ss = __shfl_sync(pair, ss, even);
+  if (hf == 1) {
+#pragma unroll
+    for (int d = 0; d < 32; ++d) ss = add_rn(ss, mul_rn(qh[d], qh[d]));
+  }
+  ss = __shfl_sync(pair, ss, even | 1);
   const float nrm = fmaxf(sqrtf(ss), 1e-6f);
 #pragma unroll
-  for (int d = 0; d < kHD; ++d) qh[d] = round_bf16(__fdiv_rn(qh[d], nrm));
+  for (int d = 0; d < 32; ++d) qh[d] = round_bf16(__fdiv_rn(qh[d], nrm));
   float sc[kTopK];
+#pragma unroll
+  for (int k = 0; k < kTopK; ++k) {
+    const float* r = rsel[warp][k] + 32 * hf;
+    float acc = 0.0f;
+    if (hf == 0) {
+#pragma unroll
+      for (int d = 0; d < 32; ++d) acc = add_rn(acc, mul_rn(qh[d], r[d]));
+    }
+    acc = __shfl_sync(pair, acc, even);
+    if (hf == 1) {
+#pragma unroll
+      for (int d = 0; d < 32; ++d) acc = add_rn(acc, mul_rn(qh[d], r[d]));
+    }
+    sc[k] = acc;  // complete in the odd lane
+  }
+  if (hf == 0 || !row_ok) return;
   float sum = 0.0f;
   int count = 0;
 #pragma unroll
   for (int k = 0; k < kTopK; ++k) {
-    float acc = 0.0f;
-#pragma unroll
-    for (int d = 0; d < kHD; ++d) acc = add_rn(acc, mul_rn(qh[d], rsel[lt][k][d]));
-    sc[k] = acc;
-    const bool ok = sel[lt][k] >= 0;
-    sum = add_rn(sum, ok ? acc : 0.0f);
+    const bool ok = sel[warp][k] >= 0;
+    sum = add_rn(sum, ok ? sc[k] : 0.0f);
     count += ok;
   }
   const float mean = __fdiv_rn(sum, (float)max(count, 1));
@@ -452,8 +474,8 @@ __global__ void __launch_bounds__(256) hisa_route_kernel(const RouteParams p) {
   uint32_t packed[2];
 #pragma unroll
   for (int k = 0; k < kTopK; k += 2) {
-    const float v0 = sel[lt][k] >= 0 ? mul_rn(__fsub_rn(sc[k], mean), scale) : 0.0f;
-    const float v1 = sel[lt][k + 1] >= 0 ? mul_rn(__fsub_rn(sc[k + 1], mean), scale) : 0.0f;
+    const float v0 = sel[warp][k] >= 0 ? mul_rn(__fsub_rn(sc[k], mean), scale) : 0.0f;
+    const float v1 = sel[warp][k + 1] >= 0 ? mul_rn(__fsub_rn(sc[k + 1], mean), scale) : 0.0f;
     const __nv_bfloat162 two = __floats2bfloat162_rn(v0, v1);
     packed[k / 2] = *reinterpret_cast<const uint32_t*>(&two);
   }
@@ -1237,7 +1259,7 @@ extern "C" int dwarf_hisa_route(const dwarf_hisa_route_args* a, void* stream) {
   int64_t n_tiles = 0;
   if (!launch_window(a->tile_begin, a->tile_count, a->pos, &p, &n_tiles)) return DWARF_ERR_SHAPE;
   if (n_tiles == 0) return DWARF_OK;
-  dim3 grid((unsigned)((n_tiles + 15) / 16), (unsigned)a->H, (unsigned)a->B);
+  dim3 grid((unsigned)((n_tiles + 7) / 8), (unsigned)a->H, (unsigned)a->B);
   hisa_route_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(p);
   return launch_status();
 }
