@@ -23,6 +23,14 @@ constexpr int kMaxWidth = 1024;
 constexpr int kSeg = 256;  // values per warp-wide 16-byte access
 
 __device__ __forceinline__ void ld8(const __nv_bfloat16* p, float (&v)[8]) { VecIO<__nv_bfloat16, 8>::load(p, v); }
+__device__ __forceinline__ void unpack8(const uint4& w, float (&v)[8]) {
+  const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    v[2 * i] = __uint_as_float(u[i] << 16);
+    v[2 * i + 1] = __uint_as_float(u[i] & 0xffff0000u);
+  }
+}
 __device__ __forceinline__ void st8(__nv_bfloat16* p, const float (&v)[8]) { VecIO<__nv_bfloat16, 8>::store(p, v); }
 
 __device__ __forceinline__ float warp_sum(float v) {
@@ -160,20 +168,36 @@ __global__ void __launch_bounds__(256) packet_kernel(dwarf_packet_args a) {
   const int lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
   if (row >= a.rows) return;
+  // Every load of the row (all scans, then the gate) is issued before any
+  // arithmetic, as raw 16-byte words.
+  uint4 raw[3][NSEG], graw[NSEG];
+  const __nv_bfloat16* gp = static_cast<const __nv_bfloat16*>(a.gate_pre) + row * a.sgp;
+#pragma unroll
+  for (int k = 0; k < 3; ++k) {
+    if (k < a.n_scans) {
+      const __nv_bfloat16* sc = static_cast<const __nv_bfloat16*>(a.scans[k]) + row * a.sscan;
+#pragma unroll
+      for (int s = 0; s < NSEG; ++s) raw[k][s] = *reinterpret_cast<const uint4*>(sc + s * kSeg + lane * 8);
+    }
+  }
+#pragma unroll
+  for (int s = 0; s < NSEG; ++s) graw[s] = *reinterpret_cast<const uint4*>(gp + s * kSeg + lane * 8);
   float pooled[NSEG][8];
 #pragma unroll
   for (int s = 0; s < NSEG; ++s)
 #pragma unroll
     for (int i = 0; i < 8; ++i) pooled[s][i] = 0.0f;
-  for (int k = 0; k < a.n_scans; ++k) {
-    const __nv_bfloat16* sc = static_cast<const __nv_bfloat16*>(a.scans[k]) + row * a.sscan;
-    const float wk = a.mix[k];
 #pragma unroll
-    for (int s = 0; s < NSEG; ++s) {
-      float t[8];
-      ld8(sc + s * kSeg + lane * 8, t);
+  for (int k = 0; k < 3; ++k) {
+    if (k < a.n_scans) {
+      const float wk = a.mix[k];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) pooled[s][i] = round_bf16(pooled[s][i] + round_bf16(wk * t[i]));
+      for (int s = 0; s < NSEG; ++s) {
+        float t[8];
+        unpack8(raw[k][s], t);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) pooled[s][i] = round_bf16(pooled[s][i] + round_bf16(wk * t[i]));
+      }
     }
   }
   float ss = 0.0f;
@@ -184,12 +208,11 @@ __global__ void __launch_bounds__(256) packet_kernel(dwarf_packet_args a) {
   const float ms = warp_sum(ss) / (float)a.width;
   const float conf = tanhf(sqrtf(ms) / 0.25f);
   const float rs = rsqrtf(ms + 1e-6f);
-  const __nv_bfloat16* gp = static_cast<const __nv_bfloat16*>(a.gate_pre) + row * a.sgp;
   __nv_bfloat16* out = static_cast<__nv_bfloat16*>(a.out) + row * a.so;
 #pragma unroll
   for (int s = 0; s < NSEG; ++s) {
     float g[8], o[8];
-    ld8(gp + s * kSeg + lane * 8, g);
+    unpack8(graw[s], g);
 #pragma unroll
     for (int i = 0; i < 8; ++i) o[i] = ((pooled[s][i] * rs) * conf) * sigmoid_f(g[i]);
     st8(out + s * kSeg + lane * 8, o);

@@ -175,6 +175,22 @@ def case_q6_unpack_config3(timer, peak):
     return {"kernel": "dwarf_q6_unpack", "ms": ms, **_rate(_nbytes(codes, scales, res["x"]), ms, peak)}
 
 
+def case_packet_model_b256(timer, peak):
+    """The InterferencePacket epilogue at the model's single-GPU shape: three bf16 scans and the
+    gate pre-activation [256 x 2048, 512] -> the bf16 packet."""
+    from .glue import packet
+
+    g = torch.Generator(device="cuda").manual_seed(6)
+    rows, width = 256 * 2048, 512
+    scans = [torch.randn(rows, width, generator=g, device="cuda", dtype=torch.bfloat16) * s for s in (0.05, 0.1, 0.3)]
+    gate_pre = torch.randn(rows, width, generator=g, device="cuda", dtype=torch.bfloat16)
+    mixture = [0.33203125, 0.333984375, 0.333984375]
+    res = {}
+    times = timer(lambda: res.__setitem__("o", packet(scans, mixture, gate_pre)), ("dwarf_packet",))
+    ms = times["dwarf_packet"]
+    return {"kernel": "dwarf_packet", "ms": ms, **_rate(5 * _nbytes(gate_pre), ms, peak)}
+
+
 def case_npci_model_b256(timer, peak):
     """The DSQG key rotation at the model's single-GPU shape (B=256, H=8, T=2048): key is the
     strided view of the fused qkvg projection, delta the strided view of the packet's kv output."""
@@ -434,6 +450,7 @@ CASES = {
     "q6_pack_config3": case_q6_pack_config3,
     "q6_unpack_config3": case_q6_unpack_config3,
     "npci_model_b256": case_npci_model_b256,
+    "packet_model_b256": case_packet_model_b256,
     "gemm_model_epilogues": case_gemm_model_epilogues,
     "dsqg_q6_config3": case_dsqg_q6_config3,
     "dsqg_q6_model_group": case_dsqg_q6_model_group,
