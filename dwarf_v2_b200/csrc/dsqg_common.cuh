@@ -50,6 +50,8 @@ struct DsqgParams {
   int32_t* status;  // optional device status word (DWARF_DEVICE_TIMEOUT)
   int64_t row_begin;  // first query row computed (gather kernel)
   const int64_t* pos;  // optional device row_begin (decode kernel)
+  int round_split;      // resident kernel with gridDim.z == 2: CTA z = 0 takes the query
+                        // rounds [round_split, end), z = 1 the rounds [0, round_split)
 };
 
 // 16 bf16 (two 16-B words) -> 16 floats.

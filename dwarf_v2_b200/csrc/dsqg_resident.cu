@@ -236,6 +236,9 @@ __global__ void __launch_bounds__(256 * TPQ, 1) dsqg_resident_kernel(const DsqgP
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int qi = lane / TPQ, hf = lane % TPQ;
   const int64_t h = blockIdx.x, b = blockIdx.y;
+  // Query rounds of this CTA: all of them, or one part of a two-way split.
+  const int r_begin = gridDim.z == 1 ? 0 : (blockIdx.z == 0 ? p.round_split : 0);
+  const int r_end = gridDim.z == 1 ? L.chunks : (blockIdx.z == 0 ? L.chunks : p.round_split);
   const int64_t hk = h / p.kv_group;
   const uint32_t sbase = smem_u32(smem);
   const uint32_t bar0 = sbase + L.o_bar;
@@ -248,7 +251,7 @@ __global__ void __launch_bounds__(256 * TPQ, 1) dsqg_resident_kernel(const DsqgP
     const uint8_t* vc = p.vc + b * p.ccb + hk * p.cch;
     const uint16_t* ks = p.ks + b * p.csb + hk * p.csh;
     const uint16_t* vs = p.vs + b * p.csb + hk * p.csh;
-    for (int c = 0; c < L.chunks; ++c) {
+    for (int c = 0; c < r_end; ++c) {  // the key rows this CTA's queries can reach
       const int r0 = c * kRQB;
       const int rows = N - r0 < kRQB ? N - r0 : kRQB;
       const uint32_t bar = bar0 + 8 * c;
@@ -305,14 +308,14 @@ __global__ void __launch_bounds__(256 * TPQ, 1) dsqg_resident_kernel(const DsqgP
     gain = p.gain_bf16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.gain)[h])
                        : reinterpret_cast<const float*>(p.gain)[h];
 
-  for (int r = 0; r < L.chunks; ++r) {
+  for (int r = 0; r < r_end; ++r) {
     const int n0 = r * kRQB;
     const bool ok = mbar_wait(bar0 + 8 * r, 0);
     if (__syncthreads_or(!ok)) {
       if (tid == 0) {
         if (status != nullptr) atomicExch(status, DWARF_DEVICE_TIMEOUT);
         // Leave no copy in flight into this CTA's shared memory.
-        for (int c = r; c < L.chunks; ++c) (void)mbar_wait(bar0 + 8 * c, 0);
+        for (int c = r; c < r_end; ++c) (void)mbar_wait(bar0 + 8 * c, 0);
       }
       return;
     }
@@ -329,6 +332,7 @@ __global__ void __launch_bounds__(256 * TPQ, 1) dsqg_resident_kernel(const DsqgP
       }
     }
     __syncthreads();
+    if (r < r_begin) continue;  // block-uniform: an earlier part's rounds (keys staged and flipped only)
 
     const int wn0 = n0 + warp * kQW;
     if (wn0 >= N) continue;  // warp-uniform; no block barrier follows before the next round
@@ -630,8 +634,22 @@ int dsqg_resident_launch(const DsqgParams& p, int64_t B, cudaStream_t stream) {
     kernel = pw == 0 ? dsqg_resident_kernel<0, 2> : (pw == 1 ? dsqg_resident_kernel<1, 2> : dsqg_resident_kernel<2, 2>);
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.bytes) != cudaSuccess)
     return DWARF_ERR_LAUNCH;
-  dim3 grid((unsigned)p.H, (unsigned)B);
-  kernel<<<grid, 256 * tpq, L.bytes, stream>>>(p, p.status);
+  // Two-way split of each (b, h) by query rounds when the (b, h) count would leave
+  // the last wave short (fewer than four waves): the later rounds (more offsets in
+  // reach, ~3/4 of the work) as one CTA, dispatched first, the earlier ones as
+  // another, so the short CTAs fill the last wave. DWARF_DSQG_SPLIT=1 / 2 forces
+  // one part / two parts (read on every call).
+  int sms = kNumSMs, device = 0;
+  if (cudaGetDevice(&device) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  const char* force = getenv("DWARF_DSQG_SPLIT");
+  bool split = L.chunks >= 4 && B * p.H < 4LL * sms;
+  if (force != nullptr && force[0] == '1') split = false;
+  if (force != nullptr && force[0] == '2') split = L.chunks >= 2;
+  DsqgParams pr = p;
+  pr.round_split = split ? (L.chunks * 3 + 4) / 8 : 0;
+  if (split && pr.round_split < 1) pr.round_split = 1;
+  dim3 grid((unsigned)p.H, (unsigned)B, split ? 2u : 1u);
+  kernel<<<grid, 256 * tpq, L.bytes, stream>>>(pr, p.status);
   return launch_status();
 }
 

@@ -342,6 +342,22 @@ def test_resident_q6_kernel_matches_oracle(B, H, Hkv, N, plane_shift, query_star
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("B,H,Hkv,N,plane_shift,query_start", [
+    (2, 4, 4, 2048, 0, 0), (1, 4, 2, 2048, 6, 37), (1, 2, 2, 1000, 14, 0)])
+def test_resident_round_split_is_bit_identical(B, H, Hkv, N, plane_shift, query_start, monkeypatch):
+    """The resident kernel may run each (batch, head) as two CTAs, the later query rounds
+    and the earlier ones (fewer (b, h) than four waves of SMs): every query's output
+    and lse must equal the one-CTA launch's bit for bit."""
+    c, offs, js = _resident_case(B, H, Hkv, N, seed=N + plane_shift + 5)
+    monkeypatch.setenv("DWARF_DSQG_SPLIT", "1")
+    one, lse1, _ = _run_q6(c, offs, js, plane_shift, query_start, "resident", monkeypatch)
+    monkeypatch.setenv("DWARF_DSQG_SPLIT", "2")
+    two, lse2, _ = _run_q6(c, offs, js, plane_shift, query_start, "resident", monkeypatch)
+    assert torch.equal(one, two)
+    assert torch.equal(lse1, lse2)
+
+
+@pytest.mark.gpu
 def test_resident_q6_kernel_fused_gain_gate_matches_gather(monkeypatch):
     c, offs, js = _resident_case(2, 4, 4, 2048, seed=3)
     gen = torch.Generator().manual_seed(4)
