@@ -106,6 +106,14 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
 
 __device__ __forceinline__ float den(uint32_t bits) { return __uint_as_float(bits); }
 
+// (a, b) rounded to bf16 and back with one packed conversion.
+__device__ __forceinline__ void round_pair_bf16(float& a, float& b) {
+  const __nv_bfloat162 t = __floats2bfloat162_rn(a, b);
+  const uint32_t w = *reinterpret_cast<const uint32_t*>(&t);
+  a = __uint_as_float(w << 16);
+  b = __uint_as_float(w & 0xffff0000u);
+}
+
 // ex2_approx (common.cuh): arguments here are <= 8; results below 2^-126
 // flush to 0, which only drops weights far below the running maximum.
 
@@ -374,6 +382,11 @@ __global__ void __launch_bounds__(256 * TPQ, 1) dsqg_resident_kernel(const DsqgP
       c1 = __int_as_float((276 - E) << 23);  // 2^(149 - E)
       qbias = -32.0f * qsum;
     }
+    // The content-gate row is read only by the epilogue: pull it into L2 now.
+    if (p.gate != nullptr && n < N) {
+      const __nv_bfloat16* g = p.gate + b * p.sgtb + (int64_t)n * p.sgtn + h * 64 + kD * hf;
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(g));
+    }
     float gy[kPL];  // y_pre of this query (multiplies phase_gain)
     {
       const float* yrow = p.y + b * p.syb + h * p.syh + (int64_t)nq * p.syn + kPL * hf;
@@ -572,21 +585,35 @@ __global__ void __launch_bounds__(256 * TPQ, 1) dsqg_resident_kernel(const DsqgP
                        -bias);
         if (i == rot) v += corr_a[sl];
         if (i == rot + 1) v += corr_b[sl];
-        o[i] = round_bf16(v * inv_l);
+        o[i] = v * inv_l;
       }
+#pragma unroll
+      for (int i = 0; i < 16; i += 2) round_pair_bf16(o[i], o[i + 1]);
       if (p.gain != nullptr) {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) o[i] = p.gain_bf16 ? round_bf16(o[i] * gain) : o[i] * gain;
+        for (int i = 0; i < 16; ++i) o[i] *= gain;
+        if (p.gain_bf16) {
+#pragma unroll
+          for (int i = 0; i < 16; i += 2) round_pair_bf16(o[i], o[i + 1]);
+        }
       }
       if (grow != nullptr) {
         const uint4* gp = reinterpret_cast<const uint4*>(grow + 16 * sl);
         const uint4 gw[2] = {__ldg(gp), __ldg(gp + 1)};
         float gv[16];
         bf16x16_to_f32(gw, gv);
+        // sigmoid(gate) rounded to bf16 (the reference's bf16 sigmoid) from the
+        // hardware exp2 and reciprocal: their few-ulp fp32 error is absorbed by the
+        // bf16 rounding except at rounding ties.
+        const bool round_out = p.gain_bf16 || p.gain == nullptr;
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float sg = round_bf16(__frcp_rn(1.0f + __expf(-gv[i])));
-          o[i] = p.gain_bf16 || p.gain == nullptr ? round_bf16(o[i] * sg) : o[i] * sg;
+        for (int i = 0; i < 16; i += 2) {
+          float s0 = __fdividef(1.0f, 1.0f + __expf(-gv[i])), s1 = __fdividef(1.0f, 1.0f + __expf(-gv[i + 1]));
+          round_pair_bf16(s0, s1);
+          float o0 = o[i] * s0, o1 = o[i + 1] * s1;
+          if (round_out) round_pair_bf16(o0, o1);
+          o[i] = o0;
+          o[i + 1] = o1;
         }
       }
       uint4 packed[2];
