@@ -38,6 +38,7 @@ present on the GPU box), with the port built once outside the timed steps.
 from __future__ import annotations
 
 import argparse
+import datetime
 import json
 import os
 import statistics
@@ -77,21 +78,42 @@ def _token_ids(rows: slice) -> torch.Tensor:
 
 
 class ClockSampler:
-    """nvidia-smi sampling of SM clocks and throttle reasons during a timed region."""
+    """nvidia-smi sampling of SM clocks and throttle reasons during a timed region.
 
-    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    One process per node: local rank 0 samples every GPU of the job on its node
+    (``indices``); the other ranks pass ``None`` and start nothing, so that N
+    pollers do not contend with the kernel launches of an N-GPU step. The
+    process starts before the warm-up steps (its NVML start-up is heavy driver
+    work that must not land in the timed region); ``mark_start`` / ``mark_end``
+    bracket the timed region on the host clock, and the summary keeps the
+    samples whose nvidia-smi timestamps fall inside it (with one sampling period
+    of slack at either end, so that a short region still has samples)."""
+
+    PERIOD_S = 0.1
+    QUERY = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, index: int):
-        self.index = index
+    def __init__(self, indices: list[int] | None):
+        self.indices = indices
         self.proc = None
+        self.t0 = self.t1 = None
+
+    def mark_start(self):
+        self.t0 = time.time()
+
+    def mark_end(self):
+        self.t1 = time.time()
 
     def __enter__(self):
+        if not self.indices:
+            return self
+        ids = ",".join(str(i) for i in self.indices)
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                ["nvidia-smi", f"--id={ids}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", str(int(self.PERIOD_S * 1000))], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
+                text=True)
         except OSError:
             self.proc = None
         return self
@@ -107,14 +129,19 @@ class ClockSampler:
     def summary(self) -> dict:
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        lo = self.t0 - self.PERIOD_S if self.t0 is not None else None
+        hi = self.t1 + self.PERIOD_S if self.t1 is not None else None
         for line in getattr(self, "lines", []):
             parts = [p.strip() for p in line.split(",")]
             try:
-                sm.append(float(parts[1]))
-                mx = float(parts[2])
+                stamp = datetime.datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                if (lo is not None and stamp < lo) or (hi is not None and stamp > hi):
+                    continue
+                sm.append(float(parts[2]))
+                mx = float(parts[3])
             except (ValueError, IndexError):
                 continue
-            for name, flag in zip(names, parts[5:9]):
+            for name, flag in zip(names, parts[6:10]):
                 if flag.lower() == "active":
                     reasons.add(name)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
@@ -230,21 +257,28 @@ def run_ours(args) -> None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    local_world = int(os.environ.get("LOCAL_WORLD_SIZE", world))
+    clocks = ClockSampler(list(range(local_world)) if local == 0 else None)
     with torch.no_grad():
-        for _ in range(max(args.warmup, 0)):
-            step(ids_dev)
-        # device-resident throughput
-        log = _lib.LaunchLog(timed=("dwarf_dsqg_fwd",))
-        barrier()
-        with ClockSampler(local) as clocks:
+        clocks.__enter__()  # started before the warm-up: its start-up stays out of the timed region
+        try:
+            for _ in range(max(args.warmup, 0)):
+                step(ids_dev)
+            # device-resident throughput
+            log = _lib.LaunchLog(timed=("dwarf_dsqg_fwd",))
+            barrier()
             start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             _lib.set_launch_log(log)
+            clocks.mark_start()
             start.record()
             for _ in range(args.steps):
                 step(ids_dev)
             end.record()
             _lib.set_launch_log(None)
             barrier()
+            clocks.mark_end()
+        finally:
+            clocks.__exit__(None, None, None)
         ms = max_over_ranks(start.elapsed_time(end) / args.steps)
         launches = log.count if graph is None else launches_per_step * args.steps
         if graph is not None:
